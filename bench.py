@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 quantised-MoE hot path (one JSON line on rank 0).
+
+Workloads (synthetic data, random-init weights of the Gemma-4 26B-A4B shapes):
+  moe30_decode_b1   (default) the routed-expert path of the 30-layer decoder for
+                    one decode token: per layer the bf16 router [128, 2816]
+                    (softmax, top-8, renormalise) and 8 of 128 MLX-affine 4-bit
+                    experts (gate/up 2816->704, GELU-tanh gating, down
+                    704->2816, weighted combine).  Every layer has its own
+                    router and 128 experts (30 x 428 MB resident in HBM, far
+                    above L2, so no flush is needed).  The 30 layers are
+                    applied to the step's hidden state.
+  moe30_decode_b32  the same with 32 tokens per step.
+A step is captured once in a CUDA graph and replayed.  `value` is tokens/s
+with inputs resident in HBM; `e2e` adds the pinned-host -> device copy of the
+step's input and the device -> host copy of its result inside the timed region.
+
+--impl reference times the CPU port of the reference's path (oracle/, C++
+OpenMP on all host cores) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K, LAYERS = 2816, 704, 128, 8, 30
+ROUTER_BYTES = E * H * 2                                   # bf16 router weight per layer
+GATE_UP_BYTES = 2 * (I * H // 2 + 2 * I * (H // 64) * 2)   # per selected expert: 2,230,272
+DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert: 1,115,136
+WORKLOADS = {"moe30_decode_b1": 1, "moe30_decode_b32": 32}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="moe30_decode_b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in (getattr(self, "out", "") or "").splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                maxs.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+
+def build_layers(fm, torch, dev, seed):
+    layers = []
+    g = torch.Generator(device=dev)
+    for l in range(LAYERS):
+        g.manual_seed(seed + l)
+        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        table = fm.ExpertTable.random(E, H, I, seed=seed + 1000 + l, device=dev)
+        layers.append(fm.Gemma4MoeBlock(fm.QuantizedLinear(wr, bits=16), table, top_k=K))
+    return layers
+
+
+class MoeStack:
+    """Prepared C-ABI calls for the 30 layers (structs and workspaces built once)."""
+
+    def __init__(self, fm, torch, layers, T, dev):
+        import ctypes
+        self.fm, self.torch, self.ctypes = fm, torch, ctypes
+        self.T = T
+        self.x = torch.zeros(T, H, dtype=torch.bfloat16, device=dev)
+        self.ys = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for _ in layers]
+        self.ids = [torch.empty(T, K, dtype=torch.int32, device=dev) for _ in layers]
+        self.wts = [torch.empty(T, K, dtype=torch.float32, device=dev) for _ in layers]
+        self.rc = [l.router_cstruct() for l in layers]
+        self.ec = [l.experts.cstruct() for l in layers]
+        nbytes = max(fm.lib().fmoe_moe_block_workspace_bytes(T, ctypes.byref(r), ctypes.byref(e))
+                     for r, e in zip(self.rc, self.ec))
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.layers = layers
+
+    def run(self, stream):
+        lib, ct = self.fm.lib(), self.ctypes
+        s = stream.cuda_stream
+        for i in range(len(self.layers)):
+            rc = lib.fmoe_moe_block_forward(self.x.data_ptr(), self.T, ct.byref(self.rc[i]), ct.byref(self.ec[i]),
+                                            self.ys[i].data_ptr(), self.ids[i].data_ptr(), self.wts[i].data_ptr(),
+                                            self.ws.data_ptr(), self.ws.numel(), s)
+            if rc:
+                self.fm.check(rc)
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    fm.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    T = WORKLOADS[args.workload]
+    layers = build_layers(fm, torch, dev, seed=4000)
+    stack = MoeStack(fm, torch, layers, T, dev)
+    g = torch.Generator(device=dev).manual_seed(5000 + rank)
+    nin = max(args.steps, 1) + args.warmup
+    xs = torch.randn(nin, T, H, generator=g, device=dev).to(torch.bfloat16)
+    stream = torch.cuda.Stream(device=dev)
+
+    # per-kernel device times (eager, profiling on) for the roofline
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            stack.x.copy_(xs[i])
+            stack.run(stream)
+        torch.cuda.synchronize()
+        fm.profile_read(reset=True)
+        fm.profile_enable(True)
+        nprof = 5
+        uniq = []
+        for i in range(nprof):
+            stack.x.copy_(xs[i])
+            stack.run(stream)
+            torch.cuda.synchronize()
+            uniq.append([int(torch.unique(ids).numel()) for ids in stack.ids])
+        fm.profile_enable(False)
+    prof = fm.profile_read(reset=True)
+
+    # capture one step
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        stack.x.copy_(xs[0])
+        stack.run(stream)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            stack.run(stream)
+    launches_per_step = sum(v[0] for v in prof.values()) // nprof
+
+    def timed(n, e2e, host_in=None, host_out=None):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(n):
+                if e2e:
+                    stack.x.copy_(host_in[i % host_in.shape[0]], non_blocking=True)
+                else:
+                    stack.x.copy_(xs[args.warmup + (i % args.steps)])
+                graph.replay()
+                if e2e:
+                    host_out.copy_(stack.ys[-1], non_blocking=True)
+            stop.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(stop)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            stack.x.copy_(xs[i])
+            graph.replay()
+    clocks = ClockSampler(local)
+    with clocks:
+        ms = timed(args.steps, False)
+    host_in = xs[: min(nin, 64)].cpu().pin_memory()
+    host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    timed(min(args.warmup, 3), True, host_in, host_out)
+    ms_e2e = timed(args.steps, True, host_in, host_out)
+
+    ms_step = ms / args.steps
+    value = world * T / (ms_step / 1e3)
+    e2e_value = world * T / (ms_e2e / args.steps / 1e3)
+
+    # roofline of the dominant kernel
+    peaks, peaks_kind = load_peaks()
+    name, (n_l, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+    avg_u = sum(sum(u) for u in uniq) / nprof  # unique experts per step summed over layers
+    if name == "moe_gate_up_kernel":
+        alg = avg_u * GATE_UP_BYTES / LAYERS + T * H * 2 + avg_u / LAYERS * T * I * 2
+    elif name == "moe_down_kernel":
+        alg = avg_u * DOWN_BYTES / LAYERS + T * H * 2
+    else:
+        alg = ROUTER_BYTES
+    achieved = alg / (tot_ms / n_l / 1e3) / 1e9
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "ncu_traffic.json")))
+        traffic = tr.get(args.workload, {}).get(name)
+    except Exception:
+        pass
+    step_bytes = avg_u * (GATE_UP_BYTES + DOWN_BYTES) + LAYERS * ROUTER_BYTES
+    result = {
+        "metric": "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u4-affine weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights MLX-affine 4-bit quantised; random init)",
+        "config": {"workload": args.workload, "layers": LAYERS, "hidden": H, "experts": E, "top_k": K,
+                   "expert_intermediate": I, "tokens_per_step": T, "router": "bf16",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (30 x 428 MB of experts resident)",
+                   "graph": "one CUDA graph per step"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2,
+                "api": "fmoe_moe_block_forward x30 (captured in a CUDA graph) + pinned host copies"},
+        "gpu_launches": launches_per_step * args.steps,
+        "step_weight_bytes": int(step_bytes),
+        "step_hbm_gbs": round(step_bytes / (ms_step / 1e3) / 1e9, 1),
+        "roofline": {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json hbm_gbs)" if peaks_kind == "measured"
+                     else "fallback 6.65 TB/s",
+                     "alg_bytes_per_launch": int(alg), "avg_launch_us": round(tot_ms / n_l * 1e3, 3),
+                     "traffic": traffic},
+        "kernels": {k: {"launches_per_step": v[0] // nprof, "avg_us": round(v[1] / v[0] * 1e3, 3)}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(layers, T)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    del graph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm (oracle port of the reference's path)
+
+
+def cpu_sample_setup(T, seed=4000):
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(seed)
+    x = oracle.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    wr = oracle.f32_to_bf16((rng.standard_normal((E, H)) * 0.02).astype(np.float32))
+    # one layer's 128 experts: the CPU time does not depend on the code values,
+    # so random codes with N(0.01, 0.001)-sized bf16 scales/biases stand in
+    offs, sizes, stride = ecb(H, I)
+    buf = rng.integers(0, 256, size=E * stride, dtype=np.uint8)
+    view = buf.reshape(E, stride)
+    for j in (1, 2, 4, 5, 7, 8):
+        n = sizes[j] // 2
+        sb = oracle.f32_to_bf16((0.01 + 0.001 * rng.standard_normal((E, n))).astype(np.float32))
+        view[:, offs[j]:offs[j] + sizes[j]] = sb.view(np.uint8).reshape(E, -1)
+    return x, wr, buf, offs, stride
+
+
+def ecb(hidden, inter):
+    sizes = [inter * hidden // 2, inter * hidden // 32, inter * hidden // 32] * 2 + \
+            [hidden * inter // 2, hidden * inter // 32, hidden * inter // 32]
+    offs = [0]
+    for s in sizes[:-1]:
+        offs.append(offs[-1] + s)
+    return offs, sizes, sum(sizes)
+
+
+def cpu_layer(x, wr, buf, offs, stride):
+    import oracle
+    ids, w, _ = oracle.router(x, wr, K)
+    oracle.moe_experts(x, ids, w, buf, stride, offs, H, I)
+
+
+def cpu_baseline(_layers, T, budget_s=10.0):
+    import oracle
+    x, wr, buf, offs, stride = cpu_sample_setup(T)
+    cpu_layer(x, wr, buf, offs, stride)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        cpu_layer(x, wr, buf, offs, stride)
+        n += 1
+    layer_s = (time.perf_counter() - t0) / n
+    return {"value": round(T / (LAYERS * layer_s), 3), "unit": "tok/s", "cores": oracle.num_threads(),
+            "kind": "port",
+            "sample": f"{n} MoE layers (router + 8 experts + combine) at T={T} on the oracle (C++ OpenMP, fp64 "
+                      f"accumulation), extrapolated to {LAYERS} layers"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import oracle
+    T = WORKLOADS[args.workload]
+    x, wr, buf, offs, stride = cpu_sample_setup(T)
+    for _ in range(args.warmup):
+        cpu_layer(x, wr, buf, offs, stride)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_layer(x, wr, buf, offs, stride)
+    layer_s = (time.perf_counter() - t0) / args.steps
+    value = T / (LAYERS * layer_s)
+    out = {
+        "impl": "reference",
+        "metric": "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)",
+        "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(layer_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u4-affine weights x bf16 activations, fp64 accumulate (CPU)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "layers": LAYERS, "tokens_per_step": T},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"each step = 1 of the {LAYERS} MoE layers at T={T}; tok/s extrapolated"},
+        "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Rust + MLX/Metal) cannot run here; this is the repository's C++ port of its "
+                "path (oracle/)",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,310 @@
+// extern "C" entry points of libfmoe (declared in include/fmoe.h): argument
+// validation, workspace carving and kernel sequencing.  No entry point
+// synchronises the stream or allocates device memory.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include "internal.h"
+
+namespace fmoe {
+
+static thread_local char g_err[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(FMOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return FMOE_OK;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int to_qw(const fmoe_qweight_t* w, QW* q) {
+  if (!w || !w->w) return set_error(FMOE_ERR_INVALID, "qweight: null weight");
+  if (w->out_features <= 0 || w->in_features <= 0) return set_error(FMOE_ERR_INVALID, "qweight: empty shape");
+  if (w->bits != 16) {
+    if (!w->scales || !w->biases) return set_error(FMOE_ERR_INVALID, "qweight: null scales/biases");
+    if (w->group_size <= 0 || w->in_features % w->group_size)
+      return set_error(FMOE_ERR_INVALID, "qweight: in_features %d not a multiple of group %d", w->in_features,
+                       w->group_size);
+  }
+  q->w = w->w;
+  q->s = static_cast<const bf16*>(w->scales);
+  q->b = static_cast<const bf16*>(w->biases);
+  q->out = w->out_features;
+  q->in = w->in_features;
+  q->bits = w->bits;
+  return FMOE_OK;
+}
+
+// Shapes the register-dequant GEMV kernels accept.
+static int check_gemv_weight(const QW& q, int group) {
+  if (q.bits != 16 && q.bits != 4 && q.bits != 8)
+    return set_error(FMOE_ERR_UNSUPPORTED, "gemv: bits=%d (kernels: 4, 8, 16=bf16)", q.bits);
+  if (q.bits != 16 && group != 64) return set_error(FMOE_ERR_UNSUPPORTED, "gemv: group_size %d (kernels: 64)", group);
+  if (q.in % 64 || q.out % 16)
+    return set_error(FMOE_ERR_UNSUPPORTED, "gemv: [out=%d, in=%d] needs in %% 64 == 0 and out %% 16 == 0", q.out, q.in);
+  if (!aligned(q.w, 16)) return set_error(FMOE_ERR_ALIGN, "gemv: weight not 16-byte aligned");
+  return FMOE_OK;
+}
+
+static int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
+  if (!e || !e->base) return set_error(FMOE_ERR_INVALID, "experts: null table");
+  if (e->bits != 4 || e->group_size != 64)
+    return set_error(FMOE_ERR_UNSUPPORTED, "experts: bits=%d group=%d (kernels: 4-bit, group 64)", e->bits,
+                     e->group_size);
+  if (e->hidden <= 0 || e->intermediate <= 0 || e->hidden % 64 || e->intermediate % 64)
+    return set_error(FMOE_ERR_UNSUPPORTED, "experts: hidden %d / intermediate %d must be multiples of 64", e->hidden,
+                     e->intermediate);
+  if (e->num_experts <= 0 || e->num_experts > 1024) return set_error(FMOE_ERR_INVALID, "experts: num_experts %d", e->num_experts);
+  if (!aligned(e->base, 16) || e->expert_stride % 16) return set_error(FMOE_ERR_ALIGN, "experts: base/stride not 16-byte aligned");
+  for (int j = 0; j < 9; ++j)
+    if (e->offsets[j] < 0 || e->offsets[j] % 8 || (j % 3 == 0 && e->offsets[j] % 16))
+      return set_error(FMOE_ERR_ALIGN, "experts: offset[%d]=%lld misaligned", j, (long long)e->offsets[j]);
+  d->base = static_cast<const uint8_t*>(e->base);
+  d->stride = e->expert_stride;
+  for (int j = 0; j < 9; ++j) d->off[j] = e->offsets[j];
+  d->E = e->num_experts;
+  d->first = e->first_expert;
+  d->H = e->hidden;
+  d->I = e->intermediate;
+  return FMOE_OK;
+}
+
+static const int kMaxDecodeTokens = 256;
+
+struct RouterWs {
+  bf16* xs;
+  float* partial;
+  int ksplit;
+};
+
+static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, RouterWs* w) {
+  const int H = r->proj.in_features, E = r->proj.out_features;
+  const int ks = gemv_ksplit(T, E, H);
+  bf16* xs = r->use_norm ? c.take<bf16>((size_t)T * H) : nullptr;
+  float* part = c.take<float>((size_t)ks * T * E);
+  if (w) *w = RouterWs{xs, part, ks};
+  return c.off;
+}
+
+static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, RouteMeta* m, bf16** act) {
+  RouteMeta mm;
+  mm.start = c.take<int32_t>(ex.E + 1);
+  mm.pairs = c.take<int32_t>((size_t)T * k);
+  mm.unique = c.take<int32_t>(ex.E);
+  mm.num_unique = c.take<int32_t>(1);
+  bf16* a = c.take<bf16>((size_t)T * k * ex.I);
+  if (m) *m = mm;
+  if (act) *act = a;
+  return c.off;
+}
+
+static int check_router(const fmoe_router_t* r, QW* q) {
+  if (!r) return set_error(FMOE_ERR_INVALID, "router: null");
+  int rc = to_qw(&r->proj, q);
+  if (rc) return rc;
+  rc = check_gemv_weight(*q, r->proj.group_size);
+  if (rc) return rc;
+  if (r->top_k < 1 || r->top_k > 16 || r->top_k > q->out) return set_error(FMOE_ERR_INVALID, "router: top_k %d", r->top_k);
+  return FMOE_OK;
+}
+
+static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int first_id,
+                      int32_t* ids, float* wts, float* logits, cudaStream_t st) {
+  const bf16* xin = x;
+  int rc;
+  if (r->use_norm) {
+    rc = launch_router_prenorm(x, T, q.in, r->root_size, r->eps, static_cast<const bf16*>(r->router_scale), w.xs, st);
+    if (rc) return rc;
+    xin = w.xs;
+  }
+  rc = launch_gemv_partial(xin, T, q, w.ksplit, w.partial, st);
+  if (rc) return rc;
+  return launch_router_topk(w.partial, w.ksplit, T, q.out, r->logit_bias, static_cast<const bf16*>(r->per_expert_scale),
+                            r->top_k, first_id, ids, wts, logits, st);
+}
+
+static int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
+                       bf16* y, Carver& c, cudaStream_t st) {
+  RouteMeta m;
+  bf16* act;
+  carve_moe(c, T, k, ex, &m, &act);
+  int rc = launch_route_build(ids, T * k, ex, m, st);
+  if (rc) return rc;
+  rc = launch_moe_gate_up(x, T, k, ex, m, act, st);
+  if (rc) return rc;
+  return launch_moe_down(act, T, k, wts, ex, m, y, st);
+}
+
+}  // namespace fmoe
+
+using namespace fmoe;
+
+extern "C" {
+
+int fmoe_version(void) { return 100; }
+
+int fmoe_last_error(char* buf, size_t len) {
+  const size_t n = strlen(g_err);
+  if (buf && len) {
+    const size_t c = n < len - 1 ? n : len - 1;
+    memcpy(buf, g_err, c);
+    buf[c] = 0;
+  }
+  return (int)n;
+}
+
+int fmoe_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits, int group_size, void* wq,
+                  void* scales, void* biases, void* stream) {
+  if (!src || !wq || !scales || !biases) return set_error(FMOE_ERR_INVALID, "quantize: null pointer");
+  if (!(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8))
+    return set_error(FMOE_ERR_INVALID, "quantize: bits=%d", bits);
+  if (group_size <= 0 || cols % group_size || (group_size * bits) % 32)
+    return set_error(FMOE_ERR_INVALID, "quantize: cols %lld / group %d", (long long)cols, group_size);
+  if (rows <= 0) return FMOE_OK;
+  return launch_quantize(src, src_is_bf16, rows, cols, bits, group_size, static_cast<uint32_t*>(wq),
+                         static_cast<bf16*>(scales), static_cast<bf16*>(biases), static_cast<cudaStream_t>(stream));
+}
+
+int fmoe_dequantize(const fmoe_qweight_t* w, void* out, void* stream) {
+  QW q;
+  int rc = to_qw(w, &q);
+  if (rc) return rc;
+  if (q.bits == 16) return set_error(FMOE_ERR_INVALID, "dequantize: weight is not quantised");
+  if (!out) return set_error(FMOE_ERR_INVALID, "dequantize: null out");
+  return launch_dequantize(q, w->group_size, nullptr, q.out, 1.0f, static_cast<bf16*>(out),
+                           static_cast<cudaStream_t>(stream));
+}
+
+int fmoe_embed_rows(const fmoe_qweight_t* w, const int32_t* ids, int64_t n, float row_scale, void* out, void* stream) {
+  QW q;
+  int rc = to_qw(w, &q);
+  if (rc) return rc;
+  if (!ids || !out) return set_error(FMOE_ERR_INVALID, "embed_rows: null ids/out");
+  if (n <= 0) return FMOE_OK;
+  return launch_dequantize(q, w->group_size, ids, n, row_scale, static_cast<bf16*>(out),
+                           static_cast<cudaStream_t>(stream));
+}
+
+size_t fmoe_router_workspace_bytes(int64_t T, const fmoe_router_t* r) {
+  if (!r || T <= 0) return 0;
+  Carver c(nullptr);
+  return carve_router(c, T, r, nullptr) + 256;
+}
+
+int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, float* weights, float* logits,
+                void* workspace, size_t workspace_bytes, void* stream) {
+  QW q;
+  int rc = check_router(r, &q);
+  if (rc) return rc;
+  if (!x || !ids || !weights) return set_error(FMOE_ERR_INVALID, "router: null x/ids/weights");
+  if (T <= 0) return FMOE_OK;
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "router: x not 16-byte aligned");
+  if (!workspace || workspace_bytes < fmoe_router_workspace_bytes(T, r))
+    return set_error(FMOE_ERR_WORKSPACE, "router: workspace %zu < %zu", workspace_bytes, fmoe_router_workspace_bytes(T, r));
+  Carver c(workspace);
+  RouterWs w;
+  carve_router(c, T, r, &w);
+  return run_router(static_cast<const bf16*>(x), T, r, q, w, 0, ids, weights, logits, static_cast<cudaStream_t>(stream));
+}
+
+size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w) {
+  if (!w || T <= 0 || w->out_features <= 0 || w->in_features < 64) return 0;
+  const int ks = gemv_ksplit(T, w->out_features, w->in_features);
+  return align_up(sizeof(float) * (size_t)ks * T * w->out_features, 256) + 256;
+}
+
+int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, void* workspace, size_t workspace_bytes,
+                 void* stream) {
+  QW q;
+  int rc = to_qw(w, &q);
+  if (rc) return rc;
+  rc = check_gemv_weight(q, w->group_size);
+  if (rc) return rc;
+  if (!x || !y) return set_error(FMOE_ERR_INVALID, "qlinear: null x/y");
+  if (T <= 0) return FMOE_OK;
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "qlinear: x not 16-byte aligned");
+  const size_t need = fmoe_qlinear_workspace_bytes(T, w);
+  if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "qlinear: workspace %zu < %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int ks = gemv_ksplit(T, q.out, q.in);
+  Carver c(workspace);
+  float* part = c.take<float>((size_t)ks * T * q.out);
+  rc = launch_gemv_partial(static_cast<const bf16*>(x), T, q, ks, part, st);
+  if (rc) return rc;
+  return launch_reduce_partials(part, ks, T * q.out, static_cast<bf16*>(y), nullptr, st);
+}
+
+size_t fmoe_moe_workspace_bytes(int64_t T, int top_k, const fmoe_experts_t* ex) {
+  ExpertsDev d;
+  if (T <= 0 || to_experts(ex, &d)) return 0;
+  Carver c(nullptr);
+  return carve_moe(c, T, top_k, d, nullptr, nullptr) + 256;
+}
+
+int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, const float* weights,
+                     const fmoe_experts_t* ex, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  ExpertsDev d;
+  int rc = to_experts(ex, &d);
+  if (rc) return rc;
+  if (!x || !ids || !weights || !y) return set_error(FMOE_ERR_INVALID, "moe_experts: null pointer");
+  if (T <= 0) return FMOE_OK;
+  if (top_k < 1 || top_k > 16) return set_error(FMOE_ERR_INVALID, "moe_experts: top_k %d", top_k);
+  if (T > kMaxDecodeTokens)
+    return set_error(FMOE_ERR_UNSUPPORTED, "moe_experts: T=%lld above the decode path's %d", (long long)T, kMaxDecodeTokens);
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "moe_experts: x not 16-byte aligned");
+  const size_t need = fmoe_moe_workspace_bytes(T, top_k, ex);
+  if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "moe_experts: workspace %zu < %zu", workspace_bytes, need);
+  Carver c(workspace);
+  return run_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<bf16*>(y), c,
+                     static_cast<cudaStream_t>(stream));
+}
+
+size_t fmoe_moe_block_workspace_bytes(int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex) {
+  ExpertsDev d;
+  if (T <= 0 || !r || to_experts(ex, &d)) return 0;
+  Carver c(nullptr);
+  carve_router(c, T, r, nullptr);
+  c.take<int32_t>((size_t)T * r->top_k);
+  c.take<float>((size_t)T * r->top_k);
+  return carve_moe(c, T, r->top_k, d, nullptr, nullptr) + 256;
+}
+
+int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex, void* y,
+                           int32_t* ids, float* weights, void* workspace, size_t workspace_bytes, void* stream) {
+  QW q;
+  int rc = check_router(r, &q);
+  if (rc) return rc;
+  ExpertsDev d;
+  rc = to_experts(ex, &d);
+  if (rc) return rc;
+  if (!x || !y) return set_error(FMOE_ERR_INVALID, "moe_block: null x/y");
+  if (T <= 0) return FMOE_OK;
+  if (q.in != d.H) return set_error(FMOE_ERR_INVALID, "moe_block: router in %d != hidden %d", q.in, d.H);
+  if (T > kMaxDecodeTokens)
+    return set_error(FMOE_ERR_UNSUPPORTED, "moe_block: T=%lld above the decode path's %d", (long long)T, kMaxDecodeTokens);
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "moe_block: x not 16-byte aligned");
+  const size_t need = fmoe_moe_block_workspace_bytes(T, r, ex);
+  if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "moe_block: workspace %zu < %zu", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  RouterWs w;
+  carve_router(c, T, r, &w);
+  int32_t* ids_ws = c.take<int32_t>((size_t)T * r->top_k);
+  float* w_ws = c.take<float>((size_t)T * r->top_k);
+  int32_t* ids_out = ids ? ids : ids_ws;
+  float* w_out = weights ? weights : w_ws;
+  rc = run_router(static_cast<const bf16*>(x), T, r, q, w, 0, ids_out, w_out, nullptr, st);
+  if (rc) return rc;
+  return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), c, st);
+}
+
+}  // extern "C"

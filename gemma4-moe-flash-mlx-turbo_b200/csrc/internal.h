@@ -1,0 +1,96 @@
+// Internal declarations shared by the libfmoe translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stddef.h>
+#include "../../include/fmoe.h"
+
+namespace fmoe {
+
+typedef __nv_bfloat16 bf16;
+
+// B200: 148 SMs.  Grids are sized from this (the ABI checks the device).
+constexpr int kNumSMs = 148;
+
+// Error reporting: records a per-thread message and returns `code`.
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+
+// RAII timing scope around one kernel launch (active only while
+// fmoe_profile_enable(1); see prof.cu).  Name = the kernel's symbol name.
+class ProfScope {
+ public:
+  ProfScope(const char* name, cudaStream_t st);
+  ~ProfScope();
+
+ private:
+  const char* name_;
+  cudaStream_t st_;
+  cudaEvent_t a_, b_;
+};
+
+// Device view of a linear weight.
+struct QW {
+  const void* w;
+  const bf16* s;
+  const bf16* b;
+  int out, in, bits;
+};
+
+// Device view of an ECB expert table.
+struct ExpertsDev {
+  const uint8_t* base;
+  int64_t stride;
+  int64_t off[9];
+  int E, first, H, I;
+};
+
+// Routing metadata built on the device from ids [T, k] (see moe.cu).
+struct RouteMeta {
+  int32_t* start;       // [E + 1] exclusive prefix of per-expert pair counts
+  int32_t* pairs;       // [T * k] pair index (t*k + slot), grouped by expert, ascending
+  int32_t* unique;      // [E] local ids of experts with >= 1 pair, ascending
+  int32_t* num_unique;  // [1]
+};
+
+// gemv.cu
+int gemv_ksplit(int64_t T, int out, int in);
+int launch_gemv_partial(const bf16* x, int64_t T, const QW& w, int ksplit, float* partial, cudaStream_t st);
+int launch_reduce_partials(const float* partial, int ksplit, int64_t n, bf16* out_bf16, float* out_f32,
+                           cudaStream_t st);
+int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps, const bf16* rscale, bf16* xs,
+                          cudaStream_t st);
+int launch_router_topk(const float* partial, int ksplit, int64_t T, int E, const float* bias, const bf16* pes, int k,
+                       int first_id, int32_t* ids, float* wts, float* logits, cudaStream_t st);
+
+// moe.cu
+int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, const RouteMeta& m, cudaStream_t st);
+int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, const RouteMeta& m, bf16* act,
+                       cudaStream_t st);
+int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
+                    bf16* y, cudaStream_t st);
+
+// quant.cu
+int launch_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits, int group, uint32_t* wq,
+                    bf16* s, bf16* b, cudaStream_t st);
+int launch_dequantize(const QW& w, int group, const int32_t* ids, int64_t n, float row_scale, bf16* out,
+                      cudaStream_t st);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Bump allocator over a caller workspace.
+struct Carver {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carver(void* p) : base(static_cast<uint8_t*>(p)) {}
+  template <class T>
+  T* take(size_t n) {
+    off = align_up(off, 256);
+    T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+}  // namespace fmoe

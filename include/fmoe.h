@@ -1,0 +1,170 @@
+/*
+ * libfmoe — C ABI of the B200 (sm_100a) quantised-MoE hot path of flash-moe.
+ *
+ * This is the seam a host engine binds to in place of flash-moe's MLX calls on
+ * the MoE / quantised-KV path and of its only native shim, src/ffi.rs:5-14
+ * (extern "C" mlx_array_from_mmap) / src/ffi_zerocopy.cpp:14-55.  Every entry
+ * point is a plain C function: device pointers, sizes, an explicit CUDA stream
+ * (passed as void*; NULL = legacy default stream) and an int status.
+ *
+ * Conventions
+ *   - bf16 tensors are raw 16-bit bfloat16 (RNE), row-major, no padding.
+ *   - MLX-affine quantised weight [out, in]: w uint32 [out, in*bits/32] holding
+ *     a little-endian bit stream of codes (value j at bits [j*bits,(j+1)*bits)),
+ *     scales / biases bf16 [out, in/group]; w ~= scale*q + bias.
+ *   - Status: 0 ok, negative FMOE_ERR_*; fmoe_last_error() gives the text of the
+ *     most recent failure on the calling thread.  No exceptions cross the ABI.
+ *   - The library never frees caller memory.  Calls are asynchronous on the
+ *     given stream; buffers must stay alive until the stream has passed them.
+ *   - Thread safety: entry points keep no global mutable state besides the
+ *     per-thread error text; concurrent calls are safe on distinct workspaces.
+ */
+#ifndef FMOE_H_
+#define FMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FMOE_OK 0
+#define FMOE_ERR_INVALID -1     /* bad argument, shape or bit width */
+#define FMOE_ERR_ALIGN -2       /* pointer or stride misaligned for the kernel */
+#define FMOE_ERR_WORKSPACE -3   /* workspace NULL or smaller than required */
+#define FMOE_ERR_CUDA -4        /* CUDA launch / runtime error */
+#define FMOE_ERR_UNSUPPORTED -5 /* configuration outside the compiled kernels */
+#define FMOE_ERR_TIMEOUT -6     /* a bounded device wait gave up */
+#define FMOE_ERR_NCCL -7        /* NCCL failure (expert parallelism) */
+#define FMOE_ERR_ALLOC -8       /* device allocation failed */
+
+/* MLX-affine quantised (bits 2/3/4/5/6/8) or plain bf16 (bits 16) linear
+ * weight [out_features, in_features].  Mirrors QuantizedLinear,
+ * src/model/mlp.rs:4-12. */
+typedef struct fmoe_qweight {
+  const void* w;      /* uint32 packed codes, or bf16 [out, in] when bits == 16 */
+  const void* scales; /* bf16 [out, in/group]; NULL when bits == 16 */
+  const void* biases; /* bf16 [out, in/group]; NULL when bits == 16 */
+  int32_t out_features;
+  int32_t in_features;
+  int32_t bits;
+  int32_t group_size;
+} fmoe_qweight_t;
+
+/* Routed experts of one MoE layer in the ECB expert-major layout written by
+ * src/splitter.rs:405-457 and read by src/memory.rs:571-607: expert e's
+ * tensor j is at base + e*expert_stride + offsets[j], j in the order
+ * gate.w gate.s gate.b up.w up.s up.b down.w down.s down.b.
+ * gate/up: [intermediate, hidden]; down: [hidden, intermediate]. */
+typedef struct fmoe_experts {
+  const void* base;
+  int64_t expert_stride;
+  int64_t offsets[9];
+  int32_t num_experts;  /* experts present in this table (local shard) */
+  int32_t first_expert; /* global id of the table's expert 0 (0 unless sharded) */
+  int32_t hidden;
+  int32_t intermediate;
+  int32_t bits;
+  int32_t group_size;
+} fmoe_experts_t;
+
+/* Router of Gemma4MoeBlock, src/model/moe.rs:298-312 / 324-345. */
+typedef struct fmoe_router {
+  fmoe_qweight_t proj;          /* router_proj [num_experts, hidden] */
+  const void* router_scale;     /* bf16 [hidden] or NULL (applied only when use_norm) */
+  const void* per_expert_scale; /* bf16 [num_experts] or NULL */
+  const float* logit_bias;      /* f32 [num_experts] or NULL; added to logits */
+  float root_size;              /* hidden^-1/2 (used when use_norm) */
+  float eps;                    /* rms_norm_eps (used when use_norm) */
+  int32_t use_norm;             /* 1: rms_norm_no_scale -> *root_size -> *router_scale */
+  int32_t top_k;                /* experts per token (<= 16) */
+} fmoe_router_t;
+
+/* ---- library -------------------------------------------------------- */
+
+/* Version as major*10000 + minor*100 + patch. */
+int fmoe_version(void);
+
+/* Copies the calling thread's most recent error text (NUL-terminated, truncated
+ * to len) and returns its full length. */
+int fmoe_last_error(char* buf, size_t len);
+
+/* Per-kernel device timing (replaces the reference's host-side phase
+ * accumulators, src/perf.rs:65-153).  While enabled, each kernel launch is
+ * bracketed by CUDA events on its stream (do not enable during stream
+ * capture).  fmoe_profile_read synchronises on the recorded events, folds them
+ * into per-kernel totals, copies up to max_entries of them and returns the
+ * number of distinct kernels (or a negative status); reset != 0 clears them. */
+typedef struct fmoe_kernel_stat {
+  char name[64];
+  int64_t launches;
+  double total_ms;
+} fmoe_kernel_stat_t;
+int fmoe_profile_enable(int on);
+int fmoe_profile_read(fmoe_kernel_stat_t* out, int max_entries, int reset);
+
+/* ---- quantisation (mlx::core::quantize / dequantize) ------------------ */
+
+/* MLX-affine quantisation of a row-major [rows, cols] matrix (fp32 when
+ * src_is_bf16 == 0, else bf16): per group, scale = (max-min)/(2^bits-1) and
+ * bias = min (both rounded to bf16), q = clamp(rint((w-bias)/scale)).
+ * Replaces mlx quantize at src/model/mod.rs:673.  bits in {2,3,4,5,6,8}. */
+int fmoe_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits,
+                  int group_size, void* wq, void* scales, void* biases, void* stream);
+
+/* out bf16 [out, in] = bf16(fma(scale, q, bias)).  Replaces mlx dequantize at
+ * src/model/mod.rs:149 and mod.rs:666-670. */
+int fmoe_dequantize(const fmoe_qweight_t* w, void* out, void* stream);
+
+/* Embedding lookup: out bf16 [n, in] = dequantize(rows ids[i]) * row_scale.
+ * Replaces take + dequantize + (x sqrt(hidden)) at src/model/mod.rs:145-160. */
+int fmoe_embed_rows(const fmoe_qweight_t* w, const int32_t* ids, int64_t n, float row_scale,
+                    void* out, void* stream);
+
+/* y bf16 [T, out] = x bf16 [T, in] . W^T.  Replaces QuantizedLinear::forward,
+ * src/model/mlp.rs:15-25 (mlx quantized_matmul, transpose=true).  Kernels:
+ * bits 4, 8 and 16 (bf16), group 64, in % 64 == 0, out % 16 == 0.  The
+ * workspace holds split-K partial sums (fmoe_qlinear_workspace_bytes). */
+size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w);
+int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* ---- MoE ------------------------------------------------------------ */
+
+/* Router, src/model/moe.rs:324-345.  x bf16 [T, hidden].  Writes ids int32
+ * [T, top_k] (global expert ids, descending logit, ties -> lower id) and
+ * weights f32 [T, top_k] (softmax over the selected logits, i.e. the
+ * renormalised top-k probabilities, times per_expert_scale).  logits (f32
+ * [T, num_experts]) may be NULL.  Needs fmoe_router_workspace_bytes(T, r). */
+size_t fmoe_router_workspace_bytes(int64_t T, const fmoe_router_t* r);
+int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, float* weights,
+                float* logits, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace for fmoe_moe_experts with T tokens (routing lists + the gated
+ * intermediate activations); no initialisation needed. */
+size_t fmoe_moe_workspace_bytes(int64_t T, int top_k, const fmoe_experts_t* ex);
+
+/* Routed experts + weighted combine, src/model/moe.rs:361-466 (unique/dedup
+ * of the selected experts, per-expert 4-bit GELU-gated MLP, weighted sum):
+ *   y[t] = sum_j weights[t,j] * down(gelu_tanh(gate.x[t]) * up.x[t]) of expert ids[t,j].
+ * x bf16 [T, hidden]; ids int32 [T, top_k] global ids (ids outside the table's
+ * [first_expert, first_expert+num_experts) contribute nothing); weights f32;
+ * y bf16 [T, hidden].  No host synchronisation. */
+int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, const float* weights,
+                     const fmoe_experts_t* ex, void* y, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Gemma4MoeBlock::forward, src/model/moe.rs:315-470: router + experts in one
+ * call.  ids / weights (may be NULL) receive the routing.  Workspace:
+ * fmoe_moe_block_workspace_bytes. */
+size_t fmoe_moe_block_workspace_bytes(int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex);
+int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex,
+                           void* y, int32_t* ids, float* weights, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FMOE_H_ */

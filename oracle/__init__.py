@@ -1,0 +1,204 @@
+"""CPU oracle for libfmoe — TEST INFRASTRUCTURE ONLY.
+
+numpy/ctypes front end of fmoe_oracle.cpp, a C++ restatement of the arithmetic
+flash-moe's MoE / KV-cache path performs through MLX (each C function cites the
+reference call site it follows).  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg may use it, and only as the checker.
+
+PARITY UNPINNED: the reference ships no tests, golden vectors or fixtures, and
+its arithmetic lives in MLX (mlx-rs 0.25.3 / mlx-sys 0.2.0), which cannot run
+here; see fmoe_oracle.cpp's header for the numeric definitions fixed instead.
+bf16 arrays are carried as numpy uint16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        path = _build.OUT
+        if not os.path.exists(path):
+            _build.build()
+        _lib = ctypes.CDLL(path)
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def num_threads() -> int:
+    return lib().orc_num_threads()
+
+
+def set_num_threads(n: int) -> None:
+    lib().orc_set_num_threads(ctypes.c_int(n))
+
+
+def f32_to_bf16(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_bf16(_p(x), ctypes.c_int64(x.size), _p(y))
+    return y
+
+
+def bf16_to_f32(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    y = np.empty(x.shape, np.float32)
+    lib().orc_bf16_to_f32(_p(x), ctypes.c_int64(x.size), _p(y))
+    return y
+
+
+def quantize(w: np.ndarray, bits: int, group: int = 64):
+    """MLX-affine quantisation of fp32 [rows, cols] -> (wq uint32, scales bf16, biases bf16)."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    wq = np.zeros((rows, cols * bits // 32), np.uint32)
+    s = np.empty((rows, cols // group), np.uint16)
+    b = np.empty_like(s)
+    lib().orc_quantize(_p(w), ctypes.c_int64(rows), ctypes.c_int64(cols), bits, group, _p(wq), _p(s), _p(b))
+    return wq, s, b
+
+
+def dequantize(wq, s, b, cols: int, bits: int, group: int = 64) -> np.ndarray:
+    wq = np.ascontiguousarray(wq, dtype=np.uint32)
+    rows = wq.shape[0]
+    out = np.empty((rows, cols), np.uint16)
+    lib().orc_dequantize(_p(wq), _p(np.ascontiguousarray(s)), _p(np.ascontiguousarray(b)), ctypes.c_int64(rows),
+                         ctypes.c_int64(cols), bits, group, _p(out))
+    return out
+
+
+def qmatmul(x_bf16, wq, s, b, in_features: int, bits: int, group: int = 64) -> np.ndarray:
+    """fp32 [T, out] = x . W^T (exact per-group form, double accumulation)."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    T = x.shape[0]
+    out = wq.shape[0]
+    y = np.empty((T, out), np.float32)
+    lib().orc_qmatmul(_p(x), ctypes.c_int64(T), _p(np.ascontiguousarray(wq, np.uint32)), _p(np.ascontiguousarray(s)),
+                      _p(np.ascontiguousarray(b)), ctypes.c_int64(out), ctypes.c_int64(in_features), bits, group, _p(y))
+    return y
+
+
+def matmul_bf16(x_bf16, w_bf16) -> np.ndarray:
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    w = np.ascontiguousarray(w_bf16, np.uint16)
+    y = np.empty((x.shape[0], w.shape[0]), np.float32)
+    lib().orc_matmul_bf16(_p(x), ctypes.c_int64(x.shape[0]), _p(w), ctypes.c_int64(w.shape[0]),
+                          ctypes.c_int64(w.shape[1]), _p(y))
+    return y
+
+
+def router(x_bf16, wr, k: int, wr_bits: int = 16, wr_s=None, wr_b=None, group=64, logit_bias=None, use_norm=False,
+           root_size=0.0, eps=1e-6, router_scale=None, per_expert_scale=None):
+    """Gemma4MoeBlock router (src/model/moe.rs:324-345) -> (ids, weights, logits)."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    T, H = x.shape
+    E = wr.shape[0]
+    ids = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    lg = np.empty((T, E), np.float32)
+    lib().orc_router(_p(x), T, H, E, _p(np.ascontiguousarray(wr)), _p(wr_s), _p(wr_b), wr_bits, group,
+                     _p(None if logit_bias is None else np.ascontiguousarray(logit_bias, np.float32)), int(use_norm),
+                     ctypes.c_float(root_size), ctypes.c_float(eps),
+                     _p(None if router_scale is None else np.ascontiguousarray(router_scale, np.uint16)),
+                     _p(None if per_expert_scale is None else np.ascontiguousarray(per_expert_scale, np.uint16)), k,
+                     _p(ids), _p(w), _p(lg))
+    return ids, w, lg
+
+
+def moe_experts(x_bf16, ids, weights, expert_buf: np.ndarray, stride: int, offsets, hidden: int, inter: int, bits=4,
+                group=64, want_act=False):
+    """Routed experts + combine (src/model/moe.rs:424-466) -> (y fp32, y bf16[, act bf16 [T,k,I]])."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    T = x.shape[0]
+    k = ids.shape[1]
+    y32 = np.empty((T, hidden), np.float32)
+    y16 = np.empty((T, hidden), np.uint16)
+    act = np.empty((T, k, inter), np.uint16) if want_act else None
+    offs = (ctypes.c_int64 * 9)(*offsets)
+    lib().orc_moe_experts(_p(x), T, hidden, inter, k, _p(np.ascontiguousarray(ids, np.int32)),
+                          _p(np.ascontiguousarray(weights, np.float32)), _p(np.ascontiguousarray(expert_buf, np.uint8)),
+                          ctypes.c_int64(stride), offs, bits, group, _p(y32), _p(y16), _p(act))
+    return (y32, y16, act) if want_act else (y32, y16)
+
+
+def hadamard(n: int) -> np.ndarray:
+    h = np.empty((n, n), np.float32)
+    lib().orc_hadamard(n, _p(h))
+    return h
+
+
+def signs(n: int, seed: int = 42) -> np.ndarray:
+    s = np.empty(n, np.float32)
+    lib().orc_signs(n, ctypes.c_uint64(seed), _p(s))
+    return s
+
+
+def lloyd_max(bits: int):
+    c = np.empty(16, np.float32)
+    b = np.empty(15, np.float32)
+    n = lib().orc_lloyd_max(bits, _p(c), _p(b))
+    return c[:n].copy(), b[:n - 1].copy()
+
+
+def turbo_round_trip(v_bf16, bits: int):
+    """TurboQuant round trip (src/cache.rs:94-129) of rows [..., D] -> (out bf16, idx uint8, norms f32)."""
+    v = np.ascontiguousarray(v_bf16, np.uint16)
+    D = v.shape[-1]
+    rows = v.size // D
+    out = np.empty(v.shape, np.uint16)
+    idx = np.empty(v.shape, np.uint8)
+    nrm = np.empty(v.shape[:-1], np.float32)
+    lib().orc_turbo_round_trip(_p(v), ctypes.c_int64(rows), D, bits, _p(out), _p(idx), _p(nrm))
+    return out, idx, nrm
+
+
+def wht_rows(x_f32) -> np.ndarray:
+    x = np.ascontiguousarray(x_f32, np.float32)
+    D = x.shape[-1]
+    out = np.empty_like(x)
+    lib().orc_wht_rows(_p(x), ctypes.c_int64(x.size // D), D, _p(out))
+    return out
+
+
+def kv_quant_affine(v_bf16, bits: int, group: int = 64):
+    """WHT-rotate then MLX-affine quantise rows [..., D] -> (wq, scales, biases)."""
+    v = np.ascontiguousarray(v_bf16, np.uint16)
+    D = v.shape[-1]
+    rows = v.size // D
+    wq = np.zeros((rows, D * bits // 32), np.uint32)
+    s = np.empty((rows, D // group), np.uint16)
+    b = np.empty_like(s)
+    lib().orc_kv_quant_affine(_p(v), ctypes.c_int64(rows), D, bits, group, _p(wq), _p(s), _p(b))
+    return wq, s, b
+
+
+def attn_decode_affine(q_bf16, Hkv, Tcap, t_lo, t_hi, kq, ks, kb, kbits, vq, vs, vb, vbits, scale, group=64):
+    q = np.ascontiguousarray(q_bf16, np.uint16)
+    B, Hq, D = q.shape
+    out = np.empty((B, Hq, D), np.float32)
+    lib().orc_attn_decode_affine(_p(q), B, Hq, Hkv, D, ctypes.c_int64(Tcap), _p(np.ascontiguousarray(t_lo, np.int32)),
+                                 _p(np.ascontiguousarray(t_hi, np.int32)), _p(kq), _p(ks), _p(kb), kbits, _p(vq), _p(vs),
+                                 _p(vb), vbits, group, ctypes.c_float(scale), _p(out))
+    return out
+
+
+def attn_decode_bf16(q_bf16, Hkv, Tcap, t_lo, t_hi, k_bf16, v_bf16, scale, tau=0.0):
+    q = np.ascontiguousarray(q_bf16, np.uint16)
+    B, Hq, D = q.shape
+    out = np.empty((B, Hq, D), np.float32)
+    lib().orc_attn_decode_bf16(_p(q), B, Hq, Hkv, D, ctypes.c_int64(Tcap), _p(np.ascontiguousarray(t_lo, np.int32)),
+                               _p(np.ascontiguousarray(t_hi, np.int32)), _p(np.ascontiguousarray(k_bf16, np.uint16)),
+                               _p(np.ascontiguousarray(v_bf16, np.uint16)), ctypes.c_float(scale), ctypes.c_float(tau),
+                               _p(out))
+    return out
