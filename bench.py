@@ -143,7 +143,7 @@ class MoeStack:
         self.ec = [l.experts.cstruct() for l in layers]
         nbytes = max(fm.lib().fmoe_moe_block_workspace_bytes(T, ctypes.byref(r), ctypes.byref(e))
                      for r, e in zip(self.rc, self.ec))
-        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)  # router counters start at zero
         self.layers = layers
 
     def run(self, stream):

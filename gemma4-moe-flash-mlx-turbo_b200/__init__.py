@@ -172,14 +172,15 @@ def _need_cuda(*ts):
 
 
 class _Workspace:
-    """Grow-only device scratch buffer."""
+    """Grow-only device scratch buffer, zero-filled when (re)allocated: the
+    router keeps completion counters in it that every call leaves at zero."""
 
     def __init__(self):
         self.buf = None
 
     def get(self, nbytes: int, device) -> torch.Tensor:
         if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
-            self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            self.buf = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=device)
         return self.buf
 
 

@@ -78,20 +78,26 @@ static int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
   return FMOE_OK;
 }
 
-static const int kMaxDecodeTokens = 256;
+static const int kMaxDecodeTokens = 128;
 
 struct RouterWs {
+  unsigned* counters;  // [1 + token chunks], zero between calls
   bf16* xs;
   float* partial;
   int ksplit;
 };
 
+static int router_ksplit(int64_t T, int E, int H) {
+  return gemv_ksplit(T, (E + 15) / 16 * 16, H);
+}
+
 static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, RouterWs* w) {
   const int H = r->proj.in_features, E = r->proj.out_features;
-  const int ks = gemv_ksplit(T, E, H);
+  const int ks = router_ksplit(T, E, H);
+  unsigned* ctr = c.take<unsigned>(1 + (size_t)(T + 7) / 8);
   bf16* xs = r->use_norm ? c.take<bf16>((size_t)T * H) : nullptr;
   float* part = c.take<float>((size_t)ks * T * E);
-  if (w) *w = RouterWs{xs, part, ks};
+  if (w) *w = RouterWs{ctr, xs, part, ks};
   return c.off;
 }
 
@@ -111,34 +117,38 @@ static int check_router(const fmoe_router_t* r, QW* q) {
   if (!r) return set_error(FMOE_ERR_INVALID, "router: null");
   int rc = to_qw(&r->proj, q);
   if (rc) return rc;
-  rc = check_gemv_weight(*q, r->proj.group_size);
-  if (rc) return rc;
+  if (q->bits != 16 && q->bits != 4 && q->bits != 8)
+    return set_error(FMOE_ERR_UNSUPPORTED, "router: bits=%d (kernels: 4, 8, 16=bf16)", q->bits);
+  if (q->bits != 16 && r->proj.group_size != 64)
+    return set_error(FMOE_ERR_UNSUPPORTED, "router: group_size %d (kernels: 64)", r->proj.group_size);
+  if (q->in % 64) return set_error(FMOE_ERR_UNSUPPORTED, "router: hidden %d not a multiple of 64", q->in);
+  if (!aligned(q->w, 16)) return set_error(FMOE_ERR_ALIGN, "router: weight not 16-byte aligned");
   if (r->top_k < 1 || r->top_k > 16 || r->top_k > q->out) return set_error(FMOE_ERR_INVALID, "router: top_k %d", r->top_k);
   return FMOE_OK;
 }
 
-static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int first_id,
-                      int32_t* ids, float* wts, float* logits, cudaStream_t st) {
+// meta != nullptr: the router kernel also builds the per-expert pair lists.
+static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
+                      float* wts, float* logits, const RouteMeta* meta, cudaStream_t st) {
   const bf16* xin = x;
-  int rc;
   if (r->use_norm) {
-    rc = launch_router_prenorm(x, T, q.in, r->root_size, r->eps, static_cast<const bf16*>(r->router_scale), w.xs, st);
+    const int rc =
+        launch_router_prenorm(x, T, q.in, r->root_size, r->eps, static_cast<const bf16*>(r->router_scale), w.xs, st);
     if (rc) return rc;
     xin = w.xs;
   }
-  rc = launch_gemv_partial(xin, T, q, w.ksplit, w.partial, st);
-  if (rc) return rc;
-  return launch_router_topk(w.partial, w.ksplit, T, q.out, r->logit_bias, static_cast<const bf16*>(r->per_expert_scale),
-                            r->top_k, first_id, ids, wts, logits, st);
+  return launch_router_fused(xin, T, q, w.ksplit, w.partial, r->logit_bias,
+                             static_cast<const bf16*>(r->per_expert_scale), r->top_k, ids, wts, logits, w.counters,
+                             meta, st);
 }
 
 static int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
-                       bf16* y, Carver& c, cudaStream_t st) {
-  RouteMeta m;
-  bf16* act;
-  carve_moe(c, T, k, ex, &m, &act);
-  int rc = launch_route_build(ids, T * k, ex, m, st);
-  if (rc) return rc;
+                       bf16* y, const RouteMeta& m, bf16* act, bool build_routes, cudaStream_t st) {
+  int rc;
+  if (build_routes) {
+    rc = launch_route_build(ids, T * k, ex, m, st);
+    if (rc) return rc;
+  }
   rc = launch_moe_gate_up(x, T, k, ex, m, act, st);
   if (rc) return rc;
   return launch_moe_down(act, T, k, wts, ex, m, y, st);
@@ -213,7 +223,8 @@ int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, 
   Carver c(workspace);
   RouterWs w;
   carve_router(c, T, r, &w);
-  return run_router(static_cast<const bf16*>(x), T, r, q, w, 0, ids, weights, logits, static_cast<cudaStream_t>(stream));
+  return run_router(static_cast<const bf16*>(x), T, r, q, w, ids, weights, logits, nullptr,
+                    static_cast<cudaStream_t>(stream));
 }
 
 size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w) {
@@ -264,7 +275,10 @@ int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, co
   const size_t need = fmoe_moe_workspace_bytes(T, top_k, ex);
   if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "moe_experts: workspace %zu < %zu", workspace_bytes, need);
   Carver c(workspace);
-  return run_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<bf16*>(y), c,
+  RouteMeta m;
+  bf16* act;
+  carve_moe(c, T, top_k, d, &m, &act);
+  return run_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<bf16*>(y), m, act, true,
                      static_cast<cudaStream_t>(stream));
 }
 
@@ -302,9 +316,15 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
   float* w_ws = c.take<float>((size_t)T * r->top_k);
   int32_t* ids_out = ids ? ids : ids_ws;
   float* w_out = weights ? weights : w_ws;
-  rc = run_router(static_cast<const bf16*>(x), T, r, q, w, 0, ids_out, w_out, nullptr, st);
+  RouteMeta m;
+  bf16* act;
+  carve_moe(c, T, r->top_k, d, &m, &act);
+  if (q.out != d.E || d.first != 0)
+    return set_error(FMOE_ERR_INVALID, "moe_block: router has %d experts, table %d (first %d)", q.out, d.E, d.first);
+  rc = run_router(static_cast<const bf16*>(x), T, r, q, w, ids_out, w_out, nullptr, &m, st);
   if (rc) return rc;
-  return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), c, st);
+  return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), m, act, false,
+                     st);
 }
 
 }  // extern "C"

@@ -97,6 +97,28 @@ __device__ __forceinline__ uint4 ld_u4(const void* p) {
   return r;
 }
 
+// Asynchronous 16-byte global -> shared copies (LDGSTS), bypassing L1.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+// Copy `bytes` (multiple of 16, both addresses 16-byte aligned) with the
+// `nthr` threads of index `tid`.
+__device__ __forceinline__ void cp_async_block(void* smem, const void* gmem, int bytes, int tid, int nthr) {
+  uint8_t* d = static_cast<uint8_t*>(smem);
+  const uint8_t* s = static_cast<const uint8_t*>(gmem);
+  for (int o = tid * 16; o < bytes; o += nthr * 16) cp_async16(d + o, s + o);
+}
+
+__device__ __forceinline__ uint2 lds_u2(const void* p) { return *static_cast<const uint2*>(p); }
+__device__ __forceinline__ float lds_bf(const bf16* p) { return __bfloat162float(*p); }
+
 // B fragments for one 64-wide group of one token, 4-bit weight order.
 // Lane t holds x[16t .. 16t+15] of the group as X[0..7] (bf16 pairs); the
 // 4-bit A side puts codes (s, s+4) of a word in one register, so step s uses

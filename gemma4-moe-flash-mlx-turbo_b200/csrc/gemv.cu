@@ -9,6 +9,7 @@
 // deterministic run to run.
 #include "internal.h"
 #include "gemv.cuh"
+#include "route.cuh"
 
 namespace fmoe {
 
@@ -85,17 +86,15 @@ __global__ void router_prenorm_kernel(const bf16* __restrict__ x, int H, float r
   }
 }
 
-// One warp per token: logits = sum of K-slices (+ bias); top-k by value
-// (ties -> lower id); weights = softmax over the k selected logits (equal to
-// softmax(all)[ids] / sum softmax(all)[ids], src/model/moe.rs:331-340), times
-// per_expert_scale (moe.rs:341-345).  E <= 32 * kTopkPerLane.
-constexpr int kTopkPerLane = 8;
-__global__ void router_topk_kernel(const float* __restrict__ partial, int ksplit, int T, int E,
-                                   const float* __restrict__ bias, const bf16* __restrict__ pes, int k,
-                                   int first_id, int32_t* __restrict__ ids, float* __restrict__ wts,
-                                   float* __restrict__ logits_out) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (warp >= T) return;
+// Top-k of one token, one warp: logits = sum of the K-slice partials (+ bias);
+// top-k by value (ties -> lower id); weights = softmax over the k selected
+// logits (equal to softmax(all)[ids] / sum softmax(all)[ids],
+// src/model/moe.rs:331-340), times per_expert_scale (moe.rs:341-345).
+// Partials are read through L2: other CTAs of the same kernel wrote them.
+constexpr int kTopkPerLane = 8;  // E <= 256
+__device__ void topk_token(const float* partial, int ksplit, int T, int E, int tkn, const float* bias, const bf16* pes,
+                           int k, int first_id, int32_t* ids, float* wts, float* logits_out) {
+  const int lane = threadIdx.x & 31;
   float v[kTopkPerLane];
 #pragma unroll
   for (int j = 0; j < kTopkPerLane; ++j) {
@@ -103,14 +102,14 @@ __global__ void router_topk_kernel(const float* __restrict__ partial, int ksplit
     float s = -INFINITY;
     if (e < E) {
       s = 0.f;
-      for (int kz = 0; kz < ksplit; ++kz) s += partial[((int64_t)kz * T + warp) * E + e];
+      for (int kz = 0; kz < ksplit; ++kz) s += __ldcg(partial + ((int64_t)kz * T + tkn) * E + e);
       if (bias) s += bias[e];
-      if (logits_out) logits_out[(int64_t)warp * E + e] = s;
+      if (logits_out) logits_out[(int64_t)tkn * E + e] = s;
     }
     v[j] = s;
   }
-  float sel_v[16];
-  int sel_e[16];
+  float mx = 0.f, den = 0.f, my_v = 0.f;
+  int my_e = 0;
   for (int r = 0; r < k; ++r) {
     float bv = -INFINITY;
     int be = 0x7fffffff;
@@ -122,6 +121,7 @@ __global__ void router_topk_kernel(const float* __restrict__ partial, int ksplit
         be = e;
       }
     }
+#pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oe = __shfl_xor_sync(0xffffffffu, be, o);
@@ -130,23 +130,79 @@ __global__ void router_topk_kernel(const float* __restrict__ partial, int ksplit
         be = oe;
       }
     }
-    sel_v[r] = bv;
-    sel_e[r] = be;
+    if (r == 0) mx = bv;
+    den += expf(bv - mx);
+    if (lane == r) {
+      my_v = bv;
+      my_e = be;
+    }
 #pragma unroll
     for (int j = 0; j < kTopkPerLane; ++j)
       if (lane + 32 * j == be) v[j] = -INFINITY;
   }
-  if (lane == 0) {
-    const float mx = sel_v[0];
-    float den = 0.f;
-    for (int r = 0; r < k; ++r) den += expf(sel_v[r] - mx);
-    for (int r = 0; r < k; ++r) {
-      float wv = expf(sel_v[r] - mx) / den;
-      if (pes) wv *= bf2f(pes[sel_e[r]]);
-      ids[(int64_t)warp * k + r] = sel_e[r] + first_id;
-      wts[(int64_t)warp * k + r] = wv;
+  if (lane < k) {
+    float wv = expf(my_v - mx) / den;
+    if (pes) wv *= bf2f(pes[my_e]);
+    ids[(int64_t)tkn * k + lane] = my_e + first_id;
+    wts[(int64_t)tkn * k + lane] = wv;
+  }
+}
+
+// Fused router: CTA (16-expert tile, 8-token chunk, K slice) computes its
+// partial logits; the last CTA to finish a token chunk (completion counter)
+// runs the chunk's top-k; the last chunk to finish builds the per-expert pair
+// lists for the expert kernels when `meta.start` is set.  Counters return to
+// zero at the end of every call.
+template <int BITS>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    router_fused_kernel(const bf16* __restrict__ x, int T, int in, int E, const void* __restrict__ w,
+                        const bf16* __restrict__ sc, const bf16* __restrict__ bi, int ksplit, float* partial,
+                        const float* __restrict__ bias, const bf16* __restrict__ pes, int k, int32_t* ids, float* wts,
+                        float* logits_out, unsigned* counters, RouteMeta meta) {
+  extern __shared__ int rsm[];
+  __shared__ float red[kGemvWarps][16][8];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int row0 = blockIdx.x * 16, tok0 = blockIdx.y * 8, kz = blockIdx.z;
+  const int G = in / 64;
+  const int gbeg = (int)((int64_t)G * kz / ksplit), gend = (int)((int64_t)G * (kz + 1) / ksplit);
+  const int wpr = in * BITS / 32;
+  const bf16* xrow = (tok0 + g < T) ? x + (int64_t)(tok0 + g) * in : nullptr;
+  float y[4] = {0.f, 0.f, 0.f, 0.f};
+  warp_tile_gemv<BITS>(y, w, sc, bi, min(row0 + g, E - 1), min(row0 + g + 8, E - 1), wpr, G, xrow, gbeg + warp, gend,
+                       kGemvWarps, t);
+  red[warp][g][2 * t] = y[0];
+  red[warp][g][2 * t + 1] = y[1];
+  red[warp][g + 8][2 * t] = y[2];
+  red[warp][g + 8][2 * t + 1] = y[3];
+  __syncthreads();
+  {
+    const int i = threadIdx.x, tk = i >> 4, r = i & 15;
+    if (tok0 + tk < T && row0 + r < E) {
+      float s = 0.f;
+#pragma unroll
+      for (int wi = 0; wi < kGemvWarps; ++wi) s += red[wi][r][tk];
+      partial[((int64_t)kz * T + tok0 + tk) * E + row0 + r] = s;
     }
   }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&counters[1 + blockIdx.y], 1u) == gridDim.x * gridDim.z - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int tk = warp; tk < 8; tk += kGemvWarps)
+    if (tok0 + tk < T) topk_token(partial, ksplit, T, E, tok0 + tk, bias, pes, k, 0, ids, wts, logits_out);
+  if (threadIdx.x == 0) counters[1 + blockIdx.y] = 0;
+  if (!meta.start) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&counters[0], 1u) == gridDim.y - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  route_build_block(ids, T * k, 0, E, meta.start, meta.pairs, meta.unique, meta.num_unique, rsm);
+  if (threadIdx.x == 0) counters[0] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -209,18 +265,29 @@ int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps
   return check_launch("router_prenorm_kernel");
 }
 
-int launch_router_topk(const float* partial, int ksplit, int64_t T, int E, const float* bias, const bf16* pes, int k,
-                       int first_id, int32_t* ids, float* wts, float* logits, cudaStream_t st) {
+int launch_router_fused(const bf16* x, int64_t T, const QW& w, int ksplit, float* partial, const float* bias,
+                        const bf16* pes, int k, int32_t* ids, float* wts, float* logits, unsigned* counters,
+                        const RouteMeta* meta, cudaStream_t st) {
+  const int E = w.out;
   if (E > 32 * kTopkPerLane) return set_error(FMOE_ERR_UNSUPPORTED, "router: num_experts %d > %d", E, 32 * kTopkPerLane);
   if (k < 1 || k > 16 || k > E) return set_error(FMOE_ERR_INVALID, "router: top_k %d out of range", k);
-  const int warps_per_block = 4;
-  const unsigned blocks = (unsigned)((T + warps_per_block - 1) / warps_per_block);
-  {
-    ProfScope prof_("router_topk_kernel", st);
-    router_topk_kernel<<<blocks, warps_per_block * 32, 0, st>>>(partial, ksplit, (int)T, E, bias, pes, k, first_id, ids,
-                                                              wts, logits);
+  dim3 grid((E + 15) / 16, (unsigned)((T + 7) / 8), ksplit);
+  RouteMeta m = meta ? *meta : RouteMeta{nullptr, nullptr, nullptr, nullptr};
+  const size_t smem = meta ? sizeof(int) * (kGemvWarps + 1) * (size_t)E : 0;
+#define FMOE_ROUTER_LAUNCH(B)                                                                                          \
+  {                                                                                                                    \
+    ProfScope prof_("router_fused_kernel<" #B ">", st);                                                                \
+    router_fused_kernel<B><<<grid, kGemvWarps * 32, smem, st>>>(x, (int)T, w.in, E, w.w, w.s, w.b, ksplit, partial,    \
+                                                                bias, pes, k, ids, wts, logits, counters, m);          \
   }
-  return check_launch("router_topk_kernel");
+  switch (w.bits) {
+    case 16: FMOE_ROUTER_LAUNCH(16) break;
+    case 4: FMOE_ROUTER_LAUNCH(4) break;
+    case 8: FMOE_ROUTER_LAUNCH(8) break;
+    default: return set_error(FMOE_ERR_UNSUPPORTED, "router: bits=%d has no kernel", w.bits);
+  }
+#undef FMOE_ROUTER_LAUNCH
+  return check_launch("router_fused_kernel");
 }
 
 }  // namespace fmoe

@@ -61,8 +61,9 @@ int launch_reduce_partials(const float* partial, int ksplit, int64_t n, bf16* ou
                            cudaStream_t st);
 int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps, const bf16* rscale, bf16* xs,
                           cudaStream_t st);
-int launch_router_topk(const float* partial, int ksplit, int64_t T, int E, const float* bias, const bf16* pes, int k,
-                       int first_id, int32_t* ids, float* wts, float* logits, cudaStream_t st);
+int launch_router_fused(const bf16* x, int64_t T, const QW& w, int ksplit, float* partial, const float* bias,
+                        const bf16* pes, int k, int32_t* ids, float* wts, float* logits, unsigned* counters,
+                        const RouteMeta* meta, cudaStream_t st);
 
 // moe.cu
 int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, const RouteMeta& m, cudaStream_t st);

@@ -136,7 +136,11 @@ int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, voi
  * [T, top_k] (global expert ids, descending logit, ties -> lower id) and
  * weights f32 [T, top_k] (softmax over the selected logits, i.e. the
  * renormalised top-k probabilities, times per_expert_scale).  logits (f32
- * [T, num_experts]) may be NULL.  Needs fmoe_router_workspace_bytes(T, r). */
+ * [T, num_experts]) may be NULL.  Needs fmoe_router_workspace_bytes(T, r) of
+ * workspace that is zero-filled before its first use: the router keeps
+ * completion counters there (one fused kernel: logits, top-k, routing lists)
+ * and every call leaves them at zero again.  Calls that share a workspace must
+ * not overlap on the GPU. */
 size_t fmoe_router_workspace_bytes(int64_t T, const fmoe_router_t* r);
 int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, float* weights,
                 float* logits, void* workspace, size_t workspace_bytes, void* stream);
@@ -156,8 +160,10 @@ int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, co
                      void* stream);
 
 /* Gemma4MoeBlock::forward, src/model/moe.rs:315-470: router + experts in one
- * call.  ids / weights (may be NULL) receive the routing.  Workspace:
- * fmoe_moe_block_workspace_bytes. */
+ * call (3 kernels: fused router + routing lists, gate/up, down + combine).
+ * ids / weights (may be NULL) receive the routing.  Workspace:
+ * fmoe_moe_block_workspace_bytes, zero-filled before first use (see
+ * fmoe_router).  T <= 128 (decode path). */
 size_t fmoe_moe_block_workspace_bytes(int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex);
 int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex,
                            void* y, int32_t* ids, float* weights, void* workspace,
