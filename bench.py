@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="moe30_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=30,
+                    help="decoder layers in the step (30 = the model; fewer only for small profiling cases)")
     return ap.parse_args()
 
 
@@ -117,10 +119,10 @@ class ClockSampler:
 # our arm
 
 
-def build_layers(fm, torch, dev, seed):
+def build_layers(fm, torch, dev, seed, n_layers):
     layers = []
     g = torch.Generator(device=dev)
-    for l in range(LAYERS):
+    for l in range(n_layers):
         g.manual_seed(seed + l)
         wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
         table = fm.ExpertTable.random(E, H, I, seed=seed + 1000 + l, device=dev)
@@ -170,10 +172,10 @@ def run_ours(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     T = WORKLOADS[args.workload]
-    layers = build_layers(fm, torch, dev, seed=4000)
+    layers = build_layers(fm, torch, dev, seed=4000, n_layers=args.layers)
     stack = MoeStack(fm, torch, layers, T, dev)
     g = torch.Generator(device=dev).manual_seed(5000 + rank)
-    nin = max(args.steps, 1) + args.warmup
+    nin = max(args.steps + args.warmup, 16)
     xs = torch.randn(nin, T, H, generator=g, device=dev).to(torch.bfloat16)
     stream = torch.cuda.Stream(device=dev)
 
@@ -249,11 +251,12 @@ def run_ours(args, rank, world, local):
     # roofline of the dominant kernel
     peaks, peaks_kind = load_peaks()
     name, (n_l, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+    nl = args.layers
     avg_u = sum(sum(u) for u in uniq) / nprof  # unique experts per step summed over layers
     if name == "moe_gate_up_kernel":
-        alg = avg_u * GATE_UP_BYTES / LAYERS + T * H * 2 + avg_u / LAYERS * T * I * 2
+        alg = avg_u * GATE_UP_BYTES / nl + T * H * 2 + avg_u / nl * T * I * 2
     elif name == "moe_down_kernel":
-        alg = avg_u * DOWN_BYTES / LAYERS + T * H * 2
+        alg = avg_u * DOWN_BYTES / nl + T * H * 2
     else:
         alg = ROUTER_BYTES
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9
@@ -263,7 +266,7 @@ def run_ours(args, rank, world, local):
         traffic = tr.get(args.workload, {}).get(name)
     except Exception:
         pass
-    step_bytes = avg_u * (GATE_UP_BYTES + DOWN_BYTES) + LAYERS * ROUTER_BYTES
+    step_bytes = avg_u * (GATE_UP_BYTES + DOWN_BYTES) + nl * ROUTER_BYTES
     result = {
         "metric": "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)",
         "value": round(value, 2),
@@ -277,7 +280,7 @@ def run_ours(args, rank, world, local):
         "vs_baseline": None,
         "dtype": "u4-affine weights x bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights MLX-affine 4-bit quantised; random init)",
-        "config": {"workload": args.workload, "layers": LAYERS, "hidden": H, "experts": E, "top_k": K,
+        "config": {"workload": args.workload, "layers": nl, "hidden": H, "experts": E, "top_k": K,
                    "expert_intermediate": I, "tokens_per_step": T, "router": "bf16",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "inputs larger than L2 (30 x 428 MB of experts resident)",
@@ -379,7 +382,7 @@ def run_reference(args, rank, world):
         "ms_per_step": round(layer_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "u4-affine weights x bf16 activations, fp64 accumulate (CPU)",
         "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "layers": LAYERS, "tokens_per_step": T},
+        "config": {"workload": args.workload, "layers": nl, "tokens_per_step": T},
         "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
                          "sample": f"each step = 1 of the {LAYERS} MoE layers at T={T}; tok/s extrapolated"},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

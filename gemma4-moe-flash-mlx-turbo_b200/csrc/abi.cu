@@ -66,7 +66,7 @@ static int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
   if (e->num_experts <= 0 || e->num_experts > 1024) return set_error(FMOE_ERR_INVALID, "experts: num_experts %d", e->num_experts);
   if (!aligned(e->base, 16) || e->expert_stride % 16) return set_error(FMOE_ERR_ALIGN, "experts: base/stride not 16-byte aligned");
   for (int j = 0; j < 9; ++j)
-    if (e->offsets[j] < 0 || e->offsets[j] % 8 || (j % 3 == 0 && e->offsets[j] % 16))
+    if (e->offsets[j] < 0 || e->offsets[j] % 16)  // TMA bulk copies need 16-byte aligned sources
       return set_error(FMOE_ERR_ALIGN, "experts: offset[%d]=%lld misaligned", j, (long long)e->offsets[j]);
   d->base = static_cast<const uint8_t*>(e->base);
   d->stride = e->expert_stride;
@@ -80,36 +80,54 @@ static int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
 
 static const int kMaxDecodeTokens = 128;
 
-struct RouterWs {
-  unsigned* counters;  // [1 + token chunks], zero between calls
-  bf16* xs;
-  float* partial;
-  int ksplit;
+// Every workspace starts with a 256-byte header: [0] device status word (0 ok;
+// otherwise the site code of a timed-out wait), [1] router completion counter.
+struct WsHead {
+  int* status;
+  unsigned* router_ctr;
 };
-
-static int router_ksplit(int64_t T, int E, int H) {
-  return gemv_ksplit(T, (E + 15) / 16 * 16, H);
+static WsHead carve_head(Carver& c) {
+  int* p = c.take<int>(64);
+  return WsHead{p, p ? reinterpret_cast<unsigned*>(p + 1) : nullptr};
 }
 
-static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, RouterWs* w) {
-  const int H = r->proj.in_features, E = r->proj.out_features;
-  const int ks = router_ksplit(T, E, H);
-  unsigned* ctr = c.take<unsigned>(1 + (size_t)(T + 7) / 8);
+struct RouterWs {
+  unsigned* counters;  // [1]: token chunks done (several chunks), zero between calls
+  bf16* xs;            // normalised router input (use_norm)
+  float* unused;
+};
+
+static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const WsHead& h, RouterWs* w) {
+  const int H = r->proj.in_features;
   bf16* xs = r->use_norm ? c.take<bf16>((size_t)T * H) : nullptr;
-  float* part = c.take<float>((size_t)ks * T * E);
-  if (w) *w = RouterWs{ctr, xs, part, ks};
+  if (w) *w = RouterWs{h.router_ctr, xs, nullptr};
   return c.off;
 }
 
-static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, RouteMeta* m, bf16** act) {
-  RouteMeta mm;
-  mm.start = c.take<int32_t>(ex.E + 1);
-  mm.pairs = c.take<int32_t>((size_t)T * k);
-  mm.unique = c.take<int32_t>(ex.E);
-  mm.num_unique = c.take<int32_t>(1);
-  bf16* a = c.take<bf16>((size_t)T * k * ex.I);
-  if (m) *m = mm;
-  if (act) *act = a;
+struct MoeWs {
+  float* rpart;         // fused decode path: [8][T][E] router partial logits
+  unsigned* gbar;       // fused decode path: [4] grid barrier counters, zero between calls
+  RouteMeta m;
+  bf16* act;            // [T*k, I] gated intermediate activations
+  float* part;          // [groups, T, H] per-expert-group partial outputs
+  unsigned* tile_ctr;   // [H/16] completion counters, zero between calls
+};
+
+static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w) {
+  MoeWs m;
+  m.gbar = c.take<unsigned>(4);
+  m.rpart = c.take<float>((size_t)8 * T * ex.E);
+  m.tile_ctr = c.take<unsigned>(ex.H / 16);
+  m.m.start = c.take<int32_t>(ex.E + 1);
+  m.m.pairs = c.take<int32_t>((size_t)T * k);
+  m.m.unique = c.take<int32_t>(ex.E);
+  m.m.num_unique = c.take<int32_t>(1);
+  m.m.work_len = (int)(T * k < ex.E ? T * k : ex.E);
+  m.m.work = c.take<int4>(m.m.work_len);
+  m.act = c.take<bf16>((size_t)T * k * ex.I);
+  const int groups = down_groups(T, k, ex.E);
+  m.part = groups > 1 ? c.take<float>((size_t)groups * T * ex.H) : nullptr;
+  if (w) *w = m;
   return c.off;
 }
 
@@ -129,7 +147,7 @@ static int check_router(const fmoe_router_t* r, QW* q) {
 
 // meta != nullptr: the router kernel also builds the per-expert pair lists.
 static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
-                      float* wts, float* logits, const RouteMeta* meta, cudaStream_t st) {
+                      float* wts, float* logits, const RouteMeta* meta, int* status, cudaStream_t st) {
   const bf16* xin = x;
   if (r->use_norm) {
     const int rc =
@@ -137,21 +155,20 @@ static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW
     if (rc) return rc;
     xin = w.xs;
   }
-  return launch_router_fused(xin, T, q, w.ksplit, w.partial, r->logit_bias,
-                             static_cast<const bf16*>(r->per_expert_scale), r->top_k, ids, wts, logits, w.counters,
-                             meta, st);
+  return launch_router_fused(xin, T, q, r->logit_bias, static_cast<const bf16*>(r->per_expert_scale), r->top_k, ids,
+                             wts, logits, w.counters, meta, status, true, st);
 }
 
 static int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
-                       bf16* y, const RouteMeta& m, bf16* act, bool build_routes, cudaStream_t st) {
+                       bf16* y, const MoeWs& w, bool build_routes, int* status, cudaStream_t st) {
   int rc;
   if (build_routes) {
-    rc = launch_route_build(ids, T * k, ex, m, st);
+    rc = launch_route_build(ids, T * k, ex, w.m, st);
     if (rc) return rc;
   }
-  rc = launch_moe_gate_up(x, T, k, ex, m, act, st);
+  rc = launch_moe_gate_up(x, T, k, ex, w.m, w.act, status, true, st);
   if (rc) return rc;
-  return launch_moe_down(act, T, k, wts, ex, m, y, st);
+  return launch_moe_down(w.act, T, k, wts, ex, w.m, w.part, w.tile_ctr, y, status, true, st);
 }
 
 }  // namespace fmoe
@@ -207,7 +224,8 @@ int fmoe_embed_rows(const fmoe_qweight_t* w, const int32_t* ids, int64_t n, floa
 size_t fmoe_router_workspace_bytes(int64_t T, const fmoe_router_t* r) {
   if (!r || T <= 0) return 0;
   Carver c(nullptr);
-  return carve_router(c, T, r, nullptr) + 256;
+  const WsHead h = carve_head(c);
+  return carve_router(c, T, r, h, nullptr) + 256;
 }
 
 int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, float* weights, float* logits,
@@ -221,9 +239,10 @@ int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, 
   if (!workspace || workspace_bytes < fmoe_router_workspace_bytes(T, r))
     return set_error(FMOE_ERR_WORKSPACE, "router: workspace %zu < %zu", workspace_bytes, fmoe_router_workspace_bytes(T, r));
   Carver c(workspace);
+  const WsHead h = carve_head(c);
   RouterWs w;
-  carve_router(c, T, r, &w);
-  return run_router(static_cast<const bf16*>(x), T, r, q, w, ids, weights, logits, nullptr,
+  carve_router(c, T, r, h, &w);
+  return run_router(static_cast<const bf16*>(x), T, r, q, w, ids, weights, logits, nullptr, h.status,
                     static_cast<cudaStream_t>(stream));
 }
 
@@ -258,7 +277,8 @@ size_t fmoe_moe_workspace_bytes(int64_t T, int top_k, const fmoe_experts_t* ex) 
   ExpertsDev d;
   if (T <= 0 || to_experts(ex, &d)) return 0;
   Carver c(nullptr);
-  return carve_moe(c, T, top_k, d, nullptr, nullptr) + 256;
+  carve_head(c);
+  return carve_moe(c, T, top_k, d, nullptr) + 256;
 }
 
 int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, const float* weights,
@@ -275,10 +295,10 @@ int fmoe_moe_experts(const void* x, int64_t T, int top_k, const int32_t* ids, co
   const size_t need = fmoe_moe_workspace_bytes(T, top_k, ex);
   if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "moe_experts: workspace %zu < %zu", workspace_bytes, need);
   Carver c(workspace);
-  RouteMeta m;
-  bf16* act;
-  carve_moe(c, T, top_k, d, &m, &act);
-  return run_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<bf16*>(y), m, act, true,
+  const WsHead h = carve_head(c);
+  MoeWs w;
+  carve_moe(c, T, top_k, d, &w);
+  return run_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<bf16*>(y), w, true, h.status,
                      static_cast<cudaStream_t>(stream));
 }
 
@@ -286,10 +306,11 @@ size_t fmoe_moe_block_workspace_bytes(int64_t T, const fmoe_router_t* r, const f
   ExpertsDev d;
   if (T <= 0 || !r || to_experts(ex, &d)) return 0;
   Carver c(nullptr);
-  carve_router(c, T, r, nullptr);
+  const WsHead h = carve_head(c);
+  carve_router(c, T, r, h, nullptr);
   c.take<int32_t>((size_t)T * r->top_k);
   c.take<float>((size_t)T * r->top_k);
-  return carve_moe(c, T, r->top_k, d, nullptr, nullptr) + 256;
+  return carve_moe(c, T, r->top_k, d, nullptr) + 256;
 }
 
 int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, const fmoe_experts_t* ex, void* y,
@@ -310,21 +331,40 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
   if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "moe_block: workspace %zu < %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver c(workspace);
+  const WsHead h = carve_head(c);
   RouterWs w;
-  carve_router(c, T, r, &w);
+  carve_router(c, T, r, h, &w);
   int32_t* ids_ws = c.take<int32_t>((size_t)T * r->top_k);
   float* w_ws = c.take<float>((size_t)T * r->top_k);
   int32_t* ids_out = ids ? ids : ids_ws;
   float* w_out = weights ? weights : w_ws;
-  RouteMeta m;
-  bf16* act;
-  carve_moe(c, T, r->top_k, d, &m, &act);
+  MoeWs mw;
+  carve_moe(c, T, r->top_k, d, &mw);
   if (q.out != d.E || d.first != 0)
     return set_error(FMOE_ERR_INVALID, "moe_block: router has %d experts, table %d (first %d)", q.out, d.E, d.first);
-  rc = run_router(static_cast<const bf16*>(x), T, r, q, w, ids_out, w_out, nullptr, &m, st);
+  if (!r->use_norm && fused_supported(T, q.out, r->top_k, q.in, q.bits) && (q.bits == 16 || r->proj.group_size == 64)) {
+    // decode: router, top-k, experts and combine in one cooperative kernel
+    return launch_moe_fused(static_cast<const bf16*>(x), T, q, r->logit_bias,
+                            static_cast<const bf16*>(r->per_expert_scale), r->top_k, d, ids_out, w_out,
+                            static_cast<bf16*>(y), mw.rpart, mw.act, mw.part, mw.tile_ctr, mw.gbar, h.status, st);
+  }
+  rc = run_router(static_cast<const bf16*>(x), T, r, q, w, ids_out, w_out, nullptr, &mw.m, h.status, st);
   if (rc) return rc;
-  return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), m, act, false,
-                     st);
+  return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), mw, false,
+                     h.status, st);
+}
+
+int fmoe_workspace_status(const void* workspace, int clear, void* stream) {
+  if (!workspace) return set_error(FMOE_ERR_INVALID, "workspace_status: null workspace");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  if (cudaMemcpyAsync(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "workspace_status: %s", cudaGetErrorString(cudaGetLastError()));
+  if (v && clear && cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(int), st) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "workspace_status: clear failed");
+  if (v) return set_error(FMOE_ERR_TIMEOUT, "a device wait gave up (site %d)", v);
+  return FMOE_OK;
 }
 
 }  // extern "C"

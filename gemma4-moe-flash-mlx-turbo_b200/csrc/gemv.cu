@@ -7,9 +7,11 @@
 // The slices' fp32 partial sums are added in fixed order by the consumer
 // (reduce_partials_kernel or router_topk_kernel), so results are
 // deterministic run to run.
+#include <cooperative_groups.h>
 #include "internal.h"
 #include "gemv.cuh"
 #include "route.cuh"
+#include "stage.cuh"
 
 namespace fmoe {
 
@@ -86,27 +88,19 @@ __global__ void router_prenorm_kernel(const bf16* __restrict__ x, int H, float r
   }
 }
 
-// Top-k of one token, one warp: logits = sum of the K-slice partials (+ bias);
-// top-k by value (ties -> lower id); weights = softmax over the k selected
-// logits (equal to softmax(all)[ids] / sum softmax(all)[ids],
-// src/model/moe.rs:331-340), times per_expert_scale (moe.rs:341-345).
-// Partials are read through L2: other CTAs of the same kernel wrote them.
+// Top-k of one token, one warp: top-k of the logits by value (ties -> lower
+// id); weights = softmax over the k selected logits (equal to
+// softmax(all)[ids] / sum softmax(all)[ids], src/model/moe.rs:331-340), times
+// per_expert_scale (moe.rs:341-345).  `row` holds the token's E logits;
+// outputs go to row `tkn` of ids / wts.
 constexpr int kTopkPerLane = 8;  // E <= 256
-__device__ void topk_token(const float* partial, int ksplit, int T, int E, int tkn, const float* bias, const bf16* pes,
-                           int k, int first_id, int32_t* ids, float* wts, float* logits_out) {
+__device__ int topk_token(const float* row, int E, int tkn, const bf16* pes, int k, int32_t* ids, float* wts) {
   const int lane = threadIdx.x & 31;
   float v[kTopkPerLane];
 #pragma unroll
   for (int j = 0; j < kTopkPerLane; ++j) {
     const int e = lane + 32 * j;
-    float s = -INFINITY;
-    if (e < E) {
-      s = 0.f;
-      for (int kz = 0; kz < ksplit; ++kz) s += __ldcg(partial + ((int64_t)kz * T + tkn) * E + e);
-      if (bias) s += bias[e];
-      if (logits_out) logits_out[(int64_t)tkn * E + e] = s;
-    }
-    v[j] = s;
+    v[j] = e < E ? row[e] : -INFINITY;
   }
   float mx = 0.f, den = 0.f, my_v = 0.f;
   int my_e = 0;
@@ -143,66 +137,222 @@ __device__ void topk_token(const float* partial, int ksplit, int T, int E, int t
   if (lane < k) {
     float wv = expf(my_v - mx) / den;
     if (pes) wv *= bf2f(pes[my_e]);
-    ids[(int64_t)tkn * k + lane] = my_e + first_id;
+    ids[(int64_t)tkn * k + lane] = my_e;
     wts[(int64_t)tkn * k + lane] = wv;
+  }
+  return my_e;
+}
+
+// Routing lists for a single token (T == 1) inside one warp: the k selected
+// experts are distinct, so expert j's slot in the ascending list is the number
+// of selected ids below it.  Lane j < k holds (id, slot j).
+__device__ __forceinline__ void route_single_token(int my_e, int k, int E, RouteMeta m) {
+  const int lane = threadIdx.x & 31;
+  int rank = 0;
+  for (int i = 0; i < k; ++i) {
+    const int ei = __shfl_sync(0xffffffffu, my_e, i);
+    rank += (lane < k && ei < my_e) ? 1 : 0;
+  }
+  if (lane < k) {
+    m.unique[rank] = my_e;
+    m.pairs[rank] = lane;
+    m.start[my_e] = rank;
+    m.start[my_e + 1] = rank + 1;  // agrees with the next selected expert's own entry when adjacent
+    if (rank < m.work_len) m.work[rank] = make_int4(my_e, rank, 1, 0);
+  }
+  for (int u = k + lane; u < m.work_len; u += 32) m.work[u] = make_int4(0, 0, 0, 0);
+  if (lane == 0) {
+    m.start[E] = k;
+    *m.num_unique = k;
   }
 }
 
-// Fused router: CTA (16-expert tile, 8-token chunk, K slice) computes its
-// partial logits; the last CTA to finish a token chunk (completion counter)
-// runs the chunk's top-k; the last chunk to finish builds the per-expert pair
-// lists for the expert kernels when `meta.start` is set.  Counters return to
-// zero at the end of every call.
+// Fused router.  One thread-block cluster per 8-token chunk covers all
+// experts: CTA rank r computes the 16-expert tile r % RT over the hidden-dim
+// slice r / RT (RT = ceil(E/16) tiles, KS slices, RT*KS <= 16 CTAs).  Each
+// CTA stages its weight slice (and scales) before waiting on the preceding
+// kernel (programmatic dependent launch), then its slice of the chunk's x rows.
+// The rank-0 CTA gathers the partial tiles through distributed shared memory
+// in slice order (deterministic), adds the bias, and runs the chunk's top-k
+// from shared memory.  With a single chunk it also builds the routing lists;
+// with several, the last chunk (completion counter, reset every call) does.
+constexpr int kRtWarps = 4;
+constexpr int kRtMaxCluster = 16;
+
+struct RtLayout {
+  int RS, XS, gmax;
+  size_t s_off, f_off, x_off, l_off, bytes;
+};
+__host__ __device__ inline RtLayout rt_layout(int H, int bits, int E, int ks) {
+  RtLayout L;
+  const int G = H / 64;
+  L.gmax = (G + ks - 1) / ks;  // groups per slice
+  L.RS = smem_stride(L.gmax * 64 * bits / 8, bits == 4 ? 8 : 16);
+  L.XS = smem_stride(L.gmax * 128, 16);
+  L.s_off = 16 * (size_t)L.RS;                                              // raw bf16 [2][16][gmax]
+  L.f_off = align16(L.s_off + (bits == 16 ? 0 : 2 * 16 * (size_t)L.gmax * 2));  // float2 [16][gmax]
+  L.x_off = align16(L.f_off + (bits == 16 ? 0 : 16 * (size_t)L.gmax * sizeof(float2)));
+  L.l_off = align16(L.x_off + 8 * (size_t)L.XS);                           // logits [8][E] (rank 0)
+  L.bytes = L.l_off + 8 * (size_t)E * sizeof(float);
+  const size_t route = sizeof(int) * (kRtWarps + 1) * (size_t)E;  // route build reuses the tile area
+  if (L.l_off < route) {
+    L.l_off = align16(route);
+    L.bytes = L.l_off + 8 * (size_t)E * sizeof(float);
+  }
+  return L;
+}
+
 template <int BITS>
-__global__ void __launch_bounds__(kGemvWarps * 32)
-    router_fused_kernel(const bf16* __restrict__ x, int T, int in, int E, const void* __restrict__ w,
-                        const bf16* __restrict__ sc, const bf16* __restrict__ bi, int ksplit, float* partial,
-                        const float* __restrict__ bias, const bf16* __restrict__ pes, int k, int32_t* ids, float* wts,
-                        float* logits_out, unsigned* counters, RouteMeta meta) {
-  extern __shared__ int rsm[];
-  __shared__ float red[kGemvWarps][16][8];
+__global__ void __launch_bounds__(kRtWarps * 32)
+    router_fused_kernel(const bf16* __restrict__ x, int T, int H, int E, int RT, int KS, const void* __restrict__ w,
+                        const bf16* __restrict__ sc, const bf16* __restrict__ bi, const float* __restrict__ bias,
+                        const bf16* __restrict__ pes, int k, int32_t* ids, float* wts, float* logits_out,
+                        unsigned* counters, RouteMeta meta, int* status) {
+  namespace cg = cooperative_groups;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ float red[kRtWarps][16][8];
+  __shared__ float part[16][8];
   __shared__ int s_last;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int row0 = blockIdx.x * 16, tok0 = blockIdx.y * 8, kz = blockIdx.z;
-  const int G = in / 64;
-  const int gbeg = (int)((int64_t)G * kz / ksplit), gend = (int)((int64_t)G * (kz + 1) / ksplit);
-  const int wpr = in * BITS / 32;
-  const bf16* xrow = (tok0 + g < T) ? x + (int64_t)(tok0 + g) * in : nullptr;
+  const int tile = rank % RT, slice = rank / RT;
+  const int row0 = tile * 16, tok0 = blockIdx.y * 8;
+  const int nv = min(8, T - tok0);
+  const int G = H / 64, RB = H * BITS / 8, GB = 64 * BITS / 8;  // bytes per group of a row
+  const RtLayout L = rt_layout(H, BITS, E, KS);
+  const int g0 = min(G, slice * L.gmax), g1 = min(G, g0 + L.gmax), ng = g1 - g0;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  // weight slice: independent of the preceding kernel (one bulk copy per row)
+  if (warp == 0) {
+    if (lane == 0) mbar_arrive_expect_tx(&bar, 16u * ng * GB + (uint32_t)nv * ng * 128);
+    __syncwarp();
+    if (lane < 16 && ng > 0) {
+      const int row = min(row0 + lane, E - 1);
+      bulk_g2s(smem + lane * L.RS, static_cast<const uint8_t*>(w) + (int64_t)row * RB + g0 * GB, ng * GB, &bar);
+    }
+  }
+  if (BITS != 16) {
+    bf16* raw = reinterpret_cast<bf16*>(smem + L.s_off);
+    for (int i = threadIdx.x; i < 16 * ng; i += blockDim.x) {
+      const int r = i / ng, j = i % ng, row = min(row0 + r, E - 1);
+      raw[r * L.gmax + j] = sc[(int64_t)row * G + g0 + j];
+      raw[16 * L.gmax + r * L.gmax + j] = bi[(int64_t)row * G + g0 + j];
+    }
+  }
+  griddep_wait();  // x may come from the preceding kernel
+  griddep_launch_dependents();
+  if (warp == 0 && lane >= 16 && lane - 16 < nv && ng > 0)
+    bulk_g2s(smem + L.x_off + (lane - 16) * L.XS, x + (int64_t)(tok0 + lane - 16) * H + g0 * 64, ng * 128, &bar);
+  const bool ok = mbar_wait(&bar, 0, status, 21);
+  __syncthreads();
+  float2* fix = reinterpret_cast<float2*>(smem + L.f_off);
+  if (BITS != 16) {
+    const bf16* raw = reinterpret_cast<const bf16*>(smem + L.s_off);
+    const float off = BITS == 4 ? 128.0f : 2176.0f;
+    for (int i = threadIdx.x; i < 16 * L.gmax; i += blockDim.x) {
+      const float s = __bfloat162float(raw[i]);
+      fix[i] = make_float2(s, fmaf(-off, s, __bfloat162float(raw[16 * L.gmax + i])));
+    }
+    __syncthreads();
+  }
+  const uint8_t* wsm = smem;
+  const uint8_t* xsm = smem + L.x_off;
   float y[4] = {0.f, 0.f, 0.f, 0.f};
-  warp_tile_gemv<BITS>(y, w, sc, bi, min(row0 + g, E - 1), min(row0 + g + 8, E - 1), wpr, G, xrow, gbeg + warp, gend,
-                       kGemvWarps, t);
+  for (int j = warp; j < ng; j += kRtWarps) {
+    if constexpr (BITS == 16) {
+      const BFrag4 b = stage_bfrag4(xsm, L.XS, nv, j, g, t);
+      const uint8_t* plo = wsm + g * L.RS + j * 128 + 32 * t;
+      const uint8_t* phi = wsm + (g + 8) * L.RS + j * 128 + 32 * t;
+      const BFrag4 alo = make_bfrag4(lds_u4(plo), lds_u4(plo + 16)), ahi = make_bfrag4(lds_u4(phi), lds_u4(phi + 16));
+#pragma unroll
+      for (int s = 0; s < 4; ++s) mma16816(y, alo.b0[s], ahi.b0[s], alo.b1[s], ahi.b1[s], b.b0[s], b.b1[s]);
+    } else if constexpr (BITS == 4) {
+      const BFrag4 b = stage_bfrag4(xsm, L.XS, nv, j, g, t);
+      const uint2 wl = lds_u2(wsm + g * L.RS + j * 32 + 8 * t);
+      const uint2 wh = lds_u2(wsm + (g + 8) * L.RS + j * 32 + 8 * t);
+      float c[4] = {0.f, 0.f, 0.f, 0.f}, xs[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_group_q4(c, wl, wh, b);
+      mma_group_ones(xs, b);
+      const float2 lo = fix[g * L.gmax + j], hi = fix[(g + 8) * L.gmax + j];
+      y[0] = fmaf(lo.x, c[0], fmaf(lo.y, xs[0], y[0]));
+      y[1] = fmaf(lo.x, c[1], fmaf(lo.y, xs[1], y[1]));
+      y[2] = fmaf(hi.x, c[2], fmaf(hi.y, xs[2], y[2]));
+      y[3] = fmaf(hi.x, c[3], fmaf(hi.y, xs[3], y[3]));
+    } else {
+      const uint8_t* px = xsm + g * L.XS + j * 128 + 32 * t;
+      uint4 xl = make_uint4(0, 0, 0, 0), xh = xl;
+      if (g < nv) {
+        xl = lds_u4(px);
+        xh = lds_u4(px + 16);
+      }
+      const BFrag8 b8 = make_bfrag8(xl, xh);
+      const uint4 wl = lds_u4(wsm + g * L.RS + j * 64 + 16 * t);
+      const uint4 wh = lds_u4(wsm + (g + 8) * L.RS + j * 64 + 16 * t);
+      float c[4] = {0.f, 0.f, 0.f, 0.f}, xs[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_group_q8(c, wl, wh, b8);
+      mma_group_ones8(xs, b8);
+      const float2 lo = fix[g * L.gmax + j], hi = fix[(g + 8) * L.gmax + j];
+      y[0] = fmaf(lo.x, c[0], fmaf(lo.y, xs[0], y[0]));
+      y[1] = fmaf(lo.x, c[1], fmaf(lo.y, xs[1], y[1]));
+      y[2] = fmaf(hi.x, c[2], fmaf(hi.y, xs[2], y[2]));
+      y[3] = fmaf(hi.x, c[3], fmaf(hi.y, xs[3], y[3]));
+    }
+  }
   red[warp][g][2 * t] = y[0];
   red[warp][g][2 * t + 1] = y[1];
   red[warp][g + 8][2 * t] = y[2];
   red[warp][g + 8][2 * t + 1] = y[3];
   __syncthreads();
   {
-    const int i = threadIdx.x, tk = i >> 4, r = i & 15;
-    if (tok0 + tk < T && row0 + r < E) {
-      float s = 0.f;
+    const int r = threadIdx.x >> 3, c = threadIdx.x & 7;  // 128 threads = 16 x 8
+    float s = 0.f;
 #pragma unroll
-      for (int wi = 0; wi < kGemvWarps; ++wi) s += red[wi][r][tk];
-      partial[((int64_t)kz * T + tok0 + tk) * E + row0 + r] = s;
+    for (int wi = 0; wi < kRtWarps; ++wi) s += red[wi][r][c];
+    part[r][c] = s;
+  }
+  cluster.sync();  // every CTA's partial tile is in its shared memory
+  float* lg = reinterpret_cast<float*>(smem + L.l_off);  // [8][E] on rank 0
+  if (rank == 0) {
+    for (int i = threadIdx.x; i < nv * E; i += blockDim.x) {
+      const int c = i / E, e = i % E;
+      float s = 0.f;
+      for (int q = 0; q < KS; ++q) s += cluster.map_shared_rank(&part[0][0], q * RT + e / 16)[(e % 16) * 8 + c];
+      if (bias) s += bias[e];
+      lg[i] = s;
+      if (logits_out && c < nv) logits_out[(int64_t)(tok0 + c) * E + e] = s;
     }
   }
-  __threadfence();
+  cluster.sync();  // peers keep their shared memory until rank 0 has read it
+  if (rank != 0 || !ok) return;
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&counters[1 + blockIdx.y], 1u) == gridDim.x * gridDim.z - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int tk = warp; tk < 8; tk += kGemvWarps)
-    if (tok0 + tk < T) topk_token(partial, ksplit, T, E, tok0 + tk, bias, pes, k, 0, ids, wts, logits_out);
-  if (threadIdx.x == 0) counters[1 + blockIdx.y] = 0;
+  if (T == 1 && meta.start) {
+    if (warp == 0) {
+      const int my_e = topk_token(lg, E, 0, pes, k, ids, wts);  // row 0 = the token's logits
+      route_single_token(my_e, k, E, meta);
+    }
+    return;
+  }
+  for (int tk = warp; tk < nv; tk += kRtWarps) topk_token(lg + tk * E, E, tok0 + tk, pes, k, ids, wts);
   if (!meta.start) return;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&counters[0], 1u) == gridDim.y - 1;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  route_build_block(ids, T * k, 0, E, meta.start, meta.pairs, meta.unique, meta.num_unique, rsm);
-  if (threadIdx.x == 0) counters[0] = 0;
+  if (gridDim.y > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&counters[0], 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+  } else {
+    __syncthreads();
+  }
+  route_build_block(ids, T * k, 0, E, meta.start, meta.pairs, meta.unique, meta.num_unique, meta.work, meta.work_len,
+                    reinterpret_cast<int*>(smem));
+  if (threadIdx.x == 0 && gridDim.y > 1) counters[0] = 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -265,20 +415,40 @@ int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps
   return check_launch("router_prenorm_kernel");
 }
 
-int launch_router_fused(const bf16* x, int64_t T, const QW& w, int ksplit, float* partial, const float* bias,
-                        const bf16* pes, int k, int32_t* ids, float* wts, float* logits, unsigned* counters,
-                        const RouteMeta* meta, cudaStream_t st) {
-  const int E = w.out;
+int launch_router_fused(const bf16* x, int64_t T, const QW& w, const float* bias, const bf16* pes, int k,
+                        int32_t* ids, float* wts, float* logits_out, unsigned* counters, const RouteMeta* meta,
+                        int* status, bool pdl, cudaStream_t st) {
+  const int E = w.out, G = w.in / 64;
   if (E > 32 * kTopkPerLane) return set_error(FMOE_ERR_UNSUPPORTED, "router: num_experts %d > %d", E, 32 * kTopkPerLane);
   if (k < 1 || k > 16 || k > E) return set_error(FMOE_ERR_INVALID, "router: top_k %d out of range", k);
-  dim3 grid((E + 15) / 16, (unsigned)((T + 7) / 8), ksplit);
-  RouteMeta m = meta ? *meta : RouteMeta{nullptr, nullptr, nullptr, nullptr};
-  const size_t smem = meta ? sizeof(int) * (kGemvWarps + 1) * (size_t)E : 0;
-#define FMOE_ROUTER_LAUNCH(B)                                                                                          \
-  {                                                                                                                    \
-    ProfScope prof_("router_fused_kernel<" #B ">", st);                                                                \
-    router_fused_kernel<B><<<grid, kGemvWarps * 32, smem, st>>>(x, (int)T, w.in, E, w.w, w.s, w.b, ksplit, partial,    \
-                                                                bias, pes, k, ids, wts, logits, counters, m);          \
+  const int RT = (E + 15) / 16;
+  int KS = kRtMaxCluster / RT;
+  if (KS > G) KS = G;
+  if (KS < 1) KS = 1;
+  const RtLayout L = rt_layout(w.in, w.bits, E, KS);
+  if (L.bytes > 227 * 1024) return set_error(FMOE_ERR_UNSUPPORTED, "router: hidden %d too large", w.in);
+  RouteMeta m = meta ? *meta : RouteMeta{nullptr, nullptr, nullptr, nullptr, nullptr, 0};
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  cfg.gridDim = dim3(RT * KS, (unsigned)((T + 7) / 8));
+  cfg.blockDim = dim3(kRtWarps * 32);
+  cfg.dynamicSmemBytes = L.bytes;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = RT * KS;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+#define FMOE_ROUTER_LAUNCH(B)                                                                                        \
+  {                                                                                                                  \
+    cudaFuncSetAttribute(router_fused_kernel<B>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);                 \
+    cudaFuncSetAttribute(router_fused_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes);         \
+    ProfScope prof_("router_fused_kernel<" #B ">", st);                                                              \
+    cudaLaunchKernelEx(&cfg, router_fused_kernel<B>, x, (int)T, w.in, E, RT, KS, w.w, w.s, w.b, bias, pes, k, ids,   \
+                       wts, logits_out, counters, m, status);                                                        \
   }
   switch (w.bits) {
     case 16: FMOE_ROUTER_LAUNCH(16) break;

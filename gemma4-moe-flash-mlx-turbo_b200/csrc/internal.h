@@ -4,7 +4,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 #include <stddef.h>
-#include "../../include/fmoe.h"
+#include "fmoe.h"
 
 namespace fmoe {
 
@@ -52,6 +52,8 @@ struct RouteMeta {
   int32_t* pairs;       // [T * k] pair index (t*k + slot), grouped by expert, ascending
   int32_t* unique;      // [E] local ids of experts with >= 1 pair, ascending
   int32_t* num_unique;  // [1]
+  int4* work;           // [work_len] per expert slot u: (expert, first pair, pair count, 0); count 0 past the end
+  int work_len;         // min(T * k, E): the expert kernels' grid extent
 };
 
 // gemv.cu
@@ -61,16 +63,23 @@ int launch_reduce_partials(const float* partial, int ksplit, int64_t n, bf16* ou
                            cudaStream_t st);
 int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps, const bf16* rscale, bf16* xs,
                           cudaStream_t st);
-int launch_router_fused(const bf16* x, int64_t T, const QW& w, int ksplit, float* partial, const float* bias,
-                        const bf16* pes, int k, int32_t* ids, float* wts, float* logits, unsigned* counters,
-                        const RouteMeta* meta, cudaStream_t st);
+int launch_router_fused(const bf16* x, int64_t T, const QW& w, const float* bias, const bf16* pes, int k,
+                        int32_t* ids, float* wts, float* logits_out, unsigned* counters, const RouteMeta* meta,
+                        int* status, bool pdl, cudaStream_t st);
 
 // moe.cu
 int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, const RouteMeta& m, cudaStream_t st);
+int down_groups(int64_t T, int k, int E);
 int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, const RouteMeta& m, bf16* act,
-                       cudaStream_t st);
+                       int* status, bool pdl, cudaStream_t st);
 int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
-                    bf16* y, cudaStream_t st);
+                    float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st);
+
+// moe_fused.cu
+int fused_supported(int64_t T, int E, int k, int H, int rbits);
+int launch_moe_fused(const bf16* x, int64_t T, const QW& wr, const float* bias, const bf16* pes, int k,
+                     const ExpertsDev& ex, int32_t* ids, float* wts, bf16* y, float* rpart, bf16* act, float* dpart,
+                     unsigned* tile_ctr, unsigned* gbar, int* status, cudaStream_t st);
 
 // quant.cu
 int launch_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits, int group, uint32_t* wq,

@@ -13,7 +13,7 @@ namespace fmoe {
 // are read through L2 (they may have been written earlier in the same kernel
 // by other CTAs).  sm: (nwarps + 1) * E ints of shared memory.
 __device__ __forceinline__ void route_build_block(const int32_t* ids, int P, int first, int E, int32_t* start, int32_t* pairs,
-                                  int32_t* unique, int32_t* num_unique, int* sm) {
+                                  int32_t* unique, int32_t* num_unique, int4* work, int work_len, int* sm) {
   const int nw = blockDim.x >> 5;
   int* wcnt = sm;           // [nw][E] counts, later offsets
   int* tot = sm + nw * E;   // [E]
@@ -50,7 +50,10 @@ __device__ __forceinline__ void route_build_block(const int32_t* ids, int P, int
       if (e < E) {
         start[e] = run + incl - c;
         tot[e] = run + incl - c;
-        if (c > 0) unique[urun + uincl - 1] = e;
+        if (c > 0) {
+          unique[urun + uincl - 1] = e;
+          if (urun + uincl - 1 < work_len) work[urun + uincl - 1] = make_int4(e, run + incl - c, c, 0);
+        }
       }
       run += __shfl_sync(0xffffffffu, incl, 31);
       urun += __shfl_sync(0xffffffffu, uincl, 31);
@@ -59,6 +62,7 @@ __device__ __forceinline__ void route_build_block(const int32_t* ids, int P, int
       start[E] = run;
       *num_unique = urun;
     }
+    for (int u = urun + lane; u < work_len; u += 32) work[u] = make_int4(0, 0, 0, 0);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {

@@ -169,6 +169,11 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
                            void* y, int32_t* ids, float* weights, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Synchronises `stream` and reads the status word every workspace starts with:
+ * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
+ * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
+int fmoe_workspace_status(const void* workspace, int clear, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -171,3 +171,28 @@ def test_moe_rejects_bad_args(fm, dev, full_layer):
     rc = fm.lib().fmoe_moe_experts(x.data_ptr(), 1, K, ids.data_ptr(), w.data_ptr(), ctypes.byref(c), y.data_ptr(),
                                    ws.buf.data_ptr(), 16, torch.cuda.current_stream().cuda_stream)
     assert rc == -3 and "workspace" in fm.last_error()
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 8])
+def test_fused_decode_matches_three_kernel_path(fm, orc, dev, full_layer, T):
+    """fmoe_moe_block_forward takes the single cooperative kernel for T <= 8;
+    the standalone router + experts entry points take the 3-kernel path.  Same
+    routing, outputs within the tolerance, both against the oracle."""
+    table, wr, host = full_layer
+    g = torch.Generator(device=dev).manual_seed(300 + T)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    block = fm.Gemma4MoeBlock(fm.QuantizedLinear(wr, bits=16), table, top_k=K)
+    y_f, ids_f, w_f = block.forward(x, return_routing=True)
+    ids_r, w_r, _ = block.route(x)
+    assert torch.equal(ids_f, ids_r)
+    assert torch.allclose(w_f, w_r, atol=1e-6, rtol=1e-5)
+    y_r = fm.moe_experts(x, ids_r, w_r, table)
+    want = _oracle_experts(orc, table, host, x, ids_f, w_f)
+    assert max_rel_err(y_f.float().cpu().numpy(), want) <= TOL
+    assert max_rel_err(y_r.float().cpu().numpy(), want) <= TOL
+    # repeated calls reuse the workspace (barrier and tile counters return to zero)
+    for _ in range(3):
+        assert torch.equal(block.forward(x), y_f)
+    import ctypes
+    assert fm.lib().fmoe_workspace_status(ctypes.c_void_p(block._ws.buf.data_ptr()), 1,
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)) == 0
