@@ -105,8 +105,6 @@ static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const W
 }
 
 struct MoeWs {
-  float* rpart;         // fused decode path: [8][T][E] router partial logits
-  unsigned* gbar;       // fused decode path: [4] grid barrier counters, zero between calls
   RouteMeta m;
   bf16* act;            // [T*k, I] gated intermediate activations
   float* part;          // [groups, T, H] per-expert-group partial outputs
@@ -115,8 +113,6 @@ struct MoeWs {
 
 static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w) {
   MoeWs m;
-  m.gbar = c.take<unsigned>(4);
-  m.rpart = c.take<float>((size_t)8 * T * ex.E);
   m.tile_ctr = c.take<unsigned>(ex.H / 16);
   m.m.start = c.take<int32_t>(ex.E + 1);
   m.m.pairs = c.take<int32_t>((size_t)T * k);
@@ -342,12 +338,6 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
   carve_moe(c, T, r->top_k, d, &mw);
   if (q.out != d.E || d.first != 0)
     return set_error(FMOE_ERR_INVALID, "moe_block: router has %d experts, table %d (first %d)", q.out, d.E, d.first);
-  if (!r->use_norm && fused_supported(T, q.out, r->top_k, q.in, q.bits) && (q.bits == 16 || r->proj.group_size == 64)) {
-    // decode: router, top-k, experts and combine in one cooperative kernel
-    return launch_moe_fused(static_cast<const bf16*>(x), T, q, r->logit_bias,
-                            static_cast<const bf16*>(r->per_expert_scale), r->top_k, d, ids_out, w_out,
-                            static_cast<bf16*>(y), mw.rpart, mw.act, mw.part, mw.tile_ctr, mw.gbar, h.status, st);
-  }
   rc = run_router(static_cast<const bf16*>(x), T, r, q, w, ids_out, w_out, nullptr, &mw.m, h.status, st);
   if (rc) return rc;
   return run_experts(static_cast<const bf16*>(x), T, r->top_k, ids_out, w_out, d, static_cast<bf16*>(y), mw, false,

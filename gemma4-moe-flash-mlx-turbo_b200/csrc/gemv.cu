@@ -88,59 +88,50 @@ __global__ void router_prenorm_kernel(const bf16* __restrict__ x, int H, float r
   }
 }
 
-// Top-k of one token, one warp: top-k of the logits by value (ties -> lower
-// id); weights = softmax over the k selected logits (equal to
-// softmax(all)[ids] / sum softmax(all)[ids], src/model/moe.rs:331-340), times
-// per_expert_scale (moe.rs:341-345).  `row` holds the token's E logits;
-// outputs go to row `tkn` of ids / wts.
-constexpr int kTopkPerLane = 8;  // E <= 256
-__device__ int topk_token(const float* row, int E, int tkn, const bf16* pes, int k, int32_t* ids, float* wts) {
-  const int lane = threadIdx.x & 31;
-  float v[kTopkPerLane];
-#pragma unroll
-  for (int j = 0; j < kTopkPerLane; ++j) {
-    const int e = lane + 32 * j;
-    v[j] = e < E ? row[e] : -INFINITY;
-  }
-  float mx = 0.f, den = 0.f, my_v = 0.f;
-  int my_e = 0;
-  for (int r = 0; r < k; ++r) {
-    float bv = -INFINITY;
-    int be = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < kTopkPerLane; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && (v[j] > bv || (v[j] == bv && e < be))) {
-        bv = v[j];
-        be = e;
-      }
+// Top-k of `nv` tokens by the whole CTA: each thread takes one (token,
+// expert) and counts the logits that beat it (descending value, ties -> lower
+// id) with 16-byte shared-memory reads — independent compares, no serial
+// reduction chain.  Then weights = softmax over the k selected logits (equal
+// to softmax(all)[ids] / sum softmax(all)[ids], src/model/moe.rs:331-340),
+// times per_expert_scale (moe.rs:341-345).  lg: shared [nv][E], E % 4 == 0.
+// Output rows tok0 .. tok0+nv-1 of ids / wts; sel_e receives [nv][16] ids.
+constexpr int kTopkMaxK = 16;
+__device__ void topk_block(const float* lg, int nv, int E, int k, int tok0, const bf16* pes, int32_t* ids, float* wts,
+                           int* sel_e, float* sel_v) {
+  for (int i = threadIdx.x; i < nv * E; i += blockDim.x) {
+    const int n = i / E, e = i % E;
+    const float* row = lg + n * E;
+    const float v = row[e];
+    int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+#pragma unroll 8
+    for (int j = 0; j < E; j += 4) {
+      const float4 u = *reinterpret_cast<const float4*>(row + j);
+      r0 += (u.x > v || (u.x == v && j < e)) ? 1 : 0;
+      r1 += (u.y > v || (u.y == v && j + 1 < e)) ? 1 : 0;
+      r2 += (u.z > v || (u.z == v && j + 2 < e)) ? 1 : 0;
+      r3 += (u.w > v || (u.w == v && j + 3 < e)) ? 1 : 0;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
+    const int rank = r0 + r1 + r2 + r3;
+    if (rank < k) {
+      sel_e[n * kTopkMaxK + rank] = e;
+      sel_v[n * kTopkMaxK + rank] = v;
     }
-    if (r == 0) mx = bv;
-    den += expf(bv - mx);
-    if (lane == r) {
-      my_v = bv;
-      my_e = be;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nv * kTopkMaxK; i += blockDim.x) {
+    const int n = i / kTopkMaxK, r = i % kTopkMaxK;
+    if (r < k) {
+      const float m = sel_v[n * kTopkMaxK];
+      float den = 0.f;
+      for (int j = 0; j < k; ++j) den += expf(sel_v[n * kTopkMaxK + j] - m);
+      float wv = expf(sel_v[n * kTopkMaxK + r] - m) / den;
+      const int e = sel_e[n * kTopkMaxK + r];
+      if (pes) wv *= bf2f(pes[e]);
+      ids[(int64_t)(tok0 + n) * k + r] = e;
+      wts[(int64_t)(tok0 + n) * k + r] = wv;
     }
-#pragma unroll
-    for (int j = 0; j < kTopkPerLane; ++j)
-      if (lane + 32 * j == be) v[j] = -INFINITY;
   }
-  if (lane < k) {
-    float wv = expf(my_v - mx) / den;
-    if (pes) wv *= bf2f(pes[my_e]);
-    ids[(int64_t)tkn * k + lane] = my_e;
-    wts[(int64_t)tkn * k + lane] = wv;
-  }
-  return my_e;
+  __syncthreads();
 }
 
 // Routing lists for a single token (T == 1) inside one warp: the k selected
@@ -214,6 +205,8 @@ __global__ void __launch_bounds__(kRtWarps * 32)
   __shared__ float red[kRtWarps][16][8];
   __shared__ float part[16][8];
   __shared__ int s_last;
+  __shared__ int sel_e[8 * kTopkMaxK];
+  __shared__ float sel_v[8 * kTopkMaxK];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -331,14 +324,11 @@ __global__ void __launch_bounds__(kRtWarps * 32)
   cluster.sync();  // peers keep their shared memory until rank 0 has read it
   if (rank != 0 || !ok) return;
   __syncthreads();
+  topk_block(lg, nv, E, k, tok0, pes, ids, wts, sel_e, sel_v);
   if (T == 1 && meta.start) {
-    if (warp == 0) {
-      const int my_e = topk_token(lg, E, 0, pes, k, ids, wts);  // row 0 = the token's logits
-      route_single_token(my_e, k, E, meta);
-    }
+    if (warp == 0) route_single_token(lane < k ? sel_e[lane] : 0, k, E, meta);
     return;
   }
-  for (int tk = warp; tk < nv; tk += kRtWarps) topk_token(lg + tk * E, E, tok0 + tk, pes, k, ids, wts);
   if (!meta.start) return;
   if (gridDim.y > 1) {
     __threadfence();
@@ -348,6 +338,7 @@ __global__ void __launch_bounds__(kRtWarps * 32)
     if (!s_last) return;
     __threadfence();
   } else {
+    __threadfence();  // ids reach L2 before route_build_block reads them through it
     __syncthreads();
   }
   route_build_block(ids, T * k, 0, E, meta.start, meta.pairs, meta.unique, meta.num_unique, meta.work, meta.work_len,
@@ -419,8 +410,8 @@ int launch_router_fused(const bf16* x, int64_t T, const QW& w, const float* bias
                         int32_t* ids, float* wts, float* logits_out, unsigned* counters, const RouteMeta* meta,
                         int* status, bool pdl, cudaStream_t st) {
   const int E = w.out, G = w.in / 64;
-  if (E > 32 * kTopkPerLane) return set_error(FMOE_ERR_UNSUPPORTED, "router: num_experts %d > %d", E, 32 * kTopkPerLane);
-  if (k < 1 || k > 16 || k > E) return set_error(FMOE_ERR_INVALID, "router: top_k %d out of range", k);
+  if (E > 256 || E % 4) return set_error(FMOE_ERR_UNSUPPORTED, "router: num_experts %d (kernels: <= 256, multiple of 4)", E);
+  if (k < 1 || k > kTopkMaxK || k > E) return set_error(FMOE_ERR_INVALID, "router: top_k %d out of range", k);
   const int RT = (E + 15) / 16;
   int KS = kRtMaxCluster / RT;
   if (KS > G) KS = G;

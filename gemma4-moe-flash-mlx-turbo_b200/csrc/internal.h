@@ -75,12 +75,6 @@ int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, co
 int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
                     float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st);
 
-// moe_fused.cu
-int fused_supported(int64_t T, int E, int k, int H, int rbits);
-int launch_moe_fused(const bf16* x, int64_t T, const QW& wr, const float* bias, const bf16* pes, int k,
-                     const ExpertsDev& ex, int32_t* ids, float* wts, bf16* y, float* rpart, bf16* act, float* dpart,
-                     unsigned* tile_ctr, unsigned* gbar, int* status, cudaStream_t st);
-
 // quant.cu
 int launch_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits, int group, uint32_t* wq,
                     bf16* s, bf16* b, cudaStream_t st);

@@ -74,6 +74,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Prefetch [src, src + bytes) into L2 without touching shared memory.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Bounded wait for phase `parity` of `bar`.  Every wait in this library gives
 // up after kMaxWaitIters polls (each poll itself blocks for a short
 // hardware-defined interval), records FMOE_ERR_TIMEOUT with a site code in

@@ -174,9 +174,9 @@ def test_moe_rejects_bad_args(fm, dev, full_layer):
 
 
 @pytest.mark.parametrize("T", [1, 2, 5, 8])
-def test_fused_decode_matches_three_kernel_path(fm, orc, dev, full_layer, T):
-    """fmoe_moe_block_forward takes the single cooperative kernel for T <= 8;
-    the standalone router + experts entry points take the 3-kernel path.  Same
+def test_block_matches_router_plus_experts(fm, orc, dev, full_layer, T):
+    """The block entry point (router kernel builds the routing lists) and the
+    standalone router + experts entry points (separate list build) agree: same
     routing, outputs within the tolerance, both against the oracle."""
     table, wr, host = full_layer
     g = torch.Generator(device=dev).manual_seed(300 + T)
