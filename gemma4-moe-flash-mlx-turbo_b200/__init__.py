@@ -95,6 +95,10 @@ SIGNATURES = {
     "fmoe_version": (_I, []),
     "fmoe_last_error": (_I, [ctypes.c_char_p, _SZ]),
     "fmoe_workspace_status": (_I, [_P, _I, _P]),
+    "fmoe_moe_block_forward_noalloc": (
+        _I,
+        [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P],
+    ),
     "fmoe_profile_enable": (_I, [_I]),
     "fmoe_profile_read": (_I, [ctypes.POINTER(KernelStatC), _I, _I]),
     "fmoe_quantize": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),

@@ -169,6 +169,25 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
                            void* y, int32_t* ids, float* weights, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Variant of fmoe_moe_block_forward for callers that cannot allocate device
+ * memory when they run the layer (an engine that gives its whole device budget
+ * to its own pool, a plugin host that forbids library allocations, a decode
+ * loop that cannot afford cudaMalloc's device synchronisation).  No
+ * counterpart in the reference.  Same arguments and results as
+ * fmoe_moe_block_forward minus the workspace: the library uses a fixed
+ * FMOE_NOALLOC_SCRATCH_BYTES scratch array of its own, in static device memory
+ * that every GPU loading the library holds until the process exits.  Calls
+ * whose fmoe_moe_block_workspace_bytes exceeds it are rejected with
+ * FMOE_ERR_WORKSPACE (for the Gemma-4 shapes: up to 16 tokens).  It calls no
+ * cudaMalloc / cudaFree.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  Every call shares the array and clears the part it uses;
+ * calls that overlap on the GPU race on it. */
+#define FMOE_NOALLOC_SCRATCH_BYTES (4u << 20)
+int fmoe_moe_block_forward_noalloc(const void* x, int64_t T, const fmoe_router_t* r,
+                                   const fmoe_experts_t* ex, void* y, int32_t* ids, float* weights,
+                                   void* stream);
+
 /* Synchronises `stream` and reads the status word every workspace starts with:
  * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
