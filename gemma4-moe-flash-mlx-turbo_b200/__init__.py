@@ -80,6 +80,26 @@ class RouterC(ctypes.Structure):
     ]
 
 
+class KvCacheC(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32),
+        ("batch", ctypes.c_int32),
+        ("kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("capacity", ctypes.c_int64),
+        ("k_bits", ctypes.c_int32),
+        ("v_bits", ctypes.c_int32),
+        ("group_size", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("k", ctypes.c_void_p),
+        ("v", ctypes.c_void_p),
+        ("k_scales", ctypes.c_void_p),
+        ("k_biases", ctypes.c_void_p),
+        ("v_scales", ctypes.c_void_p),
+        ("v_biases", ctypes.c_void_p),
+    ]
+
+
 class KernelStatC(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 64), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
 
@@ -115,6 +135,12 @@ SIGNATURES = {
         _I,
         [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P, _SZ, _P],
     ),
+    "fmoe_kv_cache_bytes": (_SZ, [_I, _I, _I, _I, _I64]),
+    "fmoe_kv_cache_init": (_I, [ctypes.POINTER(KvCacheC), _I, _I, _I, _I, _I64, _P, _SZ]),
+    "fmoe_kv_append": (_I, [ctypes.POINTER(KvCacheC), _P, _P, _I64, _I64, _P, _I, _P]),
+    "fmoe_attn_decode_workspace_bytes": (_SZ, [ctypes.POINTER(KvCacheC), _I]),
+    "fmoe_attn_decode": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _P, _F, _P, _P, _SZ, _P]),
+    "fmoe_turbo_round_trip": (_I, [_P, _I64, _I, _I, _P, _P]),
 }
 
 _lib_handle = None
@@ -403,3 +429,6 @@ class Gemma4MoeBlock:
         return (y, ids, w) if return_routing else y
 
     __call__ = forward
+
+
+from .kv import KV_AFFINE, KV_BF16, KVCache, turbo_round_trip  # noqa: E402

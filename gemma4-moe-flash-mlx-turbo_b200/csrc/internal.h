@@ -81,6 +81,22 @@ int launch_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols
 int launch_dequantize(const QW& w, int group, const int32_t* ids, int64_t n, float row_scale, bf16* out,
                       cudaStream_t st);
 
+// kv.cu: device view of one layer's KV cache (see fmoe_kv_cache_t).
+struct KvDev {
+  int mode, B, Hkv, D;
+  int64_t cap;
+  void* k;  // bf16 rows (FMOE_KV_BF16) or packed 4-bit codes (FMOE_KV_AFFINE)
+  void* v;  // bf16 rows or packed 8-bit codes
+  bf16* ks;
+  bf16* kb;
+  bf16* vs;
+  bf16* vb;
+};
+// Split-KV plan of one decode-attention launch: S slots per split.
+struct AttnPlan {
+  int S, nsplit;
+};
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Bump allocator over a caller workspace.

@@ -188,6 +188,82 @@ int fmoe_moe_block_forward_noalloc(const void* x, int64_t T, const fmoe_router_t
                                    const fmoe_experts_t* ex, void* y, int32_t* ids, float* weights,
                                    void* stream);
 
+/* ---- quantised KV cache + decode attention ---------------------------- */
+
+/* Storage modes of a layer's KV cache.
+ *   FMOE_KV_BF16    bf16 rows, the reference's KVCache (src/cache.rs:266-310);
+ *                   optionally each appended row passes through the TurboQuant
+ *                   round trip first (src/cache.rs:290-308, turbo_bits 2..4).
+ *   FMOE_KV_AFFINE  rows rotated by the normalised Walsh-Hadamard transform
+ *                   over head_dim, then MLX-affine quantised: K 4-bit, V 8-bit,
+ *                   group 64.  No reference counterpart (the benchmark's
+ *                   quantised-KV configuration); attention rotates the query the
+ *                   same way and returns its output in the original basis.
+ * Layout (per array): [batch][kv_heads][capacity][...] row-major; position p
+ * of a sequence lives in slot p % capacity (a ring: capacity = sliding window
+ * keeps the last `window` positions, src/cache.rs:139-148). */
+#define FMOE_KV_BF16 0
+#define FMOE_KV_AFFINE 1
+
+typedef struct fmoe_kv_cache {
+  int32_t mode;
+  int32_t batch;
+  int32_t kv_heads;
+  int32_t head_dim;   /* 256 or 512 */
+  int64_t capacity;   /* slots per (batch, kv head); a multiple of 16 */
+  int32_t k_bits;     /* 16 (bf16 mode) or 4 */
+  int32_t v_bits;     /* 16 (bf16 mode) or 8 */
+  int32_t group_size; /* 64 (affine mode) */
+  int32_t reserved;
+  void* k;        /* bf16 [.., head_dim], or uint32 codes [.., head_dim/8] */
+  void* v;        /* bf16 [.., head_dim], or uint32 codes [.., head_dim/4] */
+  void* k_scales; /* affine: bf16 [.., head_dim/64]; NULL in bf16 mode */
+  void* k_biases;
+  void* v_scales;
+  void* v_biases;
+} fmoe_kv_cache_t;
+
+/* Bytes of one layer's cache (0 for an unsupported shape), and the carving of
+ * a caller buffer of at least that size into *cache (host only, no launch).
+ * The contents start undefined; only slots that were appended are read. */
+size_t fmoe_kv_cache_bytes(int mode, int batch, int kv_heads, int head_dim, int64_t capacity);
+int fmoe_kv_cache_init(fmoe_kv_cache_t* cache, int mode, int batch, int kv_heads, int head_dim,
+                       int64_t capacity, void* buffer, size_t buffer_bytes);
+
+/* Append T_new positions: k, v bf16 [batch, kv_heads, T_new, head_dim] for
+ * positions pos .. pos+T_new-1 (pos_dev, when not NULL, is a device int64
+ * read instead of pos: CUDA-graph friendly).  Replaces the append half of
+ * KVCache::update_and_fetch, src/cache.rs:266-310 (the fetch half is the
+ * cache itself: attention reads it in place).  turbo_bits 2..4 applies the
+ * TurboQuant round trip in bf16 mode; 0 stores the rows as given.  In affine
+ * mode rows are rotated and quantised on the way in. */
+int fmoe_kv_append(const fmoe_kv_cache_t* cache, const void* k, const void* v, int64_t T_new,
+                   int64_t pos, const int64_t* pos_dev, int turbo_bits, void* stream);
+
+/* Decode attention of one query token per sequence over the cache:
+ * out[b, h] = softmax(scale * q[b, h] . K^T) . V over the first n_valid slots
+ * of kv head h / (q_heads / kv_heads) (GQA), q / out bf16 [batch, q_heads,
+ * head_dim].  Replaces fast::scaled_dot_product_attention at
+ * src/model/gemma4_attention.rs:95-104 with the causal / sliding masks of
+ * src/model/mod.rs:682-753 (all cached slots are attendable: the ring holds
+ * exactly the window).  n_valid = min(positions appended, capacity);
+ * n_valid_dev (device int64, optional) overrides it at run time.
+ * q_heads / kv_heads in {1, 2, 4, 8}.  One kernel (split-KV with an in-kernel
+ * merge).  The workspace (fmoe_attn_decode_workspace_bytes) must be
+ * zero-filled before first use; each call leaves its merge counters at zero.
+ * Calls sharing a workspace must not overlap on the GPU. */
+size_t fmoe_attn_decode_workspace_bytes(const fmoe_kv_cache_t* cache, int q_heads);
+int fmoe_attn_decode(const fmoe_kv_cache_t* cache, const void* q, int q_heads, int64_t n_valid,
+                     const int64_t* n_valid_dev, float scale, void* out, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* TurboQuant quantise -> dequantise round trip of `rows` bf16 vectors of
+ * length head_dim (256 or 512), bits 2..4: turbo_round_trip_kv,
+ * src/cache.rs:94-129 (the rotation R = H diag(signs) applied as a fast
+ * Walsh-Hadamard transform). */
+int fmoe_turbo_round_trip(const void* x, int64_t rows, int head_dim, int bits, void* out,
+                          void* stream);
+
 /* Synchronises `stream` and reads the status word every workspace starts with:
  * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
