@@ -46,6 +46,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="moe30_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
+    ap.add_argument("--attn-case", default=None, metavar="MODE:B:T",
+                    help="run only one decode-attention case (mode affine|bf16, batch, context): four launches, "
+                         "L2 flushed before each, the last one timed (a small case for profilers)")
     ap.add_argument("--layers", type=int, default=30,
                     help="decoder layers in the step (30 = the model; fewer only for small profiling cases)")
     return ap.parse_args()
@@ -301,13 +305,76 @@ def run_ours(args, rank, world, local):
                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
         "clocks": clocks.summary(),
     }
+    if rank == 0 and world == 1 and not args.no_attn:
+        del graph, stack, layers
+        torch.cuda.empty_cache()
+        result["kv_attention"] = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"])
+        graph = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(layers, T)
+        result["cpu_baseline"] = cpu_baseline(None, T)
     if rank == 0:
         print(json.dumps(result), flush=True)
     del graph
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# quantised-KV decode attention: 16 query heads, 8 KV heads,
+# head_dim 256; K/V N(0,1) with 1% outlier channels x20; WHT-rotated affine
+# 4-bit K / 8-bit V (the benchmark's cache) and the reference's bf16 cache.
+
+ATTN_CASES = [  # (mode, batch, positions appended, sliding window or None)
+    ("affine", 1, 32768, None), ("affine", 1, 32768, 1024), ("affine", 32, 8192, None),
+    ("affine", 32, 32768, None), ("affine", 32, 32768, 1024), ("bf16", 32, 32768, None),
+]
+
+
+def attn_submeasure(fm, torch, dev, peak_gbs, iters=20, cases=ATTN_CASES):
+    D, HKV, HQ = 256, 8, 16
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)  # > L2 (126 MB)
+    out = []
+    for mode, B, T, win in cases:
+        cap = win or T
+        if mode == "affine":
+            cache = fm.KVCache.new_affine(B, HKV, D, cap, window=win, device=dev)
+            per_pos = D // 2 + D + 4 * (D // 64) * 2
+        else:
+            cache = fm.KVCache(B, HKV, D, cap, window=win, device=dev)
+            per_pos = 4 * D
+        g = torch.Generator(device=dev).manual_seed(77)
+        ch = torch.randperm(D, generator=torch.Generator().manual_seed(78))[:3].to(dev)
+        step = max(1, (1 << 27) // (B * HKV * D * 2))
+        done = 0
+        while done < T:
+            t = min(step, T - done)
+            kv = torch.randn(2, B, HKV, t, D, generator=g, device=dev)
+            kv[..., ch] *= 20.0
+            kv = kv.to(torch.bfloat16)
+            cache.update(kv[0], kv[1])
+            done += t
+        q = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+        times = []
+        for i in range(iters + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st = torch.cuda.current_stream()
+            a.record(st)
+            cache.attend(q, 1.0)
+            b.record(st)
+            torch.cuda.synchronize()
+            if i >= 3:
+                times.append(a.elapsed_time(b) * 1e3)
+        us = statistics.median(times)
+        n = cache.stored_len()
+        alg = B * HKV * n * per_pos + 2 * B * HQ * D * 2
+        out.append({"cache": mode, "batch": B, "context": T, "window": win, "attended": n, "us": round(us, 1),
+                    "alg_bytes": alg, "gbs": round(alg / us / 1e3, 1), "frac": round(alg / us / 1e3 / peak_gbs, 3)})
+        del cache
+        torch.cuda.empty_cache()
+    return {"kernel": "attn_affine_kernel / attn_bf16_kernel (one launch per call, split-KV with in-kernel merge)",
+            "shape": "Hq 16, Hkv 8, head_dim 256, scale 1.0; L2 flushed before each timed launch; median of 20",
+            "cases": out}
 
 
 # ---------------------------------------------------------------------------
@@ -392,10 +459,25 @@ def run_reference(args, rank, world):
     print(json.dumps(out), flush=True)
 
 
+def run_attn_case(args):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    mode, B, T = args.attn_case.split(":")
+    peaks, _ = load_peaks()
+    res = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"], iters=1, cases=[(mode, int(B), int(T), None)])
+    print(json.dumps({"attn_case": args.attn_case, **res}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
-    if args.impl == "reference":
+    if args.attn_case:
+        run_attn_case(args)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local)

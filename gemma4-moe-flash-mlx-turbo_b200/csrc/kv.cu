@@ -248,18 +248,22 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 
 // ---------------------------------------------------------------------------
 // Split-KV decode attention.  CTA = (split, kv head, batch); its GQ = Hq/Hkv
-// query heads are the N columns of the score MMAs.  A split covers S
-// consecutive slots, processed in chunks of CH positions through an NST-stage
-// ring of TMA bulk copies (K and V rows with their scales / biases), so the
-// next chunk streams in while this one is computed:
-//   scores  mma.sync, K rows as A (16 positions x 64-wide group) straight from
-//           the 4-bit codes ((128+q) bf16 built in registers), query as B.
-//           The rotated query is fp32; it is split into bf16 hi + lo parts
-//           (two MMAs) so the scores keep ~16 mantissa bits.  Affine fixup
-//           per group: s * C + (b - 128 s) * sum(q).
-//   softmax running max / sum per head across chunks (online rescaling).
-//   P.V     CUDA cores: a thread owns 4 columns, V dequantised in fp32
-//           (fmaf(scale, q, bias), the oracle's dequantisation).
+// query heads are the N columns of the MMAs.  A split covers S consecutive
+// slots, processed in chunks of CH positions through a two-stage ring of TMA
+// bulk copies (K and V rows with their scales / biases): the next chunk
+// streams in while this one is computed.  Per chunk:
+//   scores  mma.sync, K rows as A (16 positions x 64-wide group).  Affine
+//           cache: A = (128 + q) bf16 built in registers from the 4-bit codes;
+//           the rotated query is fp32, split into bf16 hi + lo parts (two
+//           MMAs, ~16 mantissa bits kept), B fragments prepared once per CTA;
+//           per-group fixup s * C + (b - 128 s) * sum(q).  bf16 cache: A = K.
+//   softmax running max / sum per head across chunks (online rescaling); the
+//           tile maxima are exchanged through shared memory, probabilities
+//           stay with the warp that scored them.
+//   P.V     affine: tensor cores (f16): A = V codes as (1024 + q), two
+//           positions per register; B = p * v_scale; a second MMA with
+//           A = -1024 removes the offset; the bias half of V is summed in fp32.
+//           bf16: CUDA cores, a thread owns 4 columns of one position phase.
 // A split's (m, l, o) goes to the workspace; the last CTA of a (batch, kv
 // head) to finish merges the splits (log-sum-exp), normalises, applies the
 // inverse rotation and writes the output, so one launch does the whole op.
@@ -277,31 +281,61 @@ struct AtCfg {
   static constexpr int TPC = CH / 16;         // 16-position tiles per chunk
   static constexpr int WPT = 8 / TPC;         // warps per tile (they split the groups)
   static constexpr int GPW = G / WPT;         // groups per warp
-  static constexpr int U = D / 4;             // P.V: 4-column units per row
-  static constexpr int NPH = 256 / U;         // P.V: position phases
-  static_assert(STAGE % 128 == 0 && CH % 32 == 0 && G % WPT == 0 && 256 % U == 0, "attention tiling");
+  // bf16 P.V on CUDA cores: a thread owns 4 columns of one position phase
+  static constexpr int U = D / 4;
+  static constexpr int NPH = 256 / U;
+  // affine P.V on tensor cores: a warp owns one 64-column group and KTW of
+  // the chunk's KT 16-position k-tiles
+  static constexpr int KT = CH / 16;
+  static constexpr int WPG = 8 / G;
+  static constexpr int KTW = KT / WPG;
+  static constexpr int RSL = MODE == FMOE_KV_BF16 ? NPH : WPG;  // partial rows reduced at the end
+  static_assert(STAGE % 128 == 0 && CH % 32 == 0 && G % WPT == 0 && 256 % U == 0 && KT % WPG == 0,
+                "attention tiling");
 };
 
 constexpr int kMaxSplits = 1024;
+constexpr int kRed2Off = 8 * kMaxSplits * 4;  // merged rows, after the merge weights
 
-template <int P, int MODE, int GQ>
-struct AtSmem {
-  using C = AtCfg<P, MODE>;
-  static constexpr int D = C::D;
-  static constexpr int BAR = C::NST * C::STAGE;                              // mbarriers
-  static constexpr int QH = BAR + 64;                                        // bf16 [GQ][D] query (hi part)
-  static constexpr int QL = QH + GQ * D * 2;                                 // bf16 [GQ][D] lo part (affine)
-  static constexpr int QS = QL + (MODE == FMOE_KV_AFFINE ? GQ * D * 2 : 0);  // f32 [GQ][G] group sums
-  static constexpr int SC = QS + 16 * ((GQ * C::G * 4 + 15) / 16);           // f32 [WPT][GQ][CH] scores
-  static constexpr int PR = SC + C::WPT * GQ * C::CH * 4;                    // f32 [GQ][CH] probabilities
-  static constexpr int ST = PR + GQ * C::CH * 4;                             // f32 m[8] l[8] f[8], int flags[8]
-  static constexpr int BYTES = ST + 32 * 4;
-  // aliases of the stage area once every chunk is consumed
-  static constexpr int RED = 0;                 // f32 [NPH][GQ][D] P.V phase partials
-  static constexpr int WTS = 0;                 // f32 [GQ][kMaxSplits] merge weights
-  static constexpr int RED2 = 8 * kMaxSplits * 4;  // f32 [GQ][D] merged rows
-  static_assert(C::NPH * GQ * D * 4 <= BAR && RED2 + GQ * D * 4 <= BAR, "attention smem aliases");
+// Global sources of one split (first slot p_begin of (batch, kv head) bh).
+struct SplitSrc {
+  const uint8_t *kc, *ks, *kb, *vc, *vs, *vb;
 };
+template <class C>
+__device__ __forceinline__ SplitSrc split_src(const KvDev& c, int64_t row0) {
+  SplitSrc s;
+  s.kc = reinterpret_cast<const uint8_t*>(c.k) + row0 * C::KRB;
+  s.vc = reinterpret_cast<const uint8_t*>(c.v) + row0 * C::VRB;
+  s.ks = reinterpret_cast<const uint8_t*>(c.ks) + row0 * C::SB;
+  s.kb = reinterpret_cast<const uint8_t*>(c.kb) + row0 * C::SB;
+  s.vs = reinterpret_cast<const uint8_t*>(c.vs) + row0 * C::SB;
+  s.vb = reinterpret_cast<const uint8_t*>(c.vb) + row0 * C::SB;
+  return s;
+}
+
+// Chunk chn of the split -> stage chn % NST.  Rows are copied in even counts
+// (16-byte multiples for the 8-byte scale rows); the capacity is a multiple of
+// 16, so the extra row exists.
+template <class C, int MODE>
+__device__ __forceinline__ void issue_chunk(uint8_t* smem, uint64_t* bar, const SplitSrc& src, int chn, int nS) {
+  const int s = chn % C::NST;
+  const int rows = (min(C::CH, nS - chn * C::CH) + 1) & ~1;
+  const int64_t r0 = (int64_t)chn * C::CH;
+  uint8_t* sb = smem + s * C::STAGE;
+  if (MODE == FMOE_KV_BF16) {
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)rows * (C::KRB + C::VRB));
+    bulk_g2s(sb, src.kc + r0 * C::KRB, rows * C::KRB, &bar[s]);
+    bulk_g2s(sb + C::VC, src.vc + r0 * C::VRB, rows * C::VRB, &bar[s]);
+  } else {
+    mbar_arrive_expect_tx(&bar[s], (uint32_t)rows * (C::KRB + C::VRB + 4 * C::SB));
+    bulk_g2s(sb, src.kc + r0 * C::KRB, rows * C::KRB, &bar[s]);
+    bulk_g2s(sb + C::KS, src.ks + r0 * C::SB, rows * C::SB, &bar[s]);
+    bulk_g2s(sb + C::KB, src.kb + r0 * C::SB, rows * C::SB, &bar[s]);
+    bulk_g2s(sb + C::VC, src.vc + r0 * C::VRB, rows * C::VRB, &bar[s]);
+    bulk_g2s(sb + C::VS, src.vs + r0 * C::SB, rows * C::SB, &bar[s]);
+    bulk_g2s(sb + C::VB, src.vb + r0 * C::SB, rows * C::SB, &bar[s]);
+  }
+}
 
 __device__ __forceinline__ void mma_group_q4_hl(float (&acc)[4], uint2 wlo, uint2 whi, const BFrag4& bh,
                                                 const BFrag4& bl) {
@@ -328,25 +362,140 @@ __device__ __forceinline__ void finish_row(float (&v)[P], float l, float inv_sqr
   store_row_bf16<P>(orow, lane, v);
 }
 
-template <int P, int MODE, int GQ>
+// End of a split, called by every thread of the CTA.  red holds RSL partial
+// rows per head ([RSL][GQ][D] f32, at the start of the stage area), st_m /
+// st_l the split's running max / sum per head.  One split: finish the rows.
+// Several: publish (m, l, o) and let the last CTA of the (batch, kv head)
+// merge them.
+template <int P, int MODE, int GQ, int RSL>
+__device__ __forceinline__ void attn_epilogue(uint8_t* smem, const float* st_m, float* st_l, int* flags, bool failed,
+                                              int Hq, int b, int hk, int64_t bh, int split, int nsplit,
+                                              float inv_sqrt_d, float2* part_ml, float* part_o, unsigned* ctr,
+                                              bf16* out) {
+  constexpr int D = 32 * P;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const float* red = reinterpret_cast<const float*>(smem);
+  if (warp < GQ) {
+    const int h = warp;
+    float v[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int r = 0; r < RSL; ++r) s += red[(r * GQ + h) * D + lane * P + i];
+      v[i] = s;
+    }
+    const float m = st_m[h], l = failed ? 0.f : st_l[h];
+    const int64_t row = (int64_t)b * Hq + hk * GQ + h;
+    if (nsplit == 1) {
+      finish_row<P, MODE>(v, l, inv_sqrt_d, lane, out + row * D);
+    } else {
+      float4* po = reinterpret_cast<float4*>(part_o + (row * nsplit + split) * D + lane * P);
+#pragma unroll
+      for (int i = 0; i < P / 4; ++i) __stcg(po + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
+      if (lane == 0) __stcg(part_ml + row * nsplit + split, make_float2(m, l));
+    }
+  }
+  if (nsplit == 1) return;
+
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(&ctr[bh], 1u);
+    flags[1] = prev == (unsigned)(nsplit - 1);
+    if (flags[1]) ctr[bh] = 0u;  // every split has arrived: ready for the next call
+  }
+  __syncthreads();
+  if (!flags[1]) return;
+  __threadfence();
+  float* wts = reinterpret_cast<float*>(smem);
+  float* red2 = reinterpret_cast<float*>(smem + kRed2Off);
+  if (warp < GQ) {
+    const int64_t row = (int64_t)b * Hq + hk * GQ + warp;
+    float M = -INFINITY;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float2 ml = __ldcg(part_ml + row * nsplit + s);
+      if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f;
+    for (int s = lane; s < nsplit; s += 32) {
+      const float2 ml = __ldcg(part_ml + row * nsplit + s);
+      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
+      wts[warp * kMaxSplits + s] = w;
+      L = fmaf(w, ml.y, L);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (lane == 0) st_l[warp] = L;
+  }
+  __syncthreads();
+  for (int pi = tid; pi < GQ * (D / 4); pi += blockDim.x) {
+    const int h = pi / (D / 4), d4 = pi % (D / 4);
+    const int64_t row = (int64_t)b * Hq + hk * GQ + h;
+    const float4* src = reinterpret_cast<const float4*>(part_o + row * nsplit * D) + d4;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = wts[h * kMaxSplits + s];
+      const float4 x = __ldcg(src + (int64_t)s * (D / 4));
+      if (w != 0.f) {
+        a.x = fmaf(w, x.x, a.x);
+        a.y = fmaf(w, x.y, a.y);
+        a.z = fmaf(w, x.z, a.z);
+        a.w = fmaf(w, x.w, a.w);
+      }
+    }
+    *reinterpret_cast<float4*>(red2 + h * D + d4 * 4) = a;
+  }
+  __syncthreads();
+  if (warp < GQ) {
+    float v[P];
+#pragma unroll
+    for (int i = 0; i < P; ++i) v[i] = red2[warp * D + lane * P + i];
+    finish_row<P, MODE>(v, st_l[warp], inv_sqrt_d, lane, out + ((int64_t)b * Hq + hk * GQ + warp) * D);
+  }
+}
+
+// ---- affine (WHT-rotated 4-bit K / 8-bit V) cache
+
+template <int P, int GQ>
+struct AffSmem {
+  using C = AtCfg<P, FMOE_KV_AFFINE>;
+  static constexpr int D = C::D, G = C::G;
+  static constexpr int BAR = C::NST * C::STAGE;                    // mbarriers
+  static constexpr int QF = BAR + 64;                              // uint4 [G][hi, lo][4*GQ lanes][2] B fragments
+  static constexpr int QR = QF + G * 2 * 4 * GQ * 32;              // bf16 [hi, lo][GQ][D] rotated query rows
+  static constexpr int QS = QR + 2 * GQ * D * 2;                   // f32 [GQ][G] group sums of hi + lo
+  static constexpr int SC = QS + 16 * ((GQ * G * 4 + 15) / 16);    // f32 [GQ][CH] second-half partial scores
+  static constexpr int TM = SC + (C::WPT > 1 ? GQ * C::CH * 4 : 0);  // f32 [TPC][8] tile maxima / sums
+  static constexpr int PR = TM + C::TPC * 8 * 4;                   // f32 [GQ][CH] probabilities
+  static constexpr int ST = PR + GQ * C::CH * 4;                   // f32 m[8] l[8] pad[8], int flags[8]
+  static constexpr int BYTES = ST + 32 * 4;
+  static_assert(C::RSL * GQ * D * 4 <= BAR && kRed2Off + GQ * D * 4 <= BAR, "attention smem aliases");
+};
+
+template <int P, int GQ>
 __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
-    attn_decode_kernel(const KvDev c, const bf16* __restrict__ q, int Hq, int S, int nsplit, int64_t nvalid,
+    attn_affine_kernel(const KvDev c, const bf16* __restrict__ q, int Hq, int S, int nsplit, int64_t nvalid,
                        const int64_t* __restrict__ nvalid_dev, float scale, float inv_sqrt_d,
                        float2* __restrict__ part_ml, float* __restrict__ part_o, unsigned* __restrict__ ctr,
                        bf16* __restrict__ out, int* __restrict__ status) {
-  using C = AtCfg<P, MODE>;
-  using Sm = AtSmem<P, MODE, GQ>;
-  constexpr int D = C::D, G = C::G, CH = C::CH, NST = C::NST;
+  using C = AtCfg<P, FMOE_KV_AFFINE>;
+  using Sm = AffSmem<P, GQ>;
+  constexpr int D = C::D, G = C::G, CH = C::CH, NST = C::NST, TPC = C::TPC, WPT = C::WPT, GPW = C::GPW;
+  static_assert(GPW == 4, "a scale row of a warp's groups is one 8-byte load");
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Sm::BAR);
-  bf16* qh = reinterpret_cast<bf16*>(smem + Sm::QH);
-  bf16* ql = reinterpret_cast<bf16*>(smem + Sm::QL);
+  uint4* qf = reinterpret_cast<uint4*>(smem + Sm::QF);
+  bf16* qrow = reinterpret_cast<bf16*>(smem + Sm::QR);
   float* qsum = reinterpret_cast<float*>(smem + Sm::QS);
-  float* sc = reinterpret_cast<float*>(smem + Sm::SC);
+  float* scp = reinterpret_cast<float*>(smem + Sm::SC);
+  float* tmax = reinterpret_cast<float*>(smem + Sm::TM);
   float* pr = reinterpret_cast<float*>(smem + Sm::PR);
   float* st_m = reinterpret_cast<float*>(smem + Sm::ST);
   float* st_l = st_m + 8;
-  float* st_f = st_m + 16;
   int* flags = reinterpret_cast<int*>(st_m + 24);  // [0] a wait gave up, [1] last arriver
 
   const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
@@ -357,37 +506,355 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
   const int64_t p_begin = (int64_t)split * S;
   const int nS = (int)max((int64_t)0, min((int64_t)S, nv - p_begin));
   const int nch = (nS + CH - 1) / CH;
+  const SplitSrc src = split_src<C>(c, bh * c.cap + p_begin);
 
-  const int64_t row0 = bh * c.cap + p_begin;  // first slot of this split
-  const uint8_t* kc_g = reinterpret_cast<const uint8_t*>(c.k) + row0 * C::KRB;
-  const uint8_t* vc_g = reinterpret_cast<const uint8_t*>(c.v) + row0 * C::VRB;
-  const uint8_t* ks_g = reinterpret_cast<const uint8_t*>(c.ks) + row0 * C::SB;
-  const uint8_t* kb_g = reinterpret_cast<const uint8_t*>(c.kb) + row0 * C::SB;
-  const uint8_t* vs_g = reinterpret_cast<const uint8_t*>(c.vs) + row0 * C::SB;
-  const uint8_t* vb_g = reinterpret_cast<const uint8_t*>(c.vb) + row0 * C::SB;
+  if (tid == 0) {
+#pragma unroll
+    for (int s = 0; s < NST; ++s) mbar_init(&bar[s], 1);
+    mbar_fence_init();
+  }
+  if (tid < 8) {
+    st_m[tid] = -INFINITY;
+    st_l[tid] = 0.f;
+    flags[tid] = 0;
+  }
+  __syncthreads();
+  int issued = 0;  // meaningful in thread 0 only
+  if (tid == 0)
+    for (; issued < min(NST, nch); ++issued) issue_chunk<C, FMOE_KV_AFFINE>(smem, bar, src, issued, nS);
 
-  // Chunk ch -> stage ch % NST.  Rows are copied in even counts (16-byte
-  // multiples for the 8-byte scale rows); the capacity is a multiple of 16,
-  // so the extra row exists.
-  auto issue = [&](int chn) {
-    const int s = chn % NST;
-    const int rows = (min(CH, nS - chn * CH) + 1) & ~1;
-    const int64_t r0 = (int64_t)chn * CH;
-    uint8_t* sb = smem + s * C::STAGE;
-    if (MODE == FMOE_KV_BF16) {
-      mbar_arrive_expect_tx(&bar[s], (uint32_t)rows * (C::KRB + C::VRB));
-      bulk_g2s(sb, kc_g + r0 * C::KRB, rows * C::KRB, &bar[s]);
-      bulk_g2s(sb + C::VC, vc_g + r0 * C::VRB, rows * C::VRB, &bar[s]);
-    } else {
-      mbar_arrive_expect_tx(&bar[s], (uint32_t)rows * (C::KRB + C::VRB + 4 * C::SB));
-      bulk_g2s(sb, kc_g + r0 * C::KRB, rows * C::KRB, &bar[s]);
-      bulk_g2s(sb + C::KS, ks_g + r0 * C::SB, rows * C::SB, &bar[s]);
-      bulk_g2s(sb + C::KB, kb_g + r0 * C::SB, rows * C::SB, &bar[s]);
-      bulk_g2s(sb + C::VC, vc_g + r0 * C::VRB, rows * C::VRB, &bar[s]);
-      bulk_g2s(sb + C::VS, vs_g + r0 * C::SB, rows * C::SB, &bar[s]);
-      bulk_g2s(sb + C::VB, vb_g + r0 * C::SB, rows * C::SB, &bar[s]);
+  // rotated query rows (hi / lo bf16 parts) and their group sums
+  if (warp < GQ) {
+    float v[P];
+    load_row_f32<P>(q + ((int64_t)b * Hq + hk * GQ + warp) * D, lane, v);
+    warp_fwht<P>(v, lane);
+    float hi[P], lo[P], s = 0.f;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      v[i] *= inv_sqrt_d;
+      hi[i] = round_bf(v[i]);
+      lo[i] = round_bf(v[i] - hi[i]);
+      s += hi[i] + lo[i];
     }
-  };
+    store_row_bf16<P>(qrow + warp * D, lane, hi);
+    store_row_bf16<P>(qrow + (GQ + warp) * D, lane, lo);
+#pragma unroll
+    for (int o = 1; o < 64 / P; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane % (64 / P) == 0) qsum[warp * G + lane / (64 / P)] = s;
+  }
+  __syncthreads();
+  // B fragments of the query, one warp per group; lanes g >= GQ use zeros
+  if (warp < G && lane < 4 * GQ) {
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl) {
+      const uint8_t* p = reinterpret_cast<const uint8_t*>(qrow + (hl * GQ + g) * D) + warp * 128 + 32 * t;
+      const BFrag4 f = make_bfrag4(lds_u4(p), lds_u4(p + 16));
+      uint4* dst = qf + ((warp * 2 + hl) * 4 * GQ + lane) * 2;
+      dst[0] = make_uint4(f.b0[0], f.b0[1], f.b0[2], f.b0[3]);
+      dst[1] = make_uint4(f.b1[0], f.b1[1], f.b1[2], f.b1[3]);
+    }
+  }
+  __syncthreads();
+  float qs0[G], qs1[G];  // group sums of heads 2t, 2t+1 (the C fragment's columns)
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    qs0[gi] = 2 * t < GQ ? qsum[(2 * t) * G + gi] : 0.f;
+    qs1[gi] = 2 * t + 1 < GQ ? qsum[(2 * t + 1) * G + gi] : 0.f;
+  }
+
+  const int tile = warp % TPC, wp = warp / TPC, r0 = tile * 16;
+  const int pv_grp = warp % G, pv_slot = warp / G;
+  float m_run0 = -INFINITY, m_run1 = -INFINITY;  // heads 2t, 2t+1 (same in every thread)
+  float l_run0 = 0.f, l_run1 = 0.f;              // this lane's rows of its tile
+  float acc[4][4], cor[4], bacc0 = 0.f, bacc1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    cor[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  }
+
+  int ch = 0;
+  for (; ch < nch; ++ch) {
+    const int stg = ch % NST;
+    const int nrow = min(CH, nS - ch * CH);
+    const uint8_t* sb = smem + stg * C::STAGE;
+    if (!mbar_wait(&bar[stg], (uint32_t)(ch / NST) & 1u, status, 51)) atomicOr(&flags[0], 1);
+
+    // ---- scores of tile `tile` over the warp's groups (fp32, unscaled)
+    const bool live = r0 < nrow;
+    float y[4] = {0.f, 0.f, 0.f, 0.f};
+    if (live) {
+      const int rl = min(r0 + g, nrow - 1), rh = min(r0 + g + 8, nrow - 1);
+      const uint2 ksl = lds_u2(sb + C::KS + (rl * G + wp * GPW) * 2), kbl = lds_u2(sb + C::KB + (rl * G + wp * GPW) * 2);
+      const uint2 ksh = lds_u2(sb + C::KS + (rh * G + wp * GPW) * 2), kbh = lds_u2(sb + C::KB + (rh * G + wp * GPW) * 2);
+      const float sl[4] = {bf16lo(ksl.x), bf16hi(ksl.x), bf16lo(ksl.y), bf16hi(ksl.y)};
+      const float bl[4] = {bf16lo(kbl.x), bf16hi(kbl.x), bf16lo(kbl.y), bf16hi(kbl.y)};
+      const float sh[4] = {bf16lo(ksh.x), bf16hi(ksh.x), bf16lo(ksh.y), bf16hi(ksh.y)};
+      const float bh_[4] = {bf16lo(kbh.x), bf16hi(kbh.x), bf16lo(kbh.y), bf16hi(kbh.y)};
+#pragma unroll
+      for (int gg = 0; gg < GPW; ++gg) {
+        const int gi = wp * GPW + gg;
+        BFrag4 fh, fl;
+        if (g < GQ) {
+          const uint4* src4 = qf + ((gi * 2) * 4 * GQ + lane) * 2;
+          const uint4 h0 = src4[0], h1 = src4[1];
+          const uint4 l0 = src4[8 * GQ], l1 = src4[8 * GQ + 1];
+          fh = BFrag4{{h0.x, h0.y, h0.z, h0.w}, {h1.x, h1.y, h1.z, h1.w}};
+          fl = BFrag4{{l0.x, l0.y, l0.z, l0.w}, {l1.x, l1.y, l1.z, l1.w}};
+        } else {
+          fh = BFrag4{{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+          fl = fh;
+        }
+        const uint2 wl = lds_u2(sb + rl * C::KRB + gi * 32 + 8 * t);
+        const uint2 wh = lds_u2(sb + rh * C::KRB + gi * 32 + 8 * t);
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_group_q4_hl(cc, wl, wh, fh, fl);
+        // static register indexes (wp is 0 or 1)
+        const float q0 = wp ? qs0[(GPW + gg) % G] : qs0[gg], q1 = wp ? qs1[(GPW + gg) % G] : qs1[gg];
+        const float ol = fmaf(-128.f, sl[gg], bl[gg]), oh = fmaf(-128.f, sh[gg], bh_[gg]);
+        y[0] += fmaf(sl[gg], cc[0], ol * q0);
+        y[1] += fmaf(sl[gg], cc[1], ol * q1);
+        y[2] += fmaf(sh[gg], cc[2], oh * q0);
+        y[3] += fmaf(sh[gg], cc[3], oh * q1);
+      }
+    }
+    if constexpr (WPT > 1) {  // the second half of the groups adds through shared memory
+      if (wp == 1 && live) {
+        if (2 * t < GQ) {
+          scp[(2 * t) * CH + r0 + g] = y[0];
+          scp[(2 * t) * CH + r0 + g + 8] = y[2];
+        }
+        if (2 * t + 1 < GQ) {
+          scp[(2 * t + 1) * CH + r0 + g] = y[1];
+          scp[(2 * t + 1) * CH + r0 + g + 8] = y[3];
+        }
+      }
+      __syncthreads();
+      if (wp == 0 && live) {
+        if (2 * t < GQ) {
+          y[0] += scp[(2 * t) * CH + r0 + g];
+          y[2] += scp[(2 * t) * CH + r0 + g + 8];
+        }
+        if (2 * t + 1 < GQ) {
+          y[1] += scp[(2 * t + 1) * CH + r0 + g];
+          y[3] += scp[(2 * t + 1) * CH + r0 + g + 8];
+        }
+      }
+    }
+    // C fragment: y[0] (row g, head 2t), y[1] (g, 2t+1), y[2] (g+8, 2t), y[3] (g+8, 2t+1)
+    const bool v0 = r0 + g < nrow, v1 = r0 + g + 8 < nrow;
+    const float s00 = y[0] * scale, s01 = y[1] * scale, s10 = y[2] * scale, s11 = y[3] * scale;
+    if (wp == 0) {
+      float mx0 = fmaxf(v0 ? s00 : -INFINITY, v1 ? s10 : -INFINITY);
+      float mx1 = fmaxf(v0 ? s01 : -INFINITY, v1 ? s11 : -INFINITY);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      if (g == 0) {
+        tmax[tile * 8 + 2 * t] = mx0;
+        tmax[tile * 8 + 2 * t + 1] = mx1;
+      }
+    }
+    __syncthreads();
+    if (flags[0]) break;  // a copy never landed: every thread leaves the loop here
+
+    // ---- running max (identical in every thread), probabilities of the tile
+    float cm0 = -INFINITY, cm1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < TPC; ++w) {
+      cm0 = fmaxf(cm0, tmax[w * 8 + 2 * t]);
+      cm1 = fmaxf(cm1, tmax[w * 8 + 2 * t + 1]);
+    }
+    const float mn0 = fmaxf(m_run0, cm0), mn1 = fmaxf(m_run1, cm1);
+    const float f0 = expf(m_run0 - mn0), f1 = expf(m_run1 - mn1);
+    m_run0 = mn0;
+    m_run1 = mn1;
+    if (wp == 0) {
+      float p00 = 0.f, p01 = 0.f, p10 = 0.f, p11 = 0.f;
+      if (live) {
+        p00 = v0 ? expf(s00 - mn0) : 0.f;
+        p01 = v0 ? expf(s01 - mn1) : 0.f;
+        p10 = v1 ? expf(s10 - mn0) : 0.f;
+        p11 = v1 ? expf(s11 - mn1) : 0.f;
+        if (2 * t < GQ) {
+          pr[(2 * t) * CH + r0 + g] = p00;
+          pr[(2 * t) * CH + r0 + g + 8] = p10;
+        }
+        if (2 * t + 1 < GQ) {
+          pr[(2 * t + 1) * CH + r0 + g] = p01;
+          pr[(2 * t + 1) * CH + r0 + g + 8] = p11;
+        }
+      }
+      l_run0 = fmaf(l_run0, f0, p00 + p10);
+      l_run1 = fmaf(l_run1, f1, p01 + p11);
+    }
+    __syncthreads();
+
+    // ---- P.V: o^T[d, h] += V^T[d, pos] (p s)[pos, h] (see the header comment);
+    // m-tile i of the group: rows g / g+8 are columns grp*64 + 8g + 2i / +1
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[i][0] *= f0;
+      acc[i][1] *= f1;
+      acc[i][2] *= f0;
+      acc[i][3] *= f1;
+    }
+    cor[0] *= f0;
+    cor[1] *= f1;
+    cor[2] *= f0;
+    cor[3] *= f1;
+    bacc0 *= f0;
+    bacc1 *= f1;
+    {
+      const bf16* vsc = reinterpret_cast<const bf16*>(sb + C::VS);
+      const bf16* vbi = reinterpret_cast<const bf16*>(sb + C::VB);
+      const uint8_t* vcol = sb + C::VC + pv_grp * 64 + 8 * g;
+      float bs = 0.f;  // sum of p * v_bias over this lane's positions, head g
+#pragma unroll
+      for (int kk = 0; kk < C::KTW; ++kk) {
+        const int pk = (pv_slot * C::KTW + kk) * 16;
+        if (pk < nrow) {
+          const int p0 = pk + 2 * t, p2 = p0 + 8;
+          uint32_t b0 = 0u, b1 = 0u;
+          if (g < GQ) {
+            const float2 pa = *reinterpret_cast<const float2*>(pr + g * CH + p0);
+            const float2 pc = *reinterpret_cast<const float2*>(pr + g * CH + p2);
+            const bool q0 = p0 < nrow, q1 = p0 + 1 < nrow, q2 = p2 < nrow, q3 = p2 + 1 < nrow;
+            const float w0 = q0 ? pa.x * bf2f(vsc[p0 * G + pv_grp]) : 0.f;
+            const float w1 = q1 ? pa.y * bf2f(vsc[(p0 + 1) * G + pv_grp]) : 0.f;
+            const float w2 = q2 ? pc.x * bf2f(vsc[p2 * G + pv_grp]) : 0.f;
+            const float w3 = q3 ? pc.y * bf2f(vsc[(p2 + 1) * G + pv_grp]) : 0.f;
+            if (q0) bs = fmaf(pa.x, bf2f(vbi[p0 * G + pv_grp]), bs);
+            if (q1) bs = fmaf(pa.y, bf2f(vbi[(p0 + 1) * G + pv_grp]), bs);
+            if (q2) bs = fmaf(pc.x, bf2f(vbi[p2 * G + pv_grp]), bs);
+            if (q3) bs = fmaf(pc.y, bf2f(vbi[(p2 + 1) * G + pv_grp]), bs);
+            b0 = pack_f16x2(w0, w1);
+            b1 = pack_f16x2(w2, w3);
+          }
+          const uint2 wa = lds_u2(vcol + p0 * C::VRB), wb = lds_u2(vcol + (p0 + 1) * C::VRB);
+          const uint2 wc = lds_u2(vcol + p2 * C::VRB), wd = lds_u2(vcol + (p2 + 1) * C::VRB);
+          // bytes j of two position rows side by side, then f16 (1024 + q) pairs
+          const uint32_t ab0 = prmt(wa.x, wb.x, 0x5140u), ab1 = prmt(wa.x, wb.x, 0x7362u);
+          const uint32_t ab2 = prmt(wa.y, wb.y, 0x5140u), ab3 = prmt(wa.y, wb.y, 0x7362u);
+          const uint32_t cd0 = prmt(wc.x, wd.x, 0x5140u), cd1 = prmt(wc.x, wd.x, 0x7362u);
+          const uint32_t cd2 = prmt(wc.y, wd.y, 0x5140u), cd3 = prmt(wc.y, wd.y, 0x7362u);
+          const uint32_t K = 0x64646464u;
+          mma16816_f16(acc[0], prmt(ab0, K, 0x4140u), prmt(ab0, K, 0x4342u), prmt(cd0, K, 0x4140u),
+                       prmt(cd0, K, 0x4342u), b0, b1);
+          mma16816_f16(acc[1], prmt(ab1, K, 0x4140u), prmt(ab1, K, 0x4342u), prmt(cd1, K, 0x4140u),
+                       prmt(cd1, K, 0x4342u), b0, b1);
+          mma16816_f16(acc[2], prmt(ab2, K, 0x4140u), prmt(ab2, K, 0x4342u), prmt(cd2, K, 0x4140u),
+                       prmt(cd2, K, 0x4342u), b0, b1);
+          mma16816_f16(acc[3], prmt(ab3, K, 0x4140u), prmt(ab3, K, 0x4342u), prmt(cd3, K, 0x4140u),
+                       prmt(cd3, K, 0x4342u), b0, b1);
+          const uint32_t m1024 = 0xE400E400u;  // f16 -1024 pairs
+          mma16816_f16(cor, m1024, m1024, m1024, m1024, b0, b1);
+        }
+      }
+      // head g's bias sum -> the lanes holding heads 2t / 2t+1
+      bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+      bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+      bacc0 += __shfl_sync(0xffffffffu, bs, 8 * t);
+      bacc1 += __shfl_sync(0xffffffffu, bs, 8 * t + 4);
+    }
+    __syncthreads();
+    if (tid == 0 && issued < nch) issue_chunk<C, FMOE_KV_AFFINE>(smem, bar, src, issued++, nS);
+  }
+  // Chunks still in flight (only after a wait gave up) must land before the
+  // stage area is reused.
+  if (tid == 0)
+    for (int k = ch; k < issued; ++k) mbar_wait(&bar[k % NST], (uint32_t)(k / NST) & 1u, status, 52);
+  const bool failed = flags[0] != 0;
+  // split sums: this lane's tile rows -> tile -> split
+  if (wp == 0) {
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      l_run0 += __shfl_xor_sync(0xffffffffu, l_run0, off);
+      l_run1 += __shfl_xor_sync(0xffffffffu, l_run1, off);
+    }
+  }
+  __syncthreads();  // every thread is past its last read of tmax
+  if (wp == 0 && g == 0) {
+    tmax[tile * 8 + 2 * t] = l_run0;
+    tmax[tile * 8 + 2 * t + 1] = l_run1;
+  }
+  if (warp == 0 && g == 0) {
+    if (2 * t < GQ) st_m[2 * t] = m_run0;
+    if (2 * t + 1 < GQ) st_m[2 * t + 1] = m_run1;
+  }
+  float* red = reinterpret_cast<float*>(smem);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = pv_grp * 64 + 8 * g + 2 * i;
+    if (2 * t < GQ) {
+      float* r = red + (pv_slot * GQ + 2 * t) * D + d;
+      r[0] = acc[i][0] + cor[0] + bacc0;
+      r[1] = acc[i][2] + cor[2] + bacc0;
+    }
+    if (2 * t + 1 < GQ) {
+      float* r = red + (pv_slot * GQ + 2 * t + 1) * D + d;
+      r[0] = acc[i][1] + cor[1] + bacc1;
+      r[1] = acc[i][3] + cor[3] + bacc1;
+    }
+  }
+  __syncthreads();
+  if (tid < GQ) {
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < TPC; ++w) l += tmax[w * 8 + tid];
+    st_l[tid] = l;
+  }
+  __syncthreads();
+  attn_epilogue<P, FMOE_KV_AFFINE, GQ, C::RSL>(smem, st_m, st_l, flags, failed, Hq, b, hk, bh, split, nsplit,
+                                               inv_sqrt_d, part_ml, part_o, ctr, out);
+}
+
+// ---- bf16 cache (the reference's storage)
+
+template <int P, int GQ>
+struct Bf16Smem {
+  using C = AtCfg<P, FMOE_KV_BF16>;
+  static constexpr int D = C::D;
+  static constexpr int BAR = C::NST * C::STAGE;
+  static constexpr int QH = BAR + 64;                 // bf16 [GQ][D] query rows
+  static constexpr int SC = QH + GQ * D * 2;          // f32 [WPT][GQ][CH] partial scores
+  static constexpr int PR = SC + C::WPT * GQ * C::CH * 4;  // f32 [GQ][CH] probabilities
+  static constexpr int ST = PR + GQ * C::CH * 4;      // f32 m[8] l[8] f[8], int flags[8]
+  static constexpr int BYTES = ST + 32 * 4;
+  static_assert(C::RSL * GQ * D * 4 <= BAR && kRed2Off + GQ * D * 4 <= BAR, "attention smem aliases");
+};
+
+template <int P, int GQ>
+__global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
+    attn_bf16_kernel(const KvDev c, const bf16* __restrict__ q, int Hq, int S, int nsplit, int64_t nvalid,
+                     const int64_t* __restrict__ nvalid_dev, float scale, float inv_sqrt_d,
+                     float2* __restrict__ part_ml, float* __restrict__ part_o, unsigned* __restrict__ ctr,
+                     bf16* __restrict__ out, int* __restrict__ status) {
+  using C = AtCfg<P, FMOE_KV_BF16>;
+  using Sm = Bf16Smem<P, GQ>;
+  constexpr int D = C::D, CH = C::CH, NST = C::NST;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Sm::BAR);
+  bf16* qh = reinterpret_cast<bf16*>(smem + Sm::QH);
+  float* sc = reinterpret_cast<float*>(smem + Sm::SC);
+  float* pr = reinterpret_cast<float*>(smem + Sm::PR);
+  float* st_m = reinterpret_cast<float*>(smem + Sm::ST);
+  float* st_l = st_m + 8;
+  float* st_f = st_m + 16;
+  int* flags = reinterpret_cast<int*>(st_m + 24);
+
+  const int split = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int64_t bh = (int64_t)b * c.Hkv + hk;
+  int64_t nv = nvalid;
+  if (nvalid_dev) nv = min(max(*nvalid_dev, (int64_t)0), c.cap);
+  const int64_t p_begin = (int64_t)split * S;
+  const int nS = (int)max((int64_t)0, min((int64_t)S, nv - p_begin));
+  const int nch = (nS + CH - 1) / CH;
+  const SplitSrc src = split_src<C>(c, bh * c.cap + p_begin);
 
   if (tid == 0) {
 #pragma unroll
@@ -401,36 +868,17 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     flags[tid] = 0;
   }
   __syncthreads();
-  int issued = 0;  // meaningful in thread 0 only
+  int issued = 0;
   if (tid == 0)
-    for (; issued < min(NST, nch); ++issued) issue(issued);
-
-  // query rows of the CTA's heads, while the first chunks stream in
+    for (; issued < min(NST, nch); ++issued) issue_chunk<C, FMOE_KV_BF16>(smem, bar, src, issued, nS);
   if (warp < GQ) {
     float v[P];
     load_row_f32<P>(q + ((int64_t)b * Hq + hk * GQ + warp) * D, lane, v);
-    if (MODE == FMOE_KV_AFFINE) {
-      warp_fwht<P>(v, lane);
-      float hi[P], lo[P], s = 0.f;
-#pragma unroll
-      for (int i = 0; i < P; ++i) {
-        v[i] *= inv_sqrt_d;
-        hi[i] = round_bf(v[i]);
-        lo[i] = round_bf(v[i] - hi[i]);
-        s += hi[i] + lo[i];
-      }
-      store_row_bf16<P>(qh + warp * D, lane, hi);
-      store_row_bf16<P>(ql + warp * D, lane, lo);
-#pragma unroll
-      for (int o = 1; o < 64 / P; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane % (64 / P) == 0) qsum[warp * G + lane / (64 / P)] = s;
-    } else {
-      store_row_bf16<P>(qh + warp * D, lane, v);
-    }
+    store_row_bf16<P>(qh + warp * D, lane, v);
   }
   __syncthreads();
 
-  float o[GQ][4];
+  float o[GQ][4];  // column 4*unit + j of head h, this thread's position phase
 #pragma unroll
   for (int h = 0; h < GQ; ++h)
 #pragma unroll
@@ -441,9 +889,7 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     const int stg = ch % NST;
     const int nrow = min(CH, nS - ch * CH);
     const uint8_t* sb = smem + stg * C::STAGE;
-    if (!mbar_wait(&bar[stg], (uint32_t)(ch / NST) & 1u, status, 51)) atomicOr(&flags[0], 1);
-
-    // ---- scores (unscaled) -> sc[wp][h][i]
+    if (!mbar_wait(&bar[stg], (uint32_t)(ch / NST) & 1u, status, 53)) atomicOr(&flags[0], 1);
     {
       const int tile = warp % C::TPC, wp = warp / C::TPC, r0 = tile * 16;
       if (r0 < nrow) {
@@ -457,37 +903,14 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
             const uint8_t* pq = reinterpret_cast<const uint8_t*>(qh) + g * D * 2 + gi * 128 + 32 * t;
             bq = make_bfrag4(lds_u4(pq), lds_u4(pq + 16));
           }
-          if (MODE == FMOE_KV_BF16) {
-            const uint8_t* kl = sb + rl * C::KRB + gi * 128 + 32 * t;
-            const uint8_t* kh = sb + rh * C::KRB + gi * 128 + 32 * t;
-            const BFrag4 alo = make_bfrag4(lds_u4(kl), lds_u4(kl + 16));
-            const BFrag4 ahi = make_bfrag4(lds_u4(kh), lds_u4(kh + 16));
+          const uint8_t* kl = sb + rl * C::KRB + gi * 128 + 32 * t;
+          const uint8_t* kh = sb + rh * C::KRB + gi * 128 + 32 * t;
+          const BFrag4 alo = make_bfrag4(lds_u4(kl), lds_u4(kl + 16));
+          const BFrag4 ahi = make_bfrag4(lds_u4(kh), lds_u4(kh + 16));
 #pragma unroll
-            for (int s4 = 0; s4 < 4; ++s4)
-              mma16816(y, alo.b0[s4], ahi.b0[s4], alo.b1[s4], ahi.b1[s4], bq.b0[s4], bq.b1[s4]);
-          } else {
-            BFrag4 bl = make_bfrag4(make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0));
-            if (g < GQ) {
-              const uint8_t* pq = reinterpret_cast<const uint8_t*>(ql) + g * D * 2 + gi * 128 + 32 * t;
-              bl = make_bfrag4(lds_u4(pq), lds_u4(pq + 16));
-            }
-            const uint2 wl = lds_u2(sb + rl * C::KRB + gi * 32 + 8 * t);
-            const uint2 wh = lds_u2(sb + rh * C::KRB + gi * 32 + 8 * t);
-            float cc[4] = {0.f, 0.f, 0.f, 0.f};
-            mma_group_q4_hl(cc, wl, wh, bq, bl);
-            const bf16* ksc = reinterpret_cast<const bf16*>(sb + C::KS);
-            const bf16* kbi = reinterpret_cast<const bf16*>(sb + C::KB);
-            const float sl = bf2f(ksc[rl * G + gi]), bl_ = bf2f(kbi[rl * G + gi]);
-            const float sh = bf2f(ksc[rh * G + gi]), bh_ = bf2f(kbi[rh * G + gi]);
-            const float q0 = 2 * t < GQ ? qsum[(2 * t) * G + gi] : 0.f;
-            const float q1 = 2 * t + 1 < GQ ? qsum[(2 * t + 1) * G + gi] : 0.f;
-            y[0] += fmaf(sl, cc[0], fmaf(-128.f, sl, bl_) * q0);
-            y[1] += fmaf(sl, cc[1], fmaf(-128.f, sl, bl_) * q1);
-            y[2] += fmaf(sh, cc[2], fmaf(-128.f, sh, bh_) * q0);
-            y[3] += fmaf(sh, cc[3], fmaf(-128.f, sh, bh_) * q1);
-          }
+          for (int s4 = 0; s4 < 4; ++s4)
+            mma16816(y, alo.b0[s4], ahi.b0[s4], alo.b1[s4], ahi.b1[s4], bq.b0[s4], bq.b1[s4]);
         }
-        // C fragment: rows = positions (g, g+8), columns = heads (2t, 2t+1)
         float* scw = sc + wp * GQ * CH;
         if (2 * t < GQ) {
           if (r0 + g < nrow) scw[(2 * t) * CH + r0 + g] = y[0];
@@ -500,9 +923,7 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
       }
     }
     __syncthreads();
-    if (flags[0]) break;  // a copy never landed: every thread leaves the loop here
-
-    // ---- online softmax per head (warp h)
+    if (flags[0]) break;
     for (int h = warp; h < GQ; h += 8) {
       float sv[CH / 32];
       float cm = -INFINITY;
@@ -542,8 +963,6 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
       }
     }
     __syncthreads();
-
-    // ---- P.V
     {
       const int unit = tid % C::U, ph = tid / C::U;
 #pragma unroll
@@ -553,24 +972,8 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
         for (int j = 0; j < 4; ++j) o[h][j] *= f;
       }
       for (int i = ph; i < nrow; i += C::NPH) {
-        float v4[4];
-        if (MODE == FMOE_KV_BF16) {
-          const uint2 w = lds_u2(sb + C::VC + i * C::VRB + unit * 8);
-          v4[0] = bf16lo(w.x);
-          v4[1] = bf16hi(w.x);
-          v4[2] = bf16lo(w.y);
-          v4[3] = bf16hi(w.y);
-        } else {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(sb + C::VC + i * C::VRB + unit * 4);
-          const int gi = unit >> 4;
-          const float sv = bf2f(reinterpret_cast<const bf16*>(sb + C::VS)[i * G + gi]);
-          const float bv = bf2f(reinterpret_cast<const bf16*>(sb + C::VB)[i * G + gi]);
-          // byte j placed in the low mantissa bits of 2^23: the subtraction
-          // leaves the code exactly
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            v4[j] = fmaf(sv, __uint_as_float(prmt(w, 0x4B000000u, 0x7650u | j)) - 8388608.0f, bv);
-        }
+        const uint2 w = lds_u2(sb + C::VC + i * C::VRB + unit * 8);
+        const float v4[4] = {bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y)};
 #pragma unroll
         for (int h = 0; h < GQ; ++h) {
           const float p = pr[h * CH + i];
@@ -580,17 +983,13 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
       }
     }
     __syncthreads();
-    if (tid == 0 && issued < nch) issue(issued++);
+    if (tid == 0 && issued < nch) issue_chunk<C, FMOE_KV_BF16>(smem, bar, src, issued++, nS);
   }
-  // Chunks still in flight (only after a wait gave up) must land before the
-  // stage area is reused.
   if (tid == 0)
-    for (int k = ch; k < issued; ++k) mbar_wait(&bar[k % NST], (uint32_t)(k / NST) & 1u, status, 52);
+    for (int k = ch; k < issued; ++k) mbar_wait(&bar[k % NST], (uint32_t)(k / NST) & 1u, status, 54);
   const bool failed = flags[0] != 0;
   __syncthreads();
-
-  // ---- reduce the P.V phases, then finish or publish the split
-  float* red = reinterpret_cast<float*>(smem + Sm::RED);
+  float* red = reinterpret_cast<float*>(smem);
   {
     const int unit = tid % C::U, ph = tid / C::U;
 #pragma unroll
@@ -598,88 +997,8 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
       *reinterpret_cast<float4*>(red + (ph * GQ + h) * D + unit * 4) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
   }
   __syncthreads();
-  if (warp < GQ) {
-    const int h = warp;
-    float v[P];
-#pragma unroll
-    for (int i = 0; i < P; ++i) {
-      float s = 0.f;
-#pragma unroll
-      for (int ph = 0; ph < C::NPH; ++ph) s += red[(ph * GQ + h) * D + lane * P + i];
-      v[i] = s;
-    }
-    const float m = st_m[h], l = failed ? 0.f : st_l[h];
-    const int64_t row = (int64_t)b * Hq + hk * GQ + h;
-    if (nsplit == 1) {
-      finish_row<P, MODE>(v, l, inv_sqrt_d, lane, out + row * D);
-    } else {
-      float4* po = reinterpret_cast<float4*>(part_o + (row * nsplit + split) * D + lane * P);
-#pragma unroll
-      for (int i = 0; i < P / 4; ++i) __stcg(po + i, make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]));
-      if (lane == 0) __stcg(part_ml + row * nsplit + split, make_float2(m, l));
-    }
-  }
-  if (nsplit == 1) return;
-
-  // ---- the last CTA of this (batch, kv head) merges the splits
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const unsigned prev = atomicAdd(&ctr[bh], 1u);
-    flags[1] = prev == (unsigned)(nsplit - 1);
-    if (flags[1]) ctr[bh] = 0u;  // every split has arrived: ready for the next call
-  }
-  __syncthreads();
-  if (!flags[1]) return;
-  __threadfence();
-  float* wts = reinterpret_cast<float*>(smem + Sm::WTS);
-  float* red2 = reinterpret_cast<float*>(smem + Sm::RED2);
-  if (warp < GQ) {
-    const int64_t row = (int64_t)b * Hq + hk * GQ + warp;
-    float M = -INFINITY;
-    for (int s = lane; s < nsplit; s += 32) {
-      const float2 ml = __ldcg(part_ml + row * nsplit + s);
-      if (ml.y > 0.f) M = fmaxf(M, ml.x);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    float L = 0.f;
-    for (int s = lane; s < nsplit; s += 32) {
-      const float2 ml = __ldcg(part_ml + row * nsplit + s);
-      const float w = ml.y > 0.f ? expf(ml.x - M) : 0.f;
-      wts[warp * kMaxSplits + s] = w;
-      L = fmaf(w, ml.y, L);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    if (lane == 0) st_l[warp] = L;
-  }
-  __syncthreads();
-  for (int pi = tid; pi < GQ * (D / 4); pi += 256) {
-    const int h = pi / (D / 4), d4 = pi % (D / 4);
-    const int64_t row = (int64_t)b * Hq + hk * GQ + h;
-    const float4* src = reinterpret_cast<const float4*>(part_o + row * nsplit * D) + d4;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = wts[h * kMaxSplits + s];
-      const float4 x = __ldcg(src + (int64_t)s * (D / 4));
-      if (w != 0.f) {
-        a.x = fmaf(w, x.x, a.x);
-        a.y = fmaf(w, x.y, a.y);
-        a.z = fmaf(w, x.z, a.z);
-        a.w = fmaf(w, x.w, a.w);
-      }
-    }
-    *reinterpret_cast<float4*>(red2 + h * D + d4 * 4) = a;
-  }
-  __syncthreads();
-  if (warp < GQ) {
-    float v[P];
-#pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = red2[warp * D + lane * P + i];
-    finish_row<P, MODE>(v, st_l[warp], inv_sqrt_d, lane, out + ((int64_t)b * Hq + hk * GQ + warp) * D);
-  }
+  attn_epilogue<P, FMOE_KV_BF16, GQ, C::RSL>(smem, st_m, st_l, flags, failed, Hq, b, hk, bh, split, nsplit,
+                                             inv_sqrt_d, part_ml, part_o, ctr, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -690,24 +1009,32 @@ static int chunk_positions(int mode, int D) {
                               : (D == 256 ? AtCfg<8, FMOE_KV_AFFINE>::CH : AtCfg<16, FMOE_KV_AFFINE>::CH);
 }
 
-// CTAs the split planner aims for: two resident per SM (each keeps one chunk
-// in flight while it computes the other).  The environment variable
-// FMOE_ATTN_TARGET_CTAS overrides it (read once; a tuning knob).
-static int attn_target_ctas() {
+// Split planner.  Two CTAs are resident per SM; a launch of about one wave
+// (2 x 148 CTAs) has the lowest fixed cost (prologue, merge), four waves
+// balance the SMs better once every split still streams >= 8 chunks.  The
+// environment variable FMOE_ATTN_TARGET_CTAS, when set, replaces the choice
+// with one fixed CTA target (read once; a tuning knob).
+static int attn_target_override() {
   static const int v = [] {
     const char* e = std::getenv("FMOE_ATTN_TARGET_CTAS");
     const int x = e ? std::atoi(e) : 0;
-    return x > 0 ? x : 2 * kNumSMs;
+    return x > 0 ? x : 0;
   }();
   return v;
+}
+
+static int64_t attn_split_candidate(int64_t chunks, int64_t heads) {
+  const int64_t one = (2 * kNumSMs + heads - 1) / heads, four = (8 * kNumSMs + heads - 1) / heads;
+  if (attn_target_override()) return (attn_target_override() + heads - 1) / heads;
+  return chunks >= 8 * four ? four : one;
 }
 
 AttnPlan attn_plan(const KvDev& c, int64_t n) {
   const int CH = chunk_positions(c.mode, c.D);
   const int64_t chunks = n > 0 ? (n + CH - 1) / CH : 1;
   const int64_t heads = (int64_t)c.B * c.Hkv;
-  int64_t ns = (attn_target_ctas() + heads - 1) / heads;
-  ns = std::max<int64_t>(1, std::min<int64_t>({ns, chunks, (int64_t)kMaxSplits}));
+  const int64_t ns = std::max<int64_t>(1, std::min<int64_t>({attn_split_candidate(chunks, heads), chunks,
+                                                              (int64_t)kMaxSplits}));
   const int64_t per = (chunks + ns - 1) / ns;
   AttnPlan p;
   p.S = (int)std::min<int64_t>(per * CH, 1 << 30);
@@ -737,13 +1064,13 @@ static AttnWs carve_attn_ws(void* ws, const KvDev& c, int Hq, int nsplit) {
   return w;
 }
 
-// Upper bound of attn_plan(c, n).nsplit over every n <= capacity (the split
-// count before rounding S up to whole chunks; rounding only lowers it).
+// Upper bound of attn_plan(c, n).nsplit over every n <= capacity: the larger
+// candidate, before rounding S up to whole chunks (rounding only lowers it).
 static int attn_max_splits(const KvDev& c) {
   const int CH = chunk_positions(c.mode, c.D);
   const int64_t chunks = (c.cap + CH - 1) / CH;
   const int64_t heads = (int64_t)c.B * c.Hkv;
-  const int64_t ns = (attn_target_ctas() + heads - 1) / heads;
+  const int64_t ns = std::max(attn_split_candidate(0, heads), attn_split_candidate(INT64_MAX / 2, heads));
   return (int)std::max<int64_t>(1, std::min<int64_t>({ns, chunks, (int64_t)kMaxSplits}));
 }
 
@@ -781,21 +1108,22 @@ int launch_turbo_round_trip(const bf16* x, int64_t rows, int D, int bits, bf16* 
 template <int P, int MODE, int GQ>
 static int launch_attn_t(const KvDev& c, const bf16* q, int Hq, const AttnPlan& p, int64_t nvalid,
                          const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st) {
-  constexpr int bytes = AtSmem<P, MODE, GQ>::BYTES;
+  constexpr bool aff = MODE == FMOE_KV_AFFINE;
+  constexpr int bytes = aff ? AffSmem<P, GQ>::BYTES : Bf16Smem<P, GQ>::BYTES;
+  auto kern = aff ? attn_affine_kernel<P, GQ> : attn_bf16_kernel<P, GQ>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err =
-        cudaFuncSetAttribute(attn_decode_kernel<P, MODE, GQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  std::call_once(once, [kern] {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   });
   if (attr_err != cudaSuccess)
     return set_error(FMOE_ERR_CUDA, "attn_decode: shared memory attribute: %s", cudaGetErrorString(attr_err));
   const float inv = 1.0f / std::sqrt((float)(32 * P));
   dim3 grid(p.nsplit, c.Hkv, c.B);
-  ProfScope prof_("attn_decode_kernel", st);
-  attn_decode_kernel<P, MODE, GQ><<<grid, 256, bytes, st>>>(c, q, Hq, p.S, p.nsplit, nvalid, nvalid_dev, scale, inv,
-                                                            w.ml, w.po, w.ctr, out, w.status);
-  return check_launch("attn_decode_kernel");
+  ProfScope prof_(aff ? "attn_affine_kernel" : "attn_bf16_kernel", st);
+  kern<<<grid, 256, bytes, st>>>(c, q, Hq, p.S, p.nsplit, nvalid, nvalid_dev, scale, inv, w.ml, w.po, w.ctr, out,
+                                 w.status);
+  return check_launch("attn_decode kernel");
 }
 
 template <int P, int MODE>
