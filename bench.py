@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--workload", default="moe30_decode_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
+    ap.add_argument("--qlinear-case", default=None, metavar="OUT:IN:BITS:T",
+                    help="run only fmoe_qlinear on one shape: four launches, L2 flushed before each, the last one "
+                         "timed (a small case for profilers)")
     ap.add_argument("--attn-case", default=None, metavar="MODE:B:T",
                     help="run only one decode-attention case (mode affine|bf16, batch, context): four launches, "
                          "L2 flushed before each, the last one timed (a small case for profilers)")
@@ -472,11 +475,40 @@ def run_attn_case(args):
     print(json.dumps({"attn_case": args.attn_case, **res}), flush=True)
 
 
+def run_qlinear_case(args):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    out_f, in_f, bits, T = (int(v) for v in args.qlinear_case.split(":"))
+    g = torch.Generator(device=dev).manual_seed(11)
+    w = torch.randn(out_f, in_f, generator=g, device=dev) * 0.02
+    ql = fm.QuantizedLinear.from_float(w, bits)
+    del w
+    x = torch.randn(T, in_f, generator=g, device=dev).to(torch.bfloat16)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(4):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ql.forward(x)
+        b.record()
+        torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3
+    nbytes = out_f * in_f * bits // 8 + 2 * out_f * (in_f // 64) * 2
+    print(json.dumps({"qlinear_case": args.qlinear_case, "us": round(us, 1), "weight_bytes": nbytes,
+                      "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
     if args.attn_case:
         run_attn_case(args)
+    elif args.qlinear_case:
+        run_qlinear_case(args)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     else:

@@ -242,10 +242,19 @@ int fmoe_router(const void* x, int64_t T, const fmoe_router_t* r, int32_t* ids, 
                     static_cast<cudaStream_t>(stream));
 }
 
+// Decode-size inputs of 4 / 6 / 8-bit weights go to the streaming tensor-core
+// GEMV (qgemv.cu); everything else to the split-K GEMV (gemv.cu).
+static bool qlinear_streams(int64_t T, const QW& q, int group) {
+  return T >= 1 && T <= 8 && (q.bits == 4 || q.bits == 6 || q.bits == 8) && group == 64 && q.in % 64 == 0 &&
+         q.out % 16 == 0 && aligned(q.w, 16) && aligned(q.s, 16) && aligned(q.b, 16);
+}
+
 size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w) {
   if (!w || T <= 0 || w->out_features <= 0 || w->in_features < 64) return 0;
   const int ks = gemv_ksplit(T, w->out_features, w->in_features);
-  return align_up(sizeof(float) * (size_t)ks * T * w->out_features, 256) + 256;
+  const size_t split = sizeof(float) * (size_t)ks * T * w->out_features;
+  const size_t acc = sizeof(float) * (size_t)T * w->out_features;
+  return align_up(split > acc ? split : acc, 256) + 256;
 }
 
 int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, void* workspace, size_t workspace_bytes,
@@ -253,14 +262,40 @@ int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, voi
   QW q;
   int rc = to_qw(w, &q);
   if (rc) return rc;
-  rc = check_gemv_weight(q, w->group_size);
-  if (rc) return rc;
   if (!x || !y) return set_error(FMOE_ERR_INVALID, "qlinear: null x/y");
   if (T <= 0) return FMOE_OK;
   if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "qlinear: x not 16-byte aligned");
   const size_t need = fmoe_qlinear_workspace_bytes(T, w);
   if (!workspace || workspace_bytes < need) return set_error(FMOE_ERR_WORKSPACE, "qlinear: workspace %zu < %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (qlinear_streams(T, q, w->group_size)) {
+    QgArgs a = {};
+    a.nseg = 1;
+    a.seg[0] = QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, y, q.out, q.out, 0, 0};
+    a.K = q.in;
+    a.T = (int)T;
+    a.in_kind = QG_IN_BF16;
+    a.x = static_cast<const bf16*>(x);
+    a.ldx = q.in;
+    a.out_kind = QG_OUT_BF16;
+    QgLayout L;
+    if (qgemv_plan(a, q.bits, false, &L) == FMOE_OK) return launch_qgemv(a, L, q.bits, false, st);
+    // the rows need column chunks: accumulate in fp32, then round
+    a.out_kind = QG_OUT_F32_ADD;
+    Carver c(workspace);
+    float* acc = c.take<float>((size_t)T * q.out);
+    a.seg[0].out = acc;
+    if (qgemv_plan(a, q.bits, true, &L) == FMOE_OK) {
+      if (cudaMemsetAsync(acc, 0, sizeof(float) * (size_t)T * q.out, st) != cudaSuccess)
+        return set_error(FMOE_ERR_CUDA, "qlinear: clearing the accumulator failed");
+      rc = launch_qgemv(a, L, q.bits, false, st);
+      if (rc) return rc;
+      return launch_reduce_partials(acc, 1, T * q.out, static_cast<bf16*>(y), nullptr, st);
+    }
+    // too large for the streaming kernel's shared memory: split-K path below
+  }
+  rc = check_gemv_weight(q, w->group_size);
+  if (rc) return rc;
   const int ks = gemv_ksplit(T, q.out, q.in);
   Carver c(workspace);
   float* part = c.take<float>((size_t)ks * T * q.out);

@@ -97,6 +97,42 @@ struct AttnPlan {
   int S, nsplit;
 };
 
+// qgemv.cu: streaming quantised GEMV (decode, T <= 8) over up to 4 weight
+// matrices sharing one input.
+constexpr int kQgMaxSeg = 4;
+enum { QG_IN_BF16 = 0, QG_IN_RMSNORM = 1, QG_IN_GELU = 2 };
+enum { QG_OUT_F32 = 0, QG_OUT_F32_ADD = 1, QG_OUT_BF16 = 2 };
+struct QgSeg {
+  const uint8_t* w;  // packed codes [rows][K*bits/32 words]
+  const bf16* s;     // [rows][K/64]
+  const bf16* b;
+  void* out;         // [T][ld]: f32 or bf16 by QgArgs::out_kind
+  int rows, ld, col0;
+  int unit0;         // set by qgemv_plan
+};
+struct QgArgs {
+  QgSeg seg[kQgMaxSeg];
+  int nseg, K, T;
+  int kc, nkc, units;  // set by qgemv_plan
+  int out_kind;
+  int in_kind;
+  const bf16* x;       // [T][ldx] (QG_IN_BF16 / QG_IN_RMSNORM)
+  int ldx;
+  const bf16* norm_w;  // [K] (QG_IN_RMSNORM)
+  float eps;
+  const float* g;      // [T][ldgu] fp32 gate / up projections (QG_IN_GELU)
+  const float* u;
+  int ldgu;
+  float* zero_ptr[4];  // fp32 buffers cleared after griddepcontrol.wait (for later accumulating kernels)
+  int64_t zero_n[4];
+  int* status;
+};
+struct QgLayout {
+  int rs, soff, stage, sfull, nst, frag, xsum, red, misc, cnt, bar, bytes, grid, nw, rt;
+};
+int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L);
+int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStream_t st);
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Bump allocator over a caller workspace.

@@ -1,0 +1,553 @@
+// Streaming quantised GEMV for decode (T <= 8 tokens): y[t, r] = x[t] . W[r]^T
+// over up to four weight matrices ("segments") that share one input, e.g. the
+// q / k / v projections of an attention layer.
+//
+// Work unit = 16 weight rows x one chunk of kc input columns.  Each CTA owns a
+// contiguous range of units and streams them through an NST-stage ring of TMA
+// bulk copies (one copy per weight row into a bank-conflict-free padded row,
+// plus the rows' scale and bias blocks).  The first stages are issued before
+// griddepcontrol.wait: weights never depend on the preceding kernel, so under
+// programmatic dependent launch they stream in while that kernel finishes.
+//
+// Tensor-core math (mma.sync m16n8k16, f16 in, fp32 accumulate), one recipe
+// for every width: the A operand is (1024 + code) in f16 — exact for codes
+// < 1024 — built in registers from the packed codes (PRMT for 8-bit, LOP3 for
+// 4-bit, shifts + LOP3 for the 6-bit bit stream); the B operand is the input
+// row in f16, prepared once per CTA in fragment order.  Per 64-column group:
+//   y += s * C + (b - 1024 s) * sum(x),   C = sum (1024 + q) x.
+// The input prologue applies the producer-side elementwise op while it builds
+// the fragments: none (bf16 input), RMSNorm with a weight, or GELU-tanh gating
+// of two fp32 projections (the dense MLP's act = gelu(g) * u, rounded like
+// the reference's bf16 tensors).
+#include "internal.h"
+#include "common.cuh"
+#include "stage.cuh"
+
+namespace fmoe {
+
+// (a & m) | (b & ~m) in one instruction.
+__device__ __forceinline__ uint32_t sel_bits(uint32_t a, uint32_t b, uint32_t m) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xE4;\n" : "=r"(r) : "r"(a), "r"(b), "r"(m));
+  return r;
+}
+
+constexpr int kQgMaxWarps = 16;  // consumer warps per CTA (the count is chosen per launch)
+constexpr uint32_t kF16Magic = 0x64006400u;  // f16 1024.0 pairs; low mantissa bits take the code
+
+// A fragments of one 64-column group for rows g (lo) and g+8 (hi), MMA j:
+// a[j][0..3] = (row g, slots 2t..), (row g+8, slots 2t..), (row g, slots 2t+8..), (row g+8, slots 2t+8..).
+template <int BITS>
+__device__ __forceinline__ void load_a_frags(const uint8_t* rlo, const uint8_t* rhi, uint32_t (&a)[4][4]) {
+  if constexpr (BITS == 8) {
+    // lane's 16 codes = 4 words; word j -> k (4j, 4j+1) and (4j+2, 4j+3)
+    const uint4 l = lds_u4(rlo), h = lds_u4(rhi);
+    const uint32_t lw[4] = {l.x, l.y, l.z, l.w}, hw[4] = {h.x, h.y, h.z, h.w};
+    const uint32_t K = 0x64646464u;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a[j][0] = prmt(lw[j], K, 0x4140u);
+      a[j][1] = prmt(hw[j], K, 0x4140u);
+      a[j][2] = prmt(lw[j], K, 0x4342u);
+      a[j][3] = prmt(hw[j], K, 0x4342u);
+    }
+  } else if constexpr (BITS == 4) {
+    // lane's 16 codes = 2 words; nibbles (j, j+4) of word 0 and of word 1
+    const uint2 l = lds_u2(rlo), h = lds_u2(rhi);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a[j][0] = and_or(l.x >> (4 * j), 0x000F000Fu, kF16Magic);
+      a[j][1] = and_or(h.x >> (4 * j), 0x000F000Fu, kF16Magic);
+      a[j][2] = and_or(l.y >> (4 * j), 0x000F000Fu, kF16Magic);
+      a[j][3] = and_or(h.y >> (4 * j), 0x000F000Fu, kF16Magic);
+    }
+  } else {
+    static_assert(BITS == 6, "qgemv widths: 4, 6, 8");
+    // lane's 16 codes v0..v15 = 96 bits = 3 words; v_i at stream bit 6i.
+    // Codes whose bits sit exactly 16 apart share one select + shift:
+    // pairs (v0,v8) (v1,v9) (v6,v14) (v7,v15) (v11,v3) (v12,v4), plus
+    // (v2,v13) and (v5,v10) from shifted words.
+    const uint32_t* pl = reinterpret_cast<const uint32_t*>(rlo);
+    const uint32_t* ph = reinterpret_cast<const uint32_t*>(rhi);
+    uint32_t r[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t* p = h ? ph : pl;
+      const uint32_t w0 = p[0], w1 = p[1], w2 = p[2];
+      const uint32_t t01 = sel_bits(w0, w1, 0x0000FFFFu), t12 = sel_bits(w1, w2, 0x0000FFFFu);
+      const uint32_t t20 = sel_bits(w2, w0, 0x0000FFFFu);
+      const uint32_t M = 0x003F003Fu;
+      r[h][0] = and_or(t01, M, kF16Magic);        // (v0, v8)
+      r[h][1] = and_or(t01 >> 6, M, kF16Magic);   // (v1, v9)
+      r[h][2] = and_or(t12 >> 4, M, kF16Magic);   // (v6, v14)
+      r[h][3] = and_or(t12 >> 10, M, kF16Magic);  // (v7, v15)
+      r[h][4] = and_or(t20 >> 2, M, kF16Magic);   // (v11, v3)
+      r[h][5] = and_or(t20 >> 8, M, kF16Magic);   // (v12, v4)
+      r[h][6] = and_or(sel_bits(w0 >> 12, w2 << 2, 0x0000FFFFu), M, kF16Magic);  // (v2, v13)
+      r[h][7] = and_or(sel_bits(__funnelshift_r(w0, w1, 30), __funnelshift_r(w1, w2, 12), 0x0000FFFFu), M,
+                       kF16Magic);  // (v5, v10)
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a[j][0] = r[0][2 * j];
+      a[j][1] = r[1][2 * j];
+      a[j][2] = r[0][2 * j + 1];
+      a[j][3] = r[1][2 * j + 1];
+    }
+  }
+}
+
+// The k pairing of load_a_frags, for the B fragments: MMA j takes
+// b0 = (v[p0], v[p0']), b1 = (v[p1], v[p1']) of the lane's 16 inputs.
+template <int BITS>
+__device__ __forceinline__ void make_b_frags(const float (&v)[16], uint32_t (&b)[8]) {
+  if constexpr (BITS == 6) {
+    constexpr int lo[8] = {0, 1, 6, 7, 11, 12, 2, 5}, hi[8] = {8, 9, 14, 15, 3, 4, 13, 10};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b[j] = pack_f16x2(v[lo[2 * j]], v[hi[2 * j]]);
+      b[4 + j] = pack_f16x2(v[lo[2 * j + 1]], v[hi[2 * j + 1]]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if constexpr (BITS == 4) {
+        b[j] = pack_f16x2(v[j], v[j + 4]);
+        b[4 + j] = pack_f16x2(v[8 + j], v[12 + j]);
+      } else {
+        b[j] = pack_f16x2(v[4 * j], v[4 * j + 1]);
+        b[4 + j] = pack_f16x2(v[4 * j + 2], v[4 * j + 3]);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float f16r(float v) { return __half2float(__float2half_rn(v)); }
+
+// Unit u -> (segment, block of RT 16-row tiles, column chunk).
+struct QgUnit {
+  int sg, blk, kci;
+};
+__device__ __forceinline__ QgUnit qg_unit(const QgArgs& a, int u) {
+  int sg = 0;
+#pragma unroll
+  for (int i = 1; i < kQgMaxSeg; ++i)
+    if (i < a.nseg && u >= a.seg[i].unit0) sg = i;
+  const int v = u - a.seg[sg].unit0;
+  return QgUnit{sg, v / a.nkc, v % a.nkc};
+}
+
+template <int BITS, int RT>
+__device__ __forceinline__ void qg_issue(const QgArgs& a, const QgLayout& L, uint8_t* smem, uint64_t* bar, int u,
+                                         int st) {
+  constexpr int R = 16 * RT;
+  const QgUnit q = qg_unit(a, u);
+  const QgSeg& s = a.seg[q.sg];
+  const int64_t rowbytes = (int64_t)a.K * BITS / 8;
+  const int kcbytes = a.kc * BITS / 8, G = a.K / 64, gc = a.kc / 64;
+  uint8_t* sb = smem + (size_t)st * L.stage;
+  const uint8_t* w = s.w + (int64_t)q.blk * R * rowbytes + (int64_t)q.kci * kcbytes;
+  mbar_arrive_expect_tx(&bar[st], (uint32_t)(R * kcbytes + 2 * R * (L.sfull ? G : gc) * 2));
+#pragma unroll 4
+  for (int r = 0; r < R; ++r) bulk_g2s(sb + r * L.rs, w + r * rowbytes, kcbytes, &bar[st]);
+  const bf16* sc = s.s + (int64_t)q.blk * R * G;
+  const bf16* bi = s.b + (int64_t)q.blk * R * G;
+  if (L.sfull) {  // the block's whole [R][G] scale / bias arrays (contiguous)
+    bulk_g2s(sb + L.soff, sc, R * G * 2, &bar[st]);
+    bulk_g2s(sb + L.soff + R * G * 2, bi, R * G * 2, &bar[st]);
+  } else {  // the chunk's [R][gc] columns, one 16-byte-multiple copy per row
+    for (int r = 0; r < R; ++r) {
+      bulk_g2s(sb + L.soff + r * gc * 2, sc + (int64_t)r * G + q.kci * gc, gc * 2, &bar[st]);
+      bulk_g2s(sb + L.soff + R * gc * 2 + r * gc * 2, bi + (int64_t)r * G + q.kci * gc, gc * 2, &bar[st]);
+    }
+  }
+}
+
+// Warp roles: L.nw consumer warps share every unit (64-column groups dealt
+// round robin, any leftover groups rotating from unit to unit) and one
+// producer warp issues the copies.  A stage is refilled once all consumers
+// have released it (per-stage "empty" mbarrier), so consumers never wait on
+// each other.  A consumer loads a group's input fragments once and applies
+// them to the unit's RT row tiles.  A block's per-warp partial sums meet in
+// shared memory and the last warp to arrive (a shared counter) writes them.
+template <int BITS, int RT>
+__global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const QgArgs a, const QgLayout L) {
+  constexpr int R = 16 * RT;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [nst] full, then [nst] empty
+  uint64_t* empty = bar + L.nst;
+  int* cnt = reinterpret_cast<int*>(smem + L.cnt);
+  uint4* frag = reinterpret_cast<uint4*>(smem + L.frag);
+  float* xsum = reinterpret_cast<float*>(smem + L.xsum);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* rms = reinterpret_cast<float*>(smem + L.misc);
+  int* flag = reinterpret_cast<int*>(smem + L.misc + 8 * 4);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const int T = a.T, K = a.K, G = K / 64, gc = a.kc / 64;
+  // unit range; outputs that are stored (not accumulated) keep a block's chunks in one CTA
+  const int ub = a.out_kind == QG_OUT_F32_ADD ? 1 : a.nkc;
+  const int nb = a.units / ub;
+  const int u0 = (int)((int64_t)nb * blockIdx.x / gridDim.x) * ub;
+  const int u1 = (int)((int64_t)nb * (blockIdx.x + 1) / gridDim.x) * ub;
+  const int n = u1 - u0;
+  const int NW = L.nw;
+  const int prod = NW * 32;  // the producer thread
+
+  if (tid == 0) {
+    for (int s = 0; s < L.nst; ++s) {
+      mbar_init(&bar[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    mbar_fence_init();
+    flag[0] = 0;
+  }
+  if (tid < L.nst + 1) cnt[tid] = 0;
+  __syncthreads();
+  if (tid == prod)
+    for (int i = 0; i < n && i < L.nst; ++i) qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, i);
+
+  griddep_wait();  // the input (and the buffers cleared below) belong to earlier kernels
+  griddep_launch_dependents();
+
+  // buffers that later kernels accumulate into
+  for (int z = 0; z < 4; ++z) {
+    float* zp = a.zero_ptr[z];
+    if (!zp) continue;
+    const int64_t nz = a.zero_n[z];
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + tid; i < nz; i += (int64_t)gridDim.x * blockDim.x) zp[i] = 0.f;
+  }
+
+  // ---- input prologue: f16 B fragments + per-group sums
+  if (a.in_kind == QG_IN_RMSNORM) {
+    for (int tk = warp; tk < T; tk += NW + 1) {
+      const bf16* xr = a.x + (int64_t)tk * a.ldx;
+      float ss = 0.f;
+      for (int i = lane * 8; i < K; i += 256) {
+        const uint4 w = ld_u4(xr + i);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = bf16lo(ww[e]), hi = bf16hi(ww[e]);
+          ss = fmaf(lo, lo, fmaf(hi, hi, ss));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (lane == 0) rms[tk] = rsqrtf(ss / (float)K + a.eps);
+    }
+    __syncthreads();
+  }
+  const int nitems = G * T * 4;
+  for (int item0 = 0; item0 < nitems; item0 += blockDim.x) {
+    // every lane runs the shuffles below; items come in aligned groups of 4
+    const int item = item0 + tid;
+    const bool live = item < nitems;
+    const int tq = item & 3, tk = live ? (item >> 2) % T : 0, gi = live ? (item >> 2) / T : 0;
+    const int c0 = gi * 64 + 16 * tq;
+    float v[16];
+    if (!live) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = 0.f;
+    } else if (a.in_kind == QG_IN_GELU) {
+      const float* gp = a.g + (int64_t)tk * a.ldgu + c0;
+      const float* up = a.u + (int64_t)tk * a.ldgu + c0;
+#pragma unroll
+      for (int e = 0; e < 16; e += 4) {
+        const float4 gg = __ldcg(reinterpret_cast<const float4*>(gp + e));
+        const float4 uu = __ldcg(reinterpret_cast<const float4*>(up + e));
+        const float ga[4] = {gg.x, gg.y, gg.z, gg.w}, ua[4] = {uu.x, uu.y, uu.z, uu.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[e + q] = round_bf(gelu_tanh(round_bf(ga[q])) * round_bf(ua[q]));
+      }
+    } else {
+      const bf16* xr = a.x + (int64_t)tk * a.ldx + c0;
+      const uint4 w0 = ld_u4(xr), w1 = ld_u4(xr + 8);
+      const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[2 * e] = bf16lo(ww[e]);
+        v[2 * e + 1] = bf16hi(ww[e]);
+      }
+      if (a.in_kind == QG_IN_RMSNORM) {
+        const float r = rms[tk];
+        const bf16* nw = a.norm_w + c0;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] = round_bf(v[e] * r * bf2f(nw[e]));
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      v[e] = f16r(v[e]);
+      s += v[e];
+    }
+    uint32_t b[8];
+    make_b_frags<BITS>(v, b);
+    if (live) {
+      uint4* dst = frag + ((int64_t)gi * 4 * T + 4 * tk + tq) * 2;
+      dst[0] = make_uint4(b[0], b[1], b[2], b[3]);
+      dst[1] = make_uint4(b[4], b[5], b[6], b[7]);
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (live && tq == 0) xsum[gi * 8 + tk] = s;
+  }
+  for (int i = tid; i < G * 8; i += blockDim.x)
+    if ((i & 7) >= T) xsum[i] = 0.f;
+  __syncthreads();
+
+  // ---- producer: refill each stage once every consumer has released it,
+  // then let the last copies land before the warp (and smem) goes away
+  if (warp == NW) {
+    if (lane == 0) {
+      int i = L.nst;
+      for (; i < n; ++i) {
+        const int st = i % L.nst;
+        if (*(volatile int*)flag) break;
+        if (!mbar_wait(&empty[st], (uint32_t)((i / L.nst - 1) & 1), a.status, 63)) {
+          *(volatile int*)flag = 1;
+          break;
+        }
+        qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, st);
+      }
+      for (int k = (i > L.nst ? i - L.nst : 0); k < i && k < n; ++k)
+        mbar_wait(&bar[k % L.nst], (uint32_t)(k / L.nst) & 1u, a.status, 64);
+    }
+    return;
+  }
+
+  // ---- consumers
+  const int nred = L.nst + 1;
+  float y[RT][4];
+#pragma unroll
+  for (int tt = 0; tt < RT; ++tt) y[tt][0] = y[tt][1] = y[tt][2] = y[tt][3] = 0.f;
+  int flushes = 0;
+  const int sst = L.sfull ? G : gc;  // scale row stride in a stage
+  for (int i = 0; i < n; ++i) {
+    const int st = i % L.nst, u = u0 + i;
+    const QgUnit q = qg_unit(a, u);
+    const uint8_t* sb = smem + (size_t)st * L.stage;
+    if (!mbar_wait(&bar[st], (uint32_t)(i / L.nst) & 1u, a.status, 61)) *(volatile int*)flag = 1;
+    if (*(volatile int*)flag) break;  // a copy never landed (the status word says so)
+    const bf16* scl = reinterpret_cast<const bf16*>(sb + L.soff);
+    const bf16* bil = reinterpret_cast<const bf16*>(sb + L.soff + R * sst * 2);
+    const int rot = (int)(((int64_t)i * (gc % NW)) % NW);
+    const int vw = warp + rot < NW ? warp + rot : warp + rot - NW;
+    const uint8_t* rbase = sb + g * L.rs + t * (2 * BITS);
+    for (int gl = vw; gl < gc; gl += NW) {
+      const int gi = q.kci * gc + gl;
+      uint4 b0 = make_uint4(0, 0, 0, 0), b1 = b0;
+      if (g < T) {
+        const uint4* fp = frag + ((int64_t)gi * 4 * T + lane) * 2;
+        b0 = fp[0];
+        b1 = fp[1];
+      }
+      const uint32_t bb0[4] = {b0.x, b0.y, b0.z, b0.w}, bb1[4] = {b1.x, b1.y, b1.z, b1.w};
+      const float q0 = xsum[gi * 8 + 2 * t], q1 = xsum[gi * 8 + 2 * t + 1];
+      const int sc_ = L.sfull ? gi : gl;
+#pragma unroll
+      for (int tt = 0; tt < RT; ++tt) {
+        const uint8_t* rl = rbase + (tt * 16) * L.rs + gl * (8 * BITS);
+        uint32_t af[4][4];
+        load_a_frags<BITS>(rl, rl + 8 * L.rs, af);
+        float cc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) mma16816_f16(cc, af[j][0], af[j][1], af[j][2], af[j][3], bb0[j], bb1[j]);
+        const int r0 = tt * 16 + g;
+        const float sl = bf2f(scl[r0 * sst + sc_]), blo = bf2f(bil[r0 * sst + sc_]);
+        const float sh = bf2f(scl[(r0 + 8) * sst + sc_]), bhi = bf2f(bil[(r0 + 8) * sst + sc_]);
+        const float ol = fmaf(-1024.f, sl, blo), oh = fmaf(-1024.f, sh, bhi);
+        y[tt][0] += fmaf(sl, cc[0], ol * q0);
+        y[tt][1] += fmaf(sl, cc[1], ol * q1);
+        y[tt][2] += fmaf(sh, cc[2], oh * q0);
+        y[tt][3] += fmaf(sh, cc[3], oh * q1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    bool flush = i + 1 == n;
+    if (!flush) {
+      const QgUnit nq = qg_unit(a, u + 1);
+      flush = nq.sg != q.sg || nq.blk != q.blk;
+    }
+    if (flush) {
+      const int slot = flushes % nred;
+      float* rs = red + (size_t)slot * NW * R * T;  // [NW warps][R rows][T tokens]
+      float* rw = rs + warp * R * T;
+#pragma unroll
+      for (int tt = 0; tt < RT; ++tt) {
+        const int r0 = tt * 16 + g;
+        if (2 * t < T) {
+          rw[r0 * T + 2 * t] = y[tt][0];
+          rw[(r0 + 8) * T + 2 * t] = y[tt][2];
+        }
+        if (2 * t + 1 < T) {
+          rw[r0 * T + 2 * t + 1] = y[tt][1];
+          rw[(r0 + 8) * T + 2 * t + 1] = y[tt][3];
+        }
+        y[tt][0] = y[tt][1] = y[tt][2] = y[tt][3] = 0.f;
+      }
+      __threadfence_block();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = (atomicAdd(&cnt[slot], 1) + 1) % NW == 0;  // counters only grow
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        __threadfence_block();
+        const QgSeg& sg = a.seg[q.sg];
+        for (int o = lane; o < R * T; o += 32) {
+          const int r = o % R, tk = o / R;
+          float sum = 0.f;
+          for (int w = 0; w < NW; ++w) sum += rs[(w * R + r) * T + tk];
+          const int64_t oi = (int64_t)tk * sg.ld + sg.col0 + q.blk * R + r;
+          if (a.out_kind == QG_OUT_F32_ADD)
+            atomicAdd(static_cast<float*>(sg.out) + oi, sum);
+          else if (a.out_kind == QG_OUT_F32)
+            static_cast<float*>(sg.out)[oi] = sum;
+          else
+            static_cast<bf16*>(sg.out)[oi] = __float2bfloat16_rn(sum);
+        }
+      }
+      ++flushes;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+// Padded smem row stride: residues (mod 128 B) measured conflict-free for the
+// lane access patterns of load_a_frags.
+static int qg_row_stride(int bytes, int bits) {
+  const int want = bits == 4 ? 32 : bits == 6 ? 16 : 64;
+  int s = (bytes + 15) & ~15;
+  while (s % 128 != want) s += 16;
+  return s;
+}
+
+static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, QgLayout* L);
+
+int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L) {
+  // 32-row units when they fit, else 16-row units
+  if (qgemv_plan_rt(a, bits, allow_split, true, L) == FMOE_OK) return FMOE_OK;
+  return qgemv_plan_rt(a, bits, allow_split, false, L);
+}
+
+static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, QgLayout* L) {
+  const int K = a.K, G = K / 64;
+  if (bits != 4 && bits != 6 && bits != 8) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: bits %d", bits);
+  if (K % 64 || a.T < 1 || a.T > 8) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d, T %d", K, a.T);
+  int tiles = 0;
+  bool even32 = true;
+  for (int i = 0; i < a.nseg; ++i) {
+    if (a.seg[i].rows % 16) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: rows %d not a multiple of 16", a.seg[i].rows);
+    tiles += a.seg[i].rows / 16;
+    even32 = even32 && a.seg[i].rows % 32 == 0;
+  }
+  // Large matrices: 32-row units over the whole K (input fragments reused by
+  // two row tiles, scales copied once).  Otherwise 16-row units with the
+  // fewest column chunks that keep a stage's codes <= 48 KB, and (for
+  // accumulating outputs) more chunks while the units split unevenly over the SMs.
+  int rt = 1, nkc = 0;
+  if (try_rt2 && even32 && tiles / 2 >= 4 * kNumSMs && 32 * K * bits / 8 <= 96 * 1024) {
+    rt = 2;
+    nkc = 1;
+  } else {
+    double best_eff = -1.0;
+    for (int c = 1; c <= G; ++c) {
+      if (G % c || (c > 1 && G / c < 8)) continue;
+      if (16 * (K / c) * bits / 8 > 48 * 1024) continue;
+      if (nkc && !allow_split) break;
+      const int64_t u = (int64_t)tiles * c, per = (u + kNumSMs - 1) / kNumSMs;
+      const double eff = u < kNumSMs ? 1.0 : (double)u / (double)(per * kNumSMs);
+      if (eff > best_eff + 0.02) {
+        best_eff = eff;
+        nkc = c;
+      }
+      if (!allow_split || eff >= 0.9 || u >= 6 * kNumSMs) break;
+    }
+  }
+  if (!nkc) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: no column chunking of K %d at %d bits", K, bits);
+  L->rt = rt;
+  a.nkc = nkc;
+  a.kc = K / nkc;
+  if (a.nkc > 1 && a.out_kind != QG_OUT_F32_ADD)
+    return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d at %d bits needs column chunks (accumulating output)", K, bits);
+  const int R = 16 * rt;
+  int u = 0;
+  for (int i = 0; i < a.nseg; ++i) {
+    a.seg[i].unit0 = u;
+    u += a.seg[i].rows / R * a.nkc;
+  }
+  a.units = u;
+  const int kcb = a.kc * bits / 8, gc = a.kc / 64;
+  L->sfull = (nkc == 1 || (gc * 2) % 16 || (G * 2) % 16) ? 1 : 0;
+  L->rs = qg_row_stride(kcb, bits);
+  L->soff = R * L->rs;
+  L->stage = (int)align_up(L->soff + 2 * R * (L->sfull ? G : gc) * 2, 128);
+  // consumer warps: the count (8..16) that deals a unit's groups most evenly
+  int nw = kQgMaxWarps;
+  double nw_eff = 0.0;
+  for (int w = kQgMaxWarps; w >= 8; --w) {
+    const double e = (double)gc / (double)(w * ((gc + w - 1) / w));
+    if (e > nw_eff + 1e-9) {
+      nw_eff = e;
+      nw = w;
+    }
+  }
+  L->nw = nw;
+  const size_t frag = (size_t)G * 4 * a.T * 32, xs = (size_t)G * 8 * 4, red1 = (size_t)nw * R * a.T * 4;
+  const size_t fixed = frag + xs + red1 + 8 * 4 + 16 + 16 * 8 + 64 + 512;
+  int nst = (int)((222 * 1024 - fixed) / (L->stage + red1));
+  if (nst > 6) nst = 6;
+  if (nst < 2) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d, T %d exceed shared memory", K, a.T);
+  const size_t red = (size_t)(nst + 1) * red1;
+  L->nst = nst;
+  size_t off = (size_t)nst * L->stage;
+  L->frag = (int)off;
+  off = align_up(off + frag, 16);
+  L->xsum = (int)off;
+  off = align_up(off + xs, 16);
+  L->red = (int)off;
+  off = align_up(off + red, 16);
+  L->misc = (int)off;
+  off = align_up(off + 8 * 4 + 16, 16);
+  L->cnt = (int)off;
+  off = align_up(off + 4 * (nst + 1), 16);
+  L->bar = (int)off;
+  off += 2 * 8 * L->nst;
+  L->bytes = (int)align_up(off, 128);
+  const int ub = a.out_kind == QG_OUT_F32_ADD ? 1 : a.nkc;
+  const int nb = a.units / ub;
+  L->grid = nb < kNumSMs ? nb : kNumSMs;
+  return FMOE_OK;
+}
+
+template <int BITS, int RT>
+static int launch_qgemv_t(const QgArgs& a, const QgLayout& L, bool pdl, cudaStream_t st) {
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(qgemv_kernel<BITS, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr_done = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(L.grid);
+  cfg.blockDim = dim3((L.nw + 1) * 32);
+  cfg.dynamicSmemBytes = L.bytes;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  ProfScope prof_(BITS == 4 ? "qgemv_kernel<4>" : BITS == 6 ? "qgemv_kernel<6>" : "qgemv_kernel<8>", st);
+  cudaLaunchKernelEx(&cfg, qgemv_kernel<BITS, RT>, a, L);
+  return check_launch("qgemv_kernel");
+}
+
+int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStream_t st) {
+  if (bits == 4) return L.rt == 2 ? launch_qgemv_t<4, 2>(a, L, pdl, st) : launch_qgemv_t<4, 1>(a, L, pdl, st);
+  if (bits == 6) return L.rt == 2 ? launch_qgemv_t<6, 2>(a, L, pdl, st) : launch_qgemv_t<6, 1>(a, L, pdl, st);
+  return L.rt == 2 ? launch_qgemv_t<8, 2>(a, L, pdl, st) : launch_qgemv_t<8, 1>(a, L, pdl, st);
+}
+
+}  // namespace fmoe

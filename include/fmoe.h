@@ -124,8 +124,10 @@ int fmoe_embed_rows(const fmoe_qweight_t* w, const int32_t* ids, int64_t n, floa
 
 /* y bf16 [T, out] = x bf16 [T, in] . W^T.  Replaces QuantizedLinear::forward,
  * src/model/mlp.rs:15-25 (mlx quantized_matmul, transpose=true).  Kernels:
- * bits 4, 8 and 16 (bf16), group 64, in % 64 == 0, out % 16 == 0.  The
- * workspace holds split-K partial sums (fmoe_qlinear_workspace_bytes). */
+ * bits 4, 6 and 8 at T <= 8 (streaming tensor-core GEMV; 16-byte aligned
+ * weight, scales and biases), bits 4, 8 and 16 (bf16) at any T, group 64,
+ * in % 64 == 0, out % 16 == 0.  The workspace holds fp32 partial sums
+ * (fmoe_qlinear_workspace_bytes). */
 size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w);
 int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, void* workspace,
                  size_t workspace_bytes, void* stream);

@@ -71,3 +71,20 @@ def test_qlinear_rejects_bad_shapes(fm, dev):
     with pytest.raises(fm.FmoeError) as ei:
         ql.forward(torch.zeros(1, 128, dtype=torch.bfloat16, device=dev))
     assert ei.value.code == -5
+
+
+# The streaming tensor-core GEMV (T <= 8): decoder shapes, the 6-bit lm_head
+# width, and K large enough to need column chunks accumulated in fp32.
+@pytest.mark.parametrize("bits", [4, 6, 8])
+@pytest.mark.parametrize("shape", [(4096, 2816), (2816, 4096), (2816, 8192), (2816, 2112), (272, 2816)])
+@pytest.mark.parametrize("T", [1, 2, 8])
+def test_qlinear_streaming_matches_oracle(fm, orc, dev, bits, shape, T):
+    out_f, in_f = shape
+    g = torch.Generator(device=dev).manual_seed(7 * out_f + in_f + bits + T)
+    w = torch.randn(out_f, in_f, generator=g, device=dev) * 0.02
+    x = torch.randn(T, in_f, generator=g, device=dev).to(torch.bfloat16)
+    ql = fm.QuantizedLinear.from_float(w, bits)
+    y = ql.forward(x)
+    want = orc.qmatmul(to_np_bf16(x), to_np_u32(ql.weight), to_np_bf16(ql.scales), to_np_bf16(ql.biases), in_f,
+                       bits)
+    assert max_rel_err(y.float().cpu().numpy(), want) <= TOL
