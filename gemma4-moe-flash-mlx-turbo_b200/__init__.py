@@ -8,6 +8,8 @@ for this path (names, argument meaning, error behaviour):
     GeLUMLP.forward(x)                  src/model/mlp.rs:35-41
     Gemma4MoeBlock.forward(x)           src/model/moe.rs:315-470
     KVCache.update_and_fetch(k, v)      src/cache.rs:266-310   (see kv.py)
+    Gemma4DecoderLayer.forward(x, ...)  src/model/mod.rs:67-119  (see model.py)
+    Gemma4Model.decode_step()           src/model/mod.rs:135-363
 
 There is no CPU fallback: every call goes to the CUDA kernels in
 lib/libfmoe.so, and a missing library or device raises.
@@ -141,6 +143,10 @@ SIGNATURES = {
     "fmoe_attn_decode_workspace_bytes": (_SZ, [ctypes.POINTER(KvCacheC), _I]),
     "fmoe_attn_decode": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _P, _F, _P, _P, _SZ, _P]),
     "fmoe_turbo_round_trip": (_I, [_P, _I64, _I, _I, _P, _P]),
+    "fmoe_decoder_workspace_bytes": (_SZ, [_I64, _P, ctypes.POINTER(KvCacheC)]),
+    "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),
+    "fmoe_lm_head_workspace_bytes": (_SZ, [_I64]),
+    "fmoe_lm_head": (_I, [ctypes.POINTER(QWeightC), _P, _F, _P, _I64, _F, _P, _P, _P, _P, _SZ, _P]),
 }
 
 _lib_handle = None
@@ -432,3 +438,4 @@ class Gemma4MoeBlock:
 
 
 from .kv import KV_AFFINE, KV_BF16, KVCache, turbo_round_trip  # noqa: E402
+from .model import GEMMA4_26B, Gemma4DecoderLayer, Gemma4Model  # noqa: E402

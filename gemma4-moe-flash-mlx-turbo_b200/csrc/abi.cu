@@ -24,9 +24,9 @@ int check_launch(const char* what) {
   return FMOE_OK;
 }
 
-static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-static int to_qw(const fmoe_qweight_t* w, QW* q) {
+int to_qw(const fmoe_qweight_t* w, QW* q) {
   if (!w || !w->w) return set_error(FMOE_ERR_INVALID, "qweight: null weight");
   if (w->out_features <= 0 || w->in_features <= 0) return set_error(FMOE_ERR_INVALID, "qweight: empty shape");
   if (w->bits != 16) {
@@ -55,7 +55,7 @@ static int check_gemv_weight(const QW& q, int group) {
   return FMOE_OK;
 }
 
-static int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
+int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
   if (!e || !e->base) return set_error(FMOE_ERR_INVALID, "experts: null table");
   if (e->bits != 4 || e->group_size != 64)
     return set_error(FMOE_ERR_UNSUPPORTED, "experts: bits=%d group=%d (kernels: 4-bit, group 64)", e->bits,
@@ -82,36 +82,21 @@ static const int kMaxDecodeTokens = 128;
 
 // Every workspace starts with a 256-byte header: [0] device status word (0 ok;
 // otherwise the site code of a timed-out wait), [1] router completion counter.
-struct WsHead {
-  int* status;
-  unsigned* router_ctr;
-};
-static WsHead carve_head(Carver& c) {
+WsHead carve_head(Carver& c) {
   int* p = c.take<int>(64);
   return WsHead{p, p ? reinterpret_cast<unsigned*>(p + 1) : nullptr};
 }
 
-struct RouterWs {
-  unsigned* counters;  // [1]: token chunks done (several chunks), zero between calls
-  bf16* xs;            // normalised router input (use_norm)
-  float* unused;
-};
 
-static size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const WsHead& h, RouterWs* w) {
+size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const WsHead& h, RouterWs* w) {
   const int H = r->proj.in_features;
   bf16* xs = r->use_norm ? c.take<bf16>((size_t)T * H) : nullptr;
   if (w) *w = RouterWs{h.router_ctr, xs, nullptr};
   return c.off;
 }
 
-struct MoeWs {
-  RouteMeta m;
-  bf16* act;            // [T*k, I] gated intermediate activations
-  float* part;          // [groups, T, H] per-expert-group partial outputs
-  unsigned* tile_ctr;   // [H/16] completion counters, zero between calls
-};
 
-static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w) {
+size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w) {
   MoeWs m;
   m.tile_ctr = c.take<unsigned>(ex.H / 16);
   m.m.start = c.take<int32_t>(ex.E + 1);
@@ -127,7 +112,7 @@ static size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs
   return c.off;
 }
 
-static int check_router(const fmoe_router_t* r, QW* q) {
+int check_router(const fmoe_router_t* r, QW* q) {
   if (!r) return set_error(FMOE_ERR_INVALID, "router: null");
   int rc = to_qw(&r->proj, q);
   if (rc) return rc;
@@ -142,7 +127,7 @@ static int check_router(const fmoe_router_t* r, QW* q) {
 }
 
 // meta != nullptr: the router kernel also builds the per-expert pair lists.
-static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
+int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
                       float* wts, float* logits, const RouteMeta* meta, int* status, cudaStream_t st) {
   const bf16* xin = x;
   if (r->use_norm) {
@@ -155,7 +140,7 @@ static int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW
                              wts, logits, w.counters, meta, status, true, st);
 }
 
-static int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
+int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
                        bf16* y, const MoeWs& w, bool build_routes, int* status, cudaStream_t st) {
   int rc;
   if (build_routes) {

@@ -1,0 +1,548 @@
+// Gemma-4 decoder layer and tied lm_head for the decode step (one token per
+// sequence, T <= 8 sequences), DecoderLayer::forward_gemma4 (src/model/mod.rs:
+// 67-119) and Model::forward's lm_head + softcap (src/model/mod.rs:325-363).
+//
+// Kernel sequence of one layer (all on one stream; the GEMVs and small kernels
+// chain through programmatic dependent launch so each one's weight stream
+// starts while its predecessor drains):
+//   1 qgemv  q|k|v = input_norm(x) . [Wq Wk Wv]^T        (norm fused into the input prologue)
+//   2 qkv_post  q/k norms, RoPE, v norm, KV-cache append (kv.cu)
+//   3 attention (kv.cu)
+//   4 qgemv  o = attn . Wo^T                              (fp32, accumulating)
+//   5 ff_in  h = x + post_attn_norm(o); h1 = pre_ff_norm(h); h2 = pre_ff_norm_2(h);
+//            router input = rms_norm_no_scale(h2) * root * router_scale
+//   6 qgemv  g|u = h1 . [Wg Wu]^T                        (dense MLP)
+//   7 router (fused GEMV + top-k + routing lists) on the router input
+//   8-9 routed experts on h2 -> moe (moe.cu)
+//  10 qgemv  d = (gelu(g) * u) . Wd^T                     (GELU gating fused into the input prologue)
+//  11 ff_out x' = (h + post_ff_norm(post_ff_norm_1(d) + post_ff_norm_2(moe))) * layer_scalar
+// Every intermediate is rounded to bf16 where the reference holds a bf16 array.
+#include "internal.h"
+#include "common.cuh"
+#include "stage.cuh"
+
+namespace fmoe {
+
+constexpr int kRowThreads = 256;
+constexpr int kRowMaxPer = 16;  // hidden <= 4096
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red is reused across calls
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) s += red[w];
+  return s;
+}
+
+// One CTA per token.  h = bf16(x + bf16(rms(bf16(o)) * w_post_attn));
+// h1 / h2 = bf16(rms(h) * w); xs = bf16(bf16(bf16(rms(h2)) * bf16(root)) * router_scale).
+__global__ void __launch_bounds__(kRowThreads) ff_in_kernel(const bf16* __restrict__ x, const float* __restrict__ o_acc,
+                                                            int o_parts, int64_t o_stride, int H, const bf16* __restrict__ w_post_attn,
+                                                            const bf16* __restrict__ w_pre_ff,
+                                                            const bf16* __restrict__ w_pre_ff2, float eps, float root,
+                                                            const bf16* __restrict__ rscale, bf16* __restrict__ h_out,
+                                                            bf16* __restrict__ h1_out, bf16* __restrict__ h2_out,
+                                                            bf16* __restrict__ xs_out) {
+  __shared__ float red[kRowThreads / 32];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.x;
+  const float* o = o_acc + (int64_t)t * H;
+  const bf16* xr = x + (int64_t)t * H;
+  float a[kRowMaxPer], h[kRowMaxPer], h2[kRowMaxPer];
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) a[k] = 0.f;
+  // split-K slices added in order; one slice's loads all in flight together
+  for (int p = 0; p < o_parts; ++p) {
+    float v[kRowMaxPer];
+#pragma unroll
+    for (int k = 0; k < kRowMaxPer; ++k) {
+      const int i = threadIdx.x + k * kRowThreads;
+      v[k] = i < H ? __ldcg(o + p * o_stride + i) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kRowMaxPer; ++k) a[k] += v[k];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    a[k] = round_bf(a[k]);
+    ss = fmaf(a[k], a[k], ss);
+  }
+  const float r1 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    h[k] = i < H ? round_bf(bf2f(xr[i]) + round_bf(a[k] * r1 * bf2f(w_post_attn[i]))) : 0.f;
+    ss = fmaf(h[k], h[k], ss);
+  }
+  const float r2 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    if (i < H) {
+      h_out[(int64_t)t * H + i] = __float2bfloat16_rn(h[k]);
+      h1_out[(int64_t)t * H + i] = __float2bfloat16_rn(h[k] * r2 * bf2f(w_pre_ff[i]));
+      h2[k] = round_bf(h[k] * r2 * bf2f(w_pre_ff2[i]));
+      h2_out[(int64_t)t * H + i] = __float2bfloat16_rn(h2[k]);
+    } else {
+      h2[k] = 0.f;
+    }
+    ss = fmaf(h2[k], h2[k], ss);
+  }
+  const float r3 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float rb = round_bf(root);
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    if (i < H) {
+      float v = round_bf(round_bf(h2[k] * r3) * rb);
+      if (rscale) v = round_bf(v * bf2f(rscale[i]));
+      xs_out[(int64_t)t * H + i] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// One CTA per token.  x = bf16(bf16(h + bf16(rms(s) * w_post_ff)) * scalar),
+// s = bf16(bf16(rms(bf16(d)) * w1) + bf16(rms(moe) * w2)).
+__global__ void __launch_bounds__(kRowThreads) ff_out_kernel(const bf16* __restrict__ h_res,
+                                                             const float* __restrict__ d_acc, int d_parts,
+                                                             int64_t d_stride,
+                                                             const bf16* __restrict__ moe, int H,
+                                                             const bf16* __restrict__ w1, const bf16* __restrict__ w2,
+                                                             const bf16* __restrict__ w, float eps, float scalar,
+                                                             bf16* __restrict__ x_out) {
+  __shared__ float red[kRowThreads / 32];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.x;
+  float d[kRowMaxPer], m[kRowMaxPer];
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    d[k] = 0.f;
+    m[k] = i < H ? bf2f(moe[(int64_t)t * H + i]) : 0.f;
+  }
+  for (int p = 0; p < d_parts; ++p) {  // split-K slices in order, one slice's loads in flight together
+    float v[kRowMaxPer];
+#pragma unroll
+    for (int k = 0; k < kRowMaxPer; ++k) {
+      const int i = threadIdx.x + k * kRowThreads;
+      v[k] = i < H ? __ldcg(d_acc + p * d_stride + (int64_t)t * H + i) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kRowMaxPer; ++k) d[k] += v[k];
+  }
+  float sd = 0.f, sm = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    d[k] = round_bf(d[k]);
+    sd = fmaf(d[k], d[k], sd);
+    sm = fmaf(m[k], m[k], sm);
+  }
+  const float rd = rsqrtf(block_sum(sd, red) / (float)H + eps);
+  const float rm = rsqrtf(block_sum(sm, red) / (float)H + eps);
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    d[k] = i < H ? round_bf(round_bf(d[k] * rd * bf2f(w1[i])) + round_bf(m[k] * rm * bf2f(w2[i]))) : 0.f;
+    ss = fmaf(d[k], d[k], ss);
+  }
+  const float rs = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float sc = round_bf(scalar);
+#pragma unroll
+  for (int k = 0; k < kRowMaxPer; ++k) {
+    const int i = threadIdx.x + k * kRowThreads;
+    if (i < H) {
+      const float o = round_bf(bf2f(h_res[(int64_t)t * H + i]) + round_bf(d[k] * rs * bf2f(w[i])));
+      x_out[(int64_t)t * H + i] = __float2bfloat16_rn(o * sc);
+    }
+  }
+}
+
+// Softcap (tanh(l / c) * c in the reference's bf16 steps) and greedy argmax
+// (ties -> lowest id).  Grid (kCapCtas, T); the last CTA of a token to finish
+// merges the CTAs' candidates; it also advances the decode position counters
+// when given (pos[0] = position, pos[1] = attended slots).
+constexpr int kCapCtas = 64;
+__global__ void __launch_bounds__(kRowThreads) softcap_argmax_kernel(float* __restrict__ logits, int64_t V,
+                                                                     float cap, float2* __restrict__ cand,
+                                                                     unsigned* __restrict__ ctr,
+                                                                     int32_t* __restrict__ next_ids,
+                                                                     int64_t* __restrict__ pos) {
+  __shared__ float bv[kRowThreads / 32];
+  __shared__ int bi[kRowThreads / 32];
+  __shared__ int last;
+  griddep_wait();
+  griddep_launch_dependents();
+  const int t = blockIdx.y, c = blockIdx.x;
+  float* lr = logits + (int64_t)t * V;
+  const int64_t per = (V + kCapCtas - 1) / kCapCtas;
+  const int64_t lo = c * per, hi = min(V, lo + per);
+  float best = -INFINITY;
+  int besti = (int)min(lo, V - 1);  // a valid id even if every logit is NaN
+  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+    float v = round_bf(lr[i]);
+    if (cap > 0.f) v = round_bf(round_bf(tanhf(round_bf(v / cap))) * cap);
+    lr[i] = v;
+    if (v > best) {
+      best = v;
+      besti = (int)i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (ov == best && oi < besti)) {
+      best = ov;
+      besti = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = besti;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kRowThreads / 32; ++w)
+      if (bv[w] > best || (bv[w] == best && bi[w] < besti)) {
+        best = bv[w];
+        besti = bi[w];
+      }
+    cand[t * kCapCtas + c] = make_float2(best, __int_as_float(besti));
+    __threadfence();
+    const unsigned prev = atomicAdd(&ctr[t], 1u);
+    last = prev == kCapCtas - 1;
+  }
+  __syncthreads();
+  if (!last || threadIdx.x != 0) return;
+  __threadfence();
+  ctr[t] = 0u;
+  for (int k = 0; k < kCapCtas; ++k) {
+    const float2 cv = __ldcg(cand + t * kCapCtas + k);
+    const int ci = __float_as_int(cv.y);
+    if (k == 0 || cv.x > best || (cv.x == best && ci < besti)) {
+      best = cv.x;
+      besti = ci;
+    }
+  }
+  next_ids[t] = besti;
+  if (pos && t == 0) {
+    // every token of the step has finished: advance the position counters once
+    pos[0] += 1;
+    pos[1] += 1;
+  }
+}
+
+static cudaLaunchConfig_t row_cfg(dim3 grid, cudaStream_t st, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kRowThreads);
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// ---------------------------------------------------------------------------
+// Layer workspace (the router counter lives in the 256-byte header).
+struct DecWs {
+  WsHead h;
+  RouterWs rw;
+  MoeWs mw;
+  float *qkv, *o, *gu, *d;
+  bf16 *q, *attn, *hres, *h1, *h2, *xs, *moe;
+  int32_t* ids;
+  float* wts;
+  void* attn_ws;
+  size_t bytes;
+};
+
+static int dec_dims(const fmoe_decoder_layer_t* L, int* qkv_rows) {
+  if (!L) return set_error(FMOE_ERR_INVALID, "decoder: null layer");
+  const int H = L->q_proj.in_features, D = L->head_dim;
+  if (L->num_heads <= 0 || L->num_kv_heads <= 0 || L->num_heads % L->num_kv_heads)
+    return set_error(FMOE_ERR_INVALID, "decoder: heads %d / kv heads %d", L->num_heads, L->num_kv_heads);
+  if (H % 64 || H > kRowThreads * kRowMaxPer) return set_error(FMOE_ERR_UNSUPPORTED, "decoder: hidden %d", H);
+  if (L->q_proj.out_features != L->num_heads * D || L->k_proj.out_features != L->num_kv_heads * D ||
+      L->o_proj.in_features != L->num_heads * D || L->o_proj.out_features != H)
+    return set_error(FMOE_ERR_INVALID, "decoder: projection shapes do not match heads x head_dim");
+  if (!L->k_eq_v && (!L->v_proj.w || L->v_proj.out_features != L->num_kv_heads * D))
+    return set_error(FMOE_ERR_INVALID, "decoder: v_proj missing (k_eq_v = 0)");
+  if (L->rope_dims <= 0 || L->rope_dims > D || L->rope_dims % (D / 16))
+    return set_error(FMOE_ERR_UNSUPPORTED, "decoder: rope_dims %d (a multiple of %d up to %d)", L->rope_dims, D / 16, D);
+  *qkv_rows = (L->num_heads + (L->k_eq_v ? 1 : 2) * L->num_kv_heads) * D;
+  return FMOE_OK;
+}
+
+// Split-K slices a GEMV over K inputs can produce (qgemv keeps >= 8 groups of
+// 64 per column chunk).
+static int max_parts(int K) { return K / 512 > 1 ? K / 512 : 1; }
+
+static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, DecWs* w) {
+  DecWs d = {};
+  int qkv_rows = 0;
+  dec_dims(L, &qkv_rows);
+  const int H = L->q_proj.in_features, Id = L->mlp_gate.out_features, QD = L->num_heads * L->head_dim;
+  ExpertsDev ex = {};
+  to_experts(&L->experts, &ex);
+  // Everything that must hold its value between calls (status word, router /
+  // expert / attention merge counters) sits at offsets every layer shares.
+  d.h = carve_head(c);
+  carve_router(c, T, &L->router, d.h, &d.rw);
+  carve_moe(c, T, L->router.top_k, ex, &d.mw);
+  d.attn_ws = c.take<uint8_t>(attn_workspace_bytes(kv, L->num_heads));
+  d.qkv = c.take<float>((size_t)T * qkv_rows);
+  d.o = c.take<float>((size_t)max_parts(QD) * T * H);
+  d.gu = c.take<float>((size_t)max_parts(H) * T * 2 * Id);
+  d.d = c.take<float>((size_t)max_parts(Id) * T * H);
+  d.q = c.take<bf16>((size_t)T * QD);
+  d.attn = c.take<bf16>((size_t)T * QD);
+  d.hres = c.take<bf16>((size_t)T * H);
+  d.h1 = c.take<bf16>((size_t)T * H);
+  d.h2 = c.take<bf16>((size_t)T * H);
+  d.xs = c.take<bf16>((size_t)T * H);
+  d.moe = c.take<bf16>((size_t)T * H);
+  d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
+  d.wts = c.take<float>((size_t)T * L->router.top_k);
+  d.bytes = c.off + 256;
+  if (w) *w = d;
+  return d.bytes;
+}
+
+static QgSeg seg_of(const QW& q, void* out, int ld, int col0) {
+  return QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, out, q.out, ld, col0, 0};
+}
+
+static int check_stream_w(const QW& q, int group, const char* what) {
+  if ((q.bits != 4 && q.bits != 6 && q.bits != 8) || group != 64 || q.in % 64 || q.out % 16 ||
+      !aligned(q.w, 16) || !aligned(q.s, 16) || !aligned(q.b, 16))
+    return set_error(FMOE_ERR_UNSUPPORTED, "decoder: %s must be 4/6/8-bit, group 64, 16-byte aligned", what);
+  return FMOE_OK;
+}
+
+}  // namespace fmoe
+
+using namespace fmoe;
+
+extern "C" {
+
+size_t fmoe_decoder_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache) {
+  KvDev kv;
+  int qkv_rows;
+  if (T <= 0 || dec_dims(layer, &qkv_rows) || kv_to_dev(cache, &kv)) return 0;
+  Carver c(nullptr);
+  return carve_dec(c, T, layer, kv, nullptr);
+}
+
+int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, void* x, int64_t T,
+                               int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  int qkv_rows = 0;
+  int rc = dec_dims(L, &qkv_rows);
+  if (rc) return rc;
+  KvDev kv;
+  rc = kv_to_dev(cache, &kv);
+  if (rc) return rc;
+  if (T < 1 || T > 8) return set_error(FMOE_ERR_UNSUPPORTED, "decoder: T=%lld (decode kernels: 1..8 sequences)", (long long)T);
+  if (kv.B != T || kv.Hkv != L->num_kv_heads || kv.D != L->head_dim)
+    return set_error(FMOE_ERR_INVALID, "decoder: cache [%d, %d, ., %d] does not match T=%lld / kv heads / head_dim",
+                     kv.B, kv.Hkv, kv.D, (long long)T);
+  if (!x || !aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "decoder: x null or not 16-byte aligned");
+  QW q, k, v, o, gq, uq, dq, rq;
+  ExpertsDev ex;
+  if ((rc = to_qw(&L->q_proj, &q)) || (rc = to_qw(&L->k_proj, &k)) || (rc = to_qw(&L->o_proj, &o)) ||
+      (rc = to_qw(&L->mlp_gate, &gq)) || (rc = to_qw(&L->mlp_up, &uq)) || (rc = to_qw(&L->mlp_down, &dq)) ||
+      (rc = check_router(&L->router, &rq)) || (rc = to_experts(&L->experts, &ex)))
+    return rc;
+  if (!L->k_eq_v && (rc = to_qw(&L->v_proj, &v))) return rc;
+  if ((rc = check_stream_w(q, L->q_proj.group_size, "q_proj")) || (rc = check_stream_w(k, L->k_proj.group_size, "k_proj")) ||
+      (!L->k_eq_v && (rc = check_stream_w(v, L->v_proj.group_size, "v_proj"))) ||
+      (rc = check_stream_w(o, L->o_proj.group_size, "o_proj")) ||
+      (rc = check_stream_w(gq, L->mlp_gate.group_size, "mlp gate")) ||
+      (rc = check_stream_w(uq, L->mlp_up.group_size, "mlp up")) ||
+      (rc = check_stream_w(dq, L->mlp_down.group_size, "mlp down")))
+    return rc;
+  const int H = q.in, Id = gq.out, QD = L->num_heads * L->head_dim;
+  if (k.in != H || o.out != H || gq.in != H || uq.out != Id || uq.in != H || dq.in != Id || dq.out != H ||
+      ex.H != H || rq.in != H || (!L->k_eq_v && v.in != H))
+    return set_error(FMOE_ERR_INVALID, "decoder: hidden / intermediate sizes disagree across weights");
+  const size_t need = fmoe_decoder_workspace_bytes(T, L, cache);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return set_error(FMOE_ERR_WORKSPACE, "decoder: workspace %zu < %zu", workspace_bytes, need);
+  Carver c(workspace);
+  DecWs w;
+  carve_dec(c, T, L, kv, &w);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bf16* xb = static_cast<bf16*>(x);
+  const int Ti = (int)T;
+  int o_parts = 1, gu_parts = 1, d_parts = 1;
+
+  // 1 q|k|v = input_norm(x) . W^T  (plain fp32 stores)
+  {
+    QgArgs a = {};
+    a.nseg = L->k_eq_v ? 2 : 3;
+    a.seg[0] = seg_of(q, w.qkv, qkv_rows, 0);
+    a.seg[1] = seg_of(k, w.qkv, qkv_rows, QD);
+    if (!L->k_eq_v) a.seg[2] = seg_of(v, w.qkv, qkv_rows, QD + k.out);
+    a.K = H;
+    a.T = Ti;
+    a.out_kind = QG_OUT_F32;
+    a.in_kind = QG_IN_RMSNORM;
+    a.x = xb;
+    a.ldx = H;
+    a.norm_w = static_cast<const bf16*>(L->input_norm);
+    a.eps = L->eps;
+    a.status = w.h.status;
+    QgLayout ql;
+    if ((rc = qgemv_plan(a, q.bits, false, &ql, true)) || (rc = launch_qgemv(a, ql, q.bits, true, st))) return rc;
+  }
+  // 2 norms, RoPE, KV append
+  if ((rc = launch_qkv_post(kv, w.qkv, qkv_rows, L->num_heads, L->k_eq_v, static_cast<const bf16*>(L->q_norm),
+                            static_cast<const bf16*>(L->k_norm), L->eps, L->rope_dims, L->rope_theta, pos, pos_dev,
+                            w.q, 0, true, st)))
+    return rc;
+  // 3 attention over the slots written so far (pos_dev[1] when counters live on the device)
+  const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;
+  if ((rc = launch_attn_decode(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
+                               w.attn_ws, w.attn, st)))
+    return rc;
+  // 4 o = attn . Wo^T
+  {
+    QgArgs a = {};
+    a.nseg = 1;
+    a.seg[0] = seg_of(o, w.o, H, 0);
+    a.K = QD;
+    a.T = Ti;
+    a.out_kind = QG_OUT_F32_PART;
+    a.in_kind = QG_IN_BF16;
+    a.x = w.attn;
+    a.ldx = QD;
+    a.status = w.h.status;
+    QgLayout ql;
+    if ((rc = qgemv_plan(a, o.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, o.bits, true, st))) return rc;
+    o_parts = a.nkc;
+  }
+  // 5 residual + feed-forward input norms
+  {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = row_cfg(dim3(Ti), st, attr);
+    ProfScope prof_("ff_in_kernel", st);
+    cudaLaunchKernelEx(&cfg, ff_in_kernel, (const bf16*)xb, (const float*)w.o, o_parts, (int64_t)T * H, H,
+                       static_cast<const bf16*>(L->post_attn_norm), static_cast<const bf16*>(L->pre_ff_norm),
+                       static_cast<const bf16*>(L->pre_ff_norm_2), L->eps, L->router.root_size,
+                       static_cast<const bf16*>(L->router.router_scale), w.hres, w.h1, w.h2, w.xs);
+    if ((rc = check_launch("ff_in_kernel"))) return rc;
+  }
+  // 6 dense MLP gate | up
+  {
+    QgArgs a = {};
+    a.nseg = 2;
+    a.seg[0] = seg_of(gq, w.gu, 2 * Id, 0);
+    a.seg[1] = seg_of(uq, w.gu, 2 * Id, Id);
+    a.K = H;
+    a.T = Ti;
+    a.out_kind = QG_OUT_F32_PART;
+    a.in_kind = QG_IN_BF16;
+    a.x = w.h1;
+    a.ldx = H;
+    a.status = w.h.status;
+    QgLayout ql;
+    if ((rc = qgemv_plan(a, gq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, gq.bits, true, st))) return rc;
+    gu_parts = a.nkc;
+  }
+  // 7-9 router on the prepared input, routed experts on h2
+  {
+    fmoe_router_t r = L->router;
+    r.use_norm = 0;  // ff_in applied the norm chain
+    if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, st))) return rc;
+    if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, st))) return rc;
+  }
+  // 10 dense down on gelu(g) * u
+  {
+    QgArgs a = {};
+    a.nseg = 1;
+    a.seg[0] = seg_of(dq, w.d, H, 0);
+    a.K = Id;
+    a.T = Ti;
+    a.out_kind = QG_OUT_F32_PART;
+    a.in_kind = QG_IN_GELU;
+    a.g = w.gu;
+    a.u = w.gu + Id;
+    a.ldgu = 2 * Id;
+    a.gu_parts = gu_parts;
+    a.gu_part_stride = (int64_t)T * 2 * Id;
+    a.status = w.h.status;
+    QgLayout ql;
+    if ((rc = qgemv_plan(a, dq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, dq.bits, true, st))) return rc;
+    d_parts = a.nkc;
+  }
+  // 11 output norms, residual, layer scalar -> x
+  {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = row_cfg(dim3(Ti), st, attr);
+    ProfScope prof_("ff_out_kernel", st);
+    cudaLaunchKernelEx(&cfg, ff_out_kernel, (const bf16*)w.hres, (const float*)w.d, d_parts, (int64_t)T * H,
+                       (const bf16*)w.moe, H,
+                       static_cast<const bf16*>(L->post_ff_norm_1), static_cast<const bf16*>(L->post_ff_norm_2),
+                       static_cast<const bf16*>(L->post_ff_norm), L->eps, L->layer_scalar, xb);
+    if ((rc = check_launch("ff_out_kernel"))) return rc;
+  }
+  return FMOE_OK;
+}
+
+size_t fmoe_lm_head_workspace_bytes(int64_t T) {
+  if (T <= 0) return 0;
+  return 256 + align_up(sizeof(unsigned) * (size_t)T, 256) + sizeof(float2) * (size_t)T * kCapCtas;
+}
+
+int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps, const void* x, int64_t T,
+                 float softcap, float* logits, int32_t* next_ids, int64_t* pos_dev, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  QW q;
+  int rc = to_qw(embed, &q);
+  if (rc) return rc;
+  if ((rc = check_stream_w(q, embed->group_size, "embedding"))) return rc;
+  if (T < 1 || T > 8) return set_error(FMOE_ERR_UNSUPPORTED, "lm_head: T=%lld (1..8)", (long long)T);
+  if (!x || !logits || !next_ids || !final_norm) return set_error(FMOE_ERR_INVALID, "lm_head: null pointer");
+  if (!workspace || workspace_bytes < fmoe_lm_head_workspace_bytes(T))
+    return set_error(FMOE_ERR_WORKSPACE, "lm_head: workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  int* status = reinterpret_cast<int*>(base);
+  unsigned* ctr = reinterpret_cast<unsigned*>(base + 256);
+  float2* cand = reinterpret_cast<float2*>(base + 256 + align_up(sizeof(unsigned) * (size_t)T, 256));
+  QgArgs a = {};
+  a.nseg = 1;
+  a.seg[0] = seg_of(q, logits, q.out, 0);
+  a.K = q.in;
+  a.T = (int)T;
+  a.out_kind = QG_OUT_F32;
+  a.in_kind = QG_IN_RMSNORM;
+  a.x = static_cast<const bf16*>(x);
+  a.ldx = q.in;
+  a.norm_w = static_cast<const bf16*>(final_norm);
+  a.eps = eps;
+  a.status = status;
+  QgLayout ql;
+  if ((rc = qgemv_plan(a, q.bits, false, &ql)) || (rc = launch_qgemv(a, ql, q.bits, true, st))) return rc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = row_cfg(dim3(kCapCtas, (unsigned)T), st, attr);
+  ProfScope prof_("softcap_argmax_kernel", st);
+  cudaLaunchKernelEx(&cfg, softcap_argmax_kernel, logits, (int64_t)q.out, softcap, cand, ctr, next_ids, pos_dev);
+  return check_launch("softcap_argmax_kernel");
+}
+
+}  // extern "C"

@@ -101,7 +101,10 @@ struct AttnPlan {
 // matrices sharing one input.
 constexpr int kQgMaxSeg = 4;
 enum { QG_IN_BF16 = 0, QG_IN_RMSNORM = 1, QG_IN_GELU = 2 };
-enum { QG_OUT_F32 = 0, QG_OUT_F32_ADD = 1, QG_OUT_BF16 = 2 };
+// QG_OUT_F32_PART: column chunk c of the input stores its partial sums in
+// slice c of the output ([nkc][T][ld] f32, slice stride T * ld); the consumer
+// adds the slices in order (deterministic split-K).
+enum { QG_OUT_F32 = 0, QG_OUT_F32_ADD = 1, QG_OUT_BF16 = 2, QG_OUT_F32_PART = 3 };
 struct QgSeg {
   const uint8_t* w;  // packed codes [rows][K*bits/32 words]
   const bf16* s;     // [rows][K/64]
@@ -123,6 +126,8 @@ struct QgArgs {
   const float* g;      // [T][ldgu] fp32 gate / up projections (QG_IN_GELU)
   const float* u;
   int ldgu;
+  int gu_parts;        // QG_IN_GELU: partial slices of g / u to add (>= 1)
+  int64_t gu_part_stride;
   float* zero_ptr[4];  // fp32 buffers cleared after griddepcontrol.wait (for later accumulating kernels)
   int64_t zero_n[4];
   int* status;
@@ -130,10 +135,52 @@ struct QgArgs {
 struct QgLayout {
   int rs, soff, stage, sfull, nst, frag, xsum, red, misc, cnt, bar, bytes, grid, nw, rt;
 };
-int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L);
+int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L, bool half_sm = false);
 int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStream_t st);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Carver;
+
+// abi.cu: argument checks, workspace carving and the router / expert sequence
+// shared by the MoE-block and decoder-layer entry points.
+bool aligned(const void* p, size_t a);
+int to_qw(const fmoe_qweight_t* w, QW* q);
+int to_experts(const fmoe_experts_t* e, ExpertsDev* d);
+int check_router(const fmoe_router_t* r, QW* q);
+// Every workspace starts with a 256-byte header: [0] device status word (0 ok;
+// otherwise the site code of a timed-out wait), [1] router completion counter.
+struct WsHead {
+  int* status;
+  unsigned* router_ctr;
+};
+struct RouterWs {
+  unsigned* counters;  // [1]: token chunks done (several chunks), zero between calls
+  bf16* xs;            // normalised router input (use_norm)
+  float* unused;
+};
+struct MoeWs {
+  RouteMeta m;
+  bf16* act;           // [T*k, I] gated intermediate activations
+  float* part;         // [groups, T, H] per-expert-group partial outputs
+  unsigned* tile_ctr;  // [H/16] completion counters, zero between calls
+};
+WsHead carve_head(Carver& c);
+size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const WsHead& h, RouterWs* w);
+size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w);
+int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
+               float* wts, float* logits, const RouteMeta* meta, int* status, cudaStream_t st);
+int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex, bf16* y,
+                const MoeWs& w, bool build_routes, int* status, cudaStream_t st);
+
+// kv.cu
+int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d);
+size_t attn_workspace_bytes(const KvDev& c, int Hq);
+int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
+                       void* ws, bf16* out, cudaStream_t st);
+int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v, const bf16* q_norm,
+                    const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
+                    const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st);
 
 // Bump allocator over a caller workspace.
 struct Carver {

@@ -247,6 +247,113 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 }
 
 // ---------------------------------------------------------------------------
+// Decode-step attention input: the q / k / v projections (fp32, one row per
+// sequence) -> per-head RMSNorm -> RoPE -> query rows for attention and the
+// new K / V rows appended to the cache, one warp per (sequence, head) row.
+// Follows Gemma4Attention::forward, src/model/gemma4_attention.rs:46-84:
+//   q = rope(q_norm(q_proj x));  k = rope(k_norm(k_proj x));
+//   v = v_norm(v_proj x), or v_norm(k_proj x) before k_norm when K == V;
+// every tensor rounded to bf16 as the reference's bf16 arrays are.  RoPE is
+// MLX fast::rope, non-traditional: the first rope_dims dims rotate in pairs
+// (i, i + rope_dims/2) by angle pos * inv_freq[i].
+
+template <int P>
+__device__ __forceinline__ void warp_rms_norm(float (&v)[P], const bf16* w, float eps, int lane) {
+  constexpr int D = 32 * P;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < P; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] = round_bf(w ? v[i] * r * bf2f(w[lane * P + i]) : v[i] * r);
+}
+
+template <int P>
+__device__ __forceinline__ void warp_rope(float (&v)[P], int rope_dims, float log2_theta, float pos, int lane) {
+  const int half = rope_dims / 2;
+  const int ofs = half / P;  // partner lane distance (half is a multiple of P)
+  float o[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const float up = __shfl_down_sync(0xffffffffu, v[i], ofs & 31);
+    const float dn = __shfl_up_sync(0xffffffffu, v[i], ofs & 31);
+    const int e = lane * P + i;
+    o[i] = v[i];
+    if (e < rope_dims) {
+      // inv_freq_j = theta^(-2j / rope_dims), j = e mod half
+      const int j = e < half ? e : e - half;
+      float sn, cs;
+      sincosf(pos * exp2f(-(float)(2 * j) / (float)rope_dims * log2_theta), &sn, &cs);
+      o[i] = e < half ? round_bf(v[i] * cs - up * sn) : round_bf(dn * sn + v[i] * cs);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] = o[i];
+}
+
+template <int P>
+__global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __restrict__ qkv, int ld, int Hq,
+                                                       int k_eq_v, const bf16* __restrict__ q_norm,
+                                                       const bf16* __restrict__ k_norm, float eps, int rope_dims,
+                                                       float log2_theta, int64_t pos,
+                                                       const int64_t* __restrict__ pos_dev, bf16* __restrict__ q_out,
+                                                       int turbo_bits, float inv_sqrt_d) {
+  constexpr int D = 32 * P, G = D / 64;
+  griddep_wait();  // the projections come from the preceding kernel
+  griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int Hkv = c.Hkv, T = c.B;  // one token per sequence
+  if (row >= T * (Hq + Hkv)) return;
+  const int64_t p0 = pos_dev ? *pos_dev : pos;
+  const float fpos = (float)p0;
+  float v[P];
+  if (row < T * Hq) {
+    const int t = row / Hq, h = row % Hq;
+    const float* src = qkv + (int64_t)t * ld + h * D + lane * P;
+#pragma unroll
+    for (int i = 0; i < P; ++i) v[i] = round_bf(__ldcg(src + i));
+    warp_rms_norm<P>(v, q_norm, eps, lane);
+    warp_rope<P>(v, rope_dims, log2_theta, fpos, lane);
+    store_row_bf16<P>(q_out + ((int64_t)t * Hq + h) * D, lane, v);
+    return;
+  }
+  const int r = row - T * Hq, t = r / Hkv, hk = r % Hkv;
+  const float* ks = qkv + (int64_t)t * ld + (Hq + hk) * D + lane * P;
+  const float* vs = k_eq_v ? ks : qkv + (int64_t)t * ld + (Hq + Hkv + hk) * D + lane * P;
+  float kv[P], vv[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    kv[i] = round_bf(__ldcg(ks + i));
+    vv[i] = round_bf(__ldcg(vs + i));
+  }
+  warp_rms_norm<P>(vv, nullptr, eps, lane);  // v_norm: no learned scale
+  warp_rms_norm<P>(kv, k_norm, eps, lane);
+  warp_rope<P>(kv, rope_dims, log2_theta, fpos, lane);
+  const int64_t dst = ((int64_t)t * Hkv + hk) * c.cap + p0 % c.cap;
+  if (c.mode == FMOE_KV_BF16) {
+    if (turbo_bits) {
+      warp_turbo<P>(kv, lane, turbo_bits);
+      warp_turbo<P>(vv, lane, turbo_bits);
+    }
+    store_row_bf16<P>(reinterpret_cast<bf16*>(c.k) + dst * D, lane, kv);
+    store_row_bf16<P>(reinterpret_cast<bf16*>(c.v) + dst * D, lane, vv);
+    return;
+  }
+  warp_fwht<P>(kv, lane);
+  warp_fwht<P>(vv, lane);
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    kv[i] *= inv_sqrt_d;
+    vv[i] *= inv_sqrt_d;
+  }
+  warp_quant_store<P, 4>(kv, lane, reinterpret_cast<uint32_t*>(c.k) + dst * (D / 8), c.ks + dst * G, c.kb + dst * G);
+  warp_quant_store<P, 8>(vv, lane, reinterpret_cast<uint32_t*>(c.v) + dst * (D / 4), c.vs + dst * G, c.vb + dst * G);
+}
+
+// ---------------------------------------------------------------------------
 // Split-KV decode attention.  CTA = (split, kv head, batch); its GQ = Hq/Hkv
 // query heads are the N columns of the MMAs.  A split covers S consecutive
 // slots, processed in chunks of CH positions through a two-stage ring of TMA
@@ -274,10 +381,12 @@ struct AtCfg {
   static constexpr int KRB = MODE == FMOE_KV_BF16 ? 2 * D : D / 2;  // K bytes per position
   static constexpr int VRB = MODE == FMOE_KV_BF16 ? 2 * D : D;      // V bytes per position
   static constexpr int SB = MODE == FMOE_KV_BF16 ? 0 : 2 * G;       // bytes of one scale / bias row
-  static constexpr int CH = MODE == FMOE_KV_BF16 ? (P == 8 ? 64 : 32) : (P == 8 ? 128 : 64);
+  // bf16 cache at head_dim 256: 32-position chunks (two 32 KB stages) leave room
+  // on the SM for the next kernel of a decode chain
+  static constexpr int CH = MODE == FMOE_KV_BF16 ? 32 : (P == 8 ? 128 : 64);
   static constexpr int NST = 2;
   static constexpr int KS = CH * KRB, KB = KS + CH * SB, VC = KB + CH * SB, VS = VC + CH * VRB, VB = VS + CH * SB;
-  static constexpr int STAGE = VB + CH * SB;  // 53,248 (affine) / 65,536 (bf16) bytes
+  static constexpr int STAGE = VB + CH * SB;  // 53,248 (affine) / 32,768 or 65,536 (bf16) bytes
   static constexpr int TPC = CH / 16;         // 16-position tiles per chunk
   static constexpr int WPT = 8 / TPC;         // warps per tile (they split the groups)
   static constexpr int GPW = G / WPT;         // groups per warp
@@ -1093,6 +1202,31 @@ int launch_kv_append(const KvDev& c, const bf16* k, const bf16* v, int64_t Tn, i
   return check_launch("kv_append_kernel");
 }
 
+int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v, const bf16* q_norm,
+                    const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
+                    const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st) {
+  const float l2t = (float)std::log2((double)rope_theta);
+  const int rows = c.B * (Hq + c.Hkv);
+  const float inv = 1.0f / std::sqrt((float)c.D);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((rows + 7) / 8);
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  ProfScope prof_("qkv_post_kernel", st);
+  if (c.D == 256)
+    cudaLaunchKernelEx(&cfg, qkv_post_kernel<8>, c, qkv, ld, Hq, k_eq_v, q_norm, k_norm, eps, rope_dims, l2t, pos,
+                       pos_dev, q_out, turbo_bits, inv);
+  else
+    cudaLaunchKernelEx(&cfg, qkv_post_kernel<16>, c, qkv, ld, Hq, k_eq_v, q_norm, k_norm, eps, rope_dims, l2t,
+                       pos, pos_dev, q_out, turbo_bits, inv);
+  return check_launch("qkv_post_kernel");
+}
+
 int launch_turbo_round_trip(const bf16* x, int64_t rows, int D, int bits, bf16* out, cudaStream_t st) {
   const unsigned blocks = (unsigned)((rows + 7) / 8);
   if (D == 256) {
@@ -1225,6 +1359,10 @@ int to_kv(const fmoe_kv_cache_t* c, KvDev* d) {
 }
 
 }  // namespace
+
+namespace fmoe {
+int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d) { return to_kv(c, d); }
+}  // namespace fmoe
 
 extern "C" {
 

@@ -185,7 +185,8 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
   const int T = a.T, K = a.K, G = K / 64, gc = a.kc / 64;
   // unit range; outputs that are stored (not accumulated) keep a block's chunks in one CTA
-  const int ub = a.out_kind == QG_OUT_F32_ADD ? 1 : a.nkc;
+  const bool split_ok = a.out_kind == QG_OUT_F32_ADD || a.out_kind == QG_OUT_F32_PART;
+  const int ub = split_ok ? 1 : a.nkc;
   const int nb = a.units / ub;
   const int u0 = (int)((int64_t)nb * blockIdx.x / gridDim.x) * ub;
   const int u1 = (int)((int64_t)nb * (blockIdx.x + 1) / gridDim.x) * ub;
@@ -222,9 +223,16 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
     for (int tk = warp; tk < T; tk += NW + 1) {
       const bf16* xr = a.x + (int64_t)tk * a.ldx;
       float ss = 0.f;
-      for (int i = lane * 8; i < K; i += 256) {
-        const uint4 w = ld_u4(xr + i);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      // K <= 8192: up to 32 16-byte loads per lane, all issued before use
+      uint4 wv[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int i = lane * 8 + j * 256;
+        wv[j] = i < K ? ld_u4(xr + i) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const uint32_t ww[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float lo = bf16lo(ww[e]), hi = bf16hi(ww[e]);
@@ -251,11 +259,25 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
     } else if (a.in_kind == QG_IN_GELU) {
       const float* gp = a.g + (int64_t)tk * a.ldgu + c0;
       const float* up = a.u + (int64_t)tk * a.ldgu + c0;
+      float gs[16], us[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) gs[e] = us[e] = 0.f;
+      for (int pp = 0; pp < a.gu_parts; ++pp) {  // partial slices in order; a slice's 8 loads in flight together
+        float4 gg[4], uu[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          gg[e] = __ldcg(reinterpret_cast<const float4*>(gp + pp * a.gu_part_stride + 4 * e));
+          uu[e] = __ldcg(reinterpret_cast<const float4*>(up + pp * a.gu_part_stride + 4 * e));
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          gs[4 * e] += gg[e].x, gs[4 * e + 1] += gg[e].y, gs[4 * e + 2] += gg[e].z, gs[4 * e + 3] += gg[e].w;
+          us[4 * e] += uu[e].x, us[4 * e + 1] += uu[e].y, us[4 * e + 2] += uu[e].z, us[4 * e + 3] += uu[e].w;
+        }
+      }
 #pragma unroll
       for (int e = 0; e < 16; e += 4) {
-        const float4 gg = __ldcg(reinterpret_cast<const float4*>(gp + e));
-        const float4 uu = __ldcg(reinterpret_cast<const float4*>(up + e));
-        const float ga[4] = {gg.x, gg.y, gg.z, gg.w}, ua[4] = {uu.x, uu.y, uu.z, uu.w};
+        const float ga[4] = {gs[e], gs[e + 1], gs[e + 2], gs[e + 3]}, ua[4] = {us[e], us[e + 1], us[e + 2], us[e + 3]};
 #pragma unroll
         for (int q = 0; q < 4; ++q) v[e + q] = round_bf(gelu_tanh(round_bf(ga[q])) * round_bf(ua[q]));
       }
@@ -321,11 +343,12 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
   float y[RT][4];
 #pragma unroll
   for (int tt = 0; tt < RT; ++tt) y[tt][0] = y[tt][1] = y[tt][2] = y[tt][3] = 0.f;
-  int flushes = 0;
+  int flushes = 0, run_kc0 = -1;
   const int sst = L.sfull ? G : gc;  // scale row stride in a stage
   for (int i = 0; i < n; ++i) {
     const int st = i % L.nst, u = u0 + i;
     const QgUnit q = qg_unit(a, u);
+    if (run_kc0 < 0) run_kc0 = q.kci;
     const uint8_t* sb = smem + (size_t)st * L.stage;
     if (!mbar_wait(&bar[st], (uint32_t)(i / L.nst) & 1u, a.status, 61)) *(volatile int*)flag = 1;
     if (*(volatile int*)flag) break;  // a copy never landed (the status word says so)
@@ -365,6 +388,8 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);  // this warp is done with the stage
+    // a run of this block's column chunks ends here?  (F32_PART: the run's sum
+    // goes to the slice of its first chunk, the run's other slices get zeros)
     bool flush = i + 1 == n;
     if (!flush) {
       const QgUnit nq = qg_unit(a, u + 1);
@@ -399,16 +424,22 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
           const int r = o % R, tk = o / R;
           float sum = 0.f;
           for (int w = 0; w < NW; ++w) sum += rs[(w * R + r) * T + tk];
-          const int64_t oi = (int64_t)tk * sg.ld + sg.col0 + q.blk * R + r;
+          int64_t oi = (int64_t)tk * sg.ld + sg.col0 + q.blk * R + r;
+          if (a.out_kind == QG_OUT_F32_PART) {
+            for (int kz = run_kc0 + 1; kz <= q.kci; ++kz)
+              static_cast<float*>(sg.out)[oi + (int64_t)kz * T * sg.ld] = 0.f;
+            oi += (int64_t)run_kc0 * T * sg.ld;
+          }
           if (a.out_kind == QG_OUT_F32_ADD)
             atomicAdd(static_cast<float*>(sg.out) + oi, sum);
-          else if (a.out_kind == QG_OUT_F32)
+          else if (a.out_kind == QG_OUT_F32 || a.out_kind == QG_OUT_F32_PART)
             static_cast<float*>(sg.out)[oi] = sum;
           else
             static_cast<bf16*>(sg.out)[oi] = __float2bfloat16_rn(sum);
         }
       }
       ++flushes;
+      run_kc0 = -1;
     }
   }
 }
@@ -424,15 +455,22 @@ static int qg_row_stride(int bytes, int bits) {
   return s;
 }
 
-static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, QgLayout* L);
+static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, bool half_sm, QgLayout* L);
 
-int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L) {
-  // 32-row units when they fit, else 16-row units
-  if (qgemv_plan_rt(a, bits, allow_split, true, L) == FMOE_OK) return FMOE_OK;
-  return qgemv_plan_rt(a, bits, allow_split, false, L);
+int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L, bool half_sm) {
+  // 32-row units when they fit, else 16-row units; the whole SM when half of it is too small
+  const bool budgets[2] = {half_sm, false};
+  for (int b = 0; b < (half_sm ? 2 : 1); ++b) {
+    if (qgemv_plan_rt(a, bits, allow_split, true, budgets[b], L) == FMOE_OK) return FMOE_OK;
+    if (qgemv_plan_rt(a, bits, allow_split, false, budgets[b], L) == FMOE_OK) return FMOE_OK;
+  }
+  return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d, T %d exceed shared memory", a.K, a.T);
 }
 
-static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, QgLayout* L) {
+// half_sm: at most ~110 KB of shared memory and 8 + 1 warps, so the next
+// kernel of a programmatic-dependent chain fits on the SM beside this one and
+// streams its weights while this one finishes.
+static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, bool half_sm, QgLayout* L) {
   const int K = a.K, G = K / 64;
   if (bits != 4 && bits != 6 && bits != 8) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: bits %d", bits);
   if (K % 64 || a.T < 1 || a.T > 8) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d, T %d", K, a.T);
@@ -454,7 +492,7 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, Qg
   } else {
     double best_eff = -1.0;
     for (int c = 1; c <= G; ++c) {
-      if (G % c || (c > 1 && G / c < 8)) continue;
+      if (G % c || (c > 1 && G / c < 8)) continue;  // >= 8 groups (512 inputs) per chunk
       if (16 * (K / c) * bits / 8 > 48 * 1024) continue;
       if (nkc && !allow_split) break;
       const int64_t u = (int64_t)tiles * c, per = (u + kNumSMs - 1) / kNumSMs;
@@ -470,7 +508,7 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, Qg
   L->rt = rt;
   a.nkc = nkc;
   a.kc = K / nkc;
-  if (a.nkc > 1 && a.out_kind != QG_OUT_F32_ADD)
+  if (a.nkc > 1 && a.out_kind != QG_OUT_F32_ADD && a.out_kind != QG_OUT_F32_PART)
     return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d at %d bits needs column chunks (accumulating output)", K, bits);
   const int R = 16 * rt;
   int u = 0;
@@ -485,9 +523,10 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, Qg
   L->soff = R * L->rs;
   L->stage = (int)align_up(L->soff + 2 * R * (L->sfull ? G : gc) * 2, 128);
   // consumer warps: the count (8..16) that deals a unit's groups most evenly
-  int nw = kQgMaxWarps;
+  const int maxw = half_sm ? 8 : kQgMaxWarps;
+  int nw = maxw;
   double nw_eff = 0.0;
-  for (int w = kQgMaxWarps; w >= 8; --w) {
+  for (int w = maxw; w >= 8; --w) {
     const double e = (double)gc / (double)(w * ((gc + w - 1) / w));
     if (e > nw_eff + 1e-9) {
       nw_eff = e;
@@ -497,7 +536,8 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, Qg
   L->nw = nw;
   const size_t frag = (size_t)G * 4 * a.T * 32, xs = (size_t)G * 8 * 4, red1 = (size_t)nw * R * a.T * 4;
   const size_t fixed = frag + xs + red1 + 8 * 4 + 16 + 16 * 8 + 64 + 512;
-  int nst = (int)((222 * 1024 - fixed) / (L->stage + red1));
+  const int budget = half_sm ? 110 * 1024 : 222 * 1024;
+  int nst = (int)((budget - fixed) / (L->stage + red1));
   if (nst > 6) nst = 6;
   if (nst < 2) return set_error(FMOE_ERR_UNSUPPORTED, "qgemv: K %d, T %d exceed shared memory", K, a.T);
   const size_t red = (size_t)(nst + 1) * red1;
@@ -516,7 +556,7 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, Qg
   L->bar = (int)off;
   off += 2 * 8 * L->nst;
   L->bytes = (int)align_up(off, 128);
-  const int ub = a.out_kind == QG_OUT_F32_ADD ? 1 : a.nkc;
+  const int ub = (a.out_kind == QG_OUT_F32_ADD || a.out_kind == QG_OUT_F32_PART) ? 1 : a.nkc;
   const int nb = a.units / ub;
   L->grid = nb < kNumSMs ? nb : kNumSMs;
   return FMOE_OK;

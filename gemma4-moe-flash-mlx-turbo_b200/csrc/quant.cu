@@ -60,9 +60,10 @@ __global__ void quantize_kernel(const void* __restrict__ src, int src_is_bf16, i
 }
 
 // out[i, c] = bf16(fma(scale, q, bias)) of row ids[i] (or row i when ids is
-// null), optionally times bf16(row_scale).
+// null), optionally times bf16(row_scale).  An id outside [0, rows) yields a
+// zero row instead of a read outside the table.
 __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const bf16* __restrict__ sc,
-                                  const bf16* __restrict__ bi, int64_t cols, int bits, int group,
+                                  const bf16* __restrict__ bi, int64_t rows, int64_t cols, int bits, int group,
                                   const int32_t* __restrict__ ids, int64_t n, float row_scale, int apply_scale,
                                   bf16* __restrict__ out) {
   const int64_t gpr = cols / group, wpr = cols * bits / 32;
@@ -70,6 +71,10 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const bf16* _
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * cols; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
     const int64_t src = ids ? ids[r] : r;
+    if (src < 0 || src >= rows) {
+      out[i] = __float2bfloat16_rn(0.f);
+      continue;
+    }
     const float s = __bfloat162float(sc[src * gpr + c / group]), b = __bfloat162float(bi[src * gpr + c / group]);
     float v = round_bf(fmaf(s, (float)get_code(wq + src * wpr, c, bits), b));
     if (apply_scale) v = v * rs;
@@ -77,12 +82,14 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ wq, const bf16* _
   }
 }
 
-__global__ void gather_bf16_rows_kernel(const bf16* __restrict__ w, int64_t cols, const int32_t* __restrict__ ids,
-                                        int64_t n, float row_scale, int apply_scale, bf16* __restrict__ out) {
+__global__ void gather_bf16_rows_kernel(const bf16* __restrict__ w, int64_t rows, int64_t cols,
+                                        const int32_t* __restrict__ ids, int64_t n, float row_scale, int apply_scale,
+                                        bf16* __restrict__ out) {
   const float rs = round_bf(row_scale);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n * cols; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
-    float v = __bfloat162float(w[(int64_t)ids[r] * cols + c]);
+    const int64_t src = ids[r];
+    float v = src >= 0 && src < rows ? __bfloat162float(w[src * cols + c]) : 0.f;
     if (apply_scale) v = v * rs;
     out[i] = __float2bfloat16_rn(v);
   }
@@ -112,14 +119,14 @@ int launch_dequantize(const QW& w, int group, const int32_t* ids, int64_t n, flo
     if (!ids) return set_error(FMOE_ERR_INVALID, "dequantize: bf16 weight needs row ids");
     {
       ProfScope prof_("gather_bf16_rows_kernel", st);
-      gather_bf16_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const bf16*>(w.w), w.in, ids, n, row_scale,
-                                                              apply, out);
+      gather_bf16_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const bf16*>(w.w), w.out, w.in, ids, n,
+                                                              row_scale, apply, out);
     }
   } else {
     {
       ProfScope prof_("dequantize_kernel", st);
-      dequantize_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint32_t*>(w.w), w.s, w.b, w.in, w.bits,
-                                                        group, ids, n, row_scale, apply, out);
+      dequantize_kernel<<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint32_t*>(w.w), w.s, w.b, w.out, w.in,
+                                                        w.bits, group, ids, n, row_scale, apply, out);
     }
   }
   return check_launch("dequantize_kernel");

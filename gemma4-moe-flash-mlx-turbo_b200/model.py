@@ -1,0 +1,213 @@
+"""Gemma-4 decoder (decode step) over libfmoe: host-side mirror of src/model.
+
+    Gemma4DecoderLayer.forward(x, cache, pos)   DecoderLayer::forward_gemma4, src/model/mod.rs:67-119
+    Gemma4Model.decode_step(ids)                TextModel::forward + Model::forward, src/model/mod.rs:135-363
+                                                (embedding, 30 layers, final norm, tied lm_head, softcap)
+
+Each layer is one call into the library (fmoe_decoder_layer_forward: 11
+kernels chained on the stream); the whole step is capturable in one CUDA
+graph with the decode position kept on the device.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import (ExpertTable, ExpertsC, KvCacheC, QuantizedLinear, QWeightC, RouterC, _ptr, _stream, check, lib)
+from .kv import KV_AFFINE, KV_BF16, KVCache
+
+
+class DecoderLayerC(ctypes.Structure):
+    _fields_ = [
+        ("q_proj", QWeightC), ("k_proj", QWeightC), ("v_proj", QWeightC), ("o_proj", QWeightC),
+        ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p), ("input_norm", ctypes.c_void_p),
+        ("post_attn_norm", ctypes.c_void_p), ("pre_ff_norm", ctypes.c_void_p), ("post_ff_norm_1", ctypes.c_void_p),
+        ("pre_ff_norm_2", ctypes.c_void_p), ("post_ff_norm_2", ctypes.c_void_p), ("post_ff_norm", ctypes.c_void_p),
+        ("mlp_gate", QWeightC), ("mlp_up", QWeightC), ("mlp_down", QWeightC),
+        ("router", RouterC), ("experts", ExpertsC),
+        ("num_heads", ctypes.c_int32), ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+        ("rope_dims", ctypes.c_int32), ("k_eq_v", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float), ("layer_scalar", ctypes.c_float),
+        ("attn_scale", ctypes.c_float),
+    ]
+
+
+# Gemma-4 26B-A4B shapes (the reference's CLAUDE.md model notes): 30 layers,
+# every fifth one full attention (head_dim 512, 2 KV heads, K == V, theta 1e6)
+# and the rest sliding-window (head_dim 256, 8 KV heads, theta 1e4, window 1024).
+GEMMA4_26B = dict(hidden=2816, layers=30, heads=16, sliding_kv_heads=8, sliding_head_dim=256, full_kv_heads=2,
+                  full_head_dim=512, sliding_theta=1e4, full_theta=1e6, full_partial_rotary=0.25, window=1024,
+                  dense_inter=2112, experts=128, expert_inter=704, top_k=8, vocab=262144, eps=1e-6, softcap=30.0,
+                  attn_bits=8, dense_bits=4, embed_bits=6, router_bits=16, full_every=5)
+
+
+def layer_is_full(cfg, i):
+    return (i + 1) % cfg["full_every"] == 0
+
+
+class Gemma4DecoderLayer:
+    """Weights and hyper-parameters of one decoder layer (src/model/mod.rs:40-58,
+    gemma4_attention.rs:16-33, mlp.rs:28-33, moe.rs:298-312)."""
+
+    def __init__(self, q_proj, k_proj, v_proj, o_proj, q_norm, k_norm, norms, mlp, router, experts, num_heads,
+                 num_kv_heads, head_dim, rope_dims, rope_theta, k_eq_v, eps=1e-6, layer_scalar=1.0, attn_scale=1.0,
+                 top_k=8):
+        self.q_proj, self.k_proj, self.v_proj, self.o_proj = q_proj, k_proj, v_proj, o_proj
+        self.q_norm, self.k_norm = q_norm, k_norm
+        self.norms = norms  # dict: input, post_attn, pre_ff, post_ff_1, pre_ff_2, post_ff_2, post_ff
+        self.mlp = mlp      # (gate, up, down) QuantizedLinear
+        self.router = router  # dict: proj QuantizedLinear, router_scale, per_expert_scale, root_size
+        self.experts = experts
+        self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
+        self.rope_dims, self.rope_theta, self.k_eq_v = rope_dims, rope_theta, k_eq_v
+        self.eps, self.layer_scalar, self.attn_scale, self.top_k = eps, layer_scalar, attn_scale, top_k
+        self._c = None
+
+    def cstruct(self) -> DecoderLayerC:
+        if self._c is None:
+            n = self.norms
+            empty = QWeightC(None, None, None, 0, 0, 0, 0)
+            r = self.router
+            rc = RouterC(r["proj"].cstruct(), _ptr(r.get("router_scale")), _ptr(r.get("per_expert_scale")), None,
+                         r["root_size"], self.eps, 1, self.top_k)
+            self._c = DecoderLayerC(
+                self.q_proj.cstruct(), self.k_proj.cstruct(),
+                empty if self.k_eq_v else self.v_proj.cstruct(), self.o_proj.cstruct(),
+                _ptr(self.q_norm), _ptr(self.k_norm), _ptr(n["input"]), _ptr(n["post_attn"]), _ptr(n["pre_ff"]),
+                _ptr(n["post_ff_1"]), _ptr(n["pre_ff_2"]), _ptr(n["post_ff_2"]), _ptr(n["post_ff"]),
+                self.mlp[0].cstruct(), self.mlp[1].cstruct(), self.mlp[2].cstruct(), rc, self.experts.cstruct(),
+                self.num_heads, self.num_kv_heads, self.head_dim, self.rope_dims, int(self.k_eq_v), 0,
+                self.rope_theta, self.eps, self.layer_scalar, self.attn_scale)
+        return self._c
+
+    def workspace_bytes(self, T, cache: KVCache) -> int:
+        return lib().fmoe_decoder_workspace_bytes(T, ctypes.byref(self.cstruct()), ctypes.byref(cache.c))
+
+    def forward(self, x: torch.Tensor, cache: KVCache, pos: int, workspace: torch.Tensor, pos_dev=None):
+        """In place: x bf16 [T, hidden] (one token per sequence) -> the layer output."""
+        T = x.shape[0]
+        check(lib().fmoe_decoder_layer_forward(ctypes.byref(self.cstruct()), ctypes.byref(cache.c), _ptr(x), T, pos,
+                                               _ptr(pos_dev), _ptr(workspace), workspace.numel(), _stream()))
+        return x
+
+    __call__ = forward
+
+    @classmethod
+    def random(cls, cfg, full: bool, seed: int, device, experts=None):
+        g = torch.Generator(device=device).manual_seed(seed)
+        H = cfg["hidden"]
+        D = cfg["full_head_dim"] if full else cfg["sliding_head_dim"]
+        Hkv = cfg["full_kv_heads"] if full else cfg["sliding_kv_heads"]
+        Hq = cfg["heads"]
+
+        def qlin(out_f, in_f, bits, std=0.02):
+            w = torch.randn(out_f, in_f, generator=g, device=device) * std
+            return QuantizedLinear.from_float(w, bits)
+
+        def norm(n):
+            return (1.0 + 0.1 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16)
+
+        ab, db = cfg["attn_bits"], cfg["dense_bits"]
+        q = qlin(Hq * D, H, ab)
+        k = qlin(Hkv * D, H, ab)
+        v = None if full else qlin(Hkv * D, H, ab)
+        o = qlin(H, Hq * D, ab)
+        norms = {n: norm(H) for n in ("input", "post_attn", "pre_ff", "post_ff_1", "pre_ff_2", "post_ff_2",
+                                      "post_ff")}
+        mlp = (qlin(cfg["dense_inter"], H, db), qlin(cfg["dense_inter"], H, db), qlin(H, cfg["dense_inter"], db))
+        # O(1) router logits after the root_size scaling: unit-variance router weights
+        router = {"proj": qlin(cfg["experts"], H, cfg["router_bits"], std=1.0), "router_scale": norm(H),
+                  "per_expert_scale": norm(cfg["experts"]), "root_size": H ** -0.5}
+        if experts is None:
+            experts = ExpertTable.random(cfg["experts"], H, cfg["expert_inter"], seed=seed + 1, device=device)
+        rope_dims = int(D * cfg["full_partial_rotary"]) if full else D
+        theta = cfg["full_theta"] if full else cfg["sliding_theta"]
+        return cls(q, k, v, o, norm(D), norm(D), norms, mlp, router, experts, Hq, Hkv, D, rope_dims, theta, full,
+                   eps=cfg["eps"], layer_scalar=float(0.5 + torch.rand(1, generator=g, device=device).item()),
+                   attn_scale=1.0, top_k=cfg["top_k"])
+
+
+class Gemma4Model:
+    """Embedding (6-bit, scaled by sqrt(hidden)), decoder layers with their KV
+    caches, final norm and the tied 6-bit lm_head with softcap; greedy decode."""
+
+    def __init__(self, cfg, embed: QuantizedLinear, layers, final_norm, batch, max_positions, kv_mode=KV_BF16,
+                 device=None):
+        self.cfg = cfg
+        self.embed = embed
+        self.layers = layers
+        self.final_norm = final_norm
+        self.batch = batch
+        device = torch.device("cuda") if device is None else torch.device(device)
+        self.device = device
+        self.caches = []
+        for i, L in enumerate(layers):
+            win = None if L.k_eq_v else cfg["window"]
+            if kv_mode == KV_AFFINE:
+                c = KVCache.new_affine(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
+            else:
+                c = KVCache(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
+            self.caches.append(c)
+        ws = max(L.workspace_bytes(batch, c) for L, c in zip(layers, self.caches))
+        if ws == 0:
+            raise ValueError("decoder: unsupported layer / cache configuration")
+        self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)
+        self.lm_ws = torch.zeros(lib().fmoe_lm_head_workspace_bytes(batch) + 256, dtype=torch.uint8, device=device)
+        H, V = cfg["hidden"], embed.out_features
+        self.x = torch.zeros(batch, H, dtype=torch.bfloat16, device=device)
+        self.logits = torch.empty(batch, V, dtype=torch.float32, device=device)
+        self.ids = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.pos = 0
+        self.pos_dev = torch.zeros(2, dtype=torch.int64, device=device)  # {position, attended slots}
+        self._emb_scale = math.sqrt(H)
+        self._embed_c = embed.cstruct()
+
+    @classmethod
+    def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None):
+        n_layers = cfg["layers"] if n_layers is None else n_layers
+        layers = [Gemma4DecoderLayer.random(cfg, layer_is_full(cfg, i), seed + 100 * i, device)
+                  for i in range(n_layers)]
+        g = torch.Generator(device=device).manual_seed(seed + 7)
+        rows = []
+        # the [vocab, hidden] embedding in row blocks (bounded fp32 scratch)
+        V, H = cfg["vocab"], cfg["hidden"]
+        blk = 32768
+        wq = torch.empty(V, H * cfg["embed_bits"] // 32, dtype=torch.int32, device=device)
+        sc = torch.empty(V, H // 64, dtype=torch.bfloat16, device=device)
+        bi = torch.empty_like(sc)
+        from . import quantize
+        for r0 in range(0, V, blk):
+            w = torch.randn(min(blk, V - r0), H, generator=g, device=device) * 0.02
+            a, b_, c_ = quantize(w, cfg["embed_bits"])
+            wq[r0:r0 + w.shape[0]] = a
+            sc[r0:r0 + w.shape[0]] = b_
+            bi[r0:r0 + w.shape[0]] = c_
+            rows.append(None)
+        embed = QuantizedLinear(wq, sc, bi, cfg["embed_bits"], 64, in_features=H)
+        final_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
+        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device)
+
+    def set_position(self, pos: int):
+        self.pos = pos
+        n = min(pos + 1, 1 << 62)
+        self.pos_dev.copy_(torch.tensor([pos, n], dtype=torch.int64))
+
+    def decode_step(self, device_pos=False):
+        """One greedy decode step for every sequence: ids -> next ids (in self.ids).
+        device_pos=True reads / advances the position on the device (graph replay)."""
+        c = self._embed_c
+        check(lib().fmoe_embed_rows(ctypes.byref(c), _ptr(self.ids), self.batch, self._emb_scale, _ptr(self.x),
+                                    _stream()))
+        pd = self.pos_dev if device_pos else None
+        for L, cache in zip(self.layers, self.caches):
+            L.forward(self.x, cache, self.pos, self.ws, pd)
+        check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(self.x), self.batch,
+                                 self.cfg["softcap"], _ptr(self.logits), _ptr(self.ids), _ptr(pd), _ptr(self.lm_ws),
+                                 self.lm_ws.numel(), _stream()))
+        if not device_pos:
+            self.pos += 1
+            for cache in self.caches:
+                cache._offset = self.pos
+        return self.ids

@@ -266,6 +266,67 @@ int fmoe_attn_decode(const fmoe_kv_cache_t* cache, const void* q, int q_heads, i
 int fmoe_turbo_round_trip(const void* x, int64_t rows, int head_dim, int bits, void* out,
                           void* stream);
 
+/* ---- decoder layer + lm_head (decode step) ----------------------------- */
+
+/* One Gemma-4 decoder layer, DecoderLayer::forward_gemma4 (src/model/mod.rs:
+ * 67-119) with Gemma4Attention (src/model/gemma4_attention.rs:16-112), GeLUMLP
+ * (src/model/mlp.rs:28-41) and Gemma4MoeBlock (src/model/moe.rs:298-470).
+ * All bf16 norm weights are [hidden] except q_norm / k_norm ([head_dim]).
+ * The router's use_norm / root_size / router_scale / eps describe its input
+ * chain (rms_norm_no_scale, * root_size, * router_scale) as in fmoe_router. */
+typedef struct fmoe_decoder_layer {
+  fmoe_qweight_t q_proj, k_proj, v_proj, o_proj; /* v_proj unused when k_eq_v */
+  const void* q_norm;
+  const void* k_norm;
+  const void* input_norm;
+  const void* post_attn_norm;
+  const void* pre_ff_norm;
+  const void* post_ff_norm_1;
+  const void* pre_ff_norm_2;
+  const void* post_ff_norm_2;
+  const void* post_ff_norm;
+  fmoe_qweight_t mlp_gate, mlp_up, mlp_down; /* dense GeLU MLP */
+  fmoe_router_t router;
+  fmoe_experts_t experts;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t rope_dims;   /* rotated dims (non-traditional RoPE); head_dim * partial factor */
+  int32_t k_eq_v;      /* 1: V is the raw K projection (full-attention layers) */
+  int32_t reserved;
+  float rope_theta;
+  float eps;           /* rms_norm_eps of every norm */
+  float layer_scalar;
+  float attn_scale;    /* SDPA scale (1.0 in Gemma 4) */
+} fmoe_decoder_layer_t;
+
+/* One decode step of a layer for T = cache.batch sequences (1..8), one token
+ * each, at position pos: x bf16 [T, hidden] is the layer input and receives
+ * the layer output.  The new K/V rows go to slot pos % capacity of `cache`;
+ * attention covers min(pos + 1, capacity) slots.  pos_dev (optional) points to
+ * device int64 {pos, attended slots}, read instead of pos (CUDA-graph replay).
+ * Weights: q/k/v/o, dense MLP: 4/6/8-bit, group 64; router as fmoe_router;
+ * experts 4-bit.  Workspace: fmoe_decoder_workspace_bytes (the largest over
+ * the layers and caches used with it), zero-filled once before first use. */
+size_t fmoe_decoder_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer,
+                                    const fmoe_kv_cache_t* cache);
+int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache, void* x,
+                               int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Final norm + tied lm_head + logit softcap + greedy next token:
+ * TextModel::forward's norm (src/model/mod.rs:254), Model::forward
+ * (src/model/mod.rs:336-362): logits f32 [T, vocab] = tanh(l / softcap) *
+ * softcap with l = rms_norm(x, final_norm) . embed^T (softcap <= 0: none);
+ * next_ids int32 [T] = argmax (ties -> lowest id).  embed: the 4/6/8-bit
+ * embedding table [vocab, hidden].  pos_dev (optional): the decode position
+ * counters {pos, attended slots}, both advanced by one when the step ends.
+ * Workspace: fmoe_lm_head_workspace_bytes, zero-filled once. */
+size_t fmoe_lm_head_workspace_bytes(int64_t T);
+int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps, const void* x, int64_t T,
+                 float softcap, float* logits, int32_t* next_ids, int64_t* pos_dev, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
 /* Synchronises `stream` and reads the status word every workspace starts with:
  * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */

@@ -202,3 +202,103 @@ def attn_decode_bf16(q_bf16, Hkv, Tcap, t_lo, t_hi, k_bf16, v_bf16, scale, tau=0
                                _p(np.ascontiguousarray(v_bf16, np.uint16)), ctypes.c_float(scale), ctypes.c_float(tau),
                                _p(out))
     return out
+
+
+# ---------------------------------------------------------------------------
+# Decoder layer (config: Gemma-4 decode step), composed from the C pieces.
+
+
+def rms_norm(x_bf16, w_bf16=None, eps=1e-6):
+    """fast::rms_norm / RMSNormNoScale (src/model/norm.rs:11-29) over the last axis."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    n = x.shape[-1]
+    y = np.empty_like(x)
+    w = None if w_bf16 is None else np.ascontiguousarray(w_bf16, np.uint16)
+    lib().orc_rms_norm(_p(x), ctypes.c_int64(x.size // n), n, _p(w), ctypes.c_float(eps), _p(y))
+    return y
+
+
+def rope(x_bf16, dims, theta, pos):
+    """fast::rope (traditional=false), src/model/gemma4_attention.rs:74-81, over the last axis."""
+    x = np.ascontiguousarray(x_bf16, np.uint16)
+    D = x.shape[-1]
+    y = np.empty_like(x)
+    lib().orc_rope(_p(x), ctypes.c_int64(x.size // D), D, dims, ctypes.c_double(theta), ctypes.c_int64(pos), _p(y))
+    return y
+
+
+def _bf(x_f32):
+    return f32_to_bf16(np.asarray(x_f32, np.float32))
+
+
+def _f(x_bf16):
+    return bf16_to_f32(x_bf16)
+
+
+def _gelu(g):
+    g = g.astype(np.float64)
+    return 0.5 * g * (1.0 + np.tanh(0.7978845608028654 * (g + 0.044715 * g ** 3)))
+
+
+def _qlin(x_bf16, w):
+    """w = (wq uint32, scales, biases, in_features, bits) -> bf16 output (MLX qmm output dtype)."""
+    wq, s, b, in_f, bits = w
+    return _bf(qmatmul(x_bf16, wq, s, b, in_f, bits))
+
+
+def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
+    """One decode step of DecoderLayer::forward_gemma4 (src/model/mod.rs:67-119) for
+    T sequences (one token each) with a bf16 KV cache.
+
+    x: bf16 [T, H]; L: dict of weights (q/k/v/o/gate/up/down as _qlin tuples,
+    bf16 norms, router (wr, bits, scale, pes, root), experts (buf, stride, offsets));
+    cache_k / cache_v: bf16 [T, Hkv, cap, D], updated at slot pos % cap.
+    cfg: heads, kv_heads, head_dim, rope_dims, rope_theta, eps, k_eq_v, scalar,
+    attn_scale, top_k, hidden, inter_expert.  Returns (x_out bf16, q_rot bf16).
+    """
+    T, H = x.shape
+    Hq, Hkv, D, eps = cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"]
+    # attention block (gemma4_attention.rs:46-112)
+    xn = rms_norm(x, L["input_norm"], eps)
+    q = _qlin(xn, L["q"]).reshape(T, Hq, D)
+    k = _qlin(xn, L["k"]).reshape(T, Hkv, D)
+    v = k.copy() if cfg["k_eq_v"] else _qlin(xn, L["v"]).reshape(T, Hkv, D)
+    q = rope(rms_norm(q, L["q_norm"], eps), cfg["rope_dims"], cfg["rope_theta"], pos)
+    k = rope(rms_norm(k, L["k_norm"], eps), cfg["rope_dims"], cfg["rope_theta"], pos)
+    v = rms_norm(v, None, eps)
+    cap = cache_k.shape[2]
+    cache_k[:, :, pos % cap] = k
+    cache_v[:, :, pos % cap] = v
+    n = min(pos + 1, cap)
+    att = attn_decode_bf16(q, Hkv, cap, np.zeros(T, np.int32), np.full(T, n, np.int32), cache_k, cache_v,
+                           cfg["attn_scale"])
+    o = _qlin(_bf(att).reshape(T, Hq * D), L["o"])
+    h = _bf(_f(x) + _f(rms_norm(o, L["post_attn_norm"], eps)))
+    # feed-forward block: dense MLP + MoE in parallel (mod.rs:92-118)
+    h1 = rms_norm(h, L["pre_ff_norm"], eps)
+    h2 = rms_norm(h, L["pre_ff_norm_2"], eps)
+    g = _qlin(h1, L["gate"])
+    u = _qlin(h1, L["up"])
+    act = _bf(_gelu(_f(g)) * _f(u))
+    d = _qlin(act, L["down"])
+    wr, wr_bits, rscale, pes, root = L["router"]
+    ids, wts, logits = router(h2, wr, cfg["top_k"], wr_bits, use_norm=True, root_size=root, eps=eps,
+                              router_scale=rscale, per_expert_scale=pes)
+    cfg["_router_logits"] = logits
+    buf, stride, offs = L["experts"]
+    y, _ = moe_experts(h2, ids, wts, buf, stride, offs, H, cfg["inter_expert"])
+    moe = _bf(y)
+    s = _bf(_f(rms_norm(d, L["post_ff_norm_1"], eps)) + _f(rms_norm(moe, L["post_ff_norm_2"], eps)))
+    out = _bf(_f(h) + _f(rms_norm(s, L["post_ff_norm"], eps)))
+    sc = _f(_bf(np.float32([cfg["scalar"]])))[0]
+    return _bf(_f(out) * sc), q
+
+
+def lm_head(x, embed, final_norm, eps, softcap):
+    """Final norm + tied lm_head + softcap (mod.rs:254, 336-362) -> (logits f32, argmax ids)."""
+    xn = rms_norm(x, final_norm, eps)
+    wq, s, b, in_f, bits = embed
+    lg = _f(_bf(qmatmul(xn, wq, s, b, in_f, bits)))
+    if softcap > 0:
+        lg = _f(_bf(_f(_bf(np.tanh(_f(_bf(lg / np.float32(softcap))).astype(np.float64)))) * np.float32(softcap)))
+    return lg, np.argmax(lg, axis=1).astype(np.int32)

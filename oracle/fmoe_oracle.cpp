@@ -589,4 +589,49 @@ void orc_attn_decode_bf16(const uint16_t* q, int B, int Hq, int Hkv, int D, int6
     }
 }
 
+// ---------------------------------------------------------------------------
+// Decoder-layer pieces (config: Gemma-4 decode step).
+
+// fast::rms_norm (src/model/norm.rs:11-14) and RMSNormNoScale (norm.rs:17-29):
+// y = bf16(x * rsqrt(mean(x^2) + eps) * w) per row of n; w == NULL: no scale.
+// The mean and rsqrt are evaluated in double, the products in fp32.
+void orc_rms_norm(const uint16_t* x, int64_t rows, int n, const uint16_t* w, float eps, uint16_t* y) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * n;
+    double ss = 0;
+    for (int i = 0; i < n; ++i) {
+      const double v = bf2f(xr[i]);
+      ss += v * v;
+    }
+    const float rs = static_cast<float>(1.0 / std::sqrt(ss / n + static_cast<double>(eps)));
+    for (int i = 0; i < n; ++i) {
+      const float v = bf2f(xr[i]) * rs;
+      y[r * n + i] = f2bf(w ? v * bf2f(w[i]) : v);
+    }
+  }
+}
+
+// fast::rope as called at src/model/gemma4_attention.rs:74-81 (traditional =
+// false, scale 1, offset = cache position): for rows of D values, the first
+// `dims` rotate in pairs (i, i + dims/2) by angle pos * theta^(-2i/dims),
+// out = bf16(x1 cos - x2 sin), bf16(x1 sin + x2 cos); the rest pass through.
+// Angles and products in double.
+void orc_rope(const uint16_t* x, int64_t rows, int D, int dims, double theta, int64_t pos, uint16_t* y) {
+  const int half = dims / 2;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const uint16_t* xr = x + r * D;
+    uint16_t* yr = y + r * D;
+    for (int i = 0; i < D; ++i) yr[i] = xr[i];
+    for (int i = 0; i < half; ++i) {
+      const double ang = static_cast<double>(pos) * std::pow(theta, -2.0 * i / dims);
+      const double c = std::cos(ang), s = std::sin(ang);
+      const double a = bf2f(xr[i]), b = bf2f(xr[i + half]);
+      yr[i] = f2bf(static_cast<float>(a * c - b * s));
+      yr[i + half] = f2bf(static_cast<float>(a * s + b * c));
+    }
+  }
+}
+
 }  // extern "C"
