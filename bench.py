@@ -2,15 +2,23 @@
 """Benchmark of the B200 quantised-MoE hot path (one JSON line on rank 0).
 
 Workloads (synthetic data, random-init weights of the Gemma-4 26B-A4B shapes):
-  moe30_decode_b1   (default) the routed-expert path of the 30-layer decoder for
-                    one decode token: per layer the bf16 router [128, 2816]
-                    (softmax, top-8, renormalise) and 8 of 128 MLX-affine 4-bit
-                    experts (gate/up 2816->704, GELU-tanh gating, down
-                    704->2816, weighted combine).  Every layer has its own
-                    router and 128 experts (30 x 428 MB resident in HBM, far
-                    above L2, so no flush is needed).  The 30 layers are
-                    applied to the step's hidden state.
+  decode30_b1       (default) one greedy decode step of the whole 30-layer
+                    decoder for one sequence after a 2048-position context:
+                    6-bit embedding row, per layer 8-bit q/k/v/o projections
+                    with q/k/v norms, RoPE and a bf16 KV-cache append, decode
+                    attention (sliding window 1024 / full), the 4-bit dense
+                    MLP, the bf16 router and 8 of 128 4-bit experts, then the
+                    final norm, the tied 6-bit lm_head with softcap and argmax.
+                    The context is 2048 random bf16 K/V positions written into
+                    every layer's cache (the cost of a decode step depends on
+                    the context length, not on how it was produced).
+  moe30_decode_b1   the routed-expert path of the same decoder alone: per
+                    layer the bf16 router [128, 2816] (softmax, top-8,
+                    renormalise) and 8 of 128 MLX-affine 4-bit experts
+                    (gate/up 2816->704, GELU-tanh gating, down 704->2816,
+                    weighted combine), 30 layers.
   moe30_decode_b32  the same with 32 tokens per step.
+Weights resident in HBM (about 15 GB) are far above L2, so no flush is needed.
 A step is captured once in a CUDA graph and replayed.  `value` is tokens/s
 with inputs resident in HBM; `e2e` adds the pinned-host -> device copy of the
 step's input and the device -> host copy of its result inside the timed region.
@@ -35,7 +43,9 @@ H, I, E, K, LAYERS = 2816, 704, 128, 8, 30
 ROUTER_BYTES = E * H * 2                                   # bf16 router weight per layer
 GATE_UP_BYTES = 2 * (I * H // 2 + 2 * I * (H // 64) * 2)   # per selected expert: 2,230,272
 DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert: 1,115,136
-WORKLOADS = {"moe30_decode_b1": 1, "moe30_decode_b32": 32}
+WORKLOADS = {"decode30_b1": 1, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
+CTX = 2048                                                 # decode context (positions in every KV cache)
+EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES                  # 3,345,408
 
 
 def parse():
@@ -44,7 +54,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="moe30_decode_b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode30_b1", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
     ap.add_argument("--qlinear-case", default=None, metavar="OUT:IN:BITS:T",
@@ -164,6 +174,180 @@ class MoeStack:
                                             self.ws.data_ptr(), self.ws.numel(), s)
             if rc:
                 self.fm.check(rc)
+
+
+def qlin_bytes(q):
+    return q.weight.numel() * q.weight.element_size() + (q.scales.numel() + q.biases.numel()) * 2
+
+
+def decoder_step_bytes(m, T, ctx):
+    """Algorithmic bytes of one decode step: every weight byte the step needs
+    once (the experts the step routes to: 8 distinct per token at T = 1), the
+    KV positions attended plus the appended one, and the embedding row."""
+    per = {"attention": 0, "dense": 0, "router": 0, "experts": 0, "kv": 0, "lm_head": 0}
+    for L, c in zip(m.layers, m.caches):
+        per["attention"] += sum(qlin_bytes(q) for q in (L.q_proj, L.k_proj, L.o_proj))
+        if not L.k_eq_v:
+            per["attention"] += qlin_bytes(L.v_proj)
+        per["dense"] += sum(qlin_bytes(q) for q in L.mlp)
+        w = L.router["proj"].weight
+        per["router"] += w.numel() * w.element_size()
+        per["experts"] += min(T * K, E) * EXPERT_BYTES
+        n = min(ctx + 1, c.capacity)
+        per["kv"] += T * L.num_kv_heads * L.head_dim * 2 * 2 * (n + 1)
+    per["lm_head"] = qlin_bytes(m.embed) + T * qlin_bytes(m.embed) // m.embed.out_features
+    return sum(per.values()), per
+
+
+def run_decoder(args, rank, world, local):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    fm.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    T = WORKLOADS[args.workload]
+    cfg = dict(fm.GEMMA4_26B)
+    m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000 + rank, device=dev,
+                              n_layers=args.layers)
+    g = torch.Generator(device=dev).manual_seed(4100 + rank)
+    for L, c in zip(m.layers, m.caches):
+        chunk = 256
+        for p0 in range(0, CTX, chunk):
+            kv = torch.randn(2, T, L.num_kv_heads, chunk, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+            c.update(kv[0], kv[1])
+    ids0 = torch.randint(0, cfg["vocab"], (T,), generator=g, device=dev, dtype=torch.int32)
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+
+    # per-kernel device times of eager steps (profiling on)
+    with torch.cuda.stream(stream):
+        m.ids.copy_(ids0)
+        m.set_position(CTX)
+        m.decode_step()
+        torch.cuda.synchronize()
+        fm.profile_read(reset=True)
+        fm.profile_enable(True)
+        nprof = 3
+        for _ in range(nprof):
+            m.decode_step()
+        torch.cuda.synchronize()
+        fm.profile_enable(False)
+    prof = fm.profile_read(reset=True)
+    launches_per_step = sum(v[0] for v in prof.values()) // nprof
+
+    # one step in a CUDA graph; the position lives on the device and advances per replay
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        m.ids.copy_(ids0)
+        m.set_position(CTX)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            m.decode_step(device_pos=True)
+
+    def timed(n, e2e, host_in=None, host_out=None):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            m.ids.copy_(ids0)
+            m.set_position(CTX)
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(n):
+                if e2e:
+                    m.ids.copy_(host_in[i % host_in.shape[0]], non_blocking=True)
+                graph.replay()
+                if e2e:
+                    host_out[i % host_out.shape[0]].copy_(m.ids, non_blocking=True)
+            stop.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(stop)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(args.warmup, False)
+    clocks = ClockSampler(local)
+    with clocks:
+        ms = timed(args.steps, False)
+    host_in = torch.randint(0, cfg["vocab"], (64, T), dtype=torch.int32).pin_memory()
+    host_out = torch.empty(64, T, dtype=torch.int32).pin_memory()
+    timed(min(args.warmup, 3), True, host_in, host_out)
+    ms_e2e = timed(args.steps, True, host_in, host_out)
+    assert int(m.pos_dev[0]) == CTX + args.steps
+
+    ms_step = ms / args.steps
+    value = world * T / (ms_step / 1e3)
+    e2e_value = world * T / (ms_e2e / args.steps / 1e3)
+    peaks, peaks_kind = load_peaks()
+    step_bytes, parts = decoder_step_bytes(m, T, CTX)
+    step_gbs = step_bytes / (ms_step / 1e3) / 1e9
+
+    # roofline of the dominant kernel (most device time per step)
+    name, (n_l, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+    by_kernel = {"qgemv_kernel<8>": parts["attention"], "qgemv_kernel<4>": parts["dense"],
+                 "qgemv_kernel<6>": parts["lm_head"], "attn_bf16_kernel": parts["kv"],
+                 "moe_gate_up_kernel": parts["experts"] * 2 / 3, "moe_down_kernel": parts["experts"] / 3}
+    alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
+    achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
+    result = {
+        "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (random-init weights MLX-affine quantised; random token ids; 2048 random bf16 K/V "
+                "positions per cache)",
+        "config": {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
+                   "batch": T, "context": CTX, "kv_cache": "bf16", "attention_bits": 8, "expert_bits": 4,
+                   "dense_bits": 4, "embed_bits": 6, "router": "bf16",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "weights (about 15 GB) far larger than L2; no flush",
+                   "graph": "one CUDA graph per step, position on the device"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * 4,
+                "d2h_bytes_per_step": T * 4,
+                "api": "Gemma4Model.decode_step (embedding, fmoe_decoder_layer_forward x30, fmoe_lm_head) "
+                       "captured in a CUDA graph + pinned host copies of the token ids"},
+        "gpu_launches": launches_per_step * args.steps,
+        "step_alg_bytes": int(step_bytes),
+        "step_alg_bytes_parts": {k: int(v) for k, v in parts.items()},
+        "step_hbm_gbs": round(step_gbs, 1),
+        "step_roofline_frac": round(step_gbs / peaks["hbm_gbs"], 4),
+        "roofline": {"bound": "hbm", "kernel": name,
+                     "achieved": round(achieved, 1) if achieved else None,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4) if achieved else None,
+                     "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json hbm_gbs)" if peaks_kind == "measured"
+                     else "fallback 6.65 TB/s",
+                     "alg_bytes_per_launch": int(alg) if alg else None,
+                     "avg_launch_us": round(tot_ms / n_l * 1e3, 3), "traffic": None},
+        "kernels": {k: {"launches_per_step": v[0] // nprof, "avg_us": round(v[1] / v[0] * 1e3, 3),
+                        "us_per_step": round(v[1] / nprof * 1e3, 1)}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
+        "clocks": clocks.summary(),
+    }
+    del graph
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_decoder_baseline(T)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 def run_ours(args, rank, world, local):
@@ -432,11 +616,119 @@ def cpu_baseline(_layers, T, budget_s=10.0):
                       f"accumulation), extrapolated to {LAYERS} layers"}
 
 
+def cpu_decoder_sample(seed=4000):
+    """Numpy weights for the oracle's decoder layer (one sliding, one full) and
+    the 6-bit lm_head at the model's shapes.  The CPU time does not depend on
+    the code values, so uniform random codes with small bf16 scales stand in."""
+    import numpy as np
+    import oracle
+    rng = np.random.default_rng(seed)
+
+    def ql(out_f, in_f, bits):
+        wq = rng.integers(0, 2 ** 32, size=(out_f, in_f * bits // 32), dtype=np.uint32)
+        sc = oracle.f32_to_bf16((0.001 + 0.0001 * rng.standard_normal((out_f, in_f // 64))).astype(np.float32))
+        bi = oracle.f32_to_bf16(np.full((out_f, in_f // 64), -0.01, np.float32))
+        return (wq, sc, bi, in_f, bits)
+
+    def nrm(n):
+        return oracle.f32_to_bf16((1 + 0.1 * rng.standard_normal(n)).astype(np.float32))
+
+    offs, sizes, stride = ecb(H, I)
+    experts = (rng.integers(0, 256, size=E * stride, dtype=np.uint8), stride, offs)
+    layers = []
+    for full in (False, True):
+        Hq, Hkv, D = 16, (2 if full else 8), (512 if full else 256)
+        L = {"q": ql(Hq * D, H, 8), "k": ql(Hkv * D, H, 8), "v": None if full else ql(Hkv * D, H, 8),
+             "o": ql(H, Hq * D, 8), "q_norm": nrm(D), "k_norm": nrm(D),
+             "gate": ql(2112, H, 4), "up": ql(2112, H, 4), "down": ql(H, 2112, 4),
+             "router": (oracle.f32_to_bf16(rng.standard_normal((E, H)).astype(np.float32)), 16, nrm(H), nrm(E),
+                        H ** -0.5),
+             "experts": experts}
+        for k in ("input_norm", "post_attn_norm", "pre_ff_norm", "post_ff_norm_1", "pre_ff_norm_2",
+                  "post_ff_norm_2", "post_ff_norm"):
+            L[k] = nrm(H)
+        cap = CTX + 16 if full else 1024
+        ck = oracle.f32_to_bf16(rng.standard_normal((1, Hkv, cap, D)).astype(np.float32))
+        cfg = {"heads": Hq, "kv_heads": Hkv, "head_dim": D, "rope_dims": 128 if full else 256,
+               "rope_theta": 1e6 if full else 1e4, "eps": 1e-6, "k_eq_v": full, "scalar": 1.0, "attn_scale": 1.0,
+               "top_k": K, "hidden": H, "inter_expert": I}
+        layers.append((L, ck, ck.copy(), cfg))
+    embed = ql(262144, H, 6)
+    x = oracle.f32_to_bf16(rng.standard_normal((1, H)).astype(np.float32))
+    return layers, embed, nrm(H), x
+
+
+def cpu_decoder_times(sample, n_sliding):
+    """(sliding layer s, full layer s, lm_head s) on the oracle: n_sliding
+    sliding layers averaged, one full layer and one lm_head."""
+    import oracle
+    layers, embed, fnorm, x = sample
+    (Ls, ks, vs, cs), (Lf, kf, vf, cf) = layers
+    oracle.decoder_layer(x, Ls, ks, vs, CTX, cs)  # warm
+    t0 = time.perf_counter()
+    for _ in range(n_sliding):
+        oracle.decoder_layer(x, Ls, ks, vs, CTX, cs)
+    t_s = (time.perf_counter() - t0) / n_sliding
+    t0 = time.perf_counter()
+    oracle.decoder_layer(x, Lf, kf, vf, CTX, cf)
+    t_f = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    oracle.lm_head(x, embed, fnorm, 1e-6, 30.0)
+    t_lm = time.perf_counter() - t0
+    return t_s, t_f, t_lm
+
+
+def cpu_decoder_step_s(t_s, t_f, t_lm, layers=LAYERS):
+    n_full = layers // 5
+    return (layers - n_full) * t_s + n_full * t_f + t_lm
+
+
+def cpu_decoder_baseline(T, budget_s=15.0):
+    import oracle
+    sample = cpu_decoder_sample()
+    t0 = time.perf_counter()
+    t_s, t_f, t_lm = cpu_decoder_times(sample, 2)
+    n = max(2, int((budget_s - (time.perf_counter() - t0)) / max(t_s, 1e-3)))
+    t_s, t_f, t_lm = cpu_decoder_times(sample, n)
+    step = cpu_decoder_step_s(t_s, t_f, t_lm)
+    return {"value": round(T / step, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{n} sliding layers + 1 full layer + 1 lm_head of one decode token at context {CTX} on the "
+                      f"oracle (C++ OpenMP / numpy); step = 24 sliding + 6 full + lm_head "
+                      f"({t_s * 1e3:.1f} / {t_f * 1e3:.1f} / {t_lm * 1e3:.1f} ms)"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
     import oracle
     T = WORKLOADS[args.workload]
+    if args.workload.startswith("decode30"):
+        sample = cpu_decoder_sample()
+        cpu_decoder_times(sample, 1)
+        for _ in range(args.warmup):
+            cpu_decoder_times(sample, 1)
+        t_s, t_f, t_lm = cpu_decoder_times(sample, args.steps)
+        step = cpu_decoder_step_s(t_s, t_f, t_lm)
+        value = T / step
+        desc = (f"each step = one sliding decoder layer of one token at context {CTX} on the oracle; one full layer "
+                f"and one lm_head timed once; decode step = 24 sliding + 6 full + lm_head")
+        out = {
+            "impl": "reference",
+            "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
+            "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32/fp64 accumulate (CPU)",
+            "data": "synthetic (seeded)",
+            "config": {"workload": args.workload, "layers": LAYERS, "batch": T, "context": CTX},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference (Rust + MLX/Metal) cannot run here; this is the repository's C++/numpy port of "
+                    "its path (oracle/)",
+        }
+        print(json.dumps(out), flush=True)
+        return
     x, wr, buf, offs, stride = cpu_sample_setup(T)
     for _ in range(args.warmup):
         cpu_layer(x, wr, buf, offs, stride)
@@ -511,6 +803,8 @@ def main():
         run_qlinear_case(args)
     elif args.impl == "reference":
         run_reference(args, rank, world)
+    elif args.workload.startswith("decode30"):
+        run_decoder(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 
