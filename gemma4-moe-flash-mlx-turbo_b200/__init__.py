@@ -147,6 +147,9 @@ SIGNATURES = {
     "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),
     "fmoe_lm_head_workspace_bytes": (_SZ, [_I64]),
     "fmoe_lm_head": (_I, [ctypes.POINTER(QWeightC), _P, _F, _P, _I64, _F, _P, _P, _P, _P, _SZ, _P]),
+    "fmoe_decode_step_workspace_bytes": (_SZ, [_P]),
+    "fmoe_decode_step_prepare": (_I, [_P, _P, _SZ]),
+    "fmoe_decode_step": (_I, [_P, _P, _P, _P, _P, _SZ, _P]),
 }
 
 _lib_handle = None

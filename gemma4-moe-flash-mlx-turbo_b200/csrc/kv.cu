@@ -31,6 +31,7 @@
 #include "internal.h"
 #include "common.cuh"
 #include "stage.cuh"
+#include "rowops.cuh"
 
 namespace fmoe {
 
@@ -92,32 +93,6 @@ __device__ __forceinline__ void warp_fwht(float (&v)[P], int lane) {
       v[j] = upper ? __fsub_rn(o, v[j]) : __fadd_rn(v[j], o);
     }
   }
-}
-
-template <int P>
-__device__ __forceinline__ void load_row_f32(const bf16* row, int lane, float (&v)[P]) {
-  const uint4* p = reinterpret_cast<const uint4*>(row + lane * P);
-#pragma unroll
-  for (int i = 0; i < P / 8; ++i) {
-    const uint4 w = p[i];
-    v[8 * i + 0] = bf16lo(w.x);
-    v[8 * i + 1] = bf16hi(w.x);
-    v[8 * i + 2] = bf16lo(w.y);
-    v[8 * i + 3] = bf16hi(w.y);
-    v[8 * i + 4] = bf16lo(w.z);
-    v[8 * i + 5] = bf16hi(w.z);
-    v[8 * i + 6] = bf16lo(w.w);
-    v[8 * i + 7] = bf16hi(w.w);
-  }
-}
-
-template <int P>
-__device__ __forceinline__ void store_row_bf16(bf16* row, int lane, const float (&v)[P]) {
-  uint4* p = reinterpret_cast<uint4*>(row + lane * P);
-#pragma unroll
-  for (int i = 0; i < P / 8; ++i)
-    p[i] = make_uint4(pack_bf16x2(v[8 * i], v[8 * i + 1]), pack_bf16x2(v[8 * i + 2], v[8 * i + 3]),
-                      pack_bf16x2(v[8 * i + 4], v[8 * i + 5]), pack_bf16x2(v[8 * i + 6], v[8 * i + 7]));
 }
 
 // MLX-affine quantisation of the warp's D values in groups of 64 (64/P lanes
@@ -256,42 +231,6 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 // every tensor rounded to bf16 as the reference's bf16 arrays are.  RoPE is
 // MLX fast::rope, non-traditional: the first rope_dims dims rotate in pairs
 // (i, i + rope_dims/2) by angle pos * inv_freq[i].
-
-template <int P>
-__device__ __forceinline__ void warp_rms_norm(float (&v)[P], const bf16* w, float eps, int lane) {
-  constexpr int D = 32 * P;
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < P; ++i) ss = fmaf(v[i], v[i], ss);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float r = rsqrtf(ss / (float)D + eps);
-#pragma unroll
-  for (int i = 0; i < P; ++i) v[i] = round_bf(w ? v[i] * r * bf2f(w[lane * P + i]) : v[i] * r);
-}
-
-template <int P>
-__device__ __forceinline__ void warp_rope(float (&v)[P], int rope_dims, float log2_theta, float pos, int lane) {
-  const int half = rope_dims / 2;
-  const int ofs = half / P;  // partner lane distance (half is a multiple of P)
-  float o[P];
-#pragma unroll
-  for (int i = 0; i < P; ++i) {
-    const float up = __shfl_down_sync(0xffffffffu, v[i], ofs & 31);
-    const float dn = __shfl_up_sync(0xffffffffu, v[i], ofs & 31);
-    const int e = lane * P + i;
-    o[i] = v[i];
-    if (e < rope_dims) {
-      // inv_freq_j = theta^(-2j / rope_dims), j = e mod half
-      const int j = e < half ? e : e - half;
-      float sn, cs;
-      sincosf(pos * exp2f(-(float)(2 * j) / (float)rope_dims * log2_theta), &sn, &cs);
-      o[i] = e < half ? round_bf(v[i] * cs - up * sn) : round_bf(dn * sn + v[i] * cs);
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < P; ++i) v[i] = o[i];
-}
 
 template <int P>
 __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __restrict__ qkv, int ld, int Hq,

@@ -4,9 +4,12 @@
     Gemma4Model.decode_step(ids)                TextModel::forward + Model::forward, src/model/mod.rs:135-363
                                                 (embedding, 30 layers, final norm, tied lm_head, softcap)
 
-Each layer is one call into the library (fmoe_decoder_layer_forward: 11
-kernels chained on the stream); the whole step is capturable in one CUDA
-graph with the decode position kept on the device.
+Two execution paths, both capturable in one CUDA graph with the decode
+position kept on the device:
+  decode_step        one library call per layer (fmoe_decoder_layer_forward:
+                     11 kernels chained on the stream), any batch 1..8;
+  decode_step_fused  the whole step as one persistent kernel
+                     (fmoe_decode_step), batch 1.
 """
 from __future__ import annotations
 
@@ -31,6 +34,15 @@ class DecoderLayerC(ctypes.Structure):
         ("rope_dims", ctypes.c_int32), ("k_eq_v", ctypes.c_int32), ("reserved", ctypes.c_int32),
         ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float), ("layer_scalar", ctypes.c_float),
         ("attn_scale", ctypes.c_float),
+    ]
+
+
+class DecodeModelC(ctypes.Structure):
+    _fields_ = [
+        ("n_layers", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("layers", ctypes.POINTER(DecoderLayerC)), ("caches", ctypes.POINTER(KvCacheC)),
+        ("embed", QWeightC), ("final_norm", ctypes.c_void_p),
+        ("eps", ctypes.c_float), ("softcap", ctypes.c_float), ("embed_scale", ctypes.c_float),
     ]
 
 
@@ -163,6 +175,7 @@ class Gemma4Model:
         self.pos_dev = torch.zeros(2, dtype=torch.int64, device=device)  # {position, attended slots}
         self._emb_scale = math.sqrt(H)
         self._embed_c = embed.cstruct()
+        self._fc = None
 
     @classmethod
     def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None):
@@ -188,6 +201,39 @@ class Gemma4Model:
         embed = QuantizedLinear(wq, sc, bi, cfg["embed_bits"], 64, in_features=H)
         final_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
         return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device)
+
+    def _fused(self):
+        if self._fc is None:
+            if self.batch != 1:
+                raise ValueError("decode_step_fused: batch 1 only")
+            n = len(self.layers)
+            lay = (DecoderLayerC * n)(*[L.cstruct() for L in self.layers])
+            cac = (KvCacheC * n)(*[c.c for c in self.caches])
+            mc = DecodeModelC(n, 0, lay, cac, self._embed_c, _ptr(self.final_norm), self.cfg["eps"],
+                              self.cfg["softcap"], self._emb_scale)
+            nbytes = lib().fmoe_decode_step_workspace_bytes(ctypes.byref(mc))
+            if nbytes == 0:
+                check(lib().fmoe_decode_step_prepare(ctypes.byref(mc), None, 0))
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            check(lib().fmoe_decode_step_prepare(ctypes.byref(mc), _ptr(ws), nbytes))
+            self._fc = (mc, lay, cac, ws)
+        return self._fc
+
+    def decode_step_fused(self):
+        """One greedy decode step (batch 1) as a single persistent kernel:
+        ids -> next ids (in self.ids); the position advances on the device
+        (pos_dev) and on the host."""
+        mc, _, _, ws = self._fused()
+        check(lib().fmoe_decode_step(ctypes.byref(mc), _ptr(self.ids), _ptr(self.logits), _ptr(self.pos_dev), _ptr(ws),
+                                     ws.numel(), _stream()))
+        self.pos += 1
+        for cache in self.caches:
+            cache._offset = self.pos
+        return self.ids
+
+    def fused_status(self, clear: bool = False) -> int:
+        """Status word of the fused step's workspace (0: ok; synchronises)."""
+        return lib().fmoe_workspace_status(_ptr(self._fused()[3]), int(clear), _stream())
 
     def set_position(self, pos: int):
         self.pos = pos

@@ -327,6 +327,42 @@ int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps,
                  float softcap, float* logits, int32_t* next_ids, int64_t* pos_dev, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/* ---- whole decode step (batch 1) ----------------------------------------
+ * One persistent kernel per generated token: embedding row, every decoder
+ * layer (as fmoe_decoder_layer_forward), final norm, tied lm_head, softcap and
+ * greedy argmax — Model::forward for one sequence and one token
+ * (src/model/mod.rs:145-160, 67-119, 254, 336-362; the per-layer eval
+ * barriers of mod.rs:214,244 and moe.rs:356 disappear).  Requirements: bf16
+ * KV caches of batch 1; q/k/v/o 8-bit, dense MLP and experts 4-bit, embedding
+ * 6-bit (all group 64), bf16 router with use_norm; layers share the hidden,
+ * MLP and expert shapes. */
+typedef struct fmoe_decode_model {
+  int32_t n_layers;
+  int32_t reserved;
+  const fmoe_decoder_layer_t* layers; /* host array [n_layers] */
+  const fmoe_kv_cache_t* caches;      /* host array [n_layers] */
+  fmoe_qweight_t embed;               /* tied embedding / lm_head [vocab, hidden] */
+  const void* final_norm;             /* bf16 [hidden] */
+  float eps;                          /* final norm eps */
+  float softcap;                      /* logit softcap (<= 0: none) */
+  float embed_scale;                  /* sqrt(hidden) */
+} fmoe_decode_model_t;
+
+/* Workspace bytes (0: unsupported model).  fmoe_decode_step_prepare writes the
+ * device copy of the model description into the workspace (synchronous; call
+ * again whenever a weight or cache pointer changes). */
+size_t fmoe_decode_step_workspace_bytes(const fmoe_decode_model_t* model);
+int fmoe_decode_step_prepare(const fmoe_decode_model_t* model, void* workspace, size_t workspace_bytes);
+
+/* One step: tokens int32 [1] holds the current token and receives the next
+ * one; logits f32 [vocab] (after softcap); pos_dev int64 {position, attended
+ * slots} is read for the KV slot / context length and advanced by one.  The
+ * launch is capturable in a CUDA graph (a memset node + a cooperative kernel
+ * node).  Device-side waits are bounded: a lost dependency ends the step with
+ * FMOE_ERR_TIMEOUT in the workspace status word (fmoe_workspace_status). */
+int fmoe_decode_step(const fmoe_decode_model_t* model, int32_t* tokens, float* logits, int64_t* pos_dev,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
 /* Synchronises `stream` and reads the status word every workspace starts with:
  * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
