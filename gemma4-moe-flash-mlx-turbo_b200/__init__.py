@@ -147,6 +147,11 @@ SIGNATURES = {
     "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),
     "fmoe_lm_head_workspace_bytes": (_SZ, [_I64]),
     "fmoe_lm_head": (_I, [ctypes.POINTER(QWeightC), _P, _F, _P, _I64, _F, _P, _P, _P, _P, _SZ, _P]),
+    "fmoe_moe_prefill_prepare_bytes": (_SZ, [ctypes.POINTER(ExpertsC)]),
+    "fmoe_moe_prefill_prepare": (_I, [ctypes.POINTER(ExpertsC), _P, _SZ, _P]),
+    "fmoe_moe_prefill_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC)]),
+    "fmoe_moe_prefill": (_I, [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P, _P, _SZ,
+                              _P]),
     "fmoe_decode_step_workspace_bytes": (_SZ, [_P]),
     "fmoe_decode_step_prepare": (_I, [_P, _P, _SZ]),
     "fmoe_decode_step": (_I, [_P, _P, _P, _P, _P, _SZ, _P]),
@@ -420,11 +425,54 @@ class Gemma4MoeBlock:
                                 _stream()))
         return ids, w, lg
 
+    # Tokens above which forward() takes the tensor-core prefill path (the
+    # decode GEMV path serves at most 128 tokens per call).
+    PREFILL_MIN_TOKENS = 129
+
+    def _prepared(self, device):
+        """Transposed scale / bias copy of the expert table for the prefill GEMMs
+        (built once per table)."""
+        prep = getattr(self.experts, "_prefill_prep", None)
+        if prep is None:
+            e = self.experts.cstruct()
+            nbytes = lib().fmoe_moe_prefill_prepare_bytes(ctypes.byref(e))
+            if nbytes == 0:
+                check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), None, 0, None))
+            prep = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), _ptr(prep), nbytes, _stream()))
+            self.experts._prefill_prep = prep
+        return prep
+
+    def forward_prefill(self, x: torch.Tensor, return_routing=False):
+        """Router + experts over many tokens on the tcgen05 grouped-GEMM path
+        (fmoe_moe_prefill): token-sorted expert tiles, fp32 accumulation."""
+        _need_cuda(x)
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        T = x2.shape[0]
+        y = torch.empty_like(x2)
+        ids = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)
+        r = self.router_cstruct()
+        e = self.experts.cstruct()
+        prep = self._prepared(x.device)
+        nbytes = lib().fmoe_moe_prefill_workspace_bytes(T, ctypes.byref(r), ctypes.byref(e))
+        if nbytes == 0:
+            check(lib().fmoe_moe_prefill(None, T, ctypes.byref(r), ctypes.byref(e), None, None, None, None, None, 0,
+                                         None))
+        buf = self._ws.get(nbytes, x.device)
+        check(lib().fmoe_moe_prefill(_ptr(x2), T, ctypes.byref(r), ctypes.byref(e), _ptr(prep), _ptr(y), _ptr(ids),
+                                     _ptr(w), _ptr(buf), buf.numel(), _stream()))
+        y = y.reshape(shape)
+        return (y, ids, w) if return_routing else y
+
     def forward(self, x: torch.Tensor, return_routing=False):
         _need_cuda(x)
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
         T = x2.shape[0]
+        if T >= self.PREFILL_MIN_TOKENS:
+            return self.forward_prefill(x, return_routing)
         y = torch.empty_like(x2)
         ids = torch.empty(T, self.top_k, dtype=torch.int32, device=x.device)
         w = torch.empty(T, self.top_k, dtype=torch.float32, device=x.device)

@@ -327,6 +327,24 @@ int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps,
                  float softcap, float* logits, int32_t* next_ids, int64_t* pos_dev, void* workspace,
                  size_t workspace_bytes, void* stream);
 
+/* ---- prefill MoE block (many tokens) -------------------------------------
+ * Gemma4MoeBlock::forward (src/model/moe.rs:315-470) for T tokens on the
+ * tcgen05 tensor cores: router + top-k as fmoe_moe_block_forward, then grouped
+ * 4-bit x bf16 GEMMs over token-sorted expert tiles (gate|up with GELU-tanh
+ * gating, down) with fp32 accumulation, and the weighted top-k combine in slot
+ * order.  Each expert output is rounded to bf16 before the combine, as the
+ * reference's per-expert quantized_matmul output is (moe.rs:438-465).
+ * Requirements: hidden a multiple of 256, intermediate a multiple of 64, the
+ * whole expert table (first_expert 0), 16-byte aligned tensors.
+ * fmoe_moe_prefill_prepare writes a transposed copy of the table's scales and
+ * biases ([group][row], fmoe_moe_prefill_prepare_bytes; once per table). */
+size_t fmoe_moe_prefill_prepare_bytes(const fmoe_experts_t* experts);
+int fmoe_moe_prefill_prepare(const fmoe_experts_t* experts, void* prepared, size_t prepared_bytes, void* stream);
+size_t fmoe_moe_prefill_workspace_bytes(int64_t T, const fmoe_router_t* router, const fmoe_experts_t* experts);
+int fmoe_moe_prefill(const void* x, int64_t T, const fmoe_router_t* router, const fmoe_experts_t* experts,
+                     const void* prepared, void* y, int32_t* ids, float* weights, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
 /* ---- whole decode step (batch 1) ----------------------------------------
  * One persistent kernel per generated token: embedding row, every decoder
  * layer (as fmoe_decoder_layer_forward), final norm, tied lm_head, softcap and
