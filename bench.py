@@ -63,6 +63,10 @@ def parse():
     ap.add_argument("--attn-case", default=None, metavar="MODE:B:T",
                     help="run only one decode-attention case (mode affine|bf16, batch, context): four launches, "
                          "L2 flushed before each, the last one timed (a small case for profilers)")
+    ap.add_argument("--prefill-case", type=int, default=None, metavar="T",
+                    help="run only the prefill MoE block (BASELINE config 2: T tokens, Zipf-skewed routing) on the "
+                         "tcgen05 path: four calls, L2 flushed before each, the last one timed (a small case for "
+                         "profilers)")
     ap.add_argument("--layers", type=int, default=30,
                     help="decoder layers in the step (30 = the model; fewer only for small profiling cases)")
     return ap.parse_args()
@@ -794,10 +798,52 @@ def run_qlinear_case(args):
                       "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
 
 
+def prefill_setup(fm, torch, dev, seed=2002):
+    """BASELINE config 2's layer: 128 MLX-affine 4-bit experts, bf16 router
+    N(0, 0.02), per-expert logit bias N(0, 1) (Zipf-like load skew)."""
+    table = fm.ExpertTable.random(E, H, I, seed=seed, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(E, generator=g, device=dev)
+    return fm.Gemma4MoeBlock(fm.QuantizedLinear(wr, bits=16), table, top_k=K, logit_bias=bias), g
+
+
+def prefill_time(fm, torch, dev, block, g, T, iters):
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    y, ids, w = block.forward_prefill(x, return_routing=True)
+    uniq = int(torch.unique(ids).numel())
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    times = []
+    for i in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        block.forward_prefill(x)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return times, uniq
+
+
+def run_prefill_case(args):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    block, g = prefill_setup(fm, torch, dev)
+    times, uniq = prefill_time(fm, torch, dev, block, g, args.prefill_case, 4)
+    print(json.dumps({"prefill_case": args.prefill_case, "us": round(times[-1], 1), "unique_experts": uniq}),
+          flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
-    if args.attn_case:
+    if args.prefill_case:
+        run_prefill_case(args)
+    elif args.attn_case:
         run_attn_case(args)
     elif args.qlinear_case:
         run_qlinear_case(args)

@@ -10,16 +10,19 @@
 //   GEMM2    Y_sorted = act . Wd_e^T                                 per expert tile
 //   combine  y[t] = sum over the token's k slots of w * Y_sorted[row]  (slot order)
 //
-// GEMM kernel (persistent, one CTA per SM, 10 warps):
+// GEMM kernel (persistent, one CTA per SM, 14 warps):
 //   warp 0   producer: TMA tiles of A (128 sorted rows x 64 K, bf16, 128-byte
 //            swizzle) and of the packed 4-bit weights (3-D tensor map over the
 //            expert table), 1-D bulk copies of the step's scale / bias rows
-//   warp 1   MMA issuer: 4 x tcgen05.mma (M 128, N 256, K 16) per K tile into
+//   warp 1   MMA issuer: per K tile, 2 x 4 tcgen05.mma (K 16) with the
+//            dequantised weights as the M operand (two 128-row halves: gate
+//            and up rows, or 256 down rows) and the tile's tokens as N (their
+//            count rounded up to 16, so a lightly used expert wastes little);
 //            one of two TMEM accumulators; tcgen05.commit releases the stage
-//   warps 2-5  dequantise the weight tile into the canonical K-major
+//   warps 2-9  dequantise the weight tile into the canonical K-major
 //            128-byte-swizzled bf16 layout: w = bf16(fma(s, q, b)) per element
-//   warps 6-9  epilogue: tcgen05.ld of the accumulator, GELU gating (GEMM1) or
-//            plain bf16 store (GEMM2)
+//   warps 10-13  epilogue: tcgen05.ld of the accumulator (lane = weight row,
+//            column = token), GELU gating (GEMM1) or plain bf16 store (GEMM2)
 // Within every 8-element word of K the columns are stored in the order
 // 0 4 1 5 2 6 3 7: a 4-bit word's nibbles j and j+4 then form one bf16 pair
 // with a single AND/OR, so weights dequantise two at a time.  The gather
@@ -38,30 +41,38 @@
 namespace fmoe {
 namespace pf {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int NS = 3;
-constexpr int A_BYTES = BM * BK * 2;   // 16 KB
-constexpr int WB_BYTES = BN * BK * 2;  // 32 KB
-constexpr int WQ_BYTES = BN * BK / 2;  // 8 KB
-constexpr int SC_BYTES = 1024;         // scale | bias of 256 rows
-constexpr int OFF_A = 0, OFF_WB = A_BYTES, OFF_WQ = OFF_WB + WB_BYTES, OFF_SC = OFF_WQ + WQ_BYTES;
-constexpr int STAGE = OFF_SC + SC_BYTES;  // 57 KB, a multiple of 1024
-constexpr int OFF_BAR = NS * STAGE;
-constexpr int SMEM = OFF_BAR + 256 + 1024;  // + alignment slack for the 1024-byte swizzle atoms
-constexpr int THREADS = 320;
-constexpr int TMEM_COLS = 512;              // two 256-column fp32 accumulators
-static_assert(STAGE % 1024 == 0, "stage alignment");
+constexpr int BM = 64;                 // tokens per tile (the MMA's N, rounded up to 16)
+constexpr int BN = 256, BK = 64;       // weight rows per item (two 128-row halves), K per tile
+constexpr int NS = 6;                  // token-tile stages (shared memory, TMA)
+constexpr int NT = 3;                  // dequantised weight stages (TMEM)
+constexpr int NQ = 3;                  // packed-weight stages, KQ K tiles each
+constexpr int KQ = 4;                  // K tiles per packed-weight stage (128 bytes of 4-bit codes per row)
+constexpr int X_BYTES = BM * BK * 2;   // 8 KB
+constexpr int WQ_BYTES = BN * BK * KQ / 2;  // 32 KB: 256 rows x 128 bytes, 128-byte swizzle
+constexpr int SC_BYTES = 2 * BN * KQ * 2;   // 4 KB: scale and bias of 256 rows x KQ groups
+constexpr int WQS = WQ_BYTES + SC_BYTES;    // one packed-weight stage (codes, then scales)
+constexpr int OFF_WQ = NS * X_BYTES;
+constexpr int OFF_BAR = OFF_WQ + NQ * WQS;
+constexpr int SMEM = OFF_BAR + 512 + 1024;  // + alignment slack for the 1024-byte swizzle atoms
+constexpr int NDQ = 8;                      // dequantising warps (one weight row per thread)
+constexpr int THREADS = (2 + NDQ + 4) * 32;
+// TMEM columns: accumulators [2 buffers][2 halves][BM tokens] fp32, then the
+// dequantised weights [NT stages][2 halves][BK / 2] (two bf16 per column).
+constexpr int TMEM_COLS = 512;
+constexpr int TM_ACC = 0, TM_W = 2 * 2 * BM;
+static_assert(TM_W + NT * 2 * (BK / 2) <= TMEM_COLS, "TMEM budget");
+static_assert(X_BYTES % 1024 == 0 && OFF_WQ % 1024 == 0 && WQS % 1024 == 0, "stage alignment");
 
 struct alignas(64) Maps {
   CUtensorMap a;   // A rows (bf16 [P][K], 128-byte swizzle, box 64 x 128)
-  CUtensorMap w0;  // packed weights (u8 [E][rows][K/2], box 32 x 128 (GEMM1) / 256 (GEMM2) x 1)
+  CUtensorMap w0;  // packed weights (u8 [E][rows][K/2], 128-byte swizzle, box 128 x 128 (GEMM1) / 256 (GEMM2) x 1)
   CUtensorMap w1;  // GEMM1: the up projection
 };
 
 struct Args {
   const int4* tiles;     // (expert, first sorted row, rows, 0)
   const int* ntiles;
-  const bf16* prep;      // transposed scales / biases, expert stride eps elements
+  const bf16* prep;      // scales / biases as [group / 4][row][4] per array, expert stride eps elements
   int64_t eps;
   int64_t off_s0, off_b0, off_s1, off_b1;  // element offsets of this GEMM's arrays in an expert's block
   int H, I, E;
@@ -114,15 +125,29 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor, kind::f16: D f32, A / B bf16 K-major, M 128, N 256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor, kind::f16: D f32, A / B bf16 K-major, M 128, N = n.
+__device__ __forceinline__ uint32_t idesc_n(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
 
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t acc) {
+// D (TMEM) += A (TMEM, K-major: row = lane, two bf16 per column) . B (shared memory descriptor)^T
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
@@ -149,11 +174,14 @@ template <int MODE>  // 0: gate|up + GELU gating, 1: down
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ Maps maps, const Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* deqd = full + NS;
-  uint64_t* mmad = deqd + NS;
-  uint64_t* accf = mmad + NS;
-  uint64_t* acce = accf + 2;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // token tile landed
+  uint64_t* xfree = xfull + NS;                                     // MMAs done with it
+  uint64_t* wqf = xfree + NS;                                       // packed weights + scales landed
+  uint64_t* wqe = wqf + NQ;                                         // dequantisers done with them
+  uint64_t* tdq = wqe + NQ;                                         // dequantised weights in TMEM
+  uint64_t* tmm = tdq + NT;                                         // MMAs done with them
+  uint64_t* accf = tmm + NT;                                        // accumulator complete
+  uint64_t* acce = accf + 2;                                        // accumulator read out
   volatile int* failed = reinterpret_cast<volatile int*>(acce + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2) + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -162,9 +190,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const int NK = K / BK;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&deqd[s], 4);
-      mbar_init(&mmad[s], 1);
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xfree[s], 1);
+    }
+    for (int s = 0; s < NQ; ++s) {
+      mbar_init(&wqf[s], 1);
+      mbar_init(&wqe[s], NDQ);
+    }
+    for (int s = 0; s < NT; ++s) {
+      mbar_init(&tdq[s], NDQ);
+      mbar_init(&tmm[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&accf[s], 1);
@@ -173,7 +208,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     *failed = 0;
     mbar_fence_init();
   }
-  if (warp == 1) {  // the whole warp allocates the accumulators
+  if (warp == 1) {  // the whole warp allocates the accumulators and weight stages
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -186,164 +221,184 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   const int nitems = __ldg(a.ntiles) * NJ;
 
   if (warp == 0) {
-    // ---- producer
+    // ---- producer: token tiles (one per K tile) and packed-weight stages (one per KQ K tiles)
     if (lane == 0) {
-      int q = 0;
+      int q = 0, qq = 0;
       for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
         const int4 tl = __ldg(a.tiles + it / NJ);
         const int j = it % NJ, e = tl.x, row0 = tl.y;
         const int rows_ok = MODE == 0 ? min(128, a.I - j * 128) : BN;
         const bf16* pe = a.prep + (int64_t)e * a.eps;
         for (int kt = 0; kt < NK; ++kt, ++q) {
-          const int s = q % NS;
-          if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 301);
-          if (*failed) break;
-          uint8_t* st = smem + s * STAGE;
-          const int sc_bytes = MODE == 0 ? 4 * rows_ok * 2 : 2 * BN * 2;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(A_BYTES + WQ_BYTES + sc_bytes));
-          tma2d(st + OFF_A, &maps.a, kt * BK, row0, &full[s]);
-          if (MODE == 0) {
-            tma3d(st + OFF_WQ, &maps.w0, kt * 32, j * 128, e, &full[s]);
-            tma3d(st + OFF_WQ + WQ_BYTES / 2, &maps.w1, kt * 32, j * 128, e, &full[s]);
-            const int64_t r = (int64_t)kt * a.I + j * 128;
-            bulk_g2s(st + OFF_SC, pe + a.off_s0 + r, rows_ok * 2, &full[s]);
-            bulk_g2s(st + OFF_SC + 256, pe + a.off_b0 + r, rows_ok * 2, &full[s]);
-            bulk_g2s(st + OFF_SC + 512, pe + a.off_s1 + r, rows_ok * 2, &full[s]);
-            bulk_g2s(st + OFF_SC + 768, pe + a.off_b1 + r, rows_ok * 2, &full[s]);
-          } else {
-            tma3d(st + OFF_WQ, &maps.w0, kt * 32, j * BN, e, &full[s]);
-            const int64_t r = (int64_t)kt * a.H + j * BN;
-            bulk_g2s(st + OFF_SC, pe + a.off_s0 + r, BN * 2, &full[s]);
-            bulk_g2s(st + OFF_SC + 512, pe + a.off_b0 + r, BN * 2, &full[s]);
+          if (kt % KQ == 0) {
+            const int sq = qq % NQ;
+            if (qq >= NQ) pwait(&wqe[sq], (uint32_t)((qq / NQ) - 1) & 1u, failed, a.status, 306);
+            if (*failed) break;
+            uint8_t* wq = smem + OFF_WQ + sq * WQS;
+            uint8_t* sc = wq + WQ_BYTES;
+            const int gb = kt / KQ;  // group block: KQ groups, one per K tile
+            if (MODE == 0) {
+              mbar_arrive_expect_tx(&wqf[sq], (uint32_t)(WQ_BYTES + 4 * rows_ok * KQ * 2));
+              tma3d(wq, &maps.w0, kt * 32, j * 128, e, &wqf[sq]);
+              tma3d(wq + WQ_BYTES / 2, &maps.w1, kt * 32, j * 128, e, &wqf[sq]);
+              const int64_t r = ((int64_t)gb * a.I + j * 128) * KQ;
+              bulk_g2s(sc, pe + a.off_s0 + r, rows_ok * KQ * 2, &wqf[sq]);
+              bulk_g2s(sc + 1024, pe + a.off_b0 + r, rows_ok * KQ * 2, &wqf[sq]);
+              bulk_g2s(sc + 2048, pe + a.off_s1 + r, rows_ok * KQ * 2, &wqf[sq]);
+              bulk_g2s(sc + 3072, pe + a.off_b1 + r, rows_ok * KQ * 2, &wqf[sq]);
+            } else {
+              mbar_arrive_expect_tx(&wqf[sq], (uint32_t)(WQ_BYTES + 2 * BN * KQ * 2));
+              tma3d(wq, &maps.w0, kt * 32, j * BN, e, &wqf[sq]);
+              const int64_t r = ((int64_t)gb * a.H + j * BN) * KQ;
+              bulk_g2s(sc, pe + a.off_s0 + r, BN * KQ * 2, &wqf[sq]);
+              bulk_g2s(sc + 2048, pe + a.off_b0 + r, BN * KQ * 2, &wqf[sq]);
+            }
+            ++qq;
           }
+          const int s = q % NS;
+          if (q >= NS) pwait(&xfree[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 301);
+          if (*failed) break;
+          mbar_arrive_expect_tx(&xfull[s], (uint32_t)X_BYTES);
+          tma2d(smem + s * X_BYTES, &maps.a, kt * BK, row0, &xfull[s]);
         }
         if (*failed) break;
       }
       // every copy issued lands before the CTA ends
-      for (int k = q - NS < 0 ? 0 : q - NS; k < q; ++k) drain_wait(&full[k % NS], (uint32_t)(k / NS) & 1u);
+      for (int k = q - NS < 0 ? 0 : q - NS; k < q; ++k) drain_wait(&xfull[k % NS], (uint32_t)(k / NS) & 1u);
+      for (int k = qq - NQ < 0 ? 0 : qq - NQ; k < qq; ++k) drain_wait(&wqf[k % NQ], (uint32_t)(k / NQ) & 1u);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer
+    // ---- MMA issuer: weights (TMEM) as the M operand, the tile's tokens (shared memory) as N
     if (lane == 0) {
       int q = 0, n = 0;
       for (int it = blockIdx.x; it < nitems; it += gridDim.x, ++n) {
         const int ab = n & 1;
+        const int ntok = __ldg(a.tiles + it / NJ).z;
+        const uint32_t idesc = idesc_n((ntok + 15) & ~15);
         if (n >= 2) pwait(&acce[ab], (uint32_t)((n / 2) - 1) & 1u, failed, a.status, 302);
         tc_fence_after();
-        const uint32_t d = tmem + ab * BN;
         for (int kt = 0; kt < NK; ++kt, ++q) {
-          const int s = q % NS;
-          pwait(&deqd[s], (uint32_t)(q / NS) & 1u, failed, a.status, 303);
+          const int s = q % NS, t = q % NT;
+          pwait(&xfull[s], (uint32_t)(q / NS) & 1u, failed, a.status, 303);
+          pwait(&tdq[t], (uint32_t)(q / NT) & 1u, failed, a.status, 308);
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + s * STAGE + OFF_A), sb = smem_u32(smem + s * STAGE + OFF_WB);
+          const uint32_t sx = smem_u32(smem + s * X_BYTES);
           if (!*failed) {
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) mma_bf16(d, sw128_desc(sa + 32 * k), sw128_desc(sb + 32 * k), (kt | k) != 0);
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_ts(tmem + TM_ACC + ab * 2 * BM + h * BM, tmem + TM_W + t * BK + h * (BK / 2) + k * 8,
+                       sw128_desc(sx + 32 * k), idesc, (kt | k) != 0);
           }
-          mma_commit(&mmad[s]);
+          mma_commit(&xfree[s]);
+          mma_commit(&tmm[t]);
         }
         mma_commit(&accf[ab]);
       }
       if (n > 0) drain_wait(&accf[(n - 1) & 1], (uint32_t)((n - 1) / 2) & 1u);  // the last MMAs are done
     }
-  } else if (warp < 6) {
-    // ---- dequantisers: rows dt and dt + 128 of every weight tile
-    const int dt = threadIdx.x - 64;
-    int q = 0;
+  } else if (warp < 2 + NDQ) {
+    // ---- dequantisers: warp w writes TMEM lanes 32 * (w % 4) .. of half (w - 2) / 4;
+    // thread = one weight row of the 256-row tile, 64 bf16 per K tile = 32 TMEM columns
+    const int qw = warp & 3, h = (warp - 2) >> 2;
+    const int rr = h * 128 + qw * 32 + lane;
+    int q = 0, qq = 0;
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int j = it % NJ;
       for (int kt = 0; kt < NK; ++kt, ++q) {
-        const int s = q % NS;
-        pwait(&full[s], (uint32_t)(q / NS) & 1u, failed, a.status, 304);
-        uint8_t* st = smem + s * STAGE;
-        const bf16* sc = reinterpret_cast<const bf16*>(st + OFF_SC);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int rr = dt + 128 * h;
-          bool ok;
-          float sv, bv;
-          if (MODE == 0) {
-            ok = j * 128 + (rr & 127) < a.I;
-            sv = ok ? bf2f(sc[h * 256 + (rr & 127)]) : 0.f;
-            bv = ok ? bf2f(sc[h * 256 + 128 + (rr & 127)]) : 0.f;
-          } else {
-            ok = true;
-            sv = bf2f(sc[rr]);
-            bv = bf2f(sc[BN + rr]);
-          }
-          const uint4 w0 = *reinterpret_cast<const uint4*>(st + OFF_WQ + rr * 32);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(st + OFF_WQ + rr * 32 + 16);
-          const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-          const __nv_bfloat162 s2 = __floats2bfloat162_rn(sv, sv), b2 = __floats2bfloat162_rn(bv, bv);
-          const __nv_bfloat162 off = __floats2bfloat162_rn(128.f, 128.f);
-          uint8_t* wrow = st + OFF_WB + rr * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint32_t o[4];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              // nibbles jj and jj+4 of the word -> bf16 (128 + q) pair -> q -> fma(q, s, b)
-              const uint32_t v = and_or(ww[c] >> (4 * jj), 0x000F000Fu, 0x43004300u);
-              __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v), off);
-              __nv_bfloat162 r = __hfma2(qv, s2, b2);
-              o[jj] = ok ? *reinterpret_cast<uint32_t*>(&r) : 0u;
-            }
-            *reinterpret_cast<uint4*>(wrow + ((c ^ (rr & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
+        const int sq = qq % NQ, t = q % NT;
+        if (kt % KQ == 0) pwait(&wqf[sq], (uint32_t)(qq / NQ) & 1u, failed, a.status, 307);
+        if (q >= NT) pwait(&tmm[t], (uint32_t)((q / NT) - 1) & 1u, failed, a.status, 304);
+        const uint8_t* wq = smem + OFF_WQ + sq * WQS;
+        const bf16* sc = reinterpret_cast<const bf16*>(wq + WQ_BYTES);
+        const int kq = kt % KQ, c0 = 2 * kq;  // this K tile's two 16-byte chunks of a 128-byte row
+        bool ok;
+        float sv, bv;
+        if (MODE == 0) {
+          ok = j * 128 + (rr & 127) < a.I;
+          sv = ok ? bf2f(sc[h * 1024 + (rr & 127) * KQ + kq]) : 0.f;
+          bv = ok ? bf2f(sc[h * 1024 + 512 + (rr & 127) * KQ + kq]) : 0.f;
+        } else {
+          ok = true;
+          sv = bf2f(sc[rr * KQ + kq]);
+          bv = bf2f(sc[BN * KQ + rr * KQ + kq]);
         }
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor-core reads
+        // 128-byte-swizzled rows: chunk c of row r sits at chunk c ^ (r % 8)
+        const uint4 w0 = *reinterpret_cast<const uint4*>(wq + rr * 128 + ((c0 ^ (rr & 7)) << 4));
+        const uint4 w1 = *reinterpret_cast<const uint4*>(wq + rr * 128 + (((c0 + 1) ^ (rr & 7)) << 4));
+        const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const __nv_bfloat162 s2 = __floats2bfloat162_rn(sv, sv), b2 = __floats2bfloat162_rn(bv, bv);
+        const __nv_bfloat162 off = __floats2bfloat162_rn(128.f, 128.f);
+        uint32_t o[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            // nibbles jj and jj+4 of the word -> bf16 (128 + q) pair -> q -> fma(q, s, b)
+            const uint32_t v = and_or(ww[c] >> (4 * jj), 0x000F000Fu, 0x43004300u);
+            __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v), off);
+            __nv_bfloat162 r = __hfma2(qv, s2, b2);
+            o[4 * c + jj] = ok ? *reinterpret_cast<uint32_t*>(&r) : 0u;
+          }
+        tmem_st32(tmem + ((uint32_t)(qw * 32) << 16) + TM_W + t * BK + h * (BK / 2), o);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&deqd[s]);
+        if (lane == 0) {
+          mbar_arrive(&tdq[t]);
+          if (kt % KQ == KQ - 1 || kt == NK - 1) mbar_arrive(&wqe[sq]);
+        }
+        if (kt % KQ == KQ - 1 || kt == NK - 1) ++qq;
       }
     }
   } else {
-    // ---- epilogue: TMEM lanes 32 * (warp % 4) ..
-    const int qw = warp & 3, row = qw * 32 + lane;
+    // ---- epilogue: TMEM lane = weight row (feature) 32 * (warp % 4) + lane, column = token
+    const int qw = warp & 3, fr = qw * 32 + lane;
     int n = 0;
     for (int it = blockIdx.x; it < nitems; it += gridDim.x, ++n) {
       const int4 tl = __ldg(a.tiles + it / NJ);
-      const int j = it % NJ, row0 = tl.y, nrows = tl.z;
+      const int j = it % NJ, row0 = tl.y, nrows = tl.z, nc = (nrows + 15) / 16;
       const int ab = n & 1;
       pwait(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 305);
       tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * BN;
-      const bool live = row < nrows && !*failed;
+      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + TM_ACC + ab * 2 * BM;
+      const bool ok = !*failed;
       if (MODE == 0) {
+        const int f = j * 128 + fr;  // intermediate index of this lane's gate / up rows
+        // act is stored in the permuted word order: element 8w + jj + 4h at position 8w + 2jj + h
+        const int pos = (f & ~7) | ((f & 3) << 1) | ((f >> 2) & 1);
 #pragma unroll 1
-        for (int cc = 0; cc < 8; ++cc) {
+        for (int cc = 0; cc < nc; ++cc) {
           float g[16], u[16];
           tmem_ld16(ta + cc * 16, g);
-          tmem_ld16(ta + 128 + cc * 16, u);
+          tmem_ld16(ta + BM + cc * 16, u);
           tmem_ld_wait();
-          const int col0 = j * 128 + cc * 16;
-          if (live && col0 < a.I) {
-            float act[16];
+          if (ok && f < a.I) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) act[i] = gelu_tanh(round_bf(g[i])) * round_bf(u[i]);
-            // store in the permuted word order: position 8w + 2jj + h holds element 8w + jj + 4h
-            uint32_t o[8];
-#pragma unroll
-            for (int w = 0; w < 2; ++w)
-#pragma unroll
-              for (int jj = 0; jj < 4; ++jj) o[4 * w + jj] = bf2(act[8 * w + jj], act[8 * w + jj + 4]);
-            uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)(row0 + row) * a.I + col0);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+            for (int i = 0; i < 16; ++i) {
+              const int tok = cc * 16 + i;
+              if (tok < nrows)
+                a.out[(int64_t)(row0 + tok) * a.I + pos] = __float2bfloat16_rn(gelu_tanh(round_bf(g[i])) * round_bf(u[i]));
+            }
           }
         }
       } else {
 #pragma unroll 1
-        for (int cc = 0; cc < BN / 16; ++cc) {
-          float v[16];
-          tmem_ld16(ta + cc * 16, v);
-          tmem_ld_wait();
-          if (live) {
-            uint32_t o[8];
+        for (int hh = 0; hh < 2; ++hh) {
+          const int f = j * BN + hh * 128 + fr;
+#pragma unroll 1
+          for (int cc = 0; cc < nc; ++cc) {
+            float v[16];
+            tmem_ld16(ta + hh * BM + cc * 16, v);
+            tmem_ld_wait();
+            if (ok) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = bf2(v[2 * i], v[2 * i + 1]);
-            uint4* dst = reinterpret_cast<uint4*>(a.out + (int64_t)(row0 + row) * a.H + j * BN + cc * 16);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+              for (int i = 0; i < 16; ++i) {
+                const int tok = cc * 16 + i;
+                if (tok < nrows) a.out[(int64_t)(row0 + tok) * a.H + f] = __float2bfloat16_rn(v[i]);
+              }
+            }
           }
         }
       }
@@ -362,12 +417,17 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 // ---------------------------------------------------------------------------
 // small kernels
 
-// Transposed scale / bias copy of every expert: [gs | gb | us | ub] as
-// [G1][I], then [ds | db] as [G2][H] (bf16), expert stride eps elements.
+// Scale / bias copy of every expert laid out per K super-tile: for each array
+// (gate s, gate b, up s, up b over [I] rows; down s, down b over [H] rows),
+// [ceil(G / 4)][rows][4] bf16, groups past G zero.  One super-tile's 4 groups
+// of a row block are then one contiguous run.
+__device__ __forceinline__ int64_t prep_q1(const ExpertsDev& ex) { return (ex.H / 64 + 3) / 4; }
+__device__ __forceinline__ int64_t prep_q2(const ExpertsDev& ex) { return (ex.I / 64 + 3) / 4; }
 __global__ void prep_kernel(ExpertsDev ex, bf16* __restrict__ prep, int64_t eps) {
   const int e = blockIdx.y;
   const uint8_t* base = ex.base + (int64_t)e * ex.stride;
   const int G1 = ex.H / 64, G2 = ex.I / 64;
+  const int64_t Q1 = prep_q1(ex), Q2 = prep_q2(ex);
   bf16* pe = prep + (int64_t)e * eps;
   const int n1 = ex.I, n2 = ex.H;
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n1 + n2; r += gridDim.x * blockDim.x) {
@@ -375,27 +435,41 @@ __global__ void prep_kernel(ExpertsDev ex, bf16* __restrict__ prep, int64_t eps)
       const int arr[4] = {1, 2, 4, 5};
       for (int t = 0; t < 4; ++t) {
         const bf16* src = reinterpret_cast<const bf16*>(base + ex.off[arr[t]]) + (int64_t)r * G1;
-        for (int g = 0; g < G1; ++g) pe[(int64_t)t * G1 * n1 + (int64_t)g * n1 + r] = src[g];
+        bf16* dst = pe + (int64_t)t * Q1 * n1 * 4;
+        for (int g = 0; g < (int)Q1 * 4; ++g)
+          dst[((int64_t)(g / 4) * n1 + r) * 4 + g % 4] = g < G1 ? src[g] : __float2bfloat16_rn(0.f);
       }
     } else {
       const int rr = r - n1;
       for (int t = 0; t < 2; ++t) {
         const bf16* src = reinterpret_cast<const bf16*>(base + ex.off[7 + t]) + (int64_t)rr * G2;
-        for (int g = 0; g < G2; ++g) pe[4LL * G1 * n1 + (int64_t)t * G2 * n2 + (int64_t)g * n2 + rr] = src[g];
+        bf16* dst = pe + 4 * Q1 * n1 * 4 + (int64_t)t * Q2 * n2 * 4;
+        for (int g = 0; g < (int)Q2 * 4; ++g)
+          dst[((int64_t)(g / 4) * n2 + rr) * 4 + g % 4] = g < G2 ? src[g] : __float2bfloat16_rn(0.f);
       }
     }
   }
 }
 
-// Tile list: per expert with n > 0 pairs, ceil(n / 128) tiles of sorted rows.
+// Tile list: per expert with n > 0 pairs, ceil(n / 128) tiles of sorted rows
+// (one warp: lane l takes experts l, l + 32, ...; a prefix over lanes).
 __global__ void tiles_kernel(const int32_t* __restrict__ start, int E, int4* __restrict__ tiles, int* __restrict__ ntiles) {
-  if (threadIdx.x != 0) return;
-  int n = 0;
-  for (int e = 0; e < E; ++e) {
-    const int r0 = start[e], r1 = start[e + 1];
-    for (int r = r0; r < r1; r += BM) tiles[n++] = make_int4(e, r, min(BM, r1 - r), 0);
+  const int lane = threadIdx.x;
+  int base = 0;
+  for (int e0 = 0; e0 < E; e0 += 32) {
+    const int e = e0 + lane;
+    const int r0 = e < E ? start[e] : 0, r1 = e < E ? start[e + 1] : 0;
+    const int n = (r1 - r0 + BM - 1) / BM;
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    for (int t = 0; t < n; ++t) tiles[base + incl - n + t] = make_int4(e, r0 + t * BM, min(BM, r1 - r0 - t * BM), 0);
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
-  *ntiles = n;
+  if (lane == 0) *ntiles = base;
 }
 
 // X_sorted[i] = x[pairs[i] / k] with each 8-column word in the order 0 4 1 5 2 6 3 7;
@@ -446,7 +520,9 @@ __global__ void combine_kernel(const bf16* __restrict__ Y, const int32_t* __rest
 
 namespace {
 
-int64_t prep_eps(const ExpertsDev& d) { return 4LL * (d.H / 64) * d.I + 2LL * (d.I / 64) * d.H; }
+int64_t prep_q1h(const ExpertsDev& d) { return (d.H / 64 + 3) / 4; }
+int64_t prep_q2h(const ExpertsDev& d) { return (d.I / 64 + 3) / 4; }
+int64_t prep_eps(const ExpertsDev& d) { return 4 * (4 * prep_q1h(d) * d.I) + 2 * (4 * prep_q2h(d) * d.H); }
 
 // The driver's tensor-map encoder, resolved through the runtime (the library
 // does not link the driver library, so it loads on machines without one).
@@ -599,33 +675,33 @@ extern "C" int fmoe_moe_prefill(const void* x, int64_t T, const fmoe_router_t* r
   pf::Maps m1, m2;
   {
     const cuuint64_t dA[2] = {(cuuint64_t)d.H, (cuuint64_t)P}, sA[1] = {(cuuint64_t)d.H * 2};
-    const cuuint32_t bA[2] = {64, 128};
+    const cuuint32_t bA[2] = {64, (cuuint32_t)pf::BM};
     const cuuint64_t dW[3] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.I, (cuuint64_t)d.E};
     const cuuint64_t sW[2] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.stride};
-    const cuuint32_t bW[3] = {32, 128, 1};
+    const cuuint32_t bW[3] = {128, 128, 1};
     if ((rc = encode(&m1.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.xs, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
-        (rc = encode(&m1.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[0], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_NONE,
+        (rc = encode(&m1.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[0], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
                      "gate")) ||
-        (rc = encode(&m1.w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[3], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_NONE,
+        (rc = encode(&m1.w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[3], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
                      "up")))
       return rc;
     const cuuint64_t dA2[2] = {(cuuint64_t)d.I, (cuuint64_t)P}, sA2[1] = {(cuuint64_t)d.I * 2};
     const cuuint64_t dW2[3] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.H, (cuuint64_t)d.E};
     const cuuint64_t sW2[2] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.stride};
-    const cuuint32_t bW2[3] = {32, (cuuint32_t)pf::BN, 1};
+    const cuuint32_t bW2[3] = {128, (cuuint32_t)pf::BN, 1};
     if ((rc = encode(&m2.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.act, dA2, sA2, bA, CU_TENSOR_MAP_SWIZZLE_128B,
                      "act")) ||
         (rc = encode(&m2.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[6], dW2, sW2, bW2,
-                     CU_TENSOR_MAP_SWIZZLE_NONE, "down")))
+                     CU_TENSOR_MAP_SWIZZLE_128B, "down")))
       return rc;
     m2.w1 = m2.w0;
   }
-  const int G1 = d.H / 64, G2 = d.I / 64;
-  pf::Args a1{w.tiles, w.ntiles, static_cast<const bf16*>(prep), prep_eps(d), 0, (int64_t)G1 * d.I,
-              2LL * G1 * d.I, 3LL * G1 * d.I, d.H, d.I, d.E, w.act, w.h.status};
+  const int64_t A1 = 4 * prep_q1h(d) * d.I, A2 = 4 * prep_q2h(d) * d.H;  // elements per array
+  pf::Args a1{w.tiles, w.ntiles, static_cast<const bf16*>(prep), prep_eps(d), 0, A1, 2 * A1, 3 * A1,
+              d.H, d.I, d.E, w.act, w.h.status};
   pf::Args a2 = a1;
-  a2.off_s0 = 4LL * G1 * d.I;
-  a2.off_b0 = 4LL * G1 * d.I + (int64_t)G2 * d.H;
+  a2.off_s0 = 4 * A1;
+  a2.off_b0 = 4 * A1 + A2;
   a2.out = w.ys;
   static std::once_flag once;
   std::call_once(once, [] {
