@@ -20,7 +20,7 @@
 //            count rounded up to 16, so a lightly used expert wastes little);
 //            one of two TMEM accumulators; tcgen05.commit releases the stage
 //   warps 2-9  dequantise the weight tile into the canonical K-major
-//            128-byte-swizzled bf16 layout: w = bf16(fma(s, q, b)) per element
+//            128-byte-swizzled bf16 layout in shared memory: w = bf16(fma(s, q, b))
 //   warps 10-13  epilogue: tcgen05.ld of the accumulator (lane = weight row,
 //            column = token), GELU gating (GEMM1) or plain bf16 store (GEMM2)
 // Within every 8-element word of K the columns are stored in the order
@@ -41,27 +41,25 @@
 namespace fmoe {
 namespace pf {
 
-constexpr int BM = 64;                 // tokens per tile (the MMA's N, rounded up to 16)
+constexpr int BM = 128;                // tokens per tile (the MMA's N, rounded up to 16)
 constexpr int BN = 256, BK = 64;       // weight rows per item (two 128-row halves), K per tile
-constexpr int NS = 6;                  // token-tile stages (shared memory, TMA)
-constexpr int NT = 3;                  // dequantised weight stages (TMEM)
-constexpr int NQ = 3;                  // packed-weight stages, KQ K tiles each
+constexpr int NS = 3;                  // K-tile stages: token tile + dequantised weights (shared memory)
+constexpr int NQ = 2;                  // packed-weight stages, KQ K tiles each
 constexpr int KQ = 4;                  // K tiles per packed-weight stage (128 bytes of 4-bit codes per row)
-constexpr int X_BYTES = BM * BK * 2;   // 8 KB
+constexpr int X_BYTES = BM * BK * 2;   // 16 KB
+constexpr int WB_BYTES = BN * BK * 2;  // 32 KB
 constexpr int WQ_BYTES = BN * BK * KQ / 2;  // 32 KB: 256 rows x 128 bytes, 128-byte swizzle
 constexpr int SC_BYTES = 2 * BN * KQ * 2;   // 4 KB: scale and bias of 256 rows x KQ groups
 constexpr int WQS = WQ_BYTES + SC_BYTES;    // one packed-weight stage (codes, then scales)
-constexpr int OFF_WQ = NS * X_BYTES;
+constexpr int OFF_X = 0, OFF_WB = X_BYTES;
+constexpr int STAGE = OFF_WB + WB_BYTES;    // 48 KB, a multiple of 1024
+constexpr int OFF_WQ = NS * STAGE;
 constexpr int OFF_BAR = OFF_WQ + NQ * WQS;
 constexpr int SMEM = OFF_BAR + 512 + 1024;  // + alignment slack for the 1024-byte swizzle atoms
 constexpr int NDQ = 8;                      // dequantising warps (one weight row per thread)
 constexpr int THREADS = (2 + NDQ + 4) * 32;
-// TMEM columns: accumulators [2 buffers][2 halves][BM tokens] fp32, then the
-// dequantised weights [NT stages][2 halves][BK / 2] (two bf16 per column).
-constexpr int TMEM_COLS = 512;
-constexpr int TM_ACC = 0, TM_W = 2 * 2 * BM;
-static_assert(TM_W + NT * 2 * (BK / 2) <= TMEM_COLS, "TMEM budget");
-static_assert(X_BYTES % 1024 == 0 && OFF_WQ % 1024 == 0 && WQS % 1024 == 0, "stage alignment");
+constexpr int TMEM_COLS = 512;              // accumulators [2 buffers][2 halves][BM tokens] fp32
+static_assert(STAGE % 1024 == 0 && OFF_WQ % 1024 == 0 && WQS % 1024 == 0, "stage alignment");
 
 struct alignas(64) Maps {
   CUtensorMap a;   // A rows (bf16 [P][K], 128-byte swizzle, box 64 x 128)
@@ -130,24 +128,13 @@ __device__ __forceinline__ uint32_t idesc_n(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-// D (TMEM) += A (TMEM, K-major: row = lane, two bf16 per column) . B (shared memory descriptor)^T
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+// D (TMEM) += A (shared memory descriptor) . B (shared memory descriptor)^T
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
 }
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
                : "memory");
@@ -175,12 +162,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // token tile landed
-  uint64_t* xfree = xfull + NS;                                     // MMAs done with it
-  uint64_t* wqf = xfree + NS;                                       // packed weights + scales landed
+  uint64_t* deqd = xfull + NS;                                      // dequantised weights written
+  uint64_t* mmad = deqd + NS;                                       // MMAs done with the stage
+  uint64_t* wqf = mmad + NS;                                        // packed weights + scales landed
   uint64_t* wqe = wqf + NQ;                                         // dequantisers done with them
-  uint64_t* tdq = wqe + NQ;                                         // dequantised weights in TMEM
-  uint64_t* tmm = tdq + NT;                                         // MMAs done with them
-  uint64_t* accf = tmm + NT;                                        // accumulator complete
+  uint64_t* accf = wqe + NQ;                                        // accumulator complete
   uint64_t* acce = accf + 2;                                        // accumulator read out
   volatile int* failed = reinterpret_cast<volatile int*>(acce + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2) + 1;
@@ -191,15 +177,12 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&xfull[s], 1);
-      mbar_init(&xfree[s], 1);
+      mbar_init(&deqd[s], NDQ);
+      mbar_init(&mmad[s], 1);
     }
     for (int s = 0; s < NQ; ++s) {
       mbar_init(&wqf[s], 1);
       mbar_init(&wqe[s], NDQ);
-    }
-    for (int s = 0; s < NT; ++s) {
-      mbar_init(&tdq[s], NDQ);
-      mbar_init(&tmm[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&accf[s], 1);
@@ -208,7 +191,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     *failed = 0;
     mbar_fence_init();
   }
-  if (warp == 1) {  // the whole warp allocates the accumulators and weight stages
+  if (warp == 1) {  // the whole warp allocates the accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                  "r"(TMEM_COLS)
                  : "memory");
@@ -256,10 +239,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             ++qq;
           }
           const int s = q % NS;
-          if (q >= NS) pwait(&xfree[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 301);
+          if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 301);
           if (*failed) break;
           mbar_arrive_expect_tx(&xfull[s], (uint32_t)X_BYTES);
-          tma2d(smem + s * X_BYTES, &maps.a, kt * BK, row0, &xfull[s]);
+          tma2d(smem + s * STAGE + OFF_X, &maps.a, kt * BK, row0, &xfull[s]);
         }
         if (*failed) break;
       }
@@ -268,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       for (int k = qq - NQ < 0 ? 0 : qq - NQ; k < qq; ++k) drain_wait(&wqf[k % NQ], (uint32_t)(k / NQ) & 1u);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer: weights (TMEM) as the M operand, the tile's tokens (shared memory) as N
+    // ---- MMA issuer: weights as the M operand (two 128-row halves), the tile's tokens as N
     if (lane == 0) {
       int q = 0, n = 0;
       for (int it = blockIdx.x; it < nitems; it += gridDim.x, ++n) {
@@ -278,38 +261,35 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         if (n >= 2) pwait(&acce[ab], (uint32_t)((n / 2) - 1) & 1u, failed, a.status, 302);
         tc_fence_after();
         for (int kt = 0; kt < NK; ++kt, ++q) {
-          const int s = q % NS, t = q % NT;
-          pwait(&xfull[s], (uint32_t)(q / NS) & 1u, failed, a.status, 303);
-          pwait(&tdq[t], (uint32_t)(q / NT) & 1u, failed, a.status, 308);
+          const int s = q % NS;
+          pwait(&deqd[s], (uint32_t)(q / NS) & 1u, failed, a.status, 303);  // implies the token tile too
           tc_fence_after();
-          const uint32_t sx = smem_u32(smem + s * X_BYTES);
+          const uint32_t sx = smem_u32(smem + s * STAGE + OFF_X), sw = smem_u32(smem + s * STAGE + OFF_WB);
           if (!*failed) {
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_ts(tmem + TM_ACC + ab * 2 * BM + h * BM, tmem + TM_W + t * BK + h * (BK / 2) + k * 8,
+                mma_ss(tmem + ab * 2 * BM + h * BM, sw128_desc(sw + h * (128 * 128) + 32 * k),
                        sw128_desc(sx + 32 * k), idesc, (kt | k) != 0);
           }
-          mma_commit(&xfree[s]);
-          mma_commit(&tmm[t]);
+          mma_commit(&mmad[s]);
         }
         mma_commit(&accf[ab]);
       }
       if (n > 0) drain_wait(&accf[(n - 1) & 1], (uint32_t)((n - 1) / 2) & 1u);  // the last MMAs are done
     }
   } else if (warp < 2 + NDQ) {
-    // ---- dequantisers: warp w writes TMEM lanes 32 * (w % 4) .. of half (w - 2) / 4;
-    // thread = one weight row of the 256-row tile, 64 bf16 per K tile = 32 TMEM columns
-    const int qw = warp & 3, h = (warp - 2) >> 2;
-    const int rr = h * 128 + qw * 32 + lane;
+    // ---- dequantisers: thread = one row of the 256-row weight tile, written as 64 bf16 in
+    // the canonical K-major 128-byte-swizzled layout (chunk c of row r at chunk c ^ (r % 8))
+    const int rr = threadIdx.x - 64, h = rr >> 7;
     int q = 0, qq = 0;
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
       const int j = it % NJ;
       for (int kt = 0; kt < NK; ++kt, ++q) {
-        const int sq = qq % NQ, t = q % NT;
+        const int s = q % NS, sq = qq % NQ;
         if (kt % KQ == 0) pwait(&wqf[sq], (uint32_t)(qq / NQ) & 1u, failed, a.status, 307);
-        if (q >= NT) pwait(&tmm[t], (uint32_t)((q / NT) - 1) & 1u, failed, a.status, 304);
+        pwait(&xfull[s], (uint32_t)(q / NS) & 1u, failed, a.status, 304);  // the stage is free again
         const uint8_t* wq = smem + OFF_WQ + sq * WQS;
         const bf16* sc = reinterpret_cast<const bf16*>(wq + WQ_BYTES);
         const int kq = kt % KQ, c0 = 2 * kq;  // this K tile's two 16-byte chunks of a 128-byte row
@@ -330,23 +310,24 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         const uint32_t ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         const __nv_bfloat162 s2 = __floats2bfloat162_rn(sv, sv), b2 = __floats2bfloat162_rn(bv, bv);
         const __nv_bfloat162 off = __floats2bfloat162_rn(128.f, 128.f);
-        uint32_t o[32];
+        uint8_t* wrow = smem + s * STAGE + OFF_WB + rr * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
+        for (int c = 0; c < 8; ++c) {
+          uint32_t o[4];
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             // nibbles jj and jj+4 of the word -> bf16 (128 + q) pair -> q -> fma(q, s, b)
             const uint32_t v = and_or(ww[c] >> (4 * jj), 0x000F000Fu, 0x43004300u);
             __nv_bfloat162 qv = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v), off);
             __nv_bfloat162 r = __hfma2(qv, s2, b2);
-            o[4 * c + jj] = ok ? *reinterpret_cast<uint32_t*>(&r) : 0u;
+            o[jj] = ok ? *reinterpret_cast<uint32_t*>(&r) : 0u;
           }
-        tmem_st32(tmem + ((uint32_t)(qw * 32) << 16) + TM_W + t * BK + h * (BK / 2), o);
-        tmem_st_wait();
-        tc_fence_before();
+          *reinterpret_cast<uint4*>(wrow + ((c ^ (rr & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor-core reads
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&tdq[t]);
+          mbar_arrive(&deqd[s]);
           if (kt % KQ == KQ - 1 || kt == NK - 1) mbar_arrive(&wqe[sq]);
         }
         if (kt % KQ == KQ - 1 || kt == NK - 1) ++qq;
@@ -362,7 +343,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
       const int ab = n & 1;
       pwait(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 305);
       tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + TM_ACC + ab * 2 * BM;
+      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * 2 * BM;
       const bool ok = !*failed;
       if (MODE == 0) {
         const int f = j * 128 + fr;  // intermediate index of this lane's gate / up rows
