@@ -10,6 +10,7 @@ for this path (names, argument meaning, error behaviour):
     KVCache.update_and_fetch(k, v)      src/cache.rs:266-310   (see kv.py)
     Gemma4DecoderLayer.forward(x, ...)  src/model/mod.rs:67-119  (see model.py)
     Gemma4Model.decode_step()           src/model/mod.rs:135-363
+    ExpertParallelMoeBlock.forward(x)   moe.rs:315-470 with experts split over GPUs (see ep.py)
 
 There is no CPU fallback: every call goes to the CUDA kernels in
 lib/libfmoe.so, and a missing library or device raises.
@@ -152,6 +153,19 @@ SIGNATURES = {
     "fmoe_moe_prefill_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC)]),
     "fmoe_moe_prefill": (_I, [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P, _P, _SZ,
                               _P]),
+    "fmoe_moe_prefill_experts_workspace_bytes": (_SZ, [_I64, _I, ctypes.POINTER(ExpertsC)]),
+    "fmoe_moe_prefill_experts": (_I, [_P, _I64, _I, _P, _P, ctypes.POINTER(ExpertsC), _P, _P, _P, _SZ, _P]),
+    "fmoe_ep_unique_id": (_I, [_P, _SZ]),
+    "fmoe_ep_comm_init": (_I, [ctypes.POINTER(ctypes.c_void_p), _I, _I, _P, _SZ]),
+    "fmoe_ep_comm_destroy": (_I, [_P]),
+    "fmoe_ep_comm_abort": (_I, [_P]),
+    "fmoe_ep_comm_status": (_I, [_P]),
+    "fmoe_ep_moe_workspace_bytes": (_SZ, [_I, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC)]),
+    "fmoe_ep_moe_forward": (_I, [_P, _P, _I64, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P,
+                                 _P, _I, _P, _SZ, _P]),
+    "fmoe_decoder_ep_workspace_bytes": (_SZ, [_I64, _P, ctypes.POINTER(KvCacheC), _I, _I64]),
+    "fmoe_decoder_layer_forward_ep": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _P, _I, _P, _I64, _I64, _P, _P,
+                                           _SZ, _P]),
     "fmoe_decode_step_workspace_bytes": (_SZ, [_P]),
     "fmoe_decode_step_prepare": (_I, [_P, _P, _SZ]),
     "fmoe_decode_step": (_I, [_P, _P, _P, _P, _P, _SZ, _P]),
@@ -369,6 +383,17 @@ class ExpertTable:
         return ExpertsC(_ptr(self.buf), self.stride, (ctypes.c_int64 * 9)(*self.offsets), self.num_experts,
                         self.first_expert, self.hidden, self.inter, self.bits, self.group)
 
+    def shard(self, rank: int, world: int, copy: bool = False) -> "ExpertTable":
+        """Experts [rank*E/world, (rank+1)*E/world) of this (whole) table, for
+        expert parallelism: a view of the same bytes, or its own copy."""
+        if self.first_expert != 0:
+            raise ValueError("shard: not a whole table")
+        from .ep import shard_range
+        first, n = shard_range(self.num_experts, world, rank)
+        buf = self.buf[first * self.stride:(first + n) * self.stride]
+        return ExpertTable(buf.clone() if copy else buf, n, self.hidden, self.inter, self.bits, self.group,
+                           first_expert=first)
+
 
 def moe_experts(x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor, table: ExpertTable,
                 ws: _Workspace | None = None) -> torch.Tensor:
@@ -490,3 +515,5 @@ class Gemma4MoeBlock:
 
 from .kv import KV_AFFINE, KV_BF16, KVCache, turbo_round_trip  # noqa: E402
 from .model import GEMMA4_26B, Gemma4DecoderLayer, Gemma4Model  # noqa: E402
+from .ep import (FMOE_EP_EXACT, FMOE_EP_FIXED, EPComm, ExpertParallelMoeBlock, PeerLost, PeerWatch,  # noqa: E402
+                 shard_range)

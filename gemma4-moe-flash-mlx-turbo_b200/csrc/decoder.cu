@@ -267,6 +267,7 @@ struct DecWs {
   int32_t* ids;
   float* wts;
   void* attn_ws;
+  EpWs ep;  // expert-parallel exchange (fmoe_decoder_layer_forward_ep only)
   size_t bytes;
 };
 
@@ -291,7 +292,9 @@ static int dec_dims(const fmoe_decoder_layer_t* L, int* qkv_rows) {
 // 64 per column chunk).
 static int max_parts(int K) { return K / 512 > 1 ? K / 512 : 1; }
 
-static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, DecWs* w) {
+// ep_ranks > 0: add the expert-parallel exchange buffers for ep_cap tokens per rank.
+static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, DecWs* w,
+                        int ep_ranks = 0, int64_t ep_cap = 0) {
   DecWs d = {};
   int qkv_rows = 0;
   dec_dims(L, &qkv_rows);
@@ -317,6 +320,7 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   d.moe = c.take<bf16>((size_t)T * H);
   d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
   d.wts = c.take<float>((size_t)T * L->router.top_k);
+  if (ep_ranks > 0) carve_ep(c, ep_ranks, ep_cap, nullptr, L->router.top_k, ex, d.h, &d.ep);
   d.bytes = c.off + 256;
   if (w) *w = d;
   return d.bytes;
@@ -347,9 +351,22 @@ size_t fmoe_decoder_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer
   return carve_dec(c, T, layer, kv, nullptr);
 }
 
-int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, void* x, int64_t T,
-                               int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Expert-parallel arguments of a layer call (comm == nullptr: all experts local).
+struct EpCall {
+  const fmoe_ep_comm_t* comm;
+  int n_ranks;
+  int64_t cap;
+  const void* prep;
+  int mode;
+};
+
+int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, const EpCall& epc, void* x,
+                    int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
+                    void* stream) {
   int qkv_rows = 0;
   int rc = dec_dims(L, &qkv_rows);
   if (rc) return rc;
@@ -379,12 +396,16 @@ int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cach
   if (k.in != H || o.out != H || gq.in != H || uq.out != Id || uq.in != H || dq.in != Id || dq.out != H ||
       ex.H != H || rq.in != H || (!L->k_eq_v && v.in != H))
     return set_error(FMOE_ERR_INVALID, "decoder: hidden / intermediate sizes disagree across weights");
-  const size_t need = fmoe_decoder_workspace_bytes(T, L, cache);
+  if (epc.comm && (T > epc.cap || (rc = ep_check(epc.comm, ex, rq.out, nullptr))))
+    return rc ? rc : set_error(FMOE_ERR_INVALID, "decoder: T=%lld above the exchange capacity", (long long)T);
+  if (!epc.comm && ex.first != 0) return set_error(FMOE_ERR_INVALID, "decoder: expert slice without a communicator");
+  Carver cz(nullptr);
+  const size_t need = carve_dec(cz, T, L, kv, nullptr, epc.n_ranks, epc.cap);
   if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
     return set_error(FMOE_ERR_WORKSPACE, "decoder: workspace %zu < %zu", workspace_bytes, need);
   Carver c(workspace);
   DecWs w;
-  carve_dec(c, T, L, kv, &w);
+  carve_dec(c, T, L, kv, &w, epc.n_ranks, epc.cap);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   bf16* xb = static_cast<bf16*>(x);
   const int Ti = (int)T;
@@ -467,8 +488,15 @@ int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cach
   {
     fmoe_router_t r = L->router;
     r.use_norm = 0;  // ff_in applied the norm chain
-    if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, st))) return rc;
-    if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, st))) return rc;
+    if (epc.comm) {  // routed experts on their owning ranks
+      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, nullptr, w.h.status, st))) return rc;
+      if ((rc = ep_experts(epc.comm, w.h2, T, epc.cap, r.top_k, w.ids, w.wts, ex, static_cast<const bf16*>(epc.prep),
+                           w.moe, w.ep, epc.mode, w.h.status, st)))
+        return rc;
+    } else {
+      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, st))) return rc;
+      if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, st))) return rc;
+    }
   }
   // 10 dense down on gelu(g) * u
   {
@@ -501,6 +529,40 @@ int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cach
     if ((rc = check_launch("ff_out_kernel"))) return rc;
   }
   return FMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, void* x, int64_t T,
+                               int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  return decoder_forward(L, cache, EpCall{nullptr, 0, 0, nullptr, 0}, x, T, pos, pos_dev, workspace, workspace_bytes,
+                         stream);
+}
+
+size_t fmoe_decoder_ep_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache,
+                                       int n_ranks, int64_t cap) {
+  KvDev kv;
+  int qkv_rows;
+  if (T <= 0 || n_ranks < 1 || cap < T || dec_dims(layer, &qkv_rows) || kv_to_dev(cache, &kv)) return 0;
+  Carver c(nullptr);
+  return carve_dec(c, T, layer, kv, nullptr, n_ranks, cap);
+}
+
+int fmoe_decoder_layer_forward_ep(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, fmoe_ep_comm_t* comm,
+                                  int64_t cap, const void* prepared, int mode, void* x, int64_t T, int64_t pos,
+                                  const int64_t* pos_dev, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!comm) return set_error(FMOE_ERR_INVALID, "decoder_ep: null communicator");
+  ExpertsDev ex;
+  QW rq;
+  int rc, R = 0;
+  if ((rc = to_experts(&L->experts, &ex)) || (rc = check_router(&L->router, &rq)) ||
+      (rc = ep_check(comm, ex, rq.out, &R)))
+    return rc;
+  return decoder_forward(L, cache, EpCall{comm, R, cap, prepared, mode}, x, T, pos, pos_dev, workspace,
+                         workspace_bytes, stream);
 }
 
 size_t fmoe_lm_head_workspace_bytes(int64_t T) {

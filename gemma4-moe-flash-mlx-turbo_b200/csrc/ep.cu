@@ -1,0 +1,468 @@
+// Expert parallelism: the experts of a MoE layer split contiguously over the
+// GPUs of one box, one process per GPU, tokens exchanged over NVLink by NCCL.
+//
+// The reference runs on one device (Gemma4MoeBlock::forward,
+// src/model/moe.rs:315-470, evaluates every routed expert locally).  Here rank
+// r of n holds experts [r*E/n, (r+1)*E/n); router weights are replicated and
+// every rank routes its own tokens.  Per MoE block:
+//   plan     one CTA per destination rank: slot of token t in rank r's block =
+//            number of earlier tokens with an expert on r, -1 if none (a token
+//            crosses to a rank once, however many of its experts live there)
+//   pack     token rows + their full id / weight rows into per-rank blocks
+//   dispatch grouped ncclSend / ncclRecv (FIXED: every block is cap rows, no
+//            host sync, capturable in a CUDA graph; EXACT: counts first, one
+//            host sync, then only routed rows cross)
+//   experts  the local slice over the received rows (ids outside the slice
+//            contribute nothing): decode GEMV kernels up to 128 rows, the
+//            tcgen05 grouped GEMMs above
+//   return   the per-rank partial sums (bf16) travel back the same way
+//   combine  y[t] = sum over ranks, ascending, of the partial at slots[r][t]
+//            (fp32 accumulation; rank order = ascending expert-id order of
+//            the reference's combine, moe.rs:443-465)
+// NCCL is resolved from libnccl.so.2 at run time (the copy the host process
+// already loaded when there is one), so the library loads without it.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "internal.h"
+
+struct fmoe_ep_comm {
+  ncclComm_t nc;
+  int n_ranks;
+  int rank;
+  int device;
+  int32_t* host_counts;  // pinned [2 * n_ranks]: send counts | receive counts (EXACT mode)
+};
+
+namespace fmoe {
+namespace ep {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kGemvRows = 128;  // rows the decode expert kernels serve per call
+
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(const int32_t* __restrict__ ids, int T, int k,
+                                                             int per_rank, int cap, int32_t* __restrict__ slots,
+                                                             int32_t* __restrict__ counts) {
+  __shared__ int wsum[kPlanThreads / 32];
+  const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lo = r * per_rank, hi = lo + per_rank;
+  int run = 0;
+  for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    bool f = false;
+    if (t < T)
+      for (int j = 0; j < k; ++j) {
+        const int e = ids[(int64_t)t * k + j];
+        f |= (e >= lo && e < hi);
+      }
+    const unsigned m = __ballot_sync(0xffffffffu, f);
+    if (lane == 0) wsum[warp] = __popc(m);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int w = 0; w < nw; ++w) {
+      const int c = wsum[w];
+      before += w < warp ? c : 0;
+      total += c;
+    }
+    if (t < T) slots[(int64_t)r * cap + t] = f ? run + before + __popc(m & ((1u << lane) - 1u)) : -1;
+    run += total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) counts[r] = run;
+}
+
+// Block r of the send buffers holds the rows of the tokens routed to rank r in
+// slot order; rows from counts[r] to cap carry ids -1 (they select no expert).
+__global__ void pack_kernel(const bf16* __restrict__ x, const int32_t* __restrict__ ids,
+                            const float* __restrict__ wts, const int32_t* __restrict__ slots,
+                            const int32_t* __restrict__ counts, int T, int k, int H, int R, int cap,
+                            bf16* __restrict__ sx, int32_t* __restrict__ sids, float* __restrict__ swts) {
+  const int words = H / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n = (int64_t)R * T * words;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int r = (int)(i / ((int64_t)T * words));
+    const int rem = (int)(i % ((int64_t)T * words));
+    const int t = rem / words, w = rem % words;
+    const int s = slots[(int64_t)r * cap + t];
+    if (s < 0) continue;
+    const int64_t row = (int64_t)r * cap + s;
+    *reinterpret_cast<uint4*>(sx + row * H + 8 * w) = *reinterpret_cast<const uint4*>(x + (int64_t)t * H + 8 * w);
+    if (w < k) {  // k <= H / 8 (checked on the host)
+      sids[row * k + w] = ids[(int64_t)t * k + w];
+      swts[row * k + w] = wts[(int64_t)t * k + w];
+    }
+  }
+  const int64_t m = (int64_t)R * cap * k;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += stride) {
+    const int r = (int)(i / ((int64_t)cap * k));
+    const int j = (int)((i % ((int64_t)cap * k)) / k);
+    if (j >= counts[r]) {
+      sids[i] = -1;
+      swts[i] = 0.f;
+    }
+  }
+}
+
+// y[t] = bf16(sum over r ascending of ret[r][slots[r][t]]), fp32 accumulation.
+__global__ void combine_kernel(const bf16* __restrict__ ret, const int32_t* __restrict__ slots, int T, int R, int cap,
+                               int H, bf16* __restrict__ y) {
+  const int words = H / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * words;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = (int)(i / words), w = (int)(i % words);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < R; ++r) {
+      const int s = slots[(int64_t)r * cap + t];
+      if (s < 0) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(ret + ((int64_t)r * cap + s) * H + 8 * w);
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf16lo(vv[q]);
+        acc[2 * q + 1] += bf16hi(vv[q]);
+      }
+    }
+    *reinterpret_cast<uint4*>(y + (int64_t)t * H + 8 * w) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                   pack_bf16x2(acc[6], acc[7]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// NCCL, resolved at run time
+
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclCommAbort) comm_abort = nullptr;
+  decltype(&ncclCommGetAsyncError) comm_async_error = nullptr;
+  decltype(&ncclGroupStart) group_start = nullptr;
+  decltype(&ncclGroupEnd) group_end = nullptr;
+  decltype(&ncclSend) send = nullptr;
+  decltype(&ncclRecv) recv = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+};
+
+const NcclApi* nccl() {
+  static NcclApi api;
+  static bool ok = false;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return;
+#define FMOE_NCCL_SYM(field, name)                                   \
+  api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name)); \
+  if (!api.field) return;
+    FMOE_NCCL_SYM(get_unique_id, "ncclGetUniqueId")
+    FMOE_NCCL_SYM(comm_init_rank, "ncclCommInitRank")
+    FMOE_NCCL_SYM(comm_destroy, "ncclCommDestroy")
+    FMOE_NCCL_SYM(comm_abort, "ncclCommAbort")
+    FMOE_NCCL_SYM(comm_async_error, "ncclCommGetAsyncError")
+    FMOE_NCCL_SYM(group_start, "ncclGroupStart")
+    FMOE_NCCL_SYM(group_end, "ncclGroupEnd")
+    FMOE_NCCL_SYM(send, "ncclSend")
+    FMOE_NCCL_SYM(recv, "ncclRecv")
+    FMOE_NCCL_SYM(error_string, "ncclGetErrorString")
+#undef FMOE_NCCL_SYM
+    ok = true;
+  });
+  return ok ? &api : nullptr;
+}
+
+int nccl_error(const NcclApi* api, ncclResult_t r, const char* what) {
+  return set_error(FMOE_ERR_NCCL, "ep: %s: %s", what, api->error_string(r));
+}
+
+// One grouped exchange: to every peer p, send sbytes[p] bytes at sptr[p] and
+// receive rbytes[p] bytes into rptr[p], for each of up to three buffers.
+struct Xfer {
+  const void* sptr[3];
+  void* rptr[3];
+  size_t sbytes[3], rbytes[3];
+};
+
+int exchange(const fmoe_ep_comm* c, const std::vector<Xfer>& peers, int nbuf, cudaStream_t st, const char* what) {
+  const NcclApi* api = nccl();
+  ncclResult_t r = api->group_start();
+  if (r != ncclSuccess) return nccl_error(api, r, what);
+  ncclResult_t first = ncclSuccess;
+  for (int p = 0; p < c->n_ranks; ++p)
+    for (int b = 0; b < nbuf; ++b) {
+      const Xfer& x = peers[p];
+      if (x.sbytes[b] && (r = api->send(x.sptr[b], x.sbytes[b], ncclUint8, p, c->nc, st)) != ncclSuccess &&
+          first == ncclSuccess)
+        first = r;
+      if (x.rbytes[b] && (r = api->recv(x.rptr[b], x.rbytes[b], ncclUint8, p, c->nc, st)) != ncclSuccess &&
+          first == ncclSuccess)
+        first = r;
+    }
+  r = api->group_end();
+  if (first != ncclSuccess) return nccl_error(api, first, what);
+  if (r != ncclSuccess) return nccl_error(api, r, what);
+  return FMOE_OK;
+}
+
+}  // namespace ep
+
+size_t carve_ep(Carver& c, int R, int64_t cap, const fmoe_router_t* r, int k, const ExpertsDev& d, const WsHead& h,
+                EpWs* w) {
+  using ep::kGemvRows;
+  EpWs e;
+  const int64_t rows = (int64_t)R * cap;
+  if (r) carve_router(c, cap, r, h, &e.rw);
+  e.ids = c.take<int32_t>((size_t)cap * k);
+  e.wts = c.take<float>((size_t)cap * k);
+  e.slots = c.take<int32_t>((size_t)rows);
+  e.counts = c.take<int32_t>(R);
+  e.rcounts = c.take<int32_t>(R);
+  e.sx = c.take<bf16>((size_t)rows * d.H);
+  e.sids = c.take<int32_t>((size_t)rows * k);
+  e.swts = c.take<float>((size_t)rows * k);
+  e.rx = c.take<bf16>((size_t)rows * d.H);
+  e.rids = c.take<int32_t>((size_t)rows * k);
+  e.rwts = c.take<float>((size_t)rows * k);
+  e.ypart = c.take<bf16>((size_t)rows * d.H);
+  e.ret = c.take<bf16>((size_t)rows * d.H);
+  carve_moe(c, std::min<int64_t>(rows, kGemvRows), k, d, &e.mw);
+  e.gemm = rows > kGemvRows;
+  if (e.gemm) carve_pf_ex(c, rows, k, d, &e.pw);
+  if (w) *w = e;
+  return c.off;
+}
+
+int ep_check(const fmoe_ep_comm* c, const ExpertsDev& d, int E_total, int* n_ranks) {
+  if (!c || !c->nc) return set_error(FMOE_ERR_INVALID, "ep: null communicator");
+  if (E_total % c->n_ranks || d.E != E_total / c->n_ranks || d.first != c->rank * d.E)
+    return set_error(FMOE_ERR_INVALID, "ep: rank %d of %d must hold experts [%d, %d) of %d (table: %d from %d)",
+                     c->rank, c->n_ranks, c->rank * (E_total / std::max(c->n_ranks, 1)),
+                     (c->rank + 1) * (E_total / std::max(c->n_ranks, 1)), E_total, d.E, d.first);
+  if (!ep::nccl()) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");
+  if (n_ranks) *n_ranks = c->n_ranks;
+  return FMOE_OK;
+}
+
+// Dispatch -> local experts -> return -> combine for T routed tokens (ids /
+// wts [T, k], global expert ids).  Shared by the MoE-block and decoder-layer
+// entry points.
+int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int k, const int32_t* ids,
+               const float* wts, const ExpertsDev& d, const bf16* prep, bf16* y, const EpWs& w, int mode,
+               int* status, cudaStream_t st) {
+  using namespace ep;
+  const int R = c->n_ranks;
+  const int H = d.H;
+  int rc;
+  if (T > cap) return set_error(FMOE_ERR_INVALID, "ep: T=%lld above the exchange capacity %lld", (long long)T,
+                                (long long)cap);
+  if (mode != FMOE_EP_FIXED && mode != FMOE_EP_EXACT) return set_error(FMOE_ERR_INVALID, "ep: mode %d", mode);
+  if (mode == FMOE_EP_EXACT) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs != cudaStreamCaptureStatusNone)
+      return set_error(FMOE_ERR_INVALID, "ep: EXACT mode synchronises on the host and cannot be captured");
+  }
+  {
+    ProfScope prof_("ep_plan_kernel", st);
+    plan_kernel<<<R, kPlanThreads, 0, st>>>(ids, (int)T, k, d.E, (int)cap, w.slots, w.counts);
+  }
+  if ((rc = check_launch("ep_plan_kernel"))) return rc;
+  {
+    ProfScope prof_("ep_pack_kernel", st);
+    pack_kernel<<<2 * kNumSMs, 256, 0, st>>>(x, ids, wts, w.slots, w.counts, (int)T, k, H, R, (int)cap, w.sx, w.sids,
+                                             w.swts);
+  }
+  if ((rc = check_launch("ep_pack_kernel"))) return rc;
+
+  const size_t row_b = (size_t)H * sizeof(bf16), meta_b = (size_t)k * sizeof(int32_t);
+  std::vector<Xfer> px(R), pb(R);
+  std::vector<int64_t> scnt(R, cap), rcnt(R, cap), roff(R);
+  if (mode == FMOE_EP_EXACT) {
+    std::vector<Xfer> pc(R);
+    for (int p = 0; p < R; ++p) {
+      pc[p] = Xfer{};
+      pc[p].sptr[0] = w.counts + p;
+      pc[p].rptr[0] = w.rcounts + p;
+      pc[p].sbytes[0] = pc[p].rbytes[0] = sizeof(int32_t);
+    }
+    if ((rc = exchange(c, pc, 1, st, "count exchange"))) return rc;
+    if (cudaMemcpyAsync(c->host_counts, w.counts, R * sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaMemcpyAsync(c->host_counts + R, w.rcounts, R * sizeof(int32_t), cudaMemcpyDeviceToHost, st) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+      return set_error(FMOE_ERR_CUDA, "ep: count read-back failed: %s", cudaGetErrorString(cudaGetLastError()));
+    for (int p = 0; p < R; ++p) {
+      scnt[p] = c->host_counts[p];
+      rcnt[p] = c->host_counts[R + p];
+      if (scnt[p] < 0 || scnt[p] > cap || rcnt[p] < 0 || rcnt[p] > cap)
+        return set_error(FMOE_ERR_INVALID, "ep: exchange counts out of range (peer %d: %lld / %lld, cap %lld)", p,
+                         (long long)scnt[p], (long long)rcnt[p], (long long)cap);
+    }
+  }
+  int64_t rows = 0;
+  for (int p = 0; p < R; ++p) {
+    roff[p] = rows;
+    rows += rcnt[p];
+  }
+  for (int p = 0; p < R; ++p) {
+    const int64_t so = (int64_t)p * cap;
+    px[p] = Xfer{};
+    px[p].sptr[0] = w.sx + so * H;
+    px[p].sptr[1] = w.sids + so * k;
+    px[p].sptr[2] = w.swts + so * k;
+    px[p].rptr[0] = w.rx + roff[p] * H;
+    px[p].rptr[1] = w.rids + roff[p] * k;
+    px[p].rptr[2] = w.rwts + roff[p] * k;
+    px[p].sbytes[0] = scnt[p] * row_b;
+    px[p].sbytes[1] = px[p].sbytes[2] = scnt[p] * meta_b;
+    px[p].rbytes[0] = rcnt[p] * row_b;
+    px[p].rbytes[1] = px[p].rbytes[2] = rcnt[p] * meta_b;
+    // the way back: partials of the rows p sent here return to p's block of ret
+    pb[p] = Xfer{};
+    pb[p].sptr[0] = w.ypart + roff[p] * H;
+    pb[p].rptr[0] = w.ret + so * H;
+    pb[p].sbytes[0] = rcnt[p] * row_b;
+    pb[p].rbytes[0] = scnt[p] * row_b;
+  }
+  if ((rc = exchange(c, px, 3, st, "dispatch"))) return rc;
+  if (rows > 0) {
+    if (rows <= kGemvRows) {
+      rc = run_experts(w.rx, rows, k, w.rids, w.rwts, d, w.ypart, w.mw, true, status, st);
+    } else {
+      if (!w.gemm || !prep)
+        return set_error(FMOE_ERR_INVALID, "ep: %lld received rows need the tensor-core path (prepared scales)",
+                         (long long)rows);
+      rc = run_prefill_experts(w.rx, rows, k, w.rids, w.rwts, d, prep, w.ypart, w.pw, true, status, st);
+    }
+    if (rc) return rc;
+  }
+  if ((rc = exchange(c, pb, 1, st, "combine"))) return rc;
+  {
+    ProfScope prof_("ep_combine_kernel", st);
+    combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(w.ret, w.slots, (int)T, R, (int)cap, H, y);
+  }
+  return check_launch("ep_combine_kernel");
+}
+
+}  // namespace fmoe
+
+using namespace fmoe;
+
+extern "C" {
+
+int fmoe_ep_unique_id(void* id, size_t len) {
+  const ep::NcclApi* api = ep::nccl();
+  if (!api) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");
+  if (!id || len < sizeof(ncclUniqueId))
+    return set_error(FMOE_ERR_INVALID, "ep: unique id buffer needs %zu bytes", sizeof(ncclUniqueId));
+  ncclUniqueId u;
+  const ncclResult_t r = api->get_unique_id(&u);
+  if (r != ncclSuccess) return ep::nccl_error(api, r, "ncclGetUniqueId");
+  memcpy(id, &u, sizeof(u));
+  return FMOE_OK;
+}
+
+int fmoe_ep_comm_init(fmoe_ep_comm_t** comm, int n_ranks, int rank, const void* id, size_t len) {
+  const ep::NcclApi* api = ep::nccl();
+  if (!api) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");
+  if (!comm || !id || len < sizeof(ncclUniqueId) || n_ranks < 1 || rank < 0 || rank >= n_ranks)
+    return set_error(FMOE_ERR_INVALID, "ep: comm_init(n_ranks=%d, rank=%d)", n_ranks, rank);
+  *comm = nullptr;
+  auto* c = new fmoe_ep_comm{};
+  c->n_ranks = n_ranks;
+  c->rank = rank;
+  cudaGetDevice(&c->device);
+  if (cudaHostAlloc(&c->host_counts, 2 * n_ranks * sizeof(int32_t), cudaHostAllocDefault) != cudaSuccess) {
+    delete c;
+    return set_error(FMOE_ERR_CUDA, "ep: pinned count buffer: %s", cudaGetErrorString(cudaGetLastError()));
+  }
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof(u));
+  const ncclResult_t r = api->comm_init_rank(&c->nc, n_ranks, u, rank);
+  if (r != ncclSuccess) {
+    cudaFreeHost(c->host_counts);
+    delete c;
+    return ep::nccl_error(api, r, "ncclCommInitRank");
+  }
+  *comm = c;
+  return FMOE_OK;
+}
+
+int fmoe_ep_comm_destroy(fmoe_ep_comm_t* c) {
+  if (!c) return FMOE_OK;
+  const ep::NcclApi* api = ep::nccl();
+  ncclResult_t r = ncclSuccess;
+  if (c->nc && api) r = api->comm_destroy(c->nc);
+  cudaFreeHost(c->host_counts);
+  delete c;
+  return r == ncclSuccess ? FMOE_OK : ep::nccl_error(api, r, "ncclCommDestroy");
+}
+
+int fmoe_ep_comm_abort(fmoe_ep_comm_t* c) {
+  if (!c) return FMOE_OK;
+  const ep::NcclApi* api = ep::nccl();
+  ncclResult_t r = ncclSuccess;
+  if (c->nc && api) r = api->comm_abort(c->nc);
+  cudaFreeHost(c->host_counts);
+  delete c;
+  return r == ncclSuccess ? FMOE_OK : ep::nccl_error(api, r, "ncclCommAbort");
+}
+
+int fmoe_ep_comm_status(fmoe_ep_comm_t* c) {
+  if (!c || !c->nc) return set_error(FMOE_ERR_INVALID, "ep: null communicator");
+  const ep::NcclApi* api = ep::nccl();
+  ncclResult_t state = ncclSuccess;
+  const ncclResult_t r = api->comm_async_error(c->nc, &state);
+  if (r != ncclSuccess) return ep::nccl_error(api, r, "ncclCommGetAsyncError");
+  if (state != ncclSuccess && state != ncclInProgress) return ep::nccl_error(api, state, "asynchronous error");
+  return FMOE_OK;
+}
+
+size_t fmoe_ep_moe_workspace_bytes(int n_ranks, int64_t cap, const fmoe_router_t* r, const fmoe_experts_t* local) {
+  ExpertsDev d;
+  if (n_ranks < 1 || cap < 1 || !r || r->top_k < 1 || r->top_k > 16 || to_experts(local, &d)) return 0;
+  Carver c(nullptr);
+  const WsHead h = carve_head(c);
+  return carve_ep(c, n_ranks, cap, r, r->top_k, d, h, nullptr) + 256;
+}
+
+int fmoe_ep_moe_forward(fmoe_ep_comm_t* comm, const void* x, int64_t T, int64_t cap, const fmoe_router_t* r,
+                        const fmoe_experts_t* local, const void* prep, void* y, int32_t* ids, float* weights, int mode,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  QW q;
+  int rc;
+  if ((rc = check_router(r, &q))) return rc;
+  ExpertsDev d;
+  if ((rc = to_experts(local, &d)) || (rc = ep_check(comm, d, q.out, nullptr))) return rc;
+  if (!x || !y) return set_error(FMOE_ERR_INVALID, "ep: null x / y");
+  if (T < 0 || cap < 1 || cap > (1 << 24)) return set_error(FMOE_ERR_INVALID, "ep: T=%lld cap=%lld", (long long)T,
+                                                           (long long)cap);
+  if (q.in != d.H || d.H % 8 || d.H / 8 < r->top_k)
+    return set_error(FMOE_ERR_INVALID, "ep: router in %d vs hidden %d", q.in, d.H);
+  if (!aligned(x, 16) || !aligned(y, 16)) return set_error(FMOE_ERR_ALIGN, "ep: x / y not 16-byte aligned");
+  const size_t need = fmoe_ep_moe_workspace_bytes(comm->n_ranks, cap, r, local);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return set_error(FMOE_ERR_WORKSPACE, "ep: workspace %zu < %zu (16-byte aligned)", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Carver c(workspace);
+  const WsHead h = carve_head(c);
+  EpWs w;
+  carve_ep(c, comm->n_ranks, cap, r, r->top_k, d, h, &w);
+  int32_t* ids_out = ids ? ids : w.ids;
+  float* w_out = weights ? weights : w.wts;
+  if (T > 0 &&
+      (rc = run_router(static_cast<const bf16*>(x), T, r, q, w.rw, ids_out, w_out, nullptr, nullptr, h.status, st)))
+    return rc;
+  // Every rank takes part in both exchanges, also with no tokens of its own.
+  return ep_experts(comm, static_cast<const bf16*>(x), T, cap, r->top_k, ids_out, w_out, d,
+                    static_cast<const bf16*>(prep), static_cast<bf16*>(y), w, mode, h.status, st);
+}
+
+}  // extern "C"

@@ -173,6 +173,48 @@ int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, co
 int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex, bf16* y,
                 const MoeWs& w, bool build_routes, int* status, cudaStream_t st);
 
+// prefill.cu: the expert stage of the tensor-core path on routed tokens (any
+// expert table slice; pairs whose id is outside it contribute nothing).
+struct PfExWs {
+  RouteMeta m;
+  int4* tiles;   // [P/BM + E + 1] (expert, first sorted pair, rows, 0)
+  int* ntiles;   // [1]
+  int32_t* inv;  // [P] sorted position of pair p, -1 when the pair is not local
+  bf16* xs;      // [P, H] token rows in expert order
+  bf16* act;     // [P, I] gated activations
+  bf16* ys;      // [P, H] per-pair expert outputs
+};
+int check_prefill(const ExpertsDev& d);
+size_t carve_pf_ex(Carver& c, int64_t T, int k, const ExpertsDev& d, PfExWs* w);
+// ids / wts: [T, k].  build_routes: build w.m from ids (false when the router
+// already built it).  prep: fmoe_moe_prefill_prepare's copy for this table.
+int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& d,
+                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st);
+
+// ep.cu: expert-parallel dispatch -> local experts -> combine over NCCL.
+struct EpWs {
+  RouterWs rw;                        // router scratch (MoE-block entry point only)
+  int32_t *ids, *slots, *counts, *rcounts;
+  float* wts;
+  bf16* sx;                           // [R][cap] send blocks
+  int32_t* sids;
+  float* swts;
+  bf16* rx;                           // received rows (R * cap at most)
+  int32_t* rids;
+  float* rwts;
+  bf16 *ypart, *ret;                  // partial sums: computed here | returned from the peers
+  MoeWs mw;                           // decode expert kernels, min(R * cap, 128) rows
+  PfExWs pw;                          // tensor-core expert stage (R * cap > 128)
+  bool gemm;
+};
+size_t carve_ep(Carver& c, int R, int64_t cap, const fmoe_router_t* r, int k, const ExpertsDev& d, const WsHead& h,
+                EpWs* w);
+// The slice must be experts [rank*E/n, (rank+1)*E/n) of E_total.
+int ep_check(const fmoe_ep_comm_t* c, const ExpertsDev& d, int E_total, int* n_ranks);
+int ep_experts(const fmoe_ep_comm_t* c, const bf16* x, int64_t T, int64_t cap, int k, const int32_t* ids,
+               const float* wts, const ExpertsDev& d, const bf16* prep, bf16* y, const EpWs& w, int mode, int* status,
+               cudaStream_t st);
+
 // kv.cu
 int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d);
 size_t attn_workspace_bytes(const KvDev& c, int Hq);

@@ -454,10 +454,12 @@ __global__ void tiles_kernel(const int32_t* __restrict__ start, int E, int4* __r
 }
 
 // X_sorted[i] = x[pairs[i] / k] with each 8-column word in the order 0 4 1 5 2 6 3 7;
-// inv[pairs[i]] = i.
-__global__ void gather_kernel(const bf16* __restrict__ x, const int32_t* __restrict__ pairs, int P, int k, int H,
-                              bf16* __restrict__ xs, int32_t* __restrict__ inv) {
+// inv[pairs[i]] = i, for the *nvalid pairs of local experts (inv is -1 elsewhere).
+__global__ void gather_kernel(const bf16* __restrict__ x, const int32_t* __restrict__ pairs,
+                              const int32_t* __restrict__ nvalid, int k, int H, bf16* __restrict__ xs,
+                              int32_t* __restrict__ inv) {
   const int words = H / 8;
+  const int P = *nvalid;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)P * words;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(i / words), w = (int)(i % words);
@@ -471,7 +473,7 @@ __global__ void gather_kernel(const bf16* __restrict__ x, const int32_t* __restr
   }
 }
 
-// y[t] = bf16(sum over slots of w[t, slot] * Y[inv[t * k + slot]]) in slot order.
+// y[t] = bf16(sum over local slots of w[t, slot] * Y[inv[t * k + slot]]) in slot order.
 __global__ void combine_kernel(const bf16* __restrict__ Y, const int32_t* __restrict__ inv,
                                const float* __restrict__ wts, int T, int k, int H, bf16* __restrict__ y) {
   const int words = H / 8;
@@ -480,8 +482,10 @@ __global__ void combine_kernel(const bf16* __restrict__ Y, const int32_t* __rest
     const int t = (int)(i / words), w = (int)(i % words);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int s = 0; s < k; ++s) {
+      const int j = inv[t * k + s];
+      if (j < 0) continue;
       const float wv = wts[t * k + s];
-      const uint4 v = *reinterpret_cast<const uint4*>(Y + (int64_t)inv[t * k + s] * H + 8 * w);
+      const uint4 v = *reinterpret_cast<const uint4*>(Y + (int64_t)j * H + 8 * w);
       const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -531,6 +535,8 @@ int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, c
   return FMOE_OK;
 }
 
+}  // namespace
+
 int check_prefill(const ExpertsDev& d) {
   if (d.H % 256 || d.I % 64 || d.H > 8192 || d.E < 1)
     return set_error(FMOE_ERR_UNSUPPORTED, "prefill: hidden %d (multiple of 256), intermediate %d (multiple of 64)",
@@ -542,27 +548,9 @@ int check_prefill(const ExpertsDev& d) {
   return FMOE_OK;
 }
 
-struct PfWs {
-  WsHead h;
-  RouterWs r;
-  int32_t* ids;
-  float* wts;
-  RouteMeta m;
-  int4* tiles;
-  int* ntiles;
-  int32_t* inv;
-  bf16* xs;
-  bf16* act;
-  bf16* ys;
-};
-
-size_t carve_pf(Carver& c, int64_t T, const fmoe_router_t* r, const ExpertsDev& d, PfWs* w) {
-  PfWs p;
-  p.h = carve_head(c);
-  carve_router(c, T, r, p.h, &p.r);
-  const int64_t P = T * r->top_k;
-  p.ids = c.take<int32_t>(P);
-  p.wts = c.take<float>(P);
+size_t carve_pf_ex(Carver& c, int64_t T, int k, const ExpertsDev& d, PfExWs* w) {
+  PfExWs p;
+  const int64_t P = T * k;
   p.m.start = c.take<int32_t>(d.E + 1);
   p.m.pairs = c.take<int32_t>(P);
   p.m.unique = c.take<int32_t>(d.E);
@@ -575,6 +563,99 @@ size_t carve_pf(Carver& c, int64_t T, const fmoe_router_t* r, const ExpertsDev& 
   p.xs = c.take<bf16>((size_t)P * d.H);
   p.act = c.take<bf16>((size_t)P * d.I);
   p.ys = c.take<bf16>((size_t)P * d.H);
+  if (w) *w = p;
+  return c.off;
+}
+
+int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& d,
+                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st) {
+  int rc;
+  const int64_t P = T * k;
+  if (P > (1 << 30) / d.H) return set_error(FMOE_ERR_UNSUPPORTED, "prefill: T=%lld too large", (long long)T);
+  if (build_routes && (rc = launch_route_build(ids, P, d, w.m, st))) return rc;
+  {
+    ProfScope prof_("prefill_tiles_kernel", st);
+    pf::tiles_kernel<<<1, 32, 0, st>>>(w.m.start, d.E, w.tiles, w.ntiles);
+  }
+  if ((rc = check_launch("prefill_tiles_kernel"))) return rc;
+  if (cudaMemsetAsync(w.inv, 0xFF, (size_t)P * sizeof(int32_t), st) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "prefill: memset failed");
+  {
+    ProfScope prof_("prefill_gather_kernel", st);
+    pf::gather_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(x, w.m.pairs, w.m.start + d.E, k, d.H, w.xs, w.inv);
+  }
+  if ((rc = check_launch("prefill_gather_kernel"))) return rc;
+  // tensor maps
+  pf::Maps m1, m2;
+  {
+    const cuuint64_t dA[2] = {(cuuint64_t)d.H, (cuuint64_t)P}, sA[1] = {(cuuint64_t)d.H * 2};
+    const cuuint32_t bA[2] = {64, (cuuint32_t)pf::BM};
+    const cuuint64_t dW[3] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.I, (cuuint64_t)d.E};
+    const cuuint64_t sW[2] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.stride};
+    const cuuint32_t bW[3] = {128, 128, 1};
+    if ((rc = encode(&m1.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.xs, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
+        (rc = encode(&m1.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[0], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
+                     "gate")) ||
+        (rc = encode(&m1.w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[3], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
+                     "up")))
+      return rc;
+    const cuuint64_t dA2[2] = {(cuuint64_t)d.I, (cuuint64_t)P}, sA2[1] = {(cuuint64_t)d.I * 2};
+    const cuuint64_t dW2[3] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.H, (cuuint64_t)d.E};
+    const cuuint64_t sW2[2] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.stride};
+    const cuuint32_t bW2[3] = {128, (cuuint32_t)pf::BN, 1};
+    if ((rc = encode(&m2.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.act, dA2, sA2, bA, CU_TENSOR_MAP_SWIZZLE_128B,
+                     "act")) ||
+        (rc = encode(&m2.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[6], dW2, sW2, bW2,
+                     CU_TENSOR_MAP_SWIZZLE_128B, "down")))
+      return rc;
+    m2.w1 = m2.w0;
+  }
+  const int64_t A1 = 4 * prep_q1h(d) * d.I, A2 = 4 * prep_q2h(d) * d.H;  // elements per array
+  pf::Args a1{w.tiles, w.ntiles, prep, prep_eps(d), 0, A1, 2 * A1, 3 * A1, d.H, d.I, d.E, w.act, status};
+  pf::Args a2 = a1;
+  a2.off_s0 = 4 * A1;
+  a2.off_b0 = 4 * A1 + A2;
+  a2.out = w.ys;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(pf::tc_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+    cudaFuncSetAttribute(pf::tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
+  });
+  {
+    ProfScope prof_("tc_gemm_kernel<gate_up>", st);
+    pf::tc_gemm_kernel<0><<<kNumSMs, pf::THREADS, pf::SMEM, st>>>(m1, a1);
+  }
+  if ((rc = check_launch("tc_gemm_kernel<gate_up>"))) return rc;
+  {
+    ProfScope prof_("tc_gemm_kernel<down>", st);
+    pf::tc_gemm_kernel<1><<<kNumSMs, pf::THREADS, pf::SMEM, st>>>(m2, a2);
+  }
+  if ((rc = check_launch("tc_gemm_kernel<down>"))) return rc;
+  {
+    ProfScope prof_("prefill_combine_kernel", st);
+    pf::combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(w.ys, w.inv, wts, (int)T, k, d.H, y);
+  }
+  return check_launch("prefill_combine_kernel");
+}
+
+namespace {
+
+struct PfWs {
+  WsHead h;
+  RouterWs r;
+  int32_t* ids;
+  float* wts;
+  PfExWs ex;
+};
+
+size_t carve_pf(Carver& c, int64_t T, const fmoe_router_t* r, const ExpertsDev& d, PfWs* w) {
+  PfWs p;
+  p.h = carve_head(c);
+  carve_router(c, T, r, p.h, &p.r);
+  const int64_t P = T * r->top_k;
+  p.ids = c.take<int32_t>(P);
+  p.wts = c.take<float>(P);
+  carve_pf_ex(c, T, r->top_k, d, &p.ex);
   if (w) *w = p;
   return c.off;
 }
@@ -638,70 +719,39 @@ extern "C" int fmoe_moe_prefill(const void* x, int64_t T, const fmoe_router_t* r
   carve_pf(c, T, r, d, &w);
   int32_t* ids_out = ids ? ids : w.ids;
   float* w_out = weights ? weights : w.wts;
-  // route (builds the per-expert pair lists)
-  if ((rc = run_router(static_cast<const bf16*>(x), T, r, q, w.r, ids_out, w_out, nullptr, &w.m, w.h.status, st)))
+  // route (builds the per-expert pair lists), then the expert stage
+  if ((rc = run_router(static_cast<const bf16*>(x), T, r, q, w.r, ids_out, w_out, nullptr, &w.ex.m, w.h.status, st)))
     return rc;
-  {
-    ProfScope prof_("prefill_tiles_kernel", st);
-    pf::tiles_kernel<<<1, 32, 0, st>>>(w.m.start, d.E, w.tiles, w.ntiles);
-  }
-  if ((rc = check_launch("prefill_tiles_kernel"))) return rc;
-  {
-    ProfScope prof_("prefill_gather_kernel", st);
-    pf::gather_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(static_cast<const bf16*>(x), w.m.pairs, (int)P, k, d.H, w.xs,
-                                                        w.inv);
-  }
-  if ((rc = check_launch("prefill_gather_kernel"))) return rc;
-  // tensor maps
-  pf::Maps m1, m2;
-  {
-    const cuuint64_t dA[2] = {(cuuint64_t)d.H, (cuuint64_t)P}, sA[1] = {(cuuint64_t)d.H * 2};
-    const cuuint32_t bA[2] = {64, (cuuint32_t)pf::BM};
-    const cuuint64_t dW[3] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.I, (cuuint64_t)d.E};
-    const cuuint64_t sW[2] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.stride};
-    const cuuint32_t bW[3] = {128, 128, 1};
-    if ((rc = encode(&m1.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.xs, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
-        (rc = encode(&m1.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[0], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
-                     "gate")) ||
-        (rc = encode(&m1.w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[3], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
-                     "up")))
-      return rc;
-    const cuuint64_t dA2[2] = {(cuuint64_t)d.I, (cuuint64_t)P}, sA2[1] = {(cuuint64_t)d.I * 2};
-    const cuuint64_t dW2[3] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.H, (cuuint64_t)d.E};
-    const cuuint64_t sW2[2] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.stride};
-    const cuuint32_t bW2[3] = {128, (cuuint32_t)pf::BN, 1};
-    if ((rc = encode(&m2.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.act, dA2, sA2, bA, CU_TENSOR_MAP_SWIZZLE_128B,
-                     "act")) ||
-        (rc = encode(&m2.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[6], dW2, sW2, bW2,
-                     CU_TENSOR_MAP_SWIZZLE_128B, "down")))
-      return rc;
-    m2.w1 = m2.w0;
-  }
-  const int64_t A1 = 4 * prep_q1h(d) * d.I, A2 = 4 * prep_q2h(d) * d.H;  // elements per array
-  pf::Args a1{w.tiles, w.ntiles, static_cast<const bf16*>(prep), prep_eps(d), 0, A1, 2 * A1, 3 * A1,
-              d.H, d.I, d.E, w.act, w.h.status};
-  pf::Args a2 = a1;
-  a2.off_s0 = 4 * A1;
-  a2.off_b0 = 4 * A1 + A2;
-  a2.out = w.ys;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(pf::tc_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-    cudaFuncSetAttribute(pf::tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, pf::SMEM);
-  });
-  {
-    ProfScope prof_("tc_gemm_kernel<gate_up>", st);
-    pf::tc_gemm_kernel<0><<<kNumSMs, pf::THREADS, pf::SMEM, st>>>(m1, a1);
-  }
-  if ((rc = check_launch("tc_gemm_kernel<gate_up>"))) return rc;
-  {
-    ProfScope prof_("tc_gemm_kernel<down>", st);
-    pf::tc_gemm_kernel<1><<<kNumSMs, pf::THREADS, pf::SMEM, st>>>(m2, a2);
-  }
-  if ((rc = check_launch("tc_gemm_kernel<down>"))) return rc;
-  {
-    ProfScope prof_("prefill_combine_kernel", st);
-    pf::combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(w.ys, w.inv, w_out, (int)T, k, d.H, static_cast<bf16*>(y));
-  }
-  return check_launch("prefill_combine_kernel");
+  return run_prefill_experts(static_cast<const bf16*>(x), T, k, ids_out, w_out, d, static_cast<const bf16*>(prep),
+                             static_cast<bf16*>(y), w.ex, false, w.h.status, st);
+}
+
+extern "C" size_t fmoe_moe_prefill_experts_workspace_bytes(int64_t T, int top_k, const fmoe_experts_t* ex) {
+  ExpertsDev d;
+  if (T <= 0 || top_k < 1 || top_k > 16 || to_experts(ex, &d) || check_prefill(d)) return 0;
+  Carver c(nullptr);
+  carve_head(c);
+  return carve_pf_ex(c, T, top_k, d, nullptr) + 256;
+}
+
+extern "C" int fmoe_moe_prefill_experts(const void* x, int64_t T, int top_k, const int32_t* ids, const float* weights,
+                                        const fmoe_experts_t* ex, const void* prep, void* y, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  ExpertsDev d;
+  int rc;
+  if ((rc = to_experts(ex, &d)) || (rc = check_prefill(d))) return rc;
+  if (!x || !ids || !weights || !y || !prep)
+    return set_error(FMOE_ERR_INVALID, "prefill_experts: null x / ids / weights / y / prepared scales");
+  if (top_k < 1 || top_k > 16) return set_error(FMOE_ERR_INVALID, "prefill_experts: top_k %d", top_k);
+  if (T <= 0) return FMOE_OK;
+  if (!aligned(x, 16) || !aligned(y, 16)) return set_error(FMOE_ERR_ALIGN, "prefill_experts: x / y not 16-byte aligned");
+  const size_t need = fmoe_moe_prefill_experts_workspace_bytes(T, top_k, ex);
+  if (!workspace || workspace_bytes < need)
+    return set_error(FMOE_ERR_WORKSPACE, "prefill_experts: workspace %zu < %zu", workspace_bytes, need);
+  Carver c(workspace);
+  const WsHead h = carve_head(c);
+  PfExWs w;
+  carve_pf_ex(c, T, top_k, d, &w);
+  return run_prefill_experts(static_cast<const bf16*>(x), T, top_k, ids, weights, d, static_cast<const bf16*>(prep),
+                             static_cast<bf16*>(y), w, true, h.status, static_cast<cudaStream_t>(stream));
 }

@@ -7,7 +7,9 @@
 Two execution paths, both capturable in one CUDA graph with the decode
 position kept on the device:
   decode_step        one library call per layer (fmoe_decoder_layer_forward:
-                     11 kernels chained on the stream), any batch 1..8;
+                     11 kernels chained on the stream), any batch 1..8; with an
+                     EPComm the layers hold expert slices and the routed experts
+                     run on their owning GPUs (fmoe_decoder_layer_forward_ep);
   decode_step_fused  the whole step as one persistent kernel
                      (fmoe_decode_step), batch 1.
 """
@@ -104,10 +106,25 @@ class Gemma4DecoderLayer:
                                                _ptr(pos_dev), _ptr(workspace), workspace.numel(), _stream()))
         return x
 
+    def ep_workspace_bytes(self, T, cache: KVCache, world: int, cap: int) -> int:
+        return lib().fmoe_decoder_ep_workspace_bytes(T, ctypes.byref(self.cstruct()), ctypes.byref(cache.c), world,
+                                                     cap)
+
+    def forward_ep(self, comm, cap: int, x: torch.Tensor, cache: KVCache, pos: int, workspace: torch.Tensor,
+                   pos_dev=None, mode=0, prepared=None):
+        """forward() with this layer's experts being this rank's slice: the routed
+        experts run on their owning ranks (fmoe_decoder_layer_forward_ep)."""
+        T = x.shape[0]
+        check(lib().fmoe_decoder_layer_forward_ep(ctypes.byref(self.cstruct()), ctypes.byref(cache.c), comm.handle,
+                                                  cap, _ptr(prepared), mode, _ptr(x), T, pos, _ptr(pos_dev),
+                                                  _ptr(workspace), workspace.numel(), _stream()))
+        return x
+
     __call__ = forward
 
     @classmethod
-    def random(cls, cfg, full: bool, seed: int, device, experts=None):
+    def random(cls, cfg, full: bool, seed: int, device, experts=None, ep=None):
+        """Random-init layer; ep (an EPComm): keep only this rank's expert slice."""
         g = torch.Generator(device=device).manual_seed(seed)
         H = cfg["hidden"]
         D = cfg["full_head_dim"] if full else cfg["sliding_head_dim"]
@@ -134,6 +151,8 @@ class Gemma4DecoderLayer:
                   "per_expert_scale": norm(cfg["experts"]), "root_size": H ** -0.5}
         if experts is None:
             experts = ExpertTable.random(cfg["experts"], H, cfg["expert_inter"], seed=seed + 1, device=device)
+            if ep is not None:
+                experts = experts.shard(ep.rank, ep.world, copy=True)
         rope_dims = int(D * cfg["full_partial_rotary"]) if full else D
         theta = cfg["full_theta"] if full else cfg["sliding_theta"]
         return cls(q, k, v, o, norm(D), norm(D), norms, mlp, router, experts, Hq, Hkv, D, rope_dims, theta, full,
@@ -146,7 +165,7 @@ class Gemma4Model:
     caches, final norm and the tied 6-bit lm_head with softcap; greedy decode."""
 
     def __init__(self, cfg, embed: QuantizedLinear, layers, final_norm, batch, max_positions, kv_mode=KV_BF16,
-                 device=None):
+                 device=None, ep=None, ep_cap=None):
         self.cfg = cfg
         self.embed = embed
         self.layers = layers
@@ -162,7 +181,12 @@ class Gemma4Model:
             else:
                 c = KVCache(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
             self.caches.append(c)
-        ws = max(L.workspace_bytes(batch, c) for L, c in zip(layers, self.caches))
+        self.ep = ep
+        self.ep_cap = batch if ep_cap is None else ep_cap
+        if ep is None:
+            ws = max(L.workspace_bytes(batch, c) for L, c in zip(layers, self.caches))
+        else:
+            ws = max(L.ep_workspace_bytes(batch, c, ep.world, self.ep_cap) for L, c in zip(layers, self.caches))
         if ws == 0:
             raise ValueError("decoder: unsupported layer / cache configuration")
         self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)
@@ -178,9 +202,12 @@ class Gemma4Model:
         self._fc = None
 
     @classmethod
-    def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None):
+    def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None, ep=None,
+               ep_cap=None):
+        """Random-init model.  ep (an EPComm): every layer keeps only this rank's
+        expert slice and decode_step runs the routed experts on their owners."""
         n_layers = cfg["layers"] if n_layers is None else n_layers
-        layers = [Gemma4DecoderLayer.random(cfg, layer_is_full(cfg, i), seed + 100 * i, device)
+        layers = [Gemma4DecoderLayer.random(cfg, layer_is_full(cfg, i), seed + 100 * i, device, ep=ep)
                   for i in range(n_layers)]
         g = torch.Generator(device=device).manual_seed(seed + 7)
         rows = []
@@ -200,10 +227,12 @@ class Gemma4Model:
             rows.append(None)
         embed = QuantizedLinear(wq, sc, bi, cfg["embed_bits"], 64, in_features=H)
         final_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
-        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device)
+        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device, ep, ep_cap)
 
     def _fused(self):
         if self._fc is None:
+            if self.ep is not None:
+                raise ValueError("decode_step_fused: all experts must be local")
             if self.batch != 1:
                 raise ValueError("decode_step_fused: batch 1 only")
             n = len(self.layers)
@@ -248,7 +277,10 @@ class Gemma4Model:
                                     _stream()))
         pd = self.pos_dev if device_pos else None
         for L, cache in zip(self.layers, self.caches):
-            L.forward(self.x, cache, self.pos, self.ws, pd)
+            if self.ep is None:
+                L.forward(self.x, cache, self.pos, self.ws, pd)
+            else:
+                L.forward_ep(self.ep, self.ep_cap, self.x, cache, self.pos, self.ws, pd)
         check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(self.x), self.batch,
                                  self.cfg["softcap"], _ptr(self.logits), _ptr(self.ids), _ptr(pd), _ptr(self.lm_ws),
                                  self.lm_ws.numel(), _stream()))

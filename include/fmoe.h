@@ -345,6 +345,66 @@ int fmoe_moe_prefill(const void* x, int64_t T, const fmoe_router_t* router, cons
                      const void* prepared, void* y, int32_t* ids, float* weights, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* The expert stage of fmoe_moe_prefill on given routing (the tensor-core
+ * counterpart of fmoe_moe_experts): ids int32 / weights f32 [T, top_k] hold
+ * global expert ids; pairs whose id lies outside the table's
+ * [first_expert, first_expert + num_experts) contribute nothing, so the table
+ * may be one rank's slice.  prepared: fmoe_moe_prefill_prepare of this table. */
+size_t fmoe_moe_prefill_experts_workspace_bytes(int64_t T, int top_k, const fmoe_experts_t* experts);
+int fmoe_moe_prefill_experts(const void* x, int64_t T, int top_k, const int32_t* ids, const float* weights,
+                             const fmoe_experts_t* experts, const void* prepared, void* y, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* ---- expert parallelism (one process per GPU, NCCL over NVLink) ----------
+ * Not in the reference, which runs on one device (moe.rs:361-466 evaluates
+ * every routed expert locally): the E experts of a layer are split
+ * contiguously over n_ranks GPUs — rank r passes the fmoe_experts_t of experts
+ * [r*E/n, (r+1)*E/n) with first_expert = r*E/n — while router weights are
+ * replicated and each rank routes its own T tokens.  One MoE block: router ->
+ * dispatch (a token's row, ids and weights cross once to every rank owning
+ * one of its experts) -> local experts -> the per-rank partial sums return ->
+ * y = their sum in ascending rank order.  Transport: grouped ncclSend /
+ * ncclRecv from libnccl.so.2, resolved at run time.  Every rank of the
+ * communicator must make the same sequence of fmoe_ep_* calls with the same
+ * cap and mode (a rank without tokens passes T = 0). */
+typedef struct fmoe_ep_comm fmoe_ep_comm_t;
+
+#define FMOE_EP_UNIQUE_ID_BYTES 128
+#define FMOE_EP_FIXED 0 /* every rank exchanges cap rows with every rank: no host sync, CUDA-graph capturable */
+#define FMOE_EP_EXACT 1 /* counts cross first (one host sync per block), then only the routed rows */
+
+/* Rank 0 makes the id; the host engine hands it to the other ranks. */
+int fmoe_ep_unique_id(void* id, size_t len);
+/* Blocking: returns when all n_ranks have joined (current CUDA device). */
+int fmoe_ep_comm_init(fmoe_ep_comm_t** comm, int n_ranks, int rank, const void* id, size_t len);
+int fmoe_ep_comm_destroy(fmoe_ep_comm_t* comm);
+/* For a host watchdog: ends outstanding NCCL work with an error and frees comm. */
+int fmoe_ep_comm_abort(fmoe_ep_comm_t* comm);
+/* FMOE_OK, or FMOE_ERR_NCCL when NCCL has recorded an asynchronous error. */
+int fmoe_ep_comm_status(fmoe_ep_comm_t* comm);
+
+/* cap: the largest T any rank passes (FIXED exchanges cap rows per peer).
+ * Received rows are served by the decode expert kernels up to 128 rows, by the
+ * tensor-core path above (prepared = fmoe_moe_prefill_prepare of the local
+ * slice; required when n_ranks * cap > 128).  ids / weights (optional) receive
+ * this rank's routing.  Workspace: zero-filled once before first use. */
+size_t fmoe_ep_moe_workspace_bytes(int n_ranks, int64_t cap, const fmoe_router_t* router,
+                                   const fmoe_experts_t* local);
+int fmoe_ep_moe_forward(fmoe_ep_comm_t* comm, const void* x, int64_t T, int64_t cap, const fmoe_router_t* router,
+                        const fmoe_experts_t* local, const void* prepared, void* y, int32_t* ids, float* weights,
+                        int mode, void* workspace, size_t workspace_bytes, void* stream);
+
+/* fmoe_decoder_layer_forward with layer->experts being this rank's slice: the
+ * routed experts of the MoE block run on their owning ranks as in
+ * fmoe_ep_moe_forward (cap >= T on every rank; prepared as there).  Attention,
+ * dense MLP and router stay local. */
+size_t fmoe_decoder_ep_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache,
+                                       int n_ranks, int64_t cap);
+int fmoe_decoder_layer_forward_ep(const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache,
+                                  fmoe_ep_comm_t* comm, int64_t cap, const void* prepared, int mode, void* x,
+                                  int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* ---- whole decode step (batch 1) ----------------------------------------
  * One persistent kernel per generated token: embedding row, every decoder
  * layer (as fmoe_decoder_layer_forward), final norm, tied lm_head, softcap and

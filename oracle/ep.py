@@ -1,0 +1,108 @@
+"""Expert-parallel exchange — CPU restatement, TEST INFRASTRUCTURE ONLY.
+
+The reference runs every routed expert on one device (Gemma4MoeBlock::forward,
+src/model/moe.rs:361-466); its answer for a token is the oracle's
+moe_experts().  This file restates, in numpy, the split that libfmoe's
+expert-parallel path performs (experts contiguous over R ranks, a token sent
+once to each rank that owns one of its experts, per-rank partial sums rounded
+to bf16 and added back in ascending rank order), so that tests can check the
+exchange layout rank by rank and the whole split against the single-device
+answer.  Only tests/ use it.
+
+Layout (the same as the library's):
+    slots[r, t]  position of token t in rank r's block, -1 if none of its
+                 experts is on r; positions count earlier tokens routed to r
+    counts[r]    tokens routed to rank r
+    send blocks  [R, cap, .]: rows 0..counts[r]-1 in slot order; the id rows of
+                 the padding (counts[r]..cap-1) are -1
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import bf16_to_f32, f32_to_bf16, moe_experts
+
+
+def plan(ids: np.ndarray, R: int, per_rank: int, cap: int):
+    """-> slots int32 [R, cap] (-1 past T), counts int32 [R]."""
+    T = ids.shape[0]
+    owner = ids // per_rank  # [T, k]; ids < 0 give owner < 0
+    slots = np.full((R, cap), -1, np.int32)
+    counts = np.zeros(R, np.int32)
+    for r in range(R):
+        hit = np.any((owner == r) & (ids >= 0), axis=1)
+        pos = np.cumsum(hit) - 1
+        slots[r, :T] = np.where(hit, pos, -1)
+        counts[r] = int(hit.sum())
+    return slots, counts
+
+
+def pack(x: np.ndarray, ids: np.ndarray, wts: np.ndarray, slots: np.ndarray, counts: np.ndarray, cap: int):
+    """-> send_x uint16 [R, cap, H], send_ids int32 [R, cap, k], send_wts f32 [R, cap, k]."""
+    R = slots.shape[0]
+    T, H = x.shape
+    k = ids.shape[1] if ids.ndim == 2 else 0
+    sx = np.zeros((R, cap, H), np.uint16)
+    sids = np.full((R, cap, k), -1, np.int32)
+    swts = np.zeros((R, cap, k), np.float32)
+    for r in range(R):
+        for t in range(T):
+            s = slots[r, t]
+            if s >= 0:
+                sx[r, s] = x[t]
+                sids[r, s] = ids[t]
+                swts[r, s] = wts[t]
+    return sx, sids, swts
+
+
+def local_partial(rx: np.ndarray, rids: np.ndarray, rwts: np.ndarray, buf: np.ndarray, stride: int, offsets,
+                  hidden: int, inter: int, first: int, n: int) -> np.ndarray:
+    """bf16 [rows, H]: sum over the row's experts in [first, first + n) of
+    w * expert(x) (ascending expert id), rounded to bf16 once; rows with no
+    local expert give 0.  buf is the WHOLE table (global ids index it)."""
+    rows = rx.shape[0]
+    out = np.zeros((rows, hidden), np.uint16)
+    if rows == 0:
+        return out
+    local = (rids >= first) & (rids < first + n)
+    ids = np.where(local, rids, first).astype(np.int32)   # non-local slots: weight 0 on a local expert
+    w = np.where(local, rwts, 0.0).astype(np.float32)
+    keep = local.any(axis=1)
+    if keep.any():
+        _, y16 = moe_experts(rx[keep], ids[keep], w[keep], buf, stride, offsets, hidden, inter)
+        out[keep] = y16
+    return out
+
+
+def combine(ret: np.ndarray, slots: np.ndarray, T: int) -> np.ndarray:
+    """y bf16 [T, H] = bf16(sum over r ascending of ret[r, slots[r, t]]) (fp32 sums)."""
+    R, _, H = ret.shape
+    acc = np.zeros((T, H), np.float32)
+    for r in range(R):
+        for t in range(T):
+            s = slots[r, t]
+            if s >= 0:
+                acc[t] += bf16_to_f32(ret[r, s])
+    return f32_to_bf16(acc)
+
+
+def simulate(xs, idss, wtss, R: int, buf, stride, offsets, hidden: int, inter: int, num_experts: int, cap: int):
+    """The whole exchange for R ranks in one process: xs / idss / wtss are the
+    per-rank token rows and routing.  Returns the per-rank outputs (bf16)."""
+    per = num_experts // R
+    plans = [plan(ids, R, per, cap) for ids in idss]
+    sends = [pack(x, ids, w, s, c, cap) for x, ids, w, (s, c) in zip(xs, idss, wtss, plans)]
+    # dispatch: rank p receives block p of every sender q (only counts[p] rows matter)
+    parts = []
+    for p in range(R):
+        rx = np.concatenate([sends[q][0][p] for q in range(R)])
+        rids = np.concatenate([sends[q][1][p] for q in range(R)])
+        rwts = np.concatenate([sends[q][2][p] for q in range(R)])
+        parts.append(local_partial(rx, rids, rwts, buf, stride, offsets, hidden, inter, p * per, per)
+                     .reshape(R, cap, hidden))
+    # combine: sender q gets, from every p, the partials of its own block p
+    outs = []
+    for q in range(R):
+        ret = np.stack([parts[p][q] for p in range(R)])
+        outs.append(combine(ret, plans[q][0], xs[q].shape[0]))
+    return outs

@@ -1,0 +1,218 @@
+"""GPU parity of the expert-parallel MoE block and decoder (fmoe_ep_* /
+fmoe_decoder_layer_forward_ep) against the CPU oracle and the single-device
+path.
+
+One GPU: a one-rank NCCL communicator runs the whole exchange (plan, pack,
+grouped send/recv to itself, local experts, return, combine).  Two GPUs (when
+present): one process per GPU, 64 experts each; every rank checks its own
+tokens against the single-device block holding all 128 experts.
+
+Routing ids must equal the single-device ones; outputs within max |a - b| /
+max |b| <= 1e-2 of the oracle (evaluated on the GPU's routing).  With one rank
+the partial sum is the single-device sum, so decode outputs are bit-identical.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from gpu_util import max_rel_err, to_np_bf16
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+H, I, E, K = 2816, 704, 128, 8
+
+
+@pytest.fixture(scope="module")
+def comm1(fm, dev):
+    c = fm.EPComm(rank=0, world=1)
+    yield c
+    torch.cuda.synchronize()
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def layer(fm, dev):
+    table = fm.ExpertTable.random(E, H, I, seed=2002, device=dev)
+    g = torch.Generator(device=dev).manual_seed(2002)
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(E, generator=g, device=dev)
+    return table, wr, bias, table.buf.cpu().numpy()
+
+
+def _oracle(orc, table, host, x, ids, w):
+    y32, _ = orc.moe_experts(to_np_bf16(x), ids.cpu().numpy(), w.cpu().numpy(), host, table.stride, table.offsets,
+                             table.hidden, table.inter)
+    return y32
+
+
+@pytest.mark.parametrize("T,cap,mode", [(5, 8, 0), (64, 64, 1), (300, 300, 0), (200, 256, 1), (0, 4, 0)])
+def test_ep_one_rank_matches_oracle(fm, orc, dev, comm1, layer, T, cap, mode):
+    table, wr, bias, host = layer
+    g = torch.Generator(device=dev).manual_seed(700 + T)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    router = fm.QuantizedLinear(wr, bits=16)
+    ep = fm.ExpertParallelMoeBlock(comm1, router, table.shard(0, 1), cap=cap, top_k=K, mode=mode, logit_bias=bias)
+    y, ids, w = ep.forward(x, return_routing=True)
+    torch.cuda.synchronize()
+    comm1.status()
+    assert y.shape == (T, H)
+    if T == 0:
+        return
+    ref = fm.Gemma4MoeBlock(router, table, top_k=K, logit_bias=bias)
+    r_ids, r_w, _ = ref.route(x)
+    assert torch.equal(ids, r_ids) and torch.equal(w, r_w)
+    err = max_rel_err(y.float().cpu().numpy(), _oracle(orc, table, host, x, ids, w))
+    assert err <= TOL, err
+    assert torch.equal(y, ep.forward(x))  # deterministic
+
+
+def _decoder_pair(fm, dev, comm):
+    cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=2)
+    ctx = 300
+    m1 = fm.Gemma4Model.random(cfg, batch=1, max_positions=1024, seed=21, device=dev, n_layers=2)
+    m2 = fm.Gemma4Model(cfg, m1.embed, m1.layers, m1.final_norm, 1, 1024, device=dev, ep=comm)
+    g = torch.Generator(device=dev).manual_seed(22)
+    for L, c1, c2 in zip(m1.layers, m1.caches, m2.caches):
+        kv = torch.randn(2, 1, L.num_kv_heads, ctx, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+        c1.update(kv[0], kv[1])
+        c2.update(kv[0], kv[1])
+    for m in (m1, m2):
+        m.ids.fill_(5)
+        m.set_position(ctx)
+    want = [(m1.decode_step().clone(), m1.logits.clone()) for _ in range(3)]
+    torch.cuda.synchronize()
+    return m2, want
+
+
+def test_ep_decoder_one_rank_is_the_local_decoder(fm, dev, comm1):
+    """Two decoder layers: the expert-parallel layer call with one rank gives
+    bit-identical tokens and logits to the local call."""
+    m2, want = _decoder_pair(fm, dev, comm1)
+    got = []
+    for _ in range(3):
+        got.append((m2.decode_step().clone(), m2.logits.clone()))
+    torch.cuda.synchronize()
+    comm1.status()
+    for step, ((gi, gl), (wi, wl)) in enumerate(zip(got, want)):
+        assert torch.equal(gl, wl), (step, float((gl - wl).abs().max()))
+        assert torch.equal(gi, wi), step
+
+
+def test_ep_decoder_graph_replay(fm, dev, comm1):
+    """The same from a CUDA graph that captured the NCCL exchanges (position on
+    the device).  The graph is released before any check, so a failure cannot
+    leave the communicator with captured work outstanding."""
+    m2, want = _decoder_pair(fm, dev, comm1)
+    got = []
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.stream(s):
+            ids0, pos0 = m2.ids.clone(), m2.pos_dev.clone()
+            m2.decode_step(device_pos=True)  # outside capture: library attribute setup
+            torch.cuda.synchronize()
+            m2.ids.copy_(ids0)
+            m2.pos_dev.copy_(pos0)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=s, capture_error_mode="thread_local"):
+                m2.decode_step(device_pos=True)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(3):
+            graph.replay()
+            torch.cuda.synchronize()
+            got.append((m2.ids.clone(), m2.logits.clone()))
+    finally:
+        torch.cuda.synchronize()
+        del graph
+        torch.cuda.synchronize()
+    comm1.status()
+    for step, ((gi, gl), (wi, wl)) in enumerate(zip(got, want)):
+        assert torch.equal(gl, wl), (step, float((gl - wl).abs().max()))
+        assert torch.equal(gi, wi), step
+
+
+# ---------------------------------------------------------------------------
+# two GPUs, one process each
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _two_rank_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    try:
+        fm = __graft_entry__.load_package()
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        comm = fm.EPComm()
+        table = fm.ExpertTable.random(E, H, I, seed=2002, device=dev)  # the same on every rank
+        g = torch.Generator(device=dev).manual_seed(2002)
+        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        bias = torch.randn(E, generator=g, device=dev)
+        router = fm.QuantizedLinear(wr, bits=16)
+        ref = fm.Gemma4MoeBlock(router, table, top_k=K, logit_bias=bias)
+        errs = []
+        for T, cap, mode in [(4, 4, 0), (3, 4, 1), (200, 256, 0), (150, 256, 1)]:
+            Tr = T if rank == 0 else max(T - 1, 0)  # ragged token counts
+            gx = torch.Generator(device=dev).manual_seed(900 + 10 * T + rank)
+            x = torch.randn(Tr, H, generator=gx, device=dev).to(torch.bfloat16)
+            ep = fm.ExpertParallelMoeBlock(comm, router, table.shard(rank, world), cap=cap, top_k=K, mode=mode,
+                                           logit_bias=bias)
+            y, ids, w = ep.forward(x, return_routing=True)
+            want, r_ids, _ = ref.forward(x, return_routing=True) if Tr <= 128 else ref.forward_prefill(
+                x, return_routing=True)
+            torch.cuda.synchronize()
+            same = bool(torch.equal(ids, r_ids))
+            errs.append((T, mode, same, max_rel_err(y.float().cpu().numpy(), want.float().cpu().numpy())))
+        comm.status()
+        torch.cuda.synchronize()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, errs, None))
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_ranks_match_single_device():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    env_nvls = os.environ.get("NCCL_NVLS_ENABLE")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    try:
+        for p in procs:
+            p.start()
+        res = {}
+        for _ in range(2):
+            rank, errs, exc = q.get(timeout=600)
+            res[rank] = (errs, exc)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+        if env_nvls is None:
+            os.environ.pop("NCCL_NVLS_ENABLE", None)
+        else:
+            os.environ["NCCL_NVLS_ENABLE"] = env_nvls
+    for rank, (errs, exc) in res.items():
+        assert exc is None, f"rank {rank}: {exc}"
+        for T, mode, same, err in errs:
+            assert same, (rank, T, mode)
+            assert err <= TOL, (rank, T, mode, err)
