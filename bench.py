@@ -44,6 +44,8 @@ ROUTER_BYTES = E * H * 2                                   # bf16 router weight 
 GATE_UP_BYTES = 2 * (I * H // 2 + 2 * I * (H // 64) * 2)   # per selected expert: 2,230,272
 DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert: 1,115,136
 WORKLOADS = {"decode30_b1": 1, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
+# total tokens per step (split evenly over the GPUs), default exchange mode
+EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "fixed"), "ep_moe30_prefill_8192": (8192, "exact")}
 CTX = 2048                                                 # decode context (positions in every KV cache)
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES                  # 3,345,408
 
@@ -54,7 +56,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode30_b1", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode30_b1", choices=sorted(WORKLOADS) + sorted(EP_WORKLOADS))
+    ap.add_argument("--ep-mode", default=None, choices=["fixed", "exact"],
+                    help="expert-parallel exchange of the ep_* workloads (default: fixed for decode, exact for "
+                         "prefill)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
     ap.add_argument("--qlinear-case", default=None, metavar="OUT:IN:BITS:T",
@@ -98,10 +103,15 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        self.first = ""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # the timed region starts once sampling runs (the first line is printed)
+            import select
+            if select.select([self.proc.stdout], [], [], 5.0)[0]:
+                self.first = self.proc.stdout.readline()
         except Exception:
             self.proc = None
         return self
@@ -114,6 +124,8 @@ class ClockSampler:
                 self.out, _ = self.proc.communicate(timeout=5)
             except Exception:
                 self.proc.kill()
+        if not self.out.strip():
+            self.out = self.first  # a region shorter than one period: the sample taken as it began
 
     def summary(self):
         sms, maxs, reasons = [], [], set()
@@ -211,14 +223,17 @@ def run_decoder(args, rank, world, local):
     fm.lib()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    ep = None
     if world > 1:
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        ep = fm.EPComm()  # experts split E / world per GPU, exchanged over NVLink
     T = WORKLOADS[args.workload]
     cfg = dict(fm.GEMMA4_26B)
-    m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000 + rank, device=dev,
-                              n_layers=args.layers)
+    # the same weights on every rank (each keeps its expert slice); per-rank sequences
+    m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
+                              ep=ep)
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
     for L, c in zip(m.layers, m.caches):
         chunk = 256
@@ -251,7 +266,7 @@ def run_decoder(args, rank, world, local):
         m.ids.copy_(ids0)
         m.set_position(CTX)
         torch.cuda.synchronize()
-        with torch.cuda.graph(graph, stream=stream):
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
             m.decode_step(device_pos=True)
 
     def timed(n, e2e, host_in=None, host_out=None):
@@ -303,6 +318,10 @@ def run_decoder(args, rank, world, local):
                  "moe_gate_up_kernel": parts["experts"] * 2 / 3, "moe_down_kernel": parts["experts"] / 3}
     alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
+    par = "single GPU" if world == 1 else (
+        f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined by NCCL "
+        f"send/recv over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
+        f"replicated; one sequence per GPU")
     result = {
         "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
         "value": round(value, 2),
@@ -320,13 +339,13 @@ def run_decoder(args, rank, world, local):
         "config": {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
                    "batch": T, "context": CTX, "kv_cache": "bf16", "attention_bits": 8, "expert_bits": 4,
                    "dense_bits": 4, "embed_bits": 6, "router": "bf16",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": par,
                    "l2": "weights (about 15 GB) far larger than L2; no flush",
                    "graph": "one CUDA graph per step, position on the device"},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * 4,
                 "d2h_bytes_per_step": T * 4,
-                "api": "Gemma4Model.decode_step (embedding, fmoe_decoder_layer_forward x30, fmoe_lm_head) "
-                       "captured in a CUDA graph + pinned host copies of the token ids"},
+                "api": "Gemma4Model.decode_step (embedding, fmoe_decoder_layer_forward%s x30, fmoe_lm_head) "
+                       "captured in a CUDA graph + pinned host copies of the token ids" % ("_ep" if ep else "")},
         "gpu_launches": launches_per_step * args.steps,
         "step_alg_bytes": int(step_bytes),
         "step_alg_bytes_parts": {k: int(v) for k, v in parts.items()},
@@ -345,7 +364,10 @@ def run_decoder(args, rank, world, local):
                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
         "clocks": clocks.summary(),
     }
-    del graph
+    del graph  # graphs holding NCCL work go before the communicators
+    torch.cuda.synchronize()
+    if ep is not None:
+        ep.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_decoder_baseline(T)
     if rank == 0:
@@ -508,6 +530,183 @@ def run_ours(args, rank, world, local):
     del graph
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# expert parallelism: the MoE half of the 30-layer model
+# with its 128 experts split over the GPUs, total tokens fixed (strong scaling)
+
+
+def run_ep_moe(args, rank, world, local):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    fm.lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    total, mode_name = EP_WORKLOADS[args.workload]
+    mode_name = args.ep_mode or mode_name
+    mode = fm.FMOE_EP_FIXED if mode_name == "fixed" else fm.FMOE_EP_EXACT
+    if total % world or E % world:
+        raise SystemExit(f"{total} tokens / {E} experts do not split over {world} GPUs")
+    T = total // world
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    comm = fm.EPComm()
+    nl = args.layers
+    g = torch.Generator(device=dev)
+    shared = fm._Workspace()  # one exchange workspace for every layer (calls are sequential)
+    blocks = []
+    for l in range(nl):
+        g.manual_seed(6000 + l)
+        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        bias = torch.randn(E, generator=g, device=dev)  # config 2's Zipf-like per-expert skew
+        table = fm.ExpertTable.random(E, H, I, seed=7000 + l, device=dev).shard(rank, world, copy=True)
+        b = fm.ExpertParallelMoeBlock(comm, fm.QuantizedLinear(wr, bits=16), table, cap=T, top_k=K, mode=mode,
+                                      logit_bias=bias)
+        b._ws = shared
+        blocks.append(b)
+        torch.cuda.empty_cache()
+    gx = torch.Generator(device=dev).manual_seed(5000 + rank)
+    x = torch.randn(T, H, generator=gx, device=dev).to(torch.bfloat16)
+    ys = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for _ in range(nl)]
+    ids = [None] * nl
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+
+    def step(keep_ids=False):
+        for l, b in enumerate(blocks):
+            if keep_ids:
+                _, ids[l], _ = b.forward(x, return_routing=True, out=ys[l])
+            else:
+                b.forward(x, out=ys[l])
+
+    with torch.cuda.stream(stream):
+        step(keep_ids=True)
+        torch.cuda.synchronize()
+        fm.profile_read(reset=True)
+        fm.profile_enable(True)
+        nprof = 2
+        for _ in range(nprof):
+            step()
+        torch.cuda.synchronize()
+        fm.profile_enable(False)
+    prof = fm.profile_read(reset=True)
+    launches_per_step = sum(v[0] for v in prof.values()) // nprof
+    # pairs each rank computes: every rank's routing, counted on the expert owners
+    all_ids = torch.stack(ids)  # [layers, T, K]
+    if world > 1:
+        gathered = [torch.empty_like(all_ids) for _ in range(world)]
+        dist.all_gather(gathered, all_ids)
+        all_ids = torch.cat(gathered, dim=1)
+    per = E // world
+    local = (all_ids >= rank * per) & (all_ids < (rank + 1) * per)
+    pairs_local = int(local.sum()) / nl
+    uniq_local = sum(int(torch.unique(all_ids[l][local[l]]).numel()) for l in range(nl)) / nl
+
+    graph = None
+    if mode == fm.FMOE_EP_FIXED:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+                step()
+
+    def timed(n, e2e, host_in=None, host_out=None):
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for i in range(n):
+                if e2e:
+                    x.copy_(host_in, non_blocking=True)
+                if graph is not None:
+                    graph.replay()
+                else:
+                    step()
+                if e2e:
+                    host_out.copy_(ys[-1], non_blocking=True)
+            stop.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(stop)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(args.warmup, False)
+    clocks = ClockSampler(local)
+    with clocks:
+        ms = timed(args.steps, False)
+    host_in = x.cpu().pin_memory()
+    host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    timed(min(args.warmup, 3), True, host_in, host_out)
+    ms_e2e = timed(args.steps, True, host_in, host_out)
+    ms_step = ms / args.steps
+    value = total / (ms_step / 1e3)
+    e2e_value = total / (ms_e2e / args.steps / 1e3)
+
+    peaks, peaks_kind = load_peaks()
+    name, (n_l, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+    avg_s = tot_ms / n_l / 1e3
+    prefill = total > 1024
+    if name.startswith("tc_gemm_kernel") and prefill:  # tensor-bound: fp32-accumulated bf16 MMA FLOPs
+        fl = 2 * pairs_local * H * 2 * I if "gate_up" in name else 2 * pairs_local * I * H
+        roof = {"bound": "tensor", "achieved": round(fl / avg_s / 1e12, 2), "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(fl / avg_s / 1e12 / peaks["bf16_tflops"], 4),
+                "alg_flops_per_launch": int(fl)}
+    else:  # HBM-bound: the local experts' weights once
+        wb = GATE_UP_BYTES if "gate_up" in name else DOWN_BYTES
+        alg = uniq_local * wb if ("gate_up" in name or "down" in name) else None
+        roof = {"bound": "hbm", "achieved": round(alg / avg_s / 1e9, 1) if alg else None, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(alg / avg_s / 1e9 / peaks["hbm_gbs"], 4) if alg else None,
+                "alg_bytes_per_launch": int(alg) if alg else None}
+    roof.update({"kernel": name, "avg_launch_us": round(avg_s * 1e6, 3), "traffic": None,
+                 "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json)" if peaks_kind == "measured" else "fallback"})
+    row_b = H * 2 + K * 8
+    result = {
+        "metric": ("prefill tok/s" if prefill else "decode tok/s") +
+                  f" (MoE half of the 30-layer Gemma-4 26B-A4B-shaped model, {total} tokens per step, experts "
+                  f"split over the GPUs)",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "u4-affine weights x bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded N(0,1) activations; N(0,0.02) weights MLX-affine 4-bit; router logit bias N(0,1) "
+                "per expert)",
+        "config": {"workload": args.workload, "layers": nl, "hidden": H, "experts": E, "top_k": K,
+                   "expert_intermediate": I, "tokens_per_step": total, "tokens_per_gpu": T,
+                   "parallelism": f"expert-parallel x{world}: {per} experts per GPU, NCCL grouped send/recv "
+                                  f"dispatch + combine ({mode_name} exchange); router replicated, tokens split",
+                   "exchange_bytes_per_layer_per_gpu": (world * T * row_b * 2) if mode_name == "fixed" else None,
+                   "graph": "one CUDA graph per step" if graph is not None else "eager (exact mode syncs per layer)",
+                   "l2": "inputs larger than L2 (expert slices resident)"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
+                "d2h_bytes_per_step": T * H * 2,
+                "api": "ExpertParallelMoeBlock.forward x30 (fmoe_ep_moe_forward) + pinned host copies"},
+        "gpu_launches": launches_per_step * args.steps,
+        "local_pairs_per_layer": round(pairs_local, 1), "local_unique_experts_per_layer": round(uniq_local, 2),
+        "roofline": roof,
+        "kernels": {k: {"launches_per_step": v[0] // nprof, "avg_us": round(v[1] / v[0] * 1e3, 3)}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
+        "clocks": clocks.summary(),
+    }
+    del graph  # graphs holding NCCL work go before the communicator
+    torch.cuda.synchronize()
+    comm.close()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(None, min(T, 256))
+        result["cpu_baseline"]["sample"] += " (tok/s is per token, so a 256-token sample stands for the step)"
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
 
 
 # ---------------------------------------------------------------------------
@@ -851,6 +1050,8 @@ def main():
         run_reference(args, rank, world)
     elif args.workload.startswith("decode30"):
         run_decoder(args, rank, world, local)
+    elif args.workload in EP_WORKLOADS:
+        run_ep_moe(args, rank, world, local)
     else:
         run_ours(args, rank, world, local)
 

@@ -141,7 +141,7 @@ int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, co
 }
 
 int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex,
-                       bf16* y, const MoeWs& w, bool build_routes, int* status, cudaStream_t st) {
+                       bf16* y, const MoeWs& w, bool build_routes, int* status, cudaStream_t st, float* y32) {
   int rc;
   if (build_routes) {
     rc = launch_route_build(ids, T * k, ex, w.m, st);
@@ -149,7 +149,7 @@ int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float
   }
   rc = launch_moe_gate_up(x, T, k, ex, w.m, w.act, status, true, st);
   if (rc) return rc;
-  return launch_moe_down(w.act, T, k, wts, ex, w.m, w.part, w.tile_ctr, y, status, true, st);
+  return launch_moe_down(w.act, T, k, wts, ex, w.m, w.part, w.tile_ctr, y, status, true, st, y32);
 }
 
 }  // namespace fmoe

@@ -303,9 +303,14 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   to_experts(&L->experts, &ex);
   // Everything that must hold its value between calls (status word, router /
   // expert / attention merge counters) sits at offsets every layer shares.
+  // The expert-parallel buffers (their expert-kernel counters included) come
+  // next: their size depends on the expert shapes only, so they too sit at the
+  // same offset for every layer type, never overlapping another layer's
+  // attention scratch or counters.
   d.h = carve_head(c);
   carve_router(c, T, &L->router, d.h, &d.rw);
   carve_moe(c, T, L->router.top_k, ex, &d.mw);
+  if (ep_ranks > 0) carve_ep(c, ep_ranks, ep_cap, nullptr, L->router.top_k, ex, d.h, &d.ep);
   d.attn_ws = c.take<uint8_t>(attn_workspace_bytes(kv, L->num_heads));
   d.qkv = c.take<float>((size_t)T * qkv_rows);
   d.o = c.take<float>((size_t)max_parts(QD) * T * H);
@@ -320,7 +325,6 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   d.moe = c.take<bf16>((size_t)T * H);
   d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
   d.wts = c.take<float>((size_t)T * L->router.top_k);
-  if (ep_ranks > 0) carve_ep(c, ep_ranks, ep_cap, nullptr, L->router.top_k, ex, d.h, &d.ep);
   d.bytes = c.off + 256;
   if (w) *w = d;
   return d.bytes;

@@ -15,7 +15,8 @@
 //   experts  the local slice over the received rows (ids outside the slice
 //            contribute nothing): decode GEMV kernels up to 128 rows, the
 //            tcgen05 grouped GEMMs above
-//   return   the per-rank partial sums (bf16) travel back the same way
+//   return   the per-rank partial sums travel back the same way, in fp32 (the
+//            sum over all experts is accumulated in fp32 end to end)
 //   combine  y[t] = sum over ranks, ascending, of the partial at slots[r][t]
 //            (fp32 accumulation; rank order = ascending expert-id order of
 //            the reference's combine, moe.rs:443-465)
@@ -110,8 +111,8 @@ __global__ void pack_kernel(const bf16* __restrict__ x, const int32_t* __restric
   }
 }
 
-// y[t] = bf16(sum over r ascending of ret[r][slots[r][t]]), fp32 accumulation.
-__global__ void combine_kernel(const bf16* __restrict__ ret, const int32_t* __restrict__ slots, int T, int R, int cap,
+// y[t] = bf16(sum over r ascending of ret[r][slots[r][t]]), fp32 partials and sums.
+__global__ void combine_kernel(const float* __restrict__ ret, const int32_t* __restrict__ slots, int T, int R, int cap,
                                int H, bf16* __restrict__ y) {
   const int words = H / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * words;
@@ -121,13 +122,16 @@ __global__ void combine_kernel(const bf16* __restrict__ ret, const int32_t* __re
     for (int r = 0; r < R; ++r) {
       const int s = slots[(int64_t)r * cap + t];
       if (s < 0) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(ret + ((int64_t)r * cap + s) * H + 8 * w);
-      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc[2 * q] += bf16lo(vv[q]);
-        acc[2 * q + 1] += bf16hi(vv[q]);
-      }
+      const float4* v = reinterpret_cast<const float4*>(ret + ((int64_t)r * cap + s) * H + 8 * w);
+      const float4 a = v[0], b = v[1];
+      acc[0] += a.x;
+      acc[1] += a.y;
+      acc[2] += a.z;
+      acc[3] += a.w;
+      acc[4] += b.x;
+      acc[5] += b.y;
+      acc[6] += b.z;
+      acc[7] += b.w;
     }
     *reinterpret_cast<uint4*>(y + (int64_t)t * H + 8 * w) =
         make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
@@ -230,8 +234,8 @@ size_t carve_ep(Carver& c, int R, int64_t cap, const fmoe_router_t* r, int k, co
   e.rx = c.take<bf16>((size_t)rows * d.H);
   e.rids = c.take<int32_t>((size_t)rows * k);
   e.rwts = c.take<float>((size_t)rows * k);
-  e.ypart = c.take<bf16>((size_t)rows * d.H);
-  e.ret = c.take<bf16>((size_t)rows * d.H);
+  e.ypart = c.take<float>((size_t)rows * d.H);
+  e.ret = c.take<float>((size_t)rows * d.H);
   carve_moe(c, std::min<int64_t>(rows, kGemvRows), k, d, &e.mw);
   e.gemm = rows > kGemvRows;
   if (e.gemm) carve_pf_ex(c, rows, k, d, &e.pw);
@@ -281,7 +285,7 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
   }
   if ((rc = check_launch("ep_pack_kernel"))) return rc;
 
-  const size_t row_b = (size_t)H * sizeof(bf16), meta_b = (size_t)k * sizeof(int32_t);
+  const size_t row_b = (size_t)H * sizeof(bf16), part_b = (size_t)H * sizeof(float), meta_b = (size_t)k * sizeof(int32_t);
   std::vector<Xfer> px(R), pb(R);
   std::vector<int64_t> scnt(R, cap), rcnt(R, cap), roff(R);
   if (mode == FMOE_EP_EXACT) {
@@ -328,18 +332,18 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
     pb[p] = Xfer{};
     pb[p].sptr[0] = w.ypart + roff[p] * H;
     pb[p].rptr[0] = w.ret + so * H;
-    pb[p].sbytes[0] = rcnt[p] * row_b;
-    pb[p].rbytes[0] = scnt[p] * row_b;
+    pb[p].sbytes[0] = rcnt[p] * part_b;
+    pb[p].rbytes[0] = scnt[p] * part_b;
   }
   if ((rc = exchange(c, px, 3, st, "dispatch"))) return rc;
   if (rows > 0) {
     if (rows <= kGemvRows) {
-      rc = run_experts(w.rx, rows, k, w.rids, w.rwts, d, w.ypart, w.mw, true, status, st);
+      rc = run_experts(w.rx, rows, k, w.rids, w.rwts, d, nullptr, w.mw, true, status, st, w.ypart);
     } else {
       if (!w.gemm || !prep)
         return set_error(FMOE_ERR_INVALID, "ep: %lld received rows need the tensor-core path (prepared scales)",
                          (long long)rows);
-      rc = run_prefill_experts(w.rx, rows, k, w.rids, w.rwts, d, prep, w.ypart, w.pw, true, status, st);
+      rc = run_prefill_experts(w.rx, rows, k, w.rids, w.rwts, d, prep, nullptr, w.pw, true, status, st, w.ypart);
     }
     if (rc) return rc;
   }

@@ -72,8 +72,10 @@ int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, cons
 int down_groups(int64_t T, int k, int E);
 int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, const RouteMeta& m, bf16* act,
                        int* status, bool pdl, cudaStream_t st);
+// y32 != nullptr: the combined rows go there in fp32 instead of bf16 to y.
 int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
-                    float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st);
+                    float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st,
+                    float* y32 = nullptr);
 
 // quant.cu
 int launch_quantize(const void* src, int src_is_bf16, int64_t rows, int64_t cols, int bits, int group, uint32_t* wq,
@@ -170,8 +172,9 @@ size_t carve_router(Carver& c, int64_t T, const fmoe_router_t* r, const WsHead& 
 size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w);
 int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, const RouterWs& w, int32_t* ids,
                float* wts, float* logits, const RouteMeta* meta, int* status, cudaStream_t st);
+// y32 != nullptr: fp32 output rows there instead of bf16 ones in y.
 int run_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& ex, bf16* y,
-                const MoeWs& w, bool build_routes, int* status, cudaStream_t st);
+                const MoeWs& w, bool build_routes, int* status, cudaStream_t st, float* y32 = nullptr);
 
 // prefill.cu: the expert stage of the tensor-core path on routed tokens (any
 // expert table slice; pairs whose id is outside it contribute nothing).
@@ -189,7 +192,8 @@ size_t carve_pf_ex(Carver& c, int64_t T, int k, const ExpertsDev& d, PfExWs* w);
 // ids / wts: [T, k].  build_routes: build w.m from ids (false when the router
 // already built it).  prep: fmoe_moe_prefill_prepare's copy for this table.
 int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& d,
-                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st);
+                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st,
+                        float* y32 = nullptr);
 
 // ep.cu: expert-parallel dispatch -> local experts -> combine over NCCL.
 struct EpWs {
@@ -202,7 +206,7 @@ struct EpWs {
   bf16* rx;                           // received rows (R * cap at most)
   int32_t* rids;
   float* rwts;
-  bf16 *ypart, *ret;                  // partial sums: computed here | returned from the peers
+  float *ypart, *ret;                 // fp32 partial sums: computed here | returned from the peers
   MoeWs mw;                           // decode expert kernels, min(R * cap, 128) rows
   PfExWs pw;                          // tensor-core expert stage (R * cap > 128)
   bool gemm;

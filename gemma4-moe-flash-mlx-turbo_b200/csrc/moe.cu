@@ -231,7 +231,8 @@ __host__ __device__ inline DnLayout dn_layout(int I, int T) {
 __global__ void __launch_bounds__(kDnWarps * 32, 2)
     moe_down_kernel(const bf16* __restrict__ act, int T, int k, const float* __restrict__ wts, ExpertsDev ex,
                     const int4* __restrict__ work, int work_len, const int32_t* __restrict__ pairs,
-                    float* __restrict__ part, unsigned* __restrict__ tile_ctr, bf16* __restrict__ y, int* status) {
+                    float* __restrict__ part, unsigned* __restrict__ tile_ctr, bf16* __restrict__ y,
+                    float* __restrict__ y32, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kDnSlots][2];  // [slot][0: weights + scales, 1: act rows]
   __shared__ int s_last;
@@ -327,7 +328,11 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
       float s = 0.f;
 #pragma unroll
       for (int w = 0; w < kDnWarps; ++w) s += ysm[w * T * 16 + i];
-      y[(int64_t)(i >> 4) * H + row0 + (i & 15)] = __float2bfloat16_rn(s);
+      const int64_t o = (int64_t)(i >> 4) * H + row0 + (i & 15);
+      if (y32)
+        y32[o] = s;
+      else
+        y[o] = __float2bfloat16_rn(s);
     }
     return;
   }
@@ -346,7 +351,11 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
   for (int i = threadIdx.x; i < T * 16; i += blockDim.x) {
     float s = 0.f;
     for (int q = 0; q < ngroups; ++q) s += __ldcg(part + ((int64_t)q * T + (i >> 4)) * H + row0 + (i & 15));
-    y[(int64_t)(i >> 4) * H + row0 + (i & 15)] = __float2bfloat16_rn(s);
+    const int64_t o = (int64_t)(i >> 4) * H + row0 + (i & 15);
+    if (y32)
+      y32[o] = s;
+    else
+      y[o] = __float2bfloat16_rn(s);
   }
   if (threadIdx.x == 0) tile_ctr[blockIdx.x] = 0;
 }
@@ -406,7 +415,7 @@ int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, co
 }
 
 int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
-                    float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st) {
+                    float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st, float* y32) {
   const DnLayout L = dn_layout(ex.I, (int)T);
   if (L.bytes > 227 * 1024)
     return set_error(FMOE_ERR_UNSUPPORTED, "down: T=%lld / I=%d exceed shared memory", (long long)T, ex.I);
@@ -417,7 +426,7 @@ int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const E
   {
     ProfScope prof_("moe_down_kernel", st);
     cudaLaunchKernelEx(&cfg, moe_down_kernel, act, (int)T, k, wts, ex, (const int4*)m.work, m.work_len,
-                       (const int32_t*)m.pairs, part, tile_ctr, y, status);
+                       (const int32_t*)m.pairs, part, tile_ctr, y, y32, status);
   }
   return check_launch("moe_down_kernel");
 }

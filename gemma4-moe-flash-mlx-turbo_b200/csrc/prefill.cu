@@ -475,7 +475,8 @@ __global__ void gather_kernel(const bf16* __restrict__ x, const int32_t* __restr
 
 // y[t] = bf16(sum over local slots of w[t, slot] * Y[inv[t * k + slot]]) in slot order.
 __global__ void combine_kernel(const bf16* __restrict__ Y, const int32_t* __restrict__ inv,
-                               const float* __restrict__ wts, int T, int k, int H, bf16* __restrict__ y) {
+                               const float* __restrict__ wts, int T, int k, int H, bf16* __restrict__ y,
+                               float* __restrict__ y32) {
   const int words = H / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * words;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -493,8 +494,14 @@ __global__ void combine_kernel(const bf16* __restrict__ Y, const int32_t* __rest
         acc[2 * q + 1] = fmaf(wv, bf16hi(vv[q]), acc[2 * q + 1]);
       }
     }
-    *reinterpret_cast<uint4*>(y + (int64_t)t * H + 8 * w) =
-        make_uint4(bf2(acc[0], acc[1]), bf2(acc[2], acc[3]), bf2(acc[4], acc[5]), bf2(acc[6], acc[7]));
+    if (y32) {
+      float4* o = reinterpret_cast<float4*>(y32 + (int64_t)t * H + 8 * w);
+      o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      *reinterpret_cast<uint4*>(y + (int64_t)t * H + 8 * w) =
+          make_uint4(bf2(acc[0], acc[1]), bf2(acc[2], acc[3]), bf2(acc[4], acc[5]), bf2(acc[6], acc[7]));
+    }
   }
 }
 
@@ -568,7 +575,8 @@ size_t carve_pf_ex(Carver& c, int64_t T, int k, const ExpertsDev& d, PfExWs* w) 
 }
 
 int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, const float* wts, const ExpertsDev& d,
-                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st) {
+                        const bf16* prep, bf16* y, const PfExWs& w, bool build_routes, int* status, cudaStream_t st,
+                        float* y32) {
   int rc;
   const int64_t P = T * k;
   if (P > (1 << 30) / d.H) return set_error(FMOE_ERR_UNSUPPORTED, "prefill: T=%lld too large", (long long)T);
@@ -633,7 +641,7 @@ int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, con
   if ((rc = check_launch("tc_gemm_kernel<down>"))) return rc;
   {
     ProfScope prof_("prefill_combine_kernel", st);
-    pf::combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(w.ys, w.inv, wts, (int)T, k, d.H, y);
+    pf::combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(w.ys, w.inv, wts, (int)T, k, d.H, y, y32);
   }
   return check_launch("prefill_combine_kernel");
 }

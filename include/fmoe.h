@@ -362,7 +362,7 @@ int fmoe_moe_prefill_experts(const void* x, int64_t T, int top_k, const int32_t*
  * [r*E/n, (r+1)*E/n) with first_expert = r*E/n — while router weights are
  * replicated and each rank routes its own T tokens.  One MoE block: router ->
  * dispatch (a token's row, ids and weights cross once to every rank owning
- * one of its experts) -> local experts -> the per-rank partial sums return ->
+ * one of its experts) -> local experts -> the per-rank partial sums return (fp32) ->
  * y = their sum in ascending rank order.  Transport: grouped ncclSend /
  * ncclRecv from libnccl.so.2, resolved at run time.  Every rank of the
  * communicator must make the same sequence of fmoe_ep_* calls with the same

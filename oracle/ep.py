@@ -4,8 +4,9 @@ The reference runs every routed expert on one device (Gemma4MoeBlock::forward,
 src/model/moe.rs:361-466); its answer for a token is the oracle's
 moe_experts().  This file restates, in numpy, the split that libfmoe's
 expert-parallel path performs (experts contiguous over R ranks, a token sent
-once to each rank that owns one of its experts, per-rank partial sums rounded
-to bf16 and added back in ascending rank order), so that tests can check the
+once to each rank that owns one of its experts, per-rank fp32 partial sums
+added back in ascending rank order and rounded to bf16 once), so that tests
+can check the
 exchange layout rank by rank and the whole split against the single-device
 answer.  Only tests/ use it.
 
@@ -20,7 +21,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import bf16_to_f32, f32_to_bf16, moe_experts
+from . import f32_to_bf16, moe_experts
 
 
 def plan(ids: np.ndarray, R: int, per_rank: int, cap: int):
@@ -57,11 +58,11 @@ def pack(x: np.ndarray, ids: np.ndarray, wts: np.ndarray, slots: np.ndarray, cou
 
 def local_partial(rx: np.ndarray, rids: np.ndarray, rwts: np.ndarray, buf: np.ndarray, stride: int, offsets,
                   hidden: int, inter: int, first: int, n: int) -> np.ndarray:
-    """bf16 [rows, H]: sum over the row's experts in [first, first + n) of
-    w * expert(x) (ascending expert id), rounded to bf16 once; rows with no
-    local expert give 0.  buf is the WHOLE table (global ids index it)."""
+    """fp32 [rows, H]: sum over the row's experts in [first, first + n) of
+    w * expert(x) (ascending expert id); rows with no local expert give 0.
+    buf is the WHOLE table (global ids index it)."""
     rows = rx.shape[0]
-    out = np.zeros((rows, hidden), np.uint16)
+    out = np.zeros((rows, hidden), np.float32)
     if rows == 0:
         return out
     local = (rids >= first) & (rids < first + n)
@@ -69,20 +70,20 @@ def local_partial(rx: np.ndarray, rids: np.ndarray, rwts: np.ndarray, buf: np.nd
     w = np.where(local, rwts, 0.0).astype(np.float32)
     keep = local.any(axis=1)
     if keep.any():
-        _, y16 = moe_experts(rx[keep], ids[keep], w[keep], buf, stride, offsets, hidden, inter)
-        out[keep] = y16
+        y32, _ = moe_experts(rx[keep], ids[keep], w[keep], buf, stride, offsets, hidden, inter)
+        out[keep] = y32
     return out
 
 
 def combine(ret: np.ndarray, slots: np.ndarray, T: int) -> np.ndarray:
-    """y bf16 [T, H] = bf16(sum over r ascending of ret[r, slots[r, t]]) (fp32 sums)."""
+    """y bf16 [T, H] = bf16(sum over r ascending of ret[r, slots[r, t]]) (fp32 partials and sums)."""
     R, _, H = ret.shape
     acc = np.zeros((T, H), np.float32)
     for r in range(R):
         for t in range(T):
             s = slots[r, t]
             if s >= 0:
-                acc[t] += bf16_to_f32(ret[r, s])
+                acc[t] += ret[r, s]
     return f32_to_bf16(acc)
 
 

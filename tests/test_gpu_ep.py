@@ -187,21 +187,73 @@ def _two_rank_worker(rank, world, port, q):
         q.put((rank, None, repr(e)))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_ranks_match_single_device():
+def _two_rank_decoder_worker(rank, world, port, q):
+    """Two decoder layers (sliding + full attention) with the experts split over
+    two GPUs, one sequence per GPU; checked against the same model with all
+    experts local on this GPU."""
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    try:
+        fm = __graft_entry__.load_package()
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        comm = fm.EPComm()
+        cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=2)
+        ctx = 300
+        m1 = fm.Gemma4Model.random(cfg, batch=1, max_positions=1024, seed=21, device=dev, n_layers=2)
+        layers = []
+        for L in m1.layers:  # the same weights, expert slice only
+            L2 = fm.Gemma4DecoderLayer(L.q_proj, L.k_proj, L.v_proj, L.o_proj, L.q_norm, L.k_norm, L.norms, L.mlp,
+                                       L.router, L.experts.shard(rank, world), L.num_heads, L.num_kv_heads,
+                                       L.head_dim, L.rope_dims, L.rope_theta, L.k_eq_v, L.eps, L.layer_scalar,
+                                       L.attn_scale, L.top_k)
+            layers.append(L2)
+        m2 = fm.Gemma4Model(cfg, m1.embed, layers, m1.final_norm, 1, 1024, device=dev, ep=comm)
+        g = torch.Generator(device=dev).manual_seed(22 + rank)
+        for L, c1, c2 in zip(m1.layers, m1.caches, m2.caches):
+            kv = torch.randn(2, 1, L.num_kv_heads, ctx, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+            c1.update(kv[0], kv[1])
+            c2.update(kv[0], kv[1])
+        for m in (m1, m2):
+            m.ids.fill_(5 + rank)
+            m.set_position(ctx)
+        res = []
+        for _ in range(3):
+            a = m1.decode_step().clone()
+            la = m1.logits.clone()
+            b = m2.decode_step().clone()
+            torch.cuda.synchronize()
+            top = torch.topk(la[0], 2).values
+            sure = bool(top[0] - top[1] > 1e-3 * top[0].abs())  # ids compared where the argmax is clear
+            res.append((bool(torch.equal(a, b)) or not sure,
+                        max_rel_err(m2.logits.cpu().numpy(), la.cpu().numpy())))
+            m2.ids.copy_(a)  # continue both from the same token
+        comm.status()
+        torch.cuda.synchronize()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, res, None))
+    except Exception as e:
+        q.put((rank, None, repr(e)))
+
+
+def _spawn_two(target):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     env_nvls = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=_two_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    res = {}
     try:
         for p in procs:
             p.start()
-        res = {}
         for _ in range(2):
-            rank, errs, exc = q.get(timeout=600)
-            res[rank] = (errs, exc)
+            rank, out, exc = q.get(timeout=600)
+            res[rank] = (out, exc)
     finally:
         for p in procs:
             p.join(timeout=60)
@@ -211,7 +263,21 @@ def test_ep_two_ranks_match_single_device():
             os.environ.pop("NCCL_NVLS_ENABLE", None)
         else:
             os.environ["NCCL_NVLS_ENABLE"] = env_nvls
-    for rank, (errs, exc) in res.items():
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_rank_decoder_matches_local():
+    for rank, (res, exc) in _spawn_two(_two_rank_decoder_worker).items():
+        assert exc is None, f"rank {rank}: {exc}"
+        for step, (same_ids, err) in enumerate(res):
+            assert err <= TOL, (rank, step, err)
+            assert same_ids, (rank, step)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_ranks_match_single_device():
+    for rank, (errs, exc) in _spawn_two(_two_rank_worker).items():
         assert exc is None, f"rank {rank}: {exc}"
         for T, mode, same, err in errs:
             assert same, (rank, T, mode)
