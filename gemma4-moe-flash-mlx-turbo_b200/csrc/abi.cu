@@ -105,6 +105,7 @@ size_t carve_moe(Carver& c, int64_t T, int k, const ExpertsDev& ex, MoeWs* w) {
   m.m.num_unique = c.take<int32_t>(1);
   m.m.work_len = (int)(T * k < ex.E ? T * k : ex.E);
   m.m.work = c.take<int4>(m.m.work_len);
+  m.m.scratch = nullptr;  // decode sizes: one CTA builds the lists
   m.act = c.take<bf16>((size_t)T * k * ex.I);
   const int groups = down_groups(T, k, ex.E);
   m.part = groups > 1 ? c.take<float>((size_t)groups * T * ex.H) : nullptr;
@@ -135,6 +136,15 @@ int run_router(const bf16* x, int64_t T, const fmoe_router_t* r, const QW& q, co
         launch_router_prenorm(x, T, q.in, r->root_size, r->eps, static_cast<const bf16*>(r->router_scale), w.xs, st);
     if (rc) return rc;
     xin = w.xs;
+  }
+  if (router_tc_eligible(T, q, r->top_k) && aligned(xin, 16) && aligned(q.w, 16) && (!logits || aligned(logits, 16))) {
+    // many tokens: tensor-core GEMM + top-k epilogue
+    int rc = launch_router_tc(xin, T, q, r->logit_bias, static_cast<const bf16*>(r->per_expert_scale), r->top_k, ids,
+                              wts, logits, status, st);
+    if (rc || !meta) return rc;
+    ExpertsDev all = {};
+    all.E = q.out;  // lists over every expert of the router (first 0)
+    return launch_route_build(ids, T * r->top_k, all, *meta, st);
   }
   return launch_router_fused(xin, T, q, r->logit_bias, static_cast<const bf16*>(r->per_expert_scale), r->top_k, ids,
                              wts, logits, w.counters, meta, status, true, st);

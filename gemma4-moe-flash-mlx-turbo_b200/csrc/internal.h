@@ -54,7 +54,10 @@ struct RouteMeta {
   int32_t* num_unique;  // [1]
   int4* work;           // [work_len] per expert slot u: (expert, first pair, pair count, 0); count 0 past the end
   int work_len;         // min(T * k, E): the expert kernels' grid extent
+  int32_t* scratch;     // [route_scratch_ints(P, E)] or null: lets many pairs be listed by many CTAs
 };
+// Scratch ints that let launch_route_build spread P pairs over many CTAs.
+int64_t route_scratch_ints(int64_t P, int E);
 
 // gemv.cu
 int gemv_ksplit(int64_t T, int out, int in);
@@ -66,6 +69,12 @@ int launch_router_prenorm(const bf16* x, int64_t T, int H, float root, float eps
 int launch_router_fused(const bf16* x, int64_t T, const QW& w, const float* bias, const bf16* pes, int k,
                         int32_t* ids, float* wts, float* logits_out, unsigned* counters, const RouteMeta* meta,
                         int* status, bool pdl, cudaStream_t st);
+
+// router_tc.cu: the tensor-core router for many tokens (bf16 router weight).
+constexpr int64_t kRouterTcMinTokens = 64;
+bool router_tc_eligible(int64_t T, const QW& w, int k);
+int launch_router_tc(const bf16* x, int64_t T, const QW& w, const float* bias, const bf16* pes, int k, int32_t* ids,
+                     float* wts, float* logits, int* status, cudaStream_t st);
 
 // moe.cu
 int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, const RouteMeta& m, cudaStream_t st);

@@ -368,7 +368,144 @@ int down_groups(int64_t T, int k, int E) {
   return (int)((maxu + kDnSlots - 1) / kDnSlots);
 }
 
+// ---------------------------------------------------------------------------
+// The same lists for many pairs, spread over CTAs: units u = (CTA, warp) own
+// consecutive chunks of kRbUnit pairs.  count: per-unit expert counts;
+// scan (one CTA): per-expert totals -> start / unique / work, and each
+// (unit, expert) count becomes that unit's first output slot; scatter: each
+// warp places its chunk in index order.  The result is identical to
+// route_build_block's (pairs ascending within an expert).
+constexpr int kRbUnit = 256;  // pairs per warp
+constexpr int kRbWarps = 8;
+constexpr int64_t kRbSingleMax = 4096;  // up to this many pairs one CTA builds the lists
+
+int64_t route_scratch_ints(int64_t P, int E) {
+  return P <= kRbSingleMax ? 0 : ((P + kRbUnit - 1) / kRbUnit) * (int64_t)E;
+}
+
+__global__ void __launch_bounds__(kRbWarps * 32)
+    route_count_kernel(const int32_t* __restrict__ ids, int P, int first, int E, int32_t* __restrict__ cnt) {
+  extern __shared__ int wc[];  // [kRbWarps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kRbWarps * E; i += blockDim.x) wc[i] = 0;
+  __syncthreads();
+  const int u = blockIdx.x * kRbWarps + warp;
+  const int pb = u * kRbUnit, pe = min(P, pb + kRbUnit);
+  for (int p = pb + lane; p < pe; p += 32) {
+    const int e = ids[p] - first;
+    if (e >= 0 && e < E) atomicAdd(&wc[warp * E + e], 1);
+  }
+  __syncthreads();
+  const int U = (P + kRbUnit - 1) / kRbUnit;
+  for (int i = threadIdx.x; i < kRbWarps * E; i += blockDim.x) {
+    const int uu = blockIdx.x * kRbWarps + i / E;
+    if (uu < U) cnt[(int64_t)uu * E + i % E] = wc[i];
+  }
+}
+
+__global__ void __launch_bounds__(1024)
+    route_scan_kernel(int32_t* __restrict__ cnt, int U, int E, int32_t* __restrict__ start,
+                      int32_t* __restrict__ unique, int32_t* __restrict__ num_unique, int4* __restrict__ work,
+                      int work_len) {
+  __shared__ int tot[1024];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int u = 0; u < U; ++u) c += cnt[(int64_t)u * E + e];
+    tot[e] = c;
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive scan over experts, compaction of the non-empty ones
+    int run = 0, urun = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? tot[e] : 0;
+      int incl = c, uincl = c > 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int a = __shfl_up_sync(0xffffffffu, incl, o), b = __shfl_up_sync(0xffffffffu, uincl, o);
+        if (lane >= o) {
+          incl += a;
+          uincl += b;
+        }
+      }
+      if (e < E) {
+        start[e] = run + incl - c;
+        tot[e] = run + incl - c;
+        if (c > 0) {
+          unique[urun + uincl - 1] = e;
+          if (urun + uincl - 1 < work_len) work[urun + uincl - 1] = make_int4(e, run + incl - c, c, 0);
+        }
+      }
+      run += __shfl_sync(0xffffffffu, incl, 31);
+      urun += __shfl_sync(0xffffffffu, uincl, 31);
+    }
+    if (lane == 0) {
+      start[E] = run;
+      *num_unique = urun;
+    }
+    for (int u = urun + lane; u < work_len; u += 32) work[u] = make_int4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {  // (unit, expert) first slots
+    int o = tot[e];
+    for (int u = 0; u < U; ++u) {
+      const int c = cnt[(int64_t)u * E + e];
+      cnt[(int64_t)u * E + e] = o;
+      o += c;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kRbWarps * 32)
+    route_scatter_kernel(const int32_t* __restrict__ ids, int P, int first, int E, const int32_t* __restrict__ off,
+                         int32_t* __restrict__ pairs) {
+  extern __shared__ int wo[];  // [kRbWarps][E] next slot per (warp, expert)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int U = (P + kRbUnit - 1) / kRbUnit;
+  for (int i = threadIdx.x; i < kRbWarps * E; i += blockDim.x) {
+    const int uu = blockIdx.x * kRbWarps + i / E;
+    wo[i] = uu < U ? off[(int64_t)uu * E + i % E] : 0;
+  }
+  __syncthreads();
+  const int u = blockIdx.x * kRbWarps + warp;
+  const int pb = u * kRbUnit, pe = min(P, pb + kRbUnit);
+  const unsigned lt = (1u << lane) - 1u;
+  for (int p0 = pb; p0 < pe; p0 += 32) {
+    const int p = p0 + lane;
+    int e = -1;
+    if (p < pe) {
+      e = ids[p] - first;
+      if (e < 0 || e >= E) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) pairs[wo[warp * E + e] + __popc(peers & lt)] = p;
+    __syncwarp();
+    if (e >= 0 && (peers & lt) == 0) wo[warp * E + e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
 int launch_route_build(const int32_t* ids, int64_t P, const ExpertsDev& ex, const RouteMeta& m, cudaStream_t st) {
+  if (P > kRbSingleMax && m.scratch && ex.E <= 1024) {
+    const int U = (int)((P + kRbUnit - 1) / kRbUnit), blocks = (U + kRbWarps - 1) / kRbWarps;
+    const size_t sm = sizeof(int) * (size_t)kRbWarps * ex.E;
+    {
+      ProfScope prof_("route_count_kernel", st);
+      route_count_kernel<<<blocks, kRbWarps * 32, sm, st>>>(ids, (int)P, ex.first, ex.E, m.scratch);
+    }
+    int rc = check_launch("route_count_kernel");
+    if (rc) return rc;
+    {
+      ProfScope prof_("route_scan_kernel", st);
+      route_scan_kernel<<<1, 1024, 0, st>>>(m.scratch, U, ex.E, m.start, m.unique, m.num_unique, m.work, m.work_len);
+    }
+    if ((rc = check_launch("route_scan_kernel"))) return rc;
+    {
+      ProfScope prof_("route_scatter_kernel", st);
+      route_scatter_kernel<<<blocks, kRbWarps * 32, sm, st>>>(ids, (int)P, ex.first, ex.E, m.scratch, m.pairs);
+    }
+    return check_launch("route_scatter_kernel");
+  }
   const size_t smem = sizeof(int) * (size_t)(kRouteWarps + 1) * ex.E;
   if (smem > 200 * 1024) return set_error(FMOE_ERR_UNSUPPORTED, "route_build: %d experts too many", ex.E);
   if (smem > 48 * 1024)

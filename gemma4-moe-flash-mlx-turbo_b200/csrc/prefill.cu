@@ -34,12 +34,12 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <mutex>
-#include "internal.h"
-#include "common.cuh"
-#include "stage.cuh"
+#include "tc.cuh"
 
 namespace fmoe {
 namespace pf {
+
+using namespace tc;
 
 constexpr int BM = 128;                // tokens per tile (the MMA's N, rounded up to 16)
 constexpr int BN = 256, BK = 64;       // weight rows per item (two 128-row halves), K per tile
@@ -77,82 +77,6 @@ struct Args {
   bf16* out;             // GEMM1: act [P][I] (permuted words); GEMM2: Y [P][H]
   int* status;
 };
-
-__device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* m, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-          smem_u32(dst)),
-      "l"(m), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma3d(void* dst, const CUtensorMap* m, int x, int y, int z, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];\n" ::"r"(smem_u32(dst)),
-      "l"(m), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-// Bounded wait; after a failure anywhere in the CTA every wait returns at once.
-__device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, volatile int* failed, int* status, int site) {
-  if (*failed) return false;
-  for (int i = 0; i < kMaxWaitIters; ++i) {
-    if (try_wait(bar, parity)) return true;
-    if ((i & 1023) == 1023 && *failed) return false;
-  }
-  *failed = 1;
-  atomicCAS(status, 0, site);
-  return false;
-}
-// Bounded wait that ignores the failure flag (draining copies / MMAs in flight).
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
-  for (int i = 0; i < kMaxWaitIters && !try_wait(bar, parity); ++i) {
-  }
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
-// 1024 bytes (SBO 1024, LBO unused = 1), descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
-  return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
-}
-// Instruction descriptor, kind::f16: D f32, A / B bf16 K-major, M 128, N = n.
-__device__ __forceinline__ uint32_t idesc_n(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-// D (TMEM) += A (shared memory descriptor) . B (shared memory descriptor)^T
-__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0), "r"(0), "r"(0), "r"(0));
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 // Two bf16 from two floats, low half first.
 __device__ __forceinline__ uint32_t bf2(float lo, float hi) { return pack_bf16x2(lo, hi); }
@@ -516,9 +440,11 @@ int64_t prep_q1h(const ExpertsDev& d) { return (d.H / 64 + 3) / 4; }
 int64_t prep_q2h(const ExpertsDev& d) { return (d.I / 64 + 3) / 4; }
 int64_t prep_eps(const ExpertsDev& d) { return 4 * (4 * prep_q1h(d) * d.I) + 2 * (4 * prep_q2h(d) * d.H); }
 
+}  // namespace
+
 // The driver's tensor-map encoder, resolved through the runtime (the library
 // does not link the driver library, so it loads on machines without one).
-PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -535,14 +461,12 @@ int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, c
            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw, const char* what) {
   cuuint32_t es[3] = {1, 1, 1};
   const auto enc = tmap_encoder();
-  if (!enc) return set_error(FMOE_ERR_CUDA, "prefill: the driver's tensor-map encoder is unavailable");
+  if (!enc) return set_error(FMOE_ERR_CUDA, "tensor map: the driver's encoder is unavailable");
   const CUresult r = enc(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FMOE_ERR_CUDA, "prefill: tensor map for %s failed (%d)", what, (int)r);
+  if (r != CUDA_SUCCESS) return set_error(FMOE_ERR_CUDA, "tensor map for %s failed (%d)", what, (int)r);
   return FMOE_OK;
 }
-
-}  // namespace
 
 int check_prefill(const ExpertsDev& d) {
   if (d.H % 256 || d.I % 64 || d.H > 8192 || d.E < 1)
@@ -564,6 +488,8 @@ size_t carve_pf_ex(Carver& c, int64_t T, int k, const ExpertsDev& d, PfExWs* w) 
   p.m.num_unique = c.take<int32_t>(1);
   p.m.work_len = (int)std::min<int64_t>(P, d.E);
   p.m.work = c.take<int4>(p.m.work_len);
+  const int64_t rs = route_scratch_ints(P, d.E);
+  p.m.scratch = rs ? c.take<int32_t>(rs) : nullptr;
   p.tiles = c.take<int4>(P / pf::BM + d.E + 1);
   p.ntiles = c.take<int>(1);
   p.inv = c.take<int32_t>(P);

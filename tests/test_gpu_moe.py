@@ -85,6 +85,38 @@ def test_router_bias_norm_scales_and_4bit(fm, orc, dev):
         assert np.abs(wt.cpu().numpy()[sure] - o_w[sure]).max() < 1e-5
 
 
+@pytest.mark.parametrize("T,Es", [(64, 128), (200, 128), (1000, 128), (130, 32), (77, 256)])
+def test_router_many_tokens_tensor_core(fm, orc, dev, T, Es):
+    """T >= 64 with a bf16 router takes the tcgen05 router (GEMM + top-k
+    epilogue): logits, ids and weights against the oracle, with logit bias,
+    router norm chain and per-expert scale."""
+    g = torch.Generator(device=dev).manual_seed(40 + T)
+    x = (torch.randn(T, H, generator=g, device=dev) * 2).to(torch.bfloat16)
+    w = torch.randn(Es, H, generator=g, device=dev) * 0.05
+    bias = torch.randn(Es, generator=g, device=dev)
+    rscale = (torch.rand(H, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    pes = (torch.rand(Es, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+    table = fm.ExpertTable.random(Es, H, 64, seed=3, device=dev)
+    rp = fm.QuantizedLinear.from_float(w, 16)
+    for use_norm in (False, True):
+        block = fm.Gemma4MoeBlock(rp, table, top_k=K, router_scale=rscale, per_expert_scale=pes, use_norm=use_norm,
+                                  rms_norm_eps=1e-6, logit_bias=bias)
+        ids, wt, lg = block.route(x, want_logits=True)
+        kw = dict(logit_bias=bias.cpu().numpy(), use_norm=use_norm, root_size=H ** -0.5, eps=1e-6,
+                  router_scale=to_np_bf16(rscale), per_expert_scale=to_np_bf16(pes))
+        o_ids, o_w, o_lg = orc.router(to_np_bf16(x), to_np_bf16(rp.weight), K, **kw)
+        assert np.abs(lg.cpu().numpy() - o_lg).max() < 1e-4 * np.abs(o_lg).max()
+        sure = topk_gap(o_lg, K) > GAP
+        assert sure.mean() > 0.5
+        assert np.array_equal(ids.cpu().numpy()[sure], o_ids[sure])
+        # the tensor cores' fp32 accumulation order moves logits of magnitude ~10
+        # by ~1e-5, which moves the softmax weights by about as much
+        assert np.abs(wt.cpu().numpy()[sure] - o_w[sure]).max() < 5e-5
+        # same routing without the logits output
+        ids2, wt2, _ = block.route(x)
+        assert torch.equal(ids, ids2) and torch.equal(wt, wt2)
+
+
 @pytest.mark.parametrize("T", [1, 3, 32])
 def test_moe_block_config1(fm, orc, dev, full_layer, T):
     table, wr, host = full_layer

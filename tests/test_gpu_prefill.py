@@ -74,6 +74,22 @@ def test_prefill_one_hot_expert_many_tiles(fm, orc, dev, layer):
     assert max_rel_err(y.float().cpu().numpy(), want) <= TOL
 
 
+def test_prefill_many_pairs_equals_halves(fm, dev, layer):
+    """T = 1000 (8000 pairs: the routing lists are built by many CTAs) gives
+    bit-identically the rows of two T = 500 calls (one-CTA lists): every
+    token's routing and expert arithmetic is independent of its batch."""
+    table, wr, bias, _ = layer
+    T = 1000
+    g = torch.Generator(device=dev).manual_seed(8)
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    block = fm.Gemma4MoeBlock(fm.QuantizedLinear(wr, bits=16), table, top_k=K, logit_bias=bias)
+    y, ids, _ = block.forward_prefill(x, return_routing=True)
+    y0, ids0, _ = block.forward_prefill(x[:500], return_routing=True)
+    y1, ids1, _ = block.forward_prefill(x[500:], return_routing=True)
+    assert torch.equal(ids, torch.cat([ids0, ids1]))
+    assert torch.equal(y, torch.cat([y0, y1]))
+
+
 def test_forward_dispatches_prefill_above_128_tokens(fm, dev, layer):
     table, wr, _, _ = layer
     T = 160
