@@ -17,6 +17,8 @@
 //  10 qgemv  d = (gelu(g) * u) . Wd^T                     (GELU gating fused into the input prologue)
 //  11 ff_out x' = (h + post_ff_norm(post_ff_norm_1(d) + post_ff_norm_2(moe))) * layer_scalar
 // Every intermediate is rounded to bf16 where the reference holds a bf16 array.
+#include <mutex>
+
 #include "internal.h"
 #include "common.cuh"
 #include "stage.cuh"
@@ -26,6 +28,15 @@ namespace fmoe {
 constexpr int kRowThreads = 256;
 constexpr int kRowMaxPer = 16;  // hidden <= 4096
 
+// The row kernels (ff_in / ff_out) run one CTA of kFfThreads per token, each
+// thread kFfPer elements of the hidden row.  Every input is loaded before the
+// first reduction — the constant norm weights even before griddepcontrol.wait —
+// so a call costs one memory round trip plus three or four CTA reductions.
+constexpr int kFfThreads = 1024;
+constexpr int kFfPer = kRowThreads * kRowMaxPer / kFfThreads;  // 4: hidden <= 4096
+constexpr int kFfSlices = 4;                                   // split-K slices loaded per batch
+
+template <int NT>
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -35,76 +46,99 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float s = 0.f;
 #pragma unroll
-  for (int w = 0; w < kRowThreads / 32; ++w) s += red[w];
+  for (int w = 0; w < NT / 32; ++w) s += red[w];
   return s;
+}
+
+__device__ __forceinline__ void load_row_bf16(const bf16* p, int H, float (&v)[kFfPer]) {
+#pragma unroll
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
+    v[k] = (p && i < H) ? bf2f(p[i]) : 0.f;
+  }
+}
+
+// acc = sum over the split-K slices in slice order (kFfSlices slices' loads in
+// flight together).
+__device__ __forceinline__ void add_slices(const float* base, int parts, int64_t stride, int H,
+                                           float (&acc)[kFfPer]) {
+#pragma unroll
+  for (int k = 0; k < kFfPer; ++k) acc[k] = 0.f;
+  for (int p0 = 0; p0 < parts; p0 += kFfSlices) {
+    float v[kFfSlices][kFfPer];
+#pragma unroll
+    for (int q = 0; q < kFfSlices; ++q)
+#pragma unroll
+      for (int k = 0; k < kFfPer; ++k) {
+        const int i = threadIdx.x + k * kFfThreads;
+        v[q][k] = (p0 + q < parts && i < H) ? __ldcg(base + (p0 + q) * stride + i) : 0.f;
+      }
+#pragma unroll
+    for (int q = 0; q < kFfSlices; ++q)
+#pragma unroll
+      for (int k = 0; k < kFfPer; ++k)
+        if (p0 + q < parts) acc[k] += v[q][k];
+  }
 }
 
 // One CTA per token.  h = bf16(x + bf16(rms(bf16(o)) * w_post_attn));
 // h1 / h2 = bf16(rms(h) * w); xs = bf16(bf16(bf16(rms(h2)) * bf16(root)) * router_scale).
-__global__ void __launch_bounds__(kRowThreads) ff_in_kernel(const bf16* __restrict__ x, const float* __restrict__ o_acc,
-                                                            int o_parts, int64_t o_stride, int H, const bf16* __restrict__ w_post_attn,
-                                                            const bf16* __restrict__ w_pre_ff,
-                                                            const bf16* __restrict__ w_pre_ff2, float eps, float root,
-                                                            const bf16* __restrict__ rscale, bf16* __restrict__ h_out,
-                                                            bf16* __restrict__ h1_out, bf16* __restrict__ h2_out,
-                                                            bf16* __restrict__ xs_out) {
-  __shared__ float red[kRowThreads / 32];
+__global__ void __launch_bounds__(kFfThreads) ff_in_kernel(const bf16* __restrict__ x, const float* __restrict__ o_acc,
+                                                           int o_parts, int64_t o_stride, int H,
+                                                           const bf16* __restrict__ w_post_attn,
+                                                           const bf16* __restrict__ w_pre_ff,
+                                                           const bf16* __restrict__ w_pre_ff2, float eps, float root,
+                                                           const bf16* __restrict__ rscale, bf16* __restrict__ h_out,
+                                                           bf16* __restrict__ h1_out, bf16* __restrict__ h2_out,
+                                                           bf16* __restrict__ xs_out) {
+  __shared__ float red[kFfThreads / 32];
+  const int t = blockIdx.x;
+  float wpa[kFfPer], wpf[kFfPer], wpf2[kFfPer], rsc[kFfPer], xv[kFfPer], a[kFfPer], h[kFfPer], h2[kFfPer];
+  load_row_bf16(w_post_attn, H, wpa);  // constants: before the dependency wait
+  load_row_bf16(w_pre_ff, H, wpf);
+  load_row_bf16(w_pre_ff2, H, wpf2);
+  load_row_bf16(rscale, H, rsc);
   griddep_wait();
   griddep_launch_dependents();
-  const int t = blockIdx.x;
-  const float* o = o_acc + (int64_t)t * H;
-  const bf16* xr = x + (int64_t)t * H;
-  float a[kRowMaxPer], h[kRowMaxPer], h2[kRowMaxPer];
-#pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) a[k] = 0.f;
-  // split-K slices added in order; one slice's loads all in flight together
-  for (int p = 0; p < o_parts; ++p) {
-    float v[kRowMaxPer];
-#pragma unroll
-    for (int k = 0; k < kRowMaxPer; ++k) {
-      const int i = threadIdx.x + k * kRowThreads;
-      v[k] = i < H ? __ldcg(o + p * o_stride + i) : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < kRowMaxPer; ++k) a[k] += v[k];
-  }
+  load_row_bf16(x + (int64_t)t * H, H, xv);
+  add_slices(o_acc + (int64_t)t * H, o_parts, o_stride, H, a);
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
+  for (int k = 0; k < kFfPer; ++k) {
     a[k] = round_bf(a[k]);
     ss = fmaf(a[k], a[k], ss);
   }
-  const float r1 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float r1 = rsqrtf(block_sum<kFfThreads>(ss, red) / (float)H + eps);
   ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
-    h[k] = i < H ? round_bf(bf2f(xr[i]) + round_bf(a[k] * r1 * bf2f(w_post_attn[i]))) : 0.f;
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
+    h[k] = i < H ? round_bf(xv[k] + round_bf(a[k] * r1 * wpa[k])) : 0.f;
     ss = fmaf(h[k], h[k], ss);
   }
-  const float r2 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float r2 = rsqrtf(block_sum<kFfThreads>(ss, red) / (float)H + eps);
   ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
     if (i < H) {
       h_out[(int64_t)t * H + i] = __float2bfloat16_rn(h[k]);
-      h1_out[(int64_t)t * H + i] = __float2bfloat16_rn(h[k] * r2 * bf2f(w_pre_ff[i]));
-      h2[k] = round_bf(h[k] * r2 * bf2f(w_pre_ff2[i]));
+      h1_out[(int64_t)t * H + i] = __float2bfloat16_rn(h[k] * r2 * wpf[k]);
+      h2[k] = round_bf(h[k] * r2 * wpf2[k]);
       h2_out[(int64_t)t * H + i] = __float2bfloat16_rn(h2[k]);
     } else {
       h2[k] = 0.f;
     }
     ss = fmaf(h2[k], h2[k], ss);
   }
-  const float r3 = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float r3 = rsqrtf(block_sum<kFfThreads>(ss, red) / (float)H + eps);
   const float rb = round_bf(root);
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
     if (i < H) {
       float v = round_bf(round_bf(h2[k] * r3) * rb);
-      if (rscale) v = round_bf(v * bf2f(rscale[i]));
+      if (rscale) v = round_bf(v * rsc[k]);
       xs_out[(int64_t)t * H + i] = __float2bfloat16_rn(v);
     }
   }
@@ -112,57 +146,47 @@ __global__ void __launch_bounds__(kRowThreads) ff_in_kernel(const bf16* __restri
 
 // One CTA per token.  x = bf16(bf16(h + bf16(rms(s) * w_post_ff)) * scalar),
 // s = bf16(bf16(rms(bf16(d)) * w1) + bf16(rms(moe) * w2)).
-__global__ void __launch_bounds__(kRowThreads) ff_out_kernel(const bf16* __restrict__ h_res,
-                                                             const float* __restrict__ d_acc, int d_parts,
-                                                             int64_t d_stride,
-                                                             const bf16* __restrict__ moe, int H,
-                                                             const bf16* __restrict__ w1, const bf16* __restrict__ w2,
-                                                             const bf16* __restrict__ w, float eps, float scalar,
-                                                             bf16* __restrict__ x_out) {
-  __shared__ float red[kRowThreads / 32];
+__global__ void __launch_bounds__(kFfThreads) ff_out_kernel(const bf16* __restrict__ h_res,
+                                                            const float* __restrict__ d_acc, int d_parts,
+                                                            int64_t d_stride,
+                                                            const bf16* __restrict__ moe, int H,
+                                                            const bf16* __restrict__ w1, const bf16* __restrict__ w2,
+                                                            const bf16* __restrict__ w, float eps, float scalar,
+                                                            bf16* __restrict__ x_out) {
+  __shared__ float red[kFfThreads / 32];
+  const int t = blockIdx.x;
+  float w1v[kFfPer], w2v[kFfPer], wv[kFfPer], d[kFfPer], m[kFfPer], hr[kFfPer];
+  load_row_bf16(w1, H, w1v);  // constants: before the dependency wait
+  load_row_bf16(w2, H, w2v);
+  load_row_bf16(w, H, wv);
   griddep_wait();
   griddep_launch_dependents();
-  const int t = blockIdx.x;
-  float d[kRowMaxPer], m[kRowMaxPer];
-#pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
-    d[k] = 0.f;
-    m[k] = i < H ? bf2f(moe[(int64_t)t * H + i]) : 0.f;
-  }
-  for (int p = 0; p < d_parts; ++p) {  // split-K slices in order, one slice's loads in flight together
-    float v[kRowMaxPer];
-#pragma unroll
-    for (int k = 0; k < kRowMaxPer; ++k) {
-      const int i = threadIdx.x + k * kRowThreads;
-      v[k] = i < H ? __ldcg(d_acc + p * d_stride + (int64_t)t * H + i) : 0.f;
-    }
-#pragma unroll
-    for (int k = 0; k < kRowMaxPer; ++k) d[k] += v[k];
-  }
+  load_row_bf16(moe + (int64_t)t * H, H, m);
+  load_row_bf16(h_res + (int64_t)t * H, H, hr);
+  add_slices(d_acc + (int64_t)t * H, d_parts, d_stride, H, d);
   float sd = 0.f, sm = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
+  for (int k = 0; k < kFfPer; ++k) {
     d[k] = round_bf(d[k]);
     sd = fmaf(d[k], d[k], sd);
     sm = fmaf(m[k], m[k], sm);
   }
-  const float rd = rsqrtf(block_sum(sd, red) / (float)H + eps);
-  const float rm = rsqrtf(block_sum(sm, red) / (float)H + eps);
+  const float rd = rsqrtf(block_sum<kFfThreads>(sd, red) / (float)H + eps);
+  const float rm = rsqrtf(block_sum<kFfThreads>(sm, red) / (float)H + eps);
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
-    d[k] = i < H ? round_bf(round_bf(d[k] * rd * bf2f(w1[i])) + round_bf(m[k] * rm * bf2f(w2[i]))) : 0.f;
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
+    d[k] = i < H ? round_bf(round_bf(d[k] * rd * w1v[k]) + round_bf(m[k] * rm * w2v[k])) : 0.f;
     ss = fmaf(d[k], d[k], ss);
   }
-  const float rs = rsqrtf(block_sum(ss, red) / (float)H + eps);
+  const float rs = rsqrtf(block_sum<kFfThreads>(ss, red) / (float)H + eps);
   const float sc = round_bf(scalar);
 #pragma unroll
-  for (int k = 0; k < kRowMaxPer; ++k) {
-    const int i = threadIdx.x + k * kRowThreads;
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
     if (i < H) {
-      const float o = round_bf(bf2f(h_res[(int64_t)t * H + i]) + round_bf(d[k] * rs * bf2f(w[i])));
+      const float o = round_bf(hr[k] + round_bf(d[k] * rs * wv[k]));
       x_out[(int64_t)t * H + i] = __float2bfloat16_rn(o * sc);
     }
   }
@@ -244,16 +268,46 @@ __global__ void __launch_bounds__(kRowThreads) softcap_argmax_kernel(float* __re
   }
 }
 
-static cudaLaunchConfig_t row_cfg(dim3 grid, cudaStream_t st, cudaLaunchAttribute* attr) {
+static cudaLaunchConfig_t row_cfg(dim3 grid, cudaStream_t st, cudaLaunchAttribute* attr, int threads = kFfThreads) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kRowThreads);
+  cfg.blockDim = dim3(threads);
   cfg.stream = st;
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cfg;
+}
+
+// ---------------------------------------------------------------------------
+// The dense MLP and the routed experts of a layer depend only on ff_in's
+// outputs and meet again in ff_out, so the experts run on a second stream
+// (fork / join through events; a CUDA-graph capture of the layer records the
+// same two branches).  One side stream and event pair per device, created on
+// first use.
+struct Branch {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+static int branch_for_device(Branch* out) {
+  static Branch per_dev[64];
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return set_error(FMOE_ERR_CUDA, "decoder: no current device");
+  std::lock_guard<std::mutex> lock(mu);
+  Branch& b = per_dev[dev];
+  if (!b.side) {
+    if (cudaStreamCreateWithFlags(&b.side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&b.join, cudaEventDisableTiming) != cudaSuccess) {
+      b = Branch{};
+      return set_error(FMOE_ERR_CUDA, "decoder: side stream: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+  }
+  *out = b;
+  return FMOE_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -471,6 +525,28 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
                        static_cast<const bf16*>(L->router.router_scale), w.hres, w.h1, w.h2, w.xs);
     if ((rc = check_launch("ff_in_kernel"))) return rc;
   }
+  // fork: routed experts (7-9) on the side stream, dense MLP (6, 10) here
+  Branch br;
+  if ((rc = branch_for_device(&br))) return rc;
+  if (cudaEventRecord(br.fork, st) != cudaSuccess || cudaStreamWaitEvent(br.side, br.fork, 0) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "decoder: fork: %s", cudaGetErrorString(cudaGetLastError()));
+  // 7-9 router on the prepared input, routed experts on h2
+  {
+    const cudaStream_t sx = br.side;
+    fmoe_router_t r = L->router;
+    r.use_norm = 0;  // ff_in applied the norm chain
+    if (epc.comm) {  // routed experts on their owning ranks
+      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, nullptr, w.h.status, sx))) return rc;
+      if ((rc = ep_experts(epc.comm, w.h2, T, epc.cap, r.top_k, w.ids, w.wts, ex, static_cast<const bf16*>(epc.prep),
+                           w.moe, w.ep, epc.mode, w.h.status, sx)))
+        return rc;
+    } else {
+      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, sx))) return rc;
+      if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, sx))) return rc;
+    }
+    if (cudaEventRecord(br.join, sx) != cudaSuccess)
+      return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));
+  }
   // 6 dense MLP gate | up
   {
     QgArgs a = {};
@@ -487,20 +563,6 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     QgLayout ql;
     if ((rc = qgemv_plan(a, gq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, gq.bits, true, st))) return rc;
     gu_parts = a.nkc;
-  }
-  // 7-9 router on the prepared input, routed experts on h2
-  {
-    fmoe_router_t r = L->router;
-    r.use_norm = 0;  // ff_in applied the norm chain
-    if (epc.comm) {  // routed experts on their owning ranks
-      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, nullptr, w.h.status, st))) return rc;
-      if ((rc = ep_experts(epc.comm, w.h2, T, epc.cap, r.top_k, w.ids, w.wts, ex, static_cast<const bf16*>(epc.prep),
-                           w.moe, w.ep, epc.mode, w.h.status, st)))
-        return rc;
-    } else {
-      if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, st))) return rc;
-      if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, st))) return rc;
-    }
   }
   // 10 dense down on gelu(g) * u
   {
@@ -521,6 +583,9 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     if ((rc = qgemv_plan(a, dq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, dq.bits, true, st))) return rc;
     d_parts = a.nkc;
   }
+  // join: ff_out needs both branches
+  if (cudaStreamWaitEvent(st, br.join, 0) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));
   // 11 output norms, residual, layer scalar -> x
   {
     cudaLaunchAttribute attr[1];
@@ -605,7 +670,7 @@ int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps,
   QgLayout ql;
   if ((rc = qgemv_plan(a, q.bits, false, &ql)) || (rc = launch_qgemv(a, ql, q.bits, true, st))) return rc;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = row_cfg(dim3(kCapCtas, (unsigned)T), st, attr);
+  cudaLaunchConfig_t cfg = row_cfg(dim3(kCapCtas, (unsigned)T), st, attr, kRowThreads);
   ProfScope prof_("softcap_argmax_kernel", st);
   cudaLaunchKernelEx(&cfg, softcap_argmax_kernel, logits, (int64_t)q.out, softcap, cand, ctr, next_ids, pos_dev);
   return check_launch("softcap_argmax_kernel");

@@ -484,15 +484,20 @@ __device__ __forceinline__ void attn_epilogue(uint8_t* smem, const float* st_m, 
     const int64_t row = (int64_t)b * Hq + hk * GQ + h;
     const float4* src = reinterpret_cast<const float4*>(part_o + row * nsplit * D) + d4;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = wts[h * kMaxSplits + s];
-      const float4 x = __ldcg(src + (int64_t)s * (D / 4));
-      if (w != 0.f) {
-        a.x = fmaf(w, x.x, a.x);
-        a.y = fmaf(w, x.y, a.y);
-        a.z = fmaf(w, x.z, a.z);
-        a.w = fmaf(w, x.w, a.w);
+    for (int s0 = 0; s0 < nsplit; s0 += 8) {  // 8 loads in flight, summed in split order
+      float4 x[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        x[j] = s0 + j < nsplit ? __ldcg(src + (int64_t)(s0 + j) * (D / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float w = s0 + j < nsplit ? wts[h * kMaxSplits + s0 + j] : 0.f;
+        if (w != 0.f) {
+          a.x = fmaf(w, x[j].x, a.x);
+          a.y = fmaf(w, x[j].y, a.y);
+          a.z = fmaf(w, x[j].z, a.z);
+          a.w = fmaf(w, x[j].w, a.w);
+        }
       }
     }
     *reinterpret_cast<float4*>(red2 + h * D + d4 * 4) = a;
@@ -1077,12 +1082,22 @@ static int64_t attn_split_candidate(int64_t chunks, int64_t heads) {
   return chunks >= 8 * four ? four : one;
 }
 
-AttnPlan attn_plan(const KvDev& c, int64_t n) {
+// The last-arriving split of a (batch, kv head) merges nsplit partial rows
+// of GQ x D floats; past kMergeFloats per head that serial merge outweighs what
+// more splits save (full-attention layers: GQ 8 x D 512), so the split count
+// is capped there.
+constexpr int64_t kMergeFloats = 65536;
+static int64_t merge_cap(const KvDev& c, int Hq) {
+  const int64_t gqd = (int64_t)(Hq / c.Hkv) * c.D;
+  return std::max<int64_t>(1, kMergeFloats / std::max<int64_t>(gqd, 1));
+}
+
+AttnPlan attn_plan(const KvDev& c, int64_t n, int Hq) {
   const int CH = chunk_positions(c.mode, c.D);
   const int64_t chunks = n > 0 ? (n + CH - 1) / CH : 1;
   const int64_t heads = (int64_t)c.B * c.Hkv;
   const int64_t ns = std::max<int64_t>(1, std::min<int64_t>({attn_split_candidate(chunks, heads), chunks,
-                                                              (int64_t)kMaxSplits}));
+                                                              merge_cap(c, Hq), (int64_t)kMaxSplits}));
   const int64_t per = (chunks + ns - 1) / ns;
   AttnPlan p;
   p.S = (int)std::min<int64_t>(per * CH, 1 << 30);
@@ -1114,16 +1129,16 @@ static AttnWs carve_attn_ws(void* ws, const KvDev& c, int Hq, int nsplit) {
 
 // Upper bound of attn_plan(c, n).nsplit over every n <= capacity: the larger
 // candidate, before rounding S up to whole chunks (rounding only lowers it).
-static int attn_max_splits(const KvDev& c) {
+static int attn_max_splits(const KvDev& c, int Hq) {
   const int CH = chunk_positions(c.mode, c.D);
   const int64_t chunks = (c.cap + CH - 1) / CH;
   const int64_t heads = (int64_t)c.B * c.Hkv;
   const int64_t ns = std::max(attn_split_candidate(0, heads), attn_split_candidate(INT64_MAX / 2, heads));
-  return (int)std::max<int64_t>(1, std::min<int64_t>({ns, chunks, (int64_t)kMaxSplits}));
+  return (int)std::max<int64_t>(1, std::min<int64_t>({ns, chunks, merge_cap(c, Hq), (int64_t)kMaxSplits}));
 }
 
 size_t attn_workspace_bytes(const KvDev& c, int Hq) {
-  return carve_attn_ws(nullptr, c, Hq, attn_max_splits(c)).bytes;
+  return carve_attn_ws(nullptr, c, Hq, attn_max_splits(c, Hq)).bytes;
 }
 
 int launch_kv_append(const KvDev& c, const bf16* k, const bf16* v, int64_t Tn, int64_t pos, const int64_t* pos_dev,
@@ -1213,7 +1228,7 @@ static int launch_attn_m(const KvDev& c, int GQ, const bf16* q, int Hq, const At
 
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
                        void* ws, bf16* out, cudaStream_t st) {
-  const AttnPlan p = attn_plan(c, nvalid_dev ? c.cap : nvalid);
+  const AttnPlan p = attn_plan(c, nvalid_dev ? c.cap : nvalid, Hq);
   const AttnWs w = carve_attn_ws(ws, c, Hq, p.nsplit);
   const int GQ = Hq / c.Hkv;
   if (c.D == 256)

@@ -41,9 +41,12 @@ __device__ __forceinline__ QgUnit qg_unit(const QgArgs& a, int u) {
   return QgUnit{sg, v / a.nkc, v % a.nkc};
 }
 
+// Called by the whole producer warp: lane 0 arms the stage's barrier, then
+// the lanes issue the row copies in parallel (one copy per row; issuing them
+// from one thread costs a few hundred cycles each).
 template <int BITS, int RT>
 __device__ __forceinline__ void qg_issue(const QgArgs& a, const QgLayout& L, uint8_t* smem, uint64_t* bar, int u,
-                                         int st) {
+                                         int st, int lane) {
   constexpr int R = 16 * RT;
   const QgUnit q = qg_unit(a, u);
   const QgSeg& s = a.seg[q.sg];
@@ -51,16 +54,16 @@ __device__ __forceinline__ void qg_issue(const QgArgs& a, const QgLayout& L, uin
   const int kcbytes = a.kc * BITS / 8, G = a.K / 64, gc = a.kc / 64;
   uint8_t* sb = smem + (size_t)st * L.stage;
   const uint8_t* w = s.w + (int64_t)q.blk * R * rowbytes + (int64_t)q.kci * kcbytes;
-  mbar_arrive_expect_tx(&bar[st], (uint32_t)(R * kcbytes + 2 * R * (L.sfull ? G : gc) * 2));
-#pragma unroll 4
-  for (int r = 0; r < R; ++r) bulk_g2s(sb + r * L.rs, w + r * rowbytes, kcbytes, &bar[st]);
+  if (lane == 0) mbar_arrive_expect_tx(&bar[st], (uint32_t)(R * kcbytes + 2 * R * (L.sfull ? G : gc) * 2));
+  __syncwarp();
+  for (int r = lane; r < R; r += 32) bulk_g2s(sb + r * L.rs, w + r * rowbytes, kcbytes, &bar[st]);
   const bf16* sc = s.s + (int64_t)q.blk * R * G;
   const bf16* bi = s.b + (int64_t)q.blk * R * G;
   if (L.sfull) {  // the block's whole [R][G] scale / bias arrays (contiguous)
-    bulk_g2s(sb + L.soff, sc, R * G * 2, &bar[st]);
-    bulk_g2s(sb + L.soff + R * G * 2, bi, R * G * 2, &bar[st]);
+    if (lane == 0) bulk_g2s(sb + L.soff, sc, R * G * 2, &bar[st]);
+    if (lane == 1) bulk_g2s(sb + L.soff + R * G * 2, bi, R * G * 2, &bar[st]);
   } else {  // the chunk's [R][gc] columns, one 16-byte-multiple copy per row
-    for (int r = 0; r < R; ++r) {
+    for (int r = lane; r < R; r += 32) {
       bulk_g2s(sb + L.soff + r * gc * 2, sc + (int64_t)r * G + q.kci * gc, gc * 2, &bar[st]);
       bulk_g2s(sb + L.soff + R * gc * 2 + r * gc * 2, bi + (int64_t)r * G + q.kci * gc, gc * 2, &bar[st]);
     }
@@ -96,7 +99,6 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
   const int u1 = (int)((int64_t)nb * (blockIdx.x + 1) / gridDim.x) * ub;
   const int n = u1 - u0;
   const int NW = L.nw;
-  const int prod = NW * 32;  // the producer thread
 
   if (tid == 0) {
     for (int s = 0; s < L.nst; ++s) {
@@ -108,8 +110,8 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
   }
   if (tid < L.nst + 1) cnt[tid] = 0;
   __syncthreads();
-  if (tid == prod)
-    for (int i = 0; i < n && i < L.nst; ++i) qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, i);
+  if (warp == NW)
+    for (int i = 0; i < n && i < L.nst; ++i) qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, i, lane);
 
   griddep_wait();  // the input (and the buffers cleared below) belong to earlier kernels
   griddep_launch_dependents();
@@ -225,20 +227,24 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
   // ---- producer: refill each stage once every consumer has released it,
   // then let the last copies land before the warp (and smem) goes away
   if (warp == NW) {
-    if (lane == 0) {
-      int i = L.nst;
-      for (; i < n; ++i) {
-        const int st = i % L.nst;
-        if (*(volatile int*)flag) break;
-        if (!mbar_wait(&empty[st], (uint32_t)((i / L.nst - 1) & 1), a.status, 63)) {
+    int i = L.nst;
+    for (; i < n; ++i) {
+      const int st = i % L.nst;
+      int stop = 0;
+      if (lane == 0) {
+        if (*(volatile int*)flag) {
+          stop = 1;
+        } else if (!mbar_wait(&empty[st], (uint32_t)((i / L.nst - 1) & 1), a.status, 63)) {
           *(volatile int*)flag = 1;
-          break;
+          stop = 1;
         }
-        qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, st);
       }
+      if (__shfl_sync(0xffffffffu, stop, 0)) break;
+      qg_issue<BITS, RT>(a, L, smem, bar, u0 + i, st, lane);
+    }
+    if (lane == 0)
       for (int k = (i > L.nst ? i - L.nst : 0); k < i && k < n; ++k)
         mbar_wait(&bar[k % L.nst], (uint32_t)(k / L.nst) & 1u, a.status, 64);
-    }
     return;
   }
 
