@@ -61,6 +61,9 @@ def parse():
                     help="expert-parallel exchange of the ep_* workloads (default: fixed for decode, exact for "
                          "prefill)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after warm-up, run one eager step between cudaProfilerStart / Stop and exit (for "
+                         "ncu --profile-from-start off launch lists of the decode30 / ep_* workloads)")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
     ap.add_argument("--qlinear-case", default=None, metavar="OUT:IN:BITS:T",
                     help="run only fmoe_qlinear on one shape: four launches, L2 flushed before each, the last one "
@@ -192,6 +195,16 @@ class MoeStack:
                 self.fm.check(rc)
 
 
+def profiled_step(torch, fn):
+    """One eager step between cudaProfilerStart / Stop (ncu --profile-from-start off)."""
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    fn()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"profile_step": "done"}), flush=True)
+
+
 def qlin_bytes(q):
     return q.weight.numel() * q.weight.element_size() + (q.scales.numel() + q.biases.numel()) * 2
 
@@ -244,6 +257,19 @@ def run_decoder(args, rank, world, local):
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream())
 
+    if args.profile_step:
+        with torch.cuda.stream(stream):
+            m.ids.copy_(ids0)
+            m.set_position(CTX)
+            for _ in range(3):
+                m.decode_step()
+            torch.cuda.synchronize()
+            profiled_step(torch, m.decode_step)
+        if ep is not None:
+            ep.close()
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
     # per-kernel device times of eager steps (profiling on)
     with torch.cuda.stream(stream):
         m.ids.copy_(ids0)
@@ -585,6 +611,16 @@ def run_ep_moe(args, rank, world, local):
             else:
                 b.forward(x, out=ys[l])
 
+    if args.profile_step:
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                step()
+            torch.cuda.synchronize()
+            profiled_step(torch, step)
+        comm.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
     with torch.cuda.stream(stream):
         step(keep_ids=True)
         torch.cuda.synchronize()
