@@ -195,6 +195,14 @@ class MoeStack:
                 self.fm.check(rc)
 
 
+def ncu_traffic(workload, kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu captures (profiles/), or None."""
+    try:
+        return json.load(open(os.path.join(ROOT, "profiles", "ncu_traffic.json"))).get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
 def profiled_step(torch, fn):
     """One eager step between cudaProfilerStart / Stop (ncu --profile-from-start off)."""
     torch.cuda.synchronize()
@@ -384,7 +392,7 @@ def run_decoder(args, rank, world, local):
                      "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json hbm_gbs)" if peaks_kind == "measured"
                      else "fallback 6.65 TB/s",
                      "alg_bytes_per_launch": int(alg) if alg else None,
-                     "avg_launch_us": round(tot_ms / n_l * 1e3, 3), "traffic": None},
+                     "avg_launch_us": round(tot_ms / n_l * 1e3, 3), "traffic": ncu_traffic(args.workload, name)},
         "kernels": {k: {"launches_per_step": v[0] // nprof, "avg_us": round(v[1] / v[0] * 1e3, 3),
                         "us_per_step": round(v[1] / nprof * 1e3, 1)}
                     for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
