@@ -67,6 +67,7 @@ class ExpertsC(ctypes.Structure):
         ("intermediate", ctypes.c_int32),
         ("bits", ctypes.c_int32),
         ("group_size", ctypes.c_int32),
+        ("slot_of", ctypes.c_void_p),
     ]
 
 
@@ -343,8 +344,9 @@ class ExpertTable:
     one uint8 buffer [num_experts * stride] (expert e at e*stride)."""
 
     def __init__(self, buf: torch.Tensor, num_experts: int, hidden: int, inter: int, bits=4, group=64,
-                 first_expert=0):
+                 first_expert=0, slot_of: torch.Tensor | None = None):
         self.buf = buf
+        self.slot_of = slot_of  # device int32 [num_experts]: expert e in slot slot_of[e] of buf (host tier)
         self.num_experts = num_experts
         self.hidden = hidden
         self.inter = inter
@@ -352,7 +354,7 @@ class ExpertTable:
         self.group = group
         self.first_expert = first_expert
         self.offsets, self.sizes, self.stride = ecb_layout(hidden, inter, bits, group)
-        assert buf.numel() >= num_experts * self.stride
+        assert slot_of is not None or buf.numel() >= num_experts * self.stride
 
     @classmethod
     def random(cls, num_experts, hidden, inter, bits=4, group=64, std=0.02, seed=0, device="cuda"):
@@ -381,7 +383,13 @@ class ExpertTable:
 
     def cstruct(self) -> ExpertsC:
         return ExpertsC(_ptr(self.buf), self.stride, (ctypes.c_int64 * 9)(*self.offsets), self.num_experts,
-                        self.first_expert, self.hidden, self.inter, self.bits, self.group)
+                        self.first_expert, self.hidden, self.inter, self.bits, self.group, _ptr(self.slot_of))
+
+    def to(self, device, non_blocking: bool = True) -> "ExpertTable":
+        """The same table on another device (e.g. a pinned host copy -> HBM, asynchronously)."""
+        return ExpertTable(self.buf.to(device, non_blocking=non_blocking), self.num_experts, self.hidden, self.inter,
+                           self.bits, self.group, first_expert=self.first_expert,
+                           slot_of=None if self.slot_of is None else self.slot_of.to(device))
 
     def shard(self, rank: int, world: int, copy: bool = False) -> "ExpertTable":
         """Experts [rank*E/world, (rank+1)*E/world) of this (whole) table, for
@@ -517,3 +525,5 @@ from .kv import KV_AFFINE, KV_BF16, KVCache, turbo_round_trip  # noqa: E402
 from .model import GEMMA4_26B, Gemma4DecoderLayer, Gemma4Model  # noqa: E402
 from .ep import (FMOE_EP_EXACT, FMOE_EP_FIXED, EPComm, ExpertParallelMoeBlock, PeerLost, PeerWatch,  # noqa: E402
                  shard_range)
+from . import ecb  # noqa: E402
+from .tier import HostExpertTier, TieredMoeBlock  # noqa: E402

@@ -75,6 +75,7 @@ int to_experts(const fmoe_experts_t* e, ExpertsDev* d) {
   d->first = e->first_expert;
   d->H = e->hidden;
   d->I = e->intermediate;
+  d->slot_of = e->slot_of;
   return FMOE_OK;
 }
 

@@ -44,7 +44,12 @@ struct ExpertsDev {
   int64_t stride;
   int64_t off[9];
   int E, first, H, I;
+  const int32_t* slot_of;  // null, or the slot of each local expert in base
 };
+// Start of local expert e's tensors.
+__device__ __forceinline__ const uint8_t* expert_base(const ExpertsDev& ex, int e) {
+  return ex.base + (int64_t)(ex.slot_of ? __ldg(ex.slot_of + e) : e) * ex.stride;
+}
 
 // Routing metadata built on the device from ids [T, k] (see moe.cu).
 struct RouteMeta {

@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, 3)
   float* red = reinterpret_cast<float*>(smem + L.s_off);    // [kGuWarps][2][16][8] after use
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int row0 = blockIdx.x * 16;
-  const uint8_t* eb = ex.base + (int64_t)e * ex.stride;
+  const uint8_t* eb = expert_base(ex, e);
   const int gbeg = G * warp / kGuWarps, gend = G * (warp + 1) / kGuWarps;
 
   if (threadIdx.x == 0) {
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
   const int4 wk = u < work_len ? work[u] : make_int4(0, 0, 0, 0);
   const int pbeg = wk.y, np = wk.z;
   if (np > 0 && leader) {
-    const uint8_t* eb = ex.base + (int64_t)wk.x * ex.stride;
+    const uint8_t* eb = expert_base(ex, wk.x);
     mbar_arrive_expect_tx(bw, 16u * RB + 2u * sb);
     bulk_g2s(ss, eb + ex.off[6] + (int64_t)row0 * RB, 16 * RB, bw);
     bulk_g2s(ss + L.s_off, eb + ex.off[7] + (int64_t)row0 * Gi * 2, sb, bw);

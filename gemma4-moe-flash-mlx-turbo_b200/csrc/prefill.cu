@@ -469,6 +469,7 @@ int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, c
 }
 
 int check_prefill(const ExpertsDev& d) {
+  if (d.slot_of) return set_error(FMOE_ERR_UNSUPPORTED, "prefill: expert tables with a slot map (decode kernels only)");
   if (d.H % 256 || d.I % 64 || d.H > 8192 || d.E < 1)
     return set_error(FMOE_ERR_UNSUPPORTED, "prefill: hidden %d (multiple of 256), intermediate %d (multiple of 64)",
                      d.H, d.I);

@@ -1822,7 +1822,7 @@ int check_model(const fmoe_decode_model_t* md) {
                        E, H, K);
     const fmoe_experts_t& e = L.experts;
     if (e.bits != 4 || e.group_size != 64 || e.hidden != H || e.intermediate != Ie || e.num_experts != E ||
-        e.first_expert != 0 || !e.base || !aligned(e.base, 16) || e.expert_stride % 16)
+        e.first_expert != 0 || !e.base || !aligned(e.base, 16) || e.expert_stride % 16 || e.slot_of)
       return set_error(FMOE_ERR_UNSUPPORTED, "decode_step: layer %d experts must be all %d, 4-bit, [%d, %d]", i, E, Ie,
                        H);
     for (int j = 0; j < 9; ++j)

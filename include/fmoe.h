@@ -67,6 +67,11 @@ typedef struct fmoe_experts {
   int32_t intermediate;
   int32_t bits;
   int32_t group_size;
+  /* NULL: expert e (local index) is at base + e*expert_stride.  Else a device
+   * int32 [num_experts] slot map: expert e is at base + slot_of[e]*expert_stride
+   * (an HBM cache of slots filled from a pinned host copy; decode expert
+   * kernels only — the prefill and whole-step paths reject it). */
+  const int32_t* slot_of;
 } fmoe_experts_t;
 
 /* Router of Gemma4MoeBlock, src/model/moe.rs:298-312 / 324-345. */
