@@ -428,7 +428,10 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, bo
   }
   a.units = u;
   const int kcb = a.kc * bits / 8, gc = a.kc / 64;
-  L->sfull = (nkc == 1 || (gc * 2) % 16 || (G * 2) % 16) ? 1 : 0;
+  // Scales / biases: the row block's whole [R][G] arrays, one contiguous copy
+  // each, also for column-chunked units (a chunk's own [R][gc] columns would be
+  // 2 R copies of a few dozen bytes, which the copy engine moves far slower).
+  L->sfull = 1;
   L->rs = qg_row_stride(kcb, bits);
   L->soff = R * L->rs;
   L->stage = (int)align_up(L->soff + 2 * R * (L->sfull ? G : gc) * 2, 128);
