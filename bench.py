@@ -254,7 +254,7 @@ def run_decoder(args, rank, world, local):
     cfg = dict(fm.GEMMA4_26B)
     # the same weights on every rank (each keeps its expert slice); per-rank sequences
     m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
-                              ep=ep)
+                              ep=ep).tile_weights()
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
     for L, c in zip(m.layers, m.caches):
         chunk = 256

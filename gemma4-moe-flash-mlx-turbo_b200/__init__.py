@@ -53,6 +53,9 @@ class QWeightC(ctypes.Structure):
         ("in_features", ctypes.c_int32),
         ("bits", ctypes.c_int32),
         ("group_size", ctypes.c_int32),
+        ("tiled", ctypes.c_void_p),
+        ("tiled_kc", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 
@@ -128,6 +131,9 @@ SIGNATURES = {
     "fmoe_quantize": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),
     "fmoe_dequantize": (_I, [ctypes.POINTER(QWeightC), _P, _P]),
     "fmoe_embed_rows": (_I, [ctypes.POINTER(QWeightC), _P, _I64, _F, _P, _P]),
+    "fmoe_qgemv_chunk": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_int32, _I64, ctypes.c_int32]),
+    "fmoe_qweight_tile_bytes": (_SZ, [ctypes.POINTER(QWeightC), ctypes.c_int32]),
+    "fmoe_qweight_tile": (_I, [ctypes.POINTER(QWeightC), ctypes.c_int32, _P, _SZ, _P]),
     "fmoe_qlinear_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(QWeightC)]),
     "fmoe_qlinear": (_I, [_P, _I64, ctypes.POINTER(QWeightC), _P, _P, _SZ, _P]),
     "fmoe_router_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(RouterC)]),
@@ -275,6 +281,7 @@ class QuantizedLinear:
         self.group_size = group_size
         self.out_features = weight.shape[0]
         self.in_features = in_features or (weight.shape[1] if bits == 16 else weight.shape[1] * 32 // bits)
+        self.tiled, self.tiled_kc = None, 0
         self._ws = _Workspace()
 
     @classmethod
@@ -286,7 +293,26 @@ class QuantizedLinear:
 
     def cstruct(self) -> QWeightC:
         return QWeightC(_ptr(self.weight), _ptr(self.scales), _ptr(self.biases), self.out_features,
-                        self.in_features, self.bits, self.group_size)
+                        self.in_features, self.bits, self.group_size, _ptr(self.tiled), self.tiled_kc, 0)
+
+    def tile(self, rows_total: int | None = None, accumulate: bool = False) -> "QuantizedLinear":
+        """Add a copy of the weight in the decode GEMV's tile layout (one contiguous
+        block per 16-row unit).  rows_total: the rows of every weight sharing this
+        one's GEMV launch (they must be tiled alike); accumulate: that launch adds
+        split-K slices (o_proj, dense MLP) rather than storing rows."""
+        rows = self.out_features if rows_total is None else rows_total
+        kc = lib().fmoe_qgemv_chunk(self.in_features, self.bits, rows, int(accumulate))
+        if kc <= 0:
+            raise FmoeError(-5, f"qweight {self.out_features}x{self.in_features} at {self.bits} bits: not tileable")
+        self.tiled = None
+        c = self.cstruct()
+        nbytes = lib().fmoe_qweight_tile_bytes(ctypes.byref(c), kc)
+        if nbytes == 0:
+            raise FmoeError(-5, "qweight tile: unsupported shape")
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=self.weight.device)
+        check(lib().fmoe_qweight_tile(ctypes.byref(c), kc, _ptr(buf), nbytes, _stream()))
+        self.tiled, self.tiled_kc = buf, kc
+        return self
 
     def dequantize(self) -> torch.Tensor:
         out = torch.empty(self.out_features, self.in_features, dtype=torch.bfloat16, device=self.weight.device)

@@ -41,6 +41,8 @@ int to_qw(const fmoe_qweight_t* w, QW* q) {
   q->out = w->out_features;
   q->in = w->in_features;
   q->bits = w->bits;
+  q->tiled = static_cast<const uint8_t*>(w->tiled);
+  q->tiled_kc = w->tiled ? w->tiled_kc : 0;
   return FMOE_OK;
 }
 
@@ -267,7 +269,7 @@ int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, voi
   if (qlinear_streams(T, q, w->group_size)) {
     QgArgs a = {};
     a.nseg = 1;
-    a.seg[0] = QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, y, q.out, q.out, 0, 0};
+    a.seg[0] = QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, y, q.out, q.out, 0, 0, q.tiled, q.tiled_kc};
     a.K = q.in;
     a.T = (int)T;
     a.in_kind = QG_IN_BF16;

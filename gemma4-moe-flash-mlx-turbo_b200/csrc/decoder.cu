@@ -385,7 +385,7 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
 }
 
 static QgSeg seg_of(const QW& q, void* out, int ld, int col0) {
-  return QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, out, q.out, ld, col0, 0};
+  return QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, out, q.out, ld, col0, 0, q.tiled, q.tiled_kc};
 }
 
 static int check_stream_w(const QW& q, int group, const char* what) {

@@ -36,6 +36,8 @@ struct QW {
   const bf16* s;
   const bf16* b;
   int out, in, bits;
+  const uint8_t* tiled;  // decode-GEMV tile layout of w, or null
+  int tiled_kc;
 };
 
 // Device view of an ECB expert table.
@@ -128,6 +130,8 @@ struct QgSeg {
   void* out;         // [T][ld]: f32 or bf16 by QgArgs::out_kind
   int rows, ld, col0;
   int unit0;         // set by qgemv_plan
+  const uint8_t* tiled = nullptr;  // tile layout of w (fmoe_qweight_tile), or null
+  int tiled_kc = 0;
 };
 struct QgArgs {
   QgSeg seg[kQgMaxSeg];
@@ -152,6 +156,9 @@ struct QgLayout {
   int rs, soff, stage, sfull, nst, frag, xsum, red, misc, cnt, bar, bytes, grid, nw, rt;
 };
 int qgemv_plan(QgArgs& a, int bits, bool allow_split, QgLayout* L, bool half_sm = false);
+// Column chunk (inputs) of the plan for rows_total rows of K inputs; 0 if none.
+int qgemv_chunk(int K, int bits, int64_t rows_total, bool allow_split);
+int qgemv_row_stride(int kc_bytes, int bits);
 int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStream_t st);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }

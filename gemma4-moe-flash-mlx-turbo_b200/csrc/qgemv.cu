@@ -54,9 +54,15 @@ __device__ __forceinline__ void qg_issue(const QgArgs& a, const QgLayout& L, uin
   const int kcbytes = a.kc * BITS / 8, G = a.K / 64, gc = a.kc / 64;
   uint8_t* sb = smem + (size_t)st * L.stage;
   const uint8_t* w = s.w + (int64_t)q.blk * R * rowbytes + (int64_t)q.kci * kcbytes;
-  if (lane == 0) mbar_arrive_expect_tx(&bar[st], (uint32_t)(R * kcbytes + 2 * R * (L.sfull ? G : gc) * 2));
+  const int wbytes = s.tiled ? R * L.rs : R * kcbytes;
+  if (lane == 0) mbar_arrive_expect_tx(&bar[st], (uint32_t)(wbytes + 2 * R * (L.sfull ? G : gc) * 2));
   __syncwarp();
-  for (int r = lane; r < R; r += 32) bulk_g2s(sb + r * L.rs, w + r * rowbytes, kcbytes, &bar[st]);
+  if (s.tiled) {  // the unit's RT tiles are one contiguous run of the tile layout
+    if (lane == 0)
+      bulk_g2s(sb, s.tiled + (((int64_t)q.blk * RT) * a.nkc + q.kci) * 16 * L.rs, (uint32_t)wbytes, &bar[st]);
+  } else {
+    for (int r = lane; r < R; r += 32) bulk_g2s(sb + r * L.rs, w + r * rowbytes, kcbytes, &bar[st]);
+  }
   const bf16* sc = s.s + (int64_t)q.blk * R * G;
   const bf16* bi = s.b + (int64_t)q.blk * R * G;
   if (L.sfull) {  // the block's whole [R][G] scale / bias arrays (contiguous)
@@ -358,7 +364,7 @@ __global__ void __launch_bounds__((kQgMaxWarps + 1) * 32, 1) qgemv_kernel(const 
 
 // Padded smem row stride: residues (mod 128 B) measured conflict-free for the
 // lane access patterns of load_a_frags.
-static int qg_row_stride(int bytes, int bits) {
+int qgemv_row_stride(int bytes, int bits) {
   const int want = bits == 4 ? 32 : bits == 6 ? 16 : 64;
   int s = (bytes + 15) & ~15;
   while (s % 128 != want) s += 16;
@@ -396,7 +402,22 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, bo
   // fewest column chunks that keep a stage's codes <= 48 KB, and (for
   // accumulating outputs) more chunks while the units split unevenly over the SMs.
   int rt = 1, nkc = 0;
-  if (try_rt2 && even32 && tiles / 2 >= 4 * kNumSMs && 32 * K * bits / 8 <= 96 * 1024) {
+  // tiled segments (all or none) fix the column chunk; their layout keeps the
+  // two tiles of a 32-row unit adjacent only without column chunks
+  int tiled = 0, tkc = 0;
+  for (int i = 0; i < a.nseg; ++i)
+    if (a.seg[i].tiled) {
+      if (tiled && a.seg[i].tiled_kc != tkc) return set_error(FMOE_ERR_INVALID, "qgemv: segments tiled differently");
+      tkc = a.seg[i].tiled_kc;
+      ++tiled;
+    }
+  if (tiled && (tiled != a.nseg || tkc < 64 || tkc % 64 || K % tkc || 16 * tkc * bits / 8 > 64 * 1024))
+    return set_error(FMOE_ERR_INVALID, "qgemv: tiled chunk %d (K %d)", tkc, K);
+  if (tiled) {
+    nkc = K / tkc;
+    if (nkc > 1 && !allow_split) return set_error(FMOE_ERR_INVALID, "qgemv: tiled chunk needs split output");
+    if (try_rt2 && nkc == 1 && even32 && tiles / 2 >= 4 * kNumSMs && 32 * K * bits / 8 <= 96 * 1024) rt = 2;
+  } else if (try_rt2 && even32 && tiles / 2 >= 4 * kNumSMs && 32 * K * bits / 8 <= 96 * 1024) {
     rt = 2;
     nkc = 1;
   } else {
@@ -432,7 +453,7 @@ static int qgemv_plan_rt(QgArgs& a, int bits, bool allow_split, bool try_rt2, bo
   // each, also for column-chunked units (a chunk's own [R][gc] columns would be
   // 2 R copies of a few dozen bytes, which the copy engine moves far slower).
   L->sfull = 1;
-  L->rs = qg_row_stride(kcb, bits);
+  L->rs = qgemv_row_stride(kcb, bits);
   L->soff = R * L->rs;
   L->stage = (int)align_up(L->soff + 2 * R * (L->sfull ? G : gc) * 2, 128);
   // consumer warps: the count (8..16) that deals a unit's groups most evenly
@@ -504,3 +525,79 @@ int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStr
 }
 
 }  // namespace fmoe
+
+// ---------------------------------------------------------------------------
+// Tile layout (fmoe_qweight_tile): [16-row tile][column chunk][16 rows][rs]
+// bytes, rs = the GEMV's padded row stride for a chunk, padding zero.
+
+namespace fmoe {
+
+int qgemv_chunk(int K, int bits, int64_t rows_total, bool allow_split) {
+  if ((bits != 4 && bits != 6 && bits != 8) || K % 64 || rows_total < 16 || rows_total % 16) return 0;
+  const int G = K / 64;
+  const int64_t tiles = rows_total / 16;
+  if (rows_total % 32 == 0 && tiles / 2 >= 4 * kNumSMs && 32 * K * bits / 8 <= 96 * 1024) return K;
+  int nkc = 0;
+  double best_eff = -1.0;
+  for (int c = 1; c <= G; ++c) {
+    if (G % c || (c > 1 && G / c < 8)) continue;
+    if (16 * (K / c) * bits / 8 > 48 * 1024) continue;
+    if (nkc && !allow_split) break;
+    const int64_t u = tiles * c, per = (u + kNumSMs - 1) / kNumSMs;
+    const double eff = u < kNumSMs ? 1.0 : (double)u / (double)(per * kNumSMs);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      nkc = c;
+    }
+    if (!allow_split || eff >= 0.9 || u >= 6 * kNumSMs) break;
+  }
+  return nkc ? K / nkc : 0;
+}
+
+__global__ void qg_tile_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t rowbytes, int kcb, int nkc, int rs,
+                               uint8_t* __restrict__ out) {
+  const int wpr = rs / 16;  // 16-byte words per padded row piece
+  const int64_t n = rows * nkc * wpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int j = (int)(i % wpr);
+    const int64_t pr = i / wpr;  // (tile, chunk, row) piece
+    const int r = (int)(pr % 16);
+    const int64_t tc = pr / 16;
+    const int c = (int)(tc % nkc);
+    const int64_t tile = tc / nkc;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (j * 16 < kcb) v = *reinterpret_cast<const uint4*>(w + (tile * 16 + r) * rowbytes + (int64_t)c * kcb + j * 16);
+    reinterpret_cast<uint4*>(out)[i] = v;
+  }
+}
+
+}  // namespace fmoe
+
+using namespace fmoe;
+
+extern "C" int32_t fmoe_qgemv_chunk(int32_t in_features, int32_t bits, int64_t rows_total, int32_t accumulate) {
+  return qgemv_chunk(in_features, bits, rows_total, accumulate != 0);
+}
+
+extern "C" size_t fmoe_qweight_tile_bytes(const fmoe_qweight_t* w, int32_t kc) {
+  QW q;
+  if (to_qw(w, &q) || (q.bits != 4 && q.bits != 6 && q.bits != 8) || q.out % 16 || kc < 64 || kc % 64 ||
+      q.in % kc)
+    return 0;
+  return (size_t)q.out * (q.in / kc) * qgemv_row_stride(kc * q.bits / 8, q.bits);
+}
+
+extern "C" int fmoe_qweight_tile(const fmoe_qweight_t* w, int32_t kc, void* out, size_t bytes, void* stream) {
+  QW q;
+  int rc;
+  if ((rc = to_qw(w, &q))) return rc;
+  const size_t need = fmoe_qweight_tile_bytes(w, kc);
+  if (!need) return set_error(FMOE_ERR_INVALID, "qweight_tile: %d x %d at %d bits, chunk %d", q.out, q.in, q.bits, kc);
+  if (!out || bytes < need || !aligned(out, 16) || !aligned(q.w, 16))
+    return set_error(FMOE_ERR_WORKSPACE, "qweight_tile: %zu bytes (16-byte aligned) required", need);
+  const int kcb = kc * q.bits / 8, rs = qgemv_row_stride(kcb, q.bits);
+  qg_tile_kernel<<<4 * kNumSMs, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(q.w), q.out, (int64_t)q.in * q.bits / 8, kcb, q.in / kc, rs,
+      static_cast<uint8_t*>(out));
+  return check_launch("qg_tile_kernel");
+}

@@ -82,7 +82,7 @@ class Gemma4DecoderLayer:
     def cstruct(self) -> DecoderLayerC:
         if self._c is None:
             n = self.norms
-            empty = QWeightC(None, None, None, 0, 0, 0, 0)
+            empty = QWeightC(None, None, None, 0, 0, 0, 0, None, 0, 0)
             r = self.router
             rc = RouterC(r["proj"].cstruct(), _ptr(r.get("router_scale")), _ptr(r.get("per_expert_scale")), None,
                          r["root_size"], self.eps, 1, self.top_k)
@@ -95,6 +95,21 @@ class Gemma4DecoderLayer:
                 self.num_heads, self.num_kv_heads, self.head_dim, self.rope_dims, int(self.k_eq_v), 0,
                 self.rope_theta, self.eps, self.layer_scalar, self.attn_scale)
         return self._c
+
+    def tile_weights(self):
+        """Tile-layout copies of the projections for the decode GEMVs (one GEMV
+        launch each: q|k|v, o, dense gate|up, dense down)."""
+        qkv = [self.q_proj, self.k_proj] + ([] if self.k_eq_v else [self.v_proj])
+        rows = sum(q.out_features for q in qkv)
+        for q in qkv:
+            q.tile(rows, accumulate=False)
+        self.o_proj.tile(accumulate=True)
+        g, u, d = self.mlp
+        g.tile(g.out_features + u.out_features, accumulate=True)
+        u.tile(g.out_features + u.out_features, accumulate=True)
+        d.tile(accumulate=True)
+        self._c = None
+        return self
 
     def workspace_bytes(self, T, cache: KVCache) -> int:
         return lib().fmoe_decoder_workspace_bytes(T, ctypes.byref(self.cstruct()), ctypes.byref(cache.c))
@@ -200,6 +215,15 @@ class Gemma4Model:
         self._emb_scale = math.sqrt(H)
         self._embed_c = embed.cstruct()
         self._fc = None
+
+    def tile_weights(self):
+        """Tile-layout copies of every decode-GEMV weight (layers and lm_head)."""
+        for L in self.layers:
+            L.tile_weights()
+        self.embed.tile(accumulate=False)
+        self._embed_c = self.embed.cstruct()
+        self._fc = None
+        return self
 
     @classmethod
     def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None, ep=None,

@@ -50,6 +50,12 @@ typedef struct fmoe_qweight {
   int32_t in_features;
   int32_t bits;
   int32_t group_size;
+  /* Optional copy of w in the streaming GEMV's tile layout (fmoe_qweight_tile;
+   * NULL: none).  The decode GEMV then moves one contiguous block per 16-row
+   * unit instead of one copy per row.  tiled_kc: its column chunk in inputs. */
+  const void* tiled;
+  int32_t tiled_kc;
+  int32_t reserved;
 } fmoe_qweight_t;
 
 /* Routed experts of one MoE layer in the ECB expert-major layout written by
@@ -133,6 +139,17 @@ int fmoe_embed_rows(const fmoe_qweight_t* w, const int32_t* ids, int64_t n, floa
  * weight, scales and biases), bits 4, 8 and 16 (bf16) at any T, group 64,
  * in % 64 == 0, out % 16 == 0.  The workspace holds fp32 partial sums
  * (fmoe_qlinear_workspace_bytes). */
+/* Tile layout of a 4/6/8-bit weight for the decode GEMV: for each 16-row tile
+ * and each chunk of kc inputs, the tile's 16 row pieces (kc*bits/8 bytes each)
+ * at a padded row stride, contiguous.  fmoe_qgemv_chunk gives the kc the GEMV
+ * uses for a launch over rows_total weight rows sharing one input (all the
+ * segments of that launch must be tiled with it); accumulate != 0 for launches
+ * whose output accumulates split-K slices (the dense MLP, o_proj), 0 otherwise
+ * (q|k|v, lm_head).  0: not tileable. */
+int32_t fmoe_qgemv_chunk(int32_t in_features, int32_t bits, int64_t rows_total, int32_t accumulate);
+size_t fmoe_qweight_tile_bytes(const fmoe_qweight_t* w, int32_t kc);
+int fmoe_qweight_tile(const fmoe_qweight_t* w, int32_t kc, void* out, size_t bytes, void* stream);
+
 size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w);
 int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, void* workspace,
                  size_t workspace_bytes, void* stream);

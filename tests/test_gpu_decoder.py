@@ -111,6 +111,48 @@ def test_lm_head_matches_oracle(fm, orc, dev):
             assert int(ids[t]) == int(want_ids[t])
 
 
+@pytest.mark.parametrize("out_f,in_f,bits,T", [(8192, 2816, 8, 1), (2816, 4096, 8, 3), (4224, 2816, 4, 1),
+                                               (2816, 2112, 4, 8), (4096, 2816, 6, 2)])
+def test_tiled_weights_give_identical_gemv(fm, dev, out_f, in_f, bits, T):
+    """The tile layout only changes how the weights are staged: bit-identical
+    outputs, except where the standalone call accumulates column chunks with
+    atomics (K = 4096 at 8 bits: sums in arrival order), there within 1e-2."""
+    g = torch.Generator(device=dev).manual_seed(out_f + bits)
+    w = torch.randn(out_f, in_f, generator=g, device=dev) * 0.02
+    a = fm.QuantizedLinear.from_float(w, bits)
+    split = 16 * in_f * bits // 8 > 48 * 1024  # needs column chunks: accumulating output
+    b = fm.QuantizedLinear(a.weight, a.scales, a.biases, bits, 64, in_features=in_f).tile(accumulate=split)
+    x = torch.randn(T, in_f, generator=g, device=dev).to(torch.bfloat16)
+    ya, yb = a.forward(x), b.forward(x)
+    if split:
+        assert max_rel_err(yb.float().cpu().numpy(), ya.float().cpu().numpy()) <= 1e-2
+    else:
+        assert torch.equal(ya, yb)
+
+
+def test_decoder_tiled_weights_identical(fm, dev):
+    cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=2)
+    ctx = 300
+    m1 = fm.Gemma4Model.random(cfg, batch=1, max_positions=1024, seed=31, device=dev, n_layers=2)
+    g = torch.Generator(device=dev).manual_seed(32)
+    kvs = []
+    for L, c in zip(m1.layers, m1.caches):
+        kv = torch.randn(2, 1, L.num_kv_heads, ctx, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+        c.update(kv[0], kv[1])
+        kvs.append(kv)
+    m1.ids.fill_(9)
+    m1.set_position(ctx)
+    want = [(m1.decode_step().clone(), m1.logits.clone()) for _ in range(2)]
+    m2 = fm.Gemma4Model(cfg, m1.embed, m1.layers, m1.final_norm, 1, 1024, device=dev).tile_weights()
+    for kv, c in zip(kvs, m2.caches):
+        c.update(kv[0], kv[1])
+    m2.ids.fill_(9)
+    m2.set_position(ctx)
+    for ids, lg in want:
+        assert torch.equal(m2.decode_step(), ids)
+        assert torch.equal(m2.logits, lg)
+
+
 def test_decode_step_graph_replay_is_deterministic(fm, dev):
     """Eager steps and CUDA-graph replays (position on the device) give the same
     tokens and logits; the position advances once per step.  700 cached
