@@ -63,6 +63,7 @@ static_assert(STAGE % 1024 == 0 && OFF_WQ % 1024 == 0 && WQS % 1024 == 0, "stage
 
 struct alignas(64) Maps {
   CUtensorMap a;   // A rows (bf16 [P][K], 128-byte swizzle, box 64 x 128)
+  CUtensorMap a_small[3];  // the same with boxes of 16, 32 and 64 rows (tiles of few tokens)
   CUtensorMap w0;  // packed weights (u8 [E][rows][K/2], 128-byte swizzle, box 128 x 128 (GEMM1) / 256 (GEMM2) x 1)
   CUtensorMap w1;  // GEMM1: the up projection
 };
@@ -165,8 +166,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
           const int s = q % NS;
           if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 301);
           if (*failed) break;
-          mbar_arrive_expect_tx(&xfull[s], (uint32_t)X_BYTES);
-          tma2d(smem + s * STAGE + OFF_X, &maps.a, kt * BK, row0, &xfull[s]);
+          // only the tile's token rows (rounded up to a box of 16 / 32 / 64 / 128)
+          const int ntok = tl.z, hb = ntok <= 16 ? 0 : ntok <= 32 ? 1 : ntok <= 64 ? 2 : 3;
+          mbar_arrive_expect_tx(&xfull[s], (uint32_t)((16 << hb) * BK * 2));
+          tma2d(smem + s * STAGE + OFF_X, hb < 3 ? &maps.a_small[hb] : &maps.a, kt * BK, row0, &xfull[s]);
         }
         if (*failed) break;
       }
@@ -528,6 +531,12 @@ int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, con
     const cuuint64_t dW[3] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.I, (cuuint64_t)d.E};
     const cuuint64_t sW[2] = {(cuuint64_t)d.H / 2, (cuuint64_t)d.stride};
     const cuuint32_t bW[3] = {128, 128, 1};
+    for (int h = 0; h < 3; ++h) {
+      const cuuint32_t bS[2] = {64, (cuuint32_t)(16 << h)};
+      if ((rc = encode(&m1.a_small[h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.xs, dA, sA, bS, CU_TENSOR_MAP_SWIZZLE_128B,
+                       "x")))
+        return rc;
+    }
     if ((rc = encode(&m1.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.xs, dA, sA, bA, CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
         (rc = encode(&m1.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[0], dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
                      "gate")) ||
@@ -538,6 +547,12 @@ int run_prefill_experts(const bf16* x, int64_t T, int k, const int32_t* ids, con
     const cuuint64_t dW2[3] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.H, (cuuint64_t)d.E};
     const cuuint64_t sW2[2] = {(cuuint64_t)d.I / 2, (cuuint64_t)d.stride};
     const cuuint32_t bW2[3] = {128, (cuuint32_t)pf::BN, 1};
+    for (int h = 0; h < 3; ++h) {
+      const cuuint32_t bS[2] = {64, (cuuint32_t)(16 << h)};
+      if ((rc = encode(&m2.a_small[h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.act, dA2, sA2, bS,
+                       CU_TENSOR_MAP_SWIZZLE_128B, "act")))
+        return rc;
+    }
     if ((rc = encode(&m2.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w.act, dA2, sA2, bA, CU_TENSOR_MAP_SWIZZLE_128B,
                      "act")) ||
         (rc = encode(&m2.w0, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, d.base + d.off[6], dW2, sW2, bW2,
