@@ -57,9 +57,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode30_b1", choices=sorted(WORKLOADS) + sorted(EP_WORKLOADS))
-    ap.add_argument("--ep-mode", default=None, choices=["fixed", "exact"],
-                    help="expert-parallel exchange of the ep_* workloads (default: fixed for decode, exact for "
-                         "prefill)")
+    ap.add_argument("--ep-mode", default=None, choices=["fixed", "exact", "p2p"],
+                    help="expert-parallel exchange (default: fixed for decode, exact for prefill; p2p = fixed's "
+                         "layout stored into the peers' memory by the library's kernels; decode30 at N > 1 takes "
+                         "fixed or p2p)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one eager step between cudaProfilerStart / Stop and exit (for "
@@ -253,8 +254,11 @@ def run_decoder(args, rank, world, local):
     T = WORKLOADS[args.workload]
     cfg = dict(fm.GEMMA4_26B)
     # the same weights on every rank (each keeps its expert slice); per-rank sequences
+    ep_mode = fm.FMOE_EP_P2P if args.ep_mode == "p2p" else fm.FMOE_EP_FIXED
+    if args.ep_mode == "exact":
+        raise SystemExit("decode30: the exact exchange syncs the host per layer and cannot be captured")
     m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
-                              ep=ep).tile_weights()
+                              ep=ep, ep_mode=ep_mode).tile_weights()
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
     for L, c in zip(m.layers, m.caches):
         chunk = 256
@@ -353,8 +357,10 @@ def run_decoder(args, rank, world, local):
     alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
     par = "single GPU" if world == 1 else (
-        f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined by NCCL "
-        f"send/recv over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
+        f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined "
+        + ("by stores into the peers' exchange windows (CUDA IPC, flag-synchronised)" if args.ep_mode == "p2p"
+           else "by NCCL send/recv")
+        + " over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
         f"replicated; one sequence per GPU")
     result = {
         "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
@@ -584,7 +590,7 @@ def run_ep_moe(args, rank, world, local):
     torch.cuda.set_device(dev)
     total, mode_name = EP_WORKLOADS[args.workload]
     mode_name = args.ep_mode or mode_name
-    mode = fm.FMOE_EP_FIXED if mode_name == "fixed" else fm.FMOE_EP_EXACT
+    mode = {"fixed": fm.FMOE_EP_FIXED, "exact": fm.FMOE_EP_EXACT, "p2p": fm.FMOE_EP_P2P}[mode_name]
     if total % world or E % world:
         raise SystemExit(f"{total} tokens / {E} experts do not split over {world} GPUs")
     T = total // world
@@ -653,7 +659,7 @@ def run_ep_moe(args, rank, world, local):
     uniq_local = sum(int(torch.unique(all_ids[l][local[l]]).numel()) for l in range(nl)) / nl
 
     graph = None
-    if mode == fm.FMOE_EP_FIXED:
+    if mode in (fm.FMOE_EP_FIXED, fm.FMOE_EP_P2P):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             torch.cuda.synchronize()
@@ -726,9 +732,11 @@ def run_ep_moe(args, rank, world, local):
                 "per expert)",
         "config": {"workload": args.workload, "layers": nl, "hidden": H, "experts": E, "top_k": K,
                    "expert_intermediate": I, "tokens_per_step": total, "tokens_per_gpu": T,
-                   "parallelism": f"expert-parallel x{world}: {per} experts per GPU, NCCL grouped send/recv "
-                                  f"dispatch + combine ({mode_name} exchange); router replicated, tokens split",
-                   "exchange_bytes_per_layer_per_gpu": (world * T * row_b * 2) if mode_name == "fixed" else None,
+                   "parallelism": f"expert-parallel x{world}: {per} experts per GPU, "
+                                  + ("peer-memory stores (CUDA IPC windows)" if mode_name == "p2p"
+                                     else "NCCL grouped send/recv")
+                                  + f" dispatch + combine ({mode_name} exchange); router replicated, tokens split",
+                   "exchange_bytes_per_layer_per_gpu": (world * T * row_b * 2) if mode_name in ("fixed", "p2p") else None,
                    "graph": "one CUDA graph per step" if graph is not None else "eager (exact mode syncs per layer)",
                    "l2": "inputs larger than L2 (expert slices resident)"},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,

@@ -155,6 +155,8 @@ SIGNATURES = {
     "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),
     "fmoe_lm_head_workspace_bytes": (_SZ, [_I64]),
     "fmoe_lm_head": (_I, [ctypes.POINTER(QWeightC), _P, _F, _P, _I64, _F, _P, _P, _P, _P, _SZ, _P]),
+    "fmoe_sample_workspace_bytes": (_SZ, [_I64, _I64]),
+    "fmoe_sample": (_I, [_P, _I64, _I64, _P, _I, _F, _F, _F, ctypes.c_uint64, _P, _I, _P, _P, _SZ, _P]),
     "fmoe_moe_prefill_prepare_bytes": (_SZ, [ctypes.POINTER(ExpertsC)]),
     "fmoe_moe_prefill_prepare": (_I, [ctypes.POINTER(ExpertsC), _P, _SZ, _P]),
     "fmoe_moe_prefill_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC)]),
@@ -167,6 +169,7 @@ SIGNATURES = {
     "fmoe_ep_comm_destroy": (_I, [_P]),
     "fmoe_ep_comm_abort": (_I, [_P]),
     "fmoe_ep_comm_status": (_I, [_P]),
+    "fmoe_ep_p2p_init": (_I, [_P, _I64, _I, _I]),
     "fmoe_ep_moe_workspace_bytes": (_SZ, [_I, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC)]),
     "fmoe_ep_moe_forward": (_I, [_P, _P, _I64, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P,
                                  _P, _I, _P, _SZ, _P]),
@@ -549,7 +552,8 @@ class Gemma4MoeBlock:
 
 from .kv import KV_AFFINE, KV_BF16, KVCache, turbo_round_trip  # noqa: E402
 from .model import GEMMA4_26B, Gemma4DecoderLayer, Gemma4Model  # noqa: E402
-from .ep import (FMOE_EP_EXACT, FMOE_EP_FIXED, EPComm, ExpertParallelMoeBlock, PeerLost, PeerWatch,  # noqa: E402
+from .ep import (FMOE_EP_EXACT, FMOE_EP_FIXED, FMOE_EP_P2P, EPComm, ExpertParallelMoeBlock, PeerLost, PeerWatch,  # noqa: E402
                  shard_range)
 from . import ecb  # noqa: E402
 from .tier import HostExpertTier, TieredMoeBlock  # noqa: E402
+from .sample import Sampler, sample_tokens  # noqa: E402

@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <cstdio>
 #include <mutex>
 #include <vector>
 
@@ -39,6 +40,13 @@ struct fmoe_ep_comm {
   int rank;
   int device;
   int32_t* host_counts;  // pinned [2 * n_ranks]: send counts | receive counts (EXACT mode)
+  // peer-memory exchange (fmoe_ep_p2p_init): every rank's window mapped here
+  uint8_t* win = nullptr;
+  uint8_t* peer_win[8] = {};
+  int64_t p2p_cap = 0;
+  int p2p_hidden = 0, p2p_k = 0;
+  uint32_t* seq = nullptr;     // device: exchanges completed
+  unsigned* done = nullptr;    // device [2]: finished CTAs of the dispatch / return kernels
 };
 
 namespace fmoe {
@@ -140,6 +148,150 @@ __global__ void combine_kernel(const float* __restrict__ ret, const int32_t* __r
 }
 
 // ---------------------------------------------------------------------------
+// Peer-memory exchange (FMOE_EP_P2P): every rank owns a window mapped into the
+// others (CUDA IPC over NVLink).  The dispatch kernel stores each routed row
+// straight into the owning rank's window (block `me` of its receive rows, at
+// the token's slot) — pack and send in one pass; the return kernel stores the
+// fp32 partial sums into the source rank's window.  The last CTA of each
+// publishes a flag per destination (system-scope release after a system fence);
+// the receiver's wait kernel polls its flags (acquire, bounded) before the
+// expert kernels read the rows.  Flags carry the exchange number (device
+// counter `seq`), so nothing is reset between exchanges, and a CUDA graph can
+// replay the sequence.  Plain stores only (no TMA, no multicast).
+
+struct WinLayout {
+  size_t rx_flag, ret_flag, rx_cnt, rx, rids, rwts, ret, bytes;
+};
+__host__ __device__ inline size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+inline WinLayout win_layout(int R, int64_t cap, int H, int k) {
+  WinLayout L;
+  size_t o = 0;
+  L.rx_flag = o;
+  o += 256;
+  L.ret_flag = o;
+  o += 256;
+  L.rx_cnt = o;  // int32 [8]: rows each source rank routed here
+  o += 256;
+  L.rx = o;
+  o = al256(o + (size_t)R * cap * H * 2);
+  L.rids = o;
+  o = al256(o + (size_t)R * cap * k * 4);
+  L.rwts = o;
+  o = al256(o + (size_t)R * cap * k * 4);
+  L.ret = o;
+  o = al256(o + (size_t)R * cap * H * 4);
+  L.bytes = o;
+  return L;
+}
+struct PeerWins {
+  uint8_t* w[8];
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The last CTA (device counter `done`, reset by it) publishes seq + 1 in the
+// flag slot `me` of every rank's window at byte offset `flag_off`.
+__device__ __forceinline__ void publish_flags(const PeerWins& pw, size_t flag_off, int R, int me,
+                                              const uint32_t* seq, unsigned* done) {
+  __shared__ int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence_system();
+  const uint32_t v = *reinterpret_cast<const volatile uint32_t*>(seq) + 1;
+  if (threadIdx.x < R) st_release_sys(reinterpret_cast<uint32_t*>(pw.w[threadIdx.x] + flag_off) + me, v);
+  if (threadIdx.x == 0) *done = 0;
+}
+
+__global__ void p2p_dispatch_kernel(const bf16* __restrict__ x, const int32_t* __restrict__ ids,
+                                    const float* __restrict__ wts, const int32_t* __restrict__ slots,
+                                    const int32_t* __restrict__ counts, int T, int k, int H, int R, int cap, int me,
+                                    PeerWins pw, WinLayout L, const uint32_t* seq, unsigned* done) {
+  const int words = H / 8;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n = (int64_t)R * T * words;
+  if (blockIdx.x == 0 && threadIdx.x < R)
+    reinterpret_cast<int32_t*>(pw.w[threadIdx.x] + L.rx_cnt)[me] = counts[threadIdx.x];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int r = (int)(i / ((int64_t)T * words));
+    const int rem = (int)(i % ((int64_t)T * words));
+    const int t = rem / words, w = rem % words;
+    const int s = slots[(int64_t)r * cap + t];
+    if (s < 0) continue;
+    const int64_t row = (int64_t)me * cap + s;
+    uint8_t* win = pw.w[r];
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(win + L.rx) + row * H + 8 * w) =
+        *reinterpret_cast<const uint4*>(x + (int64_t)t * H + 8 * w);
+    if (w < k) {
+      reinterpret_cast<int32_t*>(win + L.rids)[row * k + w] = ids[(int64_t)t * k + w];
+      reinterpret_cast<float*>(win + L.rwts)[row * k + w] = wts[(int64_t)t * k + w];
+    }
+  }
+  const int64_t m = (int64_t)R * cap * k;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m; i += stride) {
+    const int r = (int)(i / ((int64_t)cap * k));
+    const int j = (int)((i % ((int64_t)cap * k)) / k), c = (int)(i % k);
+    if (j >= counts[r]) {
+      const int64_t o = ((int64_t)me * cap + j) * k + c;
+      reinterpret_cast<int32_t*>(pw.w[r] + L.rids)[o] = -1;
+      reinterpret_cast<float*>(pw.w[r] + L.rwts)[o] = 0.f;
+    }
+  }
+  publish_flags(pw, L.rx_flag, R, me, seq, done);
+}
+
+// Partial sums of the rows received from rank r (block r of ypart, its first
+// rx_cnt[r] rows) go to block `me` of r's returned rows.
+__global__ void p2p_return_kernel(const float* __restrict__ ypart, int R, int cap, int H, int me, PeerWins pw,
+                                  WinLayout L, const uint32_t* seq, unsigned* done) {
+  const int q4 = H / 4;
+  const int64_t n = (int64_t)R * cap * q4;
+  const int32_t* cnt = reinterpret_cast<const int32_t*>(pw.w[me] + L.rx_cnt);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / ((int64_t)cap * q4));
+    const int64_t rem = i % ((int64_t)cap * q4);
+    const int row = (int)(rem / q4), c = (int)(rem % q4);
+    if (row >= cnt[r]) continue;
+    reinterpret_cast<float4*>(reinterpret_cast<float*>(pw.w[r] + L.ret) + ((int64_t)me * cap + row) * H)[c] =
+        reinterpret_cast<const float4*>(ypart + ((int64_t)r * cap + row) * H)[c];
+  }
+  publish_flags(pw, L.ret_flag, R, me, seq, done);
+}
+
+// One warp: lane r waits until flag r reaches seq + 1 (bounded; a timeout sets
+// *status).  advance != 0: then seq = seq + 1 (the exchange is complete).
+constexpr int kP2pPolls = 1 << 22;
+__global__ void p2p_wait_kernel(const uint8_t* win, size_t flag_off, int R, uint32_t* seq, int advance, int* status,
+                                int site) {
+  const int lane = threadIdx.x;
+  const uint32_t target = *reinterpret_cast<volatile uint32_t*>(seq) + 1;
+  bool ok = true;
+  if (lane < R) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(win + flag_off) + lane;
+    int it = 0;
+    while ((int32_t)(ld_acquire_sys(f) - target) < 0) {
+      if (++it > kP2pPolls) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  if (!ok) atomicCAS(status, 0, site);
+  __syncwarp();
+  if (advance && lane == 0) *seq = target;
+}
+
+// ---------------------------------------------------------------------------
 // NCCL, resolved at run time
 
 struct NcclApi {
@@ -153,6 +305,7 @@ struct NcclApi {
   decltype(&ncclSend) send = nullptr;
   decltype(&ncclRecv) recv = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
 };
 
 const NcclApi* nccl() {
@@ -176,6 +329,7 @@ const NcclApi* nccl() {
     FMOE_NCCL_SYM(send, "ncclSend")
     FMOE_NCCL_SYM(recv, "ncclRecv")
     FMOE_NCCL_SYM(error_string, "ncclGetErrorString")
+    FMOE_NCCL_SYM(all_gather, "ncclAllGather")
 #undef FMOE_NCCL_SYM
     ok = true;
   });
@@ -266,7 +420,11 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
   int rc;
   if (T > cap) return set_error(FMOE_ERR_INVALID, "ep: T=%lld above the exchange capacity %lld", (long long)T,
                                 (long long)cap);
-  if (mode != FMOE_EP_FIXED && mode != FMOE_EP_EXACT) return set_error(FMOE_ERR_INVALID, "ep: mode %d", mode);
+  if (mode != FMOE_EP_FIXED && mode != FMOE_EP_EXACT && mode != FMOE_EP_P2P)
+    return set_error(FMOE_ERR_INVALID, "ep: mode %d", mode);
+  if (mode == FMOE_EP_P2P && (!c->win || c->p2p_cap != cap || c->p2p_hidden != H || c->p2p_k != k))
+    return set_error(FMOE_ERR_INVALID, "ep: peer-memory exchange not set up for cap %lld, hidden %d, top_k %d "
+                     "(fmoe_ep_p2p_init)", (long long)cap, H, k);
   if (mode == FMOE_EP_EXACT) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(st, &cs);
@@ -278,6 +436,53 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
     plan_kernel<<<R, kPlanThreads, 0, st>>>(ids, (int)T, k, d.E, (int)cap, w.slots, w.counts);
   }
   if ((rc = check_launch("ep_plan_kernel"))) return rc;
+  if (mode == FMOE_EP_P2P) {  // dispatch and return through the peers' windows
+    PeerWins pw;
+    for (int r = 0; r < 8; ++r) pw.w[r] = r < R ? c->peer_win[r] : nullptr;
+    const WinLayout L = win_layout(R, cap, H, k);
+    auto blocks = [](int64_t items) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>(2 * kNumSMs, (items + 255) / 256)); };
+    {
+      ProfScope prof_("ep_p2p_dispatch_kernel", st);
+      p2p_dispatch_kernel<<<blocks((int64_t)R * std::max<int64_t>(T, cap) * (H / 8)), 256, 0, st>>>(
+          x, ids, wts, w.slots, w.counts, (int)T, k, H, R, (int)cap, c->rank, pw, L, c->seq, c->done);
+    }
+    if ((rc = check_launch("ep_p2p_dispatch_kernel"))) return rc;
+    {
+      ProfScope prof_("ep_p2p_wait_kernel", st);
+      p2p_wait_kernel<<<1, 32, 0, st>>>(c->win, L.rx_flag, R, c->seq, 0, status, 71);
+    }
+    if ((rc = check_launch("ep_p2p_wait_kernel"))) return rc;
+    const int64_t rows = (int64_t)R * cap;
+    const bf16* rx = reinterpret_cast<const bf16*>(c->win + L.rx);
+    const int32_t* rids = reinterpret_cast<const int32_t*>(c->win + L.rids);
+    const float* rwts = reinterpret_cast<const float*>(c->win + L.rwts);
+    if (rows <= kGemvRows) {
+      rc = run_experts(rx, rows, k, rids, rwts, d, nullptr, w.mw, true, status, st, w.ypart);
+    } else {
+      if (!w.gemm || !prep)
+        return set_error(FMOE_ERR_INVALID, "ep: %lld received rows need the tensor-core path (prepared scales)",
+                         (long long)rows);
+      rc = run_prefill_experts(rx, rows, k, rids, rwts, d, prep, nullptr, w.pw, true, status, st, w.ypart);
+    }
+    if (rc) return rc;
+    {
+      ProfScope prof_("ep_p2p_return_kernel", st);
+      p2p_return_kernel<<<blocks(rows * (H / 4)), 256, 0, st>>>(w.ypart, R, (int)cap, H, c->rank, pw, L, c->seq,
+                                                               c->done + 1);
+    }
+    if ((rc = check_launch("ep_p2p_return_kernel"))) return rc;
+    {
+      ProfScope prof_("ep_p2p_wait_kernel", st);
+      p2p_wait_kernel<<<1, 32, 0, st>>>(c->win, L.ret_flag, R, c->seq, 1, status, 72);
+    }
+    if ((rc = check_launch("ep_p2p_wait_kernel"))) return rc;
+    {
+      ProfScope prof_("ep_combine_kernel", st);
+      combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(reinterpret_cast<const float*>(c->win + L.ret), w.slots,
+                                                      (int)T, R, (int)cap, H, y);
+    }
+    return check_launch("ep_combine_kernel");
+  }
   {
     ProfScope prof_("ep_pack_kernel", st);
     pack_kernel<<<2 * kNumSMs, 256, 0, st>>>(x, ids, wts, w.slots, w.counts, (int)T, k, H, R, (int)cap, w.sx, w.sids,
@@ -399,8 +604,144 @@ int fmoe_ep_comm_init(fmoe_ep_comm_t** comm, int n_ranks, int rank, const void* 
   return FMOE_OK;
 }
 
+// Releases the peer-memory window.  kP2pBarrier (a collective: all ranks call
+// it together) first waits until this rank's and then every rank's exchanges
+// are complete; kP2pLocal frees without waiting (set-up failures, before any
+// exchange); kP2pAbort frees nothing, since a peer may still be storing into
+// the window: it stays allocated, and the peers' windows mapped, until the
+// process exits.
+enum P2pRelease { kP2pAbort, kP2pLocal, kP2pBarrier };
+static int p2p_release(fmoe_ep_comm_t* c, P2pRelease how) {
+  if (!c->win) return FMOE_OK;
+  int rc = FMOE_OK;
+  const ep::NcclApi* api = ep::nccl();
+  if (how == kP2pBarrier) {
+    cudaDeviceSynchronize();
+    if (c->n_ranks > 1 && api) {
+      cudaStream_t s = nullptr;
+      uint8_t* tmp = nullptr;
+      if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
+          cudaMalloc(&tmp, 8 * ((size_t)c->n_ranks + 1)) == cudaSuccess) {
+        const ncclResult_t r = api->all_gather(tmp, tmp + 8, 8, ncclUint8, c->nc, s);
+        if (r != ncclSuccess) rc = ep::nccl_error(api, r, "window barrier");
+        cudaStreamSynchronize(s);
+      }
+      if (tmp) cudaFree(tmp);
+      if (s) cudaStreamDestroy(s);
+    }
+  }
+  if (how != kP2pAbort) {
+    for (int r = 0; r < c->n_ranks && r < 8; ++r)
+      if (r != c->rank && c->peer_win[r]) cudaIpcCloseMemHandle(c->peer_win[r]);
+    cudaFree(c->win);
+    cudaFree(c->seq);
+  }
+  c->win = nullptr;
+  c->seq = nullptr;
+  c->done = nullptr;
+  for (int r = 0; r < 8; ++r) c->peer_win[r] = nullptr;
+  c->p2p_cap = 0;
+  return rc;
+}
+
+// All-gather of n host bytes per rank (rank order) through a device buffer.
+static int gather_bytes(const ep::NcclApi* api, fmoe_ep_comm_t* c, const void* mine, size_t n, void* all) {
+  uint8_t* d = nullptr;
+  cudaStream_t s = nullptr;
+  int rc = FMOE_OK;
+  if (cudaMalloc(&d, n * (c->n_ranks + 1)) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMemcpy(d, mine, n, cudaMemcpyHostToDevice) != cudaSuccess) {
+    rc = set_error(FMOE_ERR_CUDA, "ep: gather buffer: %s", cudaGetErrorString(cudaGetLastError()));
+  } else {
+    const ncclResult_t r = api->all_gather(d, d + n, n, ncclUint8, c->nc, s);
+    if (r != ncclSuccess)
+      rc = ep::nccl_error(api, r, "all-gather");
+    else if (cudaStreamSynchronize(s) != cudaSuccess || cudaMemcpy(all, d + n, n * c->n_ranks,
+                                                                   cudaMemcpyDeviceToHost) != cudaSuccess)
+      rc = set_error(FMOE_ERR_CUDA, "ep: gather copy: %s", cudaGetErrorString(cudaGetLastError()));
+  }
+  if (d) cudaFree(d);
+  if (s) cudaStreamDestroy(s);
+  return rc;
+}
+
+int fmoe_ep_p2p_init(fmoe_ep_comm_t* c, int64_t cap, int hidden, int top_k) {
+  const ep::NcclApi* api = ep::nccl();
+  if (!api) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");
+  if (!c || !c->nc) return set_error(FMOE_ERR_INVALID, "ep: null communicator");
+  if (c->n_ranks > 8 || cap < 1 || cap > (1 << 20) || hidden < 64 || hidden % 8 || top_k < 1 || top_k > 16 ||
+      hidden / 8 < top_k)
+    return set_error(FMOE_ERR_INVALID, "ep_p2p_init: ranks %d (<= 8), cap %lld, hidden %d, top_k %d", c->n_ranks,
+                     (long long)cap, hidden, top_k);
+  int rc = p2p_release(c, kP2pBarrier);
+  if (rc) return rc;
+  // Every rank takes both all-gathers below, failed or not, and all ranks
+  // agree on the outcome (a rank that failed to allocate or map makes every
+  // rank free its window and return an error).
+  struct Rec {
+    int32_t ok, hidden, top_k, pad;
+    int64_t cap;
+    cudaIpcMemHandle_t h;
+  };
+  const ep::WinLayout L = ep::win_layout(c->n_ranks, cap, hidden, top_k);
+  Rec mine{};
+  char why[160] = "";
+  if (cudaMalloc(&c->win, L.bytes) != cudaSuccess || cudaMemset(c->win, 0, L.bytes) != cudaSuccess ||
+      cudaMalloc(&c->seq, 16) != cudaSuccess || cudaMemset(c->seq, 0, 16) != cudaSuccess ||
+      cudaDeviceSynchronize() != cudaSuccess ||  // zeroed flags before any peer can see the window
+      (c->n_ranks > 1 && cudaIpcGetMemHandle(&mine.h, c->win) != cudaSuccess))
+    snprintf(why, sizeof why, "window of %zu bytes: %s", L.bytes, cudaGetErrorString(cudaGetLastError()));
+  mine.ok = why[0] == 0;
+  mine.hidden = hidden;
+  mine.top_k = top_k;
+  mine.cap = cap;
+  std::vector<Rec> all(c->n_ranks);
+  all[c->rank] = mine;
+  if (c->n_ranks > 1 && (rc = gather_bytes(api, c, &mine, sizeof(Rec), all.data()))) {
+    p2p_release(c, kP2pLocal);
+    return rc;
+  }
+  for (int p = 0; p < c->n_ranks && !why[0]; ++p) {
+    if (!all[p].ok) snprintf(why, sizeof why, "rank %d could not allocate its window", p);
+    else if (all[p].cap != cap || all[p].hidden != hidden || all[p].top_k != top_k)  // window layouts must agree
+      snprintf(why, sizeof why, "rank %d asked for cap %lld, hidden %d, top_k %d; this rank cap %lld, hidden %d, "
+               "top_k %d", p, (long long)all[p].cap, all[p].hidden, all[p].top_k, (long long)cap, hidden, top_k);
+  }
+  if (!why[0]) {
+    c->done = reinterpret_cast<unsigned*>(c->seq + 1);
+    c->peer_win[c->rank] = c->win;
+    for (int p = 0; p < c->n_ranks && !why[0]; ++p) {
+      if (p == c->rank) continue;
+      void* ptr = nullptr;
+      if (cudaIpcOpenMemHandle(&ptr, all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+        snprintf(why, sizeof why, "map rank %d's window: %s", p, cudaGetErrorString(cudaGetLastError()));
+      else
+        c->peer_win[p] = static_cast<uint8_t*>(ptr);
+    }
+    std::vector<int32_t> oks(c->n_ranks, 1);
+    int32_t ok = why[0] == 0;
+    oks[c->rank] = ok;
+    if (c->n_ranks > 1 && (rc = gather_bytes(api, c, &ok, sizeof ok, oks.data()))) {
+      p2p_release(c, kP2pLocal);
+      return rc;
+    }
+    for (int p = 0; p < c->n_ranks && !why[0]; ++p)
+      if (!oks[p]) snprintf(why, sizeof why, "rank %d could not map every window", p);
+  }
+  if (why[0]) {
+    p2p_release(c, kP2pLocal);
+    return set_error(FMOE_ERR_CUDA, "ep_p2p_init: %s", why);
+  }
+  c->p2p_cap = cap;
+  c->p2p_hidden = hidden;
+  c->p2p_k = top_k;
+  return FMOE_OK;
+}
+
 int fmoe_ep_comm_destroy(fmoe_ep_comm_t* c) {
   if (!c) return FMOE_OK;
+  p2p_release(c, kP2pBarrier);
   const ep::NcclApi* api = ep::nccl();
   ncclResult_t r = ncclSuccess;
   if (c->nc && api) r = api->comm_destroy(c->nc);
@@ -411,6 +752,7 @@ int fmoe_ep_comm_destroy(fmoe_ep_comm_t* c) {
 
 int fmoe_ep_comm_abort(fmoe_ep_comm_t* c) {
   if (!c) return FMOE_OK;
+  p2p_release(c, kP2pAbort);
   const ep::NcclApi* api = ep::nccl();
   ncclResult_t r = ncclSuccess;
   if (c->nc && api) r = api->comm_abort(c->nc);

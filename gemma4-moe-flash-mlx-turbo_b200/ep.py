@@ -13,7 +13,9 @@ module adds the split that BASELINE config 5 asks for:
                               reported before the next exchange is launched)
 
 torch.distributed is plumbing only (rendezvous, the id broadcast, barriers);
-the dispatch and combine exchanges are the library's grouped ncclSend/ncclRecv.
+the dispatch and combine exchanges are the library's grouped ncclSend/ncclRecv,
+or (FMOE_EP_P2P) the library's own kernels storing rows straight into the
+peers' exchange windows over NVLink.
 """
 from __future__ import annotations
 
@@ -26,6 +28,7 @@ from . import (ExpertTable, FmoeError, QuantizedLinear, _need_cuda, _ptr, _strea
 
 FMOE_EP_FIXED = 0  # every rank exchanges cap rows with every rank (graph-capturable)
 FMOE_EP_EXACT = 1  # counts cross first (one host sync), then only the routed rows
+FMOE_EP_P2P = 2    # FIXED's exchange as stores into the peers' memory (CUDA IPC windows); EPComm.p2p_init
 UNIQUE_ID_BYTES = 128
 
 
@@ -63,6 +66,7 @@ class EPComm:
             dist.broadcast_object_list(obj, src=0, group=group)
             uid = ctypes.create_string_buffer(obj[0], UNIQUE_ID_BYTES)
         self._h = ctypes.c_void_p()
+        self.p2p_shape = None
         check(lib().fmoe_ep_comm_init(ctypes.byref(self._h), world, rank, uid, UNIQUE_ID_BYTES))
 
     @property
@@ -70,6 +74,17 @@ class EPComm:
         if not self._h:
             raise RuntimeError("EPComm: communicator closed")
         return self._h
+
+    def p2p_init(self, cap: int, hidden: int, top_k: int) -> None:
+        """Collective: (re)creates the peer-memory exchange windows for
+        FMOE_EP_P2P calls with this cap / hidden / top_k."""
+        self.p2p_shape = None
+        check(lib().fmoe_ep_p2p_init(self.handle, cap, hidden, top_k))
+        self.p2p_shape = (cap, hidden, top_k)
+
+    def ensure_p2p(self, cap: int, hidden: int, top_k: int) -> None:
+        if self.p2p_shape != (cap, hidden, top_k):
+            self.p2p_init(cap, hidden, top_k)
 
     def status(self) -> None:
         """Raises FmoeError if NCCL recorded an asynchronous error."""
@@ -128,8 +143,10 @@ class ExpertParallelMoeBlock:
     router is the full replicated one, and forward(x) serves this rank's tokens.
 
     cap: the most tokens any rank passes per call (FIXED exchanges cap rows per
-    peer); mode FMOE_EP_FIXED (no host sync, capturable) or FMOE_EP_EXACT (only
-    routed rows cross; one host sync per call)."""
+    peer); mode FMOE_EP_FIXED (no host sync, capturable), FMOE_EP_EXACT (only
+    routed rows cross; one host sync per call) or FMOE_EP_P2P (FIXED's layout,
+    stored straight into the peers' windows; capturable; sets up the comm's
+    windows for this cap, collectively, when they differ)."""
 
     def __init__(self, comm: EPComm, router_proj: QuantizedLinear, experts: ExpertTable, cap: int, top_k=8,
                  mode=FMOE_EP_FIXED, router_scale=None, per_expert_scale=None, root_size=None, rms_norm_eps=1e-6,
@@ -141,6 +158,8 @@ class ExpertParallelMoeBlock:
             raise ValueError(f"rank {comm.rank}: expected experts [{first}, {first + n}), got "
                              f"[{experts.first_expert}, {experts.first_expert + experts.num_experts})")
         self.comm, self.cap, self.mode = comm, cap, mode
+        if mode == FMOE_EP_P2P:
+            comm.ensure_p2p(cap, router_proj.in_features, top_k)
         # the router half of the single-device block (same fields and argument meaning)
         self._block = Gemma4MoeBlock(router_proj, experts, top_k, router_scale, per_expert_scale, root_size,
                                      rms_norm_eps, use_norm, logit_bias)

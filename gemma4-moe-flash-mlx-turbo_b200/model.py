@@ -180,7 +180,7 @@ class Gemma4Model:
     caches, final norm and the tied 6-bit lm_head with softcap; greedy decode."""
 
     def __init__(self, cfg, embed: QuantizedLinear, layers, final_norm, batch, max_positions, kv_mode=KV_BF16,
-                 device=None, ep=None, ep_cap=None):
+                 device=None, ep=None, ep_cap=None, ep_mode=0):
         self.cfg = cfg
         self.embed = embed
         self.layers = layers
@@ -198,6 +198,9 @@ class Gemma4Model:
             self.caches.append(c)
         self.ep = ep
         self.ep_cap = batch if ep_cap is None else ep_cap
+        self.ep_mode = ep_mode  # FMOE_EP_FIXED or FMOE_EP_P2P (both capturable)
+        if ep is not None and ep_mode == 2:
+            ep.ensure_p2p(self.ep_cap, cfg["hidden"], layers[0].top_k)
         if ep is None:
             ws = max(L.workspace_bytes(batch, c) for L, c in zip(layers, self.caches))
         else:
@@ -215,6 +218,21 @@ class Gemma4Model:
         self._emb_scale = math.sqrt(H)
         self._embed_c = embed.cstruct()
         self._fc = None
+        self.sampler = None
+
+    def set_sampler(self, temperature=0.0, top_p=1.0, rep_penalty=1.0, seed=0, window=64):
+        """decode_step then draws the next tokens with fmoe_sample (the engine's
+        sample(), src/engine.rs:302-355, its last-64-token repetition window
+        engine.rs:153-155) instead of the greedy argmax; None-equivalent reset:
+        set_sampler(None)."""
+        from .sample import Sampler
+
+        if temperature is None:
+            self.sampler = None
+            return self
+        self.sampler = Sampler(self.batch, self.embed.out_features, temperature, top_p, rep_penalty, seed, window,
+                               self.device)
+        return self
 
     def tile_weights(self):
         """Tile-layout copies of every decode-GEMV weight (layers and lm_head)."""
@@ -227,7 +245,7 @@ class Gemma4Model:
 
     @classmethod
     def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None, ep=None,
-               ep_cap=None):
+               ep_cap=None, ep_mode=0):
         """Random-init model.  ep (an EPComm): every layer keeps only this rank's
         expert slice and decode_step runs the routed experts on their owners."""
         n_layers = cfg["layers"] if n_layers is None else n_layers
@@ -251,7 +269,7 @@ class Gemma4Model:
             rows.append(None)
         embed = QuantizedLinear(wq, sc, bi, cfg["embed_bits"], 64, in_features=H)
         final_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
-        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device, ep, ep_cap)
+        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device, ep, ep_cap, ep_mode)
 
     def _fused(self):
         if self._fc is None:
@@ -304,10 +322,12 @@ class Gemma4Model:
             if self.ep is None:
                 L.forward(self.x, cache, self.pos, self.ws, pd)
             else:
-                L.forward_ep(self.ep, self.ep_cap, self.x, cache, self.pos, self.ws, pd)
+                L.forward_ep(self.ep, self.ep_cap, self.x, cache, self.pos, self.ws, pd, mode=self.ep_mode)
         check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(self.x), self.batch,
                                  self.cfg["softcap"], _ptr(self.logits), _ptr(self.ids), _ptr(pd), _ptr(self.lm_ws),
                                  self.lm_ws.numel(), _stream()))
+        if self.sampler is not None:  # the draw replaces the lm_head's greedy ids
+            self.sampler(self.logits, out=self.ids)
         if not device_pos:
             self.pos += 1
             for cache in self.caches:

@@ -394,6 +394,9 @@ typedef struct fmoe_ep_comm fmoe_ep_comm_t;
 #define FMOE_EP_UNIQUE_ID_BYTES 128
 #define FMOE_EP_FIXED 0 /* every rank exchanges cap rows with every rank: no host sync, CUDA-graph capturable */
 #define FMOE_EP_EXACT 1 /* counts cross first (one host sync per block), then only the routed rows */
+#define FMOE_EP_P2P 2   /* as FIXED, but the rows and partial sums are stored straight into the peers' memory
+                           (CUDA IPC over NVLink, flag-synchronised) instead of NCCL send/recv; needs
+                           fmoe_ep_p2p_init with the same cap / hidden / top_k */
 
 /* Rank 0 makes the id; the host engine hands it to the other ranks. */
 int fmoe_ep_unique_id(void* id, size_t len);
@@ -404,6 +407,13 @@ int fmoe_ep_comm_destroy(fmoe_ep_comm_t* comm);
 int fmoe_ep_comm_abort(fmoe_ep_comm_t* comm);
 /* FMOE_OK, or FMOE_ERR_NCCL when NCCL has recorded an asynchronous error. */
 int fmoe_ep_comm_status(fmoe_ep_comm_t* comm);
+/* Collective (all ranks): allocates this rank's exchange window for FMOE_EP_P2P
+ * (receive rows, ids, weights and returned partial sums for n_ranks x cap rows;
+ * flags) and maps every peer's window into this process.  At most 8 ranks.
+ * Released by fmoe_ep_comm_destroy / _abort or a new call.  Waits on peers'
+ * flags are bounded: a timeout ends with FMOE_ERR_TIMEOUT in the workspace
+ * status word. */
+int fmoe_ep_p2p_init(fmoe_ep_comm_t* comm, int64_t cap, int hidden, int top_k);
 
 /* cap: the largest T any rank passes (FIXED exchanges cap rows per peer).
  * Received rows are served by the decode expert kernels up to 128 rows, by the
@@ -467,6 +477,28 @@ int fmoe_decode_step(const fmoe_decode_model_t* model, int32_t* tokens, float* l
  * FMOE_OK, or FMOE_ERR_TIMEOUT when a kernel's bounded wait on an async copy
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
 int fmoe_workspace_status(const void* workspace, int clear, void* stream);
+
+/* ---- next-token sampling on the device (the engine's sample(), src/engine.rs:302-355) ----
+ * logits: [rows, vocab] fp32 on the device (fmoe_lm_head's output).  Per row:
+ *   repetition penalty (rep_penalty > 1 and n_recent > 0): every distinct token of
+ *     recent[row, 0..n_recent) inside [0, vocab) once: logit >= 0 divided by the
+ *     penalty, negative multiplied (entries < 0 or >= vocab are ignored: empty slots);
+ *   temperature 0: out = argmax (first maximum);
+ *   else z = logits / temperature; top_p < 1: in descending order (ties in token
+ *     order) a token is dropped when (running sum of softmax(z)) - p > top_p;
+ *     a categorical draw with P(token) proportional to p' + 1e-10, p' = softmax over the
+ *     kept tokens (0 for dropped ones), as the Gumbel-max argmax of (p' + 1e-10) / E,
+ *     E = -log(u), u = (k + 0.5) / 2^23, k = top 23 bits of a splitmix64 hash keyed by
+ *     (seed, call number, row, token) — reproducible on the host.
+ * step_dev: device uint64 call number (null: 0), advanced by one per call, so a CUDA
+ * graph replays fresh draws.  push_recent != 0 (needs step_dev): the drawn token is
+ * stored into recent[row, call number % n_recent] (a ring of the last n_recent tokens;
+ * fill it with -1 first).  n_recent <= 4096; rows <= 65535; rows * vocab < 2^31.
+ * Capturable in a CUDA graph (no host sync). */
+size_t fmoe_sample_workspace_bytes(int64_t rows, int64_t vocab);
+int fmoe_sample(const float* logits, int64_t rows, int64_t vocab, int32_t* recent, int n_recent,
+                float temperature, float top_p, float rep_penalty, uint64_t seed, uint64_t* step_dev,
+                int push_recent, int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -3,7 +3,8 @@ fmoe_decoder_layer_forward_ep) against the CPU oracle and the single-device
 path.
 
 One GPU: a one-rank NCCL communicator runs the whole exchange (plan, pack,
-grouped send/recv to itself, local experts, return, combine).  Two GPUs (when
+grouped send/recv to itself, local experts, return, combine); mode 2 (the
+peer-memory exchange) stores into the rank's own window.  Two GPUs (when
 present): one process per GPU, 64 experts each; every rank checks its own
 tokens against the single-device block holding all 128 experts.
 
@@ -49,7 +50,8 @@ def _oracle(orc, table, host, x, ids, w):
     return y32
 
 
-@pytest.mark.parametrize("T,cap,mode", [(5, 8, 0), (64, 64, 1), (300, 300, 0), (200, 256, 1), (0, 4, 0)])
+@pytest.mark.parametrize("T,cap,mode", [(5, 8, 0), (64, 64, 1), (300, 300, 0), (200, 256, 1), (0, 4, 0), (5, 8, 2),
+                                        (300, 300, 2), (0, 4, 2)])
 def test_ep_one_rank_matches_oracle(fm, orc, dev, comm1, layer, T, cap, mode):
     table, wr, bias, host = layer
     g = torch.Generator(device=dev).manual_seed(700 + T)
@@ -70,11 +72,11 @@ def test_ep_one_rank_matches_oracle(fm, orc, dev, comm1, layer, T, cap, mode):
     assert torch.equal(y, ep.forward(x))  # deterministic
 
 
-def _decoder_pair(fm, dev, comm):
+def _decoder_pair(fm, dev, comm, mode=0):
     cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=2)
     ctx = 300
     m1 = fm.Gemma4Model.random(cfg, batch=1, max_positions=1024, seed=21, device=dev, n_layers=2)
-    m2 = fm.Gemma4Model(cfg, m1.embed, m1.layers, m1.final_norm, 1, 1024, device=dev, ep=comm)
+    m2 = fm.Gemma4Model(cfg, m1.embed, m1.layers, m1.final_norm, 1, 1024, device=dev, ep=comm, ep_mode=mode)
     g = torch.Generator(device=dev).manual_seed(22)
     for L, c1, c2 in zip(m1.layers, m1.caches, m2.caches):
         kv = torch.randn(2, 1, L.num_kv_heads, ctx, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
@@ -88,10 +90,12 @@ def _decoder_pair(fm, dev, comm):
     return m2, want
 
 
-def test_ep_decoder_one_rank_is_the_local_decoder(fm, dev, comm1):
+@pytest.mark.parametrize("mode", [0, 2])
+def test_ep_decoder_one_rank_is_the_local_decoder(fm, dev, comm1, mode):
     """Two decoder layers: the expert-parallel layer call with one rank gives
-    bit-identical tokens and logits to the local call."""
-    m2, want = _decoder_pair(fm, dev, comm1)
+    bit-identical tokens and logits to the local call (NCCL or peer-memory
+    exchange)."""
+    m2, want = _decoder_pair(fm, dev, comm1, mode)
     got = []
     for _ in range(3):
         got.append((m2.decode_step().clone(), m2.logits.clone()))
@@ -102,11 +106,13 @@ def test_ep_decoder_one_rank_is_the_local_decoder(fm, dev, comm1):
         assert torch.equal(gi, wi), step
 
 
-def test_ep_decoder_graph_replay(fm, dev, comm1):
-    """The same from a CUDA graph that captured the NCCL exchanges (position on
-    the device).  The graph is released before any check, so a failure cannot
-    leave the communicator with captured work outstanding."""
-    m2, want = _decoder_pair(fm, dev, comm1)
+@pytest.mark.parametrize("mode", [0, 2])
+def test_ep_decoder_graph_replay(fm, dev, comm1, mode):
+    """The same from a CUDA graph that captured the exchanges (position on the
+    device; the peer-memory exchange's sequence counter lives on the device
+    too).  The graph is released before any check, so a failure cannot leave
+    the communicator with captured work outstanding."""
+    m2, want = _decoder_pair(fm, dev, comm1, mode)
     got = []
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -166,7 +172,8 @@ def _two_rank_worker(rank, world, port, q):
         router = fm.QuantizedLinear(wr, bits=16)
         ref = fm.Gemma4MoeBlock(router, table, top_k=K, logit_bias=bias)
         errs = []
-        for T, cap, mode in [(4, 4, 0), (3, 4, 1), (200, 256, 0), (150, 256, 1)]:
+        for T, cap, mode in [(4, 4, 0), (3, 4, 1), (200, 256, 0), (150, 256, 1), (4, 4, 2), (200, 256, 2),
+                             (1, 4, 2)]:
             Tr = T if rank == 0 else max(T - 1, 0)  # ragged token counts
             gx = torch.Generator(device=dev).manual_seed(900 + 10 * T + rank)
             x = torch.randn(Tr, H, generator=gx, device=dev).to(torch.bfloat16)
@@ -187,7 +194,7 @@ def _two_rank_worker(rank, world, port, q):
         q.put((rank, None, repr(e)))
 
 
-def _two_rank_decoder_worker(rank, world, port, q):
+def _two_rank_decoder_worker(rank, world, port, q, mode=0):
     """Two decoder layers (sliding + full attention) with the experts split over
     two GPUs, one sequence per GPU; checked against the same model with all
     experts local on this GPU."""
@@ -211,7 +218,7 @@ def _two_rank_decoder_worker(rank, world, port, q):
                                        L.head_dim, L.rope_dims, L.rope_theta, L.k_eq_v, L.eps, L.layer_scalar,
                                        L.attn_scale, L.top_k)
             layers.append(L2)
-        m2 = fm.Gemma4Model(cfg, m1.embed, layers, m1.final_norm, 1, 1024, device=dev, ep=comm)
+        m2 = fm.Gemma4Model(cfg, m1.embed, layers, m1.final_norm, 1, 1024, device=dev, ep=comm, ep_mode=mode)
         g = torch.Generator(device=dev).manual_seed(22 + rank)
         for L, c1, c2 in zip(m1.layers, m1.caches, m2.caches):
             kv = torch.randn(2, 1, L.num_kv_heads, ctx, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
@@ -240,13 +247,13 @@ def _two_rank_decoder_worker(rank, world, port, q):
         q.put((rank, None, repr(e)))
 
 
-def _spawn_two(target):
+def _spawn_two(target, *extra):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
     env_nvls = os.environ.get("NCCL_NVLS_ENABLE")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=target, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, 2, port, q) + extra) for r in range(2)]
     res = {}
     try:
         for p in procs:
@@ -267,8 +274,9 @@ def _spawn_two(target):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_rank_decoder_matches_local():
-    for rank, (res, exc) in _spawn_two(_two_rank_decoder_worker).items():
+@pytest.mark.parametrize("mode", [0, 2])
+def test_ep_two_rank_decoder_matches_local(mode):
+    for rank, (res, exc) in _spawn_two(_two_rank_decoder_worker, mode).items():
         assert exc is None, f"rank {rank}: {exc}"
         for step, (same_ids, err) in enumerate(res):
             assert err <= TOL, (rank, step, err)
