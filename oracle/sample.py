@@ -74,8 +74,9 @@ def kept_prefix(z: np.ndarray, top_p: float):
 
 
 def scores(logits_row: np.ndarray, recent, temperature: float, top_p: float, penalty: float, seed: int,
-           step: int, row: int) -> np.ndarray:
-    """Per-token Gumbel-max score (p' + 1e-10) / E of one row (temperature > 0)."""
+           step: int, row: int, kept_override: int | None = None) -> np.ndarray:
+    """Per-token Gumbel-max score (p' + 1e-10) / E of one row (temperature > 0).
+    kept_override replaces the top-p cut's token count (near-tie analysis)."""
     z = penalize(logits_row, recent, penalty) / np.float32(temperature)
     z = z.astype(np.float32)
     V = z.shape[0]
@@ -83,6 +84,8 @@ def scores(logits_row: np.ndarray, recent, temperature: float, top_p: float, pen
     e = np.exp((z - m).astype(np.float32)).astype(np.float32)
     if top_p < 1.0:
         order, kept, _ = kept_prefix(z, top_p)
+        if kept_override is not None:
+            kept = min(max(kept_override, 1), V)
         mask = np.zeros(V, bool)
         mask[order[:kept]] = True
         s = np.float32(e[mask].sum(dtype=np.float32))
@@ -107,20 +110,31 @@ def sample(logits: np.ndarray, recent, temperature: float, top_p: float, penalty
     return out
 
 
-def margin(logits_row, recent, temperature, top_p, penalty, seed, step, row) -> float:
-    """Relative gap between the best and second-best score (how far a draw is from
-    a tie) and, with top_p < 1, the distance of the cut from top_p; the smaller."""
+def margin(logits_row, recent, temperature, top_p, penalty, seed, step, row, cut_tol: float = 2e-5) -> float:
+    """How far a draw is from a near tie: the relative gap between the best and
+    second-best score; 0 when, with top_p < 1, the winner changes as the cut
+    moves over the tokens whose running sum before them lies within cut_tol of
+    top_p (fp32 sums in another order can place the cut anywhere there).
+    Moving the cut only adds or drops the tokens in between, so the two
+    extreme cuts cover every cut in the range (up to the renormalisation, a
+    relative change far below the score gap checked)."""
     if temperature == 0.0:
         z = np.sort(penalize(logits_row, recent, penalty))[::-1]
         return float((z[0] - z[1]) / max(abs(z[0]), 1e-30)) if z.shape[0] > 1 else 1.0
-    s = np.sort(scores(logits_row, recent, temperature, top_p, penalty, seed, step, row))[::-1]
+    sc = scores(logits_row, recent, temperature, top_p, penalty, seed, step, row)
+    s = np.sort(sc)[::-1]
     g = float((s[0] - s[1]) / s[0]) if s.shape[0] > 1 else 1.0
     if top_p < 1.0:
         z = (penalize(logits_row, recent, penalty) / np.float32(temperature)).astype(np.float32)
         order, kept, m = kept_prefix(z, top_p)
-        e = np.exp((z[order] - m).astype(np.float32))
-        p = e / e.sum()
-        cum = np.cumsum(p.astype(np.float64))
-        excl = cum - p
-        g = min(g, float(np.min(np.abs(excl - top_p))))
+        e = np.exp((z[order] - m).astype(np.float64))
+        excl = np.cumsum(e / e.sum()) - e / e.sum()
+        near = np.flatnonzero(np.abs(excl - top_p) <= cut_tol)
+        lo = min(kept, int(near.min())) if near.size else kept
+        hi = max(kept, int(near.max()) + 1) if near.size else kept
+        win = int(np.argmax(sc))
+        for k in {lo, hi, kept - 1, kept + 1}:
+            if int(np.argmax(scores(logits_row, recent, temperature, top_p, penalty, seed, step, row,
+                                    kept_override=k))) != win:
+                return 0.0
     return g
