@@ -604,46 +604,6 @@ int fmoe_ep_comm_init(fmoe_ep_comm_t** comm, int n_ranks, int rank, const void* 
   return FMOE_OK;
 }
 
-// Releases the peer-memory window.  kP2pBarrier (a collective: all ranks call
-// it together) first waits until this rank's and then every rank's exchanges
-// are complete; kP2pLocal frees without waiting (set-up failures, before any
-// exchange); kP2pAbort frees nothing, since a peer may still be storing into
-// the window: it stays allocated, and the peers' windows mapped, until the
-// process exits.
-enum P2pRelease { kP2pAbort, kP2pLocal, kP2pBarrier };
-static int p2p_release(fmoe_ep_comm_t* c, P2pRelease how) {
-  if (!c->win) return FMOE_OK;
-  int rc = FMOE_OK;
-  const ep::NcclApi* api = ep::nccl();
-  if (how == kP2pBarrier) {
-    cudaDeviceSynchronize();
-    if (c->n_ranks > 1 && api) {
-      cudaStream_t s = nullptr;
-      uint8_t* tmp = nullptr;
-      if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
-          cudaMalloc(&tmp, 8 * ((size_t)c->n_ranks + 1)) == cudaSuccess) {
-        const ncclResult_t r = api->all_gather(tmp, tmp + 8, 8, ncclUint8, c->nc, s);
-        if (r != ncclSuccess) rc = ep::nccl_error(api, r, "window barrier");
-        cudaStreamSynchronize(s);
-      }
-      if (tmp) cudaFree(tmp);
-      if (s) cudaStreamDestroy(s);
-    }
-  }
-  if (how != kP2pAbort) {
-    for (int r = 0; r < c->n_ranks && r < 8; ++r)
-      if (r != c->rank && c->peer_win[r]) cudaIpcCloseMemHandle(c->peer_win[r]);
-    cudaFree(c->win);
-    cudaFree(c->seq);
-  }
-  c->win = nullptr;
-  c->seq = nullptr;
-  c->done = nullptr;
-  for (int r = 0; r < 8; ++r) c->peer_win[r] = nullptr;
-  c->p2p_cap = 0;
-  return rc;
-}
-
 // All-gather of n host bytes per rank (rank order) through a device buffer.
 static int gather_bytes(const ep::NcclApi* api, fmoe_ep_comm_t* c, const void* mine, size_t n, void* all) {
   uint8_t* d = nullptr;
@@ -663,6 +623,53 @@ static int gather_bytes(const ep::NcclApi* api, fmoe_ep_comm_t* c, const void* m
   }
   if (d) cudaFree(d);
   if (s) cudaStreamDestroy(s);
+  return rc;
+}
+
+// Releases the peer-memory window.  A peer's mapping of this rank's window is
+// closed before the window is freed (freeing exported memory that another
+// process still maps is undefined), so the collective modes take two
+// barriers; all ranks call them together.
+//   kP2pBarrier  this rank's work done; barrier (every rank's exchanges are
+//                complete); close the mappings of the peers' windows;
+//                barrier; free
+//   kP2pAgreed   set-up that all ranks agreed failed after some mapped:
+//                close; barrier; free
+//   kP2pLocal    set-up failures before any rank mapped a window: free
+//   kP2pAbort    frees nothing (a peer may still be storing into the window):
+//                it stays allocated, and the peers' windows mapped, until the
+//                process exits
+enum P2pRelease { kP2pAbort, kP2pLocal, kP2pAgreed, kP2pBarrier };
+static int p2p_barrier(const ep::NcclApi* api, fmoe_ep_comm_t* c) {
+  if (c->n_ranks < 2) return FMOE_OK;
+  if (!api) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");
+  int32_t mine = 0;
+  std::vector<int32_t> all(c->n_ranks);
+  return gather_bytes(api, c, &mine, sizeof mine, all.data());
+}
+static int p2p_release(fmoe_ep_comm_t* c, P2pRelease how) {
+  if (!c->win) return FMOE_OK;
+  int rc = FMOE_OK;
+  const ep::NcclApi* api = ep::nccl();
+  if (how == kP2pBarrier) {
+    cudaDeviceSynchronize();
+    rc = p2p_barrier(api, c);
+  }
+  if (how != kP2pAbort) {
+    for (int r = 0; r < c->n_ranks && r < 8; ++r)
+      if (r != c->rank && c->peer_win[r]) cudaIpcCloseMemHandle(c->peer_win[r]);
+    if (how == kP2pBarrier || how == kP2pAgreed) {
+      const int rc2 = p2p_barrier(api, c);
+      if (!rc) rc = rc2;
+    }
+    cudaFree(c->win);
+    cudaFree(c->seq);
+  }
+  c->win = nullptr;
+  c->seq = nullptr;
+  c->done = nullptr;
+  for (int r = 0; r < 8; ++r) c->peer_win[r] = nullptr;
+  c->p2p_cap = 0;
   return rc;
 }
 
@@ -728,8 +735,12 @@ int fmoe_ep_p2p_init(fmoe_ep_comm_t* c, int64_t cap, int hidden, int top_k) {
     }
     for (int p = 0; p < c->n_ranks && !why[0]; ++p)
       if (!oks[p]) snprintf(why, sizeof why, "rank %d could not map every window", p);
+    if (why[0]) {  // every rank agreed; some may hold mappings of this window
+      p2p_release(c, kP2pAgreed);
+      return set_error(FMOE_ERR_CUDA, "ep_p2p_init: %s", why);
+    }
   }
-  if (why[0]) {
+  if (why[0]) {  // no rank mapped any window
     p2p_release(c, kP2pLocal);
     return set_error(FMOE_ERR_CUDA, "ep_p2p_init: %s", why);
   }

@@ -13,7 +13,9 @@ max |b| <= 1e-2 of the oracle (evaluated on the GPU's routing).  With one rank
 the partial sum is the single-device sum, so decode outputs are bit-identical.
 """
 import os
+import queue
 import socket
+import time
 
 import numpy as np
 import pytest
@@ -159,6 +161,7 @@ def _two_rank_worker(rank, world, port, q):
 
     import __graft_entry__
 
+    comm = None
     try:
         fm = __graft_entry__.load_package()
         torch.cuda.set_device(rank)
@@ -191,7 +194,11 @@ def _two_rank_worker(rank, world, port, q):
         dist.destroy_process_group()
         q.put((rank, errs, None))
     except Exception as e:
-        q.put((rank, None, repr(e)))
+        import traceback
+
+        q.put((rank, None, repr(e) + "\n" + traceback.format_exc()))
+        if comm is not None:  # frees this rank's NCCL state; the peer is then reported as silent
+            comm.abort()
 
 
 def _two_rank_decoder_worker(rank, world, port, q, mode=0):
@@ -202,6 +209,7 @@ def _two_rank_decoder_worker(rank, world, port, q, mode=0):
 
     import __graft_entry__
 
+    comm = None
     try:
         fm = __graft_entry__.load_package()
         torch.cuda.set_device(rank)
@@ -244,7 +252,11 @@ def _two_rank_decoder_worker(rank, world, port, q, mode=0):
         dist.destroy_process_group()
         q.put((rank, res, None))
     except Exception as e:
-        q.put((rank, None, repr(e)))
+        import traceback
+
+        q.put((rank, None, repr(e) + "\n" + traceback.format_exc()))
+        if comm is not None:  # frees this rank's NCCL state; the peer is then reported as silent
+            comm.abort()
 
 
 def _spawn_two(target, *extra):
@@ -255,29 +267,37 @@ def _spawn_two(target, *extra):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     procs = [ctx.Process(target=target, args=(r, 2, port, q) + extra) for r in range(2)]
     res = {}
+    deadline = time.monotonic() + 200  # well inside the per-test timeout, so a stuck rank is reported
     try:
         for p in procs:
             p.start()
         for _ in range(2):
-            rank, out, exc = q.get(timeout=600)
+            try:
+                rank, out, exc = q.get(timeout=max(1.0, deadline - time.monotonic()))
+            except queue.Empty:
+                break
             res[rank] = (out, exc)
     finally:
         for p in procs:
-            p.join(timeout=60)
+            p.join(timeout=30)
             if p.is_alive():
                 p.kill()
+                p.join(timeout=30)
         if env_nvls is None:
             os.environ.pop("NCCL_NVLS_ENABLE", None)
         else:
             os.environ["NCCL_NVLS_ENABLE"] = env_nvls
+    for r in range(2):
+        res.setdefault(r, (None, "no answer within 200 s (waiting in a collective for a rank that failed?)"))
     return res
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("mode", [0, 2])
 def test_ep_two_rank_decoder_matches_local(mode):
-    for rank, (res, exc) in _spawn_two(_two_rank_decoder_worker, mode).items():
-        assert exc is None, f"rank {rank}: {exc}"
+    out = _spawn_two(_two_rank_decoder_worker, mode)
+    assert all(exc is None for _, exc in out.values()), "\n".join(f"rank {r}: {e}" for r, (_, e) in out.items())
+    for rank, (res, exc) in out.items():
         for step, (same_ids, err) in enumerate(res):
             assert err <= TOL, (rank, step, err)
             assert same_ids, (rank, step)
@@ -285,8 +305,9 @@ def test_ep_two_rank_decoder_matches_local(mode):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_two_ranks_match_single_device():
-    for rank, (errs, exc) in _spawn_two(_two_rank_worker).items():
-        assert exc is None, f"rank {rank}: {exc}"
+    out = _spawn_two(_two_rank_worker)
+    assert all(exc is None for _, exc in out.values()), "\n".join(f"rank {r}: {e}" for r, (_, e) in out.items())
+    for rank, (errs, exc) in out.items():
         for T, mode, same, err in errs:
             assert same, (rank, T, mode)
             assert err <= TOL, (rank, T, mode, err)
