@@ -557,3 +557,4 @@ from .ep import (FMOE_EP_EXACT, FMOE_EP_FIXED, FMOE_EP_P2P, EPComm, ExpertParall
 from . import ecb  # noqa: E402
 from .tier import HostExpertTier, TieredMoeBlock  # noqa: E402
 from .sample import Sampler, sample_tokens  # noqa: E402
+from . import safetensors  # noqa: E402
