@@ -62,6 +62,10 @@ def parse():
                          "layout stored into the peers' memory by the library's kernels; decode30 at N > 1 takes "
                          "fixed or p2p)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sample", action="store_true",
+                    help="decode30: draw each token on the device with the reference generate command's defaults "
+                         "(temperature 0.7, top_p 0.9, repetition penalty 1.15 over the last 64 tokens) instead of "
+                         "the greedy argmax")
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one eager step between cudaProfilerStart / Stop and exit (for "
                          "ncu --profile-from-start off launch lists of the decode30 / ep_* workloads)")
@@ -259,6 +263,8 @@ def run_decoder(args, rank, world, local):
         raise SystemExit("decode30: the exact exchange syncs the host per layer and cannot be captured")
     m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
                               ep=ep, ep_mode=ep_mode).tile_weights()
+    if args.sample:
+        m.set_sampler(0.7, 0.9, 1.15, seed=4200 + rank)
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
     for L, c in zip(m.layers, m.caches):
         chunk = 256
@@ -381,7 +387,9 @@ def run_decoder(args, rank, world, local):
                    "dense_bits": 4, "embed_bits": 6, "router": "bf16",
                    "parallelism": par,
                    "l2": "weights (about 15 GB) far larger than L2; no flush",
-                   "graph": "one CUDA graph per step, position on the device"},
+                   "graph": "one CUDA graph per step, position on the device",
+                   "next_token": ("fmoe_sample on the device: temperature 0.7, top_p 0.9, repetition penalty 1.15 "
+                                  "over the last 64 tokens" if args.sample else "greedy argmax (fused in the lm_head)")},
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * 4,
                 "d2h_bytes_per_step": T * 4,
                 "api": "Gemma4Model.decode_step (embedding, fmoe_decoder_layer_forward%s x30, fmoe_lm_head) "
