@@ -346,6 +346,8 @@ def run_decoder(args, rank, world, local):
     host_out = torch.empty(64, T, dtype=torch.int32).pin_memory()
     timed(min(args.warmup, 3), True, host_in, host_out)
     ms_e2e = timed(args.steps, True, host_in, host_out)
+    if m.status() != 0:  # a bounded device wait (exchange flag, copy) gave up: the step did not run as timed
+        raise SystemExit(f"rank {rank}: device status: {fm.last_error()}")
     assert int(m.pos_dev[0]) == CTX + args.steps
 
     ms_step = ms / args.steps
@@ -707,6 +709,8 @@ def run_ep_moe(args, rank, world, local):
     host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
     timed(min(args.warmup, 3), True, host_in, host_out)
     ms_e2e = timed(args.steps, True, host_in, host_out)
+    if fm.lib().fmoe_workspace_status(shared.buf.data_ptr(), 0, fm._stream()) != 0:
+        raise SystemExit(f"rank {rank}: device status: {fm.last_error()}")
     ms_step = ms / args.steps
     value = total / (ms_step / 1e3)
     e2e_value = total / (ms_e2e / args.steps / 1e3)

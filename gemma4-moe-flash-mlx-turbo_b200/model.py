@@ -302,6 +302,12 @@ class Gemma4Model:
             cache._offset = self.pos
         return self.ids
 
+    def status(self, clear: bool = False) -> int:
+        """Status word of the layered step's workspace (0: ok; a bounded device
+        wait that gave up — e.g. a peer-memory exchange flag that never came —
+        leaves FMOE_ERR_TIMEOUT; synchronises)."""
+        return lib().fmoe_workspace_status(_ptr(self.ws), int(clear), _stream())
+
     def fused_status(self, clear: bool = False) -> int:
         """Status word of the fused step's workspace (0: ok; synchronises)."""
         return lib().fmoe_workspace_status(_ptr(self._fused()[3]), int(clear), _stream())

@@ -246,6 +246,7 @@ def _two_rank_decoder_worker(rank, world, port, q, mode=0):
             res.append((bool(torch.equal(a, b)) or not sure,
                         max_rel_err(m2.logits.cpu().numpy(), la.cpu().numpy())))
             m2.ids.copy_(a)  # continue both from the same token
+        assert m2.status() == 0, fm.last_error()  # no bounded exchange wait gave up
         comm.status()
         torch.cuda.synchronize()
         comm.close()
