@@ -23,8 +23,9 @@
 //   sample_prep_kernel     penalty, / temperature, chunk max (argmax at T = 0)
 //   sample_exp_kernel      row max, exp, chunk sums; sort keys when top_p < 1
 //   (cub radix sort of the 64-bit keys row | descending z, stable)
-//   sample_cut_kernel      one CTA per row: the running sum in sorted order,
-//                          the kept prefix and its mass
+//   sample_psum_kernel     per chunk of sorted positions: its probability mass
+//   sample_cut_kernel      per chunk: running sum from the earlier chunks' mass,
+//                          the kept tokens and their mass
 //   sample_draw_kernel     per token (p + 1e-10) / E, chunk argmax
 //   sample_finish_kernel   row argmax -> token; ring push; call counter + 1
 #include <climits>
@@ -38,16 +39,15 @@ namespace fmoe {
 namespace smp {
 
 constexpr int kThreads = 256, kPer = 16, kChunk = kThreads * kPer;
-constexpr int kCutThreads = 1024;
 constexpr int kMaxRecent = 4096;
 
 struct Part {
   float max, sum, score;
   int idx;
 };
-struct RowInfo {
-  float m, S, kept_sum;
-  int kept;
+struct Cut {  // per (row, chunk of sorted positions)
+  float psum, kept_e;
+  int kept, pad;
 };
 
 // splitmix64's output function (Steele, Lea & Flood 2014; Vigna's constants)
@@ -91,7 +91,7 @@ struct Args {
   uint64_t *keys, *keys_sorted;  // [rows, V]
   int32_t *vals, *vals_sorted;   // [rows, V]
   Part* parts;               // [rows, nch]
-  RowInfo* info;             // [rows]
+  Cut* cut;                  // [rows, nch]
 };
 
 template <int NT>
@@ -203,57 +203,97 @@ __global__ void __launch_bounds__(kThreads) sample_exp_kernel(const Args a) {
   }
 }
 
-// One CTA per row, over the row's tokens in descending order: thread t owns a
-// contiguous run of sorted positions.  cumulative(j) = sum of p over sorted
-// positions <= j; kept while cumulative - p <= top_p (a prefix).
-__global__ void __launch_bounds__(kCutThreads) sample_cut_kernel(const Args a) {
-  __shared__ float sS, sm, scan[kCutThreads];
-  __shared__ int cnt[kCutThreads / 32];
-  __shared__ float ksum[kCutThreads / 32];
-  const int row = blockIdx.x, t = threadIdx.x;
-  if (t == 0) {
-    sm = row_max(a, row);
-    sS = row_sum(a, row);
-  }
-  __syncthreads();
-  const float m = sm, S = sS;
-  const int64_t seg = (a.V + kCutThreads - 1) / kCutThreads;
-  const int64_t j0 = t * seg < a.V ? t * seg : a.V, j1 = j0 + seg < a.V ? j0 + seg : a.V;
+// Sorted positions of a chunk: thread t owns the kPer consecutive positions
+// c0 + kPer*t ...; p = exp(z - m) / S in that order.
+__device__ inline void sorted_chunk(const Args& a, int row, int64_t c0, float m, float S, float* e, float* p) {
   const uint64_t* ks = a.keys_sorted + (int64_t)row * a.V;
-  float run = 0.f;
-  for (int64_t j = j0; j < j1; ++j) run += expf(unmono(~(uint32_t)ks[j]) - m) / S;
-  scan[t] = run;
-  __syncthreads();
-  // inclusive Hillis-Steele scan of the per-thread totals
-  for (int o = 1; o < kCutThreads; o <<= 1) {
-    const float v = t >= o ? scan[t - o] : 0.f;
-    __syncthreads();
-    scan[t] += v;
-    __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int64_t j = c0 + (int64_t)threadIdx.x * kPer + i;
+    e[i] = j < a.V ? expf(unmono(~(uint32_t)ks[j]) - m) : 0.f;
+    p[i] = e[i] / S;
   }
-  float cum = t > 0 ? scan[t - 1] : 0.f;
+}
+
+__global__ void __launch_bounds__(kThreads) sample_psum_kernel(const Args a) {
+  __shared__ float sm, sS, red[kThreads / 32];
+  const int row = blockIdx.y;
+  if (threadIdx.x == 0) sm = row_max(a, row), sS = row_sum(a, row);
+  __syncthreads();
+  float e[kPer], p[kPer];
+  sorted_chunk(a, row, (int64_t)blockIdx.x * kChunk, sm, sS, e, p);
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) t += p[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float c = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) c += red[w];
+    a.cut[(int64_t)row * a.nch + blockIdx.x].psum = c;
+  }
+}
+
+// cumulative(j) = mass of the earlier chunks + the running sum inside this
+// one; a token is kept unless cumulative - p > top_p.  Chunks that start well
+// past top_p keep nothing (their first token's cumulative - p is the earlier
+// mass, up to rounding).
+__global__ void __launch_bounds__(kThreads) sample_cut_kernel(const Args a) {
+  __shared__ float sm, sS, soff, wtot[kThreads / 32], ke_w[kThreads / 32];
+  __shared__ int kc_w[kThreads / 32];
+  const int row = blockIdx.y, c = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  Cut* out = a.cut + (int64_t)row * a.nch + c;
+  if (threadIdx.x == 0) {
+    sm = row_max(a, row), sS = row_sum(a, row);
+    float off = 0.f;
+    for (int q = 0; q < c; ++q) off += a.cut[(int64_t)row * a.nch + q].psum;
+    soff = off;
+  }
+  __syncthreads();
+  if (soff - a.top_p > 1e-3f) {  // block-uniform
+    if (threadIdx.x == 0) out->kept = 0, out->kept_e = 0.f;
+    return;
+  }
+  float e[kPer], p[kPer];
+  sorted_chunk(a, row, (int64_t)c * kChunk, sm, sS, e, p);
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) tot += p[i];
+  // exclusive scan of the thread totals: within the warp, then over the warps
+  float incl = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wtot[w] = incl;
+  __syncthreads();
+  float before = soff;
+  for (int q = 0; q < w; ++q) before += wtot[q];
+  float cum = before + incl - tot;
   int kept = 0;
   float kept_e = 0.f;
-  for (int64_t j = j0; j < j1; ++j) {
-    const float e = expf(unmono(~(uint32_t)ks[j]) - m);
-    const float p = e / S;
-    cum += p;
-    if (cum - p > a.top_p) break;  // dropped from here on (the cut is a prefix)
-    ++kept;
-    kept_e += e;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    cum += p[i];
+    const int64_t j = (int64_t)c * kChunk + (int64_t)threadIdx.x * kPer + i;
+    if (j < a.V && !(cum - p[i] > a.top_p)) ++kept, kept_e += e[i];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     kept += __shfl_xor_sync(0xffffffffu, kept, o);
     kept_e += __shfl_xor_sync(0xffffffffu, kept_e, o);
   }
-  if ((t & 31) == 0) cnt[t >> 5] = kept, ksum[t >> 5] = kept_e;
+  if (lane == 0) kc_w[w] = kept, ke_w[w] = kept_e;
   __syncthreads();
-  if (t == 0) {
+  if (threadIdx.x == 0) {
     int k = 0;
     float ke = 0.f;
-    for (int w = 0; w < kCutThreads / 32; ++w) k += cnt[w], ke += ksum[w];
-    a.info[row] = RowInfo{m, S, ke, k};
+    for (int q = 0; q < kThreads / 32; ++q) k += kc_w[q], ke += ke_w[q];
+    out->kept = k;
+    out->kept_e = ke;
   }
 }
 
@@ -267,8 +307,13 @@ __global__ void __launch_bounds__(kThreads) sample_draw_kernel(const Args a) {
   const bool sort = a.top_p < 1.f;
   if (threadIdx.x == 0) {
     if (sort) {
-      const RowInfo r = a.info[row];
-      sm = r.m, sK = r.kept_sum, sk = r.kept;
+      int k = 0;
+      float ke = 0.f;
+      for (int q = 0; q < a.nch; ++q) {
+        const Cut& ct = a.cut[(int64_t)row * a.nch + q];
+        k += ct.kept, ke += ct.kept_e;
+      }
+      sm = row_max(a, row), sK = ke, sk = k;
     } else {
       sm = row_max(a, row), sK = row_sum(a, row), sk = INT_MAX;
     }
@@ -339,7 +384,7 @@ struct Ws {
   uint64_t *keys, *keys_sorted;
   int32_t *vals, *vals_sorted;
   Part* parts;
-  RowInfo* info;
+  Cut* cut;
   void* cub_tmp;
   size_t cub_bytes, total;
 };
@@ -368,7 +413,7 @@ Ws carve(int rows, int64_t V, uint8_t* base) {
   w.vals = reinterpret_cast<int32_t*>(take(n * 4));
   w.vals_sorted = reinterpret_cast<int32_t*>(take(n * 4));
   w.parts = reinterpret_cast<Part*>(take((size_t)rows * nch * sizeof(Part)));
-  w.info = reinterpret_cast<RowInfo*>(take((size_t)rows * sizeof(RowInfo)));
+  w.cut = reinterpret_cast<Cut*>(take((size_t)rows * nch * sizeof(Cut)));
   w.cub_tmp = take(w.cub_bytes);
   w.total = o;
   return w;
@@ -410,7 +455,7 @@ int fmoe_sample(const float* logits, int64_t rows, int64_t vocab, int32_t* recen
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nch = (int)((vocab + smp::kChunk - 1) / smp::kChunk);
   const smp::Args a{logits, vocab, (int)rows, nch, recent, n_recent, temperature, top_p, rep_penalty, seed,
-                    step_dev, push_recent, out, w.z, w.keys, w.keys_sorted, w.vals, w.vals_sorted, w.parts, w.info};
+                    step_dev, push_recent, out, w.z, w.keys, w.keys_sorted, w.vals, w.vals_sorted, w.parts, w.cut};
   const dim3 grid(nch, (unsigned)rows);
   int rc;
   {
@@ -431,8 +476,13 @@ int fmoe_sample(const float* logits, int64_t rows, int64_t vocab, int32_t* recen
                                                             smp::end_bit((int)rows), st);
       if (e != cudaSuccess) return set_error(FMOE_ERR_CUDA, "sample: radix sort: %s", cudaGetErrorString(e));
       {
+        ProfScope prof_("sample_psum_kernel", st);
+        smp::sample_psum_kernel<<<grid, smp::kThreads, 0, st>>>(a);
+      }
+      if ((rc = check_launch("sample_psum_kernel"))) return rc;
+      {
         ProfScope prof_("sample_cut_kernel", st);
-        smp::sample_cut_kernel<<<(unsigned)rows, smp::kCutThreads, 0, st>>>(a);
+        smp::sample_cut_kernel<<<grid, smp::kThreads, 0, st>>>(a);
       }
       if ((rc = check_launch("sample_cut_kernel"))) return rc;
     }
