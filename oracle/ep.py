@@ -107,3 +107,45 @@ def simulate(xs, idss, wtss, R: int, buf, stride, offsets, hidden: int, inter: i
         ret = np.stack([parts[p][q] for p in range(R)])
         outs.append(combine(ret, plans[q][0], xs[q].shape[0]))
     return outs
+
+
+def simulate_p2p(xs, idss, wtss, R: int, buf, stride, offsets, hidden: int, inter: int, num_experts: int, cap: int,
+                 stale_seed: int = 0):
+    """The peer-memory exchange (FMOE_EP_P2P) restated on per-rank windows that
+    still hold an earlier exchange's rows (stale data): sender `me` stores each
+    routed row into block `me` of the owner's window at its slot, writes ids -1
+    over the rest of that block and its count into rx_cnt[me] (the dispatch
+    kernel); every rank runs its experts on its whole window; rank `me` stores
+    the first rx_cnt[r] partial rows of block r into block `me` of rank r's
+    returned rows (the return kernel); each rank combines from its own window.
+    Must give simulate()'s outputs exactly.  (The ids -1 over a block's tail
+    only keep stale rows from selecting experts — work, not results: their
+    partial rows are never returned.)"""
+    per = num_experts // R
+    k = idss[0].shape[1]
+    g = np.random.default_rng(stale_seed)
+    wins = [{"rx": g.integers(0, 0x3F80, (R * cap, hidden), dtype=np.uint16),  # finite stale bf16 rows
+             "rids": g.integers(0, num_experts, (R * cap, k)).astype(np.int32),
+             "rwts": g.random((R * cap, k), dtype=np.float32),
+             "ret": g.standard_normal((R * cap, hidden)).astype(np.float32),
+             "rx_cnt": np.full(R, -7, np.int32)} for _ in range(R)]
+    plans = [plan(ids, R, per, cap) for ids in idss]
+    for me in range(R):  # dispatch
+        slots, counts = plans[me]
+        for r in range(R):
+            w = wins[r]
+            w["rx_cnt"][me] = counts[r]
+            for t in range(xs[me].shape[0]):
+                s = slots[r, t]
+                if s >= 0:
+                    row = me * cap + s
+                    w["rx"][row], w["rids"][row], w["rwts"][row] = xs[me][t], idss[me][t], wtss[me][t]
+            w["rids"][me * cap + counts[r]:(me + 1) * cap] = -1
+            w["rwts"][me * cap + counts[r]:(me + 1) * cap] = 0.0
+    ypart = [local_partial(w["rx"], w["rids"], w["rwts"], buf, stride, offsets, hidden, inter, p * per, per)
+             for p, w in enumerate(wins)]
+    for me in range(R):  # return
+        for r in range(R):
+            n = int(wins[me]["rx_cnt"][r])
+            wins[r]["ret"][me * cap:me * cap + n] = ypart[me][r * cap:r * cap + n]
+    return [combine(wins[q]["ret"].reshape(R, cap, hidden), plans[q][0], xs[q].shape[0]) for q in range(R)]

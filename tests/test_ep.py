@@ -79,6 +79,23 @@ def test_simulated_split_matches_single_device(R):
         assert _rel(oracle.bf16_to_f32(y), _single(d, x, ids, w, H, I)) <= TOL
 
 
+@pytest.mark.parametrize("R", [2, 4])
+def test_peer_memory_windows_match_the_exchange(R):
+    """The P2P mode's window protocol (stores at block `me` of the owner's
+    window, ids -1 over the rest of the block, partial sums returned for the
+    first rx_cnt rows only) over windows holding stale rows gives the same
+    outputs as the send/recv exchange, bit for bit."""
+    d, H, I, E, k = _table()
+    sizes = [5, 0, 3, 7][:R]
+    xs = [_tokens(n, H, 50 + r) for r, n in enumerate(sizes)]
+    routed = [_route(d, x, k) for x in xs]
+    args = ([r[0] for r in routed], [r[1] for r in routed], R, d["buf"], int(d["stride"]), d["offsets"], H, I, E)
+    want = oep.simulate(xs, *args, cap=max(sizes))
+    got = oep.simulate_p2p(xs, *args, cap=max(sizes), stale_seed=R)
+    for a, b in zip(got, want):
+        assert np.array_equal(a, b)
+
+
 def test_simulated_split_all_tokens_to_one_rank():
     """Every token routed to experts of the last rank: the other ranks receive
     nothing but still take part."""
