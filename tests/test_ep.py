@@ -262,6 +262,8 @@ def test_ep_abi_argument_checks(fm):
                                None, 0, None)
     assert rc == -1 and "communicator" in fm.last_error()
     assert L.fmoe_ep_comm_init(None, 2, 0, None, 0) in (-1, -7)
+    # the peer-memory windows need a communicator (FMOE_ERR_NCCL where libnccl is absent)
+    assert L.fmoe_ep_p2p_init(None, 4, 2816, 8) in (-1, -7)
     with pytest.raises(ValueError):
         fm.shard_range(128, 3, 0)
     assert fm.shard_range(128, 8, 7) == (112, 16)

@@ -61,3 +61,19 @@ def test_draw_distribution(top_p):
     want /= want.sum()
     freq = np.bincount(draws, minlength=4) / n
     assert np.all(np.abs(freq - want) <= 4 * np.sqrt(want * (1 - want) / n) + 1e-4), (freq, want)
+
+
+def test_sample_abi_rejects_bad_arguments_before_any_launch(fm):
+    """Argument checks run on the host before any CUDA call (no GPU needed)."""
+    L = fm.lib()
+    assert L.fmoe_sample_workspace_bytes(0, 10) == 0 and L.fmoe_sample_workspace_bytes(70000, 10) == 0
+    bad = [  # logits, rows, vocab, recent, n_recent, temperature, top_p, penalty, step, push, out
+        (None, 2, 10, None, 0, 1.0, 1.0, 1.0, None, 0, 0x1000),      # null logits
+        (0x1000, 0, 10, None, 0, 1.0, 1.0, 1.0, None, 0, 0x1000),    # no rows
+        (0x1000, 2, 10, None, 0, -1.0, 1.0, 1.0, None, 0, 0x1000),   # negative temperature
+        (0x1000, 2, 10, None, 0, 1.0, 1.0, 0.0, None, 0, 0x1000),    # penalty 0
+        (0x1000, 2, 10, None, 4, 1.0, 1.0, 1.2, None, 0, 0x1000),    # recent count without a list
+        (0x1000, 2, 10, 0x1000, 4, 1.0, 1.0, 1.2, None, 1, 0x1000),  # ring push without the counter
+    ]
+    for lg, rows, V, rc, n, T, tp, pen, step, push, out in bad:
+        assert L.fmoe_sample(lg, rows, V, rc, n, T, tp, pen, 0, step, push, out, None, 0, None) == -1
