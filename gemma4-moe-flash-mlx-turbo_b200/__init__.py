@@ -558,3 +558,4 @@ from . import ecb  # noqa: E402
 from .tier import HostExpertTier, TieredMoeBlock  # noqa: E402
 from .sample import Sampler, sample_tokens  # noqa: E402
 from . import safetensors  # noqa: E402
+from . import split  # noqa: E402

@@ -190,7 +190,7 @@ class Gemma4Model:
         self.device = device
         self.caches = []
         for i, L in enumerate(layers):
-            win = None if L.k_eq_v else cfg["window"]
+            win = None if getattr(L, "full_attention", L.k_eq_v) else cfg["window"]
             if kv_mode == KV_AFFINE:
                 c = KVCache.new_affine(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
             else:

@@ -30,6 +30,7 @@ _NP = {"U8": np.uint8, "I8": np.int8, "U16": np.uint16, "I16": np.int16, "F16": 
        "BOOL": np.bool_}
 _SIGNED = {"BF16": np.int16, "U16": np.int16, "U32": np.int32, "U64": np.int64}
 QLINEAR_BITS = (4, 6, 8)        # widths the decode GEMV kernels serve (4 and 8 for every token count)
+QLINEAR_GROUPS = (64,)          # the kernels' group size
 
 
 class SafetensorsError(ValueError):
@@ -121,16 +122,22 @@ def nearest_supported_bits(bits: int, supported=QLINEAR_BITS) -> int:
     return max(below) if below else 4
 
 
-def load_qlinear(weights: dict, prefix: str, bits: int, group_size: int = 64, supported=QLINEAR_BITS):
+def load_qlinear(weights: dict, prefix: str, bits: int, group_size: int = 64, supported=QLINEAR_BITS,
+                 groups=QLINEAR_GROUPS):
     """load_qlinear_flex (src/model/mod.rs:648-680): the QuantizedLinear at
     `prefix` from a loaded tensor dict; a width outside `supported` is
-    re-quantised on the GPU to nearest_supported_bits(bits)."""
+    re-quantised on the GPU to nearest_supported_bits(bits), and a group size
+    outside `groups` to group 64 (the kernels' one group size).  A bf16 weight
+    with no scales is kept as a plain bf16 linear (bits 16), the form the
+    library's router takes."""
     from . import QuantizedLinear, quantize
 
     w = weights.get(f"{prefix}.weight")
     if w is None:
         raise KeyError(f"missing weight: {prefix}.weight")
     s = weights.get(f"{prefix}.scales", weights.get(f"{prefix}.weight_scales"))
+    if s is None and w.dtype == torch.bfloat16:
+        return QuantizedLinear(w, bits=16)
     if s is None:
         raise KeyError(f"missing scales for: {prefix}")
     b = weights.get(f"{prefix}.biases", weights.get(f"{prefix}.weight_biases"))
@@ -142,8 +149,9 @@ def load_qlinear(weights: dict, prefix: str, bits: int, group_size: int = 64, su
         raise ValueError(f"{prefix}: weight {tuple(w.shape)}, scales {tuple(s.shape)}, biases {tuple(b.shape)} "
                          f"are not a {bits}-bit, group-{group_size} quantised linear")
     q = QuantizedLinear(w, s, b, bits, group_size, in_features=cols)
-    if bits in supported:
+    if bits in supported and group_size in groups:
         return q
-    target = nearest_supported_bits(bits, supported)
-    wq, s2, b2 = quantize(q.dequantize(), target, group_size)  # bf16 weights, as the reference's dequantize gives
-    return QuantizedLinear(wq, s2, b2, target, group_size, in_features=cols)
+    target = bits if bits in supported else nearest_supported_bits(bits, supported)
+    tg = group_size if group_size in groups else 64
+    wq, s2, b2 = quantize(q.dequantize(), target, tg)  # bf16 weights, as the reference's dequantize gives
+    return QuantizedLinear(wq, s2, b2, target, tg, in_features=cols)

@@ -1,0 +1,121 @@
+"""CPU checks of the split-checkpoint loader (split.py, the reference's
+load_gemma4_model, src/model/mod.rs:405-617): a two-layer synthetic split
+directory (config.json with per-component quantisation overrides, resident
+safetensors, per-layer ECB expert files) loads into decoder layers with the
+reference's names, widths, head shapes, RoPE settings and K == V rule."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+
+H, HD, GHD, I, E, IE, V = 128, 64, 128, 128, 4, 64, 256
+
+
+def _bf(u16):
+    return torch.from_numpy(np.ascontiguousarray(u16).view(np.int16)).view(torch.bfloat16)
+
+
+def _qlin(t, prefix, out_f, in_f, bits, rng, names=(".scales", ".biases")):
+    wq, s, b = oracle.quantize(rng.standard_normal((out_f, in_f)).astype(np.float32) * 0.05, bits)
+    t[f"{prefix}.weight"] = wq
+    t[prefix + names[0]] = _bf(s)
+    t[prefix + names[1]] = _bf(b)
+
+
+def _norm(n, rng):
+    return torch.from_numpy(rng.standard_normal(n).astype(np.float32)).to(torch.bfloat16)
+
+
+@pytest.fixture(scope="module")
+def split_dir(fm, tmp_path_factory):
+    d = tmp_path_factory.mktemp("split")
+    rng = np.random.default_rng(0)
+    args = {"hidden_size": H, "num_hidden_layers": 2, "num_attention_heads": 2, "num_key_value_heads": 2,
+            "head_dim": HD, "vocab_size": V, "rms_norm_eps": 1e-6, "intermediate_size": I, "num_experts": E,
+            "moe_intermediate_size": IE, "top_k_experts": 2, "layer_types": ["sliding_attention", "full_attention"],
+            "global_head_dim": GHD, "num_global_key_value_heads": 1, "attention_k_eq_v": True,
+            "final_logit_softcapping": 30.0, "sliding_window": 512,
+            "rope_parameters": {"sliding_attention": {"rope_theta": 10000.0},
+                                "full_attention": {"rope_theta": 1000000.0, "partial_rotary_factor": 0.25}}}
+    quant = {"bits": 4, "group_size": 64, "mode": "affine",
+             "language_model.model.embed_tokens": {"bits": 6, "group_size": 64}}
+    for i in range(2):
+        for p in ("q_proj", "v_proj"):
+            quant[f"language_model.model.layers.{i}.self_attn.{p}"] = {"bits": 8, "group_size": 64}
+    with open(d / "config.json", "w") as f:
+        json.dump({"text_config": args, "quantization": quant}, f)
+    t = {}
+    for i, full in enumerate([False, True]):
+        pre, hd = f"language_model.layers.{i}", GHD if full else HD
+        kv = 1 if full else 2
+        names = (".weight_scales", ".weight_biases") if full else (".scales", ".biases")  # both namings
+        _qlin(t, f"{pre}.self_attn.q_proj", 2 * hd, H, 8, rng, names)
+        _qlin(t, f"{pre}.self_attn.k_proj", kv * hd, H, 8, rng, names)
+        if not full:
+            _qlin(t, f"{pre}.self_attn.v_proj", kv * hd, H, 8, rng)
+        _qlin(t, f"{pre}.self_attn.o_proj", H, 2 * hd, 8, rng, names)
+        t[f"{pre}.self_attn.q_norm.weight"] = _norm(hd, rng)
+        t[f"{pre}.self_attn.k_norm.weight"] = _norm(hd, rng)
+        for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                  "post_feedforward_layernorm", "post_feedforward_layernorm_1", "post_feedforward_layernorm_2",
+                  "pre_feedforward_layernorm_2"):
+            t[f"{pre}.{n}.weight"] = _norm(H, rng)
+        for p, (o, n) in {"gate_proj": (I, H), "up_proj": (I, H), "down_proj": (H, I)}.items():
+            _qlin(t, f"{pre}.mlp.{p}", o, n, 4, rng)
+        t[f"{pre}.router.proj.weight"] = _norm(E * H, rng).reshape(E, H)  # a bf16 router
+        t[f"{pre}.router.scale"] = _norm(H, rng)
+        t[f"{pre}.router.per_expert_scale"] = _norm(E, rng)
+        t[f"{pre}.layer_scalar"] = torch.tensor([0.75], dtype=torch.bfloat16)
+        offs, sizes, stride = fm.ecb_layout(H, IE)
+        buf = torch.from_numpy(rng.integers(0, 255, E * stride, dtype=np.uint8))
+        os.makedirs(d / "experts", exist_ok=True)
+        fm.ecb.write(str(d / "experts" / f"layer_{i:02d}_experts.ecb"), fm.ExpertTable(buf, E, H, IE, 4, 64))
+    _qlin(t, "language_model.embed_tokens", V, H, 6, rng)
+    t["language_model.norm.weight"] = _norm(H, rng)
+    os.makedirs(d / "resident")
+    fm.safetensors.save(str(d / "resident" / "resident.safetensors"), t)
+    return str(d), t
+
+
+def test_split_layers(fm, split_dir):
+    path, t = split_dir
+    cfg, embed, layers, final_norm = fm.split.load_split(path, device="cpu")
+    assert cfg["layer_full"] == [False, True] and cfg["window"] == 512 and cfg["softcap"] == 30.0
+    assert (embed.bits, embed.in_features, embed.out_features) == (6, H, V)
+    assert torch.equal(final_norm, t["language_model.norm.weight"])
+    s, f = layers
+    assert not s.k_eq_v and s.v_proj is not None and s.head_dim == HD and s.num_kv_heads == 2
+    assert (s.rope_dims, s.rope_theta) == (HD, 10000.0) and not s.full_attention
+    assert f.k_eq_v and f.v_proj is None and f.head_dim == GHD and f.num_kv_heads == 1 and f.full_attention
+    assert (f.rope_dims, f.rope_theta) == (GHD // 4, 1e6)
+    for L in layers:
+        # k / o take the q_proj width of their layer (the reference keys attention on q_proj)
+        assert L.q_proj.bits == 8 and L.k_proj.bits == 8 and L.o_proj.bits == 8
+        assert L.mlp[0].bits == 4 and L.router["proj"].bits == 16
+        assert L.layer_scalar == 0.75 and L.top_k == 2 and L.experts.num_experts == E
+    assert s.v_proj.bits == 8  # v_proj has its own override
+    assert torch.equal(s.norms["pre_ff_2"], t["language_model.layers.0.pre_feedforward_layernorm_2.weight"])
+    assert torch.equal(f.q_proj.scales, t["language_model.layers.1.self_attn.q_proj.weight_scales"])
+
+
+def test_split_expert_slice_and_missing_tensor(fm, split_dir, tmp_path):
+    path, t = split_dir
+    _, _, layers, _ = fm.split.load_split(path, device="cpu", n_layers=1, experts=(1, 2))
+    assert (layers[0].experts.first_expert, layers[0].experts.num_experts) == (2, 2)
+    q = fm.split.QuantConfig(None)
+    assert q.bits_for("anything") == (8, 32)  # the reference's defaults without a quantization block
+    q = fm.split.QuantConfig({"bits": 4, "group_size": 64, "x.q_proj": {"bits": 8, "group_size": 64}, "mode": "a"})
+    assert q.bits_for("x.q_proj") == (8, 64) and q.bits_for("x.k_proj") == (4, 64)
+    broken = dict(t)
+    del broken["language_model.layers.0.router.scale"]
+    bdir = tmp_path / "b"
+    os.makedirs(bdir / "resident")
+    os.symlink(os.path.join(path, "experts"), bdir / "experts")
+    os.symlink(os.path.join(path, "config.json"), bdir / "config.json")
+    fm.safetensors.save(str(bdir / "resident" / "resident.safetensors"), broken)
+    with pytest.raises(KeyError, match="router.scale"):
+        fm.split.load_split(str(bdir), device="cpu", n_layers=1)
