@@ -91,6 +91,7 @@ class EPComm:
         check(lib().fmoe_ep_comm_status(self.handle))
 
     def close(self) -> None:
+        """Collective once p2p_init ran (every rank calls it); after a lost rank use abort()."""
         if self._h:
             h, self._h = self._h, ctypes.c_void_p()
             check(lib().fmoe_ep_comm_destroy(h))

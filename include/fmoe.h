@@ -402,8 +402,12 @@ typedef struct fmoe_ep_comm fmoe_ep_comm_t;
 int fmoe_ep_unique_id(void* id, size_t len);
 /* Blocking: returns when all n_ranks have joined (current CUDA device). */
 int fmoe_ep_comm_init(fmoe_ep_comm_t** comm, int n_ranks, int rank, const void* id, size_t len);
+/* Frees comm.  With peer-memory windows (fmoe_ep_p2p_init) it is collective: every
+ * rank calls it (two NCCL barriers, so no window is freed while a peer still maps
+ * it); after a rank was lost use fmoe_ep_comm_abort instead. */
 int fmoe_ep_comm_destroy(fmoe_ep_comm_t* comm);
-/* For a host watchdog: ends outstanding NCCL work with an error and frees comm. */
+/* For a host watchdog: ends outstanding NCCL work with an error and frees comm
+ * (no collective; peer-memory windows stay allocated until the process exits). */
 int fmoe_ep_comm_abort(fmoe_ep_comm_t* comm);
 /* FMOE_OK, or FMOE_ERR_NCCL when NCCL has recorded an asynchronous error. */
 int fmoe_ep_comm_status(fmoe_ep_comm_t* comm);
