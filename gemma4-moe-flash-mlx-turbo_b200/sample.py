@@ -57,10 +57,13 @@ class Sampler:
                  rep_penalty: float = 1.0, seed: int = 0, window: int = 64, device="cuda"):
         self.temperature, self.top_p, self.rep_penalty, self.seed = temperature, top_p, rep_penalty, seed
         self.rows, self.vocab = rows, vocab
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:  # the workspace is keyed by the indexed device
+            device = torch.device("cuda", torch.cuda.current_device())
         self.recent = torch.full((rows, window), -1, dtype=torch.int32, device=device)
         self.step = torch.zeros(1, dtype=torch.int64, device=device)
         self._ws = _Workspace()
-        self._ws.get(lib().fmoe_sample_workspace_bytes(rows, vocab), torch.device(device))
+        self._ws.get(lib().fmoe_sample_workspace_bytes(rows, vocab), device)  # allocated once, outside any capture
 
     def reset(self) -> None:
         self.recent.fill_(-1)
