@@ -10,6 +10,10 @@
                         oracle's routing and output.
   turbo_small.npz       seeded bf16 [6, 256] rows and the oracle's TurboQuant
                         3-bit round trip.
+  sample_small.npz      seeded fp32 logits [4, 512], recent-token lists (empty
+                        slots, duplicates, out-of-range ids) and the sampling
+                        oracle's tokens for a grid of (temperature, top_p,
+                        penalty) at call numbers 0..2, plus its first uniforms.
 """
 import json
 import os
@@ -86,6 +90,25 @@ def main():
     v = oracle.f32_to_bf16(rng.standard_normal((6, 256)).astype(np.float32))
     out, idx, nrm = oracle.turbo_round_trip(v, 3)
     np.savez_compressed(os.path.join(HERE, "turbo_small.npz"), v=v, out=out, idx=idx, norm=nrm)
+
+    sample_fixture()
+
+
+SAMPLE_CASES = [(0.0, 1.0, 1.0), (0.0, 1.0, 1.3), (0.7, 1.0, 1.0), (0.7, 0.9, 1.15), (1.5, 0.5, 1.0)]
+
+
+def sample_fixture():
+    from oracle import sample as osmp
+
+    rng = np.random.default_rng(7)
+    lg = (rng.standard_normal((4, 512)) * 2.0).astype(np.float32)
+    recent = rng.integers(-1, 520, size=(4, 16)).astype(np.int32)
+    recent[:, 1] = recent[:, 0]
+    toks = np.array([[osmp.sample(lg, recent, T, p, pen, seed=99, step=s) for s in range(3)]
+                     for T, p, pen in SAMPLE_CASES], np.int32)
+    np.savez_compressed(os.path.join(HERE, "sample_small.npz"), logits=lg, recent=recent,
+                        cases=np.array(SAMPLE_CASES, np.float32), tokens=toks,
+                        uniforms=osmp.uniforms(99, 0, 0, 8))
 
 
 if __name__ == "__main__":

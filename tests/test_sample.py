@@ -77,3 +77,16 @@ def test_sample_abi_rejects_bad_arguments_before_any_launch(fm):
     ]
     for lg, rows, V, rc, n, T, tp, pen, step, push, out in bad:
         assert L.fmoe_sample(lg, rows, V, rc, n, T, tp, pen, 0, step, push, out, None, 0, None) == -1
+
+
+def test_oracle_against_committed_fixture():
+    """Regression of the sampling oracle against tests/golden/sample_small.npz
+    (made by tests/golden/make_golden.py)."""
+    import os
+
+    d = np.load(os.path.join(os.path.dirname(__file__), "golden", "sample_small.npz"))
+    assert np.array_equal(smp.uniforms(99, 0, 0, 8), d["uniforms"])
+    for c, (T, top_p, pen) in enumerate(d["cases"]):
+        for s in range(3):
+            got = smp.sample(d["logits"], d["recent"], float(T), float(top_p), float(pen), seed=99, step=s)
+            assert np.array_equal(got, d["tokens"][c, s]), (c, s)
