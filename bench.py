@@ -419,7 +419,7 @@ def run_decoder(args, rank, world, local):
     if ep is not None:
         ep.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_decoder_baseline(T)
+        result["cpu_baseline"] = cpu_decoder_baseline(T, sampled=args.sample)
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -950,7 +950,21 @@ def cpu_decoder_step_s(t_s, t_f, t_lm, layers=LAYERS):
     return (layers - n_full) * t_s + n_full * t_f + t_lm
 
 
-def cpu_decoder_baseline(T, budget_s=15.0):
+def cpu_sample_s(vocab=262144, reps=3):
+    """Seconds per token of the sampling oracle (the engine's sample() at the
+    generate defaults: temperature 0.7, top_p 0.9, penalty 1.15 over 64 tokens)."""
+    import numpy as np
+    from oracle import sample as osmp
+    rng = np.random.default_rng(1)
+    lg = (rng.standard_normal((1, vocab)) * 3).astype(np.float32)
+    recent = rng.integers(0, vocab, (1, 64)).astype(np.int32)
+    t0 = time.perf_counter()
+    for s in range(reps):
+        osmp.sample(lg, recent, 0.7, 0.9, 1.15, seed=1, step=s)
+    return (time.perf_counter() - t0) / reps
+
+
+def cpu_decoder_baseline(T, budget_s=15.0, sampled=False):
     import oracle
     sample = cpu_decoder_sample()
     t0 = time.perf_counter()
@@ -958,10 +972,12 @@ def cpu_decoder_baseline(T, budget_s=15.0):
     n = max(2, int((budget_s - (time.perf_counter() - t0)) / max(t_s, 1e-3)))
     t_s, t_f, t_lm = cpu_decoder_times(sample, n)
     step = cpu_decoder_step_s(t_s, t_f, t_lm)
-    return {"value": round(T / step, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
+    t_smp = cpu_sample_s() * T if sampled else 0.0
+    return {"value": round(T / (step + t_smp), 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
             "sample": f"{n} sliding layers + 1 full layer + 1 lm_head of one decode token at context {CTX} on the "
                       f"oracle (C++ OpenMP / numpy); step = 24 sliding + 6 full + lm_head "
-                      f"({t_s * 1e3:.1f} / {t_f * 1e3:.1f} / {t_lm * 1e3:.1f} ms)"}
+                      f"({t_s * 1e3:.1f} / {t_f * 1e3:.1f} / {t_lm * 1e3:.1f} ms)"
+                      + (f" + sampling ({t_smp * 1e3:.1f} ms, numpy)" if sampled else "")}
 
 
 def run_reference(args, rank, world):
@@ -976,9 +992,12 @@ def run_reference(args, rank, world):
             cpu_decoder_times(sample, 1)
         t_s, t_f, t_lm = cpu_decoder_times(sample, args.steps)
         step = cpu_decoder_step_s(t_s, t_f, t_lm)
+        if args.sample:  # the engine's sample() per token at the generate defaults
+            step += cpu_sample_s() * T
         value = T / step
         desc = (f"each step = one sliding decoder layer of one token at context {CTX} on the oracle; one full layer "
-                f"and one lm_head timed once; decode step = 24 sliding + 6 full + lm_head")
+                f"and one lm_head timed once; decode step = 24 sliding + 6 full + lm_head"
+                + (" + the sampling oracle (temperature 0.7, top_p 0.9, penalty 1.15)" if args.sample else ""))
         out = {
             "impl": "reference",
             "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
@@ -987,7 +1006,9 @@ def run_reference(args, rank, world):
             "scaling": "weak", "vs_baseline": None,
             "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32/fp64 accumulate (CPU)",
             "data": "synthetic (seeded)",
-            "config": {"workload": args.workload, "layers": LAYERS, "batch": T, "context": CTX},
+            "config": {"workload": args.workload, "layers": LAYERS, "batch": T, "context": CTX,
+                       "next_token": "sampled (temperature 0.7, top_p 0.9, penalty 1.15)" if args.sample
+                       else "greedy argmax"},
             "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
