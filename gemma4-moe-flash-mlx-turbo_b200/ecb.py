@@ -109,6 +109,31 @@ def load(path: str, device="cuda", experts: tuple[int, int] | None = None, pin: 
     return ExpertTable(buf, n, shp["hidden"], shp["inter"], shp["bits"], shp["group"], first_expert=first)
 
 
+CODE_OF_DTYPE = {"U8": 0, "U32": 1, "BF16": 2, "F16": 3, "F32": 4, "I32": 5}
+
+
+def write_tensors(path: str, tensors) -> None:
+    """ECB file from expert-stacked tensors: tensors = [(dtype name, per-expert
+    shape, uint8 array [E, per-expert bytes]), ...] in file order (the
+    splitter's write_ecb_file, src/splitter.rs:405-457): header, then for every
+    expert its slice of each tensor back to back."""
+    E = tensors[0][2].shape[0]
+    if any(t[2].shape[0] != E for t in tensors):
+        raise EcbError("write_tensors: tensors disagree on the expert count")
+    stride = sum(t[2].shape[1] for t in tensors)
+    hdr = bytearray(HEADER_SIZE)
+    struct.pack_into("<4s4I", hdr, 0, MAGIC, E, stride, len(tensors), HEADER_SIZE)
+    pos = 20
+    for dt, shape, data in tensors:
+        if pos + 12 + 4 * len(shape) > HEADER_SIZE:
+            raise EcbError("write_tensors: descriptors exceed the header")
+        struct.pack_into(f"<3I{len(shape)}I", hdr, pos, data.shape[1], CODE_OF_DTYPE[dt], len(shape), *shape)
+        pos += 12 + 4 * len(shape)
+    with open(path, "wb") as f:
+        f.write(bytes(hdr))
+        f.write(np.ascontiguousarray(np.concatenate([t[2] for t in tensors], axis=1)).tobytes())
+
+
 def write(path: str, table) -> None:
     """ExpertTable (whole layer) -> ECB file in the splitter's format."""
     if table.first_expert != 0:

@@ -116,6 +116,37 @@ def save(path: str, tensors: dict[str, np.ndarray | torch.Tensor], metadata: dic
             f.write(raw)
 
 
+def read_raw(path: str, names=None) -> dict[str, tuple[str, tuple, bytes]]:
+    """{name: (dtype, shape, raw bytes)} of a safetensors file (all, or `names`)."""
+    hdr, base = read_header(path)
+    out = {}
+    with open(path, "rb") as f:
+        for name in (hdr.keys() if names is None else names):
+            dt, shape, b, e = hdr[name]
+            f.seek(base + b)
+            out[name] = (dt, shape, f.read(e - b))
+    return out
+
+
+def save_raw(path: str, tensors: dict[str, tuple[str, tuple, bytes]], metadata: dict | None = None) -> None:
+    """Write {name: (dtype, shape, raw bytes)} as a safetensors file."""
+    entries, off = {}, 0
+    for name, (dt, shape, raw) in tensors.items():
+        if len(raw) != int(np.prod(shape, dtype=np.int64)) * np.dtype(_NP[dt]).itemsize:
+            raise SafetensorsError(f"{name}: {len(raw)} bytes for {dt} {tuple(shape)}")
+        entries[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + len(raw)]}
+        off += len(raw)
+    if metadata:
+        entries["__metadata__"] = metadata
+    head = json.dumps(entries).encode()
+    head += b" " * (-len(head) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(head)))
+        f.write(head)
+        for _, _, raw in tensors.values():
+            f.write(raw)
+
+
 def nearest_supported_bits(bits: int, supported=QLINEAR_BITS) -> int:
     """The largest supported width <= bits, else 4 (src/model/mod.rs:637-643)."""
     below = [b for b in supported if b <= bits]

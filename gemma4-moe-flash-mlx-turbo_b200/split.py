@@ -6,7 +6,9 @@
     <split>/resident/resident.safetensors   every tensor but the routed experts
     <split>/experts/layer_XX_experts.ecb    each layer's routed experts (src/memory.rs:386-398)
 
-load_split() returns (cfg, embed, layers, final_norm) for Gemma4Model(cfg, embed,
+split_checkpoint() makes that layout from an MLX checkpoint (the reference's
+splitter, src/splitter.rs:99-196); load_split() returns (cfg, embed, layers,
+final_norm) for Gemma4Model(cfg, embed,
 layers, final_norm, batch, max_positions, ...).  Names, per-component bit widths
 (overrides keyed by "language_model.model.layers.N.<component>") and the
 flexible scale / bias names follow the reference; quantised linears whose width
@@ -17,6 +19,10 @@ from __future__ import annotations
 
 import json
 import os
+import re
+import shutil
+
+import numpy as np
 
 from . import ecb as _ecb
 from . import safetensors as _st
@@ -146,3 +152,91 @@ def load_split(split_dir: str, device="cuda", n_layers: int | None = None, exper
                              "e", eb, egs)
     cfg = model_cfg(args, embed.bits)
     return cfg, embed, layers, get("language_model.norm.weight")
+
+
+_CONFIG_FILES = ("config.json", "tokenizer.json", "tokenizer_config.json", "generation_config.json",
+                 "chat_template.jinja")
+_PROJ, _COMP = ("gate_proj", "up_proj", "down_proj"), ("weight", "scales", "biases")
+
+
+def _layout(names) -> str:
+    """'ud' (Unsloth: language_model.model.layers.N.experts.switch_glu.<proj>.<comp>) or
+    'fused' (mlx-community: model.language_model.layers.N.experts.{gate_up_proj,down_proj}[_scales|_biases]),
+    src/splitter.rs:24-38 for the Gemma-4 layouts."""
+    if any(".experts.switch_glu." in n for n in names):
+        return "ud"
+    if any(".experts.gate_up_proj" in n or ".experts.down_proj" in n for n in names):
+        return "fused"
+    raise ValueError("no Gemma-4 expert tensors (experts.switch_glu.* or experts.gate_up_proj / down_proj)")
+
+
+def _is_expert(name: str, layout: str) -> bool:
+    return ".experts.switch_glu." in name if layout == "ud" else (".experts.gate_up_proj" in name
+                                                                   or ".experts.down_proj" in name)
+
+
+def _canonical(name: str, layout: str) -> str:
+    """Resident names start with language_model.layers.N / language_model.embed_tokens
+    (src/splitter.rs:80-95)."""
+    if layout == "ud":
+        return name.replace("language_model.model.", "language_model.", 1)
+    return name[len("model."):] if name.startswith("model.") else name
+
+
+def _stacked(raw) -> tuple[str, tuple, np.ndarray]:
+    """(dtype, per-expert shape, uint8 [E, per-expert bytes]) of an expert-stacked tensor."""
+    dt, shape, data = raw
+    E = shape[0]
+    return dt, tuple(shape[1:]), np.frombuffer(data, np.uint8).reshape(E, -1)
+
+
+def _halves(t):
+    """Split a fused gate_up tensor along its first per-expert dim: (gate, up)
+    (src/splitter.rs:362-403)."""
+    dt, shape, a = t
+    if shape[0] % 2:
+        raise ValueError(f"fused gate_up dim {shape[0]} is odd")
+    h = a.shape[1] // 2
+    half = (shape[0] // 2,) + tuple(shape[1:])
+    return (dt, half, a[:, :h]), (dt, half, a[:, h:])
+
+
+def split_checkpoint(model_dir: str, out_dir: str) -> dict:
+    """MLX checkpoint (model.safetensors.index.json + shards) -> split layout:
+    resident/resident.safetensors (every non-expert tensor, canonical names),
+    experts/layer_XX_experts.ecb (9 tensors per layer: gate / up / down x
+    weight / scales / biases, expert-major), the config files and
+    split_config.json.  Returns the split metadata."""
+    with open(os.path.join(model_dir, "model.safetensors.index.json")) as f:
+        weight_map = json.load(f)["weight_map"]
+    layout = _layout(weight_map)
+    os.makedirs(os.path.join(out_dir, "resident"), exist_ok=True)
+    os.makedirs(os.path.join(out_dir, "experts"), exist_ok=True)
+    for name in _CONFIG_FILES:
+        if os.path.exists(os.path.join(model_dir, name)):
+            shutil.copyfile(os.path.join(model_dir, name), os.path.join(out_dir, name))
+    by_shard: dict[str, list[str]] = {}
+    for name, shard in weight_map.items():
+        by_shard.setdefault(shard, []).append(name)
+    raw = {}
+    for shard, names in sorted(by_shard.items()):
+        raw.update(_st.read_raw(os.path.join(model_dir, shard), names))
+    resident = {_canonical(n, layout): raw[n] for n in sorted(weight_map) if not _is_expert(n, layout)}
+    _st.save_raw(os.path.join(out_dir, "resident", "resident.safetensors"), resident)
+    pat = re.compile(r"layers\.(\d+)\.experts\.")
+    n_layers = 1 + max(int(pat.search(n).group(1)) for n in weight_map if _is_expert(n, layout))
+    for i in range(n_layers):
+        if layout == "ud":
+            pre = f"language_model.model.layers.{i}.experts.switch_glu"
+            tensors = [_stacked(raw[f"{pre}.{p}.{c}"]) for p in _PROJ for c in _COMP]
+        else:
+            pre = f"model.language_model.layers.{i}.experts"
+            gate, up = zip(*(_halves(_stacked(raw[f"{pre}.gate_up_proj{s}"])) for s in ("", "_scales", "_biases")))
+            down = [_stacked(raw[f"{pre}.down_proj{s}"]) for s in ("", "_scales", "_biases")]
+            tensors = list(gate) + list(up) + down
+        _ecb.write_tensors(os.path.join(out_dir, "experts", f"layer_{i:02d}_experts.ecb"), tensors)
+    meta = {"original_model": model_dir, "resident_dir": "resident", "expert_dir": "experts", "format": "ecb",
+            "layout": layout, "num_expert_layers": n_layers}
+    with open(os.path.join(out_dir, "split_config.json"), "w") as f:
+        json.dump(meta, f, indent=2)
+    return meta

@@ -119,3 +119,77 @@ def test_split_expert_slice_and_missing_tensor(fm, split_dir, tmp_path):
     fm.safetensors.save(str(bdir / "resident" / "resident.safetensors"), broken)
     with pytest.raises(KeyError, match="router.scale"):
         fm.split.load_split(str(bdir), device="cpu", n_layers=1)
+
+
+_NAME_OF_CODE = {0: "U8", 1: "U32", 2: "BF16", 3: "F16", 4: "F32", 5: "I32"}
+
+
+def _stacked_from_ecb(fm, path):
+    """An ECB file's 9 tensors as expert-stacked (dtype, (E, *shape), bytes)."""
+    hdr = fm.ecb.read_header(path)
+    E, stride = hdr["num_experts"], hdr["stride"]
+    with open(path, "rb") as f:
+        f.seek(hdr["header_size"])
+        data = np.frombuffer(f.read(E * stride), np.uint8).reshape(E, stride)
+    out, off = [], 0
+    for size, code, shape in hdr["tensors"]:
+        out.append((_NAME_OF_CODE[code], (E,) + tuple(shape), data[:, off:off + size].tobytes()))
+        off += size
+    return out
+
+
+def _checkpoint(fm, split_path, t, out, fused):
+    """The fixture as an MLX checkpoint (two shards + index) in the UD or the fused layout."""
+    st = fm.safetensors
+    os.makedirs(out)
+    res = {}
+    for name, v in t.items():
+        raw = st.read_raw(os.path.join(split_path, "resident", "resident.safetensors"), [name])[name]
+        res[("model." + name) if fused else name.replace("language_model.", "language_model.model.", 1)] = raw
+    exp = {}
+    for i in range(2):
+        s = _stacked_from_ecb(fm, os.path.join(split_path, "experts", f"layer_{i:02d}_experts.ecb"))
+        if fused:
+            pre = f"model.language_model.layers.{i}.experts"
+            for j, suf in enumerate(("", "_scales", "_biases")):
+                g, u = s[j], s[3 + j]
+                E = g[1][0]
+                gu = np.concatenate([np.frombuffer(g[2], np.uint8).reshape(E, -1),
+                                     np.frombuffer(u[2], np.uint8).reshape(E, -1)], axis=1)
+                exp[f"{pre}.gate_up_proj{suf}"] = (g[0], (E, 2 * g[1][1]) + g[1][2:], gu.tobytes())
+                exp[f"{pre}.down_proj{suf}"] = s[6 + j]
+        else:
+            pre = f"language_model.model.layers.{i}.experts.switch_glu"
+            for j, (p, c) in enumerate((p, c) for p in ("gate_proj", "up_proj", "down_proj")
+                                       for c in ("weight", "scales", "biases")):
+                exp[f"{pre}.{p}.{c}"] = s[j]
+    st.save_raw(os.path.join(out, "model-00001-of-00002.safetensors"), res)
+    st.save_raw(os.path.join(out, "model-00002-of-00002.safetensors"), exp)
+    wm = {n: "model-00001-of-00002.safetensors" for n in res} | {n: "model-00002-of-00002.safetensors" for n in exp}
+    with open(os.path.join(out, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {}, "weight_map": wm}, f)
+    with open(os.path.join(split_path, "config.json")) as f, open(os.path.join(out, "config.json"), "w") as g:
+        g.write(f.read())
+
+
+@pytest.mark.parametrize("fused", [False, True])
+def test_split_checkpoint_round_trip(fm, split_dir, tmp_path, fused):
+    """An MLX checkpoint (Unsloth UD or mlx-community fused gate_up layout) split by
+    split_checkpoint gives byte-identical ECB files and the same decoder layers as
+    the split directory it was made from."""
+    path, t = split_dir
+    ckpt, out = str(tmp_path / "ckpt"), str(tmp_path / "out")
+    _checkpoint(fm, path, t, ckpt, fused)
+    meta = fm.split.split_checkpoint(ckpt, out)
+    assert meta["layout"] == ("fused" if fused else "ud") and meta["num_expert_layers"] == 2
+    for i in range(2):
+        name = f"layer_{i:02d}_experts.ecb"
+        with open(os.path.join(path, "experts", name), "rb") as a, open(os.path.join(out, "experts", name), "rb") as b:
+            assert a.read() == b.read()
+    _, e1, l1, n1 = fm.split.load_split(path, device="cpu")
+    _, e2, l2, n2 = fm.split.load_split(out, device="cpu")
+    assert torch.equal(e1.weight, e2.weight) and torch.equal(n1, n2)
+    for a, b in zip(l1, l2):
+        assert torch.equal(a.q_proj.weight, b.q_proj.weight) and torch.equal(a.mlp[2].scales, b.mlp[2].scales)
+        assert torch.equal(a.router["per_expert_scale"], b.router["per_expert_scale"])
+        assert torch.equal(a.experts.buf, b.experts.buf)
