@@ -77,7 +77,9 @@ class EPComm:
 
     def p2p_init(self, cap: int, hidden: int, top_k: int) -> None:
         """Collective: (re)creates the peer-memory exchange windows for
-        FMOE_EP_P2P calls with this cap / hidden / top_k."""
+        FMOE_EP_P2P calls with this cap / hidden / top_k.  Re-creating frees
+        the previous windows: release CUDA graphs that captured P2P exchanges
+        on them first."""
         self.p2p_shape = None
         check(lib().fmoe_ep_p2p_init(self.handle, cap, hidden, top_k))
         self.p2p_shape = (cap, hidden, top_k)

@@ -414,7 +414,8 @@ int fmoe_ep_comm_status(fmoe_ep_comm_t* comm);
 /* Collective (all ranks): allocates this rank's exchange window for FMOE_EP_P2P
  * (receive rows, ids, weights and returned partial sums for n_ranks x cap rows;
  * flags) and maps every peer's window into this process.  At most 8 ranks.
- * Released by fmoe_ep_comm_destroy / _abort or a new call.  Waits on peers'
+ * Released by fmoe_ep_comm_destroy / _abort or a new call (which frees the old
+ * windows: destroy any CUDA graph that captured P2P exchanges on them first).  Waits on peers'
  * flags are bounded: a timeout ends with FMOE_ERR_TIMEOUT in the workspace
  * status word. */
 int fmoe_ep_p2p_init(fmoe_ep_comm_t* comm, int64_t cap, int hidden, int top_k);
