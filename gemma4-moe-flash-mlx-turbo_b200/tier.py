@@ -19,6 +19,32 @@ import torch
 from . import ExpertTable, Gemma4MoeBlock, QuantizedLinear, moe_experts
 
 
+def plan_slots(need, slot_of: np.ndarray, owner: np.ndarray, used: np.ndarray, clock: int) -> list[tuple[int, int]]:
+    """Slot bookkeeping of one ensure() call (host only): every needed expert
+    already in a slot is marked used at `clock`; each missing one gets a free
+    slot, else the least recently used slot whose expert is not needed now.
+    slot_of (expert -> slot, -1 on the host only), owner (slot -> expert, -1
+    free) and used (slot -> last clock) are updated in place.  Returns the
+    (expert, slot) copies to issue, in order."""
+    for e in need:
+        if slot_of[e] >= 0:
+            used[slot_of[e]] = clock
+    copies = []
+    for e in [int(e) for e in need if slot_of[e] < 0]:
+        free = np.flatnonzero(owner < 0)
+        if free.size:
+            s = int(free[0])
+        else:
+            cand = np.flatnonzero(used < clock)
+            s = int(cand[np.argmin(used[cand])])
+            slot_of[owner[s]] = -1
+        owner[s] = e
+        slot_of[e] = s
+        used[s] = clock
+        copies.append((e, s))
+    return copies
+
+
 class HostExpertTier:
     """host_tables: one whole-layer ExpertTable per layer in pinned host memory (e.g.
     ecb.load(..., pin=True)); slots: HBM expert slots per layer (>= the distinct
@@ -65,28 +91,15 @@ class HostExpertTier:
         if need.size > self.slots:
             raise ValueError(f"layer {layer}: {need.size} routed experts exceed {self.slots} slots")
         self.clock += 1
-        missing = [int(e) for e in need if L["slot_of"][e] < 0]
-        self.hits += need.size - len(missing)
-        self.misses += len(missing)
-        for e in need:
-            if L["slot_of"][e] >= 0:
-                L["used"][L["slot_of"][e]] = self.clock
-        if not missing:
+        copies = plan_slots(need, L["slot_of"], L["owner"], L["used"], self.clock)
+        self.hits += need.size - len(copies)
+        self.misses += len(copies)
+        if not copies:
             return
         self.copy_stream.wait_stream(stream)  # slots may still be read by earlier calls on `stream`
         with torch.cuda.stream(self.copy_stream):
-            for e in missing:
-                free = np.flatnonzero(L["owner"] < 0)
-                if free.size:
-                    s = int(free[0])
-                else:  # least recently used slot whose expert is not needed now
-                    cand = np.flatnonzero(L["used"] < self.clock)
-                    s = int(cand[np.argmin(L["used"][cand])])
-                    L["slot_of"][L["owner"][s]] = -1
-                L["owner"][s] = e
-                L["slot_of"][e] = s
-                L["used"][s] = self.clock
-                st = host.stride
+            st = host.stride
+            for e, s in copies:
                 L["hbm"][s * st:(s + 1) * st].copy_(host.buf[e * st:(e + 1) * st], non_blocking=True)
                 self.bytes_copied += st
             L["staging"].copy_(torch.from_numpy(np.maximum(L["slot_of"], 0).astype(np.int32)))
