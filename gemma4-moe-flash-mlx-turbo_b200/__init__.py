@@ -126,6 +126,7 @@ SIGNATURES = {
         _I,
         [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P],
     ),
+    "fmoe_moe_block_noalloc_status": (_I, [_I, _P]),
     "fmoe_profile_enable": (_I, [_I]),
     "fmoe_profile_read": (_I, [ctypes.POINTER(KernelStatC), _I, _I]),
     "fmoe_quantize": (_I, [_P, _I, _I64, _I64, _I, _I, _P, _P, _P, _P]),

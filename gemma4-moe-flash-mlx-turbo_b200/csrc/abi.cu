@@ -350,8 +350,8 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
   ExpertsDev d;
   rc = to_experts(ex, &d);
   if (rc) return rc;
+  if (T <= 0) return FMOE_OK;  // no tokens: nothing to route (x / y may be null)
   if (!x || !y) return set_error(FMOE_ERR_INVALID, "moe_block: null x/y");
-  if (T <= 0) return FMOE_OK;
   if (q.in != d.H) return set_error(FMOE_ERR_INVALID, "moe_block: router in %d != hidden %d", q.in, d.H);
   if (T > kMaxDecodeTokens)
     return set_error(FMOE_ERR_UNSUPPORTED, "moe_block: T=%lld above the decode path's %d", (long long)T, kMaxDecodeTokens);

@@ -51,8 +51,13 @@ using namespace fmoe;
 extern "C" int fmoe_moe_block_forward_noalloc(const void* x, int64_t T, const fmoe_router_t* r,
                                               const fmoe_experts_t* ex, void* y, int32_t* ids, float* weights,
                                               void* stream) {
+  if (T <= 0) return FMOE_OK;  // nothing to do, nothing queued on the shared array
+  // Cheap argument checks first, so a call that is going to be rejected queues
+  // nothing on the array every call shares.
+  if (!x || !y) return set_error(FMOE_ERR_INVALID, "moe_block_forward_noalloc: null x/y");
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "moe_block_forward_noalloc: x not 16-byte aligned");
   const size_t need = fmoe_moe_block_workspace_bytes(T, r, ex);
-  if (T > 0 && need == 0) return set_error(FMOE_ERR_INVALID, "moe_block_forward_noalloc: bad router or expert table");
+  if (need == 0) return set_error(FMOE_ERR_INVALID, "moe_block_forward_noalloc: bad router or expert table");
   if (need > kNoallocScratchBytes)
     return set_error(FMOE_ERR_WORKSPACE,
                      "moe_block_forward_noalloc: T=%lld needs %zu bytes of scratch, the static array holds %zu "
@@ -62,10 +67,21 @@ extern "C" int fmoe_moe_block_forward_noalloc(const void* x, int64_t T, const fm
   int rc = noalloc_scratch_ptr(&scratch);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The router's completion counter, the down kernel's tile counters and the
-  // status word must start at zero; clear the whole region this call uses.
-  if (need && cudaMemsetAsync(scratch, 0, need, st) != cudaSuccess)
+  // The router's completion counter and the down kernel's tile counters must
+  // start at zero.  Word 0 (the device status word) is left alone: a bounded
+  // device wait that gave up in an earlier call stays visible to
+  // fmoe_moe_block_noalloc_status until the caller clears it.
+  const cudaError_t e =
+      cudaMemsetAsync(static_cast<uint8_t*>(scratch) + sizeof(int), 0, need - sizeof(int), st);
+  if (e != cudaSuccess)
     return set_error(FMOE_ERR_CUDA, "moe_block_forward_noalloc: clearing the scratch failed: %s",
-                     cudaGetErrorString(cudaGetLastError()));
+                     cudaGetErrorString(e));
   return fmoe_moe_block_forward(x, T, r, ex, y, ids, weights, scratch, kNoallocScratchBytes, stream);
+}
+
+extern "C" int fmoe_moe_block_noalloc_status(int clear, void* stream) {
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_ptr(&scratch);
+  if (rc) return rc;
+  return fmoe_workspace_status(scratch, clear, stream);
 }

@@ -71,7 +71,8 @@ def model_cfg(args: dict, embed_bits: int) -> dict:
     sr = rope_config(args, False)
     return dict(hidden=args["hidden_size"], layers=args["num_hidden_layers"], heads=args["num_attention_heads"],
                 sliding_kv_heads=args["num_key_value_heads"], sliding_head_dim=args["head_dim"],
-                full_kv_heads=args.get("num_global_key_value_heads") or args["num_key_value_heads"],
+                full_kv_heads=(args.get("num_global_key_value_heads") or args["num_key_value_heads"])
+                if args.get("attention_k_eq_v") else args["num_key_value_heads"],
                 full_head_dim=args.get("global_head_dim") or args["head_dim"], sliding_theta=sr[1],
                 full_theta=fr[1], full_partial_rotary=fr[0] / (args.get("global_head_dim") or args["head_dim"]),
                 window=args.get("sliding_window") or 1024, dense_inter=args.get("intermediate_size"),

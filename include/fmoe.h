@@ -211,6 +211,12 @@ int fmoe_moe_block_forward(const void* x, int64_t T, const fmoe_router_t* r, con
 int fmoe_moe_block_forward_noalloc(const void* x, int64_t T, const fmoe_router_t* r,
                                    const fmoe_experts_t* ex, void* y, int32_t* ids, float* weights,
                                    void* stream);
+/* Device status word of the no-allocation entry point's scratch array (the
+ * fmoe_workspace_status of that array; no counterpart in the reference):
+ * FMOE_OK, or FMOE_ERR_TIMEOUT when a bounded device wait in an earlier call
+ * gave up (that call's y is then not valid).  The word persists across calls
+ * until read with clear != 0.  Synchronises `stream`. */
+int fmoe_moe_block_noalloc_status(int clear, void* stream);
 
 /* ---- quantised KV cache + decode attention ---------------------------- */
 

@@ -102,6 +102,17 @@ def test_split_layers(fm, split_dir):
     assert torch.equal(f.q_proj.scales, t["language_model.layers.1.self_attn.q_proj.weight_scales"])
 
 
+def test_model_cfg_global_kv_heads_follow_k_eq_v(fm, split_dir):
+    """num_global_key_value_heads sizes the full layers' KV heads only when
+    attention_k_eq_v is set (src/model/mod.rs:463); otherwise they keep
+    num_key_value_heads, as load_split's layers do."""
+    path, _ = split_dir
+    args, _ = fm.split.read_config(path)
+    assert fm.split.model_cfg(args, 6)["full_kv_heads"] == 1
+    off = dict(args, attention_k_eq_v=False)
+    assert fm.split.model_cfg(off, 6)["full_kv_heads"] == args["num_key_value_heads"] == 2
+
+
 def test_split_expert_slice_and_missing_tensor(fm, split_dir, tmp_path):
     path, t = split_dir
     _, _, layers, _ = fm.split.load_split(path, device="cpu", n_layers=1, experts=(1, 2))
