@@ -97,7 +97,7 @@ class KvCacheC(ctypes.Structure):
         ("k_bits", ctypes.c_int32),
         ("v_bits", ctypes.c_int32),
         ("group_size", ctypes.c_int32),
-        ("reserved", ctypes.c_int32),
+        ("turbo_bits", ctypes.c_int32),
         ("k", ctypes.c_void_p),
         ("v", ctypes.c_void_p),
         ("k_scales", ctypes.c_void_p),

@@ -17,6 +17,8 @@
 //  10 qgemv  d = (gelu(g) * u) . Wd^T                     (GELU gating fused into the input prologue)
 //  11 ff_out x' = (h + post_ff_norm(post_ff_norm_1(d) + post_ff_norm_2(moe))) * layer_scalar
 // Every intermediate is rounded to bf16 where the reference holds a bf16 array.
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "internal.h"
@@ -322,8 +324,18 @@ struct DecWs {
   float* wts;
   void* attn_ws;
   EpWs ep;  // expert-parallel exchange (fmoe_decoder_layer_forward_ep only)
+  bool dl;  // the streaming path applies (local experts): plan + its workspace
+  DlPlan dlp;
+  DlWs dlw;
   size_t bytes;
 };
+
+// The per-op kernel sequence instead of the streaming layer, for A/B timing
+// and as a cross-check (environment FMOE_DECODE_PATH=ops).
+static bool force_ops_path() {
+  const char* e = std::getenv("FMOE_DECODE_PATH");
+  return e && std::strcmp(e, "ops") == 0;
+}
 
 static int dec_dims(const fmoe_decoder_layer_t* L, int* qkv_rows) {
   if (!L) return set_error(FMOE_ERR_INVALID, "decoder: null layer");
@@ -379,6 +391,8 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   d.moe = c.take<bf16>((size_t)T * H);
   d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
   d.wts = c.take<float>((size_t)T * L->router.top_k);
+  d.dl = ep_ranks == 0 && !force_ops_path() && dl_plan(L, kv, T, &d.dlp) == FMOE_OK;
+  if (d.dl) dl_carve(c, d.dlp, &d.dlw);
   d.bytes = c.off + 256;
   if (w) *w = d;
   return d.bytes;
@@ -468,6 +482,10 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
   bf16* xb = static_cast<bf16*>(x);
   const int Ti = (int)T;
   int o_parts = 1, gu_parts = 1, d_parts = 1;
+  if (w.dl) {
+    const DlBufs b = {w.q, w.attn, w.hres, w.h1, w.h2, w.xs, w.moe, w.attn_ws};
+    return dl_layer_forward(L, kv, w.dlp, w.dlw, xb, pos, pos_dev, b, st);
+  }
 
   // 1 q|k|v = input_norm(x) . W^T  (plain fp32 stores)
   {
@@ -636,7 +654,9 @@ int fmoe_decoder_layer_forward_ep(const fmoe_decoder_layer_t* L, const fmoe_kv_c
 
 size_t fmoe_lm_head_workspace_bytes(int64_t T) {
   if (T <= 0) return 0;
-  return 256 + align_up(sizeof(unsigned) * (size_t)T, 256) + sizeof(float2) * (size_t)T * kCapCtas;
+  const size_t ops = 256 + align_up(sizeof(unsigned) * (size_t)T, 256) + sizeof(float2) * (size_t)T * kCapCtas;
+  const size_t streaming = dl_lm_workspace_bytes(T);
+  return ops > streaming ? ops : streaming;
 }
 
 int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps, const void* x, int64_t T,
@@ -651,6 +671,9 @@ int fmoe_lm_head(const fmoe_qweight_t* embed, const void* final_norm, float eps,
   if (!workspace || workspace_bytes < fmoe_lm_head_workspace_bytes(T))
     return set_error(FMOE_ERR_WORKSPACE, "lm_head: workspace too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!force_ops_path())
+    return dl_lm_head(q, static_cast<const bf16*>(final_norm), eps, static_cast<const bf16*>(x), T, softcap, logits,
+                      next_ids, pos_dev, workspace, st);
   uint8_t* base = static_cast<uint8_t*>(workspace);
   int* status = reinterpret_cast<int*>(base);
   unsigned* ctr = reinterpret_cast<unsigned*>(base + 256);

@@ -102,6 +102,7 @@ int launch_dequantize(const QW& w, int group, const int32_t* ids, int64_t n, flo
 // kv.cu: device view of one layer's KV cache (see fmoe_kv_cache_t).
 struct KvDev {
   int mode, B, Hkv, D;
+  int turbo;  // bf16 mode: TurboQuant bits applied by the decoder's append (0: none)
   int64_t cap;
   void* k;  // bf16 rows (FMOE_KV_BF16) or packed 4-bit codes (FMOE_KV_AFFINE)
   void* v;  // bf16 rows or packed 8-bit codes
@@ -243,11 +244,44 @@ int ep_experts(const fmoe_ep_comm_t* c, const bf16* x, int64_t T, int64_t cap, i
 // kv.cu
 int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d);
 size_t attn_workspace_bytes(const KvDev& c, int Hq);
+// pdl: launched as a programmatic dependent of the preceding kernel (the
+// kernel waits for it before reading q or the cache).
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
-                       void* ws, bf16* out, cudaStream_t st);
+                       void* ws, bf16* out, cudaStream_t st, bool pdl = false);
 int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v, const bf16* q_norm,
                     const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
                     const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st);
+
+// dlayer.cu: the decode layer as six streaming launches (T <= 8, experts
+// local) and the streaming lm_head.
+struct DlPlan {
+  int T, H, D, Hq, Hkv, QD, Id, Ie, E, k, Umax, qkv_tiles;
+  int qbits, obits, rbits;
+  int nw_r, nw_g, nw_d, nw_x;                      // warps of the two-family launches
+  int mp_qkv, mp_o, mp_r, mp_g, mp_d, mp_x, mp_y;  // pieces per unit (bounds)
+  size_t sm_qkv, sm_o, sm_1, sm_2, sm_3;           // dynamic shared memory per launch
+};
+struct DlWs {  // counters are zero between calls
+  unsigned *uc_qkv, *uc_o, *uc_r, *uc_g, *uc_d, *uc_x, *uc_y, *gc_qkv, *gc_y, *grid;
+  float *p_qkv, *p_o, *p_r, *p_g, *p_d, *p_x, *p_y;  // pieces
+  float *f_qkv, *f_o, *f_r, *f_d, *f_y;              // finished units
+  bf16 *act_d, *act_e;
+  int32_t *ids, *slot, *uniq, *nuniq;
+  float* wts;
+};
+struct DlBufs {  // layer buffers shared with the per-op path
+  bf16 *q, *attn, *h, *h1, *h2, *xs, *moe;
+  void* attn_ws;
+};
+struct Carver;
+// FMOE_OK when the layer call can take the streaming path (fills *p).
+int dl_plan(const fmoe_decoder_layer_t* L, const KvDev& kv, int64_t T, DlPlan* p);
+size_t dl_carve(Carver& c, const DlPlan& p, DlWs* w);
+int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPlan& p, const DlWs& w, bf16* x,
+                     int64_t pos, const int64_t* pos_dev, const DlBufs& b, cudaStream_t st);
+size_t dl_lm_workspace_bytes(int64_t T);
+int dl_lm_head(const QW& e, const bf16* norm, float eps, const bf16* x, int64_t T, float cap, float* logits,
+               int32_t* next_ids, int64_t* pos_dev, void* ws, cudaStream_t st);
 
 // Bump allocator over a caller workspace.
 struct Carver {

@@ -32,141 +32,9 @@
 #include "common.cuh"
 #include "stage.cuh"
 #include "rowops.cuh"
+#include "kvrow.cuh"
 
 namespace fmoe {
-
-// ---------------------------------------------------------------------------
-// TurboQuant constants: deterministic_signs(n, 42) (src/cache.rs:29-43) and
-// the N(0,1) Lloyd-Max tables (src/cache.rs:67-89).
-
-struct SignTable {
-  float s[512];
-};
-constexpr SignTable make_sign_table() {
-  SignTable t{};
-  uint64_t st = 42;
-  for (int i = 0; i < 512; ++i) {
-    st = st * 6364136223846793005ull + 1442695040888963407ull;
-    t.s[i] = ((st >> 63) & 1ull) ? -1.0f : 1.0f;
-  }
-  return t;
-}
-__constant__ SignTable kRhtSigns = make_sign_table();
-
-struct Codebook {
-  float c[16];
-  float b[15];
-  int n;
-};
-__constant__ Codebook kLloyd[3] = {
-    {{-1.510f, -0.453f, 0.453f, 1.510f}, {-0.982f, 0.0f, 0.982f}, 4},
-    {{-2.152f, -1.344f, -0.756f, -0.245f, 0.245f, 0.756f, 1.344f, 2.152f},
-     {-1.748f, -1.050f, -0.501f, 0.0f, 0.501f, 1.050f, 1.748f},
-     8},
-    {{-2.733f, -2.069f, -1.618f, -1.256f, -0.942f, -0.657f, -0.388f, -0.128f, 0.128f, 0.388f, 0.657f, 0.942f, 1.256f,
-      1.618f, 2.069f, 2.733f},
-     {-2.401f, -1.844f, -1.437f, -1.099f, -0.800f, -0.522f, -0.258f, 0.0f, 0.258f, 0.522f, 0.800f, 1.099f, 1.437f,
-      1.844f, 2.401f},
-     16}};
-
-// ---------------------------------------------------------------------------
-// warp-per-row helpers
-
-template <int P>
-__device__ __forceinline__ void warp_fwht(float (&v)[P], int lane) {
-#pragma unroll
-  for (int h = 1; h < P; h <<= 1)
-#pragma unroll
-    for (int i = 0; i < P; i += 2 * h)
-#pragma unroll
-      for (int j = i; j < i + h; ++j) {
-        const float a = v[j], b = v[j + h];
-        v[j] = a + b;
-        v[j + h] = a - b;
-      }
-#pragma unroll
-  for (int m = 1; m < 32; m <<= 1) {
-    const bool upper = (lane & m) != 0;
-#pragma unroll
-    for (int j = 0; j < P; ++j) {
-      const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
-      v[j] = upper ? __fsub_rn(o, v[j]) : __fadd_rn(v[j], o);
-    }
-  }
-}
-
-// MLX-affine quantisation of the warp's D values in groups of 64 (64/P lanes
-// per group), the oracle's quantize_group arithmetic; codes stored as the
-// little-endian bit stream (4-bit: P/8 words per lane, 8-bit: P/4 words).
-template <int P, int BITS>
-__device__ __forceinline__ void warp_quant_store(const float (&v)[P], int lane, uint32_t* wrow, bf16* srow,
-                                                 bf16* brow) {
-  constexpr int LG = 64 / P;
-  float mn = v[0], mx = v[0];
-#pragma unroll
-  for (int i = 1; i < P; ++i) {
-    mn = fminf(mn, v[i]);
-    mx = fmaxf(mx, v[i]);
-  }
-#pragma unroll
-  for (int o = 1; o < LG; o <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  }
-  const float nmax = (float)((1u << BITS) - 1u);
-  float scale = __fdiv_rn(__fsub_rn(mx, mn), nmax);
-  if (!(scale >= 1e-7f)) scale = 1e-7f;
-  const bf16 sb = __float2bfloat16_rn(scale), bb = __float2bfloat16_rn(mn);
-  const float s = __bfloat162float(sb), b = __bfloat162float(bb);
-  constexpr int VPW = 32 / BITS;
-  uint32_t w[P / VPW];
-#pragma unroll
-  for (int i = 0; i < P / VPW; ++i) w[i] = 0;
-#pragma unroll
-  for (int i = 0; i < P; ++i) {
-    float q = rintf(__fdiv_rn(__fsub_rn(v[i], b), s));
-    q = fminf(fmaxf(q, 0.0f), nmax);
-    w[i / VPW] |= (uint32_t)q << (BITS * (i % VPW));
-  }
-#pragma unroll
-  for (int i = 0; i < P / VPW; ++i) wrow[lane * (P / VPW) + i] = w[i];
-  if (lane % LG == 0) {
-    srow[lane / LG] = sb;
-    brow[lane / LG] = bb;
-  }
-}
-
-// TurboQuant round trip of one row in registers, src/cache.rs:94-129.  With
-// R = H diag(s), H the normalised Sylvester matrix:
-//   y   = (v / (n + 1e-8)) R sqrt(D) = s (.) FWHT(v / (n + 1e-8))
-//   out = n (c[idx] / sqrt(D)) R^T    = n / D * FWHT(s (.) c[idx])
-template <int P>
-__device__ __forceinline__ void warp_turbo(float (&v)[P], int lane, int bits) {
-  constexpr int D = 32 * P;
-  const Codebook& cb = kLloyd[bits - 2];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < P; ++i) ss = fmaf(v[i], v[i], ss);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float n = sqrtf(ss);
-  const float den = n + 1e-8f;
-#pragma unroll
-  for (int i = 0; i < P; ++i) v[i] = v[i] / den;
-  warp_fwht<P>(v, lane);
-#pragma unroll
-  for (int i = 0; i < P; ++i) {
-    const float sg = kRhtSigns.s[lane * P + i];
-    const float y = v[i] * sg;
-    int idx = 0;
-    for (int q = 0; q < cb.n - 1; ++q) idx += (y >= cb.b[q]) ? 1 : 0;
-    v[i] = cb.c[idx] * sg;
-  }
-  warp_fwht<P>(v, lane);
-  const float f = n / (float)D;
-#pragma unroll
-  for (int i = 0; i < P; ++i) v[i] *= f;
-}
 
 // ---------------------------------------------------------------------------
 // append: one warp per new (batch, kv head, token) row, K and V together
@@ -537,6 +405,11 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
                        bf16* __restrict__ out, int* __restrict__ status) {
   using C = AtCfg<P, FMOE_KV_AFFINE>;
   using Sm = AffSmem<P, GQ>;
+  // launched as a programmatic dependent: q and the newest cache rows come
+  // from the preceding kernel (a no-op otherwise); the next kernel may start
+  // streaming its weights meanwhile
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int D = C::D, G = C::G, CH = C::CH, NST = C::NST, TPC = C::TPC, WPT = C::WPT, GPW = C::GPW;
   static_assert(GPW == 4, "a scale row of a warp's groups is one 8-byte load");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -888,6 +761,11 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
                      bf16* __restrict__ out, int* __restrict__ status) {
   using C = AtCfg<P, FMOE_KV_BF16>;
   using Sm = Bf16Smem<P, GQ>;
+  // launched as a programmatic dependent: q and the newest cache rows come
+  // from the preceding kernel (a no-op otherwise); the next kernel may start
+  // streaming its weights meanwhile
+  griddep_wait();
+  griddep_launch_dependents();
   constexpr int D = C::D, CH = C::CH, NST = C::NST;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Sm::BAR);
@@ -1195,7 +1073,8 @@ int launch_turbo_round_trip(const bf16* x, int64_t rows, int D, int bits, bf16* 
 
 template <int P, int MODE, int GQ>
 static int launch_attn_t(const KvDev& c, const bf16* q, int Hq, const AttnPlan& p, int64_t nvalid,
-                         const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st) {
+                         const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st,
+                         bool pdl) {
   constexpr bool aff = MODE == FMOE_KV_AFFINE;
   constexpr int bytes = aff ? AffSmem<P, GQ>::BYTES : Bf16Smem<P, GQ>::BYTES;
   auto kern = aff ? attn_affine_kernel<P, GQ> : attn_bf16_kernel<P, GQ>;
@@ -1207,37 +1086,47 @@ static int launch_attn_t(const KvDev& c, const bf16* q, int Hq, const AttnPlan& 
   if (attr_err != cudaSuccess)
     return set_error(FMOE_ERR_CUDA, "attn_decode: shared memory attribute: %s", cudaGetErrorString(attr_err));
   const float inv = 1.0f / std::sqrt((float)(32 * P));
-  dim3 grid(p.nsplit, c.Hkv, c.B);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(p.nsplit, c.Hkv, c.B);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = bytes;
+  cfg.stream = st;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
   ProfScope prof_(aff ? "attn_affine_kernel" : "attn_bf16_kernel", st);
-  kern<<<grid, 256, bytes, st>>>(c, q, Hq, p.S, p.nsplit, nvalid, nvalid_dev, scale, inv, w.ml, w.po, w.ctr, out,
-                                 w.status);
+  cudaLaunchKernelEx(&cfg, kern, c, q, Hq, p.S, p.nsplit, nvalid, nvalid_dev, scale, inv, w.ml, w.po, w.ctr, out,
+                     w.status);
   return check_launch("attn_decode kernel");
 }
 
 template <int P, int MODE>
 static int launch_attn_m(const KvDev& c, int GQ, const bf16* q, int Hq, const AttnPlan& p, int64_t nvalid,
-                         const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st) {
+                         const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st,
+                         bool pdl) {
   switch (GQ) {
-    case 1: return launch_attn_t<P, MODE, 1>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st);
-    case 2: return launch_attn_t<P, MODE, 2>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st);
-    case 4: return launch_attn_t<P, MODE, 4>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st);
-    case 8: return launch_attn_t<P, MODE, 8>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st);
+    case 1: return launch_attn_t<P, MODE, 1>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
+    case 2: return launch_attn_t<P, MODE, 2>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
+    case 4: return launch_attn_t<P, MODE, 4>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
+    case 8: return launch_attn_t<P, MODE, 8>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
   }
   return set_error(FMOE_ERR_UNSUPPORTED, "attn_decode: %d query heads per kv head (kernels: 1, 2, 4, 8)", GQ);
 }
 
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
-                       void* ws, bf16* out, cudaStream_t st) {
+                       void* ws, bf16* out, cudaStream_t st, bool pdl) {
   const AttnPlan p = attn_plan(c, nvalid_dev ? c.cap : nvalid, Hq);
   const AttnWs w = carve_attn_ws(ws, c, Hq, p.nsplit);
   const int GQ = Hq / c.Hkv;
   if (c.D == 256)
-    return c.mode == FMOE_KV_BF16 ? launch_attn_m<8, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st)
+    return c.mode == FMOE_KV_BF16 ? launch_attn_m<8, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl)
                                   : launch_attn_m<8, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out,
-                                                                     st);
-  return c.mode == FMOE_KV_BF16 ? launch_attn_m<16, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st)
+                                                                     st, pdl);
+  return c.mode == FMOE_KV_BF16 ? launch_attn_m<16, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl)
                                 : launch_attn_m<16, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out,
-                                                                    st);
+                                                                    st, pdl);
 }
 
 }  // namespace fmoe
@@ -1294,6 +1183,8 @@ int to_kv(const fmoe_kv_cache_t* c, KvDev* d) {
                      c->k_bits, c->v_bits, c->group_size);
   if (!c->k || !c->v || !aligned16(c->k) || !aligned16(c->v))
     return set_error(FMOE_ERR_ALIGN, "kv: k/v null or not 16-byte aligned");
+  if (c->turbo_bits != 0 && (c->mode != FMOE_KV_BF16 || c->turbo_bits < 2 || c->turbo_bits > 4))
+    return set_error(FMOE_ERR_INVALID, "kv: turbo_bits %d (0, or 2..4 with the bf16 mode)", c->turbo_bits);
   if (c->mode == FMOE_KV_AFFINE &&
       (!c->k_scales || !c->k_biases || !c->v_scales || !c->v_biases || !aligned16(c->k_scales) ||
        !aligned16(c->k_biases) || !aligned16(c->v_scales) || !aligned16(c->v_biases)))
@@ -1303,6 +1194,7 @@ int to_kv(const fmoe_kv_cache_t* c, KvDev* d) {
   d->Hkv = c->kv_heads;
   d->D = c->head_dim;
   d->cap = c->capacity;
+  d->turbo = c->turbo_bits;
   d->k = c->k;
   d->v = c->v;
   d->ks = static_cast<bf16*>(c->k_scales);

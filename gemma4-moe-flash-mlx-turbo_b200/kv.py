@@ -51,6 +51,7 @@ class KVCache:
         self.c = KvCacheC()
         check(lib().fmoe_kv_cache_init(ctypes.byref(self.c), mode, batch, kv_heads, head_dim, self.capacity,
                                        _ptr(self.buf), nbytes))
+        self.c.turbo_bits = turbo_bits  # the decoder layer's append applies it too
         self._offset = 0
         self._ws = None
         self._ws_heads = 0

@@ -244,7 +244,9 @@ typedef struct fmoe_kv_cache {
   int32_t k_bits;     /* 16 (bf16 mode) or 4 */
   int32_t v_bits;     /* 16 (bf16 mode) or 8 */
   int32_t group_size; /* 64 (affine mode) */
-  int32_t reserved;
+  int32_t turbo_bits; /* bf16 mode: 0, or 2..4: the decoder layer passes each appended
+                         K / V row through the TurboQuant round trip first (the
+                         reference's quantised cache, src/cache.rs:290-308) */
   void* k;        /* bf16 [.., head_dim], or uint32 codes [.., head_dim/8] */
   void* v;        /* bf16 [.., head_dim], or uint32 codes [.., head_dim/4] */
   void* k_scales; /* affine: bf16 [.., head_dim/64]; NULL in bf16 mode */
