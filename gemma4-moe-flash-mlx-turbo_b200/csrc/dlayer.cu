@@ -49,10 +49,10 @@ namespace dl {
 constexpr int NW = 12;  // warps per CTA
 constexpr int NTHR = NW * 32;
 constexpr int kMaxT = 8;
-constexpr int kMaxHidden = 4608;      // hidden rows staged in shared memory by the row epilogues
+constexpr int kMaxHidden = 4224;      // hidden rows staged in shared memory by the row epilogues (<= 16 B each in the rings)
 constexpr int kMaxSlotsPerCta = 3;    // expert inputs one ffn3 CTA may need
 constexpr int kMaxUnique = 64;        // unique experts of one call (T * k <= 64)
-constexpr int kRingSlot = 8192;       // bytes of one warp's ring
+constexpr int kRingSlot = 6144;       // bytes of one warp's ring
 constexpr int kRingBytes = NW * kRingSlot;
 constexpr int kMaxPend = 8;           // groups one warp may complete in one launch
 
@@ -63,7 +63,8 @@ enum { SRC_MAT = 0, SRC_EXPERT = 1 };
 
 struct Fam {
   int bits, nt;        // code width; row tiles per unit (2: gate tile + up tile)
-  int K, G;            // inputs and 64-wide groups (= groups per unit)
+  int K, G;            // inputs and 64-wide groups
+  int us;              // ring steps per unit (G / groups per step)
   int w0, nw;          // global warps [w0, w0 + nw)
   int tiles;           // units per matrix (per expert slot for SRC_EXPERT)
   int64_t rowbytes;
@@ -83,8 +84,8 @@ struct Fam {
   int frag_off, xsum_off;  // shared-memory offsets of the input fragments
 };
 
-// Warp lw's range [S*lw/nw, S*(lw+1)/nw) (empty outside [0, nw)) and the warp
-// holding group s.  S * nw < 2^32 for every family (checked when planned).
+// Work is counted in ring steps: warp lw's range is [S*lw/nw, S*(lw+1)/nw)
+// (empty outside [0, nw)); warp_of gives the warp holding step s.  S * nw < 2^32 for every family (checked when planned).
 __device__ __forceinline__ int range_lo(int S, int nw, int lw) {
   lw = lw < 0 ? 0 : lw > nw ? nw : lw;
   return (int)((unsigned)S * (unsigned)lw / (unsigned)nw);
@@ -157,24 +158,21 @@ __device__ __forceinline__ UnitPtr<NT> expert_unit(const Fam& f, const ExpertsDe
 // ---------------------------------------------------------------------------
 // Per-warp streaming engine over one contiguous group range of a family.
 
-template <int BITS, int NT, int NGM, int D>
+template <int BITS, int NT, int NG, int D>
 struct Engine {
-  using Gm = sg::Geo<BITS, NGM>;
-  static constexpr int ROWS = NT * 16;
-  static constexpr int SB = ROWS * Gm::RB;    // stage bytes
-  static constexpr int CPR = NGM * Gm::CPG;   // data chunks per staged row
-  static constexpr int CPL = ROWS * CPR / 32; // chunks per lane per step
-  static_assert(ROWS * CPR % 32 == 0, "whole chunks per lane");
+  using Gm = sg::Geo<BITS>;
+  static constexpr int GS = sg::stage_bytes<BITS, NT>();  // one group's copies
+  static constexpr int SB = NG * GS;                      // stage bytes
   static_assert(D * SB <= kRingSlot, "ring slot");
   uint32_t ring;
   const uint8_t* ringp;
-  int lane, g, t, G;
+  int lane, g, t, G, us;
   int64_t rowbytes;
   int s0, s1;
-  int ipos, iu, ig;  // issue cursor
-  UnitPtr<NT> ia;
-  uint32_t sreg[D][NT][BITS == 16 ? 1 : NGM];
-  int stepn[D];
+  int ipos, iu, ig;               // issue cursor (ig: step within the unit)
+  const uint8_t* rp[2 * NT];      // rows g / g+8 of the issue unit's tiles (group 0)
+  const bf16* sp[NT];             // this lane's scale or bias word of the issue unit (group 0)
+  uint32_t sreg[D][NT][NG];
 
   __device__ __forceinline__ void init(uint8_t* r, int ln, const Fam& f, int a, int b_) {
     ringp = r;
@@ -183,50 +181,49 @@ struct Engine {
     g = ln >> 2;
     t = ln & 3;
     G = f.G;
+    us = f.us;
     rowbytes = f.rowbytes;
     s0 = a;
     s1 = b_;
   }
+  __device__ __forceinline__ void set_unit(const UnitPtr<NT>& p) {
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+      rp[2 * i] = p.w[i] + (int64_t)g * rowbytes;
+      rp[2 * i + 1] = rp[2 * i] + 8 * rowbytes;
+      // quad-cooperative scales: lane t holds s / b (t & 1) of row g + 8 (t >> 1)
+      sp[i] = ((t & 1) ? p.b[i] : p.s[i]) + (g + 8 * (t >> 1)) * G;
+    }
+  }
 
   template <class Addr>
   __device__ __forceinline__ void issue(int j, Addr& addr) {
-    const int n = min(min(NGM, G - ig), s1 - ipos);
-    stepn[j] = n;
-    const uint32_t st = ring + j * SB;
-    const int lim = n * Gm::CPG;
 #pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      const int idx = lane + 32 * k;
-      const int r = idx / CPR, c = idx - r * CPR;
-      if (c < lim) {
-        const uint8_t* src = ia.w[r >> 4] + (int64_t)(r & 15) * rowbytes + (int64_t)ig * Gm::GB + c * 16;
-        sg::cpa16(st + r * Gm::RB + sg::swz<BITS>(r, c) * 16, src);
+    for (int k = 0; k < NG; ++k) {
+      const int gi = ig * NG + k;
+      const uint8_t* src[2 * NT];
+#pragma unroll
+      for (int h = 0; h < 2 * NT; ++h) src[h] = rp[h] + gi * Gm::GB;
+      sg::issue_step<BITS, NT>(ring + j * SB + k * GS, src, lane, t);
+      if constexpr (BITS != 16) {
+#pragma unroll
+        for (int i = 0; i < NT; ++i) sreg[j][i][k] = sg::ldg_h(sp[i] + gi);
       }
     }
-    if constexpr (BITS != 16) {
-      const int rr = g + 8 * (t >> 1);
-#pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        const bf16* arr = ((t & 1) ? ia.b[i] : ia.s[i]) + rr * G + ig;
-#pragma unroll
-        for (int q = 0; q < NGM; ++q) sreg[j][i][q] = q < n ? sg::ldg_h(arr + q) : 0u;
-      }
-    }
-    ipos += n;
-    ig += n;
-    if (ig == G) {
+    ++ipos;
+    if (++ig == us) {
       ig = 0;
       ++iu;
-      if (ipos < s1) ia = addr(iu);
+      if (ipos < s1) set_unit(addr(iu));
     }
   }
 
   template <class Addr>
   __device__ __forceinline__ void prime(Addr& addr) {
     ipos = s0;
-    iu = s0 / G;
-    ig = s0 - iu * G;
-    if (ipos < s1) ia = addr(iu);
+    iu = s0 / us;
+    ig = s0 - iu * us;
+    if (ipos < s1) set_unit(addr(iu));
 #pragma unroll
     for (int j = 0; j < D; ++j) {
       if (ipos < s1) issue(j, addr);
@@ -237,8 +234,8 @@ struct Engine {
   // fr(u) -> FragPtr: the input fragments of unit u; done(u, Acc, piece_begin, piece_end).
   template <class Addr, class Frag, class Done>
   __device__ __forceinline__ void run(Addr& addr, Frag& fr, Done& done, int T) {
-    int cpos = s0, cu = s0 / G;
-    int cg = s0 - cu * G;
+    int cpos = s0, cu = s0 / us;
+    int cs = s0 - cu * us;
     int pst = s0;
     Acc<NT> y;
 #pragma unroll
@@ -246,58 +243,59 @@ struct Engine {
     FragPtr fp = {nullptr, nullptr};
     if (s0 < s1) fp = fr(cu);
     const int qb = lane & ~3;
+    const bool live_col = g < T;
+    const int gcol = live_col ? g : 0;
     while (cpos < s1) {
 #pragma unroll
       for (int j = 0; j < D; ++j) {
         if (cpos < s1) {
           sg::wait_group<D - 1>();
-          __syncwarp();  // other lanes' copies of this stage are visible
-          const int n = stepn[j];
+          if constexpr (BITS == 6) __syncwarp();  // the quad's shared row slots
           const uint8_t* st = ringp + j * SB;
+          float cc[NG][NT][4];
+          float2 xv[NG];
+          // all of the step's MMA chains first (independent), then the fixups
 #pragma unroll
-          for (int gi = 0; gi < NGM; ++gi) {
-            if (gi < n) {
-              const int gg = cg + gi;
-              uint32_t b[8];
-              if (g < T) {
-                const uint4* p = fp.frag + ((gg * T + g) * 4 + t) * 2;
-                const uint4 f0 = p[0], f1 = p[1];
-                b[0] = f0.x, b[1] = f0.y, b[2] = f0.z, b[3] = f0.w;
-                b[4] = f1.x, b[5] = f1.y, b[6] = f1.z, b[7] = f1.w;
-              } else {
+          for (int k = 0; k < NG; ++k) {
+            const int gg = cs * NG + k;
+            const uint4* p = fp.frag + ((gg * T + gcol) * 4 + t) * 2;
+            const uint4 f0 = p[0], f1 = p[1];
+            const uint32_t b[8] = {live_col ? f0.x : 0u, live_col ? f0.y : 0u, live_col ? f0.z : 0u,
+                                   live_col ? f0.w : 0u, live_col ? f1.x : 0u, live_col ? f1.y : 0u,
+                                   live_col ? f1.z : 0u, live_col ? f1.w : 0u};
+            xv[k] = *reinterpret_cast<const float2*>(fp.xsum + gg * 8 + 2 * t);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) b[e] = 0u;
-              }
-              const float x0 = fp.xsum[gg * 8 + 2 * t], x1 = fp.xsum[gg * 8 + 2 * t + 1];
-#pragma unroll
-              for (int i = 0; i < NT; ++i) {
-                float cc[4] = {0.f, 0.f, 0.f, 0.f};
-                sg::mma_group<BITS, NGM>(cc, st, 16 * i + g, 16 * i + g + 8, gi, t, b);
-                if constexpr (BITS == 16) {
-                  y.v[i][0] += cc[0], y.v[i][1] += cc[1], y.v[i][2] += cc[2], y.v[i][3] += cc[3];
-                } else {
-                  const uint32_t v = sreg[j][i][gi];
-                  const uint32_t sl = __shfl_sync(0xffffffffu, v, qb), bl = __shfl_sync(0xffffffffu, v, qb | 1);
-                  const uint32_t sh = __shfl_sync(0xffffffffu, v, qb | 2), bh = __shfl_sync(0xffffffffu, v, qb | 3);
-                  sg::fixup<BITS>(y.v[i], cc, x0, x1, sl, bl, sh, bh);
-                }
-              }
+            for (int i = 0; i < NT; ++i) {
+              cc[k][i][0] = cc[k][i][1] = cc[k][i][2] = cc[k][i][3] = 0.f;
+              sg::mma_group<BITS>(cc[k][i], st + k * GS, i, lane, t, b);
             }
           }
-          cpos += n;
-          cg += n;
-          if (cg == G || cpos == s1) {
+#pragma unroll
+          for (int k = 0; k < NG; ++k)
+#pragma unroll
+            for (int i = 0; i < NT; ++i) {
+              if constexpr (BITS == 16) {
+                y.v[i][0] += cc[k][i][0], y.v[i][1] += cc[k][i][1], y.v[i][2] += cc[k][i][2], y.v[i][3] += cc[k][i][3];
+              } else {
+                const uint32_t v = sreg[j][i][k];
+                const uint32_t sl = __shfl_sync(0xffffffffu, v, qb), bl = __shfl_sync(0xffffffffu, v, qb | 1);
+                const uint32_t sh = __shfl_sync(0xffffffffu, v, qb | 2), bh = __shfl_sync(0xffffffffu, v, qb | 3);
+                sg::fixup<BITS>(y.v[i], cc[k][i], xv[k].x, xv[k].y, sl, bl, sh, bh);
+              }
+            }
+          ++cpos;
+          if (++cs == us || cpos == s1) {
             done(cu, y, pst, cpos);
 #pragma unroll
             for (int i = 0; i < NT; ++i) y.v[i][0] = y.v[i][1] = y.v[i][2] = y.v[i][3] = 0.f;
             pst = cpos;
           }
-          if (cg == G) {
-            cg = 0;
+          if (cs == us) {
+            cs = 0;
             ++cu;
             if (cpos < s1) fp = fr(cu);
           }
-          __syncwarp();  // every lane has read the stage before it is refilled
+          if constexpr (BITS == 6) __syncwarp();  // the slots are read before they are refilled
           if (ipos < s1) issue(j, addr);
         }
         sg::commit();
@@ -401,11 +399,11 @@ struct Fin {
 template <int NT>
 __device__ __noinline__ Fin<NT> finish_piece(const Fam& f, int S, int T, int lw, int u, Acc<NT> y, int lane,
                                              int slot) {
-  const int w1 = warp_of(S, f.nw, u * f.G);
+  const int w1 = warp_of(S, f.nw, u * f.us);
   const int64_t stride = (int64_t)NT * T * 16;
   float* base = f.piece + (int64_t)slot * f.maxp * stride;
   store_block<NT>(base + (lw - w1) * stride, T, y, lane);
-  const int np = pieces_of(S, f.nw, f.G, u);
+  const int np = pieces_of(S, f.nw, f.us, u);
   Fin<NT> r;
   r.ok = arrive(f.uctr + slot, np, lane) ? 1 : 0;
   if (r.ok) sum_blocks<NT>(base, stride, np, T, r.y, lane);
@@ -414,7 +412,7 @@ __device__ __noinline__ Fin<NT> finish_piece(const Fam& f, int S, int T, int lw,
 // True when unit u's sums are complete in y (the whole unit was this warp's,
 // or this warp's piece completed it).
 #define DL_UNIT_DONE(NT, f, S, T, lw, u, y, pst, pe, lane, slot)                          \
-  ((pst) == (u) * (f).G && (pe) == ((u) + 1) * (f).G                                         \
+  ((pst) == (u) * (f).us && (pe) == ((u) + 1) * (f).us                                        \
        ? true                                                                                \
        : [&] {                                                                               \
            const Fin<NT> r_ = finish_piece<NT>((f), (S), (T), (lw), (u), (y), (lane), (slot)); \
@@ -425,15 +423,23 @@ __device__ __noinline__ Fin<NT> finish_piece(const Fam& f, int S, int T, int lw,
 // ---------------------------------------------------------------------------
 // Input fragments (prologue)
 
-// Per-token 1 / rms of x rows (warp per token), into rms[tk].
+// Per-token 1 / rms of x rows (warp per token), into rms[tk]; every load of
+// the row is issued before the first use.
 __device__ __forceinline__ void row_rms(const bf16* x, int64_t ldx, int K, int T, float eps, float* rms) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int NL = (kMaxHidden + 255) / 256;
   for (int tk = warp; tk < T; tk += NW) {
     const bf16* xr = x + tk * ldx;
+    uint4 w[NL];
+#pragma unroll
+    for (int q = 0; q < NL; ++q) {
+      const int i = lane * 8 + q * 256;
+      w[q] = i < K ? __ldcg(reinterpret_cast<const uint4*>(xr + i)) : make_uint4(0, 0, 0, 0);
+    }
     float ss = 0.f;
-    for (int i = lane * 8; i < K; i += 256) {
-      const uint4 w = ld_u4(xr + i);
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int q = 0; q < NL; ++q) {
+      const uint32_t ww[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float lo = bf16lo(ww[e]), hi = bf16hi(ww[e]);
@@ -462,7 +468,7 @@ __device__ void build_frags(uint8_t* smem, int frag_off, int xsum_off, int G, in
     if (live) {
       const int c0 = gl * 64 + 16 * tq;
       const bf16* xr = x + tk * ldx + c0;
-      const uint4 a = ld_u4(xr), bq = ld_u4(xr + 8);
+      const uint4 a = __ldcg(reinterpret_cast<const uint4*>(xr)), bq = __ldcg(reinterpret_cast<const uint4*>(xr + 8));
       const uint32_t ww[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -641,17 +647,17 @@ __device__ __noinline__ void qkv_epilogue(const QkvArgs& a, int grp, int lane) {
   }
 }
 
-template <int BITS, int NGM, int D_>
-__global__ void __launch_bounds__(NTHR, 2) qkv_kernel(const __grid_constant__ QkvArgs a) {
+template <int BITS, int D_>
+__global__ void __launch_bounds__(NTHR, 1) qkv_kernel(const __grid_constant__ QkvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float rms[kMaxT];
   __shared__ int pend[NW][kMaxPend];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.G;
+  const int S = f.tiles * f.us;
   const int lw = gw - f.w0;
-  Engine<BITS, 1, NGM, D_> en;
+  Engine<BITS, 1, 2, D_> en;
   en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
@@ -701,15 +707,36 @@ struct OArgs {
 
 // h = bf16(x + bf16(rms(bf16(o)) * w_post_attn)); h1 / h2 = bf16(rms(h) * w);
 // xs = bf16(bf16(bf16(rms(h2)) * bf16(root)) * router_scale)   (mod.rs:84-104, moe.rs:325-329)
-// `rows` (2 * H floats of shared memory: the CTA's rings, idle by now).
-__device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, float* rows) {
+// Every input of a token is first loaded into shared memory (`rows`: the
+// CTA's rings, idle by now) in one batch of independent loads, then the
+// norms run from there: one memory round trip per token, not one per pass.
+__device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, uint8_t* rows) {
   const int H = a.H;
-  float* ro = rows;      // o, then h2
-  float* rh = rows + H;  // h
+  float* ro = reinterpret_cast<float*>(rows);  // o, then h2
+  float* rh = ro + H;                          // x, then h
+  bf16* wv = reinterpret_cast<bf16*>(rh + H);  // [4][H]: post_attn, pre_ff, pre_ff_2, router_scale
+  const bf16* srcw[4] = {a.w_post_attn, a.w_pre_ff, a.w_pre_ff2, a.rscale};
   for (int tk = 0; tk < a.T; ++tk) {
-    fin_row(a.f, a.T, tk, H, ro);
+#pragma unroll
+    for (int k = 0; k < kMaxHidden / NTHR; ++k) {
+      const int i = threadIdx.x + k * NTHR;
+      if (i < H) {
+        const float o = fin_at(a.f, a.T, tk, i);
+        const float x = __bfloat162float(__ldcg(a.x + (int64_t)tk * H + i));
+        bf16 w4[4];
+        if (tk == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w4[q] = srcw[q] ? srcw[q][i] : __float2bfloat16_rn(1.0f);
+        }
+        ro[i] = o;
+        rh[i] = x;
+        if (tk == 0) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) wv[q * H + i] = w4[q];
+        }
+      }
+    }
     __syncthreads();
-    const bf16* xr = a.x + (int64_t)tk * H;
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += NTHR) {
       const float o = round_bf(ro[i]);
@@ -719,7 +746,7 @@ __device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, float* rows)
     const float r1 = rsqrtf(cta_sum(ss, red) / (float)H + a.eps);
     ss = 0.f;
     for (int i = threadIdx.x; i < H; i += NTHR) {
-      const float h = round_bf(__bfloat162float(__ldcg(xr + i)) + round_bf(ro[i] * r1 * bf2f(a.w_post_attn[i])));
+      const float h = round_bf(rh[i] + round_bf(ro[i] * r1 * bf2f(wv[i])));
       rh[i] = h;
       ss = fmaf(h, h, ss);
     }
@@ -729,8 +756,8 @@ __device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, float* rows)
       const float h = rh[i];
       const int64_t o = (int64_t)tk * H + i;
       a.h[o] = __float2bfloat16_rn(h);
-      a.h1[o] = __float2bfloat16_rn(h * r2 * bf2f(a.w_pre_ff[i]));
-      const float h2 = round_bf(h * r2 * bf2f(a.w_pre_ff2[i]));
+      a.h1[o] = __float2bfloat16_rn(h * r2 * bf2f(wv[H + i]));
+      const float h2 = round_bf(h * r2 * bf2f(wv[2 * H + i]));
       a.h2[o] = __float2bfloat16_rn(h2);
       ro[i] = h2;
       ss = fmaf(h2, h2, ss);
@@ -739,24 +766,24 @@ __device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, float* rows)
     const float rb = round_bf(a.root);
     for (int i = threadIdx.x; i < H; i += NTHR) {
       float v = round_bf(round_bf(ro[i] * r3) * rb);
-      if (a.rscale) v = round_bf(v * bf2f(a.rscale[i]));
+      if (a.rscale) v = round_bf(v * bf2f(wv[3 * H + i]));
       a.xs[(int64_t)tk * H + i] = __float2bfloat16_rn(v);
     }
     __syncthreads();  // rows reused by the next token
   }
 }
 
-template <int BITS, int NGM, int D_>
-__global__ void __launch_bounds__(NTHR, 2) o_kernel(const __grid_constant__ OArgs a) {
+template <int BITS, int D_>
+__global__ void __launch_bounds__(NTHR, 1) o_kernel(const __grid_constant__ OArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[NW];
   __shared__ int flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.G;
+  const int S = f.tiles * f.us;
   const int lw = gw - f.w0;
-  Engine<BITS, 1, NGM, D_> en;
+  Engine<BITS, 1, 2, D_> en;
   en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
@@ -771,7 +798,7 @@ __global__ void __launch_bounds__(NTHR, 2) o_kernel(const __grid_constant__ OArg
     if (DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, u)) store_block<1>(f.fin + (int64_t)u * a.T * 16, a.T, y, lane);
   };
   en.run(addr, fr, done, a.T);
-  if (grid_last(a.grid_ctr, &flag)) ff_in_rows(a, red, reinterpret_cast<float*>(smem));
+  if (grid_last(a.grid_ctr, &flag)) ff_in_rows(a, red, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -903,7 +930,7 @@ __device__ __noinline__ void route_rows(const Ffn1Args& a, int* used) {
   for (int i = threadIdx.x; i < a.T * k; i += NTHR) a.slot[i] = used[a.ids[i]] - 1;
 }
 
-__global__ void __launch_bounds__(NTHR, 2) ffn1_kernel(const __grid_constant__ Ffn1Args a) {
+__global__ void __launch_bounds__(NTHR, 1) ffn1_kernel(const __grid_constant__ Ffn1Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int flag;
   __shared__ int used[256];
@@ -911,7 +938,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn1_kernel(const __grid_constant__ F
   const int gw = blockIdx.x * NW + warp;
   const bool is_r = gw < a.fr.w0 + a.fr.nw;
   const Fam& f = is_r ? a.fr : a.fg;
-  const int S = f.tiles * f.G;
+  const int S = f.tiles * f.us;
   const int lw = gw - f.w0;
   const int lo = range_lo(S, f.nw, lw), hi = range_lo(S, f.nw, lw + 1);
   uint8_t* ring = smem + warp * kRingSlot;
@@ -934,13 +961,13 @@ __global__ void __launch_bounds__(NTHR, 2) ffn1_kernel(const __grid_constant__ F
       if (DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, u)) store_block<1>(f.fin + (int64_t)u * a.T * 16, a.T, y, lane);
     };
     if (a.fr.bits == 16) {
-      Engine<16, 1, 1, 4> en;
+      Engine<16, 1, 1, 3> en;
       en.init(ring, lane, f, lo, hi);
       en.prime(addr);
       prologue();
       en.run(addr, fr_, done, a.T);
     } else {
-      Engine<4, 1, 4, 4> en;
+      Engine<4, 1, 2, 6> en;
       en.init(ring, lane, f, lo, hi);
       en.prime(addr);
       prologue();
@@ -951,7 +978,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn1_kernel(const __grid_constant__ F
     auto done = [&](int u, Acc<2> y, int pst, int pe) {
       if (DL_UNIT_DONE(2, f, S, a.T, lw, u, y, pst, pe, lane, u)) glu_store(y, a.T, u, a.act_d, a.Id, lane);
     };
-    Engine<4, 2, 4, 2> en;
+    Engine<4, 2, 2, 3> en;
     en.init(ring, lane, f, lo, hi);
     en.prime(addr);
     prologue();
@@ -975,7 +1002,7 @@ struct Ffn2Args {
   bf16* act_e;        // [slot][T][Ie]
 };
 
-__global__ void __launch_bounds__(NTHR, 2) ffn2_kernel(const __grid_constant__ Ffn2Args a) {
+__global__ void __launch_bounds__(NTHR, 1) ffn2_kernel(const __grid_constant__ Ffn2Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int32_t uq[kMaxUnique];
   __shared__ int nu_s;
@@ -994,7 +1021,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn2_kernel(const __grid_constant__ F
   };
   if (is_d) {
     const Fam& f = a.fd;
-    const int S = f.tiles * f.G, lw = gw - f.w0;
+    const int S = f.tiles * f.us, lw = gw - f.w0;
     auto addr = [&](int u) { return mat_unit<1>(f, u); };
     auto fr_ = [&](int) {
       return FragPtr{reinterpret_cast<const uint4*>(smem + f.frag_off),
@@ -1003,7 +1030,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn2_kernel(const __grid_constant__ F
     auto done = [&](int u, Acc<1> y, int pst, int pe) {
       if (DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, u)) store_block<1>(f.fin + (int64_t)u * a.T * 16, a.T, y, lane);
     };
-    Engine<4, 1, 4, 4> en;
+    Engine<4, 1, 1, 8> en;
     en.init(ring, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
     en.prime(addr);
     prologue();
@@ -1011,7 +1038,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn2_kernel(const __grid_constant__ F
   } else {
     prologue();
     const Fam& f = a.fx;
-    const int S = nu_s * f.tiles * f.G, lw = gw - f.w0;
+    const int S = nu_s * f.tiles * f.us, lw = gw - f.w0;
     auto addr = [&](int u) { return expert_unit<2>(f, a.ex, uq, u); };
     auto fr_ = [&](int) {
       return FragPtr{reinterpret_cast<const uint4*>(smem + f.frag_off),
@@ -1022,7 +1049,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn2_kernel(const __grid_constant__ F
       const int slot = u / f.tiles, j = u - slot * f.tiles;
       glu_store(y, a.T, j, a.act_e + (int64_t)slot * a.T * a.Ie, a.Ie, lane);
     };
-    Engine<4, 2, 4, 2> en;
+    Engine<4, 2, 2, 3> en;
     en.init(ring, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
     en.prime(addr);
     en.run(addr, fr_, done, a.T);
@@ -1109,20 +1136,42 @@ __device__ __noinline__ void combine_tile(const Ffn3Args& a, int j, int lane) {
 
 // x = bf16(bf16(h + bf16(rms(s) * w_post_ff)) * scalar),
 // s = bf16(bf16(rms(bf16(d)) * w1) + bf16(rms(moe) * w2))   (mod.rs:105-118)
-__device__ __noinline__ void ff_out_rows(const Ffn3Args& a, float* red, float* rows) {
+// Inputs staged in shared memory in one batch, as in ff_in_rows.
+__device__ __noinline__ void ff_out_rows(const Ffn3Args& a, float* red, uint8_t* rows) {
   const int H = a.H;
-  float* rd = rows;      // d, then s
-  float* rm = rows + H;  // moe
+  float* rd = reinterpret_cast<float*>(rows);  // d, then s
+  float* rm = rd + H;                          // moe
+  bf16* rh = reinterpret_cast<bf16*>(rm + H);  // h
+  bf16* wv = rh + H;                           // [3][H]: post_ff_norm_1, post_ff_norm_2, post_ff_norm
+  const bf16* srcw[3] = {a.w1, a.w2, a.w};
   const float sc = round_bf(a.scalar);
   for (int tk = 0; tk < a.T; ++tk) {
-    fin_row(a.fd, a.T, tk, H, rd);
+#pragma unroll
+    for (int k = 0; k < kMaxHidden / NTHR; ++k) {
+      const int i = threadIdx.x + k * NTHR;
+      if (i < H) {
+        const float d = fin_at(a.fd, a.T, tk, i);
+        const float m = __bfloat162float(__ldcg(a.moe + (int64_t)tk * H + i));
+        const bf16 h = __ldcg(a.h + (int64_t)tk * H + i);
+        bf16 w3[3];
+        if (tk == 0) {
+#pragma unroll
+          for (int q = 0; q < 3; ++q) w3[q] = srcw[q][i];
+        }
+        rd[i] = d;
+        rm[i] = m;
+        rh[i] = h;
+        if (tk == 0) {
+#pragma unroll
+          for (int q = 0; q < 3; ++q) wv[q * H + i] = w3[q];
+        }
+      }
+    }
     __syncthreads();
     float sd = 0.f, sm = 0.f;
     for (int i = threadIdx.x; i < H; i += NTHR) {
-      const float d = round_bf(rd[i]);
-      const float m = __bfloat162float(__ldcg(a.moe + (int64_t)tk * H + i));
+      const float d = round_bf(rd[i]), m = rm[i];
       rd[i] = d;
-      rm[i] = m;
       sd = fmaf(d, d, sd);
       sm = fmaf(m, m, sm);
     }
@@ -1130,21 +1179,20 @@ __device__ __noinline__ void ff_out_rows(const Ffn3Args& a, float* red, float* r
     const float rmn = rsqrtf(cta_sum(sm, red) / (float)H + a.eps);
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += NTHR) {
-      const float v = round_bf(round_bf(rd[i] * rdn * bf2f(a.w1[i])) + round_bf(rm[i] * rmn * bf2f(a.w2[i])));
+      const float v = round_bf(round_bf(rd[i] * rdn * bf2f(wv[i])) + round_bf(rm[i] * rmn * bf2f(wv[H + i])));
       rd[i] = v;
       ss = fmaf(v, v, ss);
     }
     const float rs = rsqrtf(cta_sum(ss, red) / (float)H + a.eps);
     for (int i = threadIdx.x; i < H; i += NTHR) {
-      const float hr = __bfloat162float(__ldcg(a.h + (int64_t)tk * H + i));
-      const float o = round_bf(hr + round_bf(rd[i] * rs * bf2f(a.w[i])));
+      const float o = round_bf(bf2f(rh[i]) + round_bf(rd[i] * rs * bf2f(wv[2 * H + i])));
       a.x_out[(int64_t)tk * H + i] = __float2bfloat16_rn(o * sc);
     }
     __syncthreads();
   }
 }
 
-__global__ void __launch_bounds__(NTHR, 2) ffn3_kernel(const __grid_constant__ Ffn3Args a) {
+__global__ void __launch_bounds__(NTHR, 1) ffn3_kernel(const __grid_constant__ Ffn3Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int32_t uq[kMaxUnique];
   __shared__ int nu_s;
@@ -1162,14 +1210,14 @@ __global__ void __launch_bounds__(NTHR, 2) ffn3_kernel(const __grid_constant__ F
   if (threadIdx.x < kMaxUnique) uq[threadIdx.x] = __ldcg(a.uniq + threadIdx.x);
   __syncthreads();
   const int nu = nu_s;
-  const int S = nu * f.tiles * f.G, lw = gw - f.w0;
+  const int S = nu * f.tiles * f.us, lw = gw - f.w0;
   const int lo = range_lo(S, f.nw, lw), hi = range_lo(S, f.nw, lw + 1);
   // expert slots this CTA's warps touch: their inputs' fragments
   const int cl = range_lo(S, f.nw, blockIdx.x * NW - f.w0), ch = range_lo(S, f.nw, blockIdx.x * NW + NW - f.w0);
-  const int per = f.tiles * f.G;
+  const int per = f.tiles * f.us;
   const int s_first = cl / per, s_last = ch > cl ? (ch - 1) / per : s_first;
   auto addr = [&](int u) { return expert_unit<1>(f, a.ex, uq, u); };
-  Engine<4, 1, 4, 4> en;
+  Engine<4, 1, 1, 8> en;
   en.init(smem + warp * kRingSlot, lane, f, lo, hi);
   en.prime(addr);
   griddep_wait();  // the activations come from ffn2
@@ -1196,7 +1244,7 @@ __global__ void __launch_bounds__(NTHR, 2) ffn3_kernel(const __grid_constant__ F
   en.run(addr, fr_, done, a.T);
   __syncwarp();
   for (int i = 0; i < npend && i < kMaxPend; ++i) combine_tile(a, pend[warp][i], lane);
-  if (grid_last(a.grid_ctr, &flag)) ff_out_rows(a, red, reinterpret_cast<float*>(smem));
+  if (grid_last(a.grid_ctr, &flag)) ff_out_rows(a, red, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -1252,8 +1300,8 @@ __device__ __noinline__ Best lm_unit_finished(const LmArgs& a, int u, const Acc<
   return b;
 }
 
-template <int BITS, int NGM, int D_>
-__global__ void __launch_bounds__(NTHR, 2) lm_kernel(const __grid_constant__ LmArgs a) {
+template <int BITS, int D_>
+__global__ void __launch_bounds__(NTHR, 1) lm_kernel(const __grid_constant__ LmArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float rms[kMaxT];
   __shared__ float wbv[NW][kMaxT];
@@ -1263,8 +1311,8 @@ __global__ void __launch_bounds__(NTHR, 2) lm_kernel(const __grid_constant__ LmA
   const int g = lane >> 2, t = lane & 3;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.G, lw = gw - f.w0;
-  Engine<BITS, 1, NGM, D_> en;
+  const int S = f.tiles * f.us, lw = gw - f.w0;
+  Engine<BITS, 1, 2, D_> en;
   en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
@@ -1281,7 +1329,7 @@ __global__ void __launch_bounds__(NTHR, 2) lm_kernel(const __grid_constant__ LmA
   // Ranges are at least one unit long (planned so): a unit is split over at
   // most two warps, its pieces and counter keyed by its first warp.
   auto done = [&](int u, Acc<1> y, int pst, int pe) {
-    if (!DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, warp_of(S, f.nw, u * f.G))) return;
+    if (!DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, warp_of(S, f.nw, u * f.us))) return;
     best = lm_unit_finished(a, u, y, best, lane);
   };
   en.run(addr, fr_, done, a.T);
@@ -1349,12 +1397,13 @@ static int h_maxp(long S_min, long nw, long G) {
 }
 static bool fits32(long S, long nw) { return S > 0 && (S + 1) * nw + S < (1l << 32); }
 
-static Fam mat_fam(int bits, int K, const QW* segs, int nseg, int w0, int nw) {
+static Fam mat_fam(int bits, int K, const QW* segs, int nseg, int w0, int nw, int ng) {
   Fam f = {};
   f.bits = bits;
   f.nt = 1;
   f.K = K;
   f.G = K / 64;
+  f.us = f.G / ng;
   f.w0 = w0;
   f.nw = nw;
   f.src = SRC_MAT;
@@ -1372,19 +1421,20 @@ static Fam mat_fam(int bits, int K, const QW* segs, int nseg, int w0, int nw) {
   f.tiles = t0;
   return f;
 }
-static Fam glu_fam(const QW& gate, const QW& up, int w0, int nw) {
+static Fam glu_fam(const QW& gate, const QW& up, int w0, int nw, int ng) {
   const QW s[2] = {gate, up};
-  Fam f = mat_fam(gate.bits, gate.in, s, 2, w0, nw);
+  Fam f = mat_fam(gate.bits, gate.in, s, 2, w0, nw, ng);
   f.nt = 2;
   f.tiles = gate.out / 16;
   return f;
 }
-static Fam expert_fam(int mat, int nt, int K, int rows, int w0, int nw) {
+static Fam expert_fam(int mat, int nt, int K, int rows, int w0, int nw, int ng) {
   Fam f = {};
   f.bits = 4;
   f.nt = nt;
   f.K = K;
   f.G = K / 64;
+  f.us = f.G / ng;
   f.w0 = w0;
   f.nw = nw;
   f.src = SRC_EXPERT;
@@ -1450,10 +1500,10 @@ static int launch(F kern, const A& args, size_t smem, cudaStream_t st, const cha
   return check_launch(name);
 }
 
-// Stage shape per code width: <BITS, groups per step, ring depth>.
-#define DL_DISPATCH(bits, KERNEL, ...)                                                     \
-  ((bits) == 8 ? launch(KERNEL<8, 2, 4>, __VA_ARGS__)                                      \
-               : (bits) == 6 ? launch(KERNEL<6, 4, 2>, __VA_ARGS__) : launch(KERNEL<4, 4, 4>, __VA_ARGS__))
+// Ring depth per code width (two groups per step): <BITS, steps in flight>.
+#define DL_DISPATCH(bits, KERNEL, ...)                                                 \
+  ((bits) == 8 ? launch(KERNEL<8, 3>, __VA_ARGS__)                                     \
+               : (bits) == 6 ? launch(KERNEL<6, 4>, __VA_ARGS__) : launch(KERNEL<4, 6>, __VA_ARGS__))
 
 }  // namespace dl
 
@@ -1508,26 +1558,29 @@ int dl_plan(const fmoe_decoder_layer_t* L, const KvDev& kv, int64_t T, DlPlan* p
   d.rbits = rq.bits;
   d.qkv_tiles = (Hq + (L->k_eq_v ? 1 : 2) * Hkv) * D / 16;
   const long Gh = H / 64, Gq = d.QD / 64, Gi = d.Id / 64, Ge = d.Ie / 64;
-  const long S_qkv = (long)d.qkv_tiles * Gh, S_o = (long)(H / 16) * Gq;
-  const long S_r = (long)(d.E / 16) * Gh, S_g = (long)(d.Id / 16) * Gh, S_d = (long)(H / 16) * Gi;
-  const long S_x = (long)d.k * (d.Ie / 16) * Gh, S_y = (long)d.k * (H / 16) * Ge;  // fewest slots: k
+  // groups per ring step of each family (see the kernels' Engine instances)
+  if (Gh % 2 || Gq % 2) return FMOE_ERR_UNSUPPORTED;
+  const long Uh = Gh / 2, Uq = Gq / 2, Ur = d.rbits == 16 ? Gh : Gh / 2, Ui = Gi, Ue = Ge;
+  const long S_qkv = (long)d.qkv_tiles * Uh, S_o = (long)(H / 16) * Uq;
+  const long S_r = (long)(d.E / 16) * Ur, S_g = (long)(d.Id / 16) * Uh, S_d = (long)(H / 16) * Ui;
+  const long S_x = (long)d.k * (d.Ie / 16) * Uh, S_y = (long)d.k * (H / 16) * Ue;  // fewest slots: k
   const double b_r = (double)d.E * H * (d.rbits == 16 ? 2.0 : 0.5625);
   const double b_g = 2.0 * d.Id * H * 0.5625, b_d = (double)H * d.Id * 0.5625;
   const double b_x = (double)d.Umax * 2.0 * d.Ie * H * 0.5625;
   split_warps(b_r, b_g, S_r, S_g, &d.nw_r, &d.nw_g);
   split_warps(b_d, b_x, S_d, S_x, &d.nw_d, &d.nw_x);
   if (S_qkv < kWarps || S_o < kWarps || S_y < kWarps) return FMOE_ERR_UNSUPPORTED;
-  const long S_xmax = (long)d.Umax * (d.Ie / 16) * Gh, S_ymax = (long)d.Umax * (H / 16) * Ge;
+  const long S_xmax = (long)d.Umax * (d.Ie / 16) * Uh, S_ymax = (long)d.Umax * (H / 16) * Ue;
   if (!fits32(S_qkv, kWarps) || !fits32(S_o, kWarps) || !fits32(S_xmax, d.nw_x) || !fits32(S_ymax, kWarps) ||
       !fits32(S_r, d.nw_r) || !fits32(S_g, d.nw_g) || !fits32(S_d, d.nw_d))
     return FMOE_ERR_UNSUPPORTED;
-  d.mp_qkv = h_maxp(S_qkv, kWarps, Gh);
-  d.mp_o = h_maxp(S_o, kWarps, Gq);
-  d.mp_r = h_maxp(S_r, d.nw_r, Gh);
-  d.mp_g = h_maxp(S_g, d.nw_g, Gh);
-  d.mp_d = h_maxp(S_d, d.nw_d, Gi);
-  d.mp_x = h_maxp(S_x, d.nw_x, Gh);
-  d.mp_y = h_maxp(S_y, kWarps, Ge);
+  d.mp_qkv = h_maxp(S_qkv, kWarps, Uh);
+  d.mp_o = h_maxp(S_o, kWarps, Uq);
+  d.mp_r = h_maxp(S_r, d.nw_r, Ur);
+  d.mp_g = h_maxp(S_g, d.nw_g, Uh);
+  d.mp_d = h_maxp(S_d, d.nw_d, Ui);
+  d.mp_x = h_maxp(S_x, d.nw_x, Uh);
+  d.mp_y = h_maxp(S_y, kWarps, Ue);
   if (std::min({d.mp_qkv, d.mp_o, d.mp_r, d.mp_g, d.mp_d, d.mp_x, d.mp_y}) < 0) return FMOE_ERR_UNSUPPORTED;
   const size_t fT = 128 * (size_t)T;
   d.sm_qkv = kRingBytes + Gh * fT + Gh * 32;
@@ -1598,7 +1651,7 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   {
     QkvArgs a = {};
     const QW segs[3] = {q, k, v};
-    a.f = mat_fam(p.qbits, H, segs, L->k_eq_v ? 2 : 3, 0, kWarps);
+    a.f = mat_fam(p.qbits, H, segs, L->k_eq_v ? 2 : 3, 0, kWarps, 2);
     a.f.piece = w.p_qkv;
     a.f.maxp = p.mp_qkv;
     a.f.uctr = w.uc_qkv;
@@ -1637,7 +1690,7 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   // 3 o + feed-forward input norms
   {
     OArgs a = {};
-    a.f = mat_fam(p.obits, p.QD, &o, 1, 0, kWarps);
+    a.f = mat_fam(p.obits, p.QD, &o, 1, 0, kWarps, 2);
     a.f.piece = w.p_o;
     a.f.maxp = p.mp_o;
     a.f.uctr = w.uc_o;
@@ -1665,14 +1718,14 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   // 4 router + dense gate|up
   {
     Ffn1Args a = {};
-    a.fr = mat_fam(p.rbits, H, &rq, 1, 0, p.nw_r);
+    a.fr = mat_fam(p.rbits, H, &rq, 1, 0, p.nw_r, p.rbits == 16 ? 1 : 2);
     a.fr.piece = w.p_r;
     a.fr.maxp = p.mp_r;
     a.fr.uctr = w.uc_r;
     a.fr.fin = w.f_r;
     a.fr.frag_off = kRingBytes;
     a.fr.xsum_off = kRingBytes + a.fr.G * fT;
-    a.fg = glu_fam(gq, uq, p.nw_r, p.nw_g);
+    a.fg = glu_fam(gq, uq, p.nw_r, p.nw_g, 2);
     a.fg.piece = w.p_g;
     a.fg.maxp = p.mp_g;
     a.fg.uctr = w.uc_g;
@@ -1700,14 +1753,14 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   Fam fd;
   {
     Ffn2Args a = {};
-    a.fd = mat_fam(4, p.Id, &dq, 1, 0, p.nw_d);
+    a.fd = mat_fam(4, p.Id, &dq, 1, 0, p.nw_d, 1);
     a.fd.piece = w.p_d;
     a.fd.maxp = p.mp_d;
     a.fd.uctr = w.uc_d;
     a.fd.fin = w.f_d;
     a.fd.frag_off = kRingBytes;
     a.fd.xsum_off = kRingBytes + a.fd.G * fT;
-    a.fx = expert_fam(0, 2, H, p.Ie, p.nw_d, p.nw_x);
+    a.fx = expert_fam(0, 2, H, p.Ie, p.nw_d, p.nw_x, 2);
     a.fx.piece = w.p_x;
     a.fx.maxp = p.mp_x;
     a.fx.uctr = w.uc_x;
@@ -1729,7 +1782,7 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   // 6 experts' down + combine + output norms
   {
     Ffn3Args a = {};
-    a.fy = expert_fam(6, 1, p.Ie, H, 0, kWarps);
+    a.fy = expert_fam(6, 1, p.Ie, H, 0, kWarps, 1);
     a.fy.piece = w.p_y;
     a.fy.maxp = p.mp_y;
     a.fy.uctr = w.uc_y;
@@ -1775,7 +1828,7 @@ size_t dl_lm_workspace_bytes(int64_t T) {
 int dl_lm_head(const QW& e, const bf16* norm, float eps, const bf16* x, int64_t T, float cap, float* logits,
                int32_t* next_ids, int64_t* pos_dev, void* ws, cudaStream_t st) {
   const int H = e.in;
-  if (e.out % 16 || H % 64 || H > kMaxHidden || (e.bits != 4 && e.bits != 6 && e.bits != 8))
+  if (e.out % 16 || H % 128 || H > kMaxHidden || (e.bits != 4 && e.bits != 6 && e.bits != 8))
     return set_error(FMOE_ERR_UNSUPPORTED, "lm_head: %d-bit [%d, %d] (4/6/8-bit, rows a multiple of 16)", e.bits,
                      e.out, H);
   uint8_t* base = static_cast<uint8_t*>(ws);
@@ -1785,14 +1838,14 @@ int dl_lm_head(const QW& e, const bf16* norm, float eps, const bf16* x, int64_t 
   LmArgs a = {};
   // at most one warp per unit, so a unit spans at most two warps
   const int nw = (int)std::min<int64_t>(kWarps, e.out / 16);
-  a.f = mat_fam(e.bits, H, &e, 1, 0, nw);
+  a.f = mat_fam(e.bits, H, &e, 1, 0, nw, 2);
   a.f.piece = piece;
   a.f.maxp = 2;
   a.f.uctr = ctr + 1;
   a.f.frag_off = kRingBytes;
   const int G = H / 64;
   a.f.xsum_off = kRingBytes + G * 128 * (int)T;
-  if (!fits32((long)a.f.tiles * G, nw)) return set_error(FMOE_ERR_UNSUPPORTED, "lm_head: vocabulary too large");
+  if (!fits32((long)a.f.tiles * a.f.us, nw)) return set_error(FMOE_ERR_UNSUPPORTED, "lm_head: vocabulary too large");
   a.x = x;
   a.norm = norm;
   a.eps = eps;

@@ -1,19 +1,21 @@
 // Streaming GEMV core for decode (T <= 8 tokens).  Every warp streams its own
-// weight tiles from HBM into a private shared-memory ring with 16-byte
-// cp.async copies (no producer warp, no mbarriers) and multiplies them on the
-// warp-level tensor cores (mma.sync m16n8k16, fp32 accumulate) against input
-// fragments the CTA prepared once in shared memory.
+// weight tiles from HBM into a private shared-memory ring with cp.async and
+// multiplies them on the warp-level tensor cores (mma.sync m16n8k16, fp32
+// accumulate) against input fragments the CTA prepared once in shared memory.
 //
-// A step = one 16-row tile (two for a gate|up pair) x up to NGM consecutive
-// 64-wide groups of K.  The copy side reads each row's segment of the step as
-// contiguous 16-byte chunks, 32 lanes covering whole 128-byte lines; the math
-// side reads the same bytes back in the MMA fragment layout (lane = 4g + t
-// holds 16 codes of rows g and g+8 per group), so rows are XOR-swizzled in
-// 16-byte chunks to keep those reads free of bank conflicts.  The ring holds D
-// steps: the bytes in flight sit in shared memory, not registers, so a CTA
-// keeps tens of KB outstanding against HBM with few registers — leaving room
-// on the SM for the next kernel of a programmatic-dependent chain to become
-// resident and start its own stream before this one ends.
+// A step = NG consecutive 64-wide groups of K of one 16-row tile (two tiles
+// for a gate|up pair); the groups' MMA chains are independent (and each
+// group's four MMAs run as two chains), so a warp keeps several in flight.  Each lane copies exactly the bytes it later feeds to the MMA — lane
+// 4g + t holds 16 codes of rows g and g+8, columns 16t .. 16t+15 of the group
+// in a lane-specific k order — so a warp instruction reads 8 rows x 64 bytes
+// (as fast as contiguous streaming once every warp of the GPU has work: the
+// work is split over warps by groups, see dlayer.cu) and a lane reads back
+// only its own copies: no swizzle, no cross-lane barrier.  6-bit rows are the
+// exception: a quad's 48-byte group row arrives as three 16-byte copies of
+// lanes t = 0..2 and is read back after a __syncwarp (48-byte row slots put
+// the 12-byte lane reads of 8 rows on 32 distinct banks).  The bytes in
+// flight sit in shared memory, not registers; only one scale or bias word per
+// tile and step waits in a register.
 //
 // Per-width operand recipes (the B fragments use the same k order):
 //   4-bit  bf16 MMA, A = bf16(128 + q) from one LOP3 per code pair
@@ -32,6 +34,9 @@ namespace sg {
 __device__ __forceinline__ void cpa16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cpa8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global.L2::128B [%0], [%1], 8;\n" ::"r"(dst), "l"(src) : "memory");
+}
 __device__ __forceinline__ void commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void wait_group() {
@@ -40,71 +45,92 @@ __device__ __forceinline__ void wait_group() {
 __device__ __forceinline__ uint32_t s_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
 __device__ __forceinline__ uint32_t ldg_h(const bf16* p) {
   unsigned short r;
-  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
+  asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
   return r;
 }
 
-// Geometry of one width's stage: GB bytes per group and row, NGM groups per
-// step, RB bytes per staged row (6-bit: padded to 52 words so the 12-byte lane
-// reads of 8 rows hit 32 distinct banks), CPG chunks per group.
-template <int BITS, int NGM>
+// Stage layout of one width: LB bytes per lane and row half (6-bit: a 48-byte
+// slot per row, shared by the quad), GB bytes of one group in a row.
+template <int BITS>
 struct Geo {
   static constexpr int GB = 64 * BITS / 8;
-  static constexpr int CPG = GB / 16;
-  static constexpr int RB = NGM * GB + (BITS == 6 ? 16 : 0);
+  static constexpr int LB = BITS == 4 ? 8 : BITS == 16 ? 32 : 16;
+  static constexpr int HALF = BITS == 6 ? 8 * 48 : 32 * LB;  // bytes of one row half (8 rows)
   static constexpr float OFF = (BITS == 4 || BITS == 16) ? 128.0f : 1024.0f;
-  static_assert(BITS != 4 || NGM % 4 == 0, "4-bit rows: whole 128-byte lines per step");
-  static_assert(BITS != 8 || NGM % 2 == 0, "8-bit rows: whole 128-byte lines per step");
-  static_assert(BITS != 6 || NGM == 4, "6-bit stage padding assumes 4 groups per step");
-  static_assert(BITS != 16 || NGM == 1, "16-bit: one group (128 bytes) per step");
 };
-
-// Physical 16-byte chunk of logical chunk c in staged row r.
-template <int BITS>
-__device__ __forceinline__ int swz(int r, int c) {
-  if constexpr (BITS == 8) return c ^ ((r & 1) << 2);
-  else if constexpr (BITS == 4) return c ^ ((r & 3) << 1);
-  else if constexpr (BITS == 16) return c ^ (r & 1);
-  else return c;
+template <int BITS, int NT>
+constexpr int stage_bytes() {
+  return 2 * NT * Geo<BITS>::HALF;
 }
 
-// Byte offset (in the stage) of the lane's data for group gi of staged row r.
-template <int BITS, int NGM>
-__device__ __forceinline__ int lane_off(int r, int gi, int t) {
-  using Gm = Geo<BITS, NGM>;
-  if constexpr (BITS == 8) return r * Gm::RB + swz<8>(r, gi * 4 + t) * 16;
-  else if constexpr (BITS == 4) return r * Gm::RB + swz<4>(r, gi * 2 + (t >> 1)) * 16 + (t & 1) * 8;
-  else if constexpr (BITS == 6) return r * Gm::RB + gi * 48 + 12 * t;
-  else return r * Gm::RB;  // 16-bit: two chunks, see mma_group
-}
-
-// C[4] += (off + q) . x for one group of a 16-row tile; lo / hi = stage
-// offsets of rows g and g+8 (row index rl / rh for the 16-bit swizzle).
-template <int BITS, int NGM>
-__device__ __forceinline__ void mma_group(float (&c)[4], const uint8_t* st, int rl, int rh, int gi, int t,
-                                          const uint32_t (&b)[8]) {
-  if constexpr (BITS == 4) {
-    const uint2 l = *reinterpret_cast<const uint2*>(st + lane_off<4, NGM>(rl, gi, t));
-    const uint2 h = *reinterpret_cast<const uint2*>(st + lane_off<4, NGM>(rh, gi, t));
+// Issue this lane's copies of one step.  src[h] = row (g + 8h) of tile h/2 at
+// the step's group, lane offset not yet applied.
+template <int BITS, int NT>
+__device__ __forceinline__ void issue_step(uint32_t st, const uint8_t* const (&src)[2 * NT], int lane, int t) {
+  using Gm = Geo<BITS>;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
+  for (int h = 0; h < 2 * NT; ++h) {
+    const uint32_t d = st + h * Gm::HALF;
+    if constexpr (BITS == 4) {
+      cpa8(d + lane * 8, src[h] + 8 * t);
+    } else if constexpr (BITS == 8) {
+      cpa16(d + lane * 16, src[h] + 16 * t);
+    } else if constexpr (BITS == 16) {
+      cpa16(d + lane * 32, src[h] + 32 * t);
+      cpa16(d + lane * 32 + 16, src[h] + 32 * t + 16);
+    } else {
+      if (t < 3) cpa16(d + (lane >> 2) * 48 + 16 * t, src[h] + 16 * t);
+    }
+  }
+}
+
+// C[4] += (off + q) . x for one group of tile i of the stage.
+template <int BITS>
+__device__ __forceinline__ void mma_group(float (&c)[4], const uint8_t* st, int i, int lane, int t,
+                                          const uint32_t (&b)[8]) {
+  using Gm = Geo<BITS>;
+  const uint8_t* lo = st + (2 * i) * Gm::HALF;
+  const uint8_t* hi = lo + Gm::HALF;
+  if constexpr (BITS == 4) {
+    const uint2 l = *reinterpret_cast<const uint2*>(lo + lane * 8);
+    const uint2 h = *reinterpret_cast<const uint2*>(hi + lane * 8);
+    float c2[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < 4; s += 2) {
       mma16816(c, nib_pair(l.x, 4 * s), nib_pair(h.x, 4 * s), nib_pair(l.y, 4 * s), nib_pair(h.y, 4 * s), b[s],
                b[4 + s]);
+      mma16816(c2, nib_pair(l.x, 4 * s + 4), nib_pair(h.x, 4 * s + 4), nib_pair(l.y, 4 * s + 4),
+               nib_pair(h.y, 4 * s + 4), b[s + 1], b[5 + s]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] += c2[e];
   } else if constexpr (BITS == 16) {
-    constexpr int RB = Geo<16, NGM>::RB;
-    const uint4 l0 = *reinterpret_cast<const uint4*>(st + rl * RB + swz<16>(rl, 2 * t) * 16);
-    const uint4 l1 = *reinterpret_cast<const uint4*>(st + rl * RB + swz<16>(rl, 2 * t + 1) * 16);
-    const uint4 h0 = *reinterpret_cast<const uint4*>(st + rh * RB + swz<16>(rh, 2 * t) * 16);
-    const uint4 h1 = *reinterpret_cast<const uint4*>(st + rh * RB + swz<16>(rh, 2 * t + 1) * 16);
+    const uint4 l0 = *reinterpret_cast<const uint4*>(lo + lane * 32), l1 = *reinterpret_cast<const uint4*>(lo + lane * 32 + 16);
+    const uint4 h0 = *reinterpret_cast<const uint4*>(hi + lane * 32), h1 = *reinterpret_cast<const uint4*>(hi + lane * 32 + 16);
     const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
     const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    float c2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) mma16816(c, lw[j], hw[j], lw[j + 4], hw[j + 4], b[j], b[j + 4]);
+    for (int j = 0; j < 4; j += 2) {
+      mma16816(c, lw[j], hw[j], lw[j + 4], hw[j + 4], b[j], b[j + 4]);
+      mma16816(c2, lw[j + 1], hw[j + 1], lw[j + 5], hw[j + 5], b[j + 1], b[j + 5]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] += c2[e];
   } else {
     uint32_t a[4][4];
-    load_a_frags<BITS>(st + lane_off<BITS, NGM>(rl, gi, t), st + lane_off<BITS, NGM>(rh, gi, t), a);
+    if constexpr (BITS == 8)
+      load_a_frags<8>(lo + lane * 16, hi + lane * 16, a);
+    else
+      load_a_frags<6>(lo + (lane >> 2) * 48 + 12 * t, hi + (lane >> 2) * 48 + 12 * t, a);
+    float c2[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) mma16816_f16(c, a[j][0], a[j][1], a[j][2], a[j][3], b[j], b[4 + j]);
+    for (int j = 0; j < 4; j += 2) {
+      mma16816_f16(c, a[j][0], a[j][1], a[j][2], a[j][3], b[j], b[4 + j]);
+      mma16816_f16(c2, a[j + 1][0], a[j + 1][1], a[j + 1][2], a[j + 1][3], b[j + 1], b[5 + j]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) c[e] += c2[e];
   }
 }
 
@@ -136,7 +162,7 @@ __device__ __forceinline__ float operand_round(float v) {
 template <int BITS>
 __device__ __forceinline__ void fixup(float (&y)[4], const float (&c)[4], float x0, float x1, uint32_t sl,
                                       uint32_t bl, uint32_t sh, uint32_t bh) {
-  constexpr float off = Geo<BITS, BITS == 4 ? 4 : BITS == 6 ? 4 : BITS == 8 ? 2 : 1>::OFF;
+  constexpr float off = Geo<BITS>::OFF;
   const float s_lo = __uint_as_float(sl << 16), s_hi = __uint_as_float(sh << 16);
   const float b_lo = fmaf(-off, s_lo, __uint_as_float(bl << 16)), b_hi = fmaf(-off, s_hi, __uint_as_float(bh << 16));
   y[0] = fmaf(s_lo, c[0], fmaf(b_lo, x0, y[0]));
