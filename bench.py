@@ -46,6 +46,8 @@ DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert
 WORKLOADS = {"decode30_b1": 1, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
 # total tokens per step (split evenly over the GPUs), default exchange mode
 EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "fixed"), "ep_moe30_prefill_8192": (8192, "exact")}
+# config 5 measured inside a multi-GPU decode30 run (workload, exchange mode)
+EP_EXTRA = [("ep_moe30_decode_b256", "fixed"), ("ep_moe30_decode_b256", "p2p"), ("ep_moe30_prefill_8192", "exact")]
 CTX = 2048                                                 # decode context (positions in every KV cache)
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES                  # 3,345,408
 
@@ -69,6 +71,8 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one eager step between cudaProfilerStart / Stop and exit (for "
                          "ncu --profile-from-start off launch lists of the decode30 / ep_* workloads)")
+    ap.add_argument("--no-ep-extra", action="store_true",
+                    help="decode30 at N > 1: skip the expert-parallel config-5 sub-measurements")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
     ap.add_argument("--qlinear-case", default=None, metavar="OUT:IN:BITS:T",
                     help="run only fmoe_qlinear on one shape: four launches, L2 flushed before each, the last one "
@@ -241,6 +245,68 @@ def decoder_step_bytes(m, T, ctx):
     return sum(per.values()), per
 
 
+DECODER_METRIC = "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)"
+MOE_METRIC = "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)"
+
+
+def decoder_config(args, world):
+    """The decode30 workload's `config` (both arms print this dict)."""
+    T = WORKLOADS[args.workload]
+    par = "single GPU" if world == 1 else (
+        f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined "
+        + ("by stores into the peers' exchange windows (CUDA IPC, flag-synchronised)" if args.ep_mode == "p2p"
+           else "by NCCL send/recv")
+        + " over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
+        f"replicated; one sequence per GPU")
+    return {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
+            "batch": T, "context": CTX, "kv_cache": "bf16", "attention_bits": 8, "expert_bits": 4,
+            "dense_bits": 4, "embed_bits": 6, "router": "bf16",
+            "parallelism": par,
+            "l2": "weights (about 15 GB) far larger than L2; no flush",
+            "graph": "one CUDA graph per step, position on the device",
+            "next_token": ("sampled (fmoe_sample on the device; the oracle's sampler on the CPU): temperature "
+                           "0.7, top_p 0.9, repetition penalty 1.15 over the last 64 tokens" if args.sample
+                           else "greedy argmax (fused in the lm_head)")}
+
+
+def moe_config(args, world):
+    """The moe30_decode_* workloads' `config`."""
+    return {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
+            "expert_intermediate": I, "tokens_per_step": WORKLOADS[args.workload], "router": "bf16",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (30 x 428 MB of experts resident)",
+            "graph": "one CUDA graph per step"}
+
+
+def ep_mode_name(args):
+    return args.ep_mode or EP_WORKLOADS[args.workload][1]
+
+
+def ep_metric(args):
+    total = EP_WORKLOADS[args.workload][0]
+    return (("prefill tok/s" if "prefill" in args.workload else "decode tok/s") +
+            f" (MoE half of the 30-layer Gemma-4 26B-A4B-shaped model, {total} tokens per step, experts "
+            f"split over the GPUs)")
+
+
+def ep_config(args, world):
+    """The ep_moe30_* workloads' `config` (config 5: experts split over the GPUs)."""
+    total = EP_WORKLOADS[args.workload][0]
+    mode_name = ep_mode_name(args)
+    T = total // world
+    row_b = H * 2 + K * 8
+    return {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
+            "expert_intermediate": I, "tokens_per_step": total, "tokens_per_gpu": T,
+            "parallelism": f"expert-parallel x{world}: {E // world} experts per GPU, "
+                           + ("peer-memory stores (CUDA IPC windows)" if mode_name == "p2p"
+                              else "NCCL grouped send/recv")
+                           + f" dispatch + combine ({mode_name} exchange); router replicated, tokens split",
+            "exchange_bytes_per_layer_per_gpu": (world * T * row_b * 2) if mode_name in ("fixed", "p2p") else None,
+            "graph": "one CUDA graph per step" if mode_name in ("fixed", "p2p")
+                     else "eager (exact mode syncs per layer)",
+            "l2": "inputs larger than L2 (expert slices resident)"}
+
+
 def run_decoder(args, rank, world, local):
     import torch
     import __graft_entry__
@@ -364,14 +430,8 @@ def run_decoder(args, rank, world, local):
                  "moe_gate_up_kernel": parts["experts"] * 2 / 3, "moe_down_kernel": parts["experts"] / 3}
     alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
-    par = "single GPU" if world == 1 else (
-        f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined "
-        + ("by stores into the peers' exchange windows (CUDA IPC, flag-synchronised)" if args.ep_mode == "p2p"
-           else "by NCCL send/recv")
-        + " over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
-        f"replicated; one sequence per GPU")
     result = {
-        "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
+        "metric": DECODER_METRIC,
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": world,
@@ -384,14 +444,7 @@ def run_decoder(args, rank, world, local):
         "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32 accumulate",
         "data": "synthetic (random-init weights MLX-affine quantised; random token ids; 2048 random bf16 K/V "
                 "positions per cache)",
-        "config": {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
-                   "batch": T, "context": CTX, "kv_cache": "bf16", "attention_bits": 8, "expert_bits": 4,
-                   "dense_bits": 4, "embed_bits": 6, "router": "bf16",
-                   "parallelism": par,
-                   "l2": "weights (about 15 GB) far larger than L2; no flush",
-                   "graph": "one CUDA graph per step, position on the device",
-                   "next_token": ("fmoe_sample on the device: temperature 0.7, top_p 0.9, repetition penalty 1.15 "
-                                  "over the last 64 tokens" if args.sample else "greedy argmax (fused in the lm_head)")},
+        "config": decoder_config(args, world),
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * 4,
                 "d2h_bytes_per_step": T * 4,
                 "api": "Gemma4Model.decode_step (embedding, fmoe_decoder_layer_forward%s x30, fmoe_lm_head) "
@@ -418,8 +471,24 @@ def run_decoder(args, rank, world, local):
     torch.cuda.synchronize()
     if ep is not None:
         ep.close()
+    if rank == 0 and world == 1 and not args.no_attn:
+        # BASELINE configs 3 and 2 on the same box, as extra keys of the headline line
+        result["kv_attention"] = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"])
+        result["moe_prefill"] = prefill_submeasure(fm, torch, dev, peaks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_decoder_baseline(T, sampled=args.sample)
+    if world > 1 and not args.no_ep_extra:
+        # BASELINE config 5 (experts split over the GPUs) on the same ranks, as extra keys
+        torch.cuda.empty_cache()
+        result["ep_config5"] = {}
+        for wl, mode in EP_EXTRA:
+            sub = argparse.Namespace(**{**vars(args), "workload": wl, "ep_mode": mode, "steps": 10, "warmup": 3,
+                                        "no_cpu_baseline": True, "profile_step": False})
+            r = ep_measure(sub, rank, world, local, own_pg=False)
+            if rank == 0:
+                result["ep_config5"][f"{wl}:{mode}"] = {k: r[k] for k in ("metric", "value", "unit", "ms_per_step",
+                                                                           "steps", "warmup", "scaling", "e2e",
+                                                                           "roofline", "config")}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -535,7 +604,7 @@ def run_ours(args, rank, world, local):
         pass
     step_bytes = avg_u * (GATE_UP_BYTES + DOWN_BYTES) + nl * ROUTER_BYTES
     result = {
-        "metric": "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)",
+        "metric": MOE_METRIC,
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": world,
@@ -547,11 +616,7 @@ def run_ours(args, rank, world, local):
         "vs_baseline": None,
         "dtype": "u4-affine weights x bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights MLX-affine 4-bit quantised; random init)",
-        "config": {"workload": args.workload, "layers": nl, "hidden": H, "experts": E, "top_k": K,
-                   "expert_intermediate": I, "tokens_per_step": T, "router": "bf16",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                   "l2": "inputs larger than L2 (30 x 428 MB of experts resident)",
-                   "graph": "one CUDA graph per step"},
+        "config": moe_config(args, world),
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2,
                 "api": "fmoe_moe_block_forward x30 (captured in a CUDA graph) + pinned host copies"},
@@ -588,6 +653,14 @@ def run_ours(args, rank, world, local):
 
 
 def run_ep_moe(args, rank, world, local):
+    result = ep_measure(args, rank, world, local, own_pg=True)
+    if rank == 0 and result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def ep_measure(args, rank, world, local, own_pg):
+    """One expert-parallel workload on every rank; rank 0 gets the result dict.
+    own_pg: create / destroy the process group here (False: the caller's)."""
     import datetime
 
     import torch
@@ -604,7 +677,7 @@ def run_ep_moe(args, rank, world, local):
     if total % world or E % world:
         raise SystemExit(f"{total} tokens / {E} experts do not split over {world} GPUs")
     T = total // world
-    if world > 1:
+    if world > 1 and own_pg:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     comm = fm.EPComm()
     nl = args.layers
@@ -642,9 +715,9 @@ def run_ep_moe(args, rank, world, local):
             torch.cuda.synchronize()
             profiled_step(torch, step)
         comm.close()
-        if world > 1:
+        if world > 1 and own_pg:
             dist.destroy_process_group()
-        return
+        return None
     with torch.cuda.stream(stream):
         step(keep_ids=True)
         torch.cuda.synchronize()
@@ -732,25 +805,14 @@ def run_ep_moe(args, rank, world, local):
                 "alg_bytes_per_launch": int(alg) if alg else None}
     roof.update({"kernel": name, "avg_launch_us": round(avg_s * 1e6, 3), "traffic": None,
                  "peak_source": f"{peaks_kind} (MEASURED_PEAKS.json)" if peaks_kind == "measured" else "fallback"})
-    row_b = H * 2 + K * 8
     result = {
-        "metric": ("prefill tok/s" if prefill else "decode tok/s") +
-                  f" (MoE half of the 30-layer Gemma-4 26B-A4B-shaped model, {total} tokens per step, experts "
-                  f"split over the GPUs)",
+        "metric": ep_metric(args),
         "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "u4-affine weights x bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded N(0,1) activations; N(0,0.02) weights MLX-affine 4-bit; router logit bias N(0,1) "
                 "per expert)",
-        "config": {"workload": args.workload, "layers": nl, "hidden": H, "experts": E, "top_k": K,
-                   "expert_intermediate": I, "tokens_per_step": total, "tokens_per_gpu": T,
-                   "parallelism": f"expert-parallel x{world}: {per} experts per GPU, "
-                                  + ("peer-memory stores (CUDA IPC windows)" if mode_name == "p2p"
-                                     else "NCCL grouped send/recv")
-                                  + f" dispatch + combine ({mode_name} exchange); router replicated, tokens split",
-                   "exchange_bytes_per_layer_per_gpu": (world * T * row_b * 2) if mode_name in ("fixed", "p2p") else None,
-                   "graph": "one CUDA graph per step" if graph is not None else "eager (exact mode syncs per layer)",
-                   "l2": "inputs larger than L2 (expert slices resident)"},
+        "config": ep_config(args, world),
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * H * 2,
                 "d2h_bytes_per_step": T * H * 2,
                 "api": "ExpertParallelMoeBlock.forward x30 (fmoe_ep_moe_forward) + pinned host copies"},
@@ -765,12 +827,12 @@ def run_ep_moe(args, rank, world, local):
     torch.cuda.synchronize()
     comm.close()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(None, min(T, 256))
-        result["cpu_baseline"]["sample"] += " (tok/s is per token, so a 256-token sample stands for the step)"
-    if rank == 0:
-        print(json.dumps(result), flush=True)
-    if world > 1:
+        result["cpu_baseline"] = cpu_baseline(None, EP_WORKLOADS[args.workload][0])
+    del blocks, ys, shared
+    torch.cuda.empty_cache()
+    if world > 1 and own_pg:
         dist.destroy_process_group()
+    return result if rank == 0 else None
 
 
 # ---------------------------------------------------------------------------
@@ -862,25 +924,62 @@ def ecb(hidden, inter):
     return offs, sizes, sum(sizes)
 
 
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def oracle_all_cores():
+    """The oracle on every host core this process may use, whatever
+    OMP_NUM_THREADS says (torchrun sets it to 1)."""
+    import oracle
+    oracle.set_num_threads(host_cores())
+    return oracle.num_threads()
+
+
 def cpu_layer(x, wr, buf, offs, stride):
     import oracle
     ids, w, _ = oracle.router(x, wr, K)
     oracle.moe_experts(x, ids, w, buf, stride, offs, H, I)
 
 
-def cpu_baseline(_layers, T, budget_s=10.0):
-    import oracle
-    x, wr, buf, offs, stride = cpu_sample_setup(T)
-    cpu_layer(x, wr, buf, offs, stride)
+def cpu_moe_step(sample, n_layers=LAYERS):
+    """One whole step of the routed-expert workloads on the oracle: n_layers MoE
+    blocks (router + 8 experts + combine) over the sample's tokens.  The CPU
+    cost does not depend on which layer's weights are read (every layer's table
+    is far above the host caches), so one table stands in for all of them."""
+    for _ in range(n_layers):
+        cpu_layer(*sample)
+
+
+def cpu_moe_tokens(T, budget_s, n_steps):
+    """Tokens per CPU step so that n_steps whole 30-layer steps fit budget_s
+    (the oracle's cost is linear in routed pairs, i.e. in tokens)."""
+    probe = cpu_sample_setup(1)
+    cpu_layer(*probe)
+    t0 = time.perf_counter()
+    cpu_layer(*probe)
+    per_tok = (time.perf_counter() - t0) * LAYERS
+    return max(1, min(T, int(budget_s / max(n_steps * per_tok, 1e-9))))
+
+
+def cpu_baseline(_layers, T, budget_s=15.0):
+    """Routed-expert workloads: whole 30-layer steps on the oracle within budget_s."""
+    cores = oracle_all_cores()
+    Ts = cpu_moe_tokens(T, budget_s, 3)
+    sample = cpu_sample_setup(Ts)
+    cpu_moe_step(sample)
     n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < budget_s:
-        cpu_layer(x, wr, buf, offs, stride)
+    while n < 1 or time.perf_counter() - t0 < budget_s:
+        cpu_moe_step(sample)
         n += 1
-    layer_s = (time.perf_counter() - t0) / n
-    return {"value": round(T / (LAYERS * layer_s), 3), "unit": "tok/s", "cores": oracle.num_threads(),
-            "kind": "port",
-            "sample": f"{n} MoE layers (router + 8 experts + combine) at T={T} on the oracle (C++ OpenMP, fp64 "
-                      f"accumulation), extrapolated to {LAYERS} layers"}
+    step_s = (time.perf_counter() - t0) / n
+    return {"value": round(Ts / step_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} whole steps ({LAYERS} MoE layers: router + 8 experts + combine) of {Ts} of the "
+                      f"workload's {T} tokens on the oracle (C++ OpenMP, fp64 accumulation), {step_s * 1e3:.1f} ms "
+                      f"per step"}
 
 
 def cpu_decoder_sample(seed=4000):
@@ -925,119 +1024,102 @@ def cpu_decoder_sample(seed=4000):
     return layers, embed, nrm(H), x
 
 
-def cpu_decoder_times(sample, n_sliding):
-    """(sliding layer s, full layer s, lm_head s) on the oracle: n_sliding
-    sliding layers averaged, one full layer and one lm_head."""
+def cpu_sampler_setup(vocab=262144, seed=1):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, vocab, (1, 64)).astype(np.int32)
+
+
+def cpu_decoder_step(sample, step, recent=None):
+    """One whole decode step of one token on the oracle: the 30 layers in the
+    model's order (every fifth one full attention, the rest sliding), the
+    final norm + tied lm_head with softcap and argmax, and — with `recent` —
+    the sampler at the generate defaults (temperature 0.7, top_p 0.9,
+    repetition penalty 1.15 over the last 64 tokens).  Each layer appends its
+    K / V row at position CTX of its cache, as the GPU step does."""
     import oracle
     layers, embed, fnorm, x = sample
-    (Ls, ks, vs, cs), (Lf, kf, vf, cf) = layers
-    oracle.decoder_layer(x, Ls, ks, vs, CTX, cs)  # warm
-    t0 = time.perf_counter()
-    for _ in range(n_sliding):
-        oracle.decoder_layer(x, Ls, ks, vs, CTX, cs)
-    t_s = (time.perf_counter() - t0) / n_sliding
-    t0 = time.perf_counter()
-    oracle.decoder_layer(x, Lf, kf, vf, CTX, cf)
-    t_f = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    oracle.lm_head(x, embed, fnorm, 1e-6, 30.0)
-    t_lm = time.perf_counter() - t0
-    return t_s, t_f, t_lm
-
-
-def cpu_decoder_step_s(t_s, t_f, t_lm, layers=LAYERS):
-    n_full = layers // 5
-    return (layers - n_full) * t_s + n_full * t_f + t_lm
-
-
-def cpu_sample_s(vocab=262144, reps=3):
-    """Seconds per token of the sampling oracle (the engine's sample() at the
-    generate defaults: temperature 0.7, top_p 0.9, penalty 1.15 over 64 tokens)."""
-    import numpy as np
-    from oracle import sample as osmp
-    rng = np.random.default_rng(1)
-    lg = (rng.standard_normal((1, vocab)) * 3).astype(np.float32)
-    recent = rng.integers(0, vocab, (1, 64)).astype(np.int32)
-    t0 = time.perf_counter()
-    for s in range(reps):
-        osmp.sample(lg, recent, 0.7, 0.9, 1.15, seed=1, step=s)
-    return (time.perf_counter() - t0) / reps
+    h = x
+    for i in range(LAYERS):
+        L, ck, cv, cfg = layers[1 if (i + 1) % 5 == 0 else 0]
+        h, _ = oracle.decoder_layer(h, L, ck, cv, CTX, cfg)
+    lg, ids = oracle.lm_head(h, embed, fnorm, 1e-6, 30.0)
+    if recent is not None:
+        from oracle import sample as osmp
+        osmp.sample(lg, recent, 0.7, 0.9, 1.15, seed=1, step=step)
+    return ids
 
 
 def cpu_decoder_baseline(T, budget_s=15.0, sampled=False):
-    import oracle
+    """decode30: whole decode steps on the oracle for about budget_s (at least one)."""
+    cores = oracle_all_cores()
     sample = cpu_decoder_sample()
-    t0 = time.perf_counter()
-    t_s, t_f, t_lm = cpu_decoder_times(sample, 2)
-    n = max(2, int((budget_s - (time.perf_counter() - t0)) / max(t_s, 1e-3)))
-    t_s, t_f, t_lm = cpu_decoder_times(sample, n)
-    step = cpu_decoder_step_s(t_s, t_f, t_lm)
-    t_smp = cpu_sample_s() * T if sampled else 0.0
-    return {"value": round(T / (step + t_smp), 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{n} sliding layers + 1 full layer + 1 lm_head of one decode token at context {CTX} on the "
-                      f"oracle (C++ OpenMP / numpy); step = 24 sliding + 6 full + lm_head "
-                      f"({t_s * 1e3:.1f} / {t_f * 1e3:.1f} / {t_lm * 1e3:.1f} ms)"
-                      + (f" + sampling ({t_smp * 1e3:.1f} ms, numpy)" if sampled else "")}
+    recent = cpu_sampler_setup() if sampled else None
+    cpu_decoder_step(sample, 0, recent)
+    n, t0 = 0, time.perf_counter()
+    while n < 1 or time.perf_counter() - t0 < budget_s:
+        cpu_decoder_step(sample, n, recent)
+        n += 1
+    step_s = (time.perf_counter() - t0) / n
+    return {"value": round(T / step_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} whole decode steps of one token at context {CTX} on the oracle (C++ OpenMP / numpy): "
+                      f"24 sliding + 6 full layers + lm_head" + (" + the sampler" if sampled else "")
+                      + f", {step_s * 1e3:.1f} ms per step"}
+
+
+REF_BUDGET_S = 150.0  # the reference arm's whole run (warm-up + timed steps) stays within a few minutes
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the oracle (the repository's C++ / numpy port of the
+    reference's path) on all host cores, rank 0 alone, same metric / unit /
+    config as the GPU arm.  decode30: every step is one whole decode step.
+    Routed-expert workloads: every step is one whole 30-layer step over a
+    bounded number of the workload's tokens (the CPU cost is linear in tokens),
+    sized so that warm-up + timed steps fit REF_BUDGET_S."""
     if rank != 0:
         return
-    import oracle
-    T = WORKLOADS[args.workload]
+    cores = oracle_all_cores()
+    n_runs = args.steps + args.warmup
     if args.workload.startswith("decode30"):
+        T = WORKLOADS[args.workload]
         sample = cpu_decoder_sample()
-        cpu_decoder_times(sample, 1)
-        for _ in range(args.warmup):
-            cpu_decoder_times(sample, 1)
-        t_s, t_f, t_lm = cpu_decoder_times(sample, args.steps)
-        step = cpu_decoder_step_s(t_s, t_f, t_lm)
-        if args.sample:  # the engine's sample() per token at the generate defaults
-            step += cpu_sample_s() * T
-        value = T / step
-        desc = (f"each step = one sliding decoder layer of one token at context {CTX} on the oracle; one full layer "
-                f"and one lm_head timed once; decode step = 24 sliding + 6 full + lm_head"
-                + (" + the sampling oracle (temperature 0.7, top_p 0.9, penalty 1.15)" if args.sample else ""))
-        out = {
-            "impl": "reference",
-            "metric": "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)",
-            "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32/fp64 accumulate (CPU)",
-            "data": "synthetic (seeded)",
-            "config": {"workload": args.workload, "layers": LAYERS, "batch": T, "context": CTX,
-                       "next_token": "sampled (temperature 0.7, top_p 0.9, penalty 1.15)" if args.sample
-                       else "greedy argmax"},
-            "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
-                             "sample": desc},
-            "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "the reference (Rust + MLX/Metal) cannot run here; this is the repository's C++/numpy port of "
-                    "its path (oracle/)",
-        }
-        print(json.dumps(out), flush=True)
-        return
-    x, wr, buf, offs, stride = cpu_sample_setup(T)
-    for _ in range(args.warmup):
-        cpu_layer(x, wr, buf, offs, stride)
+        recent = cpu_sampler_setup() if args.sample else None
+        step = lambda i: cpu_decoder_step(sample, i, recent)  # noqa: E731
+        metric, config, tokens = DECODER_METRIC, decoder_config(args, world), T
+        dtype = "u8/u4/u6-affine weights x bf16 activations, fp32/fp64 accumulate (CPU)"
+        desc = (f"each step = one whole decode step of one token at context {CTX} on the oracle: 24 sliding + 6 "
+                f"full layers + lm_head" + (" + the sampler (temperature 0.7, top_p 0.9, penalty 1.15)"
+                                             if args.sample else ""))
+    else:
+        if args.workload in EP_WORKLOADS:
+            T = EP_WORKLOADS[args.workload][0]
+            metric, config = ep_metric(args), ep_config(args, world)
+        else:
+            T = WORKLOADS[args.workload]
+            metric, config = MOE_METRIC, moe_config(args, world)
+        tokens = cpu_moe_tokens(T, REF_BUDGET_S, n_runs)
+        sample = cpu_sample_setup(tokens)
+        step = lambda i: cpu_moe_step(sample)  # noqa: E731
+        dtype = "u4-affine weights x bf16 activations, fp64 accumulate (CPU)"
+        desc = (f"each step = one whole {LAYERS}-layer step (router + 8 experts + combine per layer) over {tokens} "
+                f"of the workload's {T} tokens on the oracle")
+    for i in range(args.warmup):
+        step(i)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_layer(x, wr, buf, offs, stride)
-    layer_s = (time.perf_counter() - t0) / args.steps
-    value = T / (LAYERS * layer_s)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    step_s = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = tokens / step_s
     out = {
-        "impl": "reference",
-        "metric": "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)",
-        "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(layer_s * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u4-affine weights x bf16 activations, fp64 accumulate (CPU)",
-        "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "layers": nl, "tokens_per_step": T},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": oracle.num_threads(), "kind": "port",
-                         "sample": f"each step = 1 of the {LAYERS} MoE layers at T={T}; tok/s extrapolated"},
+        "impl": "reference", "metric": metric, "value": round(value, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong" if args.workload in EP_WORKLOADS else "weak",
+        "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config,
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": cores, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "the reference (Rust + MLX/Metal) cannot run here; this is the repository's C++ port of its "
-                "path (oracle/)",
+        "note": "the reference (Rust + MLX/Metal) cannot run here; this is the repository's C++ / numpy port of "
+                "its path (oracle/), timed on the host cores",
     }
     print(json.dumps(out), flush=True)
 
@@ -1107,6 +1189,27 @@ def prefill_time(fm, torch, dev, block, g, T, iters):
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b) * 1e3)
     return times, uniq
+
+
+def prefill_submeasure(fm, torch, dev, peaks, T=512, iters=10):
+    """the prefill MoE block (router + Zipf-skewed top-8 +
+    grouped 4-bit expert GEMMs + combine) over T tokens, L2 flushed between
+    runs; median of `iters` device-timed calls of Gemma4MoeBlock.forward_prefill."""
+    block, g = prefill_setup(fm, torch, dev)
+    times, uniq = prefill_time(fm, torch, dev, block, g, T, iters + 2)
+    us = statistics.median(times[2:])
+    flops = 2.0 * T * K * 3 * H * I                      # gate, up, down of every routed pair
+    nbytes = uniq * EXPERT_BYTES + ROUTER_BYTES + 2 * T * H * 2
+    t_fl = flops / (peaks["bf16_tflops"] * 1e12) * 1e6
+    t_by = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e6
+    del block
+    torch.cuda.empty_cache()
+    return {"metric": "prefill tok/s (MoE block, one layer)", "tokens": T, "value": round(T / us * 1e6, 1),
+            "unit": "tok/s", "us": round(us, 1), "unique_experts": uniq,
+            "roofline": {"bound": "tensor" if t_fl > t_by else "hbm", "alg_flops": int(flops),
+                         "alg_bytes": int(nbytes), "floor_us": round(max(t_fl, t_by), 1),
+                         "frac": round(max(t_fl, t_by) / us, 4)},
+            "timing": f"median of {iters} CUDA-event timed calls, 512 MB L2 flush before each"}
 
 
 def run_prefill_case(args):

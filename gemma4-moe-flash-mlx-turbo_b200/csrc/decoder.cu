@@ -330,8 +330,15 @@ struct DecWs {
   size_t bytes;
 };
 
-// The per-op kernel sequence instead of the streaming layer, for A/B timing
-// and as a cross-check (environment FMOE_DECODE_PATH=ops).
+// Decode path selection (environment FMOE_DECODE_PATH, read per call):
+//   unset / "ops"  the per-op kernel sequence below (the default: fastest
+//                  measured for the whole step);
+//   "stream"       the six-launch streaming layer of dlayer.cu;
+// the lm_head always uses the streaming kernel unless "ops" is set.
+static bool stream_layer_path() {
+  const char* e = std::getenv("FMOE_DECODE_PATH");
+  return e && std::strcmp(e, "stream") == 0;
+}
 static bool force_ops_path() {
   const char* e = std::getenv("FMOE_DECODE_PATH");
   return e && std::strcmp(e, "ops") == 0;
@@ -391,7 +398,7 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   d.moe = c.take<bf16>((size_t)T * H);
   d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
   d.wts = c.take<float>((size_t)T * L->router.top_k);
-  d.dl = ep_ranks == 0 && !force_ops_path() && dl_plan(L, kv, T, &d.dlp) == FMOE_OK;
+  d.dl = ep_ranks == 0 && stream_layer_path() && dl_plan(L, kv, T, &d.dlp) == FMOE_OK;
   if (d.dl) dl_carve(c, d.dlp, &d.dlw);
   d.bytes = c.off + 256;
   if (w) *w = d;
@@ -509,7 +516,7 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
   // 2 norms, RoPE, KV append
   if ((rc = launch_qkv_post(kv, w.qkv, qkv_rows, L->num_heads, L->k_eq_v, static_cast<const bf16*>(L->q_norm),
                             static_cast<const bf16*>(L->k_norm), L->eps, L->rope_dims, L->rope_theta, pos, pos_dev,
-                            w.q, 0, true, st)))
+                            w.q, kv.turbo, true, st)))
     return rc;
   // 3 attention over the slots written so far (pos_dev[1] when counters live on the device)
   const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;

@@ -49,12 +49,13 @@ namespace dl {
 constexpr int NW = 12;  // warps per CTA
 constexpr int NTHR = NW * 32;
 constexpr int kMaxT = 8;
-constexpr int kMaxHidden = 4224;      // hidden rows staged in shared memory by the row epilogues (<= 16 B each in the rings)
+constexpr int kMaxHidden = 4096;      // hidden rows staged in shared memory by the row epilogues (<= 16 B each in the rings)
 constexpr int kMaxSlotsPerCta = 3;    // expert inputs one ffn3 CTA may need
 constexpr int kMaxUnique = 64;        // unique experts of one call (T * k <= 64)
 constexpr int kRingSlot = 6144;       // bytes of one warp's ring
 constexpr int kRingBytes = NW * kRingSlot;
 constexpr int kMaxPend = 8;           // groups one warp may complete in one launch
+static_assert(16 * kMaxHidden <= kRingBytes, "row epilogues stage 16 bytes per hidden element in the rings");
 
 // ---------------------------------------------------------------------------
 // Work families
@@ -84,21 +85,68 @@ struct Fam {
   int frag_off, xsum_off;  // shared-memory offsets of the input fragments
 };
 
-// Work is counted in ring steps: warp lw's range is [S*lw/nw, S*(lw+1)/nw)
-// (empty outside [0, nw)); warp_of gives the warp holding step s.  S * nw < 2^32 for every family (checked when planned).
-__device__ __forceinline__ int range_lo(int S, int nw, int lw) {
-  lw = lw < 0 ? 0 : lw > nw ? nw : lw;
-  return (int)((unsigned)S * (unsigned)lw / (unsigned)nw);
+// Work split of a family over its nw warps, counted in ring steps (us per
+// unit).  U > nw units: every warp takes whole units (never split).  U <= nw:
+// unit u is cut into k or k + 1 contiguous slices (the first `extra` units
+// k + 1), one per warp, so a unit has a fixed, known number of pieces; warps
+// past U * us slices (when nw / U > us) stay idle.
+struct Split {
+  int U, nw, us, k, extra;
+};
+__host__ __device__ inline Split make_split(int U, int nw, int us) {
+  Split p{U, nw, us, 0, 0};
+  if (U > 0 && U <= nw) {
+    p.k = nw / U;
+    if (p.k >= us) {
+      p.k = us;
+    } else {
+      p.extra = nw % U;
+    }
+  }
+  return p;
 }
-__device__ __forceinline__ int warp_of(int S, int nw, int s) {
-  return (int)(((unsigned)(s + 1) * (unsigned)nw + (unsigned)S - 1u) / (unsigned)S) - 1;
+__host__ __device__ inline void split_range(const Split& p, int lw, int* lo, int* hi) {
+  *lo = *hi = 0;
+  if (lw < 0 || lw >= p.nw || p.U <= 0) return;
+  if (p.k == 0) {
+    *lo = (int)((int64_t)p.U * lw / p.nw) * p.us;
+    *hi = (int)((int64_t)p.U * (lw + 1) / p.nw) * p.us;
+    return;
+  }
+  const int big = p.extra * (p.k + 1);
+  int u, q, ku;
+  if (lw < big) {
+    u = lw / (p.k + 1);
+    q = lw - u * (p.k + 1);
+    ku = p.k + 1;
+  } else {
+    const int l2 = lw - big;
+    u = p.extra + l2 / p.k;
+    q = l2 - (u - p.extra) * p.k;
+    ku = p.k;
+    if (u >= p.U) return;  // idle
+  }
+  *lo = u * p.us + p.us * q / ku;
+  *hi = u * p.us + p.us * (q + 1) / ku;
 }
-__device__ __forceinline__ int pieces_of(int S, int nw, int G, int u) {
-  return warp_of(S, nw, (u + 1) * G - 1) - warp_of(S, nw, u * G) + 1;
+__device__ __forceinline__ int2 srange(const Split& p, int lw) {
+  int lo, hi;
+  split_range(p, lw, &lo, &hi);
+  return make_int2(lo, hi);
+}
+// Pieces of unit u and the family-local warp holding its first slice.
+__host__ __device__ inline int split_pieces(const Split& p, int u) {
+  return p.k == 0 ? 1 : (u < p.extra ? p.k + 1 : p.k);
+}
+__host__ __device__ inline int split_first(const Split& p, int u) {
+  return p.k == 0 ? 0 : (u < p.extra ? u * (p.k + 1) : p.extra * (p.k + 1) + (u - p.extra) * p.k);
+}
+// Largest piece count of any unit for U in [U_min, ...).
+__host__ __device__ inline int split_maxp(int U_min, int nw, int us) {
+  const Split p = make_split(U_min, nw, us);
+  return p.k == 0 ? 1 : p.k + 1;
 }
 
-// A unit's accumulators in the lane's fragment layout (rows g / g+8, tokens
-// 2t / 2t+1 of each tile), passed by value between the engine and its hooks.
 template <int NT>
 struct Acc {
   float v[NT][4];
@@ -308,35 +356,37 @@ struct Engine {
 // ---------------------------------------------------------------------------
 // Pieces, unit completion, counters
 
-// Publish (fence) and count toward counter `c`; true for the warp that brought
-// it to `target` (the counter is then reset; that warp owns the next step).
+// Count this warp's published writes toward counter `c`: lane 0 adds with
+// acquire-release semantics after a __syncwarp (which orders the other lanes'
+// writes before it), so the warp that brings the count to `target` sees every
+// earlier warp's writes; it resets the counter and owns the next step.
+__device__ __forceinline__ unsigned atom_add_acqrel(unsigned* c, unsigned v) {
+  unsigned prev;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;\n" : "=r"(prev) : "l"(c), "r"(v) : "memory");
+  return prev;
+}
 __device__ __forceinline__ bool arrive(unsigned* c, int target, int lane) {
-  __threadfence();
   __syncwarp();
   unsigned last = 0;
   if (lane == 0) {
-    const unsigned prev = atomicAdd(c, 1u);
-    last = prev == (unsigned)target - 1u;
+    last = atom_add_acqrel(c, 1u) == (unsigned)target - 1u;
     if (last) *c = 0u;
   }
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) __threadfence();
+  __syncwarp();
   return last != 0;
 }
 
 // CTA-level: true in the last CTA of the grid to get here (counter reset).
 __device__ __forceinline__ bool grid_last(unsigned* ctr, int* flag) {
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(ctr, 1u);
-    *flag = prev == gridDim.x - 1;
+    asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+    *flag = atom_add_acqrel(ctr, 1u) == gridDim.x - 1;
     if (*flag) *ctr = 0u;
   }
   __syncthreads();
-  const bool last = *flag != 0;
-  if (last) __threadfence();
-  return last;
+  return *flag != 0;
 }
 
 // The lane's fragment values (rows g / g+8, tokens 2t / 2t+1) stored to a
@@ -397,13 +447,12 @@ struct Fin {
   int ok;
 };
 template <int NT>
-__device__ __noinline__ Fin<NT> finish_piece(const Fam& f, int S, int T, int lw, int u, Acc<NT> y, int lane,
-                                             int slot) {
-  const int w1 = warp_of(S, f.nw, u * f.us);
+__device__ __noinline__ Fin<NT> finish_piece(const Fam& f, const Split sp, int T, int lw, int u, Acc<NT> y,
+                                             int lane, int slot) {
   const int64_t stride = (int64_t)NT * T * 16;
   float* base = f.piece + (int64_t)slot * f.maxp * stride;
-  store_block<NT>(base + (lw - w1) * stride, T, y, lane);
-  const int np = pieces_of(S, f.nw, f.us, u);
+  store_block<NT>(base + (lw - split_first(sp, u)) * stride, T, y, lane);
+  const int np = split_pieces(sp, u);
   Fin<NT> r;
   r.ok = arrive(f.uctr + slot, np, lane) ? 1 : 0;
   if (r.ok) sum_blocks<NT>(base, stride, np, T, r.y, lane);
@@ -411,11 +460,11 @@ __device__ __noinline__ Fin<NT> finish_piece(const Fam& f, int S, int T, int lw,
 }
 // True when unit u's sums are complete in y (the whole unit was this warp's,
 // or this warp's piece completed it).
-#define DL_UNIT_DONE(NT, f, S, T, lw, u, y, pst, pe, lane, slot)                          \
-  ((pst) == (u) * (f).us && (pe) == ((u) + 1) * (f).us                                        \
-       ? true                                                                                \
-       : [&] {                                                                               \
-           const Fin<NT> r_ = finish_piece<NT>((f), (S), (T), (lw), (u), (y), (lane), (slot)); \
+#define DL_UNIT_DONE(NT, f, S, T, lw, u, y, pst, pe, lane, slot)                           \
+  ((pst) == (u) * (f).us && (pe) == ((u) + 1) * (f).us                                         \
+       ? true                                                                                 \
+       : [&] {                                                                                \
+           const Fin<NT> r_ = finish_piece<NT>((f), (S), (T), (lw), (u), (y), (lane), (slot));  \
            if (r_.ok) (y) = r_.y;                                                            \
            return r_.ok != 0;                                                                \
          }())
@@ -655,10 +704,11 @@ __global__ void __launch_bounds__(NTHR, 1) qkv_kernel(const __grid_constant__ Qk
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.us;
+  const Split S = make_split(f.tiles, f.nw, f.us);
   const int lw = gw - f.w0;
   Engine<BITS, 1, 2, D_> en;
-  en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
+  const int2 rg = srange(S, lw);
+  en.init(smem + warp * kRingSlot, lane, f, rg.x, rg.y);
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
   griddep_wait();
@@ -718,7 +768,7 @@ __device__ __noinline__ void ff_in_rows(const OArgs& a, float* red, uint8_t* row
   const bf16* srcw[4] = {a.w_post_attn, a.w_pre_ff, a.w_pre_ff2, a.rscale};
   for (int tk = 0; tk < a.T; ++tk) {
 #pragma unroll
-    for (int k = 0; k < kMaxHidden / NTHR; ++k) {
+    for (int k = 0; k < (kMaxHidden + NTHR - 1) / NTHR; ++k) {
       const int i = threadIdx.x + k * NTHR;
       if (i < H) {
         const float o = fin_at(a.f, a.T, tk, i);
@@ -781,10 +831,11 @@ __global__ void __launch_bounds__(NTHR, 1) o_kernel(const __grid_constant__ OArg
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.us;
+  const Split S = make_split(f.tiles, f.nw, f.us);
   const int lw = gw - f.w0;
   Engine<BITS, 1, 2, D_> en;
-  en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
+  const int2 rg = srange(S, lw);
+  en.init(smem + warp * kRingSlot, lane, f, rg.x, rg.y);
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
   griddep_wait();
@@ -938,9 +989,10 @@ __global__ void __launch_bounds__(NTHR, 1) ffn1_kernel(const __grid_constant__ F
   const int gw = blockIdx.x * NW + warp;
   const bool is_r = gw < a.fr.w0 + a.fr.nw;
   const Fam& f = is_r ? a.fr : a.fg;
-  const int S = f.tiles * f.us;
+  const Split S = make_split(f.tiles, f.nw, f.us);
   const int lw = gw - f.w0;
-  const int lo = range_lo(S, f.nw, lw), hi = range_lo(S, f.nw, lw + 1);
+  const int2 rg = srange(S, lw);
+  const int lo = rg.x, hi = rg.y;
   uint8_t* ring = smem + warp * kRingSlot;
   auto fr_ = [&](int) {
     return FragPtr{reinterpret_cast<const uint4*>(smem + f.frag_off), reinterpret_cast<const float*>(smem + f.xsum_off)};
@@ -1021,7 +1073,8 @@ __global__ void __launch_bounds__(NTHR, 1) ffn2_kernel(const __grid_constant__ F
   };
   if (is_d) {
     const Fam& f = a.fd;
-    const int S = f.tiles * f.us, lw = gw - f.w0;
+    const Split S = make_split(f.tiles, f.nw, f.us);
+    const int lw = gw - f.w0;
     auto addr = [&](int u) { return mat_unit<1>(f, u); };
     auto fr_ = [&](int) {
       return FragPtr{reinterpret_cast<const uint4*>(smem + f.frag_off),
@@ -1031,14 +1084,16 @@ __global__ void __launch_bounds__(NTHR, 1) ffn2_kernel(const __grid_constant__ F
       if (DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, u)) store_block<1>(f.fin + (int64_t)u * a.T * 16, a.T, y, lane);
     };
     Engine<4, 1, 1, 8> en;
-    en.init(ring, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
+    const int2 rg = srange(S, lw);
+    en.init(ring, lane, f, rg.x, rg.y);
     en.prime(addr);
     prologue();
     en.run(addr, fr_, done, a.T);
   } else {
     prologue();
     const Fam& f = a.fx;
-    const int S = nu_s * f.tiles * f.us, lw = gw - f.w0;
+    const Split S = make_split(nu_s * f.tiles, f.nw, f.us);
+    const int lw = gw - f.w0;
     auto addr = [&](int u) { return expert_unit<2>(f, a.ex, uq, u); };
     auto fr_ = [&](int) {
       return FragPtr{reinterpret_cast<const uint4*>(smem + f.frag_off),
@@ -1050,7 +1105,8 @@ __global__ void __launch_bounds__(NTHR, 1) ffn2_kernel(const __grid_constant__ F
       glu_store(y, a.T, j, a.act_e + (int64_t)slot * a.T * a.Ie, a.Ie, lane);
     };
     Engine<4, 2, 2, 3> en;
-    en.init(ring, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
+    const int2 rg = srange(S, lw);
+    en.init(ring, lane, f, rg.x, rg.y);
     en.prime(addr);
     en.run(addr, fr_, done, a.T);
   }
@@ -1147,7 +1203,7 @@ __device__ __noinline__ void ff_out_rows(const Ffn3Args& a, float* red, uint8_t*
   const float sc = round_bf(a.scalar);
   for (int tk = 0; tk < a.T; ++tk) {
 #pragma unroll
-    for (int k = 0; k < kMaxHidden / NTHR; ++k) {
+    for (int k = 0; k < (kMaxHidden + NTHR - 1) / NTHR; ++k) {
       const int i = threadIdx.x + k * NTHR;
       if (i < H) {
         const float d = fin_at(a.fd, a.T, tk, i);
@@ -1210,10 +1266,20 @@ __global__ void __launch_bounds__(NTHR, 1) ffn3_kernel(const __grid_constant__ F
   if (threadIdx.x < kMaxUnique) uq[threadIdx.x] = __ldcg(a.uniq + threadIdx.x);
   __syncthreads();
   const int nu = nu_s;
-  const int S = nu * f.tiles * f.us, lw = gw - f.w0;
-  const int lo = range_lo(S, f.nw, lw), hi = range_lo(S, f.nw, lw + 1);
+  const Split S = make_split(nu * f.tiles, f.nw, f.us);
+  const int lw = gw - f.w0;
+  const int2 rg = srange(S, lw);
+  const int lo = rg.x, hi = rg.y;
   // expert slots this CTA's warps touch: their inputs' fragments
-  const int cl = range_lo(S, f.nw, blockIdx.x * NW - f.w0), ch = range_lo(S, f.nw, blockIdx.x * NW + NW - f.w0);
+  int cl = 0x7fffffff, ch = 0;
+  for (int w = 0; w < NW; ++w) {
+    const int2 r = srange(S, blockIdx.x * NW + w - f.w0);
+    if (r.y > r.x) {
+      cl = min(cl, r.x);
+      ch = max(ch, r.y);
+    }
+  }
+  if (ch == 0) cl = 0;
   const int per = f.tiles * f.us;
   const int s_first = cl / per, s_last = ch > cl ? (ch - 1) / per : s_first;
   auto addr = [&](int u) { return expert_unit<1>(f, a.ex, uq, u); };
@@ -1311,9 +1377,11 @@ __global__ void __launch_bounds__(NTHR, 1) lm_kernel(const __grid_constant__ LmA
   const int g = lane >> 2, t = lane & 3;
   const int gw = blockIdx.x * NW + warp;
   const Fam& f = a.f;
-  const int S = f.tiles * f.us, lw = gw - f.w0;
+  const Split S = make_split(f.tiles, f.nw, f.us);
+    const int lw = gw - f.w0;
   Engine<BITS, 1, 2, D_> en;
-  en.init(smem + warp * kRingSlot, lane, f, range_lo(S, f.nw, lw), range_lo(S, f.nw, lw + 1));
+  const int2 rg = srange(S, lw);
+  en.init(smem + warp * kRingSlot, lane, f, rg.x, rg.y);
   auto addr = [&](int u) { return mat_unit<1>(f, u); };
   en.prime(addr);
   griddep_wait();
@@ -1329,7 +1397,7 @@ __global__ void __launch_bounds__(NTHR, 1) lm_kernel(const __grid_constant__ LmA
   // Ranges are at least one unit long (planned so): a unit is split over at
   // most two warps, its pieces and counter keyed by its first warp.
   auto done = [&](int u, Acc<1> y, int pst, int pe) {
-    if (!DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, warp_of(S, f.nw, u * f.us))) return;
+    if (!DL_UNIT_DONE(1, f, S, a.T, lw, u, y, pst, pe, lane, u)) return;
     best = lm_unit_finished(a, u, y, best, lane);
   };
   en.run(addr, fr_, done, a.T);
@@ -1387,14 +1455,6 @@ namespace dl {
 constexpr int kGrid = kNumSMs;      // one CTA per SM
 constexpr int kWarps = kGrid * NW;  // warps of a launch
 
-// pieces_of on the host (the device arithmetic, widened).
-static int h_warp_of(long S, long nw, long s) { return (int)(((s + 1) * nw + S - 1) / S) - 1; }
-// Bound on the pieces of one unit of G groups when ranges hold >= S_min / nw groups.
-static int h_maxp(long S_min, long nw, long G) {
-  const long L = S_min / nw;
-  if (L <= 0) return -1;
-  return L >= G ? 2 : (int)((G + L - 1) / L) + 1;
-}
 static bool fits32(long S, long nw) { return S > 0 && (S + 1) * nw + S < (1l << 32); }
 
 static Fam mat_fam(int bits, int K, const QW* segs, int nseg, int w0, int nw, int ng) {
@@ -1574,13 +1634,13 @@ int dl_plan(const fmoe_decoder_layer_t* L, const KvDev& kv, int64_t T, DlPlan* p
   if (!fits32(S_qkv, kWarps) || !fits32(S_o, kWarps) || !fits32(S_xmax, d.nw_x) || !fits32(S_ymax, kWarps) ||
       !fits32(S_r, d.nw_r) || !fits32(S_g, d.nw_g) || !fits32(S_d, d.nw_d))
     return FMOE_ERR_UNSUPPORTED;
-  d.mp_qkv = h_maxp(S_qkv, kWarps, Uh);
-  d.mp_o = h_maxp(S_o, kWarps, Uq);
-  d.mp_r = h_maxp(S_r, d.nw_r, Ur);
-  d.mp_g = h_maxp(S_g, d.nw_g, Uh);
-  d.mp_d = h_maxp(S_d, d.nw_d, Ui);
-  d.mp_x = h_maxp(S_x, d.nw_x, Uh);
-  d.mp_y = h_maxp(S_y, kWarps, Ue);
+  d.mp_qkv = split_maxp(d.qkv_tiles, kWarps, (int)Uh);
+  d.mp_o = split_maxp(H / 16, kWarps, (int)Uq);
+  d.mp_r = split_maxp(d.E / 16, d.nw_r, (int)Ur);
+  d.mp_g = split_maxp(d.Id / 16, d.nw_g, (int)Uh);
+  d.mp_d = split_maxp(H / 16, d.nw_d, (int)Ui);
+  d.mp_x = split_maxp(d.k * (d.Ie / 16), d.nw_x, (int)Uh);  // fewest slots: k
+  d.mp_y = split_maxp(d.k * (H / 16), kWarps, (int)Ue);
   if (std::min({d.mp_qkv, d.mp_o, d.mp_r, d.mp_g, d.mp_d, d.mp_x, d.mp_y}) < 0) return FMOE_ERR_UNSUPPORTED;
   const size_t fT = 128 * (size_t)T;
   d.sm_qkv = kRingBytes + Gh * fT + Gh * 32;
@@ -1836,11 +1896,12 @@ int dl_lm_head(const QW& e, const bf16* norm, float eps, const bf16* x, int64_t 
   float2* cand = reinterpret_cast<float2*>(base + 256 + align_up(sizeof(unsigned) * (kWarps + 1), 256));
   float* piece = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(cand) + align_up(sizeof(float2) * kGrid * T, 256));
   LmArgs a = {};
-  // at most one warp per unit, so a unit spans at most two warps
-  const int nw = (int)std::min<int64_t>(kWarps, e.out / 16);
+  const int nw = kWarps;
   a.f = mat_fam(e.bits, H, &e, 1, 0, nw, 2);
   a.f.piece = piece;
-  a.f.maxp = 2;
+  a.f.maxp = split_maxp(a.f.tiles, nw, a.f.us);
+  if ((long)a.f.maxp * std::min(a.f.tiles, nw) > 2l * kWarps)
+    return set_error(FMOE_ERR_UNSUPPORTED, "lm_head: too few rows for the piece buffer");
   a.f.uctr = ctr + 1;
   a.f.frag_off = kRingBytes;
   const int G = H / 64;

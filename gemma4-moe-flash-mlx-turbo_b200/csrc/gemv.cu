@@ -88,9 +88,10 @@ __global__ void router_prenorm_kernel(const bf16* __restrict__ x, int H, float r
   }
 }
 
-// Top-k of `nv` tokens by the whole CTA: each thread takes one (token,
-// expert) and counts the logits that beat it (descending value, ties -> lower
-// id) with 16-byte shared-memory reads — independent compares, no serial
+// Top-k of `nv` tokens by the whole CTA over logits already rounded to bf16
+// (the router projection's output dtype in the reference, moe.rs:330-334):
+// each thread takes one (token, expert) and counts the logits that beat it
+// (descending value, ties -> lower id) with 16-byte shared-memory reads — independent compares, no serial
 // reduction chain.  Then weights = softmax over the k selected logits (equal
 // to softmax(all)[ids] / sum softmax(all)[ids], src/model/moe.rs:331-340),
 // times per_expert_scale (moe.rs:341-345).  lg: shared [nv][E], E % 4 == 0.
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(kRtWarps * 32)
       float s = 0.f;
       for (int q = 0; q < KS; ++q) s += cluster.map_shared_rank(&part[0][0], q * RT + e / 16)[(e % 16) * 8 + c];
       if (bias) s += bias[e];
-      lg[i] = s;
+      lg[i] = round_bf(s);  // ranked and softmaxed in the router's bf16 output precision
       if (logits_out && c < nv) logits_out[(int64_t)(tok0 + c) * E + e] = s;
     }
   }

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           if (a.bias) v[j] += __ldg(a.bias + c0 + j);
-          lg[c0 + j] = v[j];
+          lg[c0 + j] = round_bf(v[j]);  // ranked in the router's bf16 output precision
         }
         if (a.logits && t < a.T) {
           float4* o = reinterpret_cast<float4*>(a.logits + (int64_t)t * a.E + c0);

@@ -1492,7 +1492,7 @@ __device__ void topk_warp(Ep& e, const DLayer& L, int l) {
 #pragma unroll
         for (int c = 0; c < RQ; ++c) s += part[q][c];
         if (L.logit_bias) s += L.logit_bias[ex];
-        lg[ex] = s;
+        lg[ex] = round_bf(s);  // ranked in the router's bf16 output precision
       }
     }
   }
@@ -1832,9 +1832,9 @@ int check_model(const fmoe_decode_model_t* md) {
     for (int j = 0; j < 10; ++j)
       if ((j < 9 && !norms[j]) || (norms[j] && !aligned(norms[j], 16)))
         return set_error(FMOE_ERR_INVALID, "decode_step: layer %d norms are required, 16-byte aligned", i);
-    if (c.mode != FMOE_KV_BF16 || c.batch != 1 || c.kv_heads != Hkv || c.head_dim != D || c.capacity < 16 ||
+    if (c.mode != FMOE_KV_BF16 || c.turbo_bits != 0 || c.batch != 1 || c.kv_heads != Hkv || c.head_dim != D || c.capacity < 16 ||
         c.capacity % 16 || !c.k || !c.v || !aligned(c.k, 16) || !aligned(c.v, 16))
-      return set_error(FMOE_ERR_UNSUPPORTED, "decode_step: layer %d cache must be bf16, batch 1, %d heads x %d", i, Hkv,
+      return set_error(FMOE_ERR_UNSUPPORTED, "decode_step: layer %d cache must be bf16 (no TurboQuant), batch 1, %d heads x %d", i, Hkv,
                        D);
     if (L.experts.hidden != H || L.mlp_gate.out_features != Id || L.router.proj.out_features != E ||
         L.experts.intermediate != Ie)

@@ -248,11 +248,16 @@ def _qlin(x_bf16, w):
 
 def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
     """One decode step of DecoderLayer::forward_gemma4 (src/model/mod.rs:67-119) for
-    T sequences (one token each) with a bf16 KV cache.
+    T sequences (one token each).
 
     x: bf16 [T, H]; L: dict of weights (q/k/v/o/gate/up/down as _qlin tuples,
     bf16 norms, router (wr, bits, scale, pes, root), experts (buf, stride, offsets));
-    cache_k / cache_v: bf16 [T, Hkv, cap, D], updated at slot pos % cap.
+    cache_k / cache_v: bf16 [T, Hkv, cap, D], updated at slot pos % cap — or,
+    with cfg["kv_mode"] == "affine", the tuples (codes, scales, biases) of the
+    WHT-rotated 4-bit K / 8-bit V cache ([T, Hkv, cap, ...] each), the new row
+    quantised by kv_quant_affine (src/cache.rs:266-310 with the affine store).
+    cfg["turbo_bits"] (bf16 caches only): the new K / V rows pass through the
+    TurboQuant round trip before they are stored (src/cache.rs:290-308).
     cfg: heads, kv_heads, head_dim, rope_dims, rope_theta, eps, k_eq_v, scalar,
     attn_scale, top_k, hidden, inter_expert.  Returns (x_out bf16, q_rot bf16).
     """
@@ -266,12 +271,23 @@ def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
     q = rope(rms_norm(q, L["q_norm"], eps), cfg["rope_dims"], cfg["rope_theta"], pos)
     k = rope(rms_norm(k, L["k_norm"], eps), cfg["rope_dims"], cfg["rope_theta"], pos)
     v = rms_norm(v, None, eps)
-    cap = cache_k.shape[2]
-    cache_k[:, :, pos % cap] = k
-    cache_v[:, :, pos % cap] = v
-    n = min(pos + 1, cap)
-    att = attn_decode_bf16(q, Hkv, cap, np.zeros(T, np.int32), np.full(T, n, np.int32), cache_k, cache_v,
-                           cfg["attn_scale"])
+    lo = np.zeros(T, np.int32)
+    if cfg.get("kv_mode", "bf16") == "affine":
+        cap = cache_k[0].shape[2]
+        for arr, new in zip(cache_k + cache_v, kv_quant_affine(k, 4) + kv_quant_affine(v, 8)):
+            arr[:, :, pos % cap] = new.reshape(arr[:, :, pos % cap].shape)
+        hi = np.full(T, min(pos + 1, cap), np.int32)
+        att = attn_decode_affine(q, Hkv, cap, lo, hi, *cache_k, 4, *cache_v, 8, cfg["attn_scale"])
+    else:
+        tb = cfg.get("turbo_bits", 0)
+        if tb:
+            k = turbo_round_trip(k, tb)[0]
+            v = turbo_round_trip(v, tb)[0]
+        cap = cache_k.shape[2]
+        cache_k[:, :, pos % cap] = k
+        cache_v[:, :, pos % cap] = v
+        hi = np.full(T, min(pos + 1, cap), np.int32)
+        att = attn_decode_bf16(q, Hkv, cap, lo, hi, cache_k, cache_v, cfg["attn_scale"])
     o = _qlin(_bf(att).reshape(T, Hq * D), L["o"])
     h = _bf(_f(x) + _f(rms_norm(o, L["post_attn_norm"], eps)))
     # feed-forward block: dense MLP + MoE in parallel (mod.rs:92-118)

@@ -242,9 +242,10 @@ void orc_matmul_bf16(const uint16_t* x, int64_t T, const uint16_t* w, int64_t ou
 // ---------------------------------------------------------------------------
 // Router, src/model/moe.rs:324-345 (+ rms_norm_no_scale moe.rs:473-479):
 //   if norm:  xs = bf16(bf16(bf16(x * rsqrt(mean(x^2) + eps)) * bf16(root_size)) * router_scale)
-//   logits   = xs . Wr^T  (+ logit_bias[e], a synthetic-input device)
-//   ids      = top-k of logits (descending value, ties -> lower id)
-//   w        = softmax(logits)[ids] / sum(softmax(logits)[ids])  == softmax over the k
+//   logits   = xs . Wr^T  (+ logit_bias[e], a synthetic-input device), fp32 in logits_out
+//   ids      = top-k of bf16(logits) (descending value, ties -> lower id): the
+//              reference's router output is bf16 (moe.rs:330-334)
+//   w        = softmax(bf16 logits)[ids] / sum(...)  == softmax over the k selected
 //   w       *= per_expert_scale[ids]   (optional)
 // wr_bits == 16 means Wr is plain bf16 [E, H]; otherwise MLX-affine packed.
 void orc_router(const uint16_t* x, int T, int H, int E, const void* wr, const uint16_t* wr_s,
@@ -281,6 +282,10 @@ void orc_router(const uint16_t* x, int T, int H, int E, const void* wr, const ui
     if (logit_bias)
       for (int e = 0; e < E; ++e) l[e] += logit_bias[e];
     if (logits_out) std::memcpy(logits_out + static_cast<int64_t>(t) * E, l, sizeof(float) * E);
+    // The router projection's output is bf16 in the reference (quantized_matmul /
+    // matmul keep x's dtype, moe.rs:330): rank and softmax the rounded logits;
+    // the stable sort keeps the lower id first among equal values.
+    for (int e = 0; e < E; ++e) l[e] = round_bf(l[e]);
     std::vector<int> ord(E);
     std::iota(ord.begin(), ord.end(), 0);
     std::stable_sort(ord.begin(), ord.end(), [&](int a, int b) { return l[a] > l[b]; });

@@ -25,3 +25,4 @@ def test_reference_arm_prints_one_contract_line(extra):
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["value"] == d["value"]
     assert ("sampled" in d["config"]["next_token"]) == bool(extra)
+    assert d["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))

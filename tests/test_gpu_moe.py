@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import max_rel_err, to_np_bf16, to_np_u32, topk_gap
+from gpu_util import max_rel_err, to_np_bf16, to_np_u32, topk_sure
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
@@ -36,8 +36,7 @@ def _oracle_experts(orc, table, host, x, ids, w):
 
 def _check_routing(orc, x, wr, ids, w, k, **kw):
     o_ids, o_w, o_lg = orc.router(to_np_bf16(x), to_np_bf16(wr), k, **kw)
-    gap = topk_gap(o_lg, k)
-    sure = gap > GAP
+    sure = topk_sure(o_lg, k, GAP)
     gi = ids.cpu().numpy()
     assert np.array_equal(np.sort(gi[sure], 1), np.sort(o_ids[sure], 1))
     assert np.array_equal(gi[sure], o_ids[sure])  # same order too: descending logit
@@ -79,7 +78,7 @@ def test_router_bias_norm_scales_and_4bit(fm, orc, dev):
             o = orc.router(to_np_bf16(x), to_np_u32(rp.weight), Ks, wr_bits=4, wr_s=to_np_bf16(rp.scales),
                            wr_b=to_np_bf16(rp.biases), **kw)
         o_ids, o_w, o_lg = o
-        sure = topk_gap(o_lg, Ks) > GAP
+        sure = topk_sure(o_lg, Ks, GAP)
         assert sure.mean() > 0.5
         assert np.array_equal(ids.cpu().numpy()[sure], o_ids[sure])
         assert np.abs(wt.cpu().numpy()[sure] - o_w[sure]).max() < 1e-5
@@ -106,7 +105,7 @@ def test_router_many_tokens_tensor_core(fm, orc, dev, T, Es):
                   router_scale=to_np_bf16(rscale), per_expert_scale=to_np_bf16(pes))
         o_ids, o_w, o_lg = orc.router(to_np_bf16(x), to_np_bf16(rp.weight), K, **kw)
         assert np.abs(lg.cpu().numpy() - o_lg).max() < 1e-4 * np.abs(o_lg).max()
-        sure = topk_gap(o_lg, K) > GAP
+        sure = topk_sure(o_lg, K, GAP)
         assert sure.mean() > 0.5
         assert np.array_equal(ids.cpu().numpy()[sure], o_ids[sure])
         # the tensor cores' fp32 accumulation order moves logits of magnitude ~10

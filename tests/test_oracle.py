@@ -104,10 +104,13 @@ def test_router_renormalised_topk(orc):
     wr = orc.f32_to_bf16((rng.standard_normal((16, 128)) * 0.1).astype(np.float32))
     ids, w, lg = orc.router(x, wr, 4)
     assert np.allclose(w.sum(1), 1.0, atol=1e-6)
+    # ranking and softmax see the logits rounded to bf16, the router's output
+    # dtype (moe.rs:318-330); stable argsort = ties to the lower id
+    lb = orc.bf16_to_f32(orc.f32_to_bf16(lg))
     for t in range(4):
-        order = np.argsort(-lg[t], kind="stable")[:4]
+        order = np.argsort(-lb[t], kind="stable")[:4]
         assert np.array_equal(ids[t], order)
-        p = np.exp(lg[t] - lg[t].max())
+        p = np.exp(lb[t] - lb[t].max())
         p /= p.sum()
         assert np.allclose(w[t], p[ids[t]] / p[ids[t]].sum(), rtol=1e-5)
     # per-expert scale multiplies after renormalisation (moe.rs:341-345)
