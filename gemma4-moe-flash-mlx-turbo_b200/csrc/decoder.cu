@@ -36,7 +36,7 @@ constexpr int kRowMaxPer = 16;  // hidden <= 4096
 // so a call costs one memory round trip plus three or four CTA reductions.
 constexpr int kFfThreads = 1024;
 constexpr int kFfPer = kRowThreads * kRowMaxPer / kFfThreads;  // 4: hidden <= 4096
-constexpr int kFfSlices = 4;                                   // split-K slices loaded per batch
+constexpr int kFfSlices = 8;                                   // split-K slices loaded per batch
 
 template <int NT>
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -363,7 +363,8 @@ static int dec_dims(const fmoe_decoder_layer_t* L, int* qkv_rows) {
 
 // Split-K slices a GEMV over K inputs can produce (qgemv keeps >= 8 groups of
 // 64 per column chunk).
-static int max_parts(int K) { return K / 512 > 1 ? K / 512 : 1; }
+// fp32 output slices of a decode projection over K inputs (one per 512-input chunk)
+static int max_parts(int K) { return (K + 64 * kRgChunkGroups - 1) / (64 * kRgChunkGroups); }
 
 // ep_ranks > 0: add the expert-parallel exchange buffers for ep_cap tokens per rank.
 static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, DecWs* w,
@@ -385,7 +386,7 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   carve_moe(c, T, L->router.top_k, ex, &d.mw);
   if (ep_ranks > 0) carve_ep(c, ep_ranks, ep_cap, nullptr, L->router.top_k, ex, d.h, &d.ep);
   d.attn_ws = c.take<uint8_t>(attn_workspace_bytes(kv, L->num_heads));
-  d.qkv = c.take<float>((size_t)T * qkv_rows);
+  d.qkv = c.take<float>((size_t)max_parts(L->q_proj.in_features) * T * qkv_rows);
   d.o = c.take<float>((size_t)max_parts(QD) * T * H);
   d.gu = c.take<float>((size_t)max_parts(H) * T * 2 * Id);
   d.d = c.take<float>((size_t)max_parts(Id) * T * H);
@@ -407,6 +408,18 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
 
 static QgSeg seg_of(const QW& q, void* out, int ld, int col0) {
   return QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, out, q.out, ld, col0, 0, q.tiled, q.tiled_kc};
+}
+
+static RgSeg rseg_of(const QW& q, float* out, int ld, int col0) {
+  RgSeg s = {};
+  s.w = static_cast<const uint8_t*>(q.w);
+  s.s = q.s;
+  s.b = q.b;
+  s.out = out;
+  s.rows = q.out;
+  s.ld = ld;
+  s.col0 = col0;
+  return s;
 }
 
 static int check_stream_w(const QW& q, int group, const char* what) {
@@ -494,50 +507,52 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     return dl_layer_forward(L, kv, w.dlp, w.dlw, xb, pos, pos_dev, b, st);
   }
 
-  // 1 q|k|v = input_norm(x) . W^T  (plain fp32 stores)
+  // 1 q|k|v = input_norm(x) . W^T  (fp32 slices, one per 512-input chunk)
+  int qkv_parts = 1;
   {
-    QgArgs a = {};
+    RgArgs a = {};
     a.nseg = L->k_eq_v ? 2 : 3;
-    a.seg[0] = seg_of(q, w.qkv, qkv_rows, 0);
-    a.seg[1] = seg_of(k, w.qkv, qkv_rows, QD);
-    if (!L->k_eq_v) a.seg[2] = seg_of(v, w.qkv, qkv_rows, QD + k.out);
+    a.seg[0] = rseg_of(q, w.qkv, qkv_rows, 0);
+    a.seg[1] = rseg_of(k, w.qkv, qkv_rows, QD);
+    if (!L->k_eq_v) a.seg[2] = rseg_of(v, w.qkv, qkv_rows, QD + k.out);
     a.K = H;
     a.T = Ti;
-    a.out_kind = QG_OUT_F32;
     a.in_kind = QG_IN_RMSNORM;
     a.x = xb;
     a.ldx = H;
     a.norm_w = static_cast<const bf16*>(L->input_norm);
     a.eps = L->eps;
     a.status = w.h.status;
-    QgLayout ql;
-    if ((rc = qgemv_plan(a, q.bits, false, &ql, true)) || (rc = launch_qgemv(a, ql, q.bits, true, st))) return rc;
+    RgLayout rl;
+    // the whole SM: the next kernel (q/k norms, RoPE, append) is a few CTAs
+    // that need no room beside it, and every item of the CTA fits in flight
+    if ((rc = rgemv_plan(a, q.bits, &rl, 220 * 1024)) || (rc = launch_rgemv(a, rl, q.bits, true, st))) return rc;
+    qkv_parts = a.nck;
   }
   // 2 norms, RoPE, KV append
-  if ((rc = launch_qkv_post(kv, w.qkv, qkv_rows, L->num_heads, L->k_eq_v, static_cast<const bf16*>(L->q_norm),
-                            static_cast<const bf16*>(L->k_norm), L->eps, L->rope_dims, L->rope_theta, pos, pos_dev,
-                            w.q, kv.turbo, true, st)))
+  if ((rc = launch_qkv_post(kv, w.qkv, qkv_rows, qkv_parts, (int64_t)T * qkv_rows, L->num_heads, L->k_eq_v,
+                            static_cast<const bf16*>(L->q_norm), static_cast<const bf16*>(L->k_norm), L->eps,
+                            L->rope_dims, L->rope_theta, pos, pos_dev, w.q, kv.turbo, true, st)))
     return rc;
   // 3 attention over the slots written so far (pos_dev[1] when counters live on the device)
   const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;
   if ((rc = launch_attn_decode(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
-                               w.attn_ws, w.attn, st)))
+                               w.attn_ws, w.attn, st, true)))
     return rc;
   // 4 o = attn . Wo^T
   {
-    QgArgs a = {};
+    RgArgs a = {};
     a.nseg = 1;
-    a.seg[0] = seg_of(o, w.o, H, 0);
+    a.seg[0] = rseg_of(o, w.o, H, 0);
     a.K = QD;
     a.T = Ti;
-    a.out_kind = QG_OUT_F32_PART;
     a.in_kind = QG_IN_BF16;
     a.x = w.attn;
     a.ldx = QD;
     a.status = w.h.status;
-    QgLayout ql;
-    if ((rc = qgemv_plan(a, o.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, o.bits, true, st))) return rc;
-    o_parts = a.nkc;
+    RgLayout rl;
+    if ((rc = rgemv_plan(a, o.bits, &rl)) || (rc = launch_rgemv(a, rl, o.bits, true, st))) return rc;
+    o_parts = a.nck;
   }
   // 5 residual + feed-forward input norms
   {
@@ -550,14 +565,16 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
                        static_cast<const bf16*>(L->router.router_scale), w.hres, w.h1, w.h2, w.xs);
     if ((rc = check_launch("ff_in_kernel"))) return rc;
   }
-  // fork: routed experts (7-9) on the side stream, dense MLP (6, 10) here
+  // fork: the dense MLP (6, 10) on the side stream; the router and routed
+  // experts (7-9), the longer chain, stay here, so ff_out follows the last
+  // expert kernel under programmatic dependent launch
   Branch br;
   if ((rc = branch_for_device(&br))) return rc;
   if (cudaEventRecord(br.fork, st) != cudaSuccess || cudaStreamWaitEvent(br.side, br.fork, 0) != cudaSuccess)
     return set_error(FMOE_ERR_CUDA, "decoder: fork: %s", cudaGetErrorString(cudaGetLastError()));
   // 7-9 router on the prepared input, routed experts on h2
   {
-    const cudaStream_t sx = br.side;
+    const cudaStream_t sx = st;
     fmoe_router_t r = L->router;
     r.use_norm = 0;  // ff_in applied the norm chain
     if (epc.comm) {  // routed experts on their owning ranks
@@ -569,34 +586,30 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
       if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, sx))) return rc;
       if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, sx))) return rc;
     }
-    if (cudaEventRecord(br.join, sx) != cudaSuccess)
-      return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));
   }
   // 6 dense MLP gate | up
   {
-    QgArgs a = {};
+    RgArgs a = {};
     a.nseg = 2;
-    a.seg[0] = seg_of(gq, w.gu, 2 * Id, 0);
-    a.seg[1] = seg_of(uq, w.gu, 2 * Id, Id);
+    a.seg[0] = rseg_of(gq, w.gu, 2 * Id, 0);
+    a.seg[1] = rseg_of(uq, w.gu, 2 * Id, Id);
     a.K = H;
     a.T = Ti;
-    a.out_kind = QG_OUT_F32_PART;
     a.in_kind = QG_IN_BF16;
     a.x = w.h1;
     a.ldx = H;
     a.status = w.h.status;
-    QgLayout ql;
-    if ((rc = qgemv_plan(a, gq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, gq.bits, true, st))) return rc;
-    gu_parts = a.nkc;
+    RgLayout rl;
+    if ((rc = rgemv_plan(a, gq.bits, &rl)) || (rc = launch_rgemv(a, rl, gq.bits, true, br.side))) return rc;
+    gu_parts = a.nck;
   }
   // 10 dense down on gelu(g) * u
   {
-    QgArgs a = {};
+    RgArgs a = {};
     a.nseg = 1;
-    a.seg[0] = seg_of(dq, w.d, H, 0);
+    a.seg[0] = rseg_of(dq, w.d, H, 0);
     a.K = Id;
     a.T = Ti;
-    a.out_kind = QG_OUT_F32_PART;
     a.in_kind = QG_IN_GELU;
     a.g = w.gu;
     a.u = w.gu + Id;
@@ -604,10 +617,12 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     a.gu_parts = gu_parts;
     a.gu_part_stride = (int64_t)T * 2 * Id;
     a.status = w.h.status;
-    QgLayout ql;
-    if ((rc = qgemv_plan(a, dq.bits, true, &ql, true)) || (rc = launch_qgemv(a, ql, dq.bits, true, st))) return rc;
-    d_parts = a.nkc;
+    RgLayout rl;
+    if ((rc = rgemv_plan(a, dq.bits, &rl)) || (rc = launch_rgemv(a, rl, dq.bits, true, br.side))) return rc;
+    d_parts = a.nck;
   }
+  if (cudaEventRecord(br.join, br.side) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));
   // join: ff_out needs both branches
   if (cudaStreamWaitEvent(st, br.join, 0) != cudaSuccess)
     return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));

@@ -162,6 +162,42 @@ int qgemv_chunk(int K, int bits, int64_t rows_total, bool allow_split);
 int qgemv_row_stride(int kc_bytes, int bits);
 int launch_qgemv(const QgArgs& a, const QgLayout& L, int bits, bool pdl, cudaStream_t st);
 
+// rgemv.cu: resident-weight decode GEMV (items = 16-row tile x 512-input
+// chunk, chunk-major over the CTAs; fp32 output slices out[chunk][t][ld] that
+// the consumer adds in chunk order).  Input kinds as QgArgs (QG_IN_*).
+constexpr int kRgChunkGroups = 8;  // 64-column groups per chunk
+constexpr int kRgMaxChunks = 4;    // chunks one CTA may span
+struct RgSeg {
+  const uint8_t* w;  // packed codes [rows][K*bits/8 bytes]
+  const bf16* s;     // [rows][K/64]
+  const bf16* b;
+  float* out;        // slice c, token t, row r at out[c * pstride + t * ld + col0 + r]
+  int rows, ld, col0;
+  int tile0;         // set by rgemv_plan
+  int64_t pstride;   // set by rgemv_plan: T * ld
+};
+struct RgArgs {
+  RgSeg seg[kQgMaxSeg];
+  int nseg, K, T;
+  int G, nck, tiles, items;  // set by rgemv_plan
+  int in_kind;
+  const bf16* x;       // [T][ldx] (QG_IN_BF16 / QG_IN_RMSNORM)
+  int ldx;
+  const bf16* norm_w;  // [K] (QG_IN_RMSNORM)
+  float eps;
+  const float* g;      // [T][ldgu] fp32 gate / up slices (QG_IN_GELU)
+  const float* u;
+  int ldgu;
+  int gu_parts;
+  int64_t gu_part_stride;
+  int* status;
+};
+struct RgLayout {
+  int rs, soff, stage, nst, maxch, frag, xsum, misc, normw, xs, red, bar, ring, bytes, grid;
+};
+int rgemv_plan(RgArgs& a, int bits, RgLayout* L, int smem_budget = 110 * 1024);
+int launch_rgemv(const RgArgs& a, const RgLayout& L, int bits, bool pdl, cudaStream_t st);
+
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 struct Carver;
@@ -248,7 +284,9 @@ size_t attn_workspace_bytes(const KvDev& c, int Hq);
 // kernel waits for it before reading q or the cache).
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
                        void* ws, bf16* out, cudaStream_t st, bool pdl = false);
-int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v, const bf16* q_norm,
+// qkv: fp32 projections in `parts` slices part_stride floats apart (added in order)
+int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int parts, int64_t part_stride, int Hq, int k_eq_v,
+                    const bf16* q_norm,
                     const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
                     const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st);
 

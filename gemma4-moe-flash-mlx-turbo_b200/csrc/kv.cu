@@ -100,30 +100,59 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 // MLX fast::rope, non-traditional: the first rope_dims dims rotate in pairs
 // (i, i + rope_dims/2) by angle pos * inv_freq[i].
 
+// v[i] = sum over the `parts` fp32 slices (part_stride apart, added in slice
+// order) of src[i], i < P; every slice of a batch in flight together.
 template <int P>
-__global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __restrict__ qkv, int ld, int Hq,
+__device__ __forceinline__ void sum_slices(const float* src, int parts, int64_t part_stride, float (&v)[P]) {
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] = 0.f;
+  constexpr int NB = P <= 8 ? 8 : 4;  // slices per batch
+  for (int p0 = 0; p0 < parts; p0 += NB) {
+    float w[NB][P];
+#pragma unroll
+    for (int u = 0; u < NB; ++u)
+#pragma unroll
+      for (int i = 0; i < P; ++i) w[u][i] = p0 + u < parts ? __ldcg(src + (p0 + u) * part_stride + i) : 0.f;
+#pragma unroll
+    for (int u = 0; u < NB; ++u)
+      if (p0 + u < parts)
+#pragma unroll
+        for (int i = 0; i < P; ++i) v[i] += w[u][i];
+  }
+}
+
+template <int P>
+__global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __restrict__ qkv, int ld, int parts,
+                                                       int64_t part_stride, int Hq,
                                                        int k_eq_v, const bf16* __restrict__ q_norm,
                                                        const bf16* __restrict__ k_norm, float eps, int rope_dims,
                                                        float log2_theta, int64_t pos,
                                                        const int64_t* __restrict__ pos_dev, bf16* __restrict__ q_out,
                                                        int turbo_bits, float inv_sqrt_d) {
   constexpr int D = 32 * P, G = D / 64;
-  griddep_wait();  // the projections come from the preceding kernel
-  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int Hkv = c.Hkv, T = c.B;  // one token per sequence
-  if (row >= T * (Hq + Hkv)) return;
+  const bool is_q = row < T * Hq;
+  // Before the dependency wait, what does not depend on the projections: the
+  // norm weights and the RoPE cos / sin of this step's position.  The device
+  // position is written at least two kernels earlier in the stream (before
+  // the preceding kernel's own wait), so it is final here.
   const int64_t p0 = pos_dev ? *pos_dev : pos;
-  const float fpos = (float)p0;
+  float nwv[P], cs[P], sn[P];
+  load_norm_w<P>(is_q ? q_norm : k_norm, lane, nwv);
+  rope_angles<P>(rope_dims, log2_theta, (float)p0, lane, cs, sn);
+  griddep_wait();  // the projections come from the preceding kernel
+  griddep_launch_dependents();
+  if (row >= T * (Hq + Hkv)) return;
   float v[P];
-  if (row < T * Hq) {
+  if (is_q) {
     const int t = row / Hq, h = row % Hq;
-    const float* src = qkv + (int64_t)t * ld + h * D + lane * P;
+    sum_slices<P>(qkv + (int64_t)t * ld + h * D + lane * P, parts, part_stride, v);
 #pragma unroll
-    for (int i = 0; i < P; ++i) v[i] = round_bf(__ldcg(src + i));
-    warp_rms_norm<P>(v, q_norm, eps, lane);
-    warp_rope<P>(v, rope_dims, log2_theta, fpos, lane);
+    for (int i = 0; i < P; ++i) v[i] = round_bf(v[i]);
+    warp_rms_norm_w<P>(v, nwv, q_norm != nullptr, eps, lane);
+    warp_rope_cs<P>(v, rope_dims, cs, sn, lane);
     store_row_bf16<P>(q_out + ((int64_t)t * Hq + h) * D, lane, v);
     return;
   }
@@ -131,14 +160,16 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __r
   const float* ks = qkv + (int64_t)t * ld + (Hq + hk) * D + lane * P;
   const float* vs = k_eq_v ? ks : qkv + (int64_t)t * ld + (Hq + Hkv + hk) * D + lane * P;
   float kv[P], vv[P];
+  sum_slices<P>(ks, parts, part_stride, kv);
+  sum_slices<P>(vs, parts, part_stride, vv);
 #pragma unroll
   for (int i = 0; i < P; ++i) {
-    kv[i] = round_bf(__ldcg(ks + i));
-    vv[i] = round_bf(__ldcg(vs + i));
+    kv[i] = round_bf(kv[i]);
+    vv[i] = round_bf(vv[i]);
   }
   warp_rms_norm<P>(vv, nullptr, eps, lane);  // v_norm: no learned scale
-  warp_rms_norm<P>(kv, k_norm, eps, lane);
-  warp_rope<P>(kv, rope_dims, log2_theta, fpos, lane);
+  warp_rms_norm_w<P>(kv, nwv, k_norm != nullptr, eps, lane);
+  warp_rope_cs<P>(kv, rope_dims, cs, sn, lane);
   const int64_t dst = ((int64_t)t * Hkv + hk) * c.cap + p0 % c.cap;
   if (c.mode == FMOE_KV_BF16) {
     if (turbo_bits) {
@@ -1034,7 +1065,8 @@ int launch_kv_append(const KvDev& c, const bf16* k, const bf16* v, int64_t Tn, i
   return check_launch("kv_append_kernel");
 }
 
-int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v, const bf16* q_norm,
+int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int parts, int64_t part_stride, int Hq, int k_eq_v,
+                    const bf16* q_norm,
                     const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
                     const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st) {
   const float l2t = (float)std::log2((double)rope_theta);
@@ -1051,11 +1083,11 @@ int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int Hq, int k_eq_v
   cfg.numAttrs = pdl ? 1 : 0;
   ProfScope prof_("qkv_post_kernel", st);
   if (c.D == 256)
-    cudaLaunchKernelEx(&cfg, qkv_post_kernel<8>, c, qkv, ld, Hq, k_eq_v, q_norm, k_norm, eps, rope_dims, l2t, pos,
-                       pos_dev, q_out, turbo_bits, inv);
+    cudaLaunchKernelEx(&cfg, qkv_post_kernel<8>, c, qkv, ld, parts, part_stride, Hq, k_eq_v, q_norm, k_norm, eps,
+                       rope_dims, l2t, pos, pos_dev, q_out, turbo_bits, inv);
   else
-    cudaLaunchKernelEx(&cfg, qkv_post_kernel<16>, c, qkv, ld, Hq, k_eq_v, q_norm, k_norm, eps, rope_dims, l2t,
-                       pos, pos_dev, q_out, turbo_bits, inv);
+    cudaLaunchKernelEx(&cfg, qkv_post_kernel<16>, c, qkv, ld, parts, part_stride, Hq, k_eq_v, q_norm, k_norm, eps,
+                       rope_dims, l2t, pos, pos_dev, q_out, turbo_bits, inv);
   return check_launch("qkv_post_kernel");
 }
 

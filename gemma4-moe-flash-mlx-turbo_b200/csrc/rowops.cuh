@@ -69,4 +69,61 @@ __device__ __forceinline__ void warp_rope(float (&v)[P], int rope_dims, float lo
   for (int i = 0; i < P; ++i) v[i] = o[i];
 }
 
+// The same two steps split so that everything independent of the row can run
+// early (before a programmatic-dependent wait): the norm weights as floats
+// (1 when w is null) and the lane's RoPE cos / sin.
+template <int P>
+__device__ __forceinline__ void load_norm_w(const bf16* w, int lane, float (&wv)[P]) {
+  if (w) {
+    load_row_f32<P>(w, lane, wv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < P; ++i) wv[i] = 1.f;
+  }
+}
+template <int P>
+__device__ __forceinline__ void warp_rms_norm_w(float (&v)[P], const float (&wv)[P], bool has_w, float eps, int lane) {
+  constexpr int D = 32 * P;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < P; ++i) ss = fmaf(v[i], v[i], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] = round_bf(has_w ? v[i] * r * wv[i] : v[i] * r);
+}
+template <int P>
+__device__ __forceinline__ void rope_angles(int rope_dims, float log2_theta, float pos, int lane, float (&cs)[P],
+                                            float (&sn)[P]) {
+  const int half = rope_dims / 2;
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const int e = lane * P + i;
+    cs[i] = 1.f;
+    sn[i] = 0.f;
+    if (e < rope_dims) {
+      const int j = e < half ? e : e - half;
+      sincosf(pos * exp2f(-(float)(2 * j) / (float)rope_dims * log2_theta), &sn[i], &cs[i]);
+    }
+  }
+}
+template <int P>
+__device__ __forceinline__ void warp_rope_cs(float (&v)[P], int rope_dims, const float (&cs)[P], const float (&sn)[P],
+                                             int lane) {
+  const int half = rope_dims / 2;
+  const int ofs = half / P;
+  float o[P];
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    const float up = __shfl_down_sync(0xffffffffu, v[i], ofs & 31);
+    const float dn = __shfl_up_sync(0xffffffffu, v[i], ofs & 31);
+    const int e = lane * P + i;
+    o[i] = v[i];
+    if (e < rope_dims) o[i] = e < half ? round_bf(v[i] * cs[i] - up * sn[i]) : round_bf(dn * sn[i] + v[i] * cs[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] = o[i];
+}
+
 }  // namespace fmoe
