@@ -537,7 +537,7 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
   // 3 attention over the slots written so far (pos_dev[1] when counters live on the device)
   const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;
   if ((rc = launch_attn_decode(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
-                               w.attn_ws, w.attn, st, true)))
+                               w.attn_ws, w.attn, st, true, pos, pos_dev)))
     return rc;
   // 4 o = attn . Wo^T
   {

@@ -1744,7 +1744,7 @@ int dl_layer_forward(const fmoe_decoder_layer_t* L, const KvDev& kv, const DlPla
   {
     const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;
     if ((rc = launch_attn_decode(kv, b.q, p.Hq, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale, b.attn_ws,
-                                 b.attn, st, true)))
+                                 b.attn, st, true, pos, pos_dev)))
       return rc;
   }
   // 3 o + feed-forward input norms

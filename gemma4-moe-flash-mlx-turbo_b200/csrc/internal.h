@@ -281,9 +281,12 @@ int ep_experts(const fmoe_ep_comm_t* c, const bf16* x, int64_t T, int64_t cap, i
 int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d);
 size_t attn_workspace_bytes(const KvDev& c, int Hq);
 // pdl: launched as a programmatic dependent of the preceding kernel (the
-// kernel waits for it before reading q or the cache).
+// kernel waits for it before reading q or the newest cache row).  newest /
+// newest_dev: the position whose row the preceding kernel appended (its slot
+// is newest % cap; -1: none): every other chunk is copied before the wait.
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
-                       void* ws, bf16* out, cudaStream_t st, bool pdl = false);
+                       void* ws, bf16* out, cudaStream_t st, bool pdl = false, int64_t newest = -1,
+                       const int64_t* newest_dev = nullptr);
 // qkv: fp32 projections in `parts` slices part_stride floats apart (added in order)
 int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int parts, int64_t part_stride, int Hq, int k_eq_v,
                     const bf16* q_norm,

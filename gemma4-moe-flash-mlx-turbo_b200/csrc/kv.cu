@@ -101,23 +101,31 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 // (i, i + rope_dims/2) by angle pos * inv_freq[i].
 
 // v[i] = sum over the `parts` fp32 slices (part_stride apart, added in slice
-// order) of src[i], i < P; every slice of a batch in flight together.
+// order) of src[i], i < P (src 16-byte aligned); every slice of a batch in
+// flight together.
 template <int P>
 __device__ __forceinline__ void sum_slices(const float* src, int parts, int64_t part_stride, float (&v)[P]) {
 #pragma unroll
   for (int i = 0; i < P; ++i) v[i] = 0.f;
   constexpr int NB = P <= 8 ? 8 : 4;  // slices per batch
   for (int p0 = 0; p0 < parts; p0 += NB) {
-    float w[NB][P];
+    float4 w[NB][P / 4];  // the lane's P contiguous floats as 16-byte loads (coalesced)
 #pragma unroll
     for (int u = 0; u < NB; ++u)
 #pragma unroll
-      for (int i = 0; i < P; ++i) w[u][i] = p0 + u < parts ? __ldcg(src + (p0 + u) * part_stride + i) : 0.f;
+      for (int i = 0; i < P / 4; ++i)
+        w[u][i] = p0 + u < parts ? __ldcg(reinterpret_cast<const float4*>(src + (p0 + u) * part_stride) + i)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int u = 0; u < NB; ++u)
       if (p0 + u < parts)
 #pragma unroll
-        for (int i = 0; i < P; ++i) v[i] += w[u][i];
+        for (int i = 0; i < P / 4; ++i) {
+          v[4 * i] += w[u][i].x;
+          v[4 * i + 1] += w[u][i].y;
+          v[4 * i + 2] += w[u][i].z;
+          v[4 * i + 3] += w[u][i].w;
+        }
   }
 }
 
@@ -433,14 +441,15 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     attn_affine_kernel(const KvDev c, const bf16* __restrict__ q, int Hq, int S, int nsplit, int64_t nvalid,
                        const int64_t* __restrict__ nvalid_dev, float scale, float inv_sqrt_d,
                        float2* __restrict__ part_ml, float* __restrict__ part_o, unsigned* __restrict__ ctr,
-                       bf16* __restrict__ out, int* __restrict__ status) {
+                       bf16* __restrict__ out, int* __restrict__ status, int64_t newest,
+                     const int64_t* __restrict__ newest_dev) {
   using C = AtCfg<P, FMOE_KV_AFFINE>;
   using Sm = AffSmem<P, GQ>;
-  // launched as a programmatic dependent: q and the newest cache rows come
-  // from the preceding kernel (a no-op otherwise); the next kernel may start
-  // streaming its weights meanwhile
-  griddep_wait();
-  griddep_launch_dependents();
+  // Launched as a programmatic dependent, q and the newest cache rows come
+  // from the preceding kernel: every chunk but the one holding the row
+  // appended at position `newest` (slot newest % cap; -1: none) is copied
+  // before the dependency wait.  The position and slot count are written at
+  // least two kernels earlier in the stream, so they are final here.
   constexpr int D = C::D, G = C::G, CH = C::CH, NST = C::NST, TPC = C::TPC, WPT = C::WPT, GPW = C::GPW;
   static_assert(GPW == 4, "a scale row of a warp's groups is one 8-byte load");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -476,9 +485,17 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     flags[tid] = 0;
   }
   __syncthreads();
+  int64_t pn = newest;
+  if (newest_dev) pn = *newest_dev;
+  const int64_t slot_new = pn >= 0 ? pn % c.cap : -1;
+  const int chn_new = slot_new >= p_begin && slot_new < p_begin + nS ? (int)((slot_new - p_begin) / CH) : -1;
   int issued = 0;  // meaningful in thread 0 only
   if (tid == 0)
-    for (; issued < min(NST, nch); ++issued) issue_chunk<C, FMOE_KV_AFFINE>(smem, bar, src, issued, nS);
+    for (; issued < min(NST, nch); ++issued)
+      if (issued != chn_new) issue_chunk<C, FMOE_KV_AFFINE>(smem, bar, src, issued, nS);
+  griddep_wait();
+  griddep_launch_dependents();
+  if (tid == 0 && chn_new >= 0 && chn_new < min(NST, nch)) issue_chunk<C, FMOE_KV_AFFINE>(smem, bar, src, chn_new, nS);
 
   // rotated query rows (hi / lo bf16 parts) and their group sums
   if (warp < GQ) {
@@ -789,14 +806,15 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     attn_bf16_kernel(const KvDev c, const bf16* __restrict__ q, int Hq, int S, int nsplit, int64_t nvalid,
                      const int64_t* __restrict__ nvalid_dev, float scale, float inv_sqrt_d,
                      float2* __restrict__ part_ml, float* __restrict__ part_o, unsigned* __restrict__ ctr,
-                     bf16* __restrict__ out, int* __restrict__ status) {
+                     bf16* __restrict__ out, int* __restrict__ status, int64_t newest,
+                     const int64_t* __restrict__ newest_dev) {
   using C = AtCfg<P, FMOE_KV_BF16>;
   using Sm = Bf16Smem<P, GQ>;
-  // launched as a programmatic dependent: q and the newest cache rows come
-  // from the preceding kernel (a no-op otherwise); the next kernel may start
-  // streaming its weights meanwhile
-  griddep_wait();
-  griddep_launch_dependents();
+  // Launched as a programmatic dependent, q and the newest cache rows come
+  // from the preceding kernel: every chunk but the one holding the row
+  // appended at position `newest` (slot newest % cap; -1: none) is copied
+  // before the dependency wait.  The position and slot count are written at
+  // least two kernels earlier in the stream, so they are final here.
   constexpr int D = C::D, CH = C::CH, NST = C::NST;
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Sm::BAR);
@@ -830,9 +848,17 @@ __global__ void __launch_bounds__(256, GQ >= 8 ? 1 : 2)
     flags[tid] = 0;
   }
   __syncthreads();
-  int issued = 0;
+  int64_t pn = newest;
+  if (newest_dev) pn = *newest_dev;
+  const int64_t slot_new = pn >= 0 ? pn % c.cap : -1;
+  const int chn_new = slot_new >= p_begin && slot_new < p_begin + nS ? (int)((slot_new - p_begin) / CH) : -1;
+  int issued = 0;  // meaningful in thread 0 only
   if (tid == 0)
-    for (; issued < min(NST, nch); ++issued) issue_chunk<C, FMOE_KV_BF16>(smem, bar, src, issued, nS);
+    for (; issued < min(NST, nch); ++issued)
+      if (issued != chn_new) issue_chunk<C, FMOE_KV_BF16>(smem, bar, src, issued, nS);
+  griddep_wait();
+  griddep_launch_dependents();
+  if (tid == 0 && chn_new >= 0 && chn_new < min(NST, nch)) issue_chunk<C, FMOE_KV_BF16>(smem, bar, src, chn_new, nS);
   if (warp < GQ) {
     float v[P];
     load_row_f32<P>(q + ((int64_t)b * Hq + hk * GQ + warp) * D, lane, v);
@@ -1106,7 +1132,7 @@ int launch_turbo_round_trip(const bf16* x, int64_t rows, int D, int bits, bf16* 
 template <int P, int MODE, int GQ>
 static int launch_attn_t(const KvDev& c, const bf16* q, int Hq, const AttnPlan& p, int64_t nvalid,
                          const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st,
-                         bool pdl) {
+                         bool pdl, int64_t newest, const int64_t* newest_dev) {
   constexpr bool aff = MODE == FMOE_KV_AFFINE;
   constexpr int bytes = aff ? AffSmem<P, GQ>::BYTES : Bf16Smem<P, GQ>::BYTES;
   auto kern = aff ? attn_affine_kernel<P, GQ> : attn_bf16_kernel<P, GQ>;
@@ -1130,35 +1156,43 @@ static int launch_attn_t(const KvDev& c, const bf16* q, int Hq, const AttnPlan& 
   cfg.numAttrs = pdl ? 1 : 0;
   ProfScope prof_(aff ? "attn_affine_kernel" : "attn_bf16_kernel", st);
   cudaLaunchKernelEx(&cfg, kern, c, q, Hq, p.S, p.nsplit, nvalid, nvalid_dev, scale, inv, w.ml, w.po, w.ctr, out,
-                     w.status);
+                     w.status, newest, newest_dev);
   return check_launch("attn_decode kernel");
 }
 
 template <int P, int MODE>
 static int launch_attn_m(const KvDev& c, int GQ, const bf16* q, int Hq, const AttnPlan& p, int64_t nvalid,
                          const int64_t* nvalid_dev, float scale, const AttnWs& w, bf16* out, cudaStream_t st,
-                         bool pdl) {
+                         bool pdl, int64_t newest, const int64_t* newest_dev) {
   switch (GQ) {
-    case 1: return launch_attn_t<P, MODE, 1>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
-    case 2: return launch_attn_t<P, MODE, 2>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
-    case 4: return launch_attn_t<P, MODE, 4>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
-    case 8: return launch_attn_t<P, MODE, 8>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl);
+    case 1: return launch_attn_t<P, MODE, 1>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                  newest_dev);
+    case 2: return launch_attn_t<P, MODE, 2>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                  newest_dev);
+    case 4: return launch_attn_t<P, MODE, 4>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                  newest_dev);
+    case 8: return launch_attn_t<P, MODE, 8>(c, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                  newest_dev);
   }
   return set_error(FMOE_ERR_UNSUPPORTED, "attn_decode: %d query heads per kv head (kernels: 1, 2, 4, 8)", GQ);
 }
 
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
-                       void* ws, bf16* out, cudaStream_t st, bool pdl) {
+                       void* ws, bf16* out, cudaStream_t st, bool pdl, int64_t newest, const int64_t* newest_dev) {
   const AttnPlan p = attn_plan(c, nvalid_dev ? c.cap : nvalid, Hq);
   const AttnWs w = carve_attn_ws(ws, c, Hq, p.nsplit);
   const int GQ = Hq / c.Hkv;
   if (c.D == 256)
-    return c.mode == FMOE_KV_BF16 ? launch_attn_m<8, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl)
-                                  : launch_attn_m<8, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out,
-                                                                     st, pdl);
-  return c.mode == FMOE_KV_BF16 ? launch_attn_m<16, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl)
-                                : launch_attn_m<16, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out,
-                                                                    st, pdl);
+    return c.mode == FMOE_KV_BF16
+               ? launch_attn_m<8, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                newest_dev)
+               : launch_attn_m<8, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                  newest_dev);
+  return c.mode == FMOE_KV_BF16
+             ? launch_attn_m<16, FMOE_KV_BF16>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                               newest_dev)
+             : launch_attn_m<16, FMOE_KV_AFFINE>(c, GQ, q, Hq, p, nvalid, nvalid_dev, scale, w, out, st, pdl, newest,
+                                                 newest_dev);
 }
 
 }  // namespace fmoe
