@@ -425,8 +425,9 @@ def run_decoder(args, rank, world, local):
 
     # roofline of the dominant kernel (most device time per step)
     name, (n_l, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
-    by_kernel = {"qgemv_kernel<8>": parts["attention"], "qgemv_kernel<4>": parts["dense"],
-                 "qgemv_kernel<6>": parts["lm_head"], "attn_bf16_kernel": parts["kv"],
+    by_kernel = {"rgemv_kernel<8>": parts["attention"], "rgemv_kernel<4>": parts["dense"],
+                 "qgemv_kernel<8>": parts["attention"], "qgemv_kernel<4>": parts["dense"],
+                 "dl_lm_kernel": parts["lm_head"], "qgemv_kernel<6>": parts["lm_head"], "attn_bf16_kernel": parts["kv"],
                  "moe_gate_up_kernel": parts["experts"] * 2 / 3, "moe_down_kernel": parts["experts"] / 3}
     alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
