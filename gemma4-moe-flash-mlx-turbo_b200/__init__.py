@@ -122,6 +122,7 @@ SIGNATURES = {
     "fmoe_version": (_I, []),
     "fmoe_last_error": (_I, [ctypes.c_char_p, _SZ]),
     "fmoe_workspace_status": (_I, [_P, _I, _P]),
+    "fmoe_wait_selftest": (_I, [_P, _SZ, _I, _P]),
     "fmoe_moe_block_forward_noalloc": (
         _I,
         [_P, _I64, ctypes.POINTER(RouterC), ctypes.POINTER(ExpertsC), _P, _P, _P, _P],

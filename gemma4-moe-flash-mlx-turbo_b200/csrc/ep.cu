@@ -566,6 +566,23 @@ using namespace fmoe;
 
 extern "C" {
 
+int fmoe_wait_selftest(void* workspace, size_t workspace_bytes, int flag_value, void* stream) {
+  if (!workspace || workspace_bytes < 512 || !aligned(workspace, 16))
+    return set_error(FMOE_ERR_WORKSPACE, "wait_selftest: workspace needs 512 bytes, 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  // [0, 256): header (status word); 256: exchange sequence word (0); 272: the flag
+  if (cudaMemsetAsync(w, 0, 512, st) != cudaSuccess ||
+      (flag_value && cudaMemsetAsync(w + 272, 1, 1, st) != cudaSuccess))
+    return set_error(FMOE_ERR_CUDA, "wait_selftest: %s", cudaGetErrorString(cudaGetLastError()));
+  {
+    ProfScope prof_("p2p_wait_kernel", st);
+    ep::p2p_wait_kernel<<<1, 32, 0, st>>>(w, 272, 1, reinterpret_cast<uint32_t*>(w + 256), 0,
+                                          reinterpret_cast<int*>(w), 99);
+  }
+  return check_launch("p2p_wait_kernel");
+}
+
 int fmoe_ep_unique_id(void* id, size_t len) {
   const ep::NcclApi* api = ep::nccl();
   if (!api) return set_error(FMOE_ERR_NCCL, "ep: libnccl.so.2 not found");

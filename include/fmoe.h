@@ -491,6 +491,15 @@ int fmoe_decode_step(const fmoe_decode_model_t* model, int32_t* tokens, float* l
  * gave up (fmoe_last_error names the site); clear != 0 resets the word. */
 int fmoe_workspace_status(const void* workspace, int clear, void* stream);
 
+/* Self-test of the bounded device waits (no counterpart in the reference):
+ * runs the expert-parallel exchange's flag wait (a few hundred milliseconds of
+ * polling at most) on a flag in `workspace` (>= 512 bytes, 16-byte aligned,
+ * its header cleared here) that holds `flag_value` (0: nothing ever sets it,
+ * so the wait runs out; 1: it is already set).  Returns the launch status; a
+ * following fmoe_workspace_status reports FMOE_ERR_TIMEOUT after a wait that
+ * ran out, FMOE_OK otherwise, and the context stays usable either way. */
+int fmoe_wait_selftest(void* workspace, size_t workspace_bytes, int flag_value, void* stream);
+
 /* ---- next-token sampling on the device (the engine's sample(), src/engine.rs:302-355) ----
  * logits: [rows, vocab] fp32 on the device (fmoe_lm_head's output).  Per row:
  *   repetition penalty (rep_penalty > 1 and n_recent > 0): every distinct token of

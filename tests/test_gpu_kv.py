@@ -184,16 +184,33 @@ def test_turbo_round_trip_matches_oracle(fm, orc, dev, D, bits):
     got = fm.turbo_round_trip(x, bits)
     torch.cuda.synchronize()
     want, _, _ = orc.turbo_round_trip(to_np_bf16(x), bits)
-    g = got.float().cpu().numpy()
-    w = orc.bf16_to_f32(want)
-    # Codebook indices come from an fp32 butterfly here and a double matmul in
-    # the oracle; a value within rounding of a Lloyd-Max boundary may pick the
-    # neighbouring centroid, which moves that whole row slightly.  Rows whose
-    # indices agree match to bf16 rounding; require that of >= 98% of rows and
-    # bound every row.
+    g = got.float().cpu().numpy().astype(np.float64)
+    w = orc.bf16_to_f32(want).astype(np.float64)
+    _, idx_o, nrm = orc.turbo_round_trip(to_np_bf16(x), bits)
+    # The codebook index of each rotated value comes from an fp32 butterfly
+    # here and a double-precision matmul in the oracle, so a value within
+    # rounding of a Lloyd-Max boundary may take the neighbouring centroid; one
+    # such index moves its whole row (the inverse rotation spreads it).  Undo
+    # the rotation of the GPU rows to recover their indices and require:
+    # every index equal to the oracle's or its neighbour, every differing one
+    # sitting on a boundary (within fp32 rounding of the rotated value), and
+    # rows with equal indices equal to bf16 rounding.
+    Hm = orc.hadamard(D).astype(np.float64)
+    sg = orc.signs(D).astype(np.float64)
+    cent, bnd = orc.lloyd_max(bits)
+    xin = orc.bf16_to_f32(to_np_bf16(x)).astype(np.float64)
+    n = nrm.astype(np.float64)[:, None]
+    y_o = np.sqrt(D) * sg * ((xin / (n + 1e-8)) @ Hm)             # the oracle's rotated values
+    vals_g = sg * (g @ Hm) / n * np.sqrt(D)                          # the GPU rows' centroids
+    idx_g = np.abs(vals_g[:, :, None] - cent[None, None, :].astype(np.float64)).argmin(2)
+    diff = idx_g != idx_o
+    assert (np.abs(idx_g - idx_o.astype(np.int64)) <= 1).all()
+    lo = np.minimum(idx_g, idx_o)[diff]
+    assert (np.abs(y_o[diff] - bnd.astype(np.float64)[lo]) <= 1e-4 * np.maximum(1.0, np.abs(y_o[diff]))).all()
+    assert diff.mean() <= 1e-3, diff.mean()
     row_err = np.abs(g - w).max(1) / np.maximum(np.abs(w).max(1), 1e-30)
-    assert (row_err <= 2e-3).mean() >= 0.98, np.sort(row_err)[-8:]
-    assert row_err.max() <= 0.1
+    same = ~diff.any(1)
+    assert (row_err[same] <= 2e-3).all(), np.sort(row_err[same])[-4:]
 
 
 def test_append_turbo_stores_round_trip(fm, dev):
@@ -215,3 +232,53 @@ def test_bad_arguments_raise(fm, dev):
         cache.attend(query(1, 24, 256, 1, dev))  # 3 query heads per kv head
     with pytest.raises(ValueError):
         fm.KVCache.new(1, 8, 128, 64, device=dev)  # head_dim 128 not compiled
+
+
+# BASELINE config 3 at its own shapes: 16 query heads, 8 kv heads, head_dim 256,
+# contexts 8192 / 32768, batch 32 (and 1), a sliding window of 1024 on local
+# layers; K / V N(0,1) with 1 % outlier channels x20.  The whole batch runs on
+# the GPU; the oracle checks three of the sequences (first, middle, last) on
+# the same stored K / V.
+CONFIG3 = [
+    # cache, batch, positions appended, window
+    ("affine", 32, 8192, None),
+    ("affine", 32, 32768, None),
+    ("affine", 32, 32768, 1024),
+    ("affine", 1, 32768, None),
+    ("bf16", 32, 8192, None),
+    ("bf16", 32, 32768, 1024),
+]
+
+
+@pytest.mark.parametrize("mode,B,ctx,window", CONFIG3)
+def test_attn_config3_shapes(fm, orc, dev, mode, B, ctx, window):
+    D, Hq, Hkv, scale = 256, 16, 8, 0.0625
+    cap = window or ctx
+    if mode == "affine":
+        cache = fm.KVCache.new_affine(B, Hkv, D, ctx, window=window, device=dev)
+    else:
+        cache = fm.KVCache(B, Hkv, D, ctx, window=window, device=dev)
+    step = 2048 if B > 1 else 8192  # appended in chunks (bounded staging memory)
+    for p0 in range(0, ctx, step):
+        n = min(step, ctx - p0)
+        cache.update(kv_rows(B, Hkv, n, D, 1000 + p0, dev), kv_rows(B, Hkv, n, D, 2000 + p0, dev))
+    assert cache.stored_len() == cap
+    q = query(B, Hq, D, 77, dev)
+    out = cache.attend(q, scale)
+    torch.cuda.synchronize()
+    assert cache.status() == 0
+    sel = sorted({0, B // 2, B - 1})
+    a = cache.arrays()
+    qs = to_np_bf16(q[sel])
+    lo = np.zeros(len(sel), np.int32)
+    hi = np.full(len(sel), cap, np.int32)
+    if mode == "affine":
+        want = orc.attn_decode_affine(qs, Hkv, cache.capacity, lo, hi, to_np_u32(a["k"][sel]),
+                                      to_np_bf16(a["k_scales"][sel]), to_np_bf16(a["k_biases"][sel]), 4,
+                                      to_np_u32(a["v"][sel]), to_np_bf16(a["v_scales"][sel]),
+                                      to_np_bf16(a["v_biases"][sel]), 8, scale)
+    else:
+        want = orc.attn_decode_bf16(qs, Hkv, cache.capacity, lo, hi, to_np_bf16(a["k"][sel]), to_np_bf16(a["v"][sel]),
+                                    scale)
+    err = max_rel_err(out[sel].float().cpu().numpy(), want)
+    assert err <= TOL, err
