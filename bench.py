@@ -43,7 +43,7 @@ H, I, E, K, LAYERS = 2816, 704, 128, 8, 30
 ROUTER_BYTES = E * H * 2                                   # bf16 router weight per layer
 GATE_UP_BYTES = 2 * (I * H // 2 + 2 * I * (H // 64) * 2)   # per selected expert: 2,230,272
 DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert: 1,115,136
-WORKLOADS = {"decode30_b1": 1, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
+WORKLOADS = {"decode30_b1": 1, "decode30_b32": 32, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
 # total tokens per step (split evenly over the GPUs), default exchange mode
 EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "fixed"), "ep_moe30_prefill_8192": (8192, "exact")}
 # config 5 measured inside a multi-GPU decode30 run (workload, exchange mode)
@@ -238,7 +238,9 @@ def decoder_step_bytes(m, T, ctx):
         per["dense"] += sum(qlin_bytes(q) for q in L.mlp)
         w = L.router["proj"].weight
         per["router"] += w.numel() * w.element_size()
-        per["experts"] += min(T * K, E) * EXPERT_BYTES
+        # distinct experts a step reads: 8 at T = 1; for T > 1 the expectation
+        # under uniform routing, E (1 - (1 - K/E)^T) (112.6 of 128 at T = 32)
+        per["experts"] += (K if T == 1 else E * (1.0 - (1.0 - K / E) ** T)) * EXPERT_BYTES
         n = min(ctx + 1, c.capacity)
         per["kv"] += T * L.num_kv_heads * L.head_dim * 2 * 2 * (n + 1)
     per["lm_head"] = qlin_bytes(m.embed) + T * qlin_bytes(m.embed) // m.embed.out_features
@@ -246,6 +248,11 @@ def decoder_step_bytes(m, T, ctx):
 
 
 DECODER_METRIC = "decode tok/s, batch 1 (30-layer Gemma-4 26B-A4B-shaped decoder, full step incl. lm_head)"
+
+
+def decoder_metric(args):
+    T = WORKLOADS[args.workload]
+    return DECODER_METRIC if T == 1 else DECODER_METRIC.replace("batch 1", f"batch {T}")
 MOE_METRIC = "decode tok/s (routed-expert path of the 30-layer Gemma-4 26B-A4B-shaped decoder)"
 
 
@@ -432,7 +439,7 @@ def run_decoder(args, rank, world, local):
     alg = by_kernel[name] / (n_l / nprof) if name in by_kernel else None
     achieved = alg / (tot_ms / n_l / 1e3) / 1e9 if alg else None
     result = {
-        "metric": DECODER_METRIC,
+        "metric": decoder_metric(args),
         "value": round(value, 2),
         "unit": "tok/s",
         "n_gpus": world,
@@ -983,7 +990,7 @@ def cpu_baseline(_layers, T, budget_s=15.0):
                       f"per step"}
 
 
-def cpu_decoder_sample(seed=4000):
+def cpu_decoder_sample(seed=4000, T=1):
     """Numpy weights for the oracle's decoder layer (one sliding, one full) and
     the 6-bit lm_head at the model's shapes.  The CPU time does not depend on
     the code values, so uniform random codes with small bf16 scales stand in."""
@@ -1015,24 +1022,24 @@ def cpu_decoder_sample(seed=4000):
                   "post_ff_norm_2", "post_ff_norm"):
             L[k] = nrm(H)
         cap = CTX + 16 if full else 1024
-        ck = oracle.f32_to_bf16(rng.standard_normal((1, Hkv, cap, D)).astype(np.float32))
+        ck = oracle.f32_to_bf16(rng.standard_normal((T, Hkv, cap, D)).astype(np.float32))
         cfg = {"heads": Hq, "kv_heads": Hkv, "head_dim": D, "rope_dims": 128 if full else 256,
                "rope_theta": 1e6 if full else 1e4, "eps": 1e-6, "k_eq_v": full, "scalar": 1.0, "attn_scale": 1.0,
                "top_k": K, "hidden": H, "inter_expert": I}
         layers.append((L, ck, ck.copy(), cfg))
     embed = ql(262144, H, 6)
-    x = oracle.f32_to_bf16(rng.standard_normal((1, H)).astype(np.float32))
+    x = oracle.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
     return layers, embed, nrm(H), x
 
 
-def cpu_sampler_setup(vocab=262144, seed=1):
+def cpu_sampler_setup(vocab=262144, seed=1, T=1):
     import numpy as np
     rng = np.random.default_rng(seed)
-    return rng.integers(0, vocab, (1, 64)).astype(np.int32)
+    return rng.integers(0, vocab, (T, 64)).astype(np.int32)
 
 
 def cpu_decoder_step(sample, step, recent=None):
-    """One whole decode step of one token on the oracle: the 30 layers in the
+    """One whole decode step (one token per sequence of the sample) on the oracle: the 30 layers in the
     model's order (every fifth one full attention, the rest sliding), the
     final norm + tied lm_head with softcap and argmax, and — with `recent` —
     the sampler at the generate defaults (temperature 0.7, top_p 0.9,
@@ -1054,18 +1061,32 @@ def cpu_decoder_step(sample, step, recent=None):
 def cpu_decoder_baseline(T, budget_s=15.0, sampled=False):
     """decode30: whole decode steps on the oracle for about budget_s (at least one)."""
     cores = oracle_all_cores()
-    sample = cpu_decoder_sample()
-    recent = cpu_sampler_setup() if sampled else None
+    Ts = cpu_decoder_tokens(T, budget_s, 2)
+    sample = cpu_decoder_sample(T=Ts)
+    recent = cpu_sampler_setup(T=Ts) if sampled else None
     cpu_decoder_step(sample, 0, recent)
     n, t0 = 0, time.perf_counter()
     while n < 1 or time.perf_counter() - t0 < budget_s:
         cpu_decoder_step(sample, n, recent)
         n += 1
     step_s = (time.perf_counter() - t0) / n
-    return {"value": round(T / step_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
-            "sample": f"{n} whole decode steps of one token at context {CTX} on the oracle (C++ OpenMP / numpy): "
-                      f"24 sliding + 6 full layers + lm_head" + (" + the sampler" if sampled else "")
-                      + f", {step_s * 1e3:.1f} ms per step"}
+    return {"value": round(Ts / step_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} whole decode steps of {Ts} of the workload's {T} sequences at context {CTX} on the "
+                      f"oracle (C++ OpenMP / numpy): 24 sliding + 6 full layers + lm_head"
+                      + (" + the sampler" if sampled else "") + f", {step_s * 1e3:.1f} ms per step"}
+
+
+def cpu_decoder_tokens(T, budget_s, n_steps):
+    """Sequences per CPU decode step so that n_steps whole steps fit budget_s
+    (the oracle's step cost grows about linearly with the sequences)."""
+    if T == 1:
+        return 1
+    s1 = cpu_decoder_sample(T=1)
+    cpu_decoder_step(s1, 0)
+    t0 = time.perf_counter()
+    cpu_decoder_step(s1, 0)
+    t1 = time.perf_counter() - t0
+    return max(1, min(T, int(budget_s / max(n_steps * t1, 1e-9))))
 
 
 REF_BUDGET_S = 150.0  # the reference arm's whole run (warm-up + timed steps) stays within a few minutes
@@ -1084,14 +1105,15 @@ def run_reference(args, rank, world):
     n_runs = args.steps + args.warmup
     if args.workload.startswith("decode30"):
         T = WORKLOADS[args.workload]
-        sample = cpu_decoder_sample()
-        recent = cpu_sampler_setup() if args.sample else None
+        tokens = cpu_decoder_tokens(T, REF_BUDGET_S, n_runs)
+        sample = cpu_decoder_sample(T=tokens)
+        recent = cpu_sampler_setup(T=tokens) if args.sample else None
         step = lambda i: cpu_decoder_step(sample, i, recent)  # noqa: E731
-        metric, config, tokens = DECODER_METRIC, decoder_config(args, world), T
+        metric, config = decoder_metric(args), decoder_config(args, world)
         dtype = "u8/u4/u6-affine weights x bf16 activations, fp32/fp64 accumulate (CPU)"
-        desc = (f"each step = one whole decode step of one token at context {CTX} on the oracle: 24 sliding + 6 "
-                f"full layers + lm_head" + (" + the sampler (temperature 0.7, top_p 0.9, penalty 1.15)"
-                                             if args.sample else ""))
+        desc = (f"each step = one whole decode step of {tokens} of the workload's {T} sequences at context {CTX} on "
+                f"the oracle: 24 sliding + 6 full layers + lm_head"
+                + (" + the sampler (temperature 0.7, top_p 0.9, penalty 1.15)" if args.sample else ""))
     else:
         if args.workload in EP_WORKLOADS:
             T = EP_WORKLOADS[args.workload][0]

@@ -81,6 +81,34 @@ class KVCache:
         """Positions held (attendable), src/cache.rs:232-239."""
         return min(self._offset, self.capacity)
 
+    def batch_view(self, b0: int, nb: int) -> "KVCache":
+        """Sequences [b0, b0 + nb) of this cache as a cache of batch nb over the
+        same storage (a decoder layer call takes at most 8 sequences; larger
+        batches run as several calls on views of one cache)."""
+        if b0 < 0 or nb < 1 or b0 + nb > self.batch:
+            raise ValueError(f"batch_view: [{b0}, {b0 + nb}) outside batch {self.batch}")
+        v = object.__new__(KVCache)
+        v.__dict__.update(self.__dict__)
+        v.batch = nb
+        v._ws = None
+        v._ws_heads = 0
+        c = KvCacheC()
+        ctypes.pointer(c)[0] = self.c
+        c.batch = nb
+        rows = b0 * self.kv_heads * self.capacity  # rows of the sequences before b0
+        D = self.head_dim
+        if self.mode == KV_BF16:
+            row_bytes = {"k": 2 * D, "v": 2 * D}
+        else:
+            row_bytes = {"k": D // 2, "v": D, "k_scales": D // 32, "k_biases": D // 32, "v_scales": D // 32,
+                         "v_biases": D // 32}
+        for name, rb in row_bytes.items():
+            p = getattr(self.c, name)
+            if p:
+                setattr(c, name, p + rows * rb)
+        v.c = c
+        return v
+
     # -- views of the stored arrays (tests and debugging) -------------------
     def _view(self, ptr, dtype, inner):
         off = ptr - self.buf.data_ptr()

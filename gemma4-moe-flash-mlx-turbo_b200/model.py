@@ -180,7 +180,7 @@ class Gemma4Model:
     caches, final norm and the tied 6-bit lm_head with softcap; greedy decode."""
 
     def __init__(self, cfg, embed: QuantizedLinear, layers, final_norm, batch, max_positions, kv_mode=KV_BF16,
-                 device=None, ep=None, ep_cap=None, ep_mode=0):
+                 device=None, ep=None, ep_cap=None, ep_mode=0, turbo_bits=0):
         self.cfg = cfg
         self.embed = embed
         self.layers = layers
@@ -194,21 +194,31 @@ class Gemma4Model:
             if kv_mode == KV_AFFINE:
                 c = KVCache.new_affine(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
             else:
-                c = KVCache(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, device=device)
+                # turbo_bits 2..4: appended rows take the TurboQuant round trip
+                # (the reference's default cache, src/main.rs:53, src/cache.rs:290-308)
+                c = KVCache(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, turbo_bits=turbo_bits,
+                            device=device)
             self.caches.append(c)
+        # a layer call takes at most 8 sequences: larger batches run as groups of
+        # 8 on views of the same caches (the layer's weights stay in L2 between
+        # the calls of one layer)
+        self.groups = [(b0, min(8, batch - b0)) for b0 in range(0, batch, 8)]
+        self.views = [[c.batch_view(b0, nb) for b0, nb in self.groups] if batch > 8 else [c] for c in self.caches]
         self.ep = ep
-        self.ep_cap = batch if ep_cap is None else ep_cap
+        self.ep_cap = min(batch, 8) if ep_cap is None else ep_cap
         self.ep_mode = ep_mode  # FMOE_EP_FIXED or FMOE_EP_P2P (both capturable)
         if ep is not None and ep_mode == 2:
             ep.ensure_p2p(self.ep_cap, cfg["hidden"], layers[0].top_k)
         if ep is None:
-            ws = max(L.workspace_bytes(batch, c) for L, c in zip(layers, self.caches))
+            ws = max(L.workspace_bytes(v.batch, v) for L, vs in zip(layers, self.views) for v in vs)
         else:
-            ws = max(L.ep_workspace_bytes(batch, c, ep.world, self.ep_cap) for L, c in zip(layers, self.caches))
+            ws = max(L.ep_workspace_bytes(v.batch, v, ep.world, self.ep_cap) for L, vs in zip(layers, self.views)
+                     for v in vs)
         if ws == 0:
             raise ValueError("decoder: unsupported layer / cache configuration")
         self.ws = torch.zeros(ws, dtype=torch.uint8, device=device)
-        self.lm_ws = torch.zeros(lib().fmoe_lm_head_workspace_bytes(batch) + 256, dtype=torch.uint8, device=device)
+        self.lm_ws = torch.zeros(lib().fmoe_lm_head_workspace_bytes(min(batch, 8)) + 256, dtype=torch.uint8,
+                                 device=device)
         H, V = cfg["hidden"], embed.out_features
         self.x = torch.zeros(batch, H, dtype=torch.bfloat16, device=device)
         self.logits = torch.empty(batch, V, dtype=torch.float32, device=device)
@@ -245,7 +255,7 @@ class Gemma4Model:
 
     @classmethod
     def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None, ep=None,
-               ep_cap=None, ep_mode=0):
+               ep_cap=None, ep_mode=0, turbo_bits=0):
         """Random-init model.  ep (an EPComm): every layer keeps only this rank's
         expert slice and decode_step runs the routed experts on their owners."""
         n_layers = cfg["layers"] if n_layers is None else n_layers
@@ -269,7 +279,8 @@ class Gemma4Model:
             rows.append(None)
         embed = QuantizedLinear(wq, sc, bi, cfg["embed_bits"], 64, in_features=H)
         final_norm = (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(torch.bfloat16)
-        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device, ep, ep_cap, ep_mode)
+        return cls(cfg, embed, layers, final_norm, batch, max_positions, kv_mode, device, ep, ep_cap, ep_mode,
+                   turbo_bits)
 
     def _fused(self):
         if self._fc is None:
@@ -324,14 +335,18 @@ class Gemma4Model:
         check(lib().fmoe_embed_rows(ctypes.byref(c), _ptr(self.ids), self.batch, self._emb_scale, _ptr(self.x),
                                     _stream()))
         pd = self.pos_dev if device_pos else None
-        for L, cache in zip(self.layers, self.caches):
-            if self.ep is None:
-                L.forward(self.x, cache, self.pos, self.ws, pd)
-            else:
-                L.forward_ep(self.ep, self.ep_cap, self.x, cache, self.pos, self.ws, pd, mode=self.ep_mode)
-        check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(self.x), self.batch,
-                                 self.cfg["softcap"], _ptr(self.logits), _ptr(self.ids), _ptr(pd), _ptr(self.lm_ws),
-                                 self.lm_ws.numel(), _stream()))
+        for L, views in zip(self.layers, self.views):
+            for (b0, nb), v in zip(self.groups, views):
+                x = self.x[b0:b0 + nb]
+                if self.ep is None:
+                    L.forward(x, v, self.pos, self.ws, pd)
+                else:
+                    L.forward_ep(self.ep, self.ep_cap, x, v, self.pos, self.ws, pd, mode=self.ep_mode)
+        for i, (b0, nb) in enumerate(self.groups):  # the last call advances the device position
+            check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(self.x[b0:b0 + nb]),
+                                     nb, self.cfg["softcap"], _ptr(self.logits[b0:b0 + nb]), _ptr(self.ids[b0:b0 + nb]),
+                                     _ptr(pd if i == len(self.groups) - 1 else None), _ptr(self.lm_ws),
+                                     self.lm_ws.numel(), _stream()))
         if self.sampler is not None:  # the draw replaces the lm_head's greedy ids
             self.sampler(self.logits, out=self.ids)
         if not device_pos:

@@ -10,8 +10,9 @@ RMS-normalised q / k), and its output moves by 0.9-1.6 % under +-1-ulp noise
 on 10 % of its input with unchanged routing (measured on the oracle alone at
 these shapes), so 1e-2 is below the layer's own rounding noise; its
 components are held to 1e-2 in their own tests.  A layer's MoE output depends
-on the routed ids, so a case whose router logits put the k-th and (k+1)-th
-expert within 1e-3 of each other (the benchmark's tie rule) is skipped.
+on the routed ids, so a seed whose router logits put the k-th and (k+1)-th
+expert within 1e-3 of each other (the benchmark's tie rule) is passed over
+for the next one.
 """
 import numpy as np
 import pytest
@@ -60,8 +61,17 @@ def test_decoder_layer_matches_oracle(fm, orc, dev, monkeypatch, full, T, kv, pa
     streaming six-launch layer) and the three cache kinds: bf16, bf16 with the
     TurboQuant-3 round trip on append, WHT-rotated affine K4 / V8."""
     monkeypatch.setenv("FMOE_DECODE_PATH", path)
+    for seed in (31 + 7 * T + full, 1031 + 7 * T + full, 2031 + 7 * T + full, 3031 + 7 * T + full):
+        if _layer_case(fm, orc, dev, full, T, kv, seed):
+            return
+    pytest.skip("router logits tie within 1e-3 at the top-k boundary for every seed tried")
+
+
+def _layer_case(fm, orc, dev, full, T, kv, seed):
+    """One seeded layer vs the oracle; False when the router's top-k boundary
+    is a near tie (the routed experts may then legitimately differ)."""
     cfg = dict(fm.GEMMA4_26B)
-    L = fm.Gemma4DecoderLayer.random(cfg, full, seed=31 + 7 * T + full, device=dev)
+    L = fm.Gemma4DecoderLayer.random(cfg, full, seed=seed, device=dev)
     cap = 64
     if kv == "affine":
         cache = fm.KVCache.new_affine(T, L.num_kv_heads, L.head_dim, cap, device=dev)
@@ -87,7 +97,7 @@ def test_decoder_layer_matches_oracle(fm, orc, dev, monkeypatch, full, T, kv, pa
     torch.cuda.synchronize()
     xo, _ = orc.decoder_layer(x_in, oracle_weights(L), ck, cv, pos, ocfg)
     if not topk_sure(ocfg["_router_logits"], L.top_k).all():
-        pytest.skip("router logits tie within 1e-3 at the top-k boundary")
+        return False
     a = cache.arrays()
     if kv == "affine":
         # The new rows are quantised from k / v that match the oracle's to
@@ -112,6 +122,7 @@ def test_decoder_layer_matches_oracle(fm, orc, dev, monkeypatch, full, T, kv, pa
     assert cache.status() == 0
     assert kerr <= TOL and verr <= TOL, (kerr, verr)
     assert err <= LAYER_TOL, diag
+    return True
 
 
 def _deq_np(orc, arrs, bits, pos):
