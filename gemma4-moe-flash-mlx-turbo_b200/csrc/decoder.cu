@@ -60,6 +60,20 @@ __device__ __forceinline__ void load_row_bf16(const bf16* p, int H, float (&v)[k
   }
 }
 
+// The row's bf16 bits, not yet converted: loads issued before a dependency
+// wait stay in flight across it (converting them would stall there).
+__device__ __forceinline__ void load_row_raw(const bf16* p, int H, unsigned short (&v)[kFfPer]) {
+#pragma unroll
+  for (int k = 0; k < kFfPer; ++k) {
+    const int i = threadIdx.x + k * kFfThreads;
+    v[k] = (p && i < H) ? __bfloat16_as_ushort(p[i]) : (unsigned short)0;
+  }
+}
+__device__ __forceinline__ void raw_to_f32(const unsigned short (&r)[kFfPer], float (&v)[kFfPer]) {
+#pragma unroll
+  for (int k = 0; k < kFfPer; ++k) v[k] = __uint_as_float((uint32_t)r[k] << 16);
+}
+
 // acc = sum over the split-K slices in slice order (kFfSlices slices' loads in
 // flight together).
 __device__ __forceinline__ void add_slices(const float* base, int parts, int64_t stride, int H,
@@ -96,14 +110,19 @@ __global__ void __launch_bounds__(kFfThreads) ff_in_kernel(const bf16* __restric
   __shared__ float red[kFfThreads / 32];
   const int t = blockIdx.x;
   float wpa[kFfPer], wpf[kFfPer], wpf2[kFfPer], rsc[kFfPer], xv[kFfPer], a[kFfPer], h[kFfPer], h2[kFfPer];
-  load_row_bf16(w_post_attn, H, wpa);  // constants: before the dependency wait
-  load_row_bf16(w_pre_ff, H, wpf);
-  load_row_bf16(w_pre_ff2, H, wpf2);
-  load_row_bf16(rscale, H, rsc);
+  unsigned short rwpa[kFfPer], rwpf[kFfPer], rwpf2[kFfPer], rrsc[kFfPer];
+  load_row_raw(w_post_attn, H, rwpa);  // constants: in flight across the dependency wait
+  load_row_raw(w_pre_ff, H, rwpf);
+  load_row_raw(w_pre_ff2, H, rwpf2);
+  load_row_raw(rscale, H, rrsc);
   griddep_wait();
   griddep_launch_dependents();
   load_row_bf16(x + (int64_t)t * H, H, xv);
   add_slices(o_acc + (int64_t)t * H, o_parts, o_stride, H, a);
+  raw_to_f32(rwpa, wpa);
+  raw_to_f32(rwpf, wpf);
+  raw_to_f32(rwpf2, wpf2);
+  raw_to_f32(rrsc, rsc);
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kFfPer; ++k) {
@@ -158,14 +177,18 @@ __global__ void __launch_bounds__(kFfThreads) ff_out_kernel(const bf16* __restri
   __shared__ float red[kFfThreads / 32];
   const int t = blockIdx.x;
   float w1v[kFfPer], w2v[kFfPer], wv[kFfPer], d[kFfPer], m[kFfPer], hr[kFfPer];
-  load_row_bf16(w1, H, w1v);  // constants: before the dependency wait
-  load_row_bf16(w2, H, w2v);
-  load_row_bf16(w, H, wv);
+  unsigned short rw1[kFfPer], rw2[kFfPer], rw[kFfPer];
+  load_row_raw(w1, H, rw1);  // constants: in flight across the dependency wait
+  load_row_raw(w2, H, rw2);
+  load_row_raw(w, H, rw);
   griddep_wait();
   griddep_launch_dependents();
   load_row_bf16(moe + (int64_t)t * H, H, m);
   load_row_bf16(h_res + (int64_t)t * H, H, hr);
   add_slices(d_acc + (int64_t)t * H, d_parts, d_stride, H, d);
+  raw_to_f32(rw1, w1v);
+  raw_to_f32(rw2, w2v);
+  raw_to_f32(rw, wv);
   float sd = 0.f, sm = 0.f;
 #pragma unroll
   for (int k = 0; k < kFfPer; ++k) {

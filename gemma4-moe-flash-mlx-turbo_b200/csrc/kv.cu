@@ -148,10 +148,22 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __r
   // the preceding kernel's own wait), so it is final here.
   const int64_t p0 = pos_dev ? *pos_dev : pos;
   float nwv[P], cs[P], sn[P];
-  load_norm_w<P>(is_q ? q_norm : k_norm, lane, nwv);
+  const bf16* nwp = is_q ? q_norm : k_norm;
+  uint4 nraw[P / 8];  // the norm weights' bits, in flight across the wait
+#pragma unroll
+  for (int i = 0; i < P / 8; ++i) nraw[i] = nwp ? reinterpret_cast<const uint4*>(nwp + lane * P)[i] : make_uint4(0, 0, 0, 0);
   rope_angles<P>(rope_dims, log2_theta, (float)p0, lane, cs, sn);
   griddep_wait();  // the projections come from the preceding kernel
   griddep_launch_dependents();
+#pragma unroll
+  for (int i = 0; i < P / 8; ++i) {
+    const uint32_t w4[4] = {nraw[i].x, nraw[i].y, nraw[i].z, nraw[i].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      nwv[8 * i + 2 * e] = nwp ? bf16lo(w4[e]) : 1.f;
+      nwv[8 * i + 2 * e + 1] = nwp ? bf16hi(w4[e]) : 1.f;
+    }
+  }
   if (row >= T * (Hq + Hkv)) return;
   float v[P];
   if (is_q) {

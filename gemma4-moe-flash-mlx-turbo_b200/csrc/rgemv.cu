@@ -185,16 +185,14 @@ __global__ void __launch_bounds__(NTHR, 2) rgemv_kernel(const __grid_constant__ 
   // input norm's weights come in alongside
   for (int j = warp; j < n && j < L.nst; j += NW) issue<BITS>(a, L, smem, full, issued, i0 + j, j, lane);
   const bool rmsn = a.in_kind == QG_IN_RMSNORM;
-  {
-    uint4 nv = make_uint4(0, 0, 0, 0), nv2 = nv;  // gn * 8 <= 2 * NTHR pieces
-    if (rmsn && tid < gn * 8) nv = ld_u4(a.norm_w + g0 * 64 + tid * 8);
-    if (rmsn && tid + NTHR < gn * 8) nv2 = ld_u4(a.norm_w + g0 * 64 + (tid + NTHR) * 8);
-    if (rmsn && tid < gn * 8) reinterpret_cast<uint4*>(nw)[tid] = nv;
-    if (rmsn && tid + NTHR < gn * 8) reinterpret_cast<uint4*>(nw)[tid + NTHR] = nv2;
-  }
+  uint4 nv = make_uint4(0, 0, 0, 0), nv2 = nv;  // gn * 8 <= 2 * NTHR pieces, in flight across the wait
+  if (rmsn && tid < gn * 8) nv = ld_u4(a.norm_w + g0 * 64 + tid * 8);
+  if (rmsn && tid + NTHR < gn * 8) nv2 = ld_u4(a.norm_w + g0 * 64 + (tid + NTHR) * 8);
 
   griddep_wait();  // the input belongs to earlier kernels
   griddep_launch_dependents();
+  if (rmsn && tid < gn * 8) reinterpret_cast<uint4*>(nw)[tid] = nv;
+  if (rmsn && tid + NTHR < gn * 8) reinterpret_cast<uint4*>(nw)[tid + NTHR] = nv2;
   // ---- input prologue: f16 B fragments + per-group sums of the CTA's chunks
   const int xst = gmax_of(L) * 64;  // raw-x stash stride per token (elements)
   if (a.in_kind == QG_IN_RMSNORM) {

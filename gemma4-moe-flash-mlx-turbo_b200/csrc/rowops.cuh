@@ -70,17 +70,8 @@ __device__ __forceinline__ void warp_rope(float (&v)[P], int rope_dims, float lo
 }
 
 // The same two steps split so that everything independent of the row can run
-// early (before a programmatic-dependent wait): the norm weights as floats
-// (1 when w is null) and the lane's RoPE cos / sin.
-template <int P>
-__device__ __forceinline__ void load_norm_w(const bf16* w, int lane, float (&wv)[P]) {
-  if (w) {
-    load_row_f32<P>(w, lane, wv);
-  } else {
-#pragma unroll
-    for (int i = 0; i < P; ++i) wv[i] = 1.f;
-  }
-}
+// early (before a programmatic-dependent wait): norm weights as floats and the
+// lane's RoPE cos / sin.
 template <int P>
 __device__ __forceinline__ void warp_rms_norm_w(float (&v)[P], const float (&wv)[P], bool has_w, float eps, int lane) {
   constexpr int D = 32 * P;
