@@ -334,8 +334,9 @@ def run_decoder(args, rank, world, local):
     ep_mode = fm.FMOE_EP_P2P if args.ep_mode == "p2p" else fm.FMOE_EP_FIXED
     if args.ep_mode == "exact":
         raise SystemExit("decode30: the exact exchange syncs the host per layer and cannot be captured")
+    # one layout per weight: the decoder's GEMVs read the plain MLX-affine rows
     m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
-                              ep=ep, ep_mode=ep_mode).tile_weights()
+                              ep=ep, ep_mode=ep_mode)
     if args.sample:
         m.set_sampler(0.7, 0.9, 1.15, seed=4200 + rank)
     g = torch.Generator(device=dev).manual_seed(4100 + rank)

@@ -245,7 +245,9 @@ class Gemma4Model:
         return self
 
     def tile_weights(self):
-        """Tile-layout copies of every decode-GEMV weight (layers and lm_head)."""
+        """Tile-layout copies of every decode-GEMV weight (layers and lm_head) for
+        the per-row GEMV (fmoe_qlinear).  The decoder's own projections and
+        lm_head read the plain layout and do not need them."""
         for L in self.layers:
             L.tile_weights()
         self.embed.tile(accumulate=False)
