@@ -45,7 +45,7 @@ GATE_UP_BYTES = 2 * (I * H // 2 + 2 * I * (H // 64) * 2)   # per selected expert
 DOWN_BYTES = H * I // 2 + 2 * H * (I // 64) * 2            # per selected expert: 1,115,136
 WORKLOADS = {"decode30_b1": 1, "decode30_b32": 32, "moe30_decode_b1": 1, "moe30_decode_b32": 32}
 # total tokens per step (split evenly over the GPUs), default exchange mode
-EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "fixed"), "ep_moe30_prefill_8192": (8192, "exact")}
+EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "p2p"), "ep_moe30_prefill_8192": (8192, "exact")}
 # config 5 measured inside a multi-GPU decode30 run (workload, exchange mode)
 EP_EXTRA = [("ep_moe30_decode_b256", "fixed"), ("ep_moe30_decode_b256", "p2p"), ("ep_moe30_prefill_8192", "exact")]
 CTX = 2048                                                 # decode context (positions in every KV cache)
@@ -60,7 +60,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode30_b1", choices=sorted(WORKLOADS) + sorted(EP_WORKLOADS))
     ap.add_argument("--ep-mode", default=None, choices=["fixed", "exact", "p2p"],
-                    help="expert-parallel exchange (default: fixed for decode, exact for prefill; p2p = fixed's "
+                    help="expert-parallel exchange (default: p2p for decode, exact for prefill; p2p = fixed's "
                          "layout stored into the peers' memory by the library's kernels; decode30 at N > 1 takes "
                          "fixed or p2p)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -261,8 +261,8 @@ def decoder_config(args, world):
     T = WORKLOADS[args.workload]
     par = "single GPU" if world == 1 else (
         f"expert-parallel x{world}: {E // world} experts per GPU, routed tokens dispatched / combined "
-        + ("by stores into the peers' exchange windows (CUDA IPC, flag-synchronised)" if args.ep_mode == "p2p"
-           else "by NCCL send/recv")
+        + ("by NCCL send/recv" if args.ep_mode == "fixed"
+           else "by stores into the peers' exchange windows (CUDA IPC, flag-synchronised)")
         + " over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
         f"replicated; one sequence per GPU")
     return {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
@@ -331,7 +331,9 @@ def run_decoder(args, rank, world, local):
     T = WORKLOADS[args.workload]
     cfg = dict(fm.GEMMA4_26B)
     # the same weights on every rank (each keeps its expert slice); per-rank sequences
-    ep_mode = fm.FMOE_EP_P2P if args.ep_mode == "p2p" else fm.FMOE_EP_FIXED
+    # default exchange at N > 1: peer-memory stores (measured faster than NCCL
+    # send / recv at N = 2 and 4); --ep-mode fixed selects NCCL
+    ep_mode = fm.FMOE_EP_FIXED if args.ep_mode == "fixed" else fm.FMOE_EP_P2P
     if args.ep_mode == "exact":
         raise SystemExit("decode30: the exact exchange syncs the host per layer and cannot be captured")
     # one layout per weight: the decoder's GEMVs read the plain MLX-affine rows

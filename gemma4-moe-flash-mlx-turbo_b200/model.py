@@ -180,7 +180,7 @@ class Gemma4Model:
     caches, final norm and the tied 6-bit lm_head with softcap; greedy decode."""
 
     def __init__(self, cfg, embed: QuantizedLinear, layers, final_norm, batch, max_positions, kv_mode=KV_BF16,
-                 device=None, ep=None, ep_cap=None, ep_mode=0, turbo_bits=0):
+                 device=None, ep=None, ep_cap=None, ep_mode=2, turbo_bits=0):
         self.cfg = cfg
         self.embed = embed
         self.layers = layers
@@ -206,7 +206,9 @@ class Gemma4Model:
         self.views = [[c.batch_view(b0, nb) for b0, nb in self.groups] if batch > 8 else [c] for c in self.caches]
         self.ep = ep
         self.ep_cap = min(batch, 8) if ep_cap is None else ep_cap
-        self.ep_mode = ep_mode  # FMOE_EP_FIXED or FMOE_EP_P2P (both capturable)
+        # FMOE_EP_P2P (default: peer-memory stores, measured faster than NCCL
+        # send / recv at 2 and 4 GPUs) or FMOE_EP_FIXED; both capturable
+        self.ep_mode = ep_mode
         if ep is not None and ep_mode == 2:
             ep.ensure_p2p(self.ep_cap, cfg["hidden"], layers[0].top_k)
         if ep is None:
@@ -257,7 +259,7 @@ class Gemma4Model:
 
     @classmethod
     def random(cls, cfg, batch, max_positions, seed=0, device="cuda", kv_mode=KV_BF16, n_layers=None, ep=None,
-               ep_cap=None, ep_mode=0, turbo_bits=0):
+               ep_cap=None, ep_mode=2, turbo_bits=0):
         """Random-init model.  ep (an EPComm): every layer keeps only this rank's
         expert slice and decode_step runs the routed experts on their owners."""
         n_layers = cfg["layers"] if n_layers is None else n_layers
