@@ -343,7 +343,9 @@ __global__ void __launch_bounds__(NTHR, 2) rgemv_kernel(const __grid_constant__ 
 #pragma unroll
     for (int gl = 0; gl < CG; gl += 2) {
       if (gl >= q.ng) break;
+      // per group two accumulators (MMAs 0, 2 and 1, 3): four short chains in flight
       float cc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float cd[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
       float q0[2] = {0.f, 0.f}, q1[2] = {0.f, 0.f};
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -362,8 +364,15 @@ __global__ void __launch_bounds__(NTHR, 2) rgemv_kernel(const __grid_constant__ 
         uint32_t af[4][4];
         load_a_frags<BITS>(rl, rl + 8 * L.rs, af);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) mma16816_f16(cc[h], af[jj][0], af[jj][1], af[jj][2], af[jj][3], bb0[jj], bb1[jj]);
+        for (int jj = 0; jj < 4; jj += 2) {
+          mma16816_f16(cc[h], af[jj][0], af[jj][1], af[jj][2], af[jj][3], bb0[jj], bb1[jj]);
+          mma16816_f16(cd[h], af[jj + 1][0], af[jj + 1][1], af[jj + 1][2], af[jj + 1][3], bb0[jj + 1], bb1[jj + 1]);
+        }
       }
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cc[h][e] += cd[h][e];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         if (gl + h >= q.ng) break;
