@@ -9,9 +9,9 @@ Workloads (synthetic data, random-init weights of the Gemma-4 26B-A4B shapes):
                     attention (sliding window 1024 / full), the 4-bit dense
                     MLP, the bf16 router and 8 of 128 4-bit experts, then the
                     final norm, the tied 6-bit lm_head with softcap and argmax.
-                    The context is 2048 random bf16 K/V positions written into
-                    every layer's cache (the cost of a decode step depends on
-                    the context length, not on how it was produced).
+                    The context comes from a random 2048-token prompt run
+                    through the whole decoder (Gemma4Model.prefill), whose
+                    time is reported as the decoder_prefill key.
   moe30_decode_b1   the routed-expert path of the same decoder alone: per
                     layer the bf16 router [128, 2816] (softmax, top-8,
                     renormalise) and 8 of 128 MLX-affine 4-bit experts
@@ -100,7 +100,7 @@ def load_peaks():
     try:
         return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))), "measured"
     except Exception:
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
 class ClockSampler:
@@ -342,11 +342,20 @@ def run_decoder(args, rank, world, local):
     if args.sample:
         m.set_sampler(0.7, 0.9, 1.15, seed=4200 + rank)
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
-    for L, c in zip(m.layers, m.caches):
-        chunk = 256
-        for p0 in range(0, CTX, chunk):
-            kv = torch.randn(2, T, L.num_kv_heads, chunk, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
-            c.update(kv[0], kv[1])
+    peaks, peaks_kind = load_peaks()
+    pf_result = None
+    if ep is None:
+        # BASELINE config 4's context: a CTX-token prompt per sequence prefilled
+        # through the whole decoder, which fills every KV cache
+        prompt = torch.randint(0, cfg["vocab"], (T, CTX), generator=g, device=dev, dtype=torch.int32)
+        pf_result = decoder_prefill(torch, m, prompt, peaks, timed_reps=0 if args.profile_step else 3)
+    else:
+        # expert-parallel models have no whole-decoder prefill: CTX random K/V positions
+        for L, c in zip(m.layers, m.caches):
+            chunk = 256
+            for p0 in range(0, CTX, chunk):
+                kv = torch.randn(2, T, L.num_kv_heads, chunk, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+                c.update(kv[0], kv[1])
     ids0 = torch.randint(0, cfg["vocab"], (T,), generator=g, device=dev, dtype=torch.int32)
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream())
@@ -429,7 +438,6 @@ def run_decoder(args, rank, world, local):
     ms_step = ms / args.steps
     value = world * T / (ms_step / 1e3)
     e2e_value = world * T / (ms_e2e / args.steps / 1e3)
-    peaks, peaks_kind = load_peaks()
     step_bytes, parts = decoder_step_bytes(m, T, CTX)
     step_gbs = step_bytes / (ms_step / 1e3) / 1e9
 
@@ -453,8 +461,9 @@ def run_decoder(args, rank, world, local):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "u8/u4/u6-affine weights x bf16 activations, fp32 accumulate",
-        "data": "synthetic (random-init weights MLX-affine quantised; random token ids; 2048 random bf16 K/V "
-                "positions per cache)",
+        "data": "synthetic (random-init weights MLX-affine quantised; random token ids; the 2048-position "
+                "context prefilled from a random prompt%s)" % ("" if ep is None else
+                                                              " — here random bf16 K/V rows (expert-parallel)"),
         "config": decoder_config(args, world),
         "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": T * 4,
                 "d2h_bytes_per_step": T * 4,
@@ -482,6 +491,8 @@ def run_decoder(args, rank, world, local):
     torch.cuda.synchronize()
     if ep is not None:
         ep.close()
+    if pf_result is not None and rank == 0:
+        result["decoder_prefill"] = pf_result
     if rank == 0 and world == 1 and not args.no_attn:
         # BASELINE configs 3 and 2 on the same box, as extra keys of the headline line
         result["kv_attention"] = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"])
@@ -1188,6 +1199,54 @@ def run_qlinear_case(args):
     nbytes = out_f * in_f * bits // 8 + 2 * out_f * (in_f // 64) * 2
     print(json.dumps({"qlinear_case": args.qlinear_case, "us": round(us, 1), "weight_bytes": nbytes,
                       "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
+
+
+def prefill_flops(m, T):
+    """Algorithmic FLOPs of one T-token prompt through the decoder: projections,
+    dense MLP, router, 8 routed experts per token, causal / sliding attention
+    (QK and PV over the admitted keys), and the lm_head of the last position."""
+    cfg = m.cfg
+    fl = 0.0
+    for L in m.layers:
+        D, Hq = L.head_dim, L.num_heads
+        qkv = L.q_proj.out_features + L.k_proj.out_features + (0 if L.k_eq_v else L.v_proj.out_features)
+        per_tok = 2 * H * qkv + 2 * Hq * D * H + 2 * 3 * H * L.mlp[0].out_features + 2 * H * E + 2 * K * 3 * H * I
+        full = getattr(L, "full_attention", L.k_eq_v)
+        keys = sum(t + 1 if full else min(t + 1, cfg["window"]) for t in range(T))
+        fl += T * per_tok + 4.0 * Hq * D * keys
+    return fl + 2.0 * H * cfg["vocab"]
+
+
+def decoder_prefill(torch, m, prompt, peaks, timed_reps=3):
+    """Gemma4Model.prefill of every sequence's prompt (fills the caches; the first
+    call builds the prefill buffers), then `timed_reps` CUDA-event timed prefills
+    of the same prompts from position 0 (they rewrite the same rows).  Returns
+    the sub-measurement for the JSON line, or None when untimed."""
+    B, T = prompt.shape
+    m.set_position(0)
+    m.prefill(prompt)
+    torch.cuda.synchronize()
+    if timed_reps <= 0:
+        return None
+    times = []
+    for _ in range(timed_reps):
+        m.set_position(0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        m.prefill(prompt)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    flops = B * prefill_flops(m, T)
+    tf = flops / (ms / 1e3) / 1e12
+    return {"metric": "prefill tok/s (whole decoder, %d-token prompt%s)" % (T, "" if B == 1 else " x %d" % B),
+            "value": round(B * T / (ms / 1e3), 1), "unit": "tok/s", "ms": round(ms, 3), "tokens": B * T,
+            "roofline": {"bound": "tensor", "alg_flops": int(flops), "achieved_tflops": round(tf, 1),
+                         "peak_tflops": peaks["bf16_tflops_sustained"],
+                         "frac": round(tf / peaks["bf16_tflops_sustained"], 4)},
+            "api": "Gemma4Model.prefill (fmoe_embed_rows, fmoe_decoder_layer_prefill x layers, fmoe_lm_head)",
+            "timing": f"median of {timed_reps} CUDA-event timed prefills after one warm-up prefill"}
 
 
 def prefill_setup(fm, torch, dev, seed=2002):

@@ -155,6 +155,12 @@ SIGNATURES = {
     "fmoe_turbo_round_trip": (_I, [_P, _I64, _I, _I, _P, _P]),
     "fmoe_decoder_workspace_bytes": (_SZ, [_I64, _P, ctypes.POINTER(KvCacheC)]),
     "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),
+    "fmoe_decoder_layer_prefill_workspace_bytes": (_SZ, [_P, _I64]),
+    "fmoe_decoder_layer_prefill": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _I, _P, _P, _SZ, _P]),
+    "fmoe_attn_prefill": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _I64, _I, _P, _P, _P, _F, _P]),
+    "fmoe_mlp_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(QWeightC)]),
+    "fmoe_mlp_forward": (_I, [_P, _I64, ctypes.POINTER(QWeightC), ctypes.POINTER(QWeightC), ctypes.POINTER(QWeightC),
+                              _P, _P, _SZ, _P]),
     "fmoe_lm_head_workspace_bytes": (_SZ, [_I64]),
     "fmoe_lm_head": (_I, [ctypes.POINTER(QWeightC), _P, _F, _P, _I64, _F, _P, _P, _P, _P, _SZ, _P]),
     "fmoe_sample_workspace_bytes": (_SZ, [_I64, _I64]),
@@ -272,6 +278,35 @@ def quantize(w: torch.Tensor, bits: int = 4, group_size: int = 64):
     check(lib().fmoe_quantize(_ptr(w), int(w.dtype == torch.bfloat16), rows, cols, bits, group_size,
                               _ptr(wq), _ptr(s), _ptr(b), _stream()))
     return wq, s, b
+
+
+def prefill_prep(experts, device):
+    """Transposed scale / bias copy of an expert table for the prefill GEMMs
+    (fmoe_moe_prefill_prepare; built once per table and kept on it)."""
+    prep = getattr(experts, "_prefill_prep", None)
+    if prep is None:
+        e = experts.cstruct()
+        nbytes = lib().fmoe_moe_prefill_prepare_bytes(ctypes.byref(e))
+        if nbytes == 0:
+            check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), None, 0, None))
+        prep = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), _ptr(prep), nbytes, _stream()))
+        experts._prefill_prep = prep
+    return prep
+
+
+def mlp_forward(x: torch.Tensor, gate, up, down) -> torch.Tensor:
+    """GeLUMLP::forward (src/model/mlp.rs:28-41) over T tokens on the tensor-core
+    GEMM (fmoe_mlp_forward): x bf16 [T, hidden] -> bf16 [T, hidden]."""
+    _need_cuda(x)
+    x2 = x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous()
+    T = x2.shape[0]
+    g, u, d = gate.cstruct(), up.cstruct(), down.cstruct()
+    ws = torch.empty(lib().fmoe_mlp_workspace_bytes(T, ctypes.byref(g)), dtype=torch.uint8, device=x.device)
+    y = torch.empty(T, down.out_features, dtype=torch.bfloat16, device=x.device)
+    check(lib().fmoe_mlp_forward(_ptr(x2), T, ctypes.byref(g), ctypes.byref(u), ctypes.byref(d), _ptr(y), _ptr(ws),
+                                 ws.numel(), _stream()))
+    return y.reshape(*x.shape[:-1], down.out_features)
 
 
 class QuantizedLinear:
@@ -494,18 +529,7 @@ class Gemma4MoeBlock:
     PREFILL_MIN_TOKENS = 129
 
     def _prepared(self, device):
-        """Transposed scale / bias copy of the expert table for the prefill GEMMs
-        (built once per table)."""
-        prep = getattr(self.experts, "_prefill_prep", None)
-        if prep is None:
-            e = self.experts.cstruct()
-            nbytes = lib().fmoe_moe_prefill_prepare_bytes(ctypes.byref(e))
-            if nbytes == 0:
-                check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), None, 0, None))
-            prep = torch.empty(nbytes, dtype=torch.uint8, device=device)
-            check(lib().fmoe_moe_prefill_prepare(ctypes.byref(e), _ptr(prep), nbytes, _stream()))
-            self.experts._prefill_prep = prep
-        return prep
+        return prefill_prep(self.experts, device)
 
     def forward_prefill(self, x: torch.Tensor, return_routing=False):
         """Router + experts over many tokens on the tcgen05 grouped-GEMM path

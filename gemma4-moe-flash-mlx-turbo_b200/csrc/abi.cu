@@ -249,6 +249,8 @@ static bool qlinear_streams(int64_t T, const QW& q, int group) {
 
 size_t fmoe_qlinear_workspace_bytes(int64_t T, const fmoe_qweight_t* w) {
   if (!w || T <= 0 || w->out_features <= 0 || w->in_features < 64) return 0;
+  QW q;
+  if (T > 8 && to_qw(w, &q) == FMOE_OK && qgemm_supported(q, w->group_size, q.in)) return 256;
   const int ks = gemv_ksplit(T, w->out_features, w->in_features);
   const size_t split = sizeof(float) * (size_t)ks * T * w->out_features;
   const size_t acc = sizeof(float) * (size_t)T * w->out_features;
@@ -291,6 +293,11 @@ int fmoe_qlinear(const void* x, int64_t T, const fmoe_qweight_t* w, void* y, voi
       return launch_reduce_partials(acc, 1, T * q.out, static_cast<bf16*>(y), nullptr, st);
     }
     // too large for the streaming kernel's shared memory: split-K path below
+  }
+  if (T > 8 && qgemm_supported(q, w->group_size, q.in)) {
+    // many tokens: the tensor-core GEMM (no workspace)
+    const QmOut o{&q, static_cast<bf16*>(y), q.out};
+    return launch_qgemm(static_cast<const bf16*>(x), T, q.in, &o, 1, false, nullptr, st);
   }
   rc = check_gemv_weight(q, w->group_size);
   if (rc) return rc;

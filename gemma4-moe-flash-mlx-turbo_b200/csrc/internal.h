@@ -206,6 +206,21 @@ struct Carver;
 // shared by the MoE-block and decoder-layer entry points.
 bool aligned(const void* p, size_t a);
 int to_qw(const fmoe_qweight_t* w, QW* q);
+
+// qgemm.cu: dense 4 / 8-bit group-64 linear layers over many tokens on tcgen05.
+// Up to kQmMaxSeg weights of the same K and bits share x (one launch); in the
+// gated form o[0] / o[1] are gate / up and o[0].out receives gelu(g) * u.
+constexpr int kQmMaxSeg = 3;
+struct QmOut {
+  const QW* w;
+  bf16* out;  // row t at out + t * ld
+  int ld;
+};
+bool qgemm_supported(const QW& w, int group, int K);
+int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool gated, int* status, cudaStream_t st);
+// pflayer.cu: prefill attention of T tokens of one sequence (window 0: causal)
+int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_t pos0, int window, const bf16* ks,
+                        const bf16* vs, bf16* out, float scale, cudaStream_t st);
 int to_experts(const fmoe_experts_t* e, ExpertsDev* d);
 int check_router(const fmoe_router_t* r, QW* q);
 // Every workspace starts with a 256-byte header: [0] device status word (0 ok;

@@ -1,0 +1,446 @@
+// Dense quantised linear layers over many tokens (prefill) on the 5th-generation
+// tensor cores: y[T][N] = x[T][K] . dequant(W)[N][K]^T for MLX-affine 4- or
+// 8-bit weights with groups of 64, the many-token form of
+// QuantizedLinear::forward (src/model/mlp.rs:15-25) and of GeLUMLP's gate / up /
+// down (src/model/mlp.rs:28-41).
+//
+// Persistent kernel, one CTA per SM, 14 warps.  An item is 256 weight rows x
+// one tile of up to 128 tokens; items run weight-tile-major, so the CTAs that
+// run at the same time share a weight tile in L2, and x stays in L2.
+//   warp 0      producer: TMA of the token tile (bf16 [tokens][64], 128-byte
+//               swizzle, one per K tile) and of the packed codes (two boxes of
+//               128 rows x 128 bytes = 2 (8-bit) or 4 (4-bit) K tiles, 128-byte
+//               swizzle)
+//   warp 1      MMA issuer: per K tile 2 x 4 tcgen05.mma (K 16) with the
+//               dequantised weights as the M = 128 operand (two halves) and
+//               the tokens as N (rounded up to 16), into one of two TMEM
+//               accumulators
+//   warps 2-9   dequantise one weight row each: w = bf16(s * q + b), s * q + b
+//               in fp32, written in the canonical K-major 128-byte-swizzled
+//               layout; the row's scale and bias are loaded from global memory
+//               one packed stage ahead
+//   warps 10-13 epilogue: tcgen05.ld (TMEM lane = weight row, column = token),
+//               bf16 stores, or (gated mode) gelu(gate) * up from the two
+//               halves, the first projection of the GeLU MLP
+// The plain mode takes up to three weights that share x (q, k and v), each a
+// run of items with its own output.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <mutex>
+#include "tc.cuh"
+
+namespace fmoe {
+namespace qm {
+
+using namespace tc;
+
+constexpr int BK = 64;                     // K per tile = one quantisation group
+constexpr int BN = 256;                    // weight rows per item (two M = 128 halves)
+constexpr int NS = 3;                      // K-tile stages: token tile + dequantised weights
+constexpr int NQ = 2;                      // packed-code stages
+constexpr int X_BYTES = 128 * BK * 2;      // 16 KB: up to 128 tokens x 64 bf16
+constexpr int WB_BYTES = BN * BK * 2;      // 32 KB: 256 rows x 64 bf16
+constexpr int WQ_BYTES = BN * 128;         // 32 KB: 256 rows x 128 bytes of codes
+constexpr int STAGE = X_BYTES + WB_BYTES;  // 48 KB
+constexpr int OFF_WQ = NS * STAGE;
+constexpr int OFF_BAR = OFF_WQ + NQ * WQ_BYTES;
+constexpr int SMEM = OFF_BAR + 256 + 1024;  // + slack to align the base to 1024 bytes
+constexpr int NDQ = 8;
+constexpr int THREADS = (2 + NDQ + 4) * 32;
+constexpr int TMEM_COLS = 512;  // [2 accumulators][2 halves][128 tokens] fp32
+static_assert(STAGE % 1024 == 0 && OFF_WQ % 1024 == 0 && WQ_BYTES % 1024 == 0, "stage alignment");
+static_assert(SMEM <= 227 * 1024, "shared memory");
+
+struct Seg {
+  const bf16* s;  // scales [N][G]
+  const bf16* b;  // biases [N][G]
+  bf16* out;      // row t of the output at out + t * ld
+  int N, ld;
+  int item0;      // first item of the segment
+};
+struct alignas(64) Maps {
+  CUtensorMap x[2];  // token tiles: boxes of 128 and 64 rows
+  CUtensorMap w[kQmMaxSeg];
+};
+struct Args {
+  Seg seg[kQmMaxSeg];
+  int nseg, K, G, T, tb, nt, nitems;
+  int* status;
+};
+
+struct Item {
+  int sg, j, t0, ntok;
+};
+// Item `it` -> (segment, weight tile, first token, tokens).  The gated mode has
+// one segment pair: gate (seg 0) and up (seg 1) rows j*128 .. j*128+127.
+template <int MODE>
+__device__ __forceinline__ Item item_at(const Args& a, int it) {
+  int sg = 0;
+  if (MODE == 0) {
+#pragma unroll
+    for (int s = 1; s < kQmMaxSeg; ++s)
+      if (s < a.nseg && it >= a.seg[s].item0) sg = s;
+  }
+  const int loc = it - a.seg[sg].item0;
+  Item r;
+  r.sg = sg;
+  r.j = loc / a.nt;
+  r.t0 = (loc % a.nt) * a.tb;
+  r.ntok = min(a.tb, a.T - r.t0);
+  return r;
+}
+
+// code byte i of w as a float: 0x4B000000 | q is 2^23 + q
+__device__ __forceinline__ float u8f(uint32_t w, int i) {
+  return __uint_as_float(prmt(w, 0x4B000000u, 0x7540u | (uint32_t)i)) - 8388608.f;
+}
+__device__ __forceinline__ float u4f(uint32_t w, int i) {
+  return __uint_as_float(((w >> (4 * i)) & 0xFu) | 0x4B000000u) - 8388608.f;
+}
+
+template <int BITS, int MODE>  // MODE 0: plain bf16 output; 1: gelu(gate) * up
+__global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant__ Maps maps, const Args a) {
+  constexpr int KQ = 128 / (8 * BITS);  // K tiles per packed stage
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // token tile landed
+  uint64_t* deqd = xfull + NS;                                      // dequantised weights written
+  uint64_t* mmad = deqd + NS;                                       // MMAs done with the stage
+  uint64_t* wqf = mmad + NS;                                        // packed codes landed
+  uint64_t* wqe = wqf + NQ;                                         // dequantisers done with them
+  uint64_t* accf = wqe + NQ;                                        // accumulator complete
+  uint64_t* acce = accf + 2;                                        // accumulator read out
+  volatile int* failed = reinterpret_cast<volatile int*>(acce + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2) + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NK = a.K / BK;
+  const int NKQ = (NK + KQ - 1) / KQ;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&deqd[s], NDQ);
+      mbar_init(&mmad[s], 1);
+    }
+    for (int s = 0; s < NQ; ++s) {
+      mbar_init(&wqf[s], 1);
+      mbar_init(&wqe[s], NDQ);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&accf[s], 1);
+      mbar_init(&acce[s], 4);
+    }
+    *failed = 0;
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- producer
+    if (lane == 0) {
+      int q = 0, qq = 0;
+      const CUtensorMap* xm = &maps.x[a.tb == 128 ? 0 : 1];
+      for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
+        const Item t = item_at<MODE>(a, it);
+        for (int kt = 0; kt < NK; ++kt, ++q) {
+          if (kt % KQ == 0) {
+            const int sq = qq % NQ;
+            if (qq >= NQ) pwait(&wqe[sq], (uint32_t)((qq / NQ) - 1) & 1u, failed, a.status, 401);
+            if (*failed) break;
+            uint8_t* wq = smem + OFF_WQ + sq * WQ_BYTES;
+            const int xb = (kt / KQ) * 128;  // byte column of the boxes
+            mbar_arrive_expect_tx(&wqf[sq], (uint32_t)WQ_BYTES);
+            if (MODE == 0) {
+              tma2d(wq, &maps.w[t.sg], xb, t.j * BN, &wqf[sq]);
+              tma2d(wq + WQ_BYTES / 2, &maps.w[t.sg], xb, t.j * BN + 128, &wqf[sq]);
+            } else {
+              tma2d(wq, &maps.w[0], xb, t.j * 128, &wqf[sq]);
+              tma2d(wq + WQ_BYTES / 2, &maps.w[1], xb, t.j * 128, &wqf[sq]);
+            }
+            ++qq;
+          }
+          const int s = q % NS;
+          if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 402);
+          if (*failed) break;
+          mbar_arrive_expect_tx(&xfull[s], (uint32_t)(a.tb * BK * 2));
+          tma2d(smem + s * STAGE, xm, kt * BK, t.t0, &xfull[s]);
+        }
+        if (*failed) break;
+      }
+      // every copy issued lands before the CTA ends
+      for (int k = q - NS < 0 ? 0 : q - NS; k < q; ++k) drain_wait(&xfull[k % NS], (uint32_t)(k / NS) & 1u);
+      for (int k = qq - NQ < 0 ? 0 : qq - NQ; k < qq; ++k) drain_wait(&wqf[k % NQ], (uint32_t)(k / NQ) & 1u);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      int q = 0, n = 0;
+      for (int it = blockIdx.x; it < a.nitems; it += gridDim.x, ++n) {
+        const int ab = n & 1;
+        const Item t = item_at<MODE>(a, it);
+        const uint32_t idesc = idesc_n((t.ntok + 15) & ~15);
+        if (n >= 2) pwait(&acce[ab], (uint32_t)((n / 2) - 1) & 1u, failed, a.status, 403);
+        tc_fence_after();
+        for (int kt = 0; kt < NK; ++kt, ++q) {
+          const int s = q % NS;
+          pwait(&xfull[s], (uint32_t)(q / NS) & 1u, failed, a.status, 404);
+          pwait(&deqd[s], (uint32_t)(q / NS) & 1u, failed, a.status, 405);
+          tc_fence_after();
+          const uint32_t sx = smem_u32(smem + s * STAGE), sw = smem_u32(smem + s * STAGE + X_BYTES);
+          if (!*failed) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_ss(tmem + ab * 256 + h * 128, sw128_desc(sw + h * (128 * 128) + 32 * k), sw128_desc(sx + 32 * k),
+                       idesc, (kt | k) != 0);
+          }
+          mma_commit(&mmad[s]);
+        }
+        mma_commit(&accf[ab]);
+      }
+      if (n > 0) drain_wait(&accf[(n - 1) & 1], (uint32_t)((n - 1) / 2) & 1u);
+    }
+  } else if (warp < 2 + NDQ) {
+    // ---- dequantisers: thread rr = row rr of the item's 256 rows (half rr / 128)
+    const int rr = threadIdx.x - 64, h = rr >> 7;
+    // raw bf16 scale / bias of the packed stage (item it, group block kg), KQ groups
+    auto load_sb = [&](int it, int kg, uint32_t (&sb)[KQ]) {
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) sb[i] = 0u;
+      if (it >= a.nitems) return;
+      const Item t = item_at<MODE>(a, it);
+      const Seg& sg = a.seg[MODE == 0 ? t.sg : h];
+      const int row = MODE == 0 ? t.j * BN + rr : t.j * 128 + (rr & 127);
+      if (row >= sg.N) return;
+      const bf16* sp = sg.s + (int64_t)row * a.G;
+      const bf16* bp = sg.b + (int64_t)row * a.G;
+#pragma unroll
+      for (int i = 0; i < KQ; ++i) {
+        const int kt = kg * KQ + i;
+        if (kt < NK) sb[i] = (uint32_t)ldg_u16(sp + kt) | ((uint32_t)ldg_u16(bp + kt) << 16);
+      }
+    };
+    uint32_t cur[KQ], nxt[KQ];
+    load_sb(blockIdx.x, 0, nxt);
+    int q = 0, qq = 0;
+    for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
+      for (int kt = 0; kt < NK; ++kt, ++q) {
+        const int s = q % NS, sq = qq % NQ, kq = kt % KQ;
+        if (kq == 0) {
+#pragma unroll
+          for (int i = 0; i < KQ; ++i) cur[i] = nxt[i];
+          const int kg = kt / KQ + 1;
+          if (kg < NKQ)
+            load_sb(it, kg, nxt);
+          else
+            load_sb(it + gridDim.x, 0, nxt);
+          pwait(&wqf[sq], (uint32_t)(qq / NQ) & 1u, failed, a.status, 406);
+        }
+        // the MMAs of the stage's previous use are done with its weights
+        if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 407);
+        uint32_t sbv = 0u;
+#pragma unroll
+        for (int i = 0; i < KQ; ++i)
+          if (i == kq) sbv = cur[i];
+        const float sv = __uint_as_float(sbv << 16), bv = __uint_as_float(sbv & 0xFFFF0000u);
+        const uint8_t* wrow_q = smem + OFF_WQ + sq * WQ_BYTES + rr * 128;
+        uint8_t* wrow = smem + s * STAGE + X_BYTES + rr * 128;
+        if (BITS == 8) {
+          // K tile kq = 16-byte chunks 4kq .. 4kq+3 of the 128-byte row (swizzled by row % 8)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 w = *reinterpret_cast<const uint4*>(wrow_q + (((4 * kq + c) ^ (rr & 7)) << 4));
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int hc = 0; hc < 2; ++hc) {  // output chunk 2c + hc = words 2hc, 2hc+1
+              const uint32_t w0 = ww[2 * hc], w1 = ww[2 * hc + 1];
+              const uint4 o = make_uint4(pack_bf16x2(fmaf(u8f(w0, 0), sv, bv), fmaf(u8f(w0, 1), sv, bv)),
+                                         pack_bf16x2(fmaf(u8f(w0, 2), sv, bv), fmaf(u8f(w0, 3), sv, bv)),
+                                         pack_bf16x2(fmaf(u8f(w1, 0), sv, bv), fmaf(u8f(w1, 1), sv, bv)),
+                                         pack_bf16x2(fmaf(u8f(w1, 2), sv, bv), fmaf(u8f(w1, 3), sv, bv)));
+              *reinterpret_cast<uint4*>(wrow + (((2 * c + hc) ^ (rr & 7)) << 4)) = o;
+            }
+          }
+        } else {
+          // K tile kq = 16-byte chunks 2kq, 2kq+1; one word = 8 codes = one output chunk
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const uint4 w = *reinterpret_cast<const uint4*>(wrow_q + (((2 * kq + c) ^ (rr & 7)) << 4));
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+              const uint32_t v = ww[wi];
+              const uint4 o = make_uint4(pack_bf16x2(fmaf(u4f(v, 0), sv, bv), fmaf(u4f(v, 1), sv, bv)),
+                                         pack_bf16x2(fmaf(u4f(v, 2), sv, bv), fmaf(u4f(v, 3), sv, bv)),
+                                         pack_bf16x2(fmaf(u4f(v, 4), sv, bv), fmaf(u4f(v, 5), sv, bv)),
+                                         pack_bf16x2(fmaf(u4f(v, 6), sv, bv), fmaf(u4f(v, 7), sv, bv)));
+              *reinterpret_cast<uint4*>(wrow + (((4 * c + wi) ^ (rr & 7)) << 4)) = o;
+            }
+          }
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor-core reads
+        __syncwarp();
+        const bool last = kq == KQ - 1 || kt == NK - 1;
+        if (lane == 0) {
+          mbar_arrive(&deqd[s]);
+          if (last) mbar_arrive(&wqe[sq]);
+        }
+        if (last) ++qq;
+      }
+    }
+  } else {
+    // ---- epilogue: TMEM lane = weight row 32 * (warp % 4) + lane, column = token
+    const int qw = warp & 3;
+    int n = 0;
+    for (int it = blockIdx.x; it < a.nitems; it += gridDim.x, ++n) {
+      const Item t = item_at<MODE>(a, it);
+      const int ab = n & 1, nc = (t.ntok + 15) / 16;
+      pwait(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 408);
+      tc_fence_after();
+      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * 256;
+      const bool ok = !*failed;
+      if (MODE == 0) {
+        const Seg& sg = a.seg[t.sg];
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int row = t.j * BN + hh * 128 + qw * 32 + lane;
+          bf16* o = sg.out + (int64_t)t.t0 * sg.ld + row;
+#pragma unroll 1
+          for (int cc = 0; cc < nc; ++cc) {
+            float v[16];
+            tmem_ld16(ta + hh * 128 + cc * 16, v);
+            tmem_ld_wait();
+            if (ok && row < sg.N) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (cc * 16 + i < t.ntok) o[(int64_t)(cc * 16 + i) * sg.ld] = __float2bfloat16_rn(v[i]);
+            }
+          }
+        }
+      } else {
+        const Seg& sg = a.seg[0];
+        const int f = t.j * 128 + qw * 32 + lane;
+        bf16* o = sg.out + (int64_t)t.t0 * sg.ld + f;
+#pragma unroll 1
+        for (int cc = 0; cc < nc; ++cc) {
+          float g[16], u[16];
+          tmem_ld16(ta + cc * 16, g);
+          tmem_ld16(ta + 128 + cc * 16, u);
+          tmem_ld_wait();
+          if (ok && f < sg.N) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (cc * 16 + i < t.ntok)
+                o[(int64_t)(cc * 16 + i) * sg.ld] = __float2bfloat16_rn(gelu_tanh(round_bf(g[i])) * round_bf(u[i]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[ab]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+}
+
+}  // namespace qm
+
+bool qgemm_supported(const QW& w, int group, int K) {
+  return (w.bits == 4 || w.bits == 8) && group == 64 && w.in == K && K % 64 == 0 && K >= 64 && w.out >= 1 &&
+         aligned(w.w, 16) && w.s && w.b;
+}
+
+int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool gated, int* status,
+                 cudaStream_t st) {
+  using namespace qm;
+  if (T <= 0) return FMOE_OK;
+  if (nseg < 1 || nseg > kQmMaxSeg || (gated && nseg != 2))
+    return set_error(FMOE_ERR_INVALID, "qgemm: %d weights", nseg);
+  if (!aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "qgemm: x not 16-byte aligned");
+  if (T > (1 << 30) / K) return set_error(FMOE_ERR_UNSUPPORTED, "qgemm: T=%lld too large", (long long)T);
+  const int bits = o[0].w->bits;
+  for (int s = 0; s < nseg; ++s) {
+    if (!qgemm_supported(*o[s].w, 64, K) || o[s].w->bits != bits)
+      return set_error(FMOE_ERR_UNSUPPORTED, "qgemm: weight %d (bits %d, in %d) is not a 4/8-bit group-64 weight of K %d",
+                       s, o[s].w->bits, o[s].w->in, K);
+    if (!o[s].out) return set_error(FMOE_ERR_INVALID, "qgemm: null output");
+  }
+  if (gated && o[0].w->out != o[1].w->out) return set_error(FMOE_ERR_INVALID, "qgemm: gate / up rows differ");
+  Args a = {};
+  a.nseg = nseg;
+  a.K = K;
+  a.G = K / 64;
+  a.T = (int)T;
+  a.status = status;
+  // tiles of 64 tokens when 128-token tiles would leave SMs idle
+  int nj = 0;
+  for (int s = 0; s < nseg; ++s) nj += gated ? 0 : (o[s].w->out + BN - 1) / BN;
+  if (gated) nj = (o[0].w->out + 127) / 128;
+  a.tb = (T > 64 && (int64_t)nj * ((T + 127) / 128) < kNumSMs) ? 64 : 128;
+  if (T <= 64) a.tb = 64;
+  a.nt = (int)((T + a.tb - 1) / a.tb);
+  int item = 0;
+  for (int s = 0; s < nseg; ++s) {
+    a.seg[s] = Seg{o[s].w->s, o[s].w->b, o[s].out, o[s].w->out, o[s].ld, item};
+    if (!gated) item += ((o[s].w->out + BN - 1) / BN) * a.nt;
+  }
+  a.nitems = gated ? nj * a.nt : item;
+  Maps m;
+  int rc;
+  {
+    const cuuint64_t dX[2] = {(cuuint64_t)K, (cuuint64_t)T}, sX[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t b128[2] = {64, 128}, b64[2] = {64, 64};
+    if ((rc = encode(&m.x[0], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dX, sX, b128, CU_TENSOR_MAP_SWIZZLE_128B, "x")) ||
+        (rc = encode(&m.x[1], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dX, sX, b64, CU_TENSOR_MAP_SWIZZLE_128B, "x")))
+      return rc;
+    const cuuint64_t rowb = (cuuint64_t)K * bits / 8;
+    for (int s = 0; s < nseg; ++s) {
+      const cuuint64_t dW[2] = {rowb, (cuuint64_t)o[s].w->out}, sW[1] = {rowb};
+      const cuuint32_t bW[2] = {128, 128};
+      if ((rc = encode(&m.w[s], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, o[s].w->w, dW, sW, bW, CU_TENSOR_MAP_SWIZZLE_128B,
+                       "weight codes")))
+        return rc;
+    }
+    for (int s = nseg; s < kQmMaxSeg; ++s) m.w[s] = m.w[0];
+  }
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(qgemm_kernel<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  });
+  const int grid = a.nitems < kNumSMs ? a.nitems : kNumSMs;
+  const char* name = bits == 8 ? (gated ? "qgemm_kernel<8, gated>" : "qgemm_kernel<8>")
+                               : (gated ? "qgemm_kernel<4, gated>" : "qgemm_kernel<4>");
+  {
+    ProfScope prof_(name, st);
+    if (bits == 8) {
+      if (gated)
+        qgemm_kernel<8, 1><<<grid, THREADS, SMEM, st>>>(m, a);
+      else
+        qgemm_kernel<8, 0><<<grid, THREADS, SMEM, st>>>(m, a);
+    } else {
+      if (gated)
+        qgemm_kernel<4, 1><<<grid, THREADS, SMEM, st>>>(m, a);
+      else
+        qgemm_kernel<4, 0><<<grid, THREADS, SMEM, st>>>(m, a);
+    }
+  }
+  return check_launch(name);
+}
+
+}  // namespace fmoe

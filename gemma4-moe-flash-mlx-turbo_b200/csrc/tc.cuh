@@ -43,7 +43,7 @@ __device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, volatile i
     if ((i & 1023) == 1023 && *failed) return false;
   }
   *failed = 1;
-  atomicCAS(status, 0, site);
+  if (status) atomicCAS(status, 0, site);
   return false;
 }
 // Bounded wait that ignores the failure flag (draining copies / MMAs in flight).

@@ -152,6 +152,26 @@ class KVCache:
         self.update(keys, values)
         return self
 
+    def attend_prefill(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos0: int,
+                       window: int | None = None, scale: float = 1.0) -> torch.Tensor:
+        """Prefill SDPA (fmoe_attn_prefill) of T new tokens of this one-sequence
+        cache: q bf16 [T, q_heads, head_dim], k_new / v_new bf16 [kv_heads, T,
+        head_dim] (the new rows as they will be stored); positions < pos0 come
+        from the ring.  window: the cache's own by default.  Returns bf16 [T,
+        q_heads, head_dim]; the cache is not modified."""
+        _need_cuda(q, k_new, v_new)
+        T, Hq, D = q.shape
+        if self.batch != 1 or D != self.head_dim or tuple(k_new.shape) != (self.kv_heads, T, D) or \
+                v_new.shape != k_new.shape:
+            raise ValueError(f"attend_prefill: q {tuple(q.shape)}, k_new {tuple(k_new.shape)} vs cache batch "
+                             f"{self.batch}, kv_heads {self.kv_heads}, head_dim {self.head_dim}")
+        win = self.window if window is None else window
+        out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=q.device)
+        qc, kc, vc = (t.to(torch.bfloat16).contiguous() for t in (q, k_new, v_new))
+        check(lib().fmoe_attn_prefill(ctypes.byref(self.c), _ptr(qc), Hq, T, pos0, win or 0, _ptr(kc), _ptr(vc),
+                                      _ptr(out), scale, _stream()))
+        return out
+
     def workspace_bytes(self, q_heads: int) -> int:
         return lib().fmoe_attn_decode_workspace_bytes(ctypes.byref(self.c), q_heads)
 

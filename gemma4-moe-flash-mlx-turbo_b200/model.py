@@ -20,7 +20,8 @@ import math
 
 import torch
 
-from . import (ExpertTable, ExpertsC, KvCacheC, QuantizedLinear, QWeightC, RouterC, _ptr, _stream, check, lib)
+from . import (ExpertTable, ExpertsC, KvCacheC, QuantizedLinear, QWeightC, RouterC, _ptr, _stream, check, lib,
+               prefill_prep)
 from .kv import KV_AFFINE, KV_BF16, KVCache
 
 
@@ -119,6 +120,22 @@ class Gemma4DecoderLayer:
         T = x.shape[0]
         check(lib().fmoe_decoder_layer_forward(ctypes.byref(self.cstruct()), ctypes.byref(cache.c), _ptr(x), T, pos,
                                                _ptr(pos_dev), _ptr(workspace), workspace.numel(), _stream()))
+        return x
+
+    def prefill_workspace_bytes(self, T) -> int:
+        return lib().fmoe_decoder_layer_prefill_workspace_bytes(ctypes.byref(self.cstruct()), T)
+
+    def prefill(self, x: torch.Tensor, cache: KVCache, pos0: int, workspace: torch.Tensor, window=None):
+        """In place: x bf16 [T, hidden], T prompt tokens of one sequence at
+        positions pos0 .. pos0 + T - 1 -> the layer output; the new K/V rows are
+        appended to `cache` (batch 1, or a one-sequence view).  window: the
+        cache's sliding window by default (None / 0: full causal attention).
+        fmoe_decoder_layer_prefill; workspace zero-filled before first use."""
+        T = x.shape[0]
+        win = cache.window if window is None else window
+        prep = prefill_prep(self.experts, x.device)
+        check(lib().fmoe_decoder_layer_prefill(ctypes.byref(self.cstruct()), ctypes.byref(cache.c), _ptr(x), T, pos0,
+                                               win or 0, _ptr(prep), _ptr(workspace), workspace.numel(), _stream()))
         return x
 
     def ep_workspace_bytes(self, T, cache: KVCache, world: int, cap: int) -> int:
@@ -326,6 +343,49 @@ class Gemma4Model:
     def fused_status(self, clear: bool = False) -> int:
         """Status word of the fused step's workspace (0: ok; synchronises)."""
         return lib().fmoe_workspace_status(_ptr(self._fused()[3]), int(clear), _stream())
+
+    def prefill(self, tokens: torch.Tensor, chunk: int = 2048):
+        """Run the prompt of every sequence through the model (one sequence at a
+        time, in chunks of at most `chunk` tokens through all layers), appending
+        its K/V rows, and leave each sequence's next greedy token in self.ids.
+        tokens: int32 [batch, T] (or [T] for batch 1), all sequences the same
+        length, starting at the current position.  TextModel::forward with
+        l = T (src/model/mod.rs:135-254) followed by Model::forward's lm_head on
+        the last position (mod.rs:336-362)."""
+        if self.ep is not None:
+            raise ValueError("prefill: expert-parallel models run their prompts through fmoe_moe_prefill per rank")
+        tok = tokens.to(device=self.device, dtype=torch.int32)
+        if tok.dim() == 1:
+            tok = tok.view(1, -1)
+        B, T = tok.shape
+        if B != self.batch or T < 1:
+            raise ValueError(f"prefill: tokens {tuple(tok.shape)} for batch {self.batch}")
+        chunk = max(1, min(chunk, T))
+        need = max(L.prefill_workspace_bytes(chunk) for L in self.layers)
+        if need == 0:
+            raise ValueError("prefill: unsupported layer configuration")
+        if getattr(self, "_pf_ws", None) is None or self._pf_ws.numel() < need:
+            self._pf_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        H = self.cfg["hidden"]
+        c = self._embed_c
+        pos0 = self.pos
+        for b in range(B):
+            views = [cache.batch_view(b, 1) if cache.batch > 1 else cache for cache in self.caches]
+            x = None
+            for s0 in range(0, T, chunk):
+                n = min(chunk, T - s0)
+                x = torch.empty(n, H, dtype=torch.bfloat16, device=self.device)
+                ids = tok[b, s0:s0 + n].contiguous()
+                check(lib().fmoe_embed_rows(ctypes.byref(c), _ptr(ids), n, self._emb_scale, _ptr(x), _stream()))
+                for L, v in zip(self.layers, views):
+                    L.prefill(x, v, pos0 + s0, self._pf_ws)
+            check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(x[-1:]), 1,
+                                     self.cfg["softcap"], _ptr(self.logits[b:b + 1]), _ptr(self.ids[b:b + 1]), None,
+                                     _ptr(self.lm_ws), self.lm_ws.numel(), _stream()))
+        self.set_position(pos0 + T)
+        for cache in self.caches:
+            cache._offset = self.pos
+        return self.ids
 
     def set_position(self, pos: int):
         self.pos = pos

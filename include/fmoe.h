@@ -344,6 +344,40 @@ int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* layer, const fmoe_kv_
                                int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Prefill of one layer for T prompt tokens of ONE sequence (cache batch 1, or
+ * a one-sequence view) at positions pos0 .. pos0 + T - 1: DecoderLayer::
+ * forward_gemma4 (src/model/mod.rs:67-119) with l = T.  Attention covers the
+ * cached positions and the new ones under the causal mask, and, when
+ * window > 0, only positions p - window < j <= p (create_attention_mask /
+ * create_sliding_mask, src/model/mod.rs:682-753); the new K/V rows (through
+ * the TurboQuant round trip when the cache has it, src/cache.rs:290-308) are
+ * appended after attention.  A sliding cache needs capacity >= window; a full
+ * one pos0 + T <= capacity.  bf16-storage caches only.  Projections and the
+ * dense MLP run on the tensor-core GEMM (4/8-bit, group 64); the routed
+ * experts as fmoe_moe_prefill, with expert_prep from fmoe_moe_prefill_prepare.
+ * x bf16 [T, hidden] is replaced by the layer output.  Workspace:
+ * fmoe_decoder_layer_prefill_workspace_bytes(layer, T), zero-filled once
+ * before first use; its first int is the status word (fmoe_workspace_status). */
+size_t fmoe_decoder_layer_prefill_workspace_bytes(const fmoe_decoder_layer_t* layer, int64_t T);
+int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache, void* x, int64_t T,
+                               int64_t pos0, int window, const void* expert_prep, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Prefill attention alone (the step inside fmoe_decoder_layer_prefill): q bf16
+ * [T, q_heads, head_dim] (normed, rotated), k_new / v_new bf16 [kv_heads, T,
+ * head_dim] the new rows as they will be stored; positions < pos0 are read
+ * from the ring.  out bf16 [T, q_heads * head_dim].  The cache is not
+ * modified (append the new rows afterwards with fmoe_kv_append). */
+int fmoe_attn_prefill(const fmoe_kv_cache_t* cache, const void* q, int q_heads, int64_t T, int64_t pos0, int window,
+                      const void* k_new, const void* v_new, void* out, float scale, void* stream);
+
+/* GeLUMLP::forward (src/model/mlp.rs:28-41) for T tokens on the tensor-core
+ * GEMM: y = down(gelu_tanh(gate(x)) * up(x)), bf16 [T, hidden]; 4/8-bit
+ * group-64 weights.  Workspace: fmoe_mlp_workspace_bytes(T, gate). */
+size_t fmoe_mlp_workspace_bytes(int64_t T, const fmoe_qweight_t* gate);
+int fmoe_mlp_forward(const void* x, int64_t T, const fmoe_qweight_t* gate, const fmoe_qweight_t* up,
+                     const fmoe_qweight_t* down, void* y, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Final norm + tied lm_head + logit softcap + greedy next token:
  * TextModel::forward's norm (src/model/mod.rs:254), Model::forward
  * (src/model/mod.rs:336-362): logits f32 [T, vocab] = tanh(l / softcap) *

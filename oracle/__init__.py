@@ -288,7 +288,15 @@ def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
         cache_v[:, :, pos % cap] = v
         hi = np.full(T, min(pos + 1, cap), np.int32)
         att = attn_decode_bf16(q, Hkv, cap, lo, hi, cache_k, cache_v, cfg["attn_scale"])
-    o = _qlin(_bf(att).reshape(T, Hq * D), L["o"])
+    return _ff_block(x, _bf(att).reshape(T, Hq * D), L, cfg), q
+
+
+def _ff_block(x, att, L, cfg):
+    """o_proj, residual and the feed-forward block of forward_gemma4 (mod.rs:80-118)
+    for T rows: x bf16 [T, H] the layer input, att bf16 [T, Hq * D]."""
+    T, H = x.shape
+    eps = cfg["eps"]
+    o = _qlin(att, L["o"])
     h = _bf(_f(x) + _f(rms_norm(o, L["post_attn_norm"], eps)))
     # feed-forward block: dense MLP + MoE in parallel (mod.rs:92-118)
     h1 = rms_norm(h, L["pre_ff_norm"], eps)
@@ -307,7 +315,80 @@ def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
     s = _bf(_f(rms_norm(d, L["post_ff_norm_1"], eps)) + _f(rms_norm(moe, L["post_ff_norm_2"], eps)))
     out = _bf(_f(h) + _f(rms_norm(s, L["post_ff_norm"], eps)))
     sc = _f(_bf(np.float32([cfg["scalar"]])))[0]
-    return _bf(_f(out) * sc), q
+    return _bf(_f(out) * sc)
+
+
+def mlp(x_bf16, gate, up, down):
+    """GeLUMLP::forward (src/model/mlp.rs:28-41): down(gelu_tanh(gate(x)) * up(x)), bf16 [T, H]."""
+    act = _bf(_gelu(_f(_qlin(x_bf16, gate))) * _f(_qlin(x_bf16, up)))
+    return _qlin(act, down)
+
+
+def attn_prefill_bf16(q_bf16, k_ring, v_ring, k_new, v_new, pos0: int, window: int, scale: float) -> np.ndarray:
+    """SDPA of T new tokens of one sequence over the stored rows plus the new
+    ones, as the reference's prefill runs it: update_and_fetch returns
+    concat(stored, new) (src/cache.rs:266-288) and the additive mask of
+    create_attention_mask / create_sliding_mask (src/model/mod.rs:682-753)
+    admits key position j for the query at position p iff j <= p and, with a
+    window, p - j < window; scaled_dot_product_attention then takes a softmax
+    over the admitted keys (gemma4_attention.rs:95-104).  float64 throughout.
+
+    q bf16 [T, Hq, D]; k_ring / v_ring bf16 [Hkv, cap, D] (position j < pos0 at
+    slot j % cap); k_new / v_new bf16 [Hkv, T, D].  Returns f32 [T, Hq, D]."""
+    q = _f(q_bf16).astype(np.float64)
+    T, Hq, D = q.shape
+    Hkv, cap = k_ring.shape[0], k_ring.shape[1]
+    R = Hq // Hkv
+    lo = max(0, pos0 - window + 1) if window else 0
+    old = np.arange(lo, pos0, dtype=np.int64)
+    K = np.concatenate([_f(k_ring)[:, old % cap], _f(k_new)], axis=1).astype(np.float64)
+    V = np.concatenate([_f(v_ring)[:, old % cap], _f(v_new)], axis=1).astype(np.float64)
+    kpos = np.concatenate([old, pos0 + np.arange(T, dtype=np.int64)])
+    qpos = pos0 + np.arange(T, dtype=np.int64)
+    ok = kpos[None, :] <= qpos[:, None]
+    if window:
+        ok &= (qpos[:, None] - kpos[None, :]) < window
+    out = np.empty((T, Hq, D), np.float64)
+    for h in range(Hq):
+        s = (q[:, h] @ K[h // R].T) * scale
+        s = np.where(ok, s, -np.inf)
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, h] = p @ V[h // R]
+    return out.astype(np.float32)
+
+
+def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg):
+    """Prefill of T prompt tokens of one sequence through DecoderLayer::
+    forward_gemma4 (src/model/mod.rs:67-119) at positions pos0 .. pos0 + T - 1.
+
+    x bf16 [T, H]; L, cfg as decoder_layer (bf16 caches; cfg["turbo_bits"] puts
+    the new K / V rows through the TurboQuant round trip, src/cache.rs:290-308);
+    cache_k / cache_v bf16 [1, Hkv, cap, D], updated with the new rows at slots
+    (pos0 + t) % cap.  window 0: full causal attention.  Returns (x_out bf16, q_rot bf16)."""
+    T, H = x.shape
+    Hq, Hkv, D, eps = cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"]
+    xn = rms_norm(x, L["input_norm"], eps)
+    q = _qlin(xn, L["q"]).reshape(T, Hq, D)
+    k = _qlin(xn, L["k"]).reshape(T, Hkv, D)
+    v = k.copy() if cfg["k_eq_v"] else _qlin(xn, L["v"]).reshape(T, Hkv, D)
+    qn = rms_norm(q, L["q_norm"], eps)
+    kn = rms_norm(k, L["k_norm"], eps)
+    q = np.stack([rope(qn[t], cfg["rope_dims"], cfg["rope_theta"], pos0 + t) for t in range(T)])
+    k = np.stack([rope(kn[t], cfg["rope_dims"], cfg["rope_theta"], pos0 + t) for t in range(T)])
+    v = rms_norm(v, None, eps)
+    tb = cfg.get("turbo_bits", 0)
+    if tb:
+        k = turbo_round_trip(k, tb)[0]
+        v = turbo_round_trip(v, tb)[0]
+    k_new, v_new = np.ascontiguousarray(k.transpose(1, 0, 2)), np.ascontiguousarray(v.transpose(1, 0, 2))
+    att = attn_prefill_bf16(q, cache_k[0], cache_v[0], k_new, v_new, pos0, window, cfg["attn_scale"])
+    cap = cache_k.shape[2]
+    for t in range(max(0, T - cap), T):
+        cache_k[0, :, (pos0 + t) % cap] = k_new[:, t]
+        cache_v[0, :, (pos0 + t) % cap] = v_new[:, t]
+    return _ff_block(x, _bf(att).reshape(T, Hq * D), L, cfg), q
 
 
 def lm_head(x, embed, final_norm, eps, softcap):

@@ -1,0 +1,163 @@
+"""GPU parity: prefill of a whole decoder layer (fmoe_decoder_layer_prefill) and
+its new pieces against the oracle:
+
+* the tensor-core quantised GEMM for many tokens (fmoe_qlinear with T > 8,
+  fmoe_mlp_forward) — QuantizedLinear::forward / GeLUMLP::forward,
+  src/model/mlp.rs:15-41;
+* the causal / sliding prefill attention (fmoe_attn_prefill) over the ring's
+  stored rows plus the new rows — src/model/mod.rs:682-753 masks,
+  src/cache.rs:266-288, gemma4_attention.rs:95-104;
+* a layer at the model's real shapes — src/model/mod.rs:67-119.
+
+Tolerances (max |gpu - oracle| / max |oracle|): 1e-2 for a GEMM, the MLP and
+attention (bf16 weights / P operands and bf16 outputs against the oracle's
+fp32 / float64 arithmetic); 2e-2 for a layer's output and 1e-2 for the
+appended K / V rows, as for the decode layer.  A token whose router logits put
+the k-th and (k+1)-th expert within 1e-3 may legitimately route differently;
+its layer-output row is left out of the comparison (every other row must
+match, and at least 90 % of the tokens are compared).
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import max_rel_err, to_np_bf16, to_np_u32, topk_sure
+from test_gpu_decoder import oracle_cfg, oracle_weights
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+LAYER_TOL = 2e-2
+
+
+@pytest.mark.parametrize("bits,N,K,T", [(8, 4096, 2816, 9), (8, 4096, 2816, 512), (8, 2816, 4096, 200),
+                                        (4, 2112, 2816, 64), (4, 2816, 2112, 333), (8, 1000, 704, 130),
+                                        (4, 300, 512, 1000)])
+def test_qlinear_many_tokens_matches_oracle(fm, orc, dev, bits, N, K, T):
+    g = torch.Generator(device=dev).manual_seed(N + K + T + bits)
+    q = fm.QuantizedLinear.from_float(torch.randn(N, K, generator=g, device=dev) * 0.02, bits)
+    x = torch.randn(T, K, generator=g, device=dev).to(torch.bfloat16)
+    y = q(x)
+    torch.cuda.synchronize()
+    want = orc.qmatmul(to_np_bf16(x), to_np_u32(q.weight), to_np_bf16(q.scales), to_np_bf16(q.biases), K, bits)
+    err = max_rel_err(orc.bf16_to_f32(to_np_bf16(y)), want)
+    assert err <= TOL, err
+
+
+@pytest.mark.parametrize("T", [16, 300])
+def test_mlp_forward_matches_oracle(fm, orc, dev, T):
+    H, I = 2816, 2112
+    g = torch.Generator(device=dev).manual_seed(T)
+    gate, up, down = (fm.QuantizedLinear.from_float(torch.randn(o, i, generator=g, device=dev) * 0.02, 4)
+                      for o, i in ((I, H), (I, H), (H, I)))
+    x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+    y = fm.mlp_forward(x, gate, up, down)
+    torch.cuda.synchronize()
+    ql = lambda w: (to_np_u32(w.weight), to_np_bf16(w.scales), to_np_bf16(w.biases), w.in_features, w.bits)
+    want = orc.mlp(to_np_bf16(x), ql(gate), ql(up), ql(down))
+    err = max_rel_err(orc.bf16_to_f32(to_np_bf16(y)), orc.bf16_to_f32(want))
+    assert err <= TOL, err
+
+
+ATTN_CASES = [
+    # D, Hkv, Hq, cache capacity, window (0: full), pos0, T
+    (256, 8, 16, 1024, 1024, 0, 512),     # sliding layer, first chunk of a prompt
+    (256, 8, 16, 64, 64, 100, 300),       # ring wrapped, prompt longer than the window
+    (256, 8, 16, 1024, 1024, 1500, 77),   # a later chunk: window spans ring and new rows
+    (512, 2, 16, 2048, 0, 37, 200),       # full layer (K == V heads), causal
+    (512, 2, 16, 2048, 0, 0, 1),
+    (256, 8, 16, 64, 64, 5, 1),
+]
+
+
+@pytest.mark.parametrize("D,Hkv,Hq,cap,window,pos0,T", ATTN_CASES)
+def test_attn_prefill_matches_oracle(fm, orc, dev, D, Hkv, Hq, cap, window, pos0, T):
+    g = torch.Generator(device=dev).manual_seed(D + cap + pos0 + T)
+    cache = fm.KVCache(1, Hkv, D, cap, window=window or None, device=dev)
+    if pos0:
+        cache.update(torch.randn(1, Hkv, pos0, D, generator=g, device=dev).to(torch.bfloat16),
+                     torch.randn(1, Hkv, pos0, D, generator=g, device=dev).to(torch.bfloat16))
+    q = (torch.randn(T, Hq, D, generator=g, device=dev) * 0.08).to(torch.bfloat16)
+    kn = torch.randn(Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    vn = torch.randn(Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    out = cache.attend_prefill(q, kn, vn, pos0, window=window)
+    torch.cuda.synchronize()
+    a = cache.arrays()
+    want = orc.attn_prefill_bf16(to_np_bf16(q), to_np_bf16(a["k"])[0], to_np_bf16(a["v"])[0], to_np_bf16(kn),
+                                 to_np_bf16(vn), pos0, window, 1.0)
+    err = max_rel_err(orc.bf16_to_f32(to_np_bf16(out)), want)
+    assert err <= TOL, err
+
+
+def _prefill_case(fm, orc, dev, full, T, pos0, window, turbo, seed):
+    cfg = dict(fm.GEMMA4_26B)
+    L = fm.Gemma4DecoderLayer.random(cfg, full, seed=seed, device=dev)
+    cap = window if window else 1024
+    cache = fm.KVCache(1, L.num_kv_heads, L.head_dim, cap, window=window or None, turbo_bits=turbo, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    if pos0:
+        cache.update(torch.randn(1, L.num_kv_heads, pos0, L.head_dim, generator=g, device=dev).to(torch.bfloat16),
+                     torch.randn(1, L.num_kv_heads, pos0, L.head_dim, generator=g, device=dev).to(torch.bfloat16))
+    x = torch.randn(T, cfg["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    x_in = to_np_bf16(x)
+    a = cache.arrays()
+    ck, cv = to_np_bf16(a["k"]).copy(), to_np_bf16(a["v"]).copy()
+    ws = torch.zeros(L.prefill_workspace_bytes(T), dtype=torch.uint8, device=dev)
+    L.prefill(x, cache, pos0, ws, window=window)
+    torch.cuda.synchronize()
+    assert fm.lib().fmoe_workspace_status(ws.data_ptr(), 0, None) == 0
+    ocfg = oracle_cfg(L, cfg)
+    ocfg["turbo_bits"] = turbo
+    xo, _ = orc.decoder_layer_prefill(x_in, oracle_weights(L), ck, cv, pos0, window, ocfg)
+    sure = topk_sure(ocfg["_router_logits"], L.top_k)
+    a = cache.arrays()
+    rows = [(pos0 + t) % cap for t in range(max(0, T - cap), T)]
+    kerr = max_rel_err(orc.bf16_to_f32(to_np_bf16(a["k"])[:, :, rows]), orc.bf16_to_f32(ck[:, :, rows]))
+    verr = max_rel_err(orc.bf16_to_f32(to_np_bf16(a["v"])[:, :, rows]), orc.bf16_to_f32(cv[:, :, rows]))
+    got, want = orc.bf16_to_f32(to_np_bf16(x)), orc.bf16_to_f32(xo)
+    err = max_rel_err(got[sure], want[sure])
+    print(f"layer prefill T={T} full={full}: max rel err {err:.4f} over {int(sure.sum())} of {T} tokens; "
+          f"k {kerr:.4f} v {verr:.4f}")
+    assert sure.mean() >= 0.9, sure.mean()
+    assert kerr <= TOL and verr <= TOL, (kerr, verr)
+    assert err <= LAYER_TOL, err
+
+
+@pytest.mark.parametrize("full,T,pos0,window,turbo", [
+    (False, 512, 0, 1024, 0),     # sliding layer, first 512 prompt tokens
+    (False, 300, 40, 128, 0),     # prompt longer than the window, ring already holding 40 positions
+    (True, 300, 0, 0, 0),         # full layer (K == V, partial RoPE)
+    (False, 64, 9, 1024, 3),      # TurboQuant-3 cache (the reference's default)
+])
+def test_decoder_layer_prefill_matches_oracle(fm, orc, dev, full, T, pos0, window, turbo):
+    _prefill_case(fm, orc, dev, full, T, pos0, window, turbo, seed=71 + T + full)
+
+
+def test_prefill_then_decode_matches_token_by_token_decode(fm, dev):
+    """A 2-layer model (one sliding layer with a window shorter than the prompt,
+    one full layer): prefill of a 40-token prompt gives the same last-position
+    logits as feeding the prompt one token at a time through the decode path,
+    and the decode step after it (reading the rows the prefill appended) agrees
+    as well."""
+    cfg = dict(fm.GEMMA4_26B)
+    cfg["window"] = 16
+    cfg["full_every"] = 2
+    prompt = torch.randint(0, cfg["vocab"], (40,), generator=torch.Generator().manual_seed(3)).to(torch.int32)
+    a = fm.Gemma4Model.random(cfg, 1, 128, seed=5, device=dev, n_layers=2)
+    a.prefill(prompt.to(dev))
+    b = fm.Gemma4Model.random(cfg, 1, 128, seed=5, device=dev, n_layers=2)
+    for t in range(40):
+        b.ids.copy_(prompt[t:t + 1].to(dev))
+        b.decode_step()
+    torch.cuda.synchronize()
+    assert a.pos == b.pos == 40
+    err = (a.logits - b.logits).abs().max().item() / b.logits.abs().max().item()
+    assert err <= 5e-2, err
+    s = torch.sort(b.logits[0], descending=True).values
+    if (s[0] - s[1]).item() > 0.05 * s[0].abs().item():  # a clear greedy choice
+        assert int(a.ids[0]) == int(b.ids[0])
+    b.ids.copy_(a.ids)  # the same next input on both
+    a.decode_step()
+    b.decode_step()
+    torch.cuda.synchronize()
+    err2 = (a.logits - b.logits).abs().max().item() / b.logits.abs().max().item()
+    assert err2 <= 5e-2, err2
