@@ -84,6 +84,9 @@ def parse():
                     help="run only the prefill MoE block (BASELINE config 2: T tokens, Zipf-skewed routing) on the "
                          "tcgen05 path: four calls, L2 flushed before each, the last one timed (a small case for "
                          "profilers)")
+    ap.add_argument("--pf-attn-case", default=None, metavar="D:HKV:HQ:WINDOW:T",
+                    help="run only the prefill attention (fmoe_attn_prefill) of a T-token prompt from position 0 "
+                         "(WINDOW 0: full causal): four launches, the last one timed (a small case for profilers)")
     ap.add_argument("--layers", type=int, default=30,
                     help="decoder layers in the step (30 = the model; fewer only for small profiling cases)")
     return ap.parse_args()
@@ -1174,6 +1177,32 @@ def run_attn_case(args):
     print(json.dumps({"attn_case": args.attn_case, **res}), flush=True)
 
 
+def run_pf_attn_case(args):
+    import torch
+    import __graft_entry__
+
+    fm = __graft_entry__.load_package()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    D, Hkv, Hq, win, T = (int(v) for v in args.pf_attn_case.split(":"))
+    g = torch.Generator(device=dev).manual_seed(12)
+    cache = fm.KVCache(1, Hkv, D, max(T, win or T), window=win or None, device=dev)
+    q = (torch.randn(T, Hq, D, generator=g, device=dev) * 0.08).to(torch.bfloat16)
+    kn = torch.randn(Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    vn = torch.randn(Hkv, T, D, generator=g, device=dev).to(torch.bfloat16)
+    for _ in range(4):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        cache.attend_prefill(q, kn, vn, 0, window=win)
+        b.record()
+        torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3
+    keys = sum(min(t + 1, win) if win else t + 1 for t in range(T))
+    flops = 4.0 * Hq * D * keys
+    print(json.dumps({"pf_attn_case": args.pf_attn_case, "us": round(us, 1), "alg_flops": int(flops),
+                      "tflops": round(flops / us / 1e6, 1)}), flush=True)
+
+
 def run_qlinear_case(args):
     import torch
     import __graft_entry__
@@ -1198,7 +1227,8 @@ def run_qlinear_case(args):
     us = a.elapsed_time(b) * 1e3
     nbytes = out_f * in_f * bits // 8 + 2 * out_f * (in_f // 64) * 2
     print(json.dumps({"qlinear_case": args.qlinear_case, "us": round(us, 1), "weight_bytes": nbytes,
-                      "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
+                      "gbs": round(nbytes / us / 1e3, 1), "tflops": round(2.0 * T * out_f * in_f / us / 1e6, 1)}),
+          flush=True)
 
 
 def prefill_flops(m, T):
@@ -1319,6 +1349,8 @@ def main():
         run_attn_case(args)
     elif args.qlinear_case:
         run_qlinear_case(args)
+    elif args.pf_attn_case:
+        run_pf_attn_case(args)
     elif args.impl == "reference":
         run_reference(args, rank, world)
     elif args.workload.startswith("decode30"):
