@@ -73,7 +73,7 @@ class Gemma4DecoderLayer:
         self.q_norm, self.k_norm = q_norm, k_norm
         self.norms = norms  # dict: input, post_attn, pre_ff, post_ff_1, pre_ff_2, post_ff_2, post_ff
         self.mlp = mlp      # (gate, up, down) QuantizedLinear
-        self.router = router  # dict: proj QuantizedLinear, router_scale, per_expert_scale, root_size
+        self.router = router  # dict: proj QuantizedLinear, router_scale, per_expert_scale, root_size[, logit_bias]
         self.experts = experts
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
         self.rope_dims, self.rope_theta, self.k_eq_v = rope_dims, rope_theta, k_eq_v
@@ -85,8 +85,8 @@ class Gemma4DecoderLayer:
             n = self.norms
             empty = QWeightC(None, None, None, 0, 0, 0, 0, None, 0, 0)
             r = self.router
-            rc = RouterC(r["proj"].cstruct(), _ptr(r.get("router_scale")), _ptr(r.get("per_expert_scale")), None,
-                         r["root_size"], self.eps, 1, self.top_k)
+            rc = RouterC(r["proj"].cstruct(), _ptr(r.get("router_scale")), _ptr(r.get("per_expert_scale")),
+                         _ptr(r.get("logit_bias")), r["root_size"], self.eps, 1, self.top_k)
             self._c = DecoderLayerC(
                 self.q_proj.cstruct(), self.k_proj.cstruct(),
                 empty if self.k_eq_v else self.v_proj.cstruct(), self.o_proj.cstruct(),

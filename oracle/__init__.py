@@ -307,7 +307,7 @@ def _ff_block(x, att, L, cfg):
     d = _qlin(act, L["down"])
     wr, wr_bits, rscale, pes, root = L["router"]
     ids, wts, logits = router(h2, wr, cfg["top_k"], wr_bits, use_norm=True, root_size=root, eps=eps,
-                              router_scale=rscale, per_expert_scale=pes)
+                              router_scale=rscale, per_expert_scale=pes, logit_bias=L.get("logit_bias"))
     cfg["_router_logits"] = logits
     buf, stride, offs = L["experts"]
     y, _ = moe_experts(h2, ids, wts, buf, stride, offs, H, cfg["inter_expert"])
@@ -359,14 +359,18 @@ def attn_prefill_bf16(q_bf16, k_ring, v_ring, k_new, v_new, pos0: int, window: i
     return out.astype(np.float32)
 
 
-def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg):
+def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg, new_rows=None):
     """Prefill of T prompt tokens of one sequence through DecoderLayer::
     forward_gemma4 (src/model/mod.rs:67-119) at positions pos0 .. pos0 + T - 1.
 
     x bf16 [T, H]; L, cfg as decoder_layer (bf16 caches; cfg["turbo_bits"] puts
     the new K / V rows through the TurboQuant round trip, src/cache.rs:290-308);
     cache_k / cache_v bf16 [1, Hkv, cap, D], updated with the new rows at slots
-    (pos0 + t) % cap.  window 0: full causal attention.  Returns (x_out bf16, q_rot bf16)."""
+    (pos0 + t) % cap.  window 0: full causal attention.  The new rows computed here
+    are left in cfg["_new_rows"] ([Hkv, T, D] each); new_rows = (k, v) replaces them
+    in attention and in the cache (a checker comparing the rows on their own can
+    then hold the rest of the layer to the rows actually stored).  Returns
+    (x_out bf16, q_rot bf16)."""
     T, H = x.shape
     Hq, Hkv, D, eps = cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"]
     xn = rms_norm(x, L["input_norm"], eps)
@@ -378,11 +382,15 @@ def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg):
     q = np.stack([rope(qn[t], cfg["rope_dims"], cfg["rope_theta"], pos0 + t) for t in range(T)])
     k = np.stack([rope(kn[t], cfg["rope_dims"], cfg["rope_theta"], pos0 + t) for t in range(T)])
     v = rms_norm(v, None, eps)
+    cfg["_pre_round_trip"] = (k.copy(), v.copy())  # [T, Hkv, D]
     tb = cfg.get("turbo_bits", 0)
     if tb:
         k = turbo_round_trip(k, tb)[0]
         v = turbo_round_trip(v, tb)[0]
     k_new, v_new = np.ascontiguousarray(k.transpose(1, 0, 2)), np.ascontiguousarray(v.transpose(1, 0, 2))
+    cfg["_new_rows"] = (k_new, v_new)
+    if new_rows is not None:
+        k_new, v_new = (np.ascontiguousarray(r, np.uint16) for r in new_rows)
     att = attn_prefill_bf16(q, cache_k[0], cache_v[0], k_new, v_new, pos0, window, cfg["attn_scale"])
     cap = cache_k.shape[2]
     for t in range(max(0, T - cap), T):

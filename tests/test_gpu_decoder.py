@@ -42,6 +42,7 @@ def oracle_weights(L):
         "router": (to_np_bf16(r["proj"].weight), 16, to_np_bf16(r["router_scale"]), to_np_bf16(r["per_expert_scale"]),
                    r["root_size"]),
         "experts": (L.experts.buf.cpu().numpy(), L.experts.stride, L.experts.offsets),
+        "logit_bias": None if r.get("logit_bias") is None else r["logit_bias"].float().cpu().numpy(),
     }
 
 
