@@ -71,6 +71,9 @@ def parse():
     ap.add_argument("--profile-step", action="store_true",
                     help="after warm-up, run one eager step between cudaProfilerStart / Stop and exit (for "
                          "ncu --profile-from-start off launch lists of the decode30 / ep_* workloads)")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="decode30: after one warm-up prefill of the 2048-token context, run one more prefill "
+                         "between cudaProfilerStart / Stop and exit (ncu launch lists of the prefill)")
     ap.add_argument("--no-ep-extra", action="store_true",
                     help="decode30 at N > 1: skip the expert-parallel config-5 sub-measurements")
     ap.add_argument("--no-attn", action="store_true", help="skip the quantised-KV decode-attention sub-measurement")
@@ -351,7 +354,12 @@ def run_decoder(args, rank, world, local):
         # BASELINE config 4's context: a CTX-token prompt per sequence prefilled
         # through the whole decoder, which fills every KV cache
         prompt = torch.randint(0, cfg["vocab"], (T, CTX), generator=g, device=dev, dtype=torch.int32)
-        pf_result = decoder_prefill(torch, m, prompt, peaks, timed_reps=0 if args.profile_step else 3)
+        quiet = args.profile_step or args.profile_prefill
+        pf_result = decoder_prefill(torch, m, prompt, peaks, timed_reps=0 if quiet else 3)
+        if args.profile_prefill:
+            m.set_position(0)
+            profiled_step(torch, lambda: m.prefill(prompt))
+            return
     else:
         # expert-parallel models have no whole-decoder prefill: CTX random K/V positions
         for L, c in zip(m.layers, m.caches):

@@ -8,17 +8,19 @@
 // one tile of up to 128 tokens; items run weight-tile-major, so the CTAs that
 // run at the same time share a weight tile in L2, and x stays in L2.
 //   warp 0      producer: TMA of the token tile (bf16 [tokens][64], 128-byte
-//               swizzle, one per K tile) and of the packed codes (two boxes of
+//               swizzle, one per K tile; a ring of 4, so tiles run up to 4 K
+//               tiles ahead of the MMA) and of the packed codes (two boxes of
 //               128 rows x 128 bytes = 2 (8-bit) or 4 (4-bit) K tiles, 128-byte
-//               swizzle)
+//               swizzle; 3 stages ahead of the dequantisers)
 //   warp 1      MMA issuer: per K tile 2 x 4 tcgen05.mma (K 16) with the
 //               dequantised weights as the M = 128 operand (two halves) and
 //               the tokens as N (rounded up to 16), into one of two TMEM
 //               accumulators
 //   warps 2-9   dequantise one weight row each: w = bf16(s * q + b), s * q + b
 //               in fp32, written in the canonical K-major 128-byte-swizzled
-//               layout; the row's scale and bias are loaded from global memory
-//               one packed stage ahead
+//               layout (a ring of 2 K tiles, each released by the MMA's commit);
+//               the row's scale and bias are loaded from global memory one
+//               packed stage ahead
 //   warps 10-13 epilogue: tcgen05.ld (TMEM lane = weight row, column = token),
 //               bf16 stores, or (gated mode) gelu(gate) * up from the two
 //               halves, the first projection of the GeLU MLP
@@ -36,19 +38,21 @@ using namespace tc;
 
 constexpr int BK = 64;                     // K per tile = one quantisation group
 constexpr int BN = 256;                    // weight rows per item (two M = 128 halves)
-constexpr int NS = 3;                      // K-tile stages: token tile + dequantised weights
-constexpr int NQ = 2;                      // packed-code stages
+constexpr int NX = 4;                      // token-tile ring (TMA lookahead of the MMA)
+constexpr int NW = 2;                      // dequantised-weight ring
+constexpr int NQ = 3;                      // packed-code stages (TMA lookahead of the dequantisers)
 constexpr int X_BYTES = 128 * BK * 2;      // 16 KB: up to 128 tokens x 64 bf16
 constexpr int WB_BYTES = BN * BK * 2;      // 32 KB: 256 rows x 64 bf16
 constexpr int WQ_BYTES = BN * 128;         // 32 KB: 256 rows x 128 bytes of codes
-constexpr int STAGE = X_BYTES + WB_BYTES;  // 48 KB
-constexpr int OFF_WQ = NS * STAGE;
+constexpr int OFF_X = 0;
+constexpr int OFF_WB = OFF_X + NX * X_BYTES;
+constexpr int OFF_WQ = OFF_WB + NW * WB_BYTES;
 constexpr int OFF_BAR = OFF_WQ + NQ * WQ_BYTES;
 constexpr int SMEM = OFF_BAR + 256 + 1024;  // + slack to align the base to 1024 bytes
-constexpr int NDQ = 8;
+constexpr int NDQ = 8;  // dequantising warps: one thread per weight row
 constexpr int THREADS = (2 + NDQ + 4) * 32;
 constexpr int TMEM_COLS = 512;  // [2 accumulators][2 halves][128 tokens] fp32
-static_assert(STAGE % 1024 == 0 && OFF_WQ % 1024 == 0 && WQ_BYTES % 1024 == 0, "stage alignment");
+static_assert(OFF_WB % 1024 == 0 && OFF_WQ % 1024 == 0 && OFF_BAR % 1024 == 0, "ring alignment");
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
 struct Seg {
@@ -90,6 +94,14 @@ __device__ __forceinline__ Item item_at(const Args& a, int it) {
   return r;
 }
 
+// 16-bit load issued where it stands (volatile: the compiler may not sink it to
+// its first use, a packed stage later)
+__device__ __forceinline__ uint16_t ldg_u16_now(const void* p) {
+  unsigned short r;
+  asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(r) : "l"(p));
+  return r;
+}
+
 // code byte i of w as a float: 0x4B000000 | q is 2^23 + q
 __device__ __forceinline__ float u8f(uint32_t w, int i) {
   return __uint_as_float(prmt(w, 0x4B000000u, 0x7540u | (uint32_t)i)) - 8388608.f;
@@ -104,9 +116,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + OFF_BAR);  // token tile landed
-  uint64_t* deqd = xfull + NS;                                      // dequantised weights written
-  uint64_t* mmad = deqd + NS;                                       // MMAs done with the stage
-  uint64_t* wqf = mmad + NS;                                        // packed codes landed
+  uint64_t* xfree = xfull + NX;                                     // MMAs done with the token tile
+  uint64_t* deqd = xfree + NX;                                      // dequantised weights written
+  uint64_t* wfree = deqd + NW;                                      // MMAs done with those weights
+  uint64_t* wqf = wfree + NW;                                       // packed codes landed
   uint64_t* wqe = wqf + NQ;                                         // dequantisers done with them
   uint64_t* accf = wqe + NQ;                                        // accumulator complete
   uint64_t* acce = accf + 2;                                        // accumulator read out
@@ -116,10 +129,13 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
   const int NK = a.K / BK;
   const int NKQ = (NK + KQ - 1) / KQ;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < NX; ++s) {
       mbar_init(&xfull[s], 1);
+      mbar_init(&xfree[s], 1);
+    }
+    for (int s = 0; s < NW; ++s) {
       mbar_init(&deqd[s], NDQ);
-      mbar_init(&mmad[s], 1);
+      mbar_init(&wfree[s], 1);
     }
     for (int s = 0; s < NQ; ++s) {
       mbar_init(&wqf[s], 1);
@@ -153,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
         for (int kt = 0; kt < NK; ++kt, ++q) {
           if (kt % KQ == 0) {
             const int sq = qq % NQ;
-            if (qq >= NQ) pwait(&wqe[sq], (uint32_t)((qq / NQ) - 1) & 1u, failed, a.status, 401);
+            if (qq >= NQ) pwait_sleep(&wqe[sq], (uint32_t)((qq / NQ) - 1) & 1u, failed, a.status, 401, 64);
             if (*failed) break;
             uint8_t* wq = smem + OFF_WQ + sq * WQ_BYTES;
             const int xb = (kt / KQ) * 128;  // byte column of the boxes
@@ -167,16 +183,16 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
             }
             ++qq;
           }
-          const int s = q % NS;
-          if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 402);
+          const int s = q % NX;
+          if (q >= NX) pwait_sleep(&xfree[s], (uint32_t)((q / NX) - 1) & 1u, failed, a.status, 402, 64);
           if (*failed) break;
           mbar_arrive_expect_tx(&xfull[s], (uint32_t)(a.tb * BK * 2));
-          tma2d(smem + s * STAGE, xm, kt * BK, t.t0, &xfull[s]);
+          tma2d(smem + OFF_X + s * X_BYTES, xm, kt * BK, t.t0, &xfull[s]);
         }
         if (*failed) break;
       }
       // every copy issued lands before the CTA ends
-      for (int k = q - NS < 0 ? 0 : q - NS; k < q; ++k) drain_wait(&xfull[k % NS], (uint32_t)(k / NS) & 1u);
+      for (int k = q - NX < 0 ? 0 : q - NX; k < q; ++k) drain_wait(&xfull[k % NX], (uint32_t)(k / NX) & 1u);
       for (int k = qq - NQ < 0 ? 0 : qq - NQ; k < qq; ++k) drain_wait(&wqf[k % NQ], (uint32_t)(k / NQ) & 1u);
     }
   } else if (warp == 1) {
@@ -190,11 +206,11 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
         if (n >= 2) pwait(&acce[ab], (uint32_t)((n / 2) - 1) & 1u, failed, a.status, 403);
         tc_fence_after();
         for (int kt = 0; kt < NK; ++kt, ++q) {
-          const int s = q % NS;
-          pwait(&xfull[s], (uint32_t)(q / NS) & 1u, failed, a.status, 404);
-          pwait(&deqd[s], (uint32_t)(q / NS) & 1u, failed, a.status, 405);
+          const int s = q % NX, w = q % NW;
+          pwait(&xfull[s], (uint32_t)(q / NX) & 1u, failed, a.status, 404);
+          pwait(&deqd[w], (uint32_t)(q / NW) & 1u, failed, a.status, 405);
           tc_fence_after();
-          const uint32_t sx = smem_u32(smem + s * STAGE), sw = smem_u32(smem + s * STAGE + X_BYTES);
+          const uint32_t sx = smem_u32(smem + OFF_X + s * X_BYTES), sw = smem_u32(smem + OFF_WB + w * WB_BYTES);
           if (!*failed) {
 #pragma unroll
             for (int h = 0; h < 2; ++h)
@@ -203,7 +219,8 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
                 mma_ss(tmem + ab * 256 + h * 128, sw128_desc(sw + h * (128 * 128) + 32 * k), sw128_desc(sx + 32 * k),
                        idesc, (kt | k) != 0);
           }
-          mma_commit(&mmad[s]);
+          mma_commit(&xfree[s]);
+          mma_commit(&wfree[w]);
         }
         mma_commit(&accf[ab]);
       }
@@ -226,7 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
 #pragma unroll
       for (int i = 0; i < KQ; ++i) {
         const int kt = kg * KQ + i;
-        if (kt < NK) sb[i] = (uint32_t)ldg_u16(sp + kt) | ((uint32_t)ldg_u16(bp + kt) << 16);
+        if (kt < NK) sb[i] = (uint32_t)ldg_u16_now(sp + kt) | ((uint32_t)ldg_u16_now(bp + kt) << 16);
       }
     };
     uint32_t cur[KQ], nxt[KQ];
@@ -234,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
     int q = 0, qq = 0;
     for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
       for (int kt = 0; kt < NK; ++kt, ++q) {
-        const int s = q % NS, sq = qq % NQ, kq = kt % KQ;
+        const int s = q % NW, sq = qq % NQ, kq = kt % KQ;
         if (kq == 0) {
 #pragma unroll
           for (int i = 0; i < KQ; ++i) cur[i] = nxt[i];
@@ -245,15 +262,15 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
             load_sb(it + gridDim.x, 0, nxt);
           pwait(&wqf[sq], (uint32_t)(qq / NQ) & 1u, failed, a.status, 406);
         }
-        // the MMAs of the stage's previous use are done with its weights
-        if (q >= NS) pwait(&mmad[s], (uint32_t)((q / NS) - 1) & 1u, failed, a.status, 407);
+        // the MMAs of the slot's previous use are done with its weights
+        if (q >= NW) pwait(&wfree[s], (uint32_t)((q / NW) - 1) & 1u, failed, a.status, 407);
         uint32_t sbv = 0u;
 #pragma unroll
         for (int i = 0; i < KQ; ++i)
           if (i == kq) sbv = cur[i];
         const float sv = __uint_as_float(sbv << 16), bv = __uint_as_float(sbv & 0xFFFF0000u);
         const uint8_t* wrow_q = smem + OFF_WQ + sq * WQ_BYTES + rr * 128;
-        uint8_t* wrow = smem + s * STAGE + X_BYTES + rr * 128;
+        uint8_t* wrow = smem + OFF_WB + s * WB_BYTES + rr * 128;
         if (BITS == 8) {
           // K tile kq = 16-byte chunks 4kq .. 4kq+3 of the 128-byte row (swizzled by row % 8)
 #pragma unroll
@@ -304,7 +321,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
     for (int it = blockIdx.x; it < a.nitems; it += gridDim.x, ++n) {
       const Item t = item_at<MODE>(a, it);
       const int ab = n & 1, nc = (t.ntok + 15) / 16;
-      pwait(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 408);
+      pwait_sleep(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 408, 256);
       tc_fence_after();
       const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * 256;
       const bool ok = !*failed;

@@ -46,6 +46,21 @@ __device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, volatile i
   if (status) atomicCAS(status, 0, site);
   return false;
 }
+// pwait for warps that wait long (a whole tile or item): after a short spin the
+// poll backs off by `ns` nanoseconds, so the waiting warps leave the issue slots
+// to the warps doing the work.  Bounded by the same poll count as pwait.
+__device__ __forceinline__ bool pwait_sleep(uint64_t* bar, uint32_t parity, volatile int* failed, int* status, int site,
+                                            unsigned ns) {
+  if (*failed) return false;
+  for (int i = 0; i < kMaxWaitIters; ++i) {
+    if (try_wait(bar, parity)) return true;
+    if (i >= 8) __nanosleep(ns);
+    if ((i & 255) == 255 && *failed) return false;
+  }
+  *failed = 1;
+  if (status) atomicCAS(status, 0, site);
+  return false;
+}
 // Bounded wait that ignores the failure flag (draining copies / MMAs in flight).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   for (int i = 0; i < kMaxWaitIters && !try_wait(bar, parity); ++i) {
