@@ -92,7 +92,9 @@ __global__ void __launch_bounds__(256) turbo_round_trip_kernel(const bf16* __res
 // ---------------------------------------------------------------------------
 // Decode-step attention input: the q / k / v projections (fp32, one row per
 // sequence) -> per-head RMSNorm -> RoPE -> query rows for attention and the
-// new K / V rows appended to the cache, one warp per (sequence, head) row.
+// new K / V rows appended to the cache, one warp per (sequence, head) row; a
+// kv head's K and V rows take separate warps (the TurboQuant round trip of each
+// is a chain of dependent shuffles, so the two run side by side).
 // Follows Gemma4Attention::forward, src/model/gemma4_attention.rs:46-84:
 //   q = rope(q_norm(q_proj x));  k = rope(k_norm(k_proj x));
 //   v = v_norm(v_proj x), or v_norm(k_proj x) before k_norm when K == V;
@@ -142,17 +144,21 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __r
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int Hkv = c.Hkv, T = c.B;  // one token per sequence
   const bool is_q = row < T * Hq;
+  // rows past the queries: (sequence, kv head) pairs, K then V on separate warps
+  const bool is_v = !is_q && ((row - T * Hq) & 1);
   // Before the dependency wait, what does not depend on the projections: the
   // norm weights and the RoPE cos / sin of this step's position.  The device
   // position is written at least two kernels earlier in the stream (before
   // the preceding kernel's own wait), so it is final here.
   const int64_t p0 = pos_dev ? *pos_dev : pos;
   float nwv[P], cs[P], sn[P];
-  const bf16* nwp = is_q ? q_norm : k_norm;
+  const bf16* nwp = is_q ? q_norm : (is_v ? nullptr : k_norm);
   uint4 nraw[P / 8];  // the norm weights' bits, in flight across the wait
 #pragma unroll
   for (int i = 0; i < P / 8; ++i) nraw[i] = nwp ? reinterpret_cast<const uint4*>(nwp + lane * P)[i] : make_uint4(0, 0, 0, 0);
   rope_angles<P>(rope_dims, log2_theta, (float)p0, lane, cs, sn);
+  TurboTab ttab;  // the round trip's constants, loaded before the wait
+  if (turbo_bits && !is_q && c.mode == FMOE_KV_BF16) ttab = turbo_tab<P>(lane, turbo_bits);
   griddep_wait();  // the projections come from the preceding kernel
   griddep_launch_dependents();
 #pragma unroll
@@ -164,7 +170,7 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __r
       nwv[8 * i + 2 * e + 1] = nwp ? bf16hi(w4[e]) : 1.f;
     }
   }
-  if (row >= T * (Hq + Hkv)) return;
+  if (row >= T * (Hq + 2 * Hkv)) return;
   float v[P];
   if (is_q) {
     const int t = row / Hq, h = row % Hq;
@@ -176,39 +182,33 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(KvDev c, const float* __r
     store_row_bf16<P>(q_out + ((int64_t)t * Hq + h) * D, lane, v);
     return;
   }
-  const int r = row - T * Hq, t = r / Hkv, hk = r % Hkv;
+  const int r = (row - T * Hq) >> 1, t = r / Hkv, hk = r % Hkv;
   const float* ks = qkv + (int64_t)t * ld + (Hq + hk) * D + lane * P;
-  const float* vs = k_eq_v ? ks : qkv + (int64_t)t * ld + (Hq + Hkv + hk) * D + lane * P;
-  float kv[P], vv[P];
-  sum_slices<P>(ks, parts, part_stride, kv);
-  sum_slices<P>(vs, parts, part_stride, vv);
+  // V: the value projection, or the raw key projection when K == V (before k_norm)
+  const float* src = !is_v ? ks : k_eq_v ? ks : qkv + (int64_t)t * ld + (Hq + Hkv + hk) * D + lane * P;
+  float x[P];
+  sum_slices<P>(src, parts, part_stride, x);
 #pragma unroll
-  for (int i = 0; i < P; ++i) {
-    kv[i] = round_bf(kv[i]);
-    vv[i] = round_bf(vv[i]);
+  for (int i = 0; i < P; ++i) x[i] = round_bf(x[i]);
+  if (is_v) {
+    warp_rms_norm<P>(x, nullptr, eps, lane);  // v_norm: no learned scale
+  } else {
+    warp_rms_norm_w<P>(x, nwv, k_norm != nullptr, eps, lane);
+    warp_rope_cs<P>(x, rope_dims, cs, sn, lane);
   }
-  warp_rms_norm<P>(vv, nullptr, eps, lane);  // v_norm: no learned scale
-  warp_rms_norm_w<P>(kv, nwv, k_norm != nullptr, eps, lane);
-  warp_rope_cs<P>(kv, rope_dims, cs, sn, lane);
   const int64_t dst = ((int64_t)t * Hkv + hk) * c.cap + p0 % c.cap;
   if (c.mode == FMOE_KV_BF16) {
-    if (turbo_bits) {
-      warp_turbo<P>(kv, lane, turbo_bits);
-      warp_turbo<P>(vv, lane, turbo_bits);
-    }
-    store_row_bf16<P>(reinterpret_cast<bf16*>(c.k) + dst * D, lane, kv);
-    store_row_bf16<P>(reinterpret_cast<bf16*>(c.v) + dst * D, lane, vv);
+    if (turbo_bits) warp_turbo<P>(x, lane, ttab);
+    store_row_bf16<P>(reinterpret_cast<bf16*>(is_v ? c.v : c.k) + dst * D, lane, x);
     return;
   }
-  warp_fwht<P>(kv, lane);
-  warp_fwht<P>(vv, lane);
+  warp_fwht<P>(x, lane);
 #pragma unroll
-  for (int i = 0; i < P; ++i) {
-    kv[i] *= inv_sqrt_d;
-    vv[i] *= inv_sqrt_d;
-  }
-  warp_quant_store<P, 4>(kv, lane, reinterpret_cast<uint32_t*>(c.k) + dst * (D / 8), c.ks + dst * G, c.kb + dst * G);
-  warp_quant_store<P, 8>(vv, lane, reinterpret_cast<uint32_t*>(c.v) + dst * (D / 4), c.vs + dst * G, c.vb + dst * G);
+  for (int i = 0; i < P; ++i) x[i] *= inv_sqrt_d;
+  if (is_v)
+    warp_quant_store<P, 8>(x, lane, reinterpret_cast<uint32_t*>(c.v) + dst * (D / 4), c.vs + dst * G, c.vb + dst * G);
+  else
+    warp_quant_store<P, 4>(x, lane, reinterpret_cast<uint32_t*>(c.k) + dst * (D / 8), c.ks + dst * G, c.kb + dst * G);
 }
 
 // ---------------------------------------------------------------------------
@@ -1108,7 +1108,7 @@ int launch_qkv_post(const KvDev& c, const float* qkv, int ld, int parts, int64_t
                     const bf16* k_norm, float eps, int rope_dims, float rope_theta, int64_t pos,
                     const int64_t* pos_dev, bf16* q_out, int turbo_bits, bool pdl, cudaStream_t st) {
   const float l2t = (float)std::log2((double)rope_theta);
-  const int rows = c.B * (Hq + c.Hkv);
+  const int rows = c.B * (Hq + 2 * c.Hkv);  // query rows, then K and V rows on separate warps
   const float inv = 1.0f / std::sqrt((float)c.D);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];

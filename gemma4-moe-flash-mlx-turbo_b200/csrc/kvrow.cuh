@@ -13,19 +13,22 @@ namespace fmoe {
 // TurboQuant constants: deterministic_signs(n, 42) (src/cache.rs:29-43) and
 // the N(0,1) Lloyd-Max tables (src/cache.rs:67-89).
 
-struct SignTable {
-  float s[512];
+// Sign i is bit i of the packed words (set: -1).  A lane reads the one word
+// holding its P signs, so a warp touches at most 16 distinct words (a table
+// of floats indexed by lane would serialise 32 ways in the constant cache).
+struct SignBits {
+  uint32_t w[16];
 };
-constexpr SignTable make_sign_table() {
-  SignTable t{};
+constexpr SignBits make_sign_bits() {
+  SignBits t{};
   uint64_t st = 42;
   for (int i = 0; i < 512; ++i) {
     st = st * 6364136223846793005ull + 1442695040888963407ull;
-    t.s[i] = ((st >> 63) & 1ull) ? -1.0f : 1.0f;
+    if ((st >> 63) & 1ull) t.w[i >> 5] |= 1u << (i & 31);
   }
   return t;
 }
-static __constant__ SignTable kRhtSigns = make_sign_table();
+static __constant__ SignBits kRhtSignBits = make_sign_bits();
 
 struct Codebook {
   float c[16];
@@ -110,14 +113,35 @@ __device__ __forceinline__ void warp_quant_store(const float (&v)[P], int lane, 
   }
 }
 
+// The round trip's constants for one lane: the codebook (uniform loads;
+// boundaries past the last are +inf) and the lane's P sign bits.  They do not
+// depend on the row, so callers can load them early (before a dependency wait).
+struct TurboTab {
+  float cc[16], bd[15];
+  uint32_t sbits;
+};
+template <int P>
+__device__ __forceinline__ TurboTab turbo_tab(int lane, int bits) {
+  static_assert(P <= 16, "head_dim up to 512");
+  const Codebook& cb = kLloyd[bits - 2];
+  const int nc = cb.n;
+  TurboTab t;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) t.cc[q] = q < nc ? cb.c[q] : 0.f;
+#pragma unroll
+  for (int q = 0; q < 15; ++q) t.bd[q] = q < nc - 1 ? cb.b[q] : INFINITY;
+  t.sbits = kRhtSignBits.w[(lane * P) >> 5] >> ((lane * P) & 31);
+  return t;
+}
 // TurboQuant round trip of one row in registers, src/cache.rs:94-129.  With
 // R = H diag(s), H the normalised Sylvester matrix:
 //   y   = (v / (n + 1e-8)) R sqrt(D) = s (.) FWHT(v / (n + 1e-8))
 //   out = n (c[idx] / sqrt(D)) R^T    = n / D * FWHT(s (.) c[idx])
+// The centroid is picked by compare / select in registers (no divergent
+// constant-memory indexing).
 template <int P>
-__device__ __forceinline__ void warp_turbo(float (&v)[P], int lane, int bits) {
+__device__ __forceinline__ void warp_turbo(float (&v)[P], int lane, const TurboTab& tb) {
   constexpr int D = 32 * P;
-  const Codebook& cb = kLloyd[bits - 2];
   float ss = 0.f;
 #pragma unroll
   for (int i = 0; i < P; ++i) ss = fmaf(v[i], v[i], ss);
@@ -130,16 +154,24 @@ __device__ __forceinline__ void warp_turbo(float (&v)[P], int lane, int bits) {
   warp_fwht<P>(v, lane);
 #pragma unroll
   for (int i = 0; i < P; ++i) {
-    const float sg = kRhtSigns.s[lane * P + i];
+    const float sg = ((tb.sbits >> i) & 1u) ? -1.0f : 1.0f;
     const float y = v[i] * sg;
     int idx = 0;
-    for (int q = 0; q < cb.n - 1; ++q) idx += (y >= cb.b[q]) ? 1 : 0;
-    v[i] = cb.c[idx] * sg;
+#pragma unroll
+    for (int q = 0; q < 15; ++q) idx += (y >= tb.bd[q]) ? 1 : 0;
+    float c = tb.cc[0];
+#pragma unroll
+    for (int q = 1; q < 16; ++q) c = idx == q ? tb.cc[q] : c;
+    v[i] = c * sg;
   }
   warp_fwht<P>(v, lane);
   const float f = n / (float)D;
 #pragma unroll
   for (int i = 0; i < P; ++i) v[i] *= f;
+}
+template <int P>
+__device__ __forceinline__ void warp_turbo(float (&v)[P], int lane, int bits) {
+  warp_turbo<P>(v, lane, turbo_tab<P>(lane, bits));
 }
 
 }  // namespace fmoe
