@@ -33,7 +33,10 @@ int launch_kv_append(const KvDev& c, const bf16* k, const bf16* v, int64_t Tn, i
 
 namespace pfl {
 
-constexpr int kRowThreads = 256;
+// Row kernels: one CTA per token row of H values, each thread holding up to
+// kRowVec 8-value vectors of every tensor in registers (one pass over memory;
+// H a multiple of 8, at most kRowMaxH).
+constexpr int kRowThreads = 384, kRowVec = 2, kRowMaxH = 8 * kRowThreads * kRowVec;
 
 __device__ __forceinline__ float blk_sum(float v, float* red) {
 #pragma unroll
@@ -47,21 +50,55 @@ __device__ __forceinline__ float blk_sum(float v, float* red) {
   for (int w = 0; w < kRowThreads / 32; ++w) s += red[w];
   return s;
 }
+__device__ __forceinline__ void ld8(const bf16* p, float (&v)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  v[0] = bf16lo(w.x);
+  v[1] = bf16hi(w.x);
+  v[2] = bf16lo(w.y);
+  v[3] = bf16hi(w.y);
+  v[4] = bf16lo(w.z);
+  v[5] = bf16hi(w.z);
+  v[6] = bf16lo(w.w);
+  v[7] = bf16hi(w.w);
+}
+__device__ __forceinline__ void st8(bf16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                            pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+__device__ __forceinline__ float sumsq8(const float (&v)[8], float acc) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc = fmaf(v[i], v[i], acc);
+  return acc;
+}
 
 // y = bf16(rms_norm(x) * w), one CTA per row (fast::rms_norm, src/model/norm.rs:11-29)
 __global__ void __launch_bounds__(kRowThreads) pf_norm_rows_kernel(const bf16* __restrict__ x, int H,
                                                                    const bf16* __restrict__ w, float eps,
                                                                    bf16* __restrict__ y) {
   __shared__ float red[kRowThreads / 32];
-  const bf16* xr = x + (int64_t)blockIdx.x * H;
+  const int64_t base = (int64_t)blockIdx.x * H;
+  float xv[kRowVec][8];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float v = bf2f(xr[i]);
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      ld8(x + base + 8 * c, xv[k]);
+      ss = sumsq8(xv[k], ss);
+    }
   }
   const float r = rsqrtf(blk_sum(ss, red) / (float)H + eps);
-  bf16* yr = y + (int64_t)blockIdx.x * H;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) yr[i] = __float2bfloat16_rn(bf2f(xr[i]) * r * bf2f(w[i]));
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      float wv[8], o[8];
+      ld8(w + 8 * c, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = xv[k][i] * r * wv[i];
+      st8(y + base + 8 * c, o);
+    }
+  }
 }
 
 // h = bf16(x + bf16(rms_norm(o) * w_pa)) -> x (in place); h1 / h2 = the two
@@ -73,23 +110,47 @@ __global__ void __launch_bounds__(kRowThreads) pf_ff_in_kernel(bf16* __restrict_
                                                                bf16* __restrict__ h1, bf16* __restrict__ h2) {
   __shared__ float red[kRowThreads / 32];
   const int64_t base = (int64_t)blockIdx.x * H;
+  float ov[kRowVec][8], hv[kRowVec][8];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float v = bf2f(o[base + i]);
-    ss = fmaf(v, v, ss);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      ld8(o + base + 8 * c, ov[k]);
+      ld8(x + base + 8 * c, hv[k]);
+      ss = sumsq8(ov[k], ss);
+    }
   }
   const float r1 = rsqrtf(blk_sum(ss, red) / (float)H + eps);
   ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float h = round_bf(bf2f(x[base + i]) + round_bf(bf2f(o[base + i]) * r1 * bf2f(w_pa[i])));
-    x[base + i] = __float2bfloat16_rn(h);
-    ss = fmaf(h, h, ss);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      float wv[8];
+      ld8(w_pa + 8 * c, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hv[k][i] = round_bf(hv[k][i] + round_bf(ov[k][i] * r1 * wv[i]));
+      st8(x + base + 8 * c, hv[k]);
+      ss = sumsq8(hv[k], ss);
+    }
   }
   const float r2 = rsqrtf(blk_sum(ss, red) / (float)H + eps);
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float h = bf2f(x[base + i]);  // written by this thread above
-    h1[base + i] = __float2bfloat16_rn(h * r2 * bf2f(w_pf[i]));
-    h2[base + i] = __float2bfloat16_rn(h * r2 * bf2f(w_pf2[i]));
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      float w1[8], w2[8], a1[8], a2[8];
+      ld8(w_pf + 8 * c, w1);
+      ld8(w_pf2 + 8 * c, w2);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a1[i] = hv[k][i] * r2 * w1[i];
+        a2[i] = hv[k][i] * r2 * w2[i];
+      }
+      st8(h1 + base + 8 * c, a1);
+      st8(h2 + base + 8 * c, a2);
+    }
   }
 }
 
@@ -99,77 +160,110 @@ __global__ void __launch_bounds__(kRowThreads) pf_ff_out_kernel(bf16* __restrict
                                                                 const bf16* __restrict__ moe, int H,
                                                                 const bf16* __restrict__ w1,
                                                                 const bf16* __restrict__ w2,
-                                                                const bf16* __restrict__ w, float eps, float scalar,
-                                                                bf16* __restrict__ s_tmp) {
+                                                                const bf16* __restrict__ w, float eps, float scalar) {
   __shared__ float red[kRowThreads / 32];
   const int64_t base = (int64_t)blockIdx.x * H;
+  float dv[kRowVec][8], mv[kRowVec][8];
   float sd = 0.f, sm = 0.f;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float dv = bf2f(d[base + i]), mv = bf2f(moe[base + i]);
-    sd = fmaf(dv, dv, sd);
-    sm = fmaf(mv, mv, sm);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      ld8(d + base + 8 * c, dv[k]);
+      ld8(moe + base + 8 * c, mv[k]);
+      sd = sumsq8(dv[k], sd);
+      sm = sumsq8(mv[k], sm);
+    }
   }
   const float rd = rsqrtf(blk_sum(sd, red) / (float)H + eps);
   const float rm = rsqrtf(blk_sum(sm, red) / (float)H + eps);
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float s = round_bf(round_bf(bf2f(d[base + i]) * rd * bf2f(w1[i])) +
-                             round_bf(bf2f(moe[base + i]) * rm * bf2f(w2[i])));
-    s_tmp[base + i] = __float2bfloat16_rn(s);
-    ss = fmaf(s, s, ss);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      float a[8], b[8];
+      ld8(w1 + 8 * c, a);
+      ld8(w2 + 8 * c, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dv[k][i] = round_bf(round_bf(dv[k][i] * rd * a[i]) + round_bf(mv[k][i] * rm * b[i]));
+      ss = sumsq8(dv[k], ss);
+    }
   }
   const float rs = rsqrtf(blk_sum(ss, red) / (float)H + eps);
   const float sc = round_bf(scalar);
-  for (int i = threadIdx.x; i < H; i += kRowThreads) {
-    const float o = round_bf(bf2f(x[base + i]) + round_bf(bf2f(s_tmp[base + i]) * rs * bf2f(w[i])));
-    x[base + i] = __float2bfloat16_rn(o * sc);
+#pragma unroll
+  for (int k = 0; k < kRowVec; ++k) {
+    const int c = threadIdx.x + k * kRowThreads;
+    if (8 * c < H) {
+      float hv[8], wv[8];
+      ld8(x + base + 8 * c, hv);
+      ld8(w + 8 * c, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hv[i] = round_bf(hv[i] + round_bf(dv[k][i] * rs * wv[i])) * sc;
+      st8(x + base + 8 * c, hv);
+    }
   }
 }
 
-// One warp per (token, head) row of the projections: queries normed and
-// rotated in place ([T][Hq][D]); keys / values normed (and rotated), through
-// the TurboQuant round trip when `turbo`, into the staging rows [Hkv][T][D].
-// Gemma4Attention::forward, src/model/gemma4_attention.rs:46-84.
+// One CTA per token, one warp per (token, head) row of the projections:
+// queries normed and rotated in place ([T][Hq][D]); keys / values normed (and
+// rotated), through the TurboQuant round trip when `turbo`, into the staging
+// rows [Hkv][T][D].  Gemma4Attention::forward, src/model/gemma4_attention.rs:
+// 46-84.  The token's RoPE cos / sin (rope_dims / 2 angles, the decode path's
+// formula) are computed once into shared memory and shared by its heads.
+constexpr int kPostWarps = 8;
 template <int P>
-__global__ void __launch_bounds__(256) pf_qkv_post_kernel(bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                          const bf16* __restrict__ v, int T, int Hq, int Hkv,
-                                                          const bf16* __restrict__ qn, const bf16* __restrict__ kn,
-                                                          float eps, int rope_dims, float log2_theta, int64_t pos0,
-                                                          int turbo, bf16* __restrict__ ks, bf16* __restrict__ vs) {
+__global__ void __launch_bounds__(32 * kPostWarps) pf_qkv_post_kernel(
+    bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, int T, int Hq, int Hkv,
+    const bf16* __restrict__ qn, const bf16* __restrict__ kn, float eps, int rope_dims, float log2_theta,
+    int64_t pos0, int turbo, bf16* __restrict__ ks, bf16* __restrict__ vs) {
   constexpr int D = 32 * P;
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int nh = Hq + Hkv;
-  if (row >= (int64_t)T * nh) return;
-  const int t = (int)(row / nh), hh = (int)(row % nh);
+  __shared__ float tc[D / 2], tsn[D / 2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.x;
   const float pos = (float)(pos0 + t);
-  if (hh < Hq) {
-    float x[P];
-    bf16* r = q + ((int64_t)t * Hq + hh) * D;
-    load_row_f32<P>(r, lane, x);
-    warp_rms_norm<P>(x, qn, eps, lane);
-    warp_rope<P>(x, rope_dims, log2_theta, pos, lane);
-    store_row_bf16<P>(r, lane, x);
-    return;
-  }
-  const int g = hh - Hq;
-  float kv[P], vv[P];
-  load_row_f32<P>(k + ((int64_t)t * Hkv + g) * D, lane, kv);
-  if (v)
-    load_row_f32<P>(v + ((int64_t)t * Hkv + g) * D, lane, vv);
-  else {  // K == V: the raw key projection, before its norm
+  const int half = rope_dims / 2;
+  for (int j = threadIdx.x; j < half; j += blockDim.x)
+    sincosf(pos * exp2f(-(float)(2 * j) / (float)rope_dims * log2_theta), &tsn[j], &tc[j]);
+  __syncthreads();
+  float cs[P], sn[P];
 #pragma unroll
-    for (int i = 0; i < P; ++i) vv[i] = kv[i];
+  for (int i = 0; i < P; ++i) {
+    const int e = lane * P + i;
+    const int j = e < half ? e : e - half;
+    cs[i] = e < rope_dims ? tc[j] : 1.f;
+    sn[i] = e < rope_dims ? tsn[j] : 0.f;
   }
-  warp_rms_norm<P>(kv, kn, eps, lane);
-  warp_rope<P>(kv, rope_dims, log2_theta, pos, lane);
-  warp_rms_norm<P>(vv, nullptr, eps, lane);
-  if (turbo) {
-    warp_turbo<P>(kv, lane, turbo);
-    warp_turbo<P>(vv, lane, turbo);
+  for (int hh = warp; hh < Hq + Hkv; hh += kPostWarps) {
+    if (hh < Hq) {
+      float x[P];
+      bf16* r = q + ((int64_t)t * Hq + hh) * D;
+      load_row_f32<P>(r, lane, x);
+      warp_rms_norm<P>(x, qn, eps, lane);
+      warp_rope_cs<P>(x, rope_dims, cs, sn, lane);
+      store_row_bf16<P>(r, lane, x);
+      continue;
+    }
+    const int g = hh - Hq;
+    float kv[P], vv[P];
+    load_row_f32<P>(k + ((int64_t)t * Hkv + g) * D, lane, kv);
+    if (v)
+      load_row_f32<P>(v + ((int64_t)t * Hkv + g) * D, lane, vv);
+    else {  // K == V: the raw key projection, before its norm
+#pragma unroll
+      for (int i = 0; i < P; ++i) vv[i] = kv[i];
+    }
+    warp_rms_norm<P>(kv, kn, eps, lane);
+    warp_rope_cs<P>(kv, rope_dims, cs, sn, lane);
+    warp_rms_norm<P>(vv, nullptr, eps, lane);
+    if (turbo) {
+      warp_turbo<P>(kv, lane, turbo);
+      warp_turbo<P>(vv, lane, turbo);
+    }
+    store_row_bf16<P>(ks + ((int64_t)g * T + t) * D, lane, kv);
+    store_row_bf16<P>(vs + ((int64_t)g * T + t) * D, lane, vv);
   }
-  store_row_bf16<P>(ks + ((int64_t)g * T + t) * D, lane, kv);
-  store_row_bf16<P>(vs + ((int64_t)g * T + t) * D, lane, vv);
 }
 
 // ---------------------------------------------------------------------------
@@ -453,7 +547,7 @@ int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_
 namespace {
 
 struct PfLayerWs {
-  bf16 *xn, *q, *k, *v, *ks, *vs, *att, *h1, *h2, *act, *d, *moe, *s;
+  bf16 *xn, *q, *k, *v, *ks, *vs, *att, *h1, *h2, *act, *d, *moe;
   void* moe_ws;
   size_t moe_bytes;
 };
@@ -479,7 +573,6 @@ size_t carve_pf_layer(Carver& c, const fmoe_decoder_layer_t* L, int64_t T, PfLay
   p.act = c.take<bf16>(T * I);
   p.d = c.take<bf16>(T * H);
   p.moe = c.take<bf16>(T * H);
-  p.s = c.take<bf16>(T * H);
   if (w) *w = p;
   return c.off;
 }
@@ -487,16 +580,15 @@ size_t carve_pf_layer(Carver& c, const fmoe_decoder_layer_t* L, int64_t T, PfLay
 int launch_pf_qkv_post(bf16* q, const bf16* k, const bf16* v, int64_t T, int Hq, int Hkv, int D, const bf16* qn,
                        const bf16* kn, float eps, int rope_dims, float theta, int64_t pos0, int turbo, bf16* ks,
                        bf16* vs, cudaStream_t st) {
-  const int64_t rows = T * (Hq + Hkv);
-  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  const unsigned blocks = (unsigned)T;
   const float l2t = std::log2(theta);
   ProfScope prof_("pf_qkv_post_kernel", st);
   if (D == 256)
-    pfl::pf_qkv_post_kernel<8><<<blocks, 256, 0, st>>>(q, k, v, (int)T, Hq, Hkv, qn, kn, eps, rope_dims, l2t, pos0,
-                                                      turbo, ks, vs);
+    pfl::pf_qkv_post_kernel<8><<<blocks, 32 * pfl::kPostWarps, 0, st>>>(q, k, v, (int)T, Hq, Hkv, qn, kn, eps,
+                                                                        rope_dims, l2t, pos0, turbo, ks, vs);
   else
-    pfl::pf_qkv_post_kernel<16><<<blocks, 256, 0, st>>>(q, k, v, (int)T, Hq, Hkv, qn, kn, eps, rope_dims, l2t, pos0,
-                                                       turbo, ks, vs);
+    pfl::pf_qkv_post_kernel<16><<<blocks, 32 * pfl::kPostWarps, 0, st>>>(q, k, v, (int)T, Hq, Hkv, qn, kn, eps,
+                                                                         rope_dims, l2t, pos0, turbo, ks, vs);
   return check_launch("pf_qkv_post_kernel");
 }
 
@@ -580,6 +672,9 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
       g.in != H || dn.out != H)
     return set_error(FMOE_ERR_INVALID, "layer_prefill: projection shapes do not match the heads");
   if (H % 8 || !aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "layer_prefill: x must be 16-byte aligned, H %% 8 == 0");
+  if (H > pfl::kRowMaxH) return set_error(FMOE_ERR_UNSUPPORTED, "layer_prefill: hidden %d > %d", H, pfl::kRowMaxH);
+  if (L->rope_dims < 0 || L->rope_dims > D || L->rope_dims % 2)
+    return set_error(FMOE_ERR_INVALID, "layer_prefill: rope_dims %d for head_dim %d", L->rope_dims, D);
   const size_t need = fmoe_decoder_layer_prefill_workspace_bytes(L, T);
   if (!need) return set_error(FMOE_ERR_UNSUPPORTED, "layer_prefill: the routed experts have no prefill path");
   if (!workspace || workspace_bytes < need)
@@ -635,7 +730,7 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
     ProfScope prof_("pf_ff_out_kernel", st);
     pfl::pf_ff_out_kernel<<<rows, pfl::kRowThreads, 0, st>>>(
         xb, w.d, w.moe, H, static_cast<const bf16*>(L->post_ff_norm_1), static_cast<const bf16*>(L->post_ff_norm_2),
-        static_cast<const bf16*>(L->post_ff_norm), L->eps, L->layer_scalar, w.s);
+        static_cast<const bf16*>(L->post_ff_norm), L->eps, L->layer_scalar);
   }
   return check_launch("pf_ff_out_kernel");
 }
