@@ -5,7 +5,8 @@ Workloads (synthetic data, random-init weights of the Gemma-4 26B-A4B shapes):
   decode30_b1       (default) one greedy decode step of the whole 30-layer
                     decoder for one sequence after a 2048-position context:
                     6-bit embedding row, per layer 8-bit q/k/v/o projections
-                    with q/k/v norms, RoPE and a bf16 KV-cache append, decode
+                    with q/k/v norms, RoPE and a KV-cache append (default:
+                    TurboQuant 3-bit round trip, the reference's), decode
                     attention (sliding window 1024 / full), the 4-bit dense
                     MLP, the bf16 router and 8 of 128 4-bit experts, then the
                     final norm, the tied 6-bit lm_head with softcap and argmax.
@@ -49,6 +50,12 @@ EP_WORKLOADS = {"ep_moe30_decode_b256": (256, "p2p"), "ep_moe30_prefill_8192": (
 # config 5 measured inside a multi-GPU decode30 run (workload, exchange mode)
 EP_EXTRA = [("ep_moe30_decode_b256", "fixed"), ("ep_moe30_decode_b256", "p2p"), ("ep_moe30_prefill_8192", "exact")]
 CTX = 2048                                                 # decode context (positions in every KV cache)
+# decode30's KV cache: "turbo3" (bf16 rows through the TurboQuant 3-bit round trip on
+# append, the reference's default cache), "bf16" or "affine" (WHT + K4 / V8); --kv-cache
+KV_KINDS = ("turbo3", "bf16", "affine")
+DECODE_KV = "turbo3"
+KV_DESC = {"turbo3": "bf16 rows through the TurboQuant 3-bit round trip on append (the reference's default cache)",
+           "bf16": "bf16 rows", "affine": "WHT-rotated MLX-affine K 4-bit / V 8-bit"}
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES                  # 3,345,408
 
 
@@ -64,6 +71,9 @@ def parse():
                          "layout stored into the peers' memory by the library's kernels; decode30 at N > 1 takes "
                          "fixed or p2p)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-cache", default="turbo3", choices=list(KV_KINDS),
+                    help="decode30's KV cache (default turbo3, the reference's default); the other two are "
+                         "measured as the kv_cache_variants key at N = 1")
     ap.add_argument("--sample", action="store_true",
                     help="decode30: draw each token on the device with the reference generate command's defaults "
                          "(temperature 0.7, top_p 0.9, repetition penalty 1.15 over the last 64 tokens) instead of "
@@ -272,7 +282,8 @@ def decoder_config(args, world):
         + " over NVLink (fixed capacity, in the CUDA graph); attention, dense MLP, router, embedding "
         f"replicated; one sequence per GPU")
     return {"workload": args.workload, "layers": args.layers, "hidden": H, "experts": E, "top_k": K,
-            "batch": T, "context": CTX, "kv_cache": "bf16", "attention_bits": 8, "expert_bits": 4,
+            "batch": T, "context": CTX, "kv_cache": f"{args.kv_cache}: {KV_DESC[args.kv_cache]}",
+            "attention_bits": 8, "expert_bits": 4,
             "dense_bits": 4, "embed_bits": 6, "router": "bf16",
             "parallelism": par,
             "l2": "weights (about 15 GB) far larger than L2; no flush",
@@ -344,16 +355,16 @@ def run_decoder(args, rank, world, local):
         raise SystemExit("decode30: the exact exchange syncs the host per layer and cannot be captured")
     # one layout per weight: the decoder's GEMVs read the plain MLX-affine rows
     m = fm.Gemma4Model.random(cfg, batch=T, max_positions=CTX + 64, seed=4000, device=dev, n_layers=args.layers,
-                              ep=ep, ep_mode=ep_mode)
+                              ep=ep, ep_mode=ep_mode, **kv_kwargs(fm, args.kv_cache))
     if args.sample:
         m.set_sampler(0.7, 0.9, 1.15, seed=4200 + rank)
     g = torch.Generator(device=dev).manual_seed(4100 + rank)
     peaks, peaks_kind = load_peaks()
     pf_result = None
-    if ep is None:
+    prompt = torch.randint(0, cfg["vocab"], (T, CTX), generator=g, device=dev, dtype=torch.int32)
+    if ep is None and args.kv_cache != "affine":
         # BASELINE config 4's context: a CTX-token prompt per sequence prefilled
         # through the whole decoder, which fills every KV cache
-        prompt = torch.randint(0, cfg["vocab"], (T, CTX), generator=g, device=dev, dtype=torch.int32)
         quiet = args.profile_step or args.profile_prefill
         pf_result = decoder_prefill(torch, m, prompt, peaks, timed_reps=0 if quiet else 3)
         if args.profile_prefill:
@@ -361,12 +372,8 @@ def run_decoder(args, rank, world, local):
             profiled_step(torch, lambda: m.prefill(prompt))
             return
     else:
-        # expert-parallel models have no whole-decoder prefill: CTX random K/V positions
-        for L, c in zip(m.layers, m.caches):
-            chunk = 256
-            for p0 in range(0, CTX, chunk):
-                kv = torch.randn(2, T, L.num_kv_heads, chunk, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
-                c.update(kv[0], kv[1])
+        # expert-parallel models and affine caches have no whole-decoder prefill
+        random_context(torch, m, T, g, dev)
     ids0 = torch.randint(0, cfg["vocab"], (T,), generator=g, device=dev, dtype=torch.int32)
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream())
@@ -504,6 +511,10 @@ def run_decoder(args, rank, world, local):
         ep.close()
     if pf_result is not None and rank == 0:
         result["decoder_prefill"] = pf_result
+    if rank == 0 and world == 1 and not args.profile_step:
+        # the other KV caches on the same weights: decode tok/s of each
+        result["kv_cache_variants"] = {k: kv_variant(fm, torch, m, cfg, T, k, prompt, ids0, stream, dev, g)
+                                       for k in KV_KINDS if k != args.kv_cache}
     if rank == 0 and world == 1 and not args.no_attn:
         # BASELINE configs 3 and 2 on the same box, as extra keys of the headline line
         result["kv_attention"] = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"])
@@ -1015,10 +1026,12 @@ def cpu_baseline(_layers, T, budget_s=15.0):
                       f"per step"}
 
 
-def cpu_decoder_sample(seed=4000, T=1):
+def cpu_decoder_sample(seed=4000, T=1, kv=None):
     """Numpy weights for the oracle's decoder layer (one sliding, one full) and
-    the 6-bit lm_head at the model's shapes.  The CPU time does not depend on
-    the code values, so uniform random codes with small bf16 scales stand in."""
+    the 6-bit lm_head at the model's shapes, with caches of the run's KV kind
+    (DECODE_KV unless given).  The CPU time does not depend on the code values,
+    so uniform random codes with small bf16 scales stand in."""
+    kv = DECODE_KV if kv is None else kv
     import numpy as np
     import oracle
     rng = np.random.default_rng(seed)
@@ -1050,8 +1063,14 @@ def cpu_decoder_sample(seed=4000, T=1):
         ck = oracle.f32_to_bf16(rng.standard_normal((T, Hkv, cap, D)).astype(np.float32))
         cfg = {"heads": Hq, "kv_heads": Hkv, "head_dim": D, "rope_dims": 128 if full else 256,
                "rope_theta": 1e6 if full else 1e4, "eps": 1e-6, "k_eq_v": full, "scalar": 1.0, "attn_scale": 1.0,
-               "top_k": K, "hidden": H, "inter_expert": I}
-        layers.append((L, ck, ck.copy(), cfg))
+               "top_k": K, "hidden": H, "inter_expert": I, "turbo_bits": 3 if kv == "turbo3" else 0}
+        if kv == "affine":
+            cfg["kv_mode"] = "affine"
+            kq = tuple(a.reshape(T, Hkv, cap, -1) for a in oracle.kv_quant_affine(ck, 4))
+            vq = tuple(a.reshape(T, Hkv, cap, -1) for a in oracle.kv_quant_affine(ck, 8))
+            layers.append((L, kq, vq, cfg))
+        else:
+            layers.append((L, ck, ck.copy(), cfg))
     embed = ql(262144, H, 6)
     x = oracle.f32_to_bf16(rng.standard_normal((T, H)).astype(np.float32))
     return layers, embed, nrm(H), x
@@ -1097,7 +1116,7 @@ def cpu_decoder_baseline(T, budget_s=15.0, sampled=False):
     step_s = (time.perf_counter() - t0) / n
     return {"value": round(Ts / step_s, 3), "unit": "tok/s", "cores": cores, "kind": "port",
             "sample": f"{n} whole decode steps of {Ts} of the workload's {T} sequences at context {CTX} on the "
-                      f"oracle (C++ OpenMP / numpy): 24 sliding + 6 full layers + lm_head"
+                      f"oracle (C++ OpenMP / numpy), {DECODE_KV} KV cache: 24 sliding + 6 full layers + lm_head"
                       + (" + the sampler" if sampled else "") + f", {step_s * 1e3:.1f} ms per step"}
 
 
@@ -1239,6 +1258,58 @@ def run_qlinear_case(args):
           flush=True)
 
 
+def kv_kwargs(fm, kind):
+    """Gemma4Model arguments of a decode30 KV-cache kind."""
+    if kind == "affine":
+        return {"kv_mode": fm.KV_AFFINE}
+    return {"turbo_bits": 3 if kind == "turbo3" else 0}
+
+
+def random_context(torch, m, T, g, dev):
+    """CTX random bf16 K/V positions appended to every cache (through the cache's own
+    append: TurboQuant round trip or affine quantisation as the cache has it)."""
+    for L, c in zip(m.layers, m.caches):
+        chunk = 256
+        for p0 in range(0, CTX, chunk):
+            kv = torch.randn(2, T, L.num_kv_heads, chunk, L.head_dim, generator=g, device=dev).to(torch.bfloat16)
+            c.update(kv[0], kv[1])
+
+
+def kv_variant(fm, torch, m, cfg, T, kind, prompt, ids0, stream, dev, g, steps=50, warmup=5):
+    """decode30 with another KV-cache kind on the same weights (new caches only):
+    context from the same prompt (prefill) or, for the affine cache, random K/V;
+    one CUDA graph per step, `steps` replays timed with CUDA events after `warmup`."""
+    v = fm.Gemma4Model(cfg, m.embed, m.layers, m.final_norm, T, CTX + 64, device=dev, **kv_kwargs(fm, kind))
+    with torch.cuda.stream(stream):
+        if kind == "affine":
+            random_context(torch, v, T, g, dev)
+        else:
+            v.set_position(0)
+            v.prefill(prompt)
+        v.ids.copy_(ids0)
+        v.set_position(CTX)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream, capture_error_mode="thread_local"):
+            v.decode_step(device_pos=True)
+        v.set_position(CTX)
+        for _ in range(warmup):
+            graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if v.status() != 0:
+        raise SystemExit(f"kv variant {kind}: device status: {fm.last_error()}")
+    del graph
+    return {"kv_cache": KV_DESC[kind], "value": round(T / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms, 5),
+            "context": "prefilled from the same prompt" if kind != "affine" else "random bf16 K/V, quantised on append",
+            "timing": f"{steps} CUDA-graph replays after {warmup}"}
+
+
 def prefill_flops(m, T):
     """Algorithmic FLOPs of one T-token prompt through the decoder: projections,
     dense MLP, router, 8 routed experts per token, causal / sliding attention
@@ -1349,7 +1420,9 @@ def run_prefill_case(args):
 
 
 def main():
+    global DECODE_KV
     args = parse()
+    DECODE_KV = args.kv_cache
     rank, world, local = dist_env()
     if args.prefill_case:
         run_prefill_case(args)
