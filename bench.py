@@ -362,7 +362,7 @@ def run_decoder(args, rank, world, local):
     peaks, peaks_kind = load_peaks()
     pf_result = None
     prompt = torch.randint(0, cfg["vocab"], (T, CTX), generator=g, device=dev, dtype=torch.int32)
-    if ep is None and args.kv_cache != "affine":
+    if ep is None:
         # BASELINE config 4's context: a CTX-token prompt per sequence prefilled
         # through the whole decoder, which fills every KV cache
         quiet = args.profile_step or args.profile_prefill
@@ -372,7 +372,7 @@ def run_decoder(args, rank, world, local):
             profiled_step(torch, lambda: m.prefill(prompt))
             return
     else:
-        # expert-parallel models and affine caches have no whole-decoder prefill
+        # expert-parallel models have no whole-decoder prefill
         random_context(torch, m, T, g, dev)
     ids0 = torch.randint(0, cfg["vocab"], (T,), generator=g, device=dev, dtype=torch.int32)
     stream = torch.cuda.Stream(device=dev)
@@ -1277,15 +1277,12 @@ def random_context(torch, m, T, g, dev):
 
 def kv_variant(fm, torch, m, cfg, T, kind, prompt, ids0, stream, dev, g, steps=50, warmup=5):
     """decode30 with another KV-cache kind on the same weights (new caches only):
-    context from the same prompt (prefill) or, for the affine cache, random K/V;
-    one CUDA graph per step, `steps` replays timed with CUDA events after `warmup`."""
+    context from the same prompt (prefill); one CUDA graph per step, `steps`
+    replays timed with CUDA events after `warmup`."""
     v = fm.Gemma4Model(cfg, m.embed, m.layers, m.final_norm, T, CTX + 64, device=dev, **kv_kwargs(fm, kind))
     with torch.cuda.stream(stream):
-        if kind == "affine":
-            random_context(torch, v, T, g, dev)
-        else:
-            v.set_position(0)
-            v.prefill(prompt)
+        v.set_position(0)
+        v.prefill(prompt)
         v.ids.copy_(ids0)
         v.set_position(CTX)
         torch.cuda.synchronize()
@@ -1306,7 +1303,7 @@ def kv_variant(fm, torch, m, cfg, T, kind, prompt, ids0, stream, dev, g, steps=5
         raise SystemExit(f"kv variant {kind}: device status: {fm.last_error()}")
     del graph
     return {"kv_cache": KV_DESC[kind], "value": round(T / (ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ms, 5),
-            "context": "prefilled from the same prompt" if kind != "affine" else "random bf16 K/V, quantised on append",
+            "context": "prefilled from the same prompt",
             "timing": f"{steps} CUDA-graph replays after {warmup}"}
 
 

@@ -219,8 +219,10 @@ struct QmOut {
 bool qgemm_supported(const QW& w, int group, int K);
 int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool gated, int* status, cudaStream_t st);
 // pflayer.cu: prefill attention of T tokens of one sequence (window 0: causal)
+// affine_ok: an affine (rotated K4 / V8) ring is dequantised as it is read; q and
+// the staged rows must then be in the rotated basis (the decoder layer's prefill).
 int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_t pos0, int window, const bf16* ks,
-                        const bf16* vs, bf16* out, float scale, cudaStream_t st);
+                        const bf16* vs, bf16* out, float scale, cudaStream_t st, bool affine_ok = false);
 int to_experts(const fmoe_experts_t* e, ExpertsDev* d);
 int check_router(const fmoe_router_t* r, QW* q);
 // Every workspace starts with a 256-byte header: [0] device status word (0 ok;

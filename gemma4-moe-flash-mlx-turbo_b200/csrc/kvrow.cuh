@@ -113,6 +113,35 @@ __device__ __forceinline__ void warp_quant_store(const float (&v)[P], int lane, 
   }
 }
 
+// The same quantisation as warp_quant_store, the row replaced by what the
+// cache will return for it: bf16(fma(s, q, b)) with the group's bf16 scale and
+// bias (MLX dequantisation), in the same basis.
+template <int P, int BITS>
+__device__ __forceinline__ void warp_quant_round_trip(float (&v)[P], int lane) {
+  constexpr int LG = 64 / P;
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < P; ++i) {
+    mn = fminf(mn, v[i]);
+    mx = fmaxf(mx, v[i]);
+  }
+#pragma unroll
+  for (int o = 1; o < LG; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const float nmax = (float)((1u << BITS) - 1u);
+  float scale = __fdiv_rn(__fsub_rn(mx, mn), nmax);
+  if (!(scale >= 1e-7f)) scale = 1e-7f;
+  const float s = __bfloat162float(__float2bfloat16_rn(scale)), b = __bfloat162float(__float2bfloat16_rn(mn));
+#pragma unroll
+  for (int i = 0; i < P; ++i) {
+    float q = rintf(__fdiv_rn(__fsub_rn(v[i], b), s));
+    q = fminf(fmaxf(q, 0.0f), nmax);
+    v[i] = __bfloat162float(__float2bfloat16_rn(fmaf(s, q, b)));
+  }
+}
+
 // The round trip's constants for one lane: the codebook (uniform loads;
 // boundaries past the last are +inf) and the lane's P sign bits.  They do not
 // depend on the row, so callers can load them early (before a dependency wait).

@@ -266,6 +266,59 @@ __global__ void __launch_bounds__(32 * kPostWarps) pf_qkv_post_kernel(
   }
 }
 
+// The affine (rotated K4 / V8) cache's prefill: queries rotated in place by the
+// normalised WHT (the basis the cache keeps K and V in); the new K / V rows
+// rotated and taken through the cache's quantise -> dequantise round trip into
+// kr / vr [Hkv][T][D], which attention reads for them (the rows it will read
+// back from the cache for every later token).  One warp per row; the rotation
+// and quantisation are kv_append_kernel's, step for step.
+template <int P>
+__global__ void __launch_bounds__(256) pf_affine_prep_kernel(bf16* __restrict__ q, const bf16* __restrict__ ks,
+                                                             const bf16* __restrict__ vs, int T, int Hq, int Hkv,
+                                                             float inv_sqrt_d, bf16* __restrict__ kr,
+                                                             bf16* __restrict__ vr) {
+  constexpr int D = 32 * P;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t nq = (int64_t)T * Hq, nkv = (int64_t)Hkv * T;
+  if (row >= nq + 2 * nkv) return;
+  float x[P];
+  if (row < nq) {
+    load_row_f32<P>(q + row * D, lane, x);
+    warp_fwht<P>(x, lane);
+#pragma unroll
+    for (int i = 0; i < P; ++i) x[i] *= inv_sqrt_d;
+    store_row_bf16<P>(q + row * D, lane, x);
+    return;
+  }
+  const bool is_v = row - nq >= nkv;
+  const int64_t r = is_v ? row - nq - nkv : row - nq;
+  load_row_f32<P>((is_v ? vs : ks) + r * D, lane, x);
+  warp_fwht<P>(x, lane);
+#pragma unroll
+  for (int i = 0; i < P; ++i) x[i] *= inv_sqrt_d;
+  if (is_v)
+    warp_quant_round_trip<P, 8>(x, lane);
+  else
+    warp_quant_round_trip<P, 4>(x, lane);
+  store_row_bf16<P>((is_v ? vr : kr) + r * D, lane, x);
+}
+
+// Rows back from the rotated basis (the normalised WHT is its own inverse).
+template <int P>
+__global__ void __launch_bounds__(256) pf_rotate_rows_kernel(bf16* __restrict__ x, int64_t rows, float inv_sqrt_d) {
+  constexpr int D = 32 * P;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float v[P];
+  load_row_f32<P>(x + row * D, lane, v);
+  warp_fwht<P>(v, lane);
+#pragma unroll
+  for (int i = 0; i < P; ++i) v[i] *= inv_sqrt_d;
+  store_row_bf16<P>(x + row * D, lane, v);
+}
+
 // ---------------------------------------------------------------------------
 // Prefill attention: one CTA per (tile of 64 query rows, kv head).  A row is a
 // (token, query head of the kv head's group) pair, token-major, so a tile holds
@@ -301,7 +354,36 @@ struct PaArgs {
   int T, Hq, R, QT, win;
   int64_t pos0, cap;
   float sl;         // attention scale * log2(e)
+  // affine (WHT-rotated K4 / V8) ring instead of kr / vr: codes, scales, biases
+  const uint32_t* kq;
+  const bf16 *kss, *kbb;
+  const uint32_t* vq;
+  const bf16 *vss, *vbb;
 };
+
+// Chunk c (values 8c .. 8c+7) of an affine ring row dequantised to bf16, as the
+// cache returns it: bf16(fma(s, q, b)) with the group's scale and bias.
+template <int D>
+__device__ __forceinline__ uint4 affine_chunk(const uint32_t* codes, int bits, const bf16* sc, const bf16* bi,
+                                              int64_t row, int c) {
+  const int g = c >> 3;  // 64 values per group = 8 chunks
+  const float s = bf2f(sc[row * (D / 64) + g]), b = bf2f(bi[row * (D / 64) + g]);
+  float v[8];
+  if (bits == 4) {
+    const uint32_t w = codes[row * (D / 8) + c];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = round_bf(fmaf(s, (float)((w >> (4 * i)) & 15u), b));
+  } else {
+    const uint32_t w0 = codes[row * (D / 4) + 2 * c], w1 = codes[row * (D / 4) + 2 * c + 1];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = round_bf(fmaf(s, (float)((w0 >> (8 * i)) & 255u), b));
+      v[4 + i] = round_bf(fmaf(s, (float)((w1 >> (8 * i)) & 255u), b));
+    }
+  }
+  return make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                    pack_bf16x2(v[6], v[7]));
+}
 
 __device__ __forceinline__ void cp16(void* dst, const void* src, int n) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src), "r"(n) : "memory");
@@ -317,7 +399,7 @@ __device__ __forceinline__ void ldsm4t(const void* p, uint32_t& r0, uint32_t& r1
                : "r"(smem_u32(p)));
 }
 
-template <int D>
+template <int D, bool AFF>  // AFF: the ring is the rotated affine cache, dequantised as it is read
 __global__ void __launch_bounds__(PaCfg<D>::THREADS, D == 256 ? 2 : 1) pf_attn_kernel(const PaArgs a) {
   using C = PaCfg<D>;
   constexpr int CH = D / 8;  // 16-byte chunks per row
@@ -352,6 +434,12 @@ __global__ void __launch_bounds__(PaCfg<D>::THREADS, D == 256 ? 2 : 1) pf_attn_k
         n = 16;
         if (kp < a.pos0) {
           const int64_t row = (int64_t)g * a.cap + kp % a.cap;
+          if (AFF) {  // plain loads, dequantised into the tile
+            const int off = r * C::ROWB + ((c ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(kd + off) = affine_chunk<D>(a.kq, 4, a.kss, a.kbb, row, c);
+            *reinterpret_cast<uint4*>(vd + off) = affine_chunk<D>(a.vq, 8, a.vss, a.vbb, row, c);
+            continue;
+          }
           ksrc = a.kr + row * D + c * 8;
           vsrc = a.vr + row * D + c * 8;
         } else {
@@ -498,10 +586,12 @@ __global__ void __launch_bounds__(PaCfg<D>::THREADS, D == 256 ? 2 : 1) pf_attn_k
 // Attention of T new tokens (one sequence) at positions pos0.. over the ring's
 // rows of earlier positions and the staged new rows.
 int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_t pos0, int window,
-                        const bf16* ks, const bf16* vs, bf16* out, float scale, cudaStream_t st) {
+                        const bf16* ks, const bf16* vs, bf16* out, float scale, cudaStream_t st, bool affine_ok) {
   using namespace pfl;
   if (T <= 0) return FMOE_OK;
-  if (c.mode != FMOE_KV_BF16) return set_error(FMOE_ERR_UNSUPPORTED, "attn_prefill: bf16-storage caches only");
+  if (c.mode != FMOE_KV_BF16 && !(affine_ok && c.mode == FMOE_KV_AFFINE))
+    return set_error(FMOE_ERR_UNSUPPORTED, "attn_prefill: bf16-storage caches only");
+  const bool aff = c.mode == FMOE_KV_AFFINE;
   if (c.B != 1) return set_error(FMOE_ERR_INVALID, "attn_prefill: one sequence per call (batch %d)", c.B);
   if (c.D != 256 && c.D != 512) return set_error(FMOE_ERR_UNSUPPORTED, "attn_prefill: head_dim %d", c.D);
   const int R = Hq / c.Hkv;
@@ -531,15 +621,24 @@ int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_
   a.pos0 = pos0;
   a.cap = c.cap;
   a.sl = scale * 1.4426950408889634f;
+  a.kq = aff ? static_cast<const uint32_t*>(c.k) : nullptr;
+  a.vq = aff ? static_cast<const uint32_t*>(c.v) : nullptr;
+  a.kss = c.ks;
+  a.kbb = c.kb;
+  a.vss = c.vs;
+  a.vbb = c.vb;
+  if (aff) a.kr = a.vr = nullptr;
   const dim3 grid((unsigned)((T + a.QT - 1) / a.QT), (unsigned)c.Hkv);
   if (c.D == 256) {
-    cudaFuncSetAttribute(pf_attn_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, PaCfg<256>::SMEM);
-    ProfScope prof_("pf_attn_kernel<256>", st);
-    pf_attn_kernel<256><<<grid, PaCfg<256>::THREADS, PaCfg<256>::SMEM, st>>>(a);
+    auto k = aff ? pf_attn_kernel<256, true> : pf_attn_kernel<256, false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PaCfg<256>::SMEM);
+    ProfScope prof_(aff ? "pf_attn_kernel<256, affine>" : "pf_attn_kernel<256>", st);
+    k<<<grid, PaCfg<256>::THREADS, PaCfg<256>::SMEM, st>>>(a);
   } else {
-    cudaFuncSetAttribute(pf_attn_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, PaCfg<512>::SMEM);
-    ProfScope prof_("pf_attn_kernel<512>", st);
-    pf_attn_kernel<512><<<grid, PaCfg<512>::THREADS, PaCfg<512>::SMEM, st>>>(a);
+    auto k = aff ? pf_attn_kernel<512, true> : pf_attn_kernel<512, false>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PaCfg<512>::SMEM);
+    ProfScope prof_(aff ? "pf_attn_kernel<512, affine>" : "pf_attn_kernel<512>", st);
+    k<<<grid, PaCfg<512>::THREADS, PaCfg<512>::SMEM, st>>>(a);
   }
   return check_launch("pf_attn_kernel");
 }
@@ -547,7 +646,7 @@ int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_
 namespace {
 
 struct PfLayerWs {
-  bf16 *xn, *q, *k, *v, *ks, *vs, *att, *h1, *h2, *act, *d, *moe;
+  bf16 *xn, *q, *k, *v, *ks, *vs, *kr, *vr, *att, *h1, *h2, *act, *d, *moe;
   void* moe_ws;
   size_t moe_bytes;
 };
@@ -567,6 +666,8 @@ size_t carve_pf_layer(Carver& c, const fmoe_decoder_layer_t* L, int64_t T, PfLay
   p.v = L->k_eq_v ? nullptr : c.take<bf16>(T * KV);
   p.ks = c.take<bf16>(T * KV);
   p.vs = c.take<bf16>(T * KV);
+  p.kr = c.take<bf16>(T * KV);  // affine caches: the new rows as the cache returns them (rotated basis)
+  p.vr = c.take<bf16>(T * KV);
   p.att = c.take<bf16>(T * Q);
   p.h1 = c.take<bf16>(T * H);
   p.h2 = c.take<bf16>(T * H);
@@ -702,8 +803,33 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
                                L->rope_dims, L->rope_theta, pos0, c.mode == FMOE_KV_BF16 ? c.turbo : 0, w.ks, w.vs,
                                st)))
     return rc;
-  if ((rc = launch_attn_prefill(c, w.q, Hq, T, pos0, window, w.ks, w.vs, w.att, L->attn_scale, st))) return rc;
-  // the staged rows are already round-tripped: append them as they are
+  const bool aff = c.mode == FMOE_KV_AFFINE;
+  const float inv = 1.0f / std::sqrt((float)D);
+  if (aff) {  // attention in the cache's rotated basis
+    const int64_t rows = T * Hq + 2 * (int64_t)Hkv * T;
+    const unsigned blocks = (unsigned)((rows + 7) / 8);
+    ProfScope prof_("pf_affine_prep_kernel", st);
+    if (D == 256)
+      pfl::pf_affine_prep_kernel<8><<<blocks, 256, 0, st>>>(w.q, w.ks, w.vs, (int)T, Hq, Hkv, inv, w.kr, w.vr);
+    else
+      pfl::pf_affine_prep_kernel<16><<<blocks, 256, 0, st>>>(w.q, w.ks, w.vs, (int)T, Hq, Hkv, inv, w.kr, w.vr);
+    if ((rc = check_launch("pf_affine_prep_kernel"))) return rc;
+  }
+  if ((rc = launch_attn_prefill(c, w.q, Hq, T, pos0, window, aff ? w.kr : w.ks, aff ? w.vr : w.vs, w.att,
+                                L->attn_scale, st, true)))
+    return rc;
+  if (aff) {  // the output back to the original basis
+    const int64_t rows = T * Hq;
+    const unsigned blocks = (unsigned)((rows + 7) / 8);
+    ProfScope prof_("pf_rotate_rows_kernel", st);
+    if (D == 256)
+      pfl::pf_rotate_rows_kernel<8><<<blocks, 256, 0, st>>>(w.att, rows, inv);
+    else
+      pfl::pf_rotate_rows_kernel<16><<<blocks, 256, 0, st>>>(w.att, rows, inv);
+    if ((rc = check_launch("pf_rotate_rows_kernel"))) return rc;
+  }
+  // the staged rows: already round-tripped (TurboQuant) and appended as they
+  // are, or (affine) rotated and quantised by the append itself
   if ((rc = launch_kv_append(c, w.ks, w.vs, T, pos0, nullptr, 0, st))) return rc;
   {
     const QmOut oo{&o, w.xn, H};

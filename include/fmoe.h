@@ -352,7 +352,9 @@ int fmoe_decoder_layer_forward(const fmoe_decoder_layer_t* layer, const fmoe_kv_
  * create_sliding_mask, src/model/mod.rs:682-753); the new K/V rows (through
  * the TurboQuant round trip when the cache has it, src/cache.rs:290-308) are
  * appended after attention.  A sliding cache needs capacity >= window; a full
- * one pos0 + T <= capacity.  bf16-storage caches only.  Projections and the
+ * one pos0 + T <= capacity.  bf16 caches (with or without TurboQuant) and the
+ * rotated affine K4 / V8 cache, whose new rows enter attention as the cache
+ * returns them (rotated, quantised, dequantised).  Projections and the
  * dense MLP run on the tensor-core GEMM (4/8-bit, group 64); the routed
  * experts as fmoe_moe_prefill, with expert_prep from fmoe_moe_prefill_prepare.
  * x bf16 [T, hidden] is replaced by the layer output.  Workspace:
@@ -367,7 +369,8 @@ int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* layer, const fmoe_kv_
  * [T, q_heads, head_dim] (normed, rotated), k_new / v_new bf16 [kv_heads, T,
  * head_dim] the new rows as they will be stored; positions < pos0 are read
  * from the ring.  out bf16 [T, q_heads * head_dim].  The cache is not
- * modified (append the new rows afterwards with fmoe_kv_append). */
+ * modified (append the new rows afterwards with fmoe_kv_append).  bf16 caches
+ * (the affine cache is prefilled through fmoe_decoder_layer_prefill). */
 int fmoe_attn_prefill(const fmoe_kv_cache_t* cache, const void* q, int q_heads, int64_t T, int64_t pos0, int window,
                       const void* k_new, const void* v_new, void* out, float scale, void* stream);
 

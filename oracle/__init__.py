@@ -335,14 +335,48 @@ def attn_prefill_bf16(q_bf16, k_ring, v_ring, k_new, v_new, pos0: int, window: i
 
     q bf16 [T, Hq, D]; k_ring / v_ring bf16 [Hkv, cap, D] (position j < pos0 at
     slot j % cap); k_new / v_new bf16 [Hkv, T, D].  Returns f32 [T, Hq, D]."""
-    q = _f(q_bf16).astype(np.float64)
+    return _attn_prefill(_f(q_bf16), _f(k_ring), _f(v_ring), _f(k_new), _f(v_new), pos0, window, scale)
+
+
+def attn_prefill_affine(q_bf16, k_ring, v_ring, k_new, v_new, pos0: int, window: int, scale: float):
+    """attn_prefill_bf16 over the WHT-rotated affine K4 / V8 cache: the stored
+    rows are dequantised (rotated basis), the new rows take the cache's own
+    round trip (rotate, quantise as kv_quant_affine, dequantise), the query is
+    rotated the same way and the output rotated back (the normalised WHT is its
+    own inverse), as the decode attention over this cache does.
+
+    k_ring / v_ring: (codes, scales, biases) [Hkv, cap, ...]; k_new / v_new bf16
+    [Hkv, T, D].  Returns (out f32 [T, Hq, D], new K codes, new V codes), the
+    codes as (wq, s, b) [Hkv, T, ...] for the cache's slots."""
+    q = np.ascontiguousarray(q_bf16, np.uint16)
     T, Hq, D = q.shape
-    Hkv, cap = k_ring.shape[0], k_ring.shape[1]
+    Hkv, cap = k_ring[0].shape[0], k_ring[0].shape[1]
+
+    def deq(arrs, bits, rows):
+        wq, sc, bi = (a.reshape(rows, -1) for a in arrs)
+        return _f(dequantize(wq, sc, bi, D, bits))
+
+    kc = tuple(a.reshape(Hkv, T, -1) for a in kv_quant_affine(k_new, 4))
+    vc = tuple(a.reshape(Hkv, T, -1) for a in kv_quant_affine(v_new, 8))
+    kr = deq(k_ring, 4, Hkv * cap).reshape(Hkv, cap, D)
+    vr = deq(v_ring, 8, Hkv * cap).reshape(Hkv, cap, D)
+    kn = deq(kc, 4, Hkv * T).reshape(Hkv, T, D)
+    vn = deq(vc, 8, Hkv * T).reshape(Hkv, T, D)
+    qr = wht_rows(_f(q).reshape(T * Hq, D)).reshape(T, Hq, D)
+    out = _attn_prefill(qr, kr, vr, kn, vn, pos0, window, scale)
+    return wht_rows(out.reshape(T * Hq, D)).reshape(T, Hq, D), kc, vc
+
+
+def _attn_prefill(q, kr, vr, kn, vn, pos0, window, scale):
+    """The masked softmax attention of attn_prefill_bf16 on float arrays."""
+    q = np.asarray(q, np.float64)
+    T, Hq, D = q.shape
+    Hkv, cap = kr.shape[0], kr.shape[1]
     R = Hq // Hkv
     lo = max(0, pos0 - window + 1) if window else 0
     old = np.arange(lo, pos0, dtype=np.int64)
-    K = np.concatenate([_f(k_ring)[:, old % cap], _f(k_new)], axis=1).astype(np.float64)
-    V = np.concatenate([_f(v_ring)[:, old % cap], _f(v_new)], axis=1).astype(np.float64)
+    K = np.concatenate([kr[:, old % cap], kn], axis=1).astype(np.float64)
+    V = np.concatenate([vr[:, old % cap], vn], axis=1).astype(np.float64)
     kpos = np.concatenate([old, pos0 + np.arange(T, dtype=np.int64)])
     qpos = pos0 + np.arange(T, dtype=np.int64)
     ok = kpos[None, :] <= qpos[:, None]
@@ -363,10 +397,12 @@ def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg, n
     """Prefill of T prompt tokens of one sequence through DecoderLayer::
     forward_gemma4 (src/model/mod.rs:67-119) at positions pos0 .. pos0 + T - 1.
 
-    x bf16 [T, H]; L, cfg as decoder_layer (bf16 caches; cfg["turbo_bits"] puts
-    the new K / V rows through the TurboQuant round trip, src/cache.rs:290-308);
+    x bf16 [T, H]; L, cfg as decoder_layer (cfg["turbo_bits"] puts the new K / V
+    rows through the TurboQuant round trip, src/cache.rs:290-308);
     cache_k / cache_v bf16 [1, Hkv, cap, D], updated with the new rows at slots
-    (pos0 + t) % cap.  window 0: full causal attention.  The new rows computed here
+    (pos0 + t) % cap — or, with cfg["kv_mode"] == "affine", the (codes, scales,
+    biases) tuples of the rotated K4 / V8 cache, attended by attn_prefill_affine
+    and updated with the new rows' codes.  window 0: full causal attention.  The new rows computed here
     are left in cfg["_new_rows"] ([Hkv, T, D] each); new_rows = (k, v) replaces them
     in attention and in the cache (a checker comparing the rows on their own can
     then hold the rest of the layer to the rows actually stored).  Returns
@@ -391,6 +427,14 @@ def decoder_layer_prefill(x, L, cache_k, cache_v, pos0: int, window: int, cfg, n
     cfg["_new_rows"] = (k_new, v_new)
     if new_rows is not None:
         k_new, v_new = (np.ascontiguousarray(r, np.uint16) for r in new_rows)
+    if cfg.get("kv_mode", "bf16") == "affine":
+        att, kc, vc = attn_prefill_affine(q, tuple(a[0] for a in cache_k), tuple(a[0] for a in cache_v), k_new,
+                                          v_new, pos0, window, cfg["attn_scale"])
+        cap = cache_k[0].shape[2]
+        for t in range(max(0, T - cap), T):
+            for arr, new in zip(cache_k + cache_v, kc + vc):
+                arr[0, :, (pos0 + t) % cap] = new[:, t]
+        return _ff_block(x, _bf(att).reshape(T, Hq * D), L, cfg), q
     att = attn_prefill_bf16(q, cache_k[0], cache_v[0], k_new, v_new, pos0, window, cfg["attn_scale"])
     cap = cache_k.shape[2]
     for t in range(max(0, T - cap), T):

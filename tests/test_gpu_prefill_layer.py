@@ -190,6 +190,97 @@ def test_decoder_layer_prefill_matches_oracle(fm, orc, dev, full, T, pos0, windo
     _prefill_case(fm, orc, dev, full, T, pos0, window, turbo, seed=71 + T + full)
 
 
+def _affine_arrays(orc, cache):
+    a = cache.arrays()
+    k = (to_np_u32(a["k"]).copy(), to_np_bf16(a["k_scales"]).copy(), to_np_bf16(a["k_biases"]).copy())
+    v = (to_np_u32(a["v"]).copy(), to_np_bf16(a["v_scales"]).copy(), to_np_bf16(a["v_biases"]).copy())
+    return k, v
+
+
+def _affine_rows_close(orc, got, want, slots, bits, D):
+    """The appended rows of the rotated affine cache, dequantised.  Their inputs
+    match the oracle's to ~1 bf16 ulp of the group's values, so a group's bf16
+    scale and bias may move (every value then shifts a little with the same
+    code) and a value near a code boundary may take the neighbouring code; at 8
+    bits a step (range / 255) is itself about one such ulp.  Every value within
+    1.1 steps plus two ulps of its group's largest value of the oracle's; at 4
+    bits, where a step is coarse, at most 2 % of the values beyond half a step
+    (a different code)."""
+    def deq(arrs):
+        q, s_, b_ = (x[0][:, slots].reshape(len(slots) * x.shape[1], -1) for x in arrs)
+        return orc.bf16_to_f32(orc.dequantize(q, s_, b_, D, bits)), orc.bf16_to_f32(s_)
+    g, _ = deq(got)
+    w, sw = deq(want)
+    step = np.repeat(np.abs(sw), 64, axis=1)
+    gmax = np.repeat(np.abs(w).reshape(w.shape[0], -1, 64).max(axis=2), 64, axis=1)
+    ulp = np.exp2(np.floor(np.log2(np.maximum(gmax, 1e-30))) - 7)
+    d = np.abs(g - w)
+    flips = float(np.mean(d > 0.5 * step + ulp))
+    print(f"  affine {bits}-bit rows: max |diff| / (1.1 step + 2 ulp) "
+          f"{float((d / (1.1 * step + 2 * ulp)).max()):.3f}, beyond half a step {flips:.4f}")
+    assert (d <= 1.1 * step + 2 * ulp).all()
+    if bits == 4:
+        assert flips <= 0.02
+
+
+def _prefill_case_affine(fm, orc, dev, full, T, pos0, window, seed):
+    cfg = dict(fm.GEMMA4_26B)
+    L = fm.Gemma4DecoderLayer.random(cfg, full, seed=seed, device=dev)
+    keep = torch.randperm(cfg["experts"], generator=torch.Generator().manual_seed(seed))[:L.top_k]
+    bias = torch.full((cfg["experts"],), -8.0)
+    bias[keep] = 0.0
+    L.router["logit_bias"] = bias.to(dev)
+    L._c = None
+    cap = window if window else 1024
+    cache = fm.KVCache.new_affine(1, L.num_kv_heads, L.head_dim, cap, window=window or None, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    if pos0:
+        cache.update(torch.randn(1, L.num_kv_heads, pos0, L.head_dim, generator=g, device=dev).to(torch.bfloat16),
+                     torch.randn(1, L.num_kv_heads, pos0, L.head_dim, generator=g, device=dev).to(torch.bfloat16))
+    x = torch.randn(T, cfg["hidden"], generator=g, device=dev).to(torch.bfloat16)
+    x_in = to_np_bf16(x)
+    ck, cv = _affine_arrays(orc, cache)
+    ck0, cv0 = tuple(a.copy() for a in ck), tuple(a.copy() for a in cv)
+    ws = torch.zeros(L.prefill_workspace_bytes(T), dtype=torch.uint8, device=dev)
+    L.prefill(x, cache, pos0, ws, window=window)
+    torch.cuda.synchronize()
+    assert fm.lib().fmoe_workspace_status(ws.data_ptr(), 0, None) == 0
+    ocfg = oracle_cfg(L, cfg)
+    ocfg["kv_mode"] = "affine"
+    W = oracle_weights(L)
+    xo, _ = orc.decoder_layer_prefill(x_in, W, ck, cv, pos0, window, ocfg)
+    rng = np.random.default_rng(seed)
+    xp = x_in.copy()
+    hit = rng.random(xp.shape) < 0.1
+    xp[hit] = (xp[hit].astype(np.int32) + rng.choice(np.array([-1, 1]), int(hit.sum()))).astype(np.uint16)
+    xo_n, _ = orc.decoder_layer_prefill(xp, W, ck0, cv0, pos0, window, dict(ocfg))
+    assert topk_sure(ocfg["_router_logits"], L.top_k, margin=0.0).all()
+    gk, gv = _affine_arrays(orc, cache)
+    slots = [(pos0 + t) % cap for t in range(max(0, T - cap), T)]
+    _affine_rows_close(orc, gk, ck, slots, 4, L.head_dim)
+    _affine_rows_close(orc, gv, cv, slots, 8, L.head_dim)
+    got, want = orc.bf16_to_f32(to_np_bf16(x)), orc.bf16_to_f32(xo)
+    scale = np.abs(want).max()
+    tok_err = np.abs(got - want).max(axis=1) / scale
+    tok_noise = np.abs(orc.bf16_to_f32(xo_n) - want).max(axis=1) / scale
+    stats = {q: (float(np.percentile(tok_err, q)), float(np.percentile(tok_noise, q))) for q in (50, 99, 100)}
+    print(f"layer prefill (affine cache) T={T} full={full}: token error / oracle noise at the median, p99, max: "
+          + ", ".join(f"{e:.4f} / {n:.4f}" for e, n in stats.values()))
+    for q, (e, n) in stats.items():
+        assert e <= max(LAYER_TOL, 1.5 * n), (q, e, n)
+
+
+@pytest.mark.parametrize("full,T,pos0,window", [
+    (False, 300, 40, 128),   # sliding: ring rows dequantised as they are read, prompt longer than the window
+    (True, 64, 37, 0),       # full layer, head_dim 512
+])
+def test_decoder_layer_prefill_affine_cache_matches_oracle(fm, orc, dev, full, T, pos0, window):
+    """The rotated affine K4 / V8 cache: queries and new rows rotated, the new
+    rows through the cache's quantise / dequantise round trip, the stored rows
+    dequantised in the attention tile loader, the output rotated back."""
+    _prefill_case_affine(fm, orc, dev, full, T, pos0, window, seed=171 + T + full)
+
+
 def test_prefill_then_decode_matches_token_by_token_decode(fm, dev):
     """A 2-layer model (one sliding layer with a window shorter than the prompt,
     one full layer): prefill of a 40-token prompt gives the same last-position

@@ -62,3 +62,30 @@ def test_attn_prefill_masks_future_and_old_positions():
     out = orc.attn_prefill_bf16(q, ring_k, rv, k_new, v_new, pos0, window, 1.0)
     np.testing.assert_array_equal(out[1:], base[1:])
     assert not np.allclose(out[0], base[0])
+
+
+@pytest.mark.parametrize("D,Hkv,Hq,cap,window,pos0,T", [(256, 2, 4, 16, 16, 20, 7), (512, 1, 4, 64, 0, 5, 9)])
+def test_attn_prefill_affine_equals_sequential_decode(D, Hkv, Hq, cap, window, pos0, T):
+    """Over the rotated affine K4 / V8 cache: the prefill attention equals T
+    decode-attention steps of the affine decode oracle, each after storing its
+    token's codes (the prefill rounds the dequantised rows and the rotated
+    query to bf16, the decode oracle keeps them wider: 1e-2)."""
+    rng = np.random.default_rng(D + cap + T)
+    rows = _bf(rng.standard_normal((Hkv, cap, D)))
+    kq = tuple(a.reshape(1, Hkv, cap, -1) for a in orc.kv_quant_affine(rows, 4))
+    vq = tuple(a.reshape(1, Hkv, cap, -1) for a in orc.kv_quant_affine(_bf(rng.standard_normal((Hkv, cap, D))), 8))
+    q = _bf(rng.standard_normal((T, Hq, D)) * 0.1)
+    k_new = _bf(rng.standard_normal((Hkv, T, D)))
+    v_new = _bf(rng.standard_normal((Hkv, T, D)))
+    got, kc, vc = orc.attn_prefill_affine(q, tuple(a[0] for a in kq), tuple(a[0] for a in vq), k_new, v_new, pos0,
+                                          window, 1.0)
+    ck, cv = tuple(a.copy() for a in kq), tuple(a.copy() for a in vq)
+    for t in range(T):
+        p = pos0 + t
+        for arr, new in zip(ck + cv, kc + vc):
+            arr[0, :, p % cap] = new[:, t]
+        n = min(p + 1, cap)
+        want = orc.attn_decode_affine(q[t:t + 1], Hkv, cap, np.zeros(1, np.int32), np.full(1, n, np.int32), *ck, 4,
+                                      *cv, 8, 1.0)
+        err = np.abs(got[t] - want[0]).max() / np.abs(want[0]).max()
+        assert err <= 1e-2, (t, err)
