@@ -4,24 +4,25 @@
 // QuantizedLinear::forward (src/model/mlp.rs:15-25) and of GeLUMLP's gate / up /
 // down (src/model/mlp.rs:28-41).
 //
-// Persistent kernel, one CTA per SM, 14 warps.  An item is 256 weight rows x
-// one tile of up to 128 tokens; items run weight-tile-major, so the CTAs that
-// run at the same time share a weight tile in L2, and x stays in L2.
+// Persistent kernel.  An item is 128 (plain form, two CTAs per SM, 10 warps)
+// or 256 (gated form, one CTA per SM, 14 warps) weight rows x one tile of up to
+// 128 tokens; items run weight-tile-major, so the CTAs that run at the same
+// time share a weight tile in L2, and x stays in L2.
 //   warp 0      producer: TMA of the token tile (bf16 [tokens][64], 128-byte
-//               swizzle, one per K tile; a ring of 4, so tiles run up to 4 K
-//               tiles ahead of the MMA) and of the packed codes (two boxes of
-//               128 rows x 128 bytes = 2 (8-bit) or 4 (4-bit) K tiles, 128-byte
-//               swizzle; 3 stages ahead of the dequantisers)
-//   warp 1      MMA issuer: per K tile 2 x 4 tcgen05.mma (K 16) with the
-//               dequantised weights as the M = 128 operand (two halves) and
+//               swizzle, one per K tile; a ring of 4 (gated) or 2 (plain)) and
+//               of the packed codes (boxes of 128 rows x 128 bytes = 2 (8-bit)
+//               or 4 (4-bit) K tiles, 128-byte swizzle; 3 or 2 stages ahead of
+//               the dequantisers)
+//   warp 1      MMA issuer: per K tile 4 tcgen05.mma (K 16) per half with the
+//               dequantised weights as the M = 128 operand and
 //               the tokens as N (rounded up to 16), into one of two TMEM
 //               accumulators
-//   warps 2-9   dequantise one weight row each: w = bf16(s * q + b), s * q + b
+//   next 4 / 8  dequantise one weight row each: w = bf16(s * q + b), s * q + b
 //               in fp32, written in the canonical K-major 128-byte-swizzled
 //               layout (a ring of 2 K tiles, each released by the MMA's commit);
 //               the row's scale and bias are loaded from global memory one
 //               packed stage ahead
-//   warps 10-13 epilogue: tcgen05.ld (TMEM lane = weight row, column = token),
+//   last 4      epilogue: tcgen05.ld (TMEM lane = weight row, column = token),
 //               bf16 stores, or (gated mode) gelu(gate) * up from the two
 //               halves, the first projection of the GeLU MLP
 // The plain mode takes up to three weights that share x (q, k and v), each a
@@ -36,24 +37,35 @@ namespace qm {
 
 using namespace tc;
 
-constexpr int BK = 64;                     // K per tile = one quantisation group
-constexpr int BN = 256;                    // weight rows per item (two M = 128 halves)
-constexpr int NX = 4;                      // token-tile ring (TMA lookahead of the MMA)
-constexpr int NW = 2;                      // dequantised-weight ring
-constexpr int NQ = 3;                      // packed-code stages (TMA lookahead of the dequantisers)
-constexpr int X_BYTES = 128 * BK * 2;      // 16 KB: up to 128 tokens x 64 bf16
-constexpr int WB_BYTES = BN * BK * 2;      // 32 KB: 256 rows x 64 bf16
-constexpr int WQ_BYTES = BN * 128;         // 32 KB: 256 rows x 128 bytes of codes
-constexpr int OFF_X = 0;
-constexpr int OFF_WB = OFF_X + NX * X_BYTES;
-constexpr int OFF_WQ = OFF_WB + NW * WB_BYTES;
-constexpr int OFF_BAR = OFF_WQ + NQ * WQ_BYTES;
-constexpr int SMEM = OFF_BAR + 256 + 1024;  // + slack to align the base to 1024 bytes
-constexpr int NDQ = 8;  // dequantising warps: one thread per weight row
-constexpr int THREADS = (2 + NDQ + 4) * 32;
-constexpr int TMEM_COLS = 512;  // [2 accumulators][2 halves][128 tokens] fp32
-static_assert(OFF_WB % 1024 == 0 && OFF_WQ % 1024 == 0 && OFF_BAR % 1024 == 0, "ring alignment");
-static_assert(SMEM <= 227 * 1024, "shared memory");
+constexpr int BK = 64;                 // K per tile = one quantisation group
+constexpr int X_BYTES = 128 * BK * 2;  // 16 KB: up to 128 tokens x 64 bf16
+
+// Tile configuration by the number of 128-row halves (M = 128 MMAs) per item.
+// NH = 2: 256 weight rows per item, one CTA per SM (the gated MLP form needs
+// the gate and up halves together).  NH = 1: 128 rows per item and about
+// 97 KB of shared memory and 256 TMEM columns, so two CTAs share an SM and one
+// covers the other's dependency latency.
+template <int NH>
+struct Cfg {
+  static constexpr int BN = 128 * NH;            // weight rows per item
+  static constexpr int NX = NH == 2 ? 4 : 2;     // token-tile ring (TMA lookahead of the MMA)
+  static constexpr int NW = 2;                   // dequantised-weight ring
+  static constexpr int NQ = NH == 2 ? 3 : 2;     // packed-code stages (lookahead of the dequantisers)
+  static constexpr int WB_BYTES = BN * BK * 2;   // BN rows x 64 bf16
+  static constexpr int WQ_BYTES = BN * 128;      // BN rows x 128 bytes of codes
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_WB = OFF_X + NX * X_BYTES;
+  static constexpr int OFF_WQ = OFF_WB + NW * WB_BYTES;
+  static constexpr int OFF_BAR = OFF_WQ + NQ * WQ_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;  // + slack to align the base to 1024 bytes
+  static constexpr int NDQ = 4 * NH;                 // dequantising warps: one thread per weight row
+  static constexpr int THREADS = (2 + NDQ + 4) * 32;
+  static constexpr int ACC = 128 * NH;               // TMEM columns of one accumulator ([halves][128 tokens])
+  static constexpr int TMEM_COLS = 2 * ACC;          // two accumulators
+  static constexpr int MINB = NH == 2 ? 1 : 2;       // CTAs per SM
+  static_assert(OFF_WB % 1024 == 0 && OFF_WQ % 1024 == 0 && OFF_BAR % 1024 == 0, "ring alignment");
+  static_assert(SMEM <= 227 * 1024 && MINB * (SMEM + 1024) <= 228 * 1024, "shared memory");
+};
 
 struct Seg {
   const bf16* s;  // scales [N][G]
@@ -110,8 +122,15 @@ __device__ __forceinline__ float u4f(uint32_t w, int i) {
   return __uint_as_float(((w >> (4 * i)) & 0xFu) | 0x4B000000u) - 8388608.f;
 }
 
-template <int BITS, int MODE>  // MODE 0: plain bf16 output; 1: gelu(gate) * up
-__global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant__ Maps maps, const Args a) {
+template <int BITS, int MODE, int NH>  // MODE 0: plain bf16 output; 1: gelu(gate) * up
+__global__ void __launch_bounds__(Cfg<NH>::THREADS, Cfg<NH>::MINB)
+    qgemm_kernel(const __grid_constant__ Maps maps, const Args a) {
+  using C = Cfg<NH>;
+  static_assert(MODE == 0 || NH == 2, "the gated form takes gate and up halves together");
+  constexpr int BN = C::BN, NX = C::NX, NW = C::NW, NQ = C::NQ, NDQ = C::NDQ;
+  constexpr int WB_BYTES = C::WB_BYTES, WQ_BYTES = C::WQ_BYTES;
+  constexpr int OFF_X = C::OFF_X, OFF_WB = C::OFF_WB, OFF_WQ = C::OFF_WQ, OFF_BAR = C::OFF_BAR;
+  constexpr int TMEM_COLS = C::TMEM_COLS, ACC = C::ACC;
   constexpr int KQ = 128 / (8 * BITS);  // K tiles per packed stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -176,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
             mbar_arrive_expect_tx(&wqf[sq], (uint32_t)WQ_BYTES);
             if (MODE == 0) {
               tma2d(wq, &maps.w[t.sg], xb, t.j * BN, &wqf[sq]);
-              tma2d(wq + WQ_BYTES / 2, &maps.w[t.sg], xb, t.j * BN + 128, &wqf[sq]);
+              if (NH == 2) tma2d(wq + WQ_BYTES / 2, &maps.w[t.sg], xb, t.j * BN + 128, &wqf[sq]);
             } else {
               tma2d(wq, &maps.w[0], xb, t.j * 128, &wqf[sq]);
               tma2d(wq + WQ_BYTES / 2, &maps.w[1], xb, t.j * 128, &wqf[sq]);
@@ -213,10 +232,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
           const uint32_t sx = smem_u32(smem + OFF_X + s * X_BYTES), sw = smem_u32(smem + OFF_WB + w * WB_BYTES);
           if (!*failed) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int h = 0; h < NH; ++h)
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_ss(tmem + ab * 256 + h * 128, sw128_desc(sw + h * (128 * 128) + 32 * k), sw128_desc(sx + 32 * k),
+                mma_ss(tmem + ab * ACC + h * 128, sw128_desc(sw + h * (128 * 128) + 32 * k), sw128_desc(sx + 32 * k),
                        idesc, (kt | k) != 0);
           }
           mma_commit(&xfree[s]);
@@ -323,12 +342,12 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_kernel(const __grid_constant
       const int ab = n & 1, nc = (t.ntok + 15) / 16;
       pwait_sleep(&accf[ab], (uint32_t)(n / 2) & 1u, failed, a.status, 408, 256);
       tc_fence_after();
-      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * 256;
+      const uint32_t ta = tmem + ((uint32_t)(qw * 32) << 16) + ab * ACC;
       const bool ok = !*failed;
       if (MODE == 0) {
         const Seg& sg = a.seg[t.sg];
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < NH; ++hh) {
           const int row = t.j * BN + hh * 128 + qw * 32 + lane;
           bf16* o = sg.out + (int64_t)t.t0 * sg.ld + row;
 #pragma unroll 1
@@ -402,11 +421,14 @@ int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool
   a.G = K / 64;
   a.T = (int)T;
   a.status = status;
-  // tiles of 64 tokens when 128-token tiles would leave SMs idle
+  // plain form: 128-row items, two CTAs per SM; gated form: gate + up halves, one
+  const int BN = gated ? Cfg<2>::BN : Cfg<1>::BN;
+  const int slots = gated ? kNumSMs : 2 * kNumSMs;
+  // tiles of 64 tokens when 128-token tiles would leave CTA slots idle
   int nj = 0;
   for (int s = 0; s < nseg; ++s) nj += gated ? 0 : (o[s].w->out + BN - 1) / BN;
   if (gated) nj = (o[0].w->out + 127) / 128;
-  a.tb = (T > 64 && (int64_t)nj * ((T + 127) / 128) < kNumSMs) ? 64 : 128;
+  a.tb = (T > 64 && (int64_t)nj * ((T + 127) / 128) < slots) ? 64 : 128;
   if (T <= 64) a.tb = 64;
   a.nt = (int)((T + a.tb - 1) / a.tb);
   int item = 0;
@@ -435,26 +457,26 @@ int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool
   }
   static std::once_flag once;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(qgemm_kernel<4, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    cudaFuncSetAttribute(qgemm_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    cudaFuncSetAttribute(qgemm_kernel<8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    cudaFuncSetAttribute(qgemm_kernel<8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<4, 0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<1>::SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<4, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<2>::SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<8, 0, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<1>::SMEM);
+    cudaFuncSetAttribute(qgemm_kernel<8, 1, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<2>::SMEM);
   });
-  const int grid = a.nitems < kNumSMs ? a.nitems : kNumSMs;
+  const int grid = a.nitems < slots ? a.nitems : slots;
   const char* name = bits == 8 ? (gated ? "qgemm_kernel<8, gated>" : "qgemm_kernel<8>")
                                : (gated ? "qgemm_kernel<4, gated>" : "qgemm_kernel<4>");
   {
     ProfScope prof_(name, st);
     if (bits == 8) {
       if (gated)
-        qgemm_kernel<8, 1><<<grid, THREADS, SMEM, st>>>(m, a);
+        qgemm_kernel<8, 1, 2><<<grid, Cfg<2>::THREADS, Cfg<2>::SMEM, st>>>(m, a);
       else
-        qgemm_kernel<8, 0><<<grid, THREADS, SMEM, st>>>(m, a);
+        qgemm_kernel<8, 0, 1><<<grid, Cfg<1>::THREADS, Cfg<1>::SMEM, st>>>(m, a);
     } else {
       if (gated)
-        qgemm_kernel<4, 1><<<grid, THREADS, SMEM, st>>>(m, a);
+        qgemm_kernel<4, 1, 2><<<grid, Cfg<2>::THREADS, Cfg<2>::SMEM, st>>>(m, a);
       else
-        qgemm_kernel<4, 0><<<grid, THREADS, SMEM, st>>>(m, a);
+        qgemm_kernel<4, 0, 1><<<grid, Cfg<1>::THREADS, Cfg<1>::SMEM, st>>>(m, a);
     }
   }
   return check_launch(name);
