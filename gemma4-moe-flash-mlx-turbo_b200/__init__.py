@@ -152,6 +152,7 @@ SIGNATURES = {
     "fmoe_kv_append": (_I, [ctypes.POINTER(KvCacheC), _P, _P, _I64, _I64, _P, _I, _P]),
     "fmoe_attn_decode_workspace_bytes": (_SZ, [ctypes.POINTER(KvCacheC), _I]),
     "fmoe_attn_decode": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _P, _F, _P, _P, _SZ, _P]),
+    "fmoe_attn_decode_sparse_v": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _F, _F, _P, _P]),
     "fmoe_turbo_round_trip": (_I, [_P, _I64, _I, _I, _P, _P]),
     "fmoe_decoder_workspace_bytes": (_SZ, [_I64, _P, ctypes.POINTER(KvCacheC)]),
     "fmoe_decoder_layer_forward": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _P, _P, _SZ, _P]),

@@ -210,6 +210,7 @@ int to_qw(const fmoe_qweight_t* w, QW* q);
 // qgemm.cu: dense 4 / 8-bit group-64 linear layers over many tokens on tcgen05.
 // Up to kQmMaxSeg weights of the same K and bits share x (one launch); in the
 // gated form o[0] / o[1] are gate / up and o[0].out receives gelu(g) * u.
+constexpr int kSvMaxSlots = 32768;  // sparsev.cu: attended slots of one sparse-V call (scores in shared memory)
 constexpr int kQmMaxSeg = 3;
 struct QmOut {
   const QW* w;

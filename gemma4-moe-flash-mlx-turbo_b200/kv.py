@@ -152,6 +152,23 @@ class KVCache:
         self.update(keys, values)
         return self
 
+    def attend_sparse_v(self, q: torch.Tensor, tau: float, scale: float = 1.0,
+                        n_valid: int | None = None) -> torch.Tensor:
+        """Sparse-V decode attention (fmoe_attn_decode_sparse_v; the reference's
+        sparse_v_attention, src/model/gemma4_attention.rs:196-234): softmax
+        weights below tau set to zero, not renormalised.  q bf16 [batch,
+        q_heads, head_dim] -> bf16 [batch, q_heads, head_dim]."""
+        _need_cuda(q)
+        B, Hq, D = q.shape
+        if B != self.batch or D != self.head_dim:
+            raise ValueError(f"attend_sparse_v: q {tuple(q.shape)} vs cache batch {self.batch}, head_dim {D}")
+        out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=q.device)
+        n = self.stored_len() if n_valid is None else n_valid
+        qc = q.to(torch.bfloat16).contiguous()
+        check(lib().fmoe_attn_decode_sparse_v(ctypes.byref(self.c), _ptr(qc), Hq, n, scale, tau, _ptr(out),
+                                              _stream()))
+        return out
+
     def attend_prefill(self, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, pos0: int,
                        window: int | None = None, scale: float = 1.0) -> torch.Tensor:
         """Prefill SDPA (fmoe_attn_prefill) of T new tokens of this one-sequence

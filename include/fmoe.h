@@ -289,6 +289,17 @@ int fmoe_attn_decode(const fmoe_kv_cache_t* cache, const void* q, int q_heads, i
                      const int64_t* n_valid_dev, float scale, void* out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Sparse-V decode attention, the reference's optional decode path
+ * (sparse_v_attention, src/model/gemma4_attention.rs:196-234; threshold flag
+ * src/main.rs:62-64): over the first n_valid slots of every sequence's ring,
+ * p = softmax(scale * q . K^T); weights p < tau are set to zero (the others
+ * are not renormalised); out = p . V.  q / out bf16 [batch, q_heads,
+ * head_dim].  tau = 0 gives the dense attention.  bf16-storage caches (with or
+ * without the TurboQuant round trip), 1 <= n_valid <= min(capacity, 32768).
+ * No workspace; two passes over the keys per (sequence, query head). */
+int fmoe_attn_decode_sparse_v(const fmoe_kv_cache_t* cache, const void* q, int q_heads, int64_t n_valid,
+                              float scale, float tau, void* out, void* stream);
+
 /* TurboQuant quantise -> dequantise round trip of `rows` bf16 vectors of
  * length head_dim (256 or 512), bits 2..4: turbo_round_trip_kv,
  * src/cache.rs:94-129 (the rotation R = H diag(signs) applied as a fast
