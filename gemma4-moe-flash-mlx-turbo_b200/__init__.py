@@ -159,6 +159,8 @@ SIGNATURES = {
     "fmoe_decoder_layer_prefill_workspace_bytes": (_SZ, [_P, _I64]),
     "fmoe_decoder_layer_prefill": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _I64, _I64, _I, _P, _P, _SZ, _P]),
     "fmoe_attn_prefill": (_I, [ctypes.POINTER(KvCacheC), _P, _I, _I64, _I64, _I, _P, _P, _P, _F, _P]),
+    "fmoe_decoder_layer_prefill_ep_workspace_bytes": (_SZ, [_P, _I64, _I]),
+    "fmoe_decoder_layer_prefill_ep": (_I, [_P, ctypes.POINTER(KvCacheC), _P, _P, _I64, _I64, _I, _P, _P, _SZ, _P]),
     "fmoe_mlp_workspace_bytes": (_SZ, [_I64, ctypes.POINTER(QWeightC)]),
     "fmoe_mlp_forward": (_I, [_P, _I64, ctypes.POINTER(QWeightC), ctypes.POINTER(QWeightC), ctypes.POINTER(QWeightC),
                               _P, _P, _SZ, _P]),

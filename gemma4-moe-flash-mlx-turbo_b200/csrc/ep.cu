@@ -397,6 +397,8 @@ size_t carve_ep(Carver& c, int R, int64_t cap, const fmoe_router_t* r, int k, co
   return c.off;
 }
 
+int ep_comm_ranks(const fmoe_ep_comm* c) { return c ? c->n_ranks : 0; }
+
 int ep_check(const fmoe_ep_comm* c, const ExpertsDev& d, int E_total, int* n_ranks) {
   if (!c || !c->nc) return set_error(FMOE_ERR_INVALID, "ep: null communicator");
   if (E_total % c->n_ranks || d.E != E_total / c->n_ranks || d.first != c->rank * d.E)

@@ -291,6 +291,7 @@ size_t carve_ep(Carver& c, int R, int64_t cap, const fmoe_router_t* r, int k, co
                 EpWs* w);
 // The slice must be experts [rank*E/n, (rank+1)*E/n) of E_total.
 int ep_check(const fmoe_ep_comm_t* c, const ExpertsDev& d, int E_total, int* n_ranks);
+int ep_comm_ranks(const fmoe_ep_comm_t* c);  // ranks of the communicator (0 for null)
 int ep_experts(const fmoe_ep_comm_t* c, const bf16* x, int64_t T, int64_t cap, int k, const int32_t* ids,
                const float* wts, const ExpertsDev& d, const bf16* prep, bf16* y, const EpWs& w, int mode, int* status,
                cudaStream_t st);

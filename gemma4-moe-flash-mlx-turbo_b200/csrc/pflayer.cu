@@ -652,9 +652,12 @@ struct PfLayerWs {
 };
 
 // The MoE prefill's workspace comes first, so its status word is the layer's.
-size_t carve_pf_layer(Carver& c, const fmoe_decoder_layer_t* L, int64_t T, PfLayerWs* w) {
+// n_ranks > 0: the routed experts are this rank's slice, run by the
+// expert-parallel MoE (exact exchange, cap = T).
+size_t carve_pf_layer(Carver& c, const fmoe_decoder_layer_t* L, int64_t T, PfLayerWs* w, int n_ranks = 0) {
   PfLayerWs p{};
-  const size_t mb = fmoe_moe_prefill_workspace_bytes(T, &L->router, &L->experts);
+  const size_t mb = n_ranks > 0 ? fmoe_ep_moe_workspace_bytes(n_ranks, T, &L->router, &L->experts)
+                                : fmoe_moe_prefill_workspace_bytes(T, &L->router, &L->experts);
   if (!mb) return 0;
   p.moe_ws = c.take<uint8_t>(mb);
   p.moe_bytes = mb;
@@ -744,16 +747,18 @@ extern "C" int fmoe_mlp_forward(const void* x, int64_t T, const fmoe_qweight_t* 
   return launch_qgemm(act, T, d.in, &dn, 1, false, status, st);
 }
 
-extern "C" size_t fmoe_decoder_layer_prefill_workspace_bytes(const fmoe_decoder_layer_t* L, int64_t T) {
+namespace {
+
+size_t pf_layer_bytes(const fmoe_decoder_layer_t* L, int64_t T, int n_ranks) {
   if (!L || T <= 0) return 0;
   Carver c(nullptr);
-  const size_t n = carve_pf_layer(c, L, T, nullptr);
+  const size_t n = carve_pf_layer(c, L, T, nullptr, n_ranks);
   return n ? n + 256 : 0;
 }
 
-extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, void* x,
-                                          int64_t T, int64_t pos0, int window, const void* expert_prep,
-                                          void* workspace, size_t workspace_bytes, void* stream) {
+int layer_prefill(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, fmoe_ep_comm_t* comm, void* x,
+                  int64_t T, int64_t pos0, int window, const void* expert_prep, void* workspace,
+                  size_t workspace_bytes, void* stream) {
   if (!L || !cache || !x) return set_error(FMOE_ERR_INVALID, "layer_prefill: null layer / cache / x");
   if (T <= 0) return FMOE_OK;
   if (!expert_prep) return set_error(FMOE_ERR_INVALID, "layer_prefill: null prepared expert scales");
@@ -776,14 +781,15 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
   if (H > pfl::kRowMaxH) return set_error(FMOE_ERR_UNSUPPORTED, "layer_prefill: hidden %d > %d", H, pfl::kRowMaxH);
   if (L->rope_dims < 0 || L->rope_dims > D || L->rope_dims % 2)
     return set_error(FMOE_ERR_INVALID, "layer_prefill: rope_dims %d for head_dim %d", L->rope_dims, D);
-  const size_t need = fmoe_decoder_layer_prefill_workspace_bytes(L, T);
+  const int n_ranks = ep_comm_ranks(comm);
+  const size_t need = pf_layer_bytes(L, T, n_ranks);
   if (!need) return set_error(FMOE_ERR_UNSUPPORTED, "layer_prefill: the routed experts have no prefill path");
   if (!workspace || workspace_bytes < need)
     return set_error(FMOE_ERR_WORKSPACE, "layer_prefill: workspace %zu < %zu", workspace_bytes, need);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Carver cv(workspace);
   PfLayerWs w;
-  carve_pf_layer(cv, L, T, &w);
+  carve_pf_layer(cv, L, T, &w, n_ranks);
   int* status = static_cast<int*>(workspace);  // the MoE workspace's header
   bf16* xb = static_cast<bf16*>(x);
   const unsigned rows = (unsigned)T;
@@ -849,9 +855,14 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
     const QmOut dd{&dn, w.d, H};
     if ((rc = launch_qgemm(w.act, T, g.out, &dd, 1, false, status, st))) return rc;
   }
-  if ((rc = fmoe_moe_prefill(w.h2, T, &L->router, &L->experts, expert_prep, w.moe, nullptr, nullptr, w.moe_ws,
-                             w.moe_bytes, st)))
+  if (comm) {  // this rank's expert slice; every rank passes the same T (cap)
+    if ((rc = fmoe_ep_moe_forward(comm, w.h2, T, T, &L->router, &L->experts, expert_prep, w.moe, nullptr, nullptr,
+                                  FMOE_EP_EXACT, w.moe_ws, w.moe_bytes, st)))
+      return rc;
+  } else if ((rc = fmoe_moe_prefill(w.h2, T, &L->router, &L->experts, expert_prep, w.moe, nullptr, nullptr, w.moe_ws,
+                                    w.moe_bytes, st))) {
     return rc;
+  }
   {
     ProfScope prof_("pf_ff_out_kernel", st);
     pfl::pf_ff_out_kernel<<<rows, pfl::kRowThreads, 0, st>>>(
@@ -859,4 +870,30 @@ extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const f
         static_cast<const bf16*>(L->post_ff_norm), L->eps, L->layer_scalar);
   }
   return check_launch("pf_ff_out_kernel");
+}
+
+}  // namespace
+
+extern "C" size_t fmoe_decoder_layer_prefill_workspace_bytes(const fmoe_decoder_layer_t* L, int64_t T) {
+  return pf_layer_bytes(L, T, 0);
+}
+
+extern "C" int fmoe_decoder_layer_prefill(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, void* x,
+                                          int64_t T, int64_t pos0, int window, const void* expert_prep,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  return layer_prefill(L, cache, nullptr, x, T, pos0, window, expert_prep, workspace, workspace_bytes, stream);
+}
+
+extern "C" size_t fmoe_decoder_layer_prefill_ep_workspace_bytes(const fmoe_decoder_layer_t* L, int64_t T,
+                                                                 int n_ranks) {
+  if (n_ranks < 1) return 0;
+  return pf_layer_bytes(L, T, n_ranks);
+}
+
+extern "C" int fmoe_decoder_layer_prefill_ep(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
+                                             fmoe_ep_comm_t* comm, void* x, int64_t T, int64_t pos0, int window,
+                                             const void* expert_prep, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+  if (!comm) return set_error(FMOE_ERR_INVALID, "layer_prefill_ep: null communicator");
+  return layer_prefill(L, cache, comm, x, T, pos0, window, expert_prep, workspace, workspace_bytes, stream);
 }

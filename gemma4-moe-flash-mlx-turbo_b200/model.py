@@ -138,6 +138,21 @@ class Gemma4DecoderLayer:
                                                win or 0, _ptr(prep), _ptr(workspace), workspace.numel(), _stream()))
         return x
 
+    def prefill_ep_workspace_bytes(self, T, world: int) -> int:
+        return lib().fmoe_decoder_layer_prefill_ep_workspace_bytes(ctypes.byref(self.cstruct()), T, world)
+
+    def prefill_ep(self, comm, x: torch.Tensor, cache: KVCache, pos0: int, workspace: torch.Tensor, window=None):
+        """prefill() with this layer's experts being this rank's slice: the routed
+        experts run on their owning ranks (fmoe_decoder_layer_prefill_ep; every
+        rank calls it with the same T)."""
+        T = x.shape[0]
+        win = cache.window if window is None else window
+        prep = prefill_prep(self.experts, x.device)
+        check(lib().fmoe_decoder_layer_prefill_ep(ctypes.byref(self.cstruct()), ctypes.byref(cache.c), comm.handle,
+                                                  _ptr(x), T, pos0, win or 0, _ptr(prep), _ptr(workspace),
+                                                  workspace.numel(), _stream()))
+        return x
+
     def ep_workspace_bytes(self, T, cache: KVCache, world: int, cap: int) -> int:
         return lib().fmoe_decoder_ep_workspace_bytes(T, ctypes.byref(self.cstruct()), ctypes.byref(cache.c), world,
                                                      cap)
@@ -348,12 +363,12 @@ class Gemma4Model:
         """Run the prompt of every sequence through the model (one sequence at a
         time, in chunks of at most `chunk` tokens through all layers), appending
         its K/V rows, and leave each sequence's next greedy token in self.ids.
+        Expert-parallel models: collective, every rank with prompts of the same
+        length (the routed experts run on their owning ranks).
         tokens: int32 [batch, T] (or [T] for batch 1), all sequences the same
         length, starting at the current position.  TextModel::forward with
         l = T (src/model/mod.rs:135-254) followed by Model::forward's lm_head on
         the last position (mod.rs:336-362)."""
-        if self.ep is not None:
-            raise ValueError("prefill: expert-parallel models run their prompts through fmoe_moe_prefill per rank")
         tok = tokens.to(device=self.device, dtype=torch.int32)
         if tok.dim() == 1:
             tok = tok.view(1, -1)
@@ -361,7 +376,10 @@ class Gemma4Model:
         if B != self.batch or T < 1:
             raise ValueError(f"prefill: tokens {tuple(tok.shape)} for batch {self.batch}")
         chunk = max(1, min(chunk, T))
-        need = max(L.prefill_workspace_bytes(chunk) for L in self.layers)
+        if self.ep is None:
+            need = max(L.prefill_workspace_bytes(chunk) for L in self.layers)
+        else:  # every rank runs the same chunks (the expert exchange is collective)
+            need = max(L.prefill_ep_workspace_bytes(chunk, self.ep.world) for L in self.layers)
         if need == 0:
             raise ValueError("prefill: unsupported layer configuration")
         if getattr(self, "_pf_ws", None) is None or self._pf_ws.numel() < need:
@@ -378,7 +396,10 @@ class Gemma4Model:
                 ids = tok[b, s0:s0 + n].contiguous()
                 check(lib().fmoe_embed_rows(ctypes.byref(c), _ptr(ids), n, self._emb_scale, _ptr(x), _stream()))
                 for L, v in zip(self.layers, views):
-                    L.prefill(x, v, pos0 + s0, self._pf_ws)
+                    if self.ep is None:
+                        L.prefill(x, v, pos0 + s0, self._pf_ws)
+                    else:
+                        L.prefill_ep(self.ep, x, v, pos0 + s0, self._pf_ws)
             check(lib().fmoe_lm_head(ctypes.byref(c), _ptr(self.final_norm), self.cfg["eps"], _ptr(x[-1:]), 1,
                                      self.cfg["softcap"], _ptr(self.logits[b:b + 1]), _ptr(self.ids[b:b + 1]), None,
                                      _ptr(self.lm_ws), self.lm_ws.numel(), _stream()))

@@ -487,6 +487,17 @@ int fmoe_ep_moe_forward(fmoe_ep_comm_t* comm, const void* x, int64_t T, int64_t 
                         const fmoe_experts_t* local, const void* prepared, void* y, int32_t* ids, float* weights,
                         int mode, void* workspace, size_t workspace_bytes, void* stream);
 
+/* fmoe_decoder_layer_prefill with layer->experts being this rank's slice: the
+ * routed experts run through fmoe_ep_moe_forward (FMOE_EP_EXACT, cap = T),
+ * everything else on this rank.  Collective: every rank calls it for every
+ * layer with the same T (each with its own sequence and cache).  expert_prep:
+ * fmoe_moe_prefill_prepare of the local slice.  Workspace:
+ * fmoe_decoder_layer_prefill_ep_workspace_bytes, zero-filled once. */
+size_t fmoe_decoder_layer_prefill_ep_workspace_bytes(const fmoe_decoder_layer_t* layer, int64_t T, int n_ranks);
+int fmoe_decoder_layer_prefill_ep(const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache,
+                                  fmoe_ep_comm_t* comm, void* x, int64_t T, int64_t pos0, int window,
+                                  const void* expert_prep, void* workspace, size_t workspace_bytes, void* stream);
+
 /* fmoe_decoder_layer_forward with layer->experts being this rank's slice: the
  * routed experts of the MoE block run on their owning ranks as in
  * fmoe_ep_moe_forward (cap >= T on every rank; prepared as there).  Attention,

@@ -148,6 +148,72 @@ def test_ep_decoder_graph_replay(fm, dev, comm1, mode):
 # two GPUs, one process each
 
 
+def _prefill_pair(fm, dev, comm, rank=0, world=1, T=200):
+    """A 2-layer model (window 64 < prompt) prefilled locally and, on the same
+    weights with this rank's expert slice, through the expert-parallel layer
+    prefill; returns (local logits, ids, expert-parallel model)."""
+    cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=2, window=64)
+    m1 = fm.Gemma4Model.random(cfg, batch=1, max_positions=512, seed=31, device=dev, n_layers=2)
+    layers = []
+    for L in m1.layers:  # the same weights, expert slice only
+        layers.append(fm.Gemma4DecoderLayer(L.q_proj, L.k_proj, L.v_proj, L.o_proj, L.q_norm, L.k_norm, L.norms,
+                                            L.mlp, L.router, L.experts.shard(rank, world) if world > 1 else L.experts,
+                                            L.num_heads, L.num_kv_heads, L.head_dim, L.rope_dims, L.rope_theta,
+                                            L.k_eq_v, L.eps, L.layer_scalar, L.attn_scale, L.top_k))
+    m2 = fm.Gemma4Model(cfg, m1.embed, layers, m1.final_norm, 1, 512, device=dev, ep=comm, ep_mode=0)
+    prompt = torch.randint(0, cfg["vocab"], (T,), generator=torch.Generator().manual_seed(7 + rank)).to(torch.int32)
+    m1.prefill(prompt.to(dev))
+    want_lg, want_id = m1.logits.clone(), m1.ids.clone()
+    m2.prefill(prompt.to(dev))
+    torch.cuda.synchronize()
+    return want_lg, want_id, m2
+
+
+def test_ep_prefill_one_rank_matches_local(fm, dev, comm1):
+    """The whole-decoder prefill with the routed experts through the
+    expert-parallel MoE (exact exchange; one rank) matches the local prefill:
+    last-position logits and the next token."""
+    want_lg, want_id, m2 = _prefill_pair(fm, dev, comm1)
+    comm1.status()
+    err = max_rel_err(m2.logits.cpu().numpy(), want_lg.cpu().numpy())
+    assert err <= TOL, err
+    top = torch.topk(want_lg[0], 2).values
+    if top[0] - top[1] > 1e-3 * top[0].abs():
+        assert torch.equal(m2.ids, want_id)
+
+
+def _two_rank_prefill_worker(rank, world, port, q):
+    """Two decoder layers prefilled over a 200-token prompt per rank with the
+    experts split over two GPUs, against the same model with all experts local."""
+    import torch.distributed as dist
+
+    import __graft_entry__
+
+    comm = None
+    try:
+        fm = __graft_entry__.load_package()
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+        comm = fm.EPComm()
+        want_lg, want_id, m2 = _prefill_pair(fm, dev, comm, rank, world)
+        top = torch.topk(want_lg[0], 2).values
+        sure = bool(top[0] - top[1] > 1e-3 * top[0].abs())
+        res = (bool(torch.equal(m2.ids, want_id)) or not sure,
+               max_rel_err(m2.logits.cpu().numpy(), want_lg.cpu().numpy()))
+        comm.status()
+        torch.cuda.synchronize()
+        comm.close()
+        dist.destroy_process_group()
+        q.put((rank, res, None))
+    except Exception as e:
+        import traceback
+
+        q.put((rank, None, repr(e) + "\n" + traceback.format_exc()))
+        if comm is not None:
+            comm.abort()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -315,3 +381,12 @@ def test_ep_two_ranks_match_single_device():
         for T, mode, same, err in errs:
             assert same, (rank, T, mode)
             assert err <= TOL, (rank, T, mode, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_rank_prefill_matches_local():
+    out = _spawn_two(_two_rank_prefill_worker)
+    assert all(exc is None for _, exc in out.values()), "\n".join(f"rank {r}: {e}" for r, (_, e) in out.items())
+    for rank, ((same_ids, err), exc) in out.items():
+        assert err <= TOL, (rank, err)
+        assert same_ids, rank
