@@ -46,7 +46,7 @@ struct fmoe_ep_comm {
   int64_t p2p_cap = 0;
   int p2p_hidden = 0, p2p_k = 0;
   uint32_t* seq = nullptr;     // device: exchanges completed
-  unsigned* done = nullptr;    // device [2]: finished CTAs of the dispatch / return kernels
+  unsigned* done = nullptr;    // device [3]: finished CTAs of the dispatch / return / combine kernels
 };
 
 namespace fmoe {
@@ -249,6 +249,87 @@ __global__ void p2p_dispatch_kernel(const bf16* __restrict__ x, const int32_t* _
   publish_flags(pw, L.rx_flag, R, me, seq, done);
 }
 
+// Decode-sized exchanges (R * T <= kP2pPlanSlots): every CTA forms the routing
+// plan of plan_kernel in shared memory (for each destination rank, its tokens'
+// slots in token order) instead of reading it from a separate launch; CTA 0
+// also stores it for the combine.  The stores and flags are those of
+// p2p_dispatch_kernel.
+constexpr int kP2pThreads = 256;
+constexpr int kP2pPlanSlots = 4096;
+__global__ void __launch_bounds__(kP2pThreads) p2p_plan_dispatch_kernel(
+    const bf16* __restrict__ x, const int32_t* __restrict__ ids, const float* __restrict__ wts, int T, int k, int H,
+    int R, int cap, int per_rank, int me, int32_t* __restrict__ slots, int32_t* __restrict__ counts, PeerWins pw,
+    WinLayout L, const uint32_t* seq, unsigned* done) {
+  __shared__ int s_slot[kP2pPlanSlots];
+  __shared__ int s_cnt[8];
+  __shared__ int wsum[kP2pThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int r = 0; r < R; ++r) {
+    const int lo = r * per_rank, hi = lo + per_rank;
+    int run = 0;
+    for (int t0 = 0; t0 < T; t0 += kP2pThreads) {
+      const int t = t0 + threadIdx.x;
+      bool f = false;
+      if (t < T)
+        for (int j = 0; j < k; ++j) {
+          const int e = ids[(int64_t)t * k + j];
+          f |= (e >= lo && e < hi);
+        }
+      const unsigned m = __ballot_sync(0xffffffffu, f);
+      if (lane == 0) wsum[warp] = __popc(m);
+      __syncthreads();
+      int before = 0, total = 0;
+#pragma unroll
+      for (int w = 0; w < kP2pThreads / 32; ++w) {
+        const int c = wsum[w];
+        before += w < warp ? c : 0;
+        total += c;
+      }
+      if (t < T) s_slot[r * T + t] = f ? run + before + __popc(m & ((1u << lane) - 1u)) : -1;
+      run += total;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) s_cnt[r] = run;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < R * T; i += kP2pThreads) slots[(int64_t)(i / T) * cap + i % T] = s_slot[i];
+    if (threadIdx.x < R) {
+      counts[threadIdx.x] = s_cnt[threadIdx.x];
+      reinterpret_cast<int32_t*>(pw.w[threadIdx.x] + L.rx_cnt)[me] = s_cnt[threadIdx.x];
+    }
+  }
+  const int words = H / 8;
+  const int64_t stride = (int64_t)gridDim.x * kP2pThreads;
+  const int64_t n = (int64_t)R * T * words;
+  for (int64_t i = (int64_t)blockIdx.x * kP2pThreads + threadIdx.x; i < n; i += stride) {
+    const int r = (int)(i / ((int64_t)T * words));
+    const int rem = (int)(i % ((int64_t)T * words));
+    const int t = rem / words, w = rem % words;
+    const int s = s_slot[r * T + t];
+    if (s < 0) continue;
+    const int64_t row = (int64_t)me * cap + s;
+    uint8_t* win = pw.w[r];
+    *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(win + L.rx) + row * H + 8 * w) =
+        *reinterpret_cast<const uint4*>(x + (int64_t)t * H + 8 * w);
+    if (w < k) {
+      reinterpret_cast<int32_t*>(win + L.rids)[row * k + w] = ids[(int64_t)t * k + w];
+      reinterpret_cast<float*>(win + L.rwts)[row * k + w] = wts[(int64_t)t * k + w];
+    }
+  }
+  const int64_t m = (int64_t)R * cap * k;
+  for (int64_t i = (int64_t)blockIdx.x * kP2pThreads + threadIdx.x; i < m; i += stride) {
+    const int r = (int)(i / ((int64_t)cap * k));
+    const int j = (int)((i % ((int64_t)cap * k)) / k), c = (int)(i % k);
+    if (j >= s_cnt[r]) {
+      const int64_t o = ((int64_t)me * cap + j) * k + c;
+      reinterpret_cast<int32_t*>(pw.w[r] + L.rids)[o] = -1;
+      reinterpret_cast<float*>(pw.w[r] + L.rwts)[o] = 0.f;
+    }
+  }
+  publish_flags(pw, L.rx_flag, R, me, seq, done);
+}
+
 // Partial sums of the rows received from rank r (block r of ypart, its first
 // rx_cnt[r] rows) go to block `me` of r's returned rows.
 __global__ void p2p_return_kernel(const float* __restrict__ ypart, int R, int cap, int H, int me, PeerWins pw,
@@ -270,25 +351,76 @@ __global__ void p2p_return_kernel(const float* __restrict__ ypart, int R, int ca
 // One warp: lane r waits until flag r reaches seq + 1 (bounded; a timeout sets
 // *status).  advance != 0: then seq = seq + 1 (the exchange is complete).
 constexpr int kP2pPolls = 1 << 22;
+// Polls one flag until it reaches target (acquire, bounded); false on timeout.
+__device__ __forceinline__ bool poll_flag(const uint32_t* f, uint32_t target) {
+  int it = 0;
+  while ((int32_t)(ld_acquire_sys(f) - target) < 0) {
+    if (++it > kP2pPolls) return false;
+    __nanosleep(64);
+  }
+  return true;
+}
+
 __global__ void p2p_wait_kernel(const uint8_t* win, size_t flag_off, int R, uint32_t* seq, int advance, int* status,
                                 int site) {
   const int lane = threadIdx.x;
   const uint32_t target = *reinterpret_cast<volatile uint32_t*>(seq) + 1;
   bool ok = true;
-  if (lane < R) {
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(win + flag_off) + lane;
-    int it = 0;
-    while ((int32_t)(ld_acquire_sys(f) - target) < 0) {
-      if (++it > kP2pPolls) {
-        ok = false;
-        break;
-      }
-      __nanosleep(64);
-    }
-  }
+  if (lane < R) ok = poll_flag(reinterpret_cast<const uint32_t*>(win + flag_off) + lane, target);
   if (!ok) atomicCAS(status, 0, site);
   __syncwarp();
   if (advance && lane == 0) *seq = target;
+}
+
+// The return wait and the combine in one launch: threads r < R of every CTA
+// wait for rank r's return flag (bounded, as p2p_wait_kernel), then the CTA
+// sums its rows as combine_kernel does, reading the returned partials from L2
+// (peer stores land there).  The last CTA to finish advances seq (the
+// exchange is complete) and resets its counter.
+__global__ void __launch_bounds__(kP2pThreads) p2p_combine_kernel(const uint8_t* win, size_t flag_off,
+                                                                  size_t ret_off, const int32_t* __restrict__ slots,
+                                                                  int T, int R, int cap, int H,
+                                                                  bf16* __restrict__ y, uint32_t* seq,
+                                                                  unsigned* done, int* status, int site) {
+  __shared__ uint32_t s_target;
+  __shared__ int s_last;
+  if (threadIdx.x == 0) s_target = *reinterpret_cast<volatile uint32_t*>(seq) + 1;
+  __syncthreads();
+  const uint32_t target = s_target;
+  if (threadIdx.x < R && !poll_flag(reinterpret_cast<const uint32_t*>(win + flag_off) + threadIdx.x, target))
+    atomicCAS(status, 0, site);
+  __syncthreads();
+  const float* ret = reinterpret_cast<const float*>(win + ret_off);
+  const int words = H / 8;
+  for (int64_t i = (int64_t)blockIdx.x * kP2pThreads + threadIdx.x; i < (int64_t)T * words;
+       i += (int64_t)gridDim.x * kP2pThreads) {
+    const int t = (int)(i / words), w = (int)(i % words);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < R; ++r) {
+      const int s = slots[(int64_t)r * cap + t];
+      if (s < 0) continue;
+      const float4* v = reinterpret_cast<const float4*>(ret + ((int64_t)r * cap + s) * H + 8 * w);
+      const float4 a = __ldcg(v), b = __ldcg(v + 1);
+      acc[0] += a.x;
+      acc[1] += a.y;
+      acc[2] += a.z;
+      acc[3] += a.w;
+      acc[4] += b.x;
+      acc[5] += b.y;
+      acc[6] += b.z;
+      acc[7] += b.w;
+    }
+    *reinterpret_cast<uint4*>(y + (int64_t)t * H + 8 * w) =
+        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                   pack_bf16x2(acc[6], acc[7]));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    *seq = target;
+    *done = 0;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -433,20 +565,26 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
     if (cs != cudaStreamCaptureStatusNone)
       return set_error(FMOE_ERR_INVALID, "ep: EXACT mode synchronises on the host and cannot be captured");
   }
-  {
+  const bool fused_plan = mode == FMOE_EP_P2P && (int64_t)R * T <= kP2pPlanSlots;
+  if (!fused_plan) {
     ProfScope prof_("ep_plan_kernel", st);
     plan_kernel<<<R, kPlanThreads, 0, st>>>(ids, (int)T, k, d.E, (int)cap, w.slots, w.counts);
   }
-  if ((rc = check_launch("ep_plan_kernel"))) return rc;
+  if (!fused_plan && (rc = check_launch("ep_plan_kernel"))) return rc;
   if (mode == FMOE_EP_P2P) {  // dispatch and return through the peers' windows
     PeerWins pw;
     for (int r = 0; r < 8; ++r) pw.w[r] = r < R ? c->peer_win[r] : nullptr;
     const WinLayout L = win_layout(R, cap, H, k);
     auto blocks = [](int64_t items) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>(2 * kNumSMs, (items + 255) / 256)); };
-    {
+    const unsigned dgrid = blocks((int64_t)R * std::max<int64_t>(T, cap) * (H / 8));
+    if (fused_plan) {
+      ProfScope prof_("ep_p2p_plan_dispatch_kernel", st);
+      p2p_plan_dispatch_kernel<<<dgrid, kP2pThreads, 0, st>>>(x, ids, wts, (int)T, k, H, R, (int)cap, d.E, c->rank,
+                                                              w.slots, w.counts, pw, L, c->seq, c->done);
+    } else {
       ProfScope prof_("ep_p2p_dispatch_kernel", st);
-      p2p_dispatch_kernel<<<blocks((int64_t)R * std::max<int64_t>(T, cap) * (H / 8)), 256, 0, st>>>(
-          x, ids, wts, w.slots, w.counts, (int)T, k, H, R, (int)cap, c->rank, pw, L, c->seq, c->done);
+      p2p_dispatch_kernel<<<dgrid, 256, 0, st>>>(x, ids, wts, w.slots, w.counts, (int)T, k, H, R, (int)cap, c->rank,
+                                                 pw, L, c->seq, c->done);
     }
     if ((rc = check_launch("ep_p2p_dispatch_kernel"))) return rc;
     {
@@ -474,16 +612,13 @@ int ep_experts(const fmoe_ep_comm* c, const bf16* x, int64_t T, int64_t cap, int
     }
     if ((rc = check_launch("ep_p2p_return_kernel"))) return rc;
     {
-      ProfScope prof_("ep_p2p_wait_kernel", st);
-      p2p_wait_kernel<<<1, 32, 0, st>>>(c->win, L.ret_flag, R, c->seq, 1, status, 72);
+      ProfScope prof_("ep_p2p_combine_kernel", st);
+      const unsigned cgrid = (unsigned)std::max<int64_t>(
+          1, std::min<int64_t>(4 * kNumSMs, (T * (H / 8) + kP2pThreads - 1) / kP2pThreads));
+      p2p_combine_kernel<<<cgrid, kP2pThreads, 0, st>>>(c->win, L.ret_flag, L.ret, w.slots, (int)T, R, (int)cap, H,
+                                                        y, c->seq, c->done + 2, status, 72);
     }
-    if ((rc = check_launch("ep_p2p_wait_kernel"))) return rc;
-    {
-      ProfScope prof_("ep_combine_kernel", st);
-      combine_kernel<<<2 * kNumSMs * 4, 256, 0, st>>>(reinterpret_cast<const float*>(c->win + L.ret), w.slots,
-                                                      (int)T, R, (int)cap, H, y);
-    }
-    return check_launch("ep_combine_kernel");
+    return check_launch("ep_p2p_combine_kernel");
   }
   {
     ProfScope prof_("ep_pack_kernel", st);
