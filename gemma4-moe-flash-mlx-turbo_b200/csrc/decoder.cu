@@ -525,7 +525,11 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
   bf16* xb = static_cast<bf16*>(x);
   const int Ti = (int)T;
   int o_parts = 1, gu_parts = 1, d_parts = 1;
+  if (!(L->sparse_v_tau >= 0.f))
+    return set_error(FMOE_ERR_INVALID, "decoder: sparse_v_tau %g", (double)L->sparse_v_tau);
   if (w.dl) {
+    if (L->sparse_v_tau > 0.f)
+      return set_error(FMOE_ERR_UNSUPPORTED, "decoder: sparse-V gating on the layered path only");
     const DlBufs b = {w.q, w.attn, w.hres, w.h1, w.h2, w.xs, w.moe, w.attn_ws};
     return dl_layer_forward(L, kv, w.dlp, w.dlw, xb, pos, pos_dev, b, st);
   }
@@ -559,9 +563,14 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     return rc;
   // 3 attention over the slots written so far (pos_dev[1] when counters live on the device)
   const int64_t nvalid = pos + 1 < kv.cap ? pos + 1 : kv.cap;
-  if ((rc = launch_attn_decode(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
-                               w.attn_ws, w.attn, st, true, pos, pos_dev)))
+  if (L->sparse_v_tau > 0.f) {  // gated softmax weights (gemma4_attention.rs:91-93, 196-234)
+    if ((rc = launch_sparse_v(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
+                              L->sparse_v_tau, w.attn, st)))
+      return rc;
+  } else if ((rc = launch_attn_decode(kv, w.q, L->num_heads, nvalid, pos_dev ? pos_dev + 1 : nullptr, L->attn_scale,
+                                      w.attn_ws, w.attn, st, true, pos, pos_dev))) {
     return rc;
+  }
   // 4 o = attn . Wo^T
   {
     RgArgs a = {};

@@ -303,6 +303,9 @@ size_t attn_workspace_bytes(const KvDev& c, int Hq);
 // kernel waits for it before reading q or the newest cache row).  newest /
 // newest_dev: the position whose row the preceding kernel appended (its slot
 // is newest % cap; -1: none): every other chunk is copied before the wait.
+// sparsev.cu: gated decode attention (n_dev: attended slots on the device, or null)
+int launch_sparse_v(const KvDev& c, const bf16* q, int q_heads, int64_t n_valid, const int64_t* n_dev, float scale,
+                    float tau, bf16* out, cudaStream_t st);
 int launch_attn_decode(const KvDev& c, const bf16* q, int Hq, int64_t nvalid, const int64_t* nvalid_dev, float scale,
                        void* ws, bf16* out, cudaStream_t st, bool pdl = false, int64_t newest = -1,
                        const int64_t* newest_dev = nullptr);

@@ -11,7 +11,9 @@
 //   pass 2  one thread per output dimension: sum over the keys of the gated
 //           weight times V (V rows read across the threads, coalesced)
 // bf16 caches only (the TurboQuant round trip applies on append, as in the
-// dense path); at most kSvMaxSlots attended slots.
+// dense path); at most kSvMaxSlots attended slots.  The decoder layer runs it
+// in place of the split-KV attention when its sparse_v_tau is above zero
+// (decode only, gemma4_attention.rs:91-93).
 #include <cmath>
 #include "internal.h"
 #include "common.cuh"
@@ -22,10 +24,14 @@ namespace sv {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
+// n_dev (optional): the attended slot count on the device (CUDA-graph replay),
+// clamped to the capacity; otherwise n.
 template <int D>
-__global__ void __launch_bounds__(kThreads) sparse_v_kernel(KvDev c, const bf16* __restrict__ q, int Hq, int n,
-                                                            float scale, float tau, bf16* __restrict__ out) {
+__global__ void __launch_bounds__(kThreads) sparse_v_kernel(KvDev c, const bf16* __restrict__ q, int Hq, int n_host,
+                                                            const int64_t* __restrict__ n_dev, float scale, float tau,
+                                                            bf16* __restrict__ out) {
   constexpr int P = D / 32;
+  const int n = n_dev ? (int)(*n_dev < c.cap ? *n_dev : c.cap) : n_host;
   extern __shared__ float sc[];  // [n] scores
   __shared__ float wm[kWarps], wl[kWarps];
   const int b = blockIdx.x / Hq, h = blockIdx.x % Hq;
@@ -79,6 +85,30 @@ __global__ void __launch_bounds__(kThreads) sparse_v_kernel(KvDev c, const bf16*
 
 int kv_to_dev(const fmoe_kv_cache_t* c, KvDev* d);
 
+int launch_sparse_v(const KvDev& c, const bf16* q, int q_heads, int64_t n_valid, const int64_t* n_dev, float scale,
+                    float tau, bf16* out, cudaStream_t st) {
+  if (c.mode != FMOE_KV_BF16) return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: bf16-storage caches only");
+  if (c.D != 256 && c.D != 512) return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: head_dim %d", c.D);
+  if (q_heads < c.Hkv || q_heads % c.Hkv)
+    return set_error(FMOE_ERR_INVALID, "sparse_v: %d query heads over %d kv heads", q_heads, c.Hkv);
+  if (n_dev ? c.cap > kSvMaxSlots : (n_valid < 1 || n_valid > c.cap || n_valid > kSvMaxSlots))
+    return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: %lld attended slots, capacity %lld (at most %d)",
+                     (long long)n_valid, (long long)c.cap, kSvMaxSlots);
+  if (!(tau >= 0.f)) return set_error(FMOE_ERR_INVALID, "sparse_v: threshold %g", (double)tau);
+  const unsigned grid = (unsigned)(c.B * q_heads);
+  const size_t smem = sizeof(float) * (size_t)(n_dev ? c.cap : n_valid);
+  if (c.D == 256) {
+    cudaFuncSetAttribute(sv::sparse_v_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(4 * kSvMaxSlots));
+    ProfScope prof_("sparse_v_kernel<256>", st);
+    sv::sparse_v_kernel<256><<<grid, sv::kThreads, smem, st>>>(c, q, q_heads, (int)n_valid, n_dev, scale, tau, out);
+  } else {
+    cudaFuncSetAttribute(sv::sparse_v_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(4 * kSvMaxSlots));
+    ProfScope prof_("sparse_v_kernel<512>", st);
+    sv::sparse_v_kernel<512><<<grid, sv::kThreads, smem, st>>>(c, q, q_heads, (int)n_valid, n_dev, scale, tau, out);
+  }
+  return check_launch("sparse_v_kernel");
+}
+
 }  // namespace fmoe
 
 using namespace fmoe;
@@ -89,27 +119,6 @@ extern "C" int fmoe_attn_decode_sparse_v(const fmoe_kv_cache_t* cache, const voi
   int rc;
   if (!cache || !q || !out) return set_error(FMOE_ERR_INVALID, "sparse_v: null cache / q / out");
   if ((rc = kv_to_dev(cache, &c))) return rc;
-  if (c.mode != FMOE_KV_BF16) return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: bf16-storage caches only");
-  if (c.D != 256 && c.D != 512) return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: head_dim %d", c.D);
-  if (q_heads < c.Hkv || q_heads % c.Hkv)
-    return set_error(FMOE_ERR_INVALID, "sparse_v: %d query heads over %d kv heads", q_heads, c.Hkv);
-  if (n_valid < 1 || n_valid > c.cap || n_valid > kSvMaxSlots)
-    return set_error(FMOE_ERR_UNSUPPORTED, "sparse_v: %lld attended slots (1 .. min(capacity, %d))",
-                     (long long)n_valid, kSvMaxSlots);
-  if (!(tau >= 0.f)) return set_error(FMOE_ERR_INVALID, "sparse_v: threshold %g", (double)tau);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned grid = (unsigned)(c.B * q_heads);
-  const size_t smem = sizeof(float) * (size_t)n_valid;
-  if (c.D == 256) {
-    cudaFuncSetAttribute(sv::sparse_v_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(4 * kSvMaxSlots));
-    ProfScope prof_("sparse_v_kernel<256>", st);
-    sv::sparse_v_kernel<256><<<grid, sv::kThreads, smem, st>>>(c, static_cast<const bf16*>(q), q_heads, (int)n_valid,
-                                                             scale, tau, static_cast<bf16*>(out));
-  } else {
-    cudaFuncSetAttribute(sv::sparse_v_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(4 * kSvMaxSlots));
-    ProfScope prof_("sparse_v_kernel<512>", st);
-    sv::sparse_v_kernel<512><<<grid, sv::kThreads, smem, st>>>(c, static_cast<const bf16*>(q), q_heads, (int)n_valid,
-                                                             scale, tau, static_cast<bf16*>(out));
-  }
-  return check_launch("sparse_v_kernel");
+  return launch_sparse_v(c, static_cast<const bf16*>(q), q_heads, n_valid, nullptr, scale, tau, static_cast<bf16*>(out),
+                         static_cast<cudaStream_t>(stream));
 }

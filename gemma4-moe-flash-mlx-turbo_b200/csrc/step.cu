@@ -1805,6 +1805,8 @@ int check_model(const fmoe_decode_model_t* md) {
     const fmoe_decoder_layer_t& L = md->layers[i];
     const fmoe_kv_cache_t& c = md->caches[i];
     const int Hq = L.num_heads, Hkv = L.num_kv_heads, D = L.head_dim;
+    if (L.sparse_v_tau != 0.f)
+      return set_error(FMOE_ERR_UNSUPPORTED, "decode_step: layer %d: sparse-V gating on the layered path only", i);
     if ((D != 256 && D != 512) || Hkv < 1 || Hq % Hkv || Hq / Hkv > 8 || Hq + 2 * Hkv > 48 || Hkv > 16 ||
         (Hq * D) % step::OKC || Hq * D > 8192 || L.rope_dims < 2 || L.rope_dims > D || L.rope_dims % (2 * (D / 32)))
       return set_error(FMOE_ERR_UNSUPPORTED, "decode_step: layer %d attention shape (heads %d/%d, dim %d)", i, Hq, Hkv,

@@ -34,7 +34,7 @@ class DecoderLayerC(ctypes.Structure):
         ("mlp_gate", QWeightC), ("mlp_up", QWeightC), ("mlp_down", QWeightC),
         ("router", RouterC), ("experts", ExpertsC),
         ("num_heads", ctypes.c_int32), ("num_kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32),
-        ("rope_dims", ctypes.c_int32), ("k_eq_v", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("rope_dims", ctypes.c_int32), ("k_eq_v", ctypes.c_int32), ("sparse_v_tau", ctypes.c_float),
         ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float), ("layer_scalar", ctypes.c_float),
         ("attn_scale", ctypes.c_float),
     ]
@@ -78,6 +78,7 @@ class Gemma4DecoderLayer:
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
         self.rope_dims, self.rope_theta, self.k_eq_v = rope_dims, rope_theta, k_eq_v
         self.eps, self.layer_scalar, self.attn_scale, self.top_k = eps, layer_scalar, attn_scale, top_k
+        self.sparse_v_tau = 0.0  # decode-only sparse-V gate (gemma4_attention.rs:91-93); 0: off
         self._c = None
 
     def cstruct(self) -> DecoderLayerC:
@@ -93,8 +94,8 @@ class Gemma4DecoderLayer:
                 _ptr(self.q_norm), _ptr(self.k_norm), _ptr(n["input"]), _ptr(n["post_attn"]), _ptr(n["pre_ff"]),
                 _ptr(n["post_ff_1"]), _ptr(n["pre_ff_2"]), _ptr(n["post_ff_2"]), _ptr(n["post_ff"]),
                 self.mlp[0].cstruct(), self.mlp[1].cstruct(), self.mlp[2].cstruct(), rc, self.experts.cstruct(),
-                self.num_heads, self.num_kv_heads, self.head_dim, self.rope_dims, int(self.k_eq_v), 0,
-                self.rope_theta, self.eps, self.layer_scalar, self.attn_scale)
+                self.num_heads, self.num_kv_heads, self.head_dim, self.rope_dims, int(self.k_eq_v),
+                float(self.sparse_v_tau), self.rope_theta, self.eps, self.layer_scalar, self.attn_scale)
         return self._c
 
     def tile_weights(self):
@@ -407,6 +408,19 @@ class Gemma4Model:
         for cache in self.caches:
             cache._offset = self.pos
         return self.ids
+
+    def set_sparse_v_threshold(self, tau: float):
+        """Model::set_sparse_v_threshold (src/model/mod.rs:367-372): every
+        layer's decode attention zeroes the softmax weights below tau (no
+        renormalisation); 0 turns it off; prefill is unaffected.  Applies to the
+        layered decode path (bf16 / TurboQuant caches); re-capture any CUDA graph
+        of decode_step afterwards."""
+        if not tau >= 0.0:
+            raise ValueError(f"sparse-V threshold {tau}")
+        for L in self.layers:
+            L.sparse_v_tau = float(tau)
+            L._c = None
+        self._fc = None
 
     def set_position(self, pos: int):
         self.pos = pos

@@ -334,7 +334,9 @@ typedef struct fmoe_decoder_layer {
   int32_t head_dim;
   int32_t rope_dims;   /* rotated dims (non-traditional RoPE); head_dim * partial factor */
   int32_t k_eq_v;      /* 1: V is the raw K projection (full-attention layers) */
-  int32_t reserved;
+  float sparse_v_tau;  /* > 0: decode attention zeroes softmax weights below it, no
+                        * renormalisation (sparse-V gating, gemma4_attention.rs:91-93,
+                        * 196-234; bf16 / TurboQuant caches, layered path); 0: off */
   float rope_theta;
   float eps;           /* rms_norm_eps of every norm */
   float layer_scalar;

@@ -287,7 +287,8 @@ def decoder_layer(x, L, cache_k, cache_v, pos, cfg):
         cache_k[:, :, pos % cap] = k
         cache_v[:, :, pos % cap] = v
         hi = np.full(T, min(pos + 1, cap), np.int32)
-        att = attn_decode_bf16(q, Hkv, cap, lo, hi, cache_k, cache_v, cfg["attn_scale"])
+        # cfg["sparse_v_tau"] > 0: the decode-only gate of gemma4_attention.rs:91-93, 196-234
+        att = attn_decode_bf16(q, Hkv, cap, lo, hi, cache_k, cache_v, cfg["attn_scale"], tau=cfg.get("sparse_v_tau", 0.0))
     return _ff_block(x, _bf(att).reshape(T, Hq * D), L, cfg), q
 
 
