@@ -429,6 +429,74 @@ static size_t carve_dec(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   return d.bytes;
 }
 
+// Batched decode (9 .. kBatMaxT sequences): the attention half runs per group
+// of <= 8 sequences on the group-sized buffers; the feed-forward half runs
+// once over all T.  Same shared-offset order as carve_dec.
+constexpr int kBatMaxT = 64;
+struct BatWs {
+  WsHead h;
+  RouterWs rw;
+  MoeWs mw;
+  void* attn_ws;
+  float *qkv, *o;
+  bf16 *q, *attn;
+  bf16 *hres, *h1, *h2, *xs, *moe, *act, *dd;
+  int32_t* ids;
+  float* wts;
+  size_t bytes;
+};
+static size_t carve_bat(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, BatWs* w) {
+  BatWs d = {};
+  int qkv_rows = 0;
+  dec_dims(L, &qkv_rows);
+  const int H = L->q_proj.in_features, Id = L->mlp_gate.out_features, QD = L->num_heads * L->head_dim;
+  const int64_t G = T < 8 ? T : 8;
+  ExpertsDev ex = {};
+  to_experts(&L->experts, &ex);
+  KvDev kg = kv;
+  kg.B = (int)G;
+  d.h = carve_head(c);
+  carve_router(c, T, &L->router, d.h, &d.rw);
+  carve_moe(c, T, L->router.top_k, ex, &d.mw);
+  d.attn_ws = c.take<uint8_t>(attn_workspace_bytes(kg, L->num_heads));
+  d.qkv = c.take<float>((size_t)max_parts(H) * G * qkv_rows);
+  d.o = c.take<float>((size_t)max_parts(QD) * G * H);
+  d.q = c.take<bf16>((size_t)G * QD);
+  d.attn = c.take<bf16>((size_t)G * QD);
+  d.hres = c.take<bf16>((size_t)T * H);
+  d.h1 = c.take<bf16>((size_t)T * H);
+  d.h2 = c.take<bf16>((size_t)T * H);
+  d.xs = c.take<bf16>((size_t)T * H);
+  d.moe = c.take<bf16>((size_t)T * H);
+  d.act = c.take<bf16>((size_t)T * Id);
+  d.dd = c.take<bf16>((size_t)T * H);
+  d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
+  d.wts = c.take<float>((size_t)T * L->router.top_k);
+  d.bytes = c.off + 256;
+  if (w) *w = d;
+  return d.bytes;
+}
+
+// Sequences [b0, b0 + nb) of a cache as a cache of batch nb (same storage).
+static KvDev kv_group(const KvDev& kv, int b0, int nb) {
+  KvDev g = kv;
+  g.B = nb;
+  const int64_t rows = (int64_t)b0 * kv.Hkv * kv.cap;
+  const int D = kv.D;
+  if (kv.mode == FMOE_KV_BF16) {
+    g.k = static_cast<bf16*>(kv.k) + rows * D;
+    g.v = static_cast<bf16*>(kv.v) + rows * D;
+  } else {  // packed 4-bit K, 8-bit V; bf16 scale / bias per 64 elements
+    g.k = static_cast<uint8_t*>(kv.k) + rows * (D / 2);
+    g.v = static_cast<uint8_t*>(kv.v) + rows * D;
+    g.ks = kv.ks + rows * (D / 64);
+    g.kb = kv.kb + rows * (D / 64);
+    g.vs = kv.vs + rows * (D / 64);
+    g.vb = kv.vb + rows * (D / 64);
+  }
+  return g;
+}
+
 static QgSeg seg_of(const QW& q, void* out, int ld, int col0) {
   return QgSeg{static_cast<const uint8_t*>(q.w), q.s, q.b, out, q.out, ld, col0, 0, q.tiled, q.tiled_kc};
 }
@@ -461,9 +529,9 @@ extern "C" {
 size_t fmoe_decoder_workspace_bytes(int64_t T, const fmoe_decoder_layer_t* layer, const fmoe_kv_cache_t* cache) {
   KvDev kv;
   int qkv_rows;
-  if (T <= 0 || dec_dims(layer, &qkv_rows) || kv_to_dev(cache, &kv)) return 0;
+  if (T <= 0 || T > kBatMaxT || dec_dims(layer, &qkv_rows) || kv_to_dev(cache, &kv)) return 0;
   Carver c(nullptr);
-  return carve_dec(c, T, layer, kv, nullptr);
+  return T > 8 ? carve_bat(c, T, layer, kv, nullptr) : carve_dec(c, T, layer, kv, nullptr);
 }
 
 }  // extern "C"
@@ -479,61 +547,22 @@ struct EpCall {
   int mode;
 };
 
-int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, const EpCall& epc, void* x,
-                    int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
-                    void* stream) {
-  int qkv_rows = 0;
-  int rc = dec_dims(L, &qkv_rows);
-  if (rc) return rc;
-  KvDev kv;
-  rc = kv_to_dev(cache, &kv);
-  if (rc) return rc;
-  if (T < 1 || T > 8) return set_error(FMOE_ERR_UNSUPPORTED, "decoder: T=%lld (decode kernels: 1..8 sequences)", (long long)T);
-  if (kv.B != T || kv.Hkv != L->num_kv_heads || kv.D != L->head_dim)
-    return set_error(FMOE_ERR_INVALID, "decoder: cache [%d, %d, ., %d] does not match T=%lld / kv heads / head_dim",
-                     kv.B, kv.Hkv, kv.D, (long long)T);
-  if (!x || !aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "decoder: x null or not 16-byte aligned");
-  QW q, k, v, o, gq, uq, dq, rq;
-  ExpertsDev ex;
-  if ((rc = to_qw(&L->q_proj, &q)) || (rc = to_qw(&L->k_proj, &k)) || (rc = to_qw(&L->o_proj, &o)) ||
-      (rc = to_qw(&L->mlp_gate, &gq)) || (rc = to_qw(&L->mlp_up, &uq)) || (rc = to_qw(&L->mlp_down, &dq)) ||
-      (rc = check_router(&L->router, &rq)) || (rc = to_experts(&L->experts, &ex)))
-    return rc;
-  if (!L->k_eq_v && (rc = to_qw(&L->v_proj, &v))) return rc;
-  if ((rc = check_stream_w(q, L->q_proj.group_size, "q_proj")) || (rc = check_stream_w(k, L->k_proj.group_size, "k_proj")) ||
-      (!L->k_eq_v && (rc = check_stream_w(v, L->v_proj.group_size, "v_proj"))) ||
-      (rc = check_stream_w(o, L->o_proj.group_size, "o_proj")) ||
-      (rc = check_stream_w(gq, L->mlp_gate.group_size, "mlp gate")) ||
-      (rc = check_stream_w(uq, L->mlp_up.group_size, "mlp up")) ||
-      (rc = check_stream_w(dq, L->mlp_down.group_size, "mlp down")))
-    return rc;
-  const int H = q.in, Id = gq.out, QD = L->num_heads * L->head_dim;
-  if (k.in != H || o.out != H || gq.in != H || uq.out != Id || uq.in != H || dq.in != Id || dq.out != H ||
-      ex.H != H || rq.in != H || (!L->k_eq_v && v.in != H))
-    return set_error(FMOE_ERR_INVALID, "decoder: hidden / intermediate sizes disagree across weights");
-  if (epc.comm && (T > epc.cap || (rc = ep_check(epc.comm, ex, rq.out, nullptr))))
-    return rc ? rc : set_error(FMOE_ERR_INVALID, "decoder: T=%lld above the exchange capacity", (long long)T);
-  if (!epc.comm && ex.first != 0) return set_error(FMOE_ERR_INVALID, "decoder: expert slice without a communicator");
-  Carver cz(nullptr);
-  const size_t need = carve_dec(cz, T, L, kv, nullptr, epc.n_ranks, epc.cap);
-  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
-    return set_error(FMOE_ERR_WORKSPACE, "decoder: workspace %zu < %zu", workspace_bytes, need);
-  Carver c(workspace);
-  DecWs w;
-  carve_dec(c, T, L, kv, &w, epc.n_ranks, epc.cap);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  bf16* xb = static_cast<bf16*>(x);
+// Steps 1-5 of a layer for T <= 8 sequences (kv: their cache, or a view of
+// sequences of a larger one): q|k|v, norms / RoPE / append, attention, o, and
+// ff_in's residual and feed-forward input norms into h / h1 / h2 / xs.
+struct AttnBufs {
+  float *qkv, *o;
+  bf16 *q, *attn;
+  void* attn_ws;
+  bf16 *hres, *h1, *h2, *xs;
+  int* status;
+};
+int attn_half(const fmoe_decoder_layer_t* L, const KvDev& kv, const QW& q, const QW& k, const QW& v, const QW& o,
+              int qkv_rows, bf16* xb, int64_t T, int64_t pos, const int64_t* pos_dev, const AttnBufs& w,
+              cudaStream_t st) {
+  const int H = q.in, QD = L->num_heads * L->head_dim;
   const int Ti = (int)T;
-  int o_parts = 1, gu_parts = 1, d_parts = 1;
-  if (!(L->sparse_v_tau >= 0.f))
-    return set_error(FMOE_ERR_INVALID, "decoder: sparse_v_tau %g", (double)L->sparse_v_tau);
-  if (w.dl) {
-    if (L->sparse_v_tau > 0.f)
-      return set_error(FMOE_ERR_UNSUPPORTED, "decoder: sparse-V gating on the layered path only");
-    const DlBufs b = {w.q, w.attn, w.hres, w.h1, w.h2, w.xs, w.moe, w.attn_ws};
-    return dl_layer_forward(L, kv, w.dlp, w.dlw, xb, pos, pos_dev, b, st);
-  }
-
+  int rc, o_parts = 1;
   // 1 q|k|v = input_norm(x) . W^T  (fp32 slices, one per 512-input chunk)
   int qkv_parts = 1;
   {
@@ -549,7 +578,7 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     a.ldx = H;
     a.norm_w = static_cast<const bf16*>(L->input_norm);
     a.eps = L->eps;
-    a.status = w.h.status;
+    a.status = w.status;
     RgLayout rl;
     // the whole SM: the next kernel (q/k norms, RoPE, append) is a few CTAs
     // that need no room beside it, and every item of the CTA fits in flight
@@ -581,7 +610,7 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
     a.in_kind = QG_IN_BF16;
     a.x = w.attn;
     a.ldx = QD;
-    a.status = w.h.status;
+    a.status = w.status;
     RgLayout rl;
     if ((rc = rgemv_plan(a, o.bits, &rl)) || (rc = launch_rgemv(a, rl, o.bits, true, st))) return rc;
     o_parts = a.nck;
@@ -596,6 +625,124 @@ int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache,
                        static_cast<const bf16*>(L->pre_ff_norm_2), L->eps, L->router.root_size,
                        static_cast<const bf16*>(L->router.router_scale), w.hres, w.h1, w.h2, w.xs);
     if ((rc = check_launch("ff_in_kernel"))) return rc;
+  }
+  return FMOE_OK;
+}
+
+// T > 8 sequences: the attention half per group of <= 8 (views of the cache),
+// then router, routed experts and the dense MLP (tensor-core GEMM, T tokens as
+// N) once over all T, and the output norms / residual per token.  Each
+// expert's weights are read once per layer instead of once per group.
+int decoder_forward_batched(const fmoe_decoder_layer_t* L, const KvDev& kv, const QW& q, const QW& k, const QW& v,
+                            const QW& o, const QW& gq, const QW& uq, const QW& dq, const QW& rq,
+                            const ExpertsDev& ex, int qkv_rows, bf16* xb, int64_t T, int64_t pos,
+                            const int64_t* pos_dev, const BatWs& w, cudaStream_t st) {
+  const int H = q.in, Id = gq.out;
+  int rc;
+  if (!qgemm_supported(gq, L->mlp_gate.group_size, H) || !qgemm_supported(uq, L->mlp_up.group_size, H) ||
+      !qgemm_supported(dq, L->mlp_down.group_size, Id))
+    return set_error(FMOE_ERR_UNSUPPORTED, "decoder: batched dense MLP needs 4/8-bit group-64 weights");
+  for (int64_t b0 = 0; b0 < T; b0 += 8) {
+    const int nb = (int)(T - b0 < 8 ? T - b0 : 8);
+    const AttnBufs ab = {w.qkv, w.o, w.q, w.attn, w.attn_ws, w.hres + b0 * H, w.h1 + b0 * H, w.h2 + b0 * H,
+                         w.xs + b0 * H, w.h.status};
+    if ((rc = attn_half(L, kv_group(kv, (int)b0, nb), q, k, v, o, qkv_rows, xb + b0 * H, nb, pos, pos_dev, ab, st)))
+      return rc;
+  }
+  Branch br;
+  if ((rc = branch_for_device(&br))) return rc;
+  if (cudaEventRecord(br.fork, st) != cudaSuccess || cudaStreamWaitEvent(br.side, br.fork, 0) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "decoder: fork: %s", cudaGetErrorString(cudaGetLastError()));
+  {
+    fmoe_router_t r = L->router;
+    r.use_norm = 0;  // ff_in applied the norm chain
+    if ((rc = run_router(w.xs, T, &r, rq, w.rw, w.ids, w.wts, nullptr, &w.mw.m, w.h.status, st))) return rc;
+    if ((rc = run_experts(w.h2, T, r.top_k, w.ids, w.wts, ex, w.moe, w.mw, false, w.h.status, st))) return rc;
+  }
+  {  // dense MLP: gated gate|up GEMM (gelu(g) * u), then down
+    const QmOut gu[2] = {{&gq, w.act, Id}, {&uq, w.act, Id}};
+    if ((rc = launch_qgemm(w.h1, T, H, gu, 2, true, w.h.status, br.side))) return rc;
+    const QmOut dd{&dq, w.dd, H};
+    if ((rc = launch_qgemm(w.act, T, Id, &dd, 1, false, w.h.status, br.side))) return rc;
+  }
+  if (cudaEventRecord(br.join, br.side) != cudaSuccess || cudaStreamWaitEvent(st, br.join, 0) != cudaSuccess)
+    return set_error(FMOE_ERR_CUDA, "decoder: join: %s", cudaGetErrorString(cudaGetLastError()));
+  return launch_ff_out_rows(xb, w.hres, w.dd, w.moe, T, H, static_cast<const bf16*>(L->post_ff_norm_1),
+                            static_cast<const bf16*>(L->post_ff_norm_2), static_cast<const bf16*>(L->post_ff_norm),
+                            L->eps, L->layer_scalar, st);
+}
+
+int decoder_forward(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, const EpCall& epc, void* x,
+                    int64_t T, int64_t pos, const int64_t* pos_dev, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int qkv_rows = 0;
+  int rc = dec_dims(L, &qkv_rows);
+  if (rc) return rc;
+  KvDev kv;
+  rc = kv_to_dev(cache, &kv);
+  if (rc) return rc;
+  if (T < 1 || T > (epc.comm ? 8 : kBatMaxT))
+    return set_error(FMOE_ERR_UNSUPPORTED, "decoder: T=%lld (1..8 sequences per call; up to %d with all experts local)",
+                     (long long)T, kBatMaxT);
+  if (kv.B != T || kv.Hkv != L->num_kv_heads || kv.D != L->head_dim)
+    return set_error(FMOE_ERR_INVALID, "decoder: cache [%d, %d, ., %d] does not match T=%lld / kv heads / head_dim",
+                     kv.B, kv.Hkv, kv.D, (long long)T);
+  if (!x || !aligned(x, 16)) return set_error(FMOE_ERR_ALIGN, "decoder: x null or not 16-byte aligned");
+  QW q, k, v, o, gq, uq, dq, rq;
+  ExpertsDev ex;
+  if ((rc = to_qw(&L->q_proj, &q)) || (rc = to_qw(&L->k_proj, &k)) || (rc = to_qw(&L->o_proj, &o)) ||
+      (rc = to_qw(&L->mlp_gate, &gq)) || (rc = to_qw(&L->mlp_up, &uq)) || (rc = to_qw(&L->mlp_down, &dq)) ||
+      (rc = check_router(&L->router, &rq)) || (rc = to_experts(&L->experts, &ex)))
+    return rc;
+  if (!L->k_eq_v && (rc = to_qw(&L->v_proj, &v))) return rc;
+  if ((rc = check_stream_w(q, L->q_proj.group_size, "q_proj")) || (rc = check_stream_w(k, L->k_proj.group_size, "k_proj")) ||
+      (!L->k_eq_v && (rc = check_stream_w(v, L->v_proj.group_size, "v_proj"))) ||
+      (rc = check_stream_w(o, L->o_proj.group_size, "o_proj")) ||
+      (rc = check_stream_w(gq, L->mlp_gate.group_size, "mlp gate")) ||
+      (rc = check_stream_w(uq, L->mlp_up.group_size, "mlp up")) ||
+      (rc = check_stream_w(dq, L->mlp_down.group_size, "mlp down")))
+    return rc;
+  const int H = q.in, Id = gq.out, QD = L->num_heads * L->head_dim;
+  if (k.in != H || o.out != H || gq.in != H || uq.out != Id || uq.in != H || dq.in != Id || dq.out != H ||
+      ex.H != H || rq.in != H || (!L->k_eq_v && v.in != H))
+    return set_error(FMOE_ERR_INVALID, "decoder: hidden / intermediate sizes disagree across weights");
+  if (epc.comm && (T > epc.cap || (rc = ep_check(epc.comm, ex, rq.out, nullptr))))
+    return rc ? rc : set_error(FMOE_ERR_INVALID, "decoder: T=%lld above the exchange capacity", (long long)T);
+  if (!epc.comm && ex.first != 0) return set_error(FMOE_ERR_INVALID, "decoder: expert slice without a communicator");
+  if (!(L->sparse_v_tau >= 0.f))
+    return set_error(FMOE_ERR_INVALID, "decoder: sparse_v_tau %g", (double)L->sparse_v_tau);
+  if (T > 8) {
+    Carver bz(nullptr);
+    const size_t bneed = carve_bat(bz, T, L, kv, nullptr);
+    if (!workspace || workspace_bytes < bneed || !aligned(workspace, 16))
+      return set_error(FMOE_ERR_WORKSPACE, "decoder: workspace %zu < %zu", workspace_bytes, bneed);
+    Carver bc(workspace);
+    BatWs bw;
+    carve_bat(bc, T, L, kv, &bw);
+    return decoder_forward_batched(L, kv, q, k, v, o, gq, uq, dq, rq, ex, qkv_rows, static_cast<bf16*>(x), T, pos,
+                                   pos_dev, bw, static_cast<cudaStream_t>(stream));
+  }
+  Carver cz(nullptr);
+  const size_t need = carve_dec(cz, T, L, kv, nullptr, epc.n_ranks, epc.cap);
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 16))
+    return set_error(FMOE_ERR_WORKSPACE, "decoder: workspace %zu < %zu", workspace_bytes, need);
+  Carver c(workspace);
+  DecWs w;
+  carve_dec(c, T, L, kv, &w, epc.n_ranks, epc.cap);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bf16* xb = static_cast<bf16*>(x);
+  const int Ti = (int)T;
+  int gu_parts = 1, d_parts = 1;
+  if (w.dl) {
+    if (L->sparse_v_tau > 0.f)
+      return set_error(FMOE_ERR_UNSUPPORTED, "decoder: sparse-V gating on the layered path only");
+    const DlBufs b = {w.q, w.attn, w.hres, w.h1, w.h2, w.xs, w.moe, w.attn_ws};
+    return dl_layer_forward(L, kv, w.dlp, w.dlw, xb, pos, pos_dev, b, st);
+  }
+
+  {
+    const AttnBufs ab = {w.qkv, w.o, w.q, w.attn, w.attn_ws, w.hres, w.h1, w.h2, w.xs, w.h.status};
+    if ((rc = attn_half(L, kv, q, k, v, o, qkv_rows, xb, T, pos, pos_dev, ab, st))) return rc;
   }
   // fork: the dense MLP (6, 10) on the side stream; the router and routed
   // experts (7-9), the longer chain, stay here, so ff_out follows the last

@@ -219,6 +219,9 @@ struct QmOut {
 };
 bool qgemm_supported(const QW& w, int group, int K);
 int launch_qgemm(const bf16* x, int64_t T, int K, const QmOut* o, int nseg, bool gated, int* status, cudaStream_t st);
+// pflayer.cu: output norms / residual / layer scalar of rows (h may equal x)
+int launch_ff_out_rows(bf16* x, const bf16* h, const bf16* d, const bf16* moe, int64_t rows, int H, const bf16* w1,
+                       const bf16* w2, const bf16* w, float eps, float scalar, cudaStream_t st);
 // pflayer.cu: prefill attention of T tokens of one sequence (window 0: causal)
 // affine_ok: an affine (rotated K4 / V8) ring is dequantised as it is read; q and
 // the staged rows must then be in the rotated basis (the decoder layer's prefill).

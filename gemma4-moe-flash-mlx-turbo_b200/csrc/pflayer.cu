@@ -156,7 +156,9 @@ __global__ void __launch_bounds__(kRowThreads) pf_ff_in_kernel(bf16* __restrict_
 
 // x = bf16(bf16(h + bf16(rms_norm(s) * w)) * scalar), s = bf16(pff1(d) + pff2(moe)),
 // h = x on entry.  The same steps as the decode ff_out kernel.
-__global__ void __launch_bounds__(kRowThreads) pf_ff_out_kernel(bf16* __restrict__ x, const bf16* __restrict__ d,
+// h: the residual stream h of each row (x itself in the prefill, which then
+// updates x in place; the batched decode layer's separate h rows).
+__global__ void __launch_bounds__(kRowThreads) pf_ff_out_kernel(bf16* x, const bf16* h, const bf16* __restrict__ d,
                                                                 const bf16* __restrict__ moe, int H,
                                                                 const bf16* __restrict__ w1,
                                                                 const bf16* __restrict__ w2,
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(kRowThreads) pf_ff_out_kernel(bf16* __restrict
     const int c = threadIdx.x + k * kRowThreads;
     if (8 * c < H) {
       float hv[8], wv[8];
-      ld8(x + base + 8 * c, hv);
+      ld8(h + base + 8 * c, hv);
       ld8(w + 8 * c, wv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) hv[i] = round_bf(hv[i] + round_bf(dv[k][i] * rs * wv[i])) * sc;
@@ -585,6 +587,17 @@ __global__ void __launch_bounds__(PaCfg<D>::THREADS, D == 256 ? 2 : 1) pf_attn_k
 
 // Attention of T new tokens (one sequence) at positions pos0.. over the ring's
 // rows of earlier positions and the staged new rows.
+// Output norms, residual and layer scalar of `rows` rows (the decode layer's
+// batched feed-forward half): x = (h + post_ff(pff1(d) + pff2(moe))) * scalar.
+int launch_ff_out_rows(bf16* x, const bf16* h, const bf16* d, const bf16* moe, int64_t rows, int H, const bf16* w1,
+                       const bf16* w2, const bf16* w, float eps, float scalar, cudaStream_t st) {
+  if (H % 8 || H > pfl::kRowThreads * pfl::kRowVec * 8)
+    return set_error(FMOE_ERR_UNSUPPORTED, "ff_out_rows: hidden %d", H);
+  ProfScope prof_("pf_ff_out_kernel", st);
+  pfl::pf_ff_out_kernel<<<(unsigned)rows, pfl::kRowThreads, 0, st>>>(x, h, d, moe, H, w1, w2, w, eps, scalar);
+  return check_launch("pf_ff_out_kernel");
+}
+
 int launch_attn_prefill(const KvDev& c, const bf16* q, int Hq, int64_t T, int64_t pos0, int window,
                         const bf16* ks, const bf16* vs, bf16* out, float scale, cudaStream_t st, bool affine_ok) {
   using namespace pfl;
@@ -866,7 +879,7 @@ int layer_prefill(const fmoe_decoder_layer_t* L, const fmoe_kv_cache_t* cache, f
   {
     ProfScope prof_("pf_ff_out_kernel", st);
     pfl::pf_ff_out_kernel<<<rows, pfl::kRowThreads, 0, st>>>(
-        xb, w.d, w.moe, H, static_cast<const bf16*>(L->post_ff_norm_1), static_cast<const bf16*>(L->post_ff_norm_2),
+        xb, xb, w.d, w.moe, H, static_cast<const bf16*>(L->post_ff_norm_1), static_cast<const bf16*>(L->post_ff_norm_2),
         static_cast<const bf16*>(L->post_ff_norm), L->eps, L->layer_scalar);
   }
   return check_launch("pf_ff_out_kernel");

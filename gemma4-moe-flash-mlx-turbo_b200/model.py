@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 
 import torch
 
@@ -232,11 +233,17 @@ class Gemma4Model:
                 c = KVCache(batch, L.num_kv_heads, L.head_dim, max_positions, window=win, turbo_bits=turbo_bits,
                             device=device)
             self.caches.append(c)
-        # a layer call takes at most 8 sequences: larger batches run as groups of
-        # 8 on views of the same caches (the layer's weights stay in L2 between
-        # the calls of one layer)
+        # the lm_head takes at most 8 sequences per call: larger batches run as
+        # groups of 8.  A layer call takes up to 64 sequences when every expert is
+        # local (its attention half runs per group of 8 inside the library, its
+        # feed-forward half once over the batch, so each expert is read once per
+        # layer); otherwise (expert-parallel, or FMOE_BATCHED_LAYER=0) groups of 8
+        # on views of the same caches
         self.groups = [(b0, min(8, batch - b0)) for b0 in range(0, batch, 8)]
-        self.views = [[c.batch_view(b0, nb) for b0, nb in self.groups] if batch > 8 else [c] for c in self.caches]
+        batched = ep is None and 8 < batch <= 64 and os.environ.get("FMOE_BATCHED_LAYER", "1") != "0"
+        self.layer_groups = [(0, batch)] if batched else self.groups
+        self.views = [[c.batch_view(b0, nb) for b0, nb in self.groups] if batch > 8 and not batched else [c]
+                      for c in self.caches]
         self.ep = ep
         self.ep_cap = min(batch, 8) if ep_cap is None else ep_cap
         # FMOE_EP_P2P (default: peer-memory stores, measured faster than NCCL
@@ -435,7 +442,7 @@ class Gemma4Model:
                                     _stream()))
         pd = self.pos_dev if device_pos else None
         for L, views in zip(self.layers, self.views):
-            for (b0, nb), v in zip(self.groups, views):
+            for (b0, nb), v in zip(self.layer_groups, views):
                 x = self.x[b0:b0 + nb]
                 if self.ep is None:
                     L.forward(x, v, self.pos, self.ws, pd)

@@ -198,16 +198,21 @@ def _layered_step_case(fm, orc, dev, kv, full, seed):
     return True
 
 
-def test_layered_step_batch32_matches_oracle(fm, orc, dev):
-    """Decode at batch 32 (BASELINE config 4's batch): the model runs each layer
-    as four calls of 8 sequences on views of one cache.  Every sequence's logits
-    against the oracle's composition of the step for all 32 tokens at once;
-    sequences whose routing is a near tie at the top-k boundary are left out
-    (at least half must remain)."""
-    B, ctx, seed = 32, 300, 511
-    cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=5)
+@pytest.mark.parametrize("B,full_every,batched", [(32, 5, "1"), (32, 5, "0"), (20, 1, "1")])
+def test_layered_step_batch32_matches_oracle(fm, orc, dev, monkeypatch, B, full_every, batched):
+    """Decode at batch 32 (BASELINE config 4's batch), and a ragged batch of 20
+    on a full-attention layer: batched "1" runs each layer as one call (the
+    attention half per group of 8 inside the library, router / experts / dense
+    MLP once over the batch); "0" as calls of 8 sequences on views of one cache.
+    Every sequence's logits against the oracle's composition of the step for all
+    tokens at once; sequences whose routing is a near tie at the top-k boundary
+    are left out (at least half must remain)."""
+    monkeypatch.setenv("FMOE_BATCHED_LAYER", batched)
+    ctx, seed = 300, 511
+    cfg = dict(fm.GEMMA4_26B, vocab=4096, full_every=full_every)
     m = fm.Gemma4Model.random(cfg, batch=B, max_positions=1024 + 64, seed=seed, device=dev, n_layers=1)
-    assert len(m.groups) == 4
+    assert len(m.groups) == (B + 7) // 8
+    assert len(m.layer_groups) == (1 if batched == "1" else len(m.groups))
     L, cache = m.layers[0], m.caches[0]
     g = torch.Generator(device=dev).manual_seed(seed + 1)
     for p0 in range(0, ctx, 150):
