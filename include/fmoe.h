@@ -343,8 +343,11 @@ typedef struct fmoe_decoder_layer {
   float attn_scale;    /* SDPA scale (1.0 in Gemma 4) */
 } fmoe_decoder_layer_t;
 
-/* One decode step of a layer for T = cache.batch sequences (1..8), one token
- * each, at position pos: x bf16 [T, hidden] is the layer input and receives
+/* One decode step of a layer for T = cache.batch sequences (1..8; up to 64
+ * with every expert local: the attention half then runs per group of 8
+ * sequences and the router, routed experts and dense MLP once over all T, the
+ * dense MLP on the tensor-core GEMM, so each expert is read once per layer),
+ * one token each, at position pos: x bf16 [T, hidden] is the layer input and receives
  * the layer output.  The new K/V rows go to slot pos % capacity of `cache`;
  * attention covers min(pos + 1, capacity) slots.  pos_dev (optional) points to
  * device int64 {pos, attended slots}, read instead of pos (CUDA-graph replay).
