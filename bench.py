@@ -515,6 +515,18 @@ def run_decoder(args, rank, world, local):
         # the other KV caches on the same weights: decode tok/s of each
         result["kv_cache_variants"] = {k: kv_variant(fm, torch, m, cfg, T, k, prompt, ids0, stream, dev, g)
                                        for k in KV_KINDS if k != args.kv_cache}
+    if rank == 0 and world == 1 and not args.profile_step and T == 1:
+        # BASELINE config 4's batch 32 on the same weights and cache kind (its own
+        # prompts, prefilled), as an extra key of the headline line
+        B = WORKLOADS["decode30_b32"]
+        p32 = torch.randint(0, cfg["vocab"], (B, CTX), generator=g, device=dev, dtype=torch.int32)
+        i32 = torch.randint(0, cfg["vocab"], (B,), generator=g, device=dev, dtype=torch.int32)
+        r32 = kv_variant(fm, torch, m, cfg, B, args.kv_cache, p32, i32, stream, dev, g, steps=20, warmup=3)
+        r32["workload"] = "decode30_b32"
+        r32["context"] = f"{B} random {CTX}-token prompts, prefilled"
+        r32["api"] = ("Gemma4Model.decode_step at batch 32: one fmoe_decoder_layer_forward per layer (attention "
+                      "half per group of 8, router / experts / dense MLP over all 32), fmoe_lm_head per group of 8")
+        result["decode30_b32"] = r32
     if rank == 0 and world == 1 and not args.no_attn:
         # BASELINE configs 3 and 2 on the same box, as extra keys of the headline line
         result["kv_attention"] = attn_submeasure(fm, torch, dev, peaks["hbm_gbs"])
