@@ -204,16 +204,18 @@ __global__ void __launch_bounds__(kGuWarps * 32, 3)
 // rows.  Per-warp fp32 sums per (token, row) are added in warp order; with
 // more than one expert group the groups' partials go through the workspace
 // and the last CTA of each row tile (completion counter) adds them in group
-// order, so the result is deterministic.
+// order, so the result is deterministic.  Slots per CTA: 8 up to 16 tokens; 4
+// above (the per-warp (token, row) sums grow with T: at 32 tokens a CTA of 8
+// slots would no longer leave room for a second on its SM).
 constexpr int kDnSlots = 8;
-constexpr int kDnWarps = 2 * kDnSlots;
 constexpr int kDnPairs = 2;
+inline int dn_slots(int64_t T) { return T > 16 ? 4 : kDnSlots; }
 
 struct DnLayout {
   int RS, AS, gmax;
   size_t slot_bytes, s_off, f_off, a_off, y_off, bytes;
 };
-__host__ __device__ inline DnLayout dn_layout(int I, int T) {
+__host__ __device__ inline DnLayout dn_layout(int I, int T, int slots) {
   DnLayout L;
   const int Gi = I / 64;
   L.gmax = (Gi + 1) / 2;                                           // groups per half
@@ -223,21 +225,23 @@ __host__ __device__ inline DnLayout dn_layout(int I, int T) {
   L.f_off = align16(L.s_off + 2 * 16 * (size_t)Gi * 2);            // float2 [2 halves][16][gmax]
   L.a_off = align16(L.f_off + 2 * 16 * (size_t)L.gmax * sizeof(float2));
   L.slot_bytes = align16(L.a_off + (size_t)kDnPairs * L.AS);
-  L.y_off = kDnSlots * L.slot_bytes;
-  L.bytes = L.y_off + sizeof(float) * kDnWarps * (size_t)T * 16;
+  L.y_off = slots * L.slot_bytes;
+  L.bytes = L.y_off + sizeof(float) * 2 * slots * (size_t)T * 16;
   return L;
 }
 
-__global__ void __launch_bounds__(kDnWarps * 32, 2)
+template <int SLOTS>
+__global__ void __launch_bounds__(2 * SLOTS * 32, SLOTS == 8 ? 2 : 3)
     moe_down_kernel(const bf16* __restrict__ act, int T, int k, const float* __restrict__ wts, ExpertsDev ex,
                     const int4* __restrict__ work, int work_len, const int32_t* __restrict__ pairs,
                     float* __restrict__ part, unsigned* __restrict__ tile_ctr, bf16* __restrict__ y,
                     float* __restrict__ y32, int* status) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bars[kDnSlots][2];  // [slot][0: weights + scales, 1: act rows]
+  constexpr int kDnWarps = 2 * SLOTS;
+  __shared__ __align__(8) uint64_t bars[SLOTS][2];  // [slot][0: weights + scales, 1: act rows]
   __shared__ int s_last;
   const int H = ex.H, I = ex.I, Gi = I / 64;
-  const DnLayout L = dn_layout(I, T);
+  const DnLayout L = dn_layout(I, T, SLOTS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int half = warp & 1, slot = warp >> 1;
   const int gh0 = half ? L.gmax : 0, gh1 = half ? Gi : L.gmax, ng = gh1 - gh0;
@@ -249,10 +253,10 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
   float* ysm = reinterpret_cast<float*>(smem + L.y_off);  // [kDnWarps][T][16]
   uint64_t* bw = &bars[slot][0];
   uint64_t* ba = &bars[slot][1];
-  const int u = blockIdx.y * kDnSlots + slot;
+  const int u = blockIdx.y * SLOTS + slot;
   const int RB = I / 2, sb = 16 * Gi * 2;
   const bool leader = half == 0 && lane == 0;
-  if (threadIdx.x < kDnSlots * 2) {
+  if (threadIdx.x < SLOTS * 2) {
     mbar_init(&bars[threadIdx.x >> 1][threadIdx.x & 1], 1);
     mbar_fence_init();
   }
@@ -365,7 +369,8 @@ __global__ void __launch_bounds__(kDnWarps * 32, 2)
 
 int down_groups(int64_t T, int k, int E) {
   const int64_t maxu = T * k < E ? T * k : E;
-  return (int)((maxu + kDnSlots - 1) / kDnSlots);
+  const int slots = dn_slots(T);
+  return (int)((maxu + slots - 1) / slots);
 }
 
 // ---------------------------------------------------------------------------
@@ -553,16 +558,18 @@ int launch_moe_gate_up(const bf16* x, int64_t T, int k, const ExpertsDev& ex, co
 
 int launch_moe_down(const bf16* act, int64_t T, int k, const float* wts, const ExpertsDev& ex, const RouteMeta& m,
                     float* part, unsigned* tile_ctr, bf16* y, int* status, bool pdl, cudaStream_t st, float* y32) {
-  const DnLayout L = dn_layout(ex.I, (int)T);
+  const int slots = dn_slots(T);
+  const DnLayout L = dn_layout(ex.I, (int)T, slots);
   if (L.bytes > 227 * 1024)
     return set_error(FMOE_ERR_UNSUPPORTED, "down: T=%lld / I=%d exceed shared memory", (long long)T, ex.I);
-  cudaFuncSetAttribute(moe_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes);
+  auto kern = slots == 8 ? moe_down_kernel<8> : moe_down_kernel<4>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.bytes);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg =
-      pdl_config(dim3(ex.H / 16, (m.work_len + kDnSlots - 1) / kDnSlots), dim3(kDnWarps * 32), L.bytes, st, pdl, attr);
+      pdl_config(dim3(ex.H / 16, (m.work_len + slots - 1) / slots), dim3(2 * slots * 32), L.bytes, st, pdl, attr);
   {
     ProfScope prof_("moe_down_kernel", st);
-    cudaLaunchKernelEx(&cfg, moe_down_kernel, act, (int)T, k, wts, ex, (const int4*)m.work, m.work_len,
+    cudaLaunchKernelEx(&cfg, kern, act, (int)T, k, wts, ex, (const int4*)m.work, m.work_len,
                        (const int32_t*)m.pairs, part, tile_ctr, y, y32, status);
   }
   return check_launch("moe_down_kernel");
