@@ -315,14 +315,15 @@ struct Branch {
   cudaStream_t side = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
 };
-static int branch_for_device(Branch* out) {
-  static Branch per_dev[64];
+// which: 0 the dense-MLP branch; 1 the second attention stream of the batched layer.
+static int branch_for_device(Branch* out, int which = 0) {
+  static Branch per_dev[64][2];
   static std::mutex mu;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return set_error(FMOE_ERR_CUDA, "decoder: no current device");
   std::lock_guard<std::mutex> lock(mu);
-  Branch& b = per_dev[dev];
+  Branch& b = per_dev[dev][which];
   if (!b.side) {
     if (cudaStreamCreateWithFlags(&b.side, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming) != cudaSuccess ||
@@ -443,6 +444,12 @@ struct BatWs {
   bf16 *hres, *h1, *h2, *xs, *moe, *act, *dd;
   int32_t* ids;
   float* wts;
+  // the odd groups' attention-half buffers (second stream); the attention
+  // counters there are cleared by each call, as their offset varies by layer
+  void* attn_ws2;
+  size_t attn_ws2_ctr_bytes;
+  float *qkv2, *o2;
+  bf16 *q2, *attn2;
   size_t bytes;
 };
 static size_t carve_bat(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, const KvDev& kv, BatWs* w) {
@@ -472,6 +479,12 @@ static size_t carve_bat(Carver& c, int64_t T, const fmoe_decoder_layer_t* L, con
   d.dd = c.take<bf16>((size_t)T * H);
   d.ids = c.take<int32_t>((size_t)T * L->router.top_k);
   d.wts = c.take<float>((size_t)T * L->router.top_k);
+  d.attn_ws2 = c.take<uint8_t>(attn_workspace_bytes(kg, L->num_heads));
+  d.attn_ws2_ctr_bytes = 256 + sizeof(unsigned) * (size_t)G * kv.Hkv;  // status word slot + merge counters
+  d.qkv2 = c.take<float>((size_t)max_parts(H) * G * qkv_rows);
+  d.o2 = c.take<float>((size_t)max_parts(QD) * G * H);
+  d.q2 = c.take<bf16>((size_t)G * QD);
+  d.attn2 = c.take<bf16>((size_t)G * QD);
   d.bytes = c.off + 256;
   if (w) *w = d;
   return d.bytes;
@@ -642,13 +655,30 @@ int decoder_forward_batched(const fmoe_decoder_layer_t* L, const KvDev& kv, cons
   if (!qgemm_supported(gq, L->mlp_gate.group_size, H) || !qgemm_supported(uq, L->mlp_up.group_size, H) ||
       !qgemm_supported(dq, L->mlp_down.group_size, Id))
     return set_error(FMOE_ERR_UNSUPPORTED, "decoder: batched dense MLP needs 4/8-bit group-64 weights");
+  // even groups on the caller's stream, odd groups on a second stream with
+  // their own buffers: one group's row kernels and attention overlap the other
+  // group's projections
+  const char* ns = std::getenv("FMOE_BATCHED_STREAMS");
+  const bool two = T > 8 && !(ns && ns[0] == '1');
+  Branch bg;
+  if (two) {
+    if ((rc = branch_for_device(&bg, 1))) return rc;
+    if (cudaEventRecord(bg.fork, st) != cudaSuccess || cudaStreamWaitEvent(bg.side, bg.fork, 0) != cudaSuccess ||
+        cudaMemsetAsync(w.attn_ws2, 0, w.attn_ws2_ctr_bytes, bg.side) != cudaSuccess)
+      return set_error(FMOE_ERR_CUDA, "decoder: attention fork: %s", cudaGetErrorString(cudaGetLastError()));
+  }
   for (int64_t b0 = 0; b0 < T; b0 += 8) {
     const int nb = (int)(T - b0 < 8 ? T - b0 : 8);
-    const AttnBufs ab = {w.qkv, w.o, w.q, w.attn, w.attn_ws, w.hres + b0 * H, w.h1 + b0 * H, w.h2 + b0 * H,
-                         w.xs + b0 * H, w.h.status};
-    if ((rc = attn_half(L, kv_group(kv, (int)b0, nb), q, k, v, o, qkv_rows, xb + b0 * H, nb, pos, pos_dev, ab, st)))
+    const bool odd = two && ((b0 / 8) & 1);
+    const AttnBufs ab = {odd ? w.qkv2 : w.qkv, odd ? w.o2 : w.o, odd ? w.q2 : w.q, odd ? w.attn2 : w.attn,
+                         odd ? w.attn_ws2 : w.attn_ws, w.hres + b0 * H, w.h1 + b0 * H, w.h2 + b0 * H, w.xs + b0 * H,
+                         w.h.status};
+    if ((rc = attn_half(L, kv_group(kv, (int)b0, nb), q, k, v, o, qkv_rows, xb + b0 * H, nb, pos, pos_dev, ab,
+                        odd ? bg.side : st)))
       return rc;
   }
+  if (two && (cudaEventRecord(bg.join, bg.side) != cudaSuccess || cudaStreamWaitEvent(st, bg.join, 0) != cudaSuccess))
+    return set_error(FMOE_ERR_CUDA, "decoder: attention join: %s", cudaGetErrorString(cudaGetLastError()));
   Branch br;
   if ((rc = branch_for_device(&br))) return rc;
   if (cudaEventRecord(br.fork, st) != cudaSuccess || cudaStreamWaitEvent(br.side, br.fork, 0) != cudaSuccess)
