@@ -346,7 +346,8 @@ typedef struct fmoe_decoder_layer {
 /* One decode step of a layer for T = cache.batch sequences (1..8; up to 64
  * with every expert local: the attention half then runs per group of 8
  * sequences and the router, routed experts and dense MLP once over all T, the
- * dense MLP on the tensor-core GEMM, so each expert is read once per layer),
+ * dense MLP on the tensor-core GEMM, so each expert is read once per layer;
+ * alternate groups' attention on a second library stream, joined back),
  * one token each, at position pos: x bf16 [T, hidden] is the layer input and receives
  * the layer output.  The new K/V rows go to slot pos % capacity of `cache`;
  * attention covers min(pos + 1, capacity) slots.  pos_dev (optional) points to
